@@ -1,0 +1,254 @@
+"""Python access to the b2decode C ABI (include/b2decode.h).
+
+The library is the product; this module only binds it with ctypes for tests,
+the smoke check and the bench.  It refuses to run without the compiled
+library: there is no Python or CPU fallback for any computation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from typing import Iterator, Sequence
+
+import numpy as np
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libb2decode.so")
+HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "b2decode.h")
+
+B2_OK = 0
+ERRORS = {
+    -1: "IO", -2: "FORMAT", -3: "UNSUPPORTED_TYPE", -4: "OOM", -5: "CUDA", -6: "NCCL", -7: "TIMEOUT",
+    -8: "BAD_ARG", -9: "CONTEXT", -10: "NOT_LOADED",
+}
+QTYPE_Q8_0 = 8
+QTYPE_Q4_0 = 2
+
+
+class B2Error(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"B2_ERR_{ERRORS.get(code, code)} ({code}): {msg}")
+        self.code = code
+
+
+class LoadOpts(C.Structure):
+    _fields_ = [("num_ctx", C.c_int32), ("device", C.c_int32), ("kv_fp32", C.c_int32), ("reserved0", C.c_int32),
+                ("reserved1", C.c_int32), ("reserved2", C.c_int32)]
+
+
+class Config(C.Structure):
+    _fields_ = [("arch", C.c_char * 32), ("vocab_size", C.c_int32), ("hidden_size", C.c_int32),
+                ("intermediate_size", C.c_int32), ("num_layers", C.c_int32), ("num_heads", C.c_int32),
+                ("num_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("max_seq_len", C.c_int32),
+                ("rms_norm_eps", C.c_float), ("rope_theta", C.c_float), ("tied_embeddings", C.c_int32),
+                ("has_qkv_bias", C.c_int32), ("weight_type", C.c_int32), ("bos_id", C.c_int32),
+                ("eos_id", C.c_int32), ("weight_bytes", C.c_int64), ("stream_bytes_per_token", C.c_int64)]
+
+
+class Timings(C.Structure):
+    _fields_ = [("prompt_ns", C.c_int64), ("eval_ns", C.c_int64), ("prompt_tokens", C.c_int32),
+                ("completion_tokens", C.c_int32)]
+
+
+class SampleOpts(C.Structure):
+    _fields_ = [("temperature", C.c_double), ("top_k", C.c_int32), ("top_p", C.c_double),
+                ("repeat_penalty", C.c_double), ("num_predict", C.c_int32), ("seed", C.c_uint64)]
+
+
+def build(verbose: bool = False) -> str:
+    """Compiles libb2decode.so in-tree (nvcc, sm_100a)."""
+    out = subprocess.run(["make", "-j8", "-C", PKG_DIR], capture_output=True, text=True)
+    if out.returncode != 0:
+        raise RuntimeError("libb2decode build failed:\n" + out.stdout[-4000:] + out.stderr[-4000:])
+    if verbose:
+        print(out.stdout[-2000:])
+    return LIB_PATH
+
+
+_lib = None
+
+_P = C.c_void_p
+_i32 = C.c_int32
+_i64 = C.c_int64
+_i32p = C.POINTER(C.c_int32)
+_f32p = C.POINTER(C.c_float)
+
+# name -> (restype, argtypes); every symbol the header declares
+SIGNATURES = {
+    "b2_load": (C.c_int, [C.c_char_p, C.POINTER(LoadOpts), C.POINTER(_P)]),
+    "b2_free": (None, [_P]),
+    "b2_get_config": (C.c_int, [_P, C.POINTER(Config)]),
+    "b2_last_error": (C.c_char_p, []),
+    "b2_reset": (C.c_int, [_P]),
+    "b2_cache_len": (C.c_int, [_P, _i32p]),
+    "b2_forward": (C.c_int, [_P, _i32p, _i32, _f32p]),
+    "b2_forward_argmax": (C.c_int, [_P, _i32p, _i32, _i32p]),
+    "b2_decode_greedy": (C.c_int, [_P, _i32, _i32, _i32, _i32p, _i32p]),
+    "b2_predict": (C.c_int, [_P, _i32p, _i32, C.POINTER(SampleOpts), _i32p, _i32, _i32p, _i32, _i32p,
+                             C.POINTER(Timings)]),
+    "b2_stream_begin": (C.c_int, [_P, _i32p, _i32, C.POINTER(SampleOpts), _i32p, _i32]),
+    "b2_stream_next": (C.c_int, [_P, _i32p, _i32p]),
+    "b2_sample_logits": (C.c_int32, [_f32p, _i32, C.POINTER(SampleOpts), _i32p, _i32, C.c_float]),
+    "b2_embed": (C.c_int, [_P, _i32p, _i32, _f32p]),
+    "b2_dequant_tensor": (C.c_int, [_P, C.c_char_p, _f32p, _i64, C.POINTER(_i64)]),
+    "b2_matvec": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _P]),
+    "b2_attention_decode": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
+    "b2_device_status": (C.c_int, [_P]),
+    "b2_stream_handle": (_P, [_P]),
+    "b2_debug_wait_skew": (C.c_int, [_P, _i32]),
+}
+
+
+def lib():
+    """Loads libb2decode.so; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it first (make -C {PKG_DIR}); "
+                               "there is no fallback implementation")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().b2_last_error().decode(errors="replace")
+
+
+def _check(rc: int) -> None:
+    if rc != B2_OK:
+        raise B2Error(rc, last_error())
+
+
+def _ids(a) -> tuple:
+    arr = np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(-1))
+    return arr, arr.ctypes.data_as(_i32p)
+
+
+def sample_opts(temperature=0.0, top_k=0, top_p=0.0, repeat_penalty=1.0, num_predict=0, seed=0) -> SampleOpts:
+    return SampleOpts(float(temperature), int(top_k), float(top_p), float(repeat_penalty), int(num_predict),
+                      int(seed))
+
+
+class Model:
+    """One loaded GGUF model on one GPU (a b2_model handle)."""
+
+    def __init__(self, path: str, num_ctx: int = 0, device: int = 0, kv_fp32: bool = False):
+        L = lib()
+        opts = LoadOpts(int(num_ctx), int(device), 1 if kv_fp32 else 0, 0, 0, 0)
+        h = _P()
+        _check(L.b2_load(path.encode(), C.byref(opts), C.byref(h)))
+        self._h = h
+        c = Config()
+        _check(L.b2_get_config(self._h, C.byref(c)))
+        self.cfg = {k: getattr(c, k) for k, _ in Config._fields_}
+        self.cfg["arch"] = c.arch.decode()
+        self.vocab = c.vocab_size
+
+    # engine.go Unload
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().b2_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def reset(self) -> None:
+        _check(lib().b2_reset(self._h))
+
+    @property
+    def cache_len(self) -> int:
+        n = C.c_int32()
+        _check(lib().b2_cache_len(self._h, C.byref(n)))
+        return n.value
+
+    def forward(self, tokens) -> np.ndarray:
+        arr, p = _ids(tokens)
+        out = np.empty(self.vocab, dtype=np.float32)
+        _check(lib().b2_forward(self._h, p, len(arr), out.ctypes.data_as(_f32p)))
+        return out
+
+    def forward_argmax(self, tokens) -> int:
+        arr, p = _ids(tokens)
+        nxt = C.c_int32()
+        _check(lib().b2_forward_argmax(self._h, p, len(arr), C.byref(nxt)))
+        return nxt.value
+
+    def decode_greedy(self, first: int, n_steps: int, eos: int = -1) -> np.ndarray:
+        out = np.zeros(max(n_steps, 1), dtype=np.int32)
+        n = C.c_int32()
+        _check(lib().b2_decode_greedy(self._h, int(first), int(n_steps), int(eos), out.ctypes.data_as(_i32p),
+                                      C.byref(n)))
+        return out[: n.value].copy()
+
+    def predict(self, prompt, opts: SampleOpts | None = None, stop_ids: Sequence[int] = (), max_out: int = 4096):
+        arr, p = _ids(prompt)
+        st, sp = _ids(list(stop_ids) or [0])
+        out = np.zeros(max_out, dtype=np.int32)
+        n = C.c_int32()
+        t = Timings()
+        _check(lib().b2_predict(self._h, p, len(arr), C.byref(opts or sample_opts()), sp, len(stop_ids),
+                                out.ctypes.data_as(_i32p), max_out, C.byref(n), C.byref(t)))
+        return out[: n.value].copy(), {k: getattr(t, k) for k, _ in Timings._fields_}
+
+    def stream(self, prompt, opts: SampleOpts | None = None, stop_ids: Sequence[int] = ()) -> Iterator[int]:
+        arr, p = _ids(prompt)
+        st, sp = _ids(list(stop_ids) or [0])
+        _check(lib().b2_stream_begin(self._h, p, len(arr), C.byref(opts or sample_opts()), sp, len(stop_ids)))
+        tok, done = C.c_int32(), C.c_int32()
+        while True:
+            _check(lib().b2_stream_next(self._h, C.byref(tok), C.byref(done)))
+            if done.value:
+                return
+            yield tok.value
+
+    def embed(self, tokens) -> np.ndarray:
+        arr, p = _ids(tokens)
+        out = np.empty(self.cfg["hidden_size"], dtype=np.float32)
+        _check(lib().b2_embed(self._h, p, len(arr), out.ctypes.data_as(_f32p)))
+        return out
+
+    def dequant(self, name: str, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        got = C.c_int64()
+        _check(lib().b2_dequant_tensor(self._h, name.encode(), out.ctypes.data_as(_f32p), n, C.byref(got)))
+        return out[: got.value]
+
+    def device_status(self) -> int:
+        return lib().b2_device_status(self._h)
+
+    def stream_handle(self) -> int:
+        return lib().b2_stream_handle(self._h) or 0
+
+    def debug_wait_skew(self, skew: int) -> None:
+        _check(lib().b2_debug_wait_skew(self._h, int(skew)))
+
+
+def sample_logits(logits, opts: SampleOpts, generated=(), r: float = 0.5) -> int:
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    g, gp = _ids(list(generated) or [0])
+    return int(lib().b2_sample_logits(lg.ctypes.data_as(_f32p), lg.size, C.byref(opts), gp, len(generated),
+                                      float(r)))
+
+
+def matvec(qtype: int, w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:
+    """y = W x on the device; pointers are device addresses (e.g. tensor.data_ptr())."""
+    _check(lib().b2_matvec(qtype, w_ptr, x_ptr, y_ptr, rows, cols, stream or None))
+
+
+def attention_decode(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, nh: int, nkv: int, hd: int,
+                     ctx: int, stream: int = 0) -> None:
+    _check(lib().b2_attention_decode(q_ptr, k_ptr, v_ptr, out_ptr, batch, nh, nkv, hd, ctx, stream or None))

@@ -1,0 +1,610 @@
+// Model load and the per-token drivers.
+//
+// Load follows transformer.go:215-310 (Engine.Load) and 1122-1335
+// (loadWeights) for what is read and how it is interpreted, but nothing is
+// dequantised on the host: Q8_0 / Q4_0 blocks are copied byte for byte into
+// one HBM arena.  Placement is chosen for the decode kernel: Wq, Wk and Wv
+// rows are adjacent (one fused [qd + 2*kvd] x H matrix), gate rows are
+// followed by up rows, every region starts on a 256-byte boundary and is
+// padded so 16-byte bulk copies never leave the arena.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "model.h"
+
+namespace b2 {
+
+int (*g_malloc_hook)(void** p, size_t bytes) = nullptr;
+
+namespace {
+
+int dev_malloc(void** p, size_t bytes) {
+    if (g_malloc_hook) return g_malloc_hook(p, bytes);
+    return cudaMalloc(p, bytes) == cudaSuccess ? 0 : -1;
+}
+
+size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// gguf.go:616-643 float16ToFloat32 (host side, for small F16 vectors).
+float f16_to_f32(uint16_t h) {
+    uint32_t sign = (h >> 15) & 1, exp = (h >> 10) & 0x1F, mant = h & 0x3FF, f;
+    if (exp == 0) {
+        if (mant == 0) {
+            f = sign << 31;
+        } else {
+            exp = 1;
+            while ((mant & 0x400) == 0) { mant <<= 1; exp--; }
+            mant &= 0x3FF;
+            f = (sign << 31) | ((exp + 127 - 15) << 23) | (mant << 13);
+        }
+    } else if (exp == 0x1F) {
+        f = (sign << 31) | (0xFFu << 23) | (mant << 13);
+    } else {
+        f = (sign << 31) | ((exp + 127 - 15) << 23) | (mant << 13);
+    }
+    float o;
+    memcpy(&o, &f, 4);
+    return o;
+}
+
+struct Region {
+    std::string tensor;  // source tensor name
+    size_t off;          // destination offset in the arena
+};
+
+__global__ void dequant_kernel(const uint8_t* src, uint32_t type, uint64_t n, float* dst) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        float v;
+        if (type == 8) {  // gguf.go:540-582
+            const uint8_t* p = src + (i >> 5) * 34;
+            v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(int8_t)p[2 + (i & 31)];
+        } else if (type == 2) {  // ggml Q4_0 order
+            const uint8_t* p = src + (i >> 5) * 18;
+            const int e = (int)(i & 31);
+            const uint8_t byte = p[2 + (e & 15)];
+            v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(((e < 16) ? (byte & 15) : (byte >> 4)) - 8);
+        } else {
+            v = reinterpret_cast<const float*>(src)[i];
+        }
+        dst[i] = v;
+    }
+}
+
+__global__ void embed_mean_kernel(const ModelDev m, const int* toks, int n, float* out) {
+    // transformer.go:445-490 Embed: sum rows in order, scale by 1/n, L2 normalise.
+    __shared__ float red[32];
+    __shared__ float total;
+    const float scale = 1.0f / (float)n;
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < m.H; j += blockDim.x) {
+        float e = 0.0f;
+        for (int t = 0; t < n; t++) {
+            const int tok = toks[t];
+            if (tok < 0 || tok >= m.V) continue;
+            const uint8_t* row = m.tok_embd + (size_t)tok * m.rb_h;
+            const int b = j >> 5, k = j & 31;
+            float v;
+            if (m.qtype == 8) {
+                const uint8_t* p = row + 34 * b;
+                v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(int8_t)p[2 + k];
+            } else {
+                const uint8_t* p = row + 18 * b;
+                const uint8_t byte = p[2 + (k & 15)];
+                v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(((k < 16) ? (byte & 15) : (byte >> 4)) - 8);
+            }
+            e += v;
+        }
+        e *= scale;
+        out[j] = e;
+        ss += e * e;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
+        total = (float)sqrt((double)t);
+    }
+    __syncthreads();
+    if (total > 0.0f)
+        for (int j = threadIdx.x; j < m.H; j += blockDim.x) out[j] = out[j] / total;
+}
+
+}  // namespace
+
+int launch_dequant(const void* src, uint32_t type, uint64_t n, float* dst, cudaStream_t s) {
+    int blocks = (int)std::min<uint64_t>((n + 255) / 256, 148 * 16);
+    if (blocks < 1) blocks = 1;
+    dequant_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t*>(src), type, n, dst);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+int launch_embed_mean(const b2_model* m, const int* d_tokens, int n, float* d_out, cudaStream_t s) {
+    embed_mean_kernel<<<1, 256, 0, s>>>(m->dev, d_tokens, n, d_out);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
+}
+
+int check_device_status(b2_model* m, std::string* err) {
+    int code = 0;
+    cudaError_t e = cudaMemcpyAsync(&code, m->dev.err, sizeof(int), cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) {
+        *err = std::string("CUDA: ") + cudaGetErrorString(e);
+        return B2_ERR_CUDA;
+    }
+    if (code != 0) {
+        cudaMemsetAsync(m->dev.err, 0, sizeof(int), m->stream);
+        cudaStreamSynchronize(m->stream);
+        *err = "device-side wait timed out (bounded wait gave up)";
+        return code;
+    }
+    return B2_OK;
+}
+
+static int splits_for(const b2_model* m, int ctx) {
+    int s = (ctx + 63) / 64;
+    int cap = std::max(1, std::min(kMaxSplits, m->grid / std::max(1, m->dev.nkv)));
+    return std::max(1, std::min(s, cap));
+}
+
+int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err) {
+    if (n <= 0) { *err = "no tokens"; return B2_ERR_BAD_ARG; }
+    if (m->cache_len + n > m->cfg.max_seq_len) {
+        *err = "context length exceeded: " + std::to_string(m->cache_len + n) + " > " +
+               std::to_string(m->cfg.max_seq_len);
+        return B2_ERR_CONTEXT;
+    }
+    if (m->pin_pending) cudaEventSynchronize(m->ev_pin);  // h_pinned may still feed an earlier copy
+    memcpy(m->h_pinned, host_tokens, sizeof(int32_t) * n);
+    cudaError_t e = cudaMemcpyAsync(m->d_tokens, m->h_pinned, sizeof(int32_t) * n, cudaMemcpyHostToDevice, m->stream);
+    if (e != cudaSuccess) { *err = cudaGetErrorString(e); return B2_ERR_CUDA; }
+    cudaEventRecord(m->ev_pin, m->stream);
+    m->pin_pending = true;
+    const int P = kPhasesPerLayer * m->dev.L;
+    for (int i = 0; i < n; i++) {
+        StepArgs a{};
+        a.tok = m->d_tokens + i;
+        a.pos = m->cache_len + i;
+        a.p_begin = 0;
+        // transformer.go:545-555: logits are needed for the last token only.
+        a.p_end = (i == n - 1) ? P + 1 : P;
+        a.epoch = ++m->epoch;
+        a.skew = m->wait_skew;
+        m->wait_skew = 0;
+        a.splits = splits_for(m, a.pos + 1);
+        int rc = launch_decode(m->dev, a, m->grid, m->stream, err);
+        if (rc) return rc;
+    }
+    m->cache_len += n;
+    return B2_OK;
+}
+
+int run_greedy(b2_model* m, int32_t first, int n_steps, int32_t eos, int32_t* out_ids, int32_t* n_out,
+               std::string* err) {
+    *n_out = 0;
+    if (n_steps <= 0) return B2_OK;
+    if (m->cache_len + n_steps > m->cfg.max_seq_len) {
+        *err = "context length exceeded: " + std::to_string(m->cache_len + n_steps) + " > " +
+               std::to_string(m->cfg.max_seq_len);
+        return B2_ERR_CONTEXT;
+    }
+    if (m->pin_pending) cudaEventSynchronize(m->ev_pin);
+    m->h_pinned[0] = first;
+    cudaMemcpyAsync(m->d_tokens, m->h_pinned, sizeof(int32_t), cudaMemcpyHostToDevice, m->stream);
+    cudaEventRecord(m->ev_pin, m->stream);
+    m->pin_pending = true;
+    cudaMemsetAsync(m->d_done, 0, sizeof(int), m->stream);
+    const int P = kPhasesPerLayer * m->dev.L;
+    for (int i = 0; i < n_steps; i++) {
+        StepArgs a{};
+        a.tok = (i == 0) ? m->d_tokens : m->dev.token;
+        a.pos = m->cache_len + i;
+        a.p_begin = 0;
+        a.p_end = P + 1;
+        a.epoch = ++m->epoch;
+        a.skew = m->wait_skew;
+        m->wait_skew = 0;
+        a.splits = splits_for(m, a.pos + 1);
+        a.out_ids = m->d_out_ids;
+        a.step = i;
+        a.eos = eos;
+        a.done = m->d_done;
+        int rc = launch_decode(m->dev, a, m->grid, m->stream, err);
+        if (rc) return rc;
+    }
+    cudaError_t e = cudaMemcpyAsync(m->h_pinned, m->d_out_ids, sizeof(int32_t) * n_steps, cudaMemcpyDeviceToHost,
+                                    m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) { *err = cudaGetErrorString(e); return B2_ERR_CUDA; }
+    int rc = check_device_status(m, err);
+    if (rc) return rc;
+    // Step i consumed one token at position cache_len + i and produced ids[i].
+    // Predict stops before feeding EOS back (transformer.go:355-357), so the
+    // cache holds the positions of `first` and every emitted id but the last.
+    int k = 0;
+    for (; k < n_steps; k++) {
+        if (eos >= 0 && m->h_pinned[k] == eos) break;
+        out_ids[k] = m->h_pinned[k];
+    }
+    *n_out = k;
+    m->cache_len += (k < n_steps) ? k + 1 : n_steps;
+    return B2_OK;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+namespace {
+
+int fail(std::string* err, int code, const std::string& msg) {
+    *err = msg;
+    return code;
+}
+
+}  // namespace
+
+void b2_free_impl(b2_model* m);
+
+int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std::string* err) {
+    *out = nullptr;
+    b2_load_opts o{};
+    if (opts) o = *opts;
+    if (o.reserved0 > 1) return fail(err, B2_ERR_BAD_ARG, "tensor-parallel degree > 1 is not supported by b2_load");
+    auto m = new b2_model();
+    auto bail = [&](int code, const std::string& msg) {
+        *err = msg;
+        b2_free_impl(m);
+        return code;
+    };
+    int rc = gguf_parse(path, &m->gguf, err);
+    if (rc) { std::string e = *err; return bail(rc, e); }
+    const GgufFile& g = m->gguf;
+    b2_config& c = m->cfg;
+
+    // transformer.go:1350-1421 extractConfig.
+    c.rms_norm_eps = 1e-5f;
+    c.rope_theta = 10000.0f;
+    std::string arch;
+    if (!g.get_str("general.architecture", &arch)) arch = "llama";
+    snprintf(c.arch, sizeof c.arch, "%s", arch.c_str());
+    const std::string pre = arch + ".";
+    uint32_t u;
+    float fv;
+    if (g.get_u32(pre + "embedding_length", &u)) c.hidden_size = (int)u;
+    if (g.get_u32(pre + "feed_forward_length", &u)) c.intermediate_size = (int)u;
+    if (g.get_u32(pre + "block_count", &u)) c.num_layers = (int)u;
+    if (g.get_u32(pre + "attention.head_count", &u)) c.num_heads = (int)u;
+    c.num_kv_heads = g.get_u32(pre + "attention.head_count_kv", &u) ? (int)u : c.num_heads;
+    c.max_seq_len = g.get_u32(pre + "context_length", &u) ? (int)u : 4096;
+    if (g.get_f32(pre + "attention.layer_norm_rms_epsilon", &fv)) c.rms_norm_eps = fv;
+    if (g.get_f32(pre + "rope.freq_base", &fv)) c.rope_theta = fv;
+    c.vocab_size = (int)std::max<int64_t>(0, g.array_len("tokenizer.ggml.tokens"));
+    if (c.num_heads > 0 && c.hidden_size > 0) c.head_dim = c.hidden_size / c.num_heads;
+    if (c.intermediate_size == 0 && c.hidden_size > 0)
+        c.intermediate_size = ((c.hidden_size * 8 / 3) + 255) / 256 * 256;
+    if (c.hidden_size == 0) return bail(B2_ERR_FORMAT, "embedding_length not found in GGUF metadata");
+    if (c.num_layers == 0) return bail(B2_ERR_FORMAT, "block_count not found in GGUF metadata");
+    if (o.num_ctx > 0 && o.num_ctx < c.max_seq_len) c.max_seq_len = o.num_ctx;  // transformer.go:233-235
+    c.bos_id = g.get_u32("tokenizer.ggml.bos_token_id", &u) ? (int)u : 1;      // bpe.go:48,105
+    c.eos_id = g.get_u32("tokenizer.ggml.eos_token_id", &u) ? (int)u : 2;      // bpe.go:49,108
+
+    const int H = c.hidden_size, FF = c.intermediate_size, V = c.vocab_size, L = c.num_layers;
+    const int nh = c.num_heads, nkv = c.num_kv_heads, hd = c.head_dim;
+    const int qd = nh * hd, kvd = nkv * hd;
+    if (V <= 0) return bail(B2_ERR_FORMAT, "tokenizer.ggml.tokens missing: vocab size unknown");
+    if (nkv <= 0 || nh % nkv != 0 || hd % 8 != 0 || H % 32 || FF % 32 || qd % 32)
+        return bail(B2_ERR_UNSUPPORTED_TYPE, "unsupported head geometry (need nh % nkv == 0, head_dim % 8 == 0, widths % 32 == 0)");
+    if (c.max_seq_len <= 0) return bail(B2_ERR_FORMAT, "context length is zero");
+
+    // Tensor checks (transformer.go:1143-1306 reads the same names).
+    auto need = [&](const std::string& name) -> const GgufTensor* { return g.find(name); };
+    const GgufTensor* te = need("token_embd.weight");
+    if (!te) return bail(B2_ERR_FORMAT, "token_embd: tensor \"token_embd.weight\" not found");
+    const uint32_t qt = te->type;
+    if (qt != GGML_Q8_0 && qt != GGML_Q4_0)
+        return bail(B2_ERR_UNSUPPORTED_TYPE, "token_embd.weight must be Q8_0 or Q4_0");
+    auto check_mat = [&](const std::string& name, int cols, int rows, std::string* e) -> bool {
+        const GgufTensor* t = g.find(name);
+        if (!t) { *e = "tensor \"" + name + "\" not found"; return false; }
+        if (t->type != qt) { *e = name + ": all matrices must share one type (Q8_0 or Q4_0)"; return false; }
+        if (t->dims.size() != 2 || (int64_t)t->dims[0] != cols || (int64_t)t->dims[1] != rows) {
+            *e = name + ": unexpected shape";
+            return false;
+        }
+        return true;
+    };
+    std::string e2;
+    if (!check_mat("token_embd.weight", H, V, &e2)) return bail(B2_ERR_FORMAT, e2);
+    const GgufTensor* ow = g.find("output.weight");
+    c.tied_embeddings = ow ? 0 : 1;
+    if (ow && !check_mat("output.weight", H, V, &e2)) return bail(B2_ERR_UNSUPPORTED_TYPE, e2);
+    if (!g.find("output_norm.weight")) return bail(B2_ERR_FORMAT, "output_norm: tensor \"output_norm.weight\" not found");
+    c.has_qkv_bias = g.find("blk.0.attn_q.bias") ? 1 : 0;
+    for (int l = 0; l < L; l++) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        if (!check_mat(p + "attn_q.weight", H, qd, &e2) || !check_mat(p + "attn_k.weight", H, kvd, &e2) ||
+            !check_mat(p + "attn_v.weight", H, kvd, &e2) || !check_mat(p + "attn_output.weight", qd, H, &e2) ||
+            !check_mat(p + "ffn_gate.weight", H, FF, &e2) || !check_mat(p + "ffn_up.weight", H, FF, &e2) ||
+            !check_mat(p + "ffn_down.weight", FF, H, &e2))
+            return bail(B2_ERR_FORMAT, "layer " + std::to_string(l) + ": " + e2);
+        for (const char* nm : {"attn_norm.weight", "ffn_norm.weight"})
+            if (!g.find(p + nm)) return bail(B2_ERR_FORMAT, "layer " + std::to_string(l) + ": tensor \"" + p + nm + "\" not found");
+    }
+    c.weight_type = (int)qt;
+
+    // ---------------------------------------------------------- arena plan
+    const size_t bpb = qt == GGML_Q8_0 ? 34 : 18;
+    const size_t rb_h = H / 32 * bpb, rb_q = qd / 32 * bpb, rb_f = FF / 32 * bpb;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o2 = off;
+        off += up256(bytes + 16);
+        return o2;
+    };
+    std::vector<Region> regions;
+    std::vector<std::pair<std::string, size_t>> small;  // f32 vectors: name -> offset
+    const size_t off_embd = take((size_t)V * rb_h);
+    regions.push_back({"token_embd.weight", off_embd});
+    size_t off_out = off_embd;
+    if (ow) {
+        off_out = take((size_t)V * rb_h);
+        regions.push_back({"output.weight", off_out});
+    }
+    const size_t off_onorm = take((size_t)H * 4);
+    small.push_back({"output_norm.weight", off_onorm});
+    struct LOff { size_t qkv, wo, gu, wd, an, fn, b; };
+    std::vector<LOff> lo(L);
+    for (int l = 0; l < L; l++) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        lo[l].qkv = take((size_t)(qd + 2 * kvd) * rb_h);
+        regions.push_back({p + "attn_q.weight", lo[l].qkv});
+        regions.push_back({p + "attn_k.weight", lo[l].qkv + (size_t)qd * rb_h});
+        regions.push_back({p + "attn_v.weight", lo[l].qkv + (size_t)(qd + kvd) * rb_h});
+        lo[l].wo = take((size_t)H * rb_q);
+        regions.push_back({p + "attn_output.weight", lo[l].wo});
+        lo[l].gu = take((size_t)2 * FF * rb_h);
+        regions.push_back({p + "ffn_gate.weight", lo[l].gu});
+        regions.push_back({p + "ffn_up.weight", lo[l].gu + (size_t)FF * rb_h});
+        lo[l].wd = take((size_t)H * rb_f);
+        regions.push_back({p + "ffn_down.weight", lo[l].wd});
+        lo[l].an = take((size_t)H * 4);
+        small.push_back({p + "attn_norm.weight", lo[l].an});
+        lo[l].fn = take((size_t)H * 4);
+        small.push_back({p + "ffn_norm.weight", lo[l].fn});
+        lo[l].b = 0;
+        if (c.has_qkv_bias) {
+            lo[l].b = take((size_t)(qd + 2 * kvd) * 4);
+            small.push_back({p + "attn_q.bias", lo[l].b});
+            small.push_back({p + "attn_k.bias", lo[l].b + (size_t)qd * 4});
+            small.push_back({p + "attn_v.bias", lo[l].b + (size_t)(qd + kvd) * 4});
+        }
+    }
+    const size_t weight_end = off;
+    const int S = c.max_seq_len;
+    const size_t off_cos = take((size_t)S * (hd / 2) * 4);
+    const size_t off_sin = take((size_t)S * (hd / 2) * 4);
+    const size_t kv_el = o.kv_fp32 ? 4 : 2;
+    const size_t off_k = take((size_t)L * S * kvd * kv_el);
+    const size_t off_v = take((size_t)L * S * kvd * kv_el);
+
+    int dev_count = 0;
+    if (cudaGetDeviceCount(&dev_count) != cudaSuccess || dev_count == 0)
+        return bail(B2_ERR_CUDA, "no CUDA device available (the engine has no CPU fallback)");
+    if (o.device < 0 || o.device >= dev_count) return bail(B2_ERR_BAD_ARG, "device ordinal out of range");
+    m->device = o.device;
+    cudaSetDevice(m->device);
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
+    m->grid = sms;
+
+    const size_t off_x = take((size_t)H * 4);
+    const size_t off_q = take((size_t)qd * 4);
+    const size_t off_attn = take((size_t)qd * 4);
+    const size_t off_part = take((size_t)nh * kMaxSplits * (hd + 2) * 4);
+    const size_t off_hctr = take((size_t)nkv * kBarStride * 4);
+    const size_t off_act = take((size_t)FF * 4);
+    const size_t off_logits = take((size_t)V * 4);
+    const size_t off_bv = take((size_t)m->grid * 4);
+    const size_t off_bi = take((size_t)m->grid * 4);
+    const size_t off_tok = take(4);
+    const size_t off_bar = take((size_t)(kPhasesPerLayer * L + 2) * kBarStride * 4);
+    const size_t off_err = take(4);
+    const size_t off_toks = take((size_t)S * 4);
+    const size_t off_ids = take((size_t)S * 4);
+    const size_t off_done = take(4);
+    const size_t off_layers = take(sizeof(LayerDev) * L);
+    m->arena_bytes = off;
+
+    if (dev_malloc(&m->arena, m->arena_bytes) != 0) {
+        m->arena = nullptr;
+        return bail(B2_ERR_OOM, "device allocation of " + std::to_string(m->arena_bytes) + " bytes failed");
+    }
+    uint8_t* A = static_cast<uint8_t*>(m->arena);
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(B2_ERR_CUDA, "stream creation failed");
+    cudaEventCreate(&m->ev0);
+    cudaEventCreate(&m->ev1);
+    cudaEventCreateWithFlags(&m->ev_pin, cudaEventDisableTiming);
+    cudaMemsetAsync(A + weight_end, 0, m->arena_bytes - weight_end, m->stream);
+    if (cudaMallocHost(&m->h_pinned, sizeof(int32_t) * std::max(S, 16)) != cudaSuccess ||
+        cudaMallocHost(&m->h_logits, sizeof(float) * V) != cudaSuccess)
+        return bail(B2_ERR_OOM, "pinned host allocation failed");
+
+    // ---------------------------------------------------------- upload
+    FILE* f = fopen(path, "rb");
+    if (!f) return bail(B2_ERR_IO, std::string("open model file: ") + path);
+    const size_t stage_bytes = 64u << 20;
+    uint8_t* stage[2] = {nullptr, nullptr};
+    if (cudaMallocHost(&stage[0], stage_bytes) != cudaSuccess || cudaMallocHost(&stage[1], stage_bytes) != cudaSuccess) {
+        fclose(f);
+        if (stage[0]) cudaFreeHost(stage[0]);
+        return bail(B2_ERR_OOM, "pinned staging allocation failed");
+    }
+    cudaEvent_t sev[2];
+    cudaEventCreate(&sev[0]);
+    cudaEventCreate(&sev[1]);
+    bool sev_used[2] = {false, false};
+    int which = 0;
+    bool io_ok = true;
+    // Verbatim block copies: file -> pinned stage -> HBM, double-buffered.
+    for (const Region& r : regions) {
+        const GgufTensor* t = g.find(r.tensor);
+        uint64_t left = t->bytes(), src = g.data_offset + t->offset, dst = r.off;
+        if (fseeko(f, (off_t)src, SEEK_SET) != 0) { io_ok = false; break; }
+        while (left > 0 && io_ok) {
+            const size_t nb = (size_t)std::min<uint64_t>(left, stage_bytes);
+            if (sev_used[which]) cudaEventSynchronize(sev[which]);
+            if (fread(stage[which], 1, nb, f) != nb) { io_ok = false; break; }
+            cudaMemcpyAsync(A + dst, stage[which], nb, cudaMemcpyHostToDevice, m->stream);
+            cudaEventRecord(sev[which], m->stream);
+            sev_used[which] = true;
+            which ^= 1;
+            left -= nb;
+            dst += nb;
+        }
+        if (!io_ok) break;
+        m->tensors[r.tensor] = TensorLoc{A + r.off, t->type, t->elements()};
+    }
+    // Small vectors (norm gains, biases) as fp32; F16/BF16 widened on the host
+    // exactly as gguf.go:510-536 does.
+    std::vector<float> buf;
+    for (const auto& s : small) {
+        if (!io_ok) break;
+        const GgufTensor* t = g.find(s.first);
+        const size_t n = t ? (size_t)t->elements() : 0;
+        const int64_t expect = s.first.find("attn_q.bias") != std::string::npos ? qd
+                             : (s.first.find("attn_k.bias") != std::string::npos || s.first.find("attn_v.bias") != std::string::npos) ? kvd : H;
+        buf.assign(expect, 0.0f);  // an absent optional bias stays zero (transformer.go:632-646)
+        if (t) {
+            if ((int64_t)n != expect) { fclose(f); return bail(B2_ERR_FORMAT, s.first + ": unexpected length"); }
+            std::vector<uint8_t> raw(t->bytes());
+            if (fseeko(f, (off_t)(g.data_offset + t->offset), SEEK_SET) != 0 || fread(raw.data(), 1, raw.size(), f) != raw.size()) {
+                io_ok = false;
+                break;
+            }
+            for (size_t i = 0; i < n; i++) {
+                if (t->type == GGML_F32) memcpy(&buf[i], &raw[i * 4], 4);
+                else if (t->type == GGML_F16) buf[i] = f16_to_f32((uint16_t)(raw[2 * i] | (raw[2 * i + 1] << 8)));
+                else if (t->type == GGML_BF16) { uint32_t bits = (uint32_t)(raw[2 * i] | (raw[2 * i + 1] << 8)) << 16; memcpy(&buf[i], &bits, 4); }
+                else { fclose(f); return bail(B2_ERR_UNSUPPORTED_TYPE, s.first + ": vectors must be F32, F16 or BF16"); }
+            }
+            m->tensors[s.first] = TensorLoc{A + s.second, GGML_F32, n};
+        }
+        cudaMemcpyAsync(A + s.second, buf.data(), buf.size() * 4, cudaMemcpyHostToDevice, m->stream);
+        cudaStreamSynchronize(m->stream);
+    }
+    fclose(f);
+    cudaStreamSynchronize(m->stream);
+    cudaEventDestroy(sev[0]);
+    cudaEventDestroy(sev[1]);
+    cudaFreeHost(stage[0]);
+    cudaFreeHost(stage[1]);
+    if (!io_ok) return bail(B2_ERR_IO, "short read while uploading tensors");
+
+    // RoPE table with the Go formula (transformer.go:939-942): freq in float64
+    // pow rounded to float32, angle in float32, cos/sin in float64 rounded.
+    {
+        std::vector<float> cs((size_t)S * (hd / 2)), sn((size_t)S * (hd / 2));
+        for (int i = 0; i < hd / 2; i++) {
+            const float freq = 1.0f / (float)std::pow((double)c.rope_theta, (double)(2 * i) / (double)hd);
+            for (int p = 0; p < S; p++) {
+                const float ang = (float)p * freq;
+                cs[(size_t)p * (hd / 2) + i] = (float)std::cos((double)ang);
+                sn[(size_t)p * (hd / 2) + i] = (float)std::sin((double)ang);
+            }
+        }
+        cudaMemcpy(A + off_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(A + off_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+    }
+
+    // ---------------------------------------------------------- device view
+    ModelDev& d = m->dev;
+    d.H = H; d.FF = FF; d.V = V; d.L = L; d.nh = nh; d.nkv = nkv; d.hd = hd; d.qd = qd; d.kvd = kvd;
+    d.max_seq = S;
+    d.qtype = (int)qt;
+    d.rb_h = (int)rb_h; d.rb_q = (int)rb_q; d.rb_f = (int)rb_f;
+    d.eps = c.rms_norm_eps;
+    d.kv_fp32 = o.kv_fp32 ? 1 : 0;
+    d.tok_embd = A + off_embd;
+    d.lm_head = A + off_out;
+    d.out_norm = reinterpret_cast<const float*>(A + off_onorm);
+    d.rope_cos = reinterpret_cast<const float*>(A + off_cos);
+    d.rope_sin = reinterpret_cast<const float*>(A + off_sin);
+    d.kcache = A + off_k;
+    d.vcache = A + off_v;
+    d.x = reinterpret_cast<float*>(A + off_x);
+    d.q = reinterpret_cast<float*>(A + off_q);
+    d.attn = reinterpret_cast<float*>(A + off_attn);
+    d.part = reinterpret_cast<float*>(A + off_part);
+    d.head_ctr = reinterpret_cast<unsigned*>(A + off_hctr);
+    d.act = reinterpret_cast<float*>(A + off_act);
+    d.logits = reinterpret_cast<float*>(A + off_logits);
+    d.best_val = reinterpret_cast<float*>(A + off_bv);
+    d.best_idx = reinterpret_cast<int*>(A + off_bi);
+    d.token = reinterpret_cast<int*>(A + off_tok);
+    d.bar = reinterpret_cast<unsigned*>(A + off_bar);
+    d.err = reinterpret_cast<int*>(A + off_err);
+    m->d_tokens = reinterpret_cast<int*>(A + off_toks);
+    m->d_out_ids = reinterpret_cast<int*>(A + off_ids);
+    m->d_done = reinterpret_cast<int*>(A + off_done);
+    m->layers_host.resize(L);
+    for (int l = 0; l < L; l++) {
+        LayerDev& ld = m->layers_host[l];
+        ld.wqkv = A + lo[l].qkv;
+        ld.wo = A + lo[l].wo;
+        ld.wgu = A + lo[l].gu;
+        ld.wd = A + lo[l].wd;
+        ld.attn_norm = reinterpret_cast<const float*>(A + lo[l].an);
+        ld.ffn_norm = reinterpret_cast<const float*>(A + lo[l].fn);
+        ld.bqkv = c.has_qkv_bias ? reinterpret_cast<const float*>(A + lo[l].b) : nullptr;
+    }
+    m->d_layers = reinterpret_cast<LayerDev*>(A + off_layers);
+    cudaMemcpy(m->d_layers, m->layers_host.data(), sizeof(LayerDev) * L, cudaMemcpyHostToDevice);
+    d.layers = m->d_layers;
+
+    // Shared-memory ring geometry.
+    const int grp = nh / nkv;
+    int xs = std::max(std::max(H, FF), qd);
+    xs = std::max(xs, grp * hd * 2 + grp * 64 + 3 * grp + 32);
+    xs = (xs + 31) & ~31;
+    d.xs_floats = xs;
+    const size_t need_slot = std::max(std::max(2 * rb_h + 192, rb_q + 32), rb_f + 32);
+    int slot = std::max<int>(16384, (int)((need_slot + 1023) & ~size_t(1023)));
+    const int budget = 232448 - 128 - xs * 4 - 1024;
+    int ns = budget / slot;
+    if (ns > 16) ns = 16;
+    if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
+    d.slot_bytes = slot;
+    d.nslots = ns;
+
+    c.weight_bytes = (int64_t)weight_end;
+    {
+        int64_t layer = (int64_t)(qd + 2 * kvd) * rb_h + (int64_t)H * rb_q + (int64_t)2 * FF * rb_h + (int64_t)H * rb_f;
+        int64_t smallb = 4 * (2 * (int64_t)H + (c.has_qkv_bias ? (qd + 2 * kvd) : 0));
+        c.stream_bytes_per_token = (int64_t)L * (layer + smallb) + (int64_t)V * rb_h + 4 * (int64_t)H;
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return bail(B2_ERR_CUDA, std::string("CUDA: ") + cudaGetErrorString(e));
+    *out = m;
+    return B2_OK;
+}
+
+void b2_free_impl(b2_model* m) {
+    if (!m) return;
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->arena) cudaFree(m->arena);
+    if (m->h_pinned) cudaFreeHost(m->h_pinned);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
+    if (m->ev0) cudaEventDestroy(m->ev0);
+    if (m->ev1) cudaEventDestroy(m->ev1);
+    if (m->ev_pin) cudaEventDestroy(m->ev_pin);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}

@@ -1,0 +1,84 @@
+// Host-side model object behind the b2_model handle.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <map>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "../../include/b2decode.h"
+#include "dev.cuh"
+#include "gguf.h"
+
+namespace b2 {
+
+struct TensorLoc {
+    void* dev = nullptr;     // device address of the first block / element
+    uint32_t type = 0;       // ggml type as resident (F32 for the small vectors)
+    uint64_t elements = 0;
+};
+
+// PredictStream state (transformer.go:385-442) for the iterator form.
+struct StreamState {
+    bool active = false;
+    b2_sample_opts opts{};
+    std::vector<int32_t> stop;
+    std::vector<int32_t> generated;
+    int max_gen = 0;
+    int emitted = 0;
+    bool have_logits = false;  // prefill done, logits of the last token are current
+    std::mt19937_64 rng;
+};
+
+// Process-wide launch hooks for tests of the failure paths (fault injection
+// on the host: a failing allocation is simulated, nothing faults the GPU).
+extern int (*g_malloc_hook)(void** p, size_t bytes);
+
+}  // namespace b2
+
+struct b2_model {
+    int device = 0;
+    b2::GgufFile gguf;
+    b2_config cfg{};
+    b2::ModelDev dev{};
+    std::vector<b2::LayerDev> layers_host;
+    b2::LayerDev* d_layers = nullptr;
+    void* arena = nullptr;
+    size_t arena_bytes = 0;
+    std::map<std::string, b2::TensorLoc> tensors;
+    cudaStream_t stream = nullptr;
+    int grid = 0;
+    unsigned epoch = 0;
+    unsigned wait_skew = 0;    // test hook: extra arrivals the next launch waits for
+    int cache_len = 0;
+    int* d_tokens = nullptr;   // [max_seq] step inputs
+    int* d_out_ids = nullptr;  // [max_seq] greedy outputs
+    int* d_done = nullptr;     // [1] EOS seen by the device-resident loop
+    int* h_pinned = nullptr;   // pinned staging for token ids (max_seq ints)
+    float* h_logits = nullptr; // pinned staging for logits (vocab floats)
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cudaEvent_t ev_pin = nullptr;  // last H2D copy out of h_pinned
+    bool pin_pending = false;
+    b2::StreamState st;
+};
+
+namespace b2 {
+
+size_t decode_smem_bytes(const ModelDev& m);
+int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err);
+
+// Kernel-level entry points (matvec.cu / attention.cu / model.cu).
+int launch_dequant(const void* src, uint32_t type, uint64_t n, float* dst, cudaStream_t s);
+int launch_embed_mean(const b2_model* m, const int* d_tokens, int n, float* d_out, cudaStream_t s);
+
+// Runs n tokens through the model from the current cache position (prefill
+// when n > 1).  Logits of the last token stay in dev.logits and its argmax in
+// dev.token.  Returns B2_* codes.
+int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err);
+// Device-resident greedy loop; see b2_decode_greedy.
+int run_greedy(b2_model* m, int32_t first, int n_steps, int32_t eos, int32_t* out_ids, int32_t* n_out,
+               std::string* err);
+int check_device_status(b2_model* m, std::string* err);
+
+}  // namespace b2

@@ -1,0 +1,192 @@
+/*
+ * b2decode — B200 (sm_100a) decode engine for GGUF Q8_0 / Q4_0 LLaMA/Qwen2
+ * models, a drop-in for the per-token forward pass of the Local-LLM-Pure-Go
+ * engine.
+ *
+ * C ABI: plain pointers and sizes, no C++ or CUDA types.  Every function that
+ * can fail returns 0 on success or a negative B2_ERR_* code; the message of
+ * the last failure on the calling thread is b2_last_error().  No exception or
+ * abort crosses the ABI.  The library owns all device memory of a model.  Host
+ * buffers passed in are read or written only during the call.  Calls on one
+ * b2_model must be serialised by the caller (the Go engine holds one
+ * sync.Mutex per engine, transformer.go:96).
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   Local-LLM-Pure-Go/internal/engine/engine.go:15-39          Engine interface
+ *   Local-LLM-Pure-Go/internal/engine/native/transformer/transformer.go
+ *   Local-LLM-Pure-Go/internal/engine/native/gguf/gguf.go
+ */
+#ifndef B2DECODE_H
+#define B2DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2_OK 0
+#define B2_ERR_IO (-1)               /* file missing or short read */
+#define B2_ERR_FORMAT (-2)           /* bad magic/version, truncated or inconsistent GGUF */
+#define B2_ERR_UNSUPPORTED_TYPE (-3) /* tensor type the engine cannot run */
+#define B2_ERR_OOM (-4)              /* device or host allocation failed */
+#define B2_ERR_CUDA (-5)             /* CUDA runtime error */
+#define B2_ERR_NCCL (-6)             /* collective failure */
+#define B2_ERR_TIMEOUT (-7)          /* a bounded device-side wait gave up */
+#define B2_ERR_BAD_ARG (-8)          /* invalid argument */
+#define B2_ERR_CONTEXT (-9)          /* position beyond the KV-cache capacity */
+#define B2_ERR_NOT_LOADED (-10)      /* model handle is NULL or unloaded */
+
+typedef struct b2_model b2_model;
+
+/* engine.go:42-47 LoadOptions, plus device placement. */
+typedef struct {
+    int32_t num_ctx;    /* LoadOptions.NumCtx: caps context_length when > 0 (transformer.go:233-235) */
+    int32_t device;     /* CUDA device ordinal */
+    int32_t kv_fp32;    /* 0: fp16 KV cache (default); 1: fp32 KV cache as in the Go engine */
+    int32_t reserved0;  /* LoadOptions.NumGPU / tensor-parallel degree; must be 0 or 1 here */
+    int32_t reserved1;
+    int32_t reserved2;
+} b2_load_opts;
+
+/* transformer.go:33-46 ModelConfig, plus what loadWeights derives. */
+typedef struct {
+    char arch[32];
+    int32_t vocab_size;
+    int32_t hidden_size;
+    int32_t intermediate_size;
+    int32_t num_layers;
+    int32_t num_heads;
+    int32_t num_kv_heads;
+    int32_t head_dim;
+    int32_t max_seq_len;       /* min(context_length, num_ctx) */
+    float rms_norm_eps;
+    float rope_theta;
+    int32_t tied_embeddings;   /* 1: lm_head reads token_embd (transformer.go:551-554) */
+    int32_t has_qkv_bias;
+    int32_t weight_type;       /* ggml type of the layer matrices: 8 = Q8_0, 2 = Q4_0 */
+    int32_t bos_id;            /* tokenizer.ggml.bos_token_id (bpe.go:48,105) */
+    int32_t eos_id;            /* tokenizer.ggml.eos_token_id (bpe.go:49,108) */
+    int64_t weight_bytes;      /* bytes of weights resident in HBM */
+    int64_t stream_bytes_per_token; /* algorithmic HBM bytes one B=1 decode token reads */
+} b2_config;
+
+/* Real phase timings (the Go engine reports fixed 1/3 and 2/3 splits,
+ * transformer.go:379-380). */
+typedef struct {
+    int64_t prompt_ns;
+    int64_t eval_ns;
+    int32_t prompt_tokens;
+    int32_t completion_tokens;
+} b2_timings;
+
+/* domain.Options (internal/domain/types.go:142-160) fields used by sample. */
+typedef struct {
+    double temperature;     /* <= 0 means 1.0; greedy when < 0.01 (transformer.go:982-1004) */
+    int32_t top_k;
+    double top_p;
+    double repeat_penalty;  /* applied when > 1 */
+    int32_t num_predict;    /* <= 0 means 256 */
+    uint64_t seed;          /* seed of the engine's uniform generator */
+} b2_sample_opts;
+
+/* ---- model lifecycle (engine.go Load/Unload/ModelInfo/IsLoaded) ---- */
+
+/* transformer.go:215-310 Engine.Load: parse the GGUF, extract the config,
+ * copy every Q8_0/Q4_0 block verbatim into one HBM arena (no host dequant),
+ * allocate the KV cache.  opts may be NULL. */
+int b2_load(const char* gguf_path, const b2_load_opts* opts, b2_model** out);
+/* transformer.go:312-322 Unload. NULL is ignored. */
+void b2_free(b2_model* m);
+int b2_get_config(const b2_model* m, b2_config* out);
+/* Message of the last failure on this thread ("" if none). */
+const char* b2_last_error(void);
+
+/* ---- forward pass ---- */
+
+/* transformer.go:742-749 resetCache. */
+int b2_reset(b2_model* m);
+/* Number of cached positions (kvCache.Len, transformer.go:88-92). */
+int b2_cache_len(const b2_model* m, int32_t* len_out);
+
+/* transformer.go:519-557 forward: run n tokens (prefill when n > 1) from the
+ * current cache position; write the vocab_size logits of the last token to
+ * logits_out (may be NULL). */
+int b2_forward(b2_model* m, const int32_t* tokens, int32_t n, float* logits_out);
+/* forward followed by argmax (transformer.go:1038-1046, first maximum wins)
+ * computed on the device. */
+int b2_forward_argmax(b2_model* m, const int32_t* tokens, int32_t n, int32_t* next_out);
+/* Device-resident greedy loop: feed `first`, then each argmax, n_steps times;
+ * stop after emitting eos (eos < 0 disables the stop).  out_ids receives up to
+ * n_steps ids, *n_out how many (the eos id itself is not emitted, as in
+ * Predict, transformer.go:355-357). */
+int b2_decode_greedy(b2_model* m, int32_t first, int32_t n_steps, int32_t eos, int32_t* out_ids,
+                     int32_t* n_out);
+
+/* ---- engine loop (engine.go Predict / PredictStream on token ids) ---- */
+
+/* transformer.go:325-382 Predict: reset, prepend BOS, prefill, then up to
+ * num_predict steps of forward + sample, stopping at EOS or at any id in
+ * stop_ids (the token-id form of isStopToken, transformer.go:1430-1437).
+ * Greedy runs device-resident; otherwise logits are sampled on the host
+ * exactly as sample() does (transformer.go:981-1036). */
+int b2_predict(b2_model* m, const int32_t* prompt, int32_t n_prompt, const b2_sample_opts* opts,
+               const int32_t* stop_ids, int32_t n_stop, int32_t* out_ids, int32_t max_out, int32_t* n_out,
+               b2_timings* timings);
+/* transformer.go:385-442 PredictStream as an iterator: begin resets and
+ * prefills; each next call yields one token id or done=1 (EOS, stop id or
+ * num_predict reached). */
+int b2_stream_begin(b2_model* m, const int32_t* prompt, int32_t n_prompt, const b2_sample_opts* opts,
+                    const int32_t* stop_ids, int32_t n_stop);
+int b2_stream_next(b2_model* m, int32_t* token_out, int32_t* done_out);
+
+/* transformer.go:981-1036 sample() on host logits (modified in place), with
+ * the caller's uniform r in [0,1) for the multinomial draw. */
+int32_t b2_sample_logits(float* logits, int32_t n, const b2_sample_opts* opts, const int32_t* generated,
+                         int32_t n_generated, float r);
+
+/* transformer.go:445-490 Embed: mean of the token_embd rows of the ids,
+ * L2-normalised, written to out[hidden_size]. */
+int b2_embed(b2_model* m, const int32_t* tokens, int32_t n, float* out);
+
+/* ---- debug / kernel-level entry points ---- */
+
+/* gguf.go:491-508 Dequantize of one named tensor, decoded on the device from
+ * the resident blocks (Q4_0 in the ggml element order).  n = capacity of out
+ * in floats; returns 0 and writes *n_out elements. */
+int b2_dequant_tensor(const b2_model* m, const char* name, float* out, int64_t n, int64_t* n_out);
+
+/* transformer.go:810-865 matVecMulQ8Chunk over all rows, on the device:
+ * y[r] = sum_b d_b * sum_j q_bj * x[32b+j].  w, x, y are DEVICE pointers
+ * (GGUF block rows, fp32).  qtype 8 = Q8_0, 2 = Q4_0 (ggml layout).
+ * stream is a cudaStream_t (NULL = legacy default stream). */
+int b2_matvec(int32_t qtype, const void* w, const float* x, float* y, int32_t rows, int32_t cols,
+              void* stream);
+
+/* transformer.go:663-685 attention of one query token per sequence over an
+ * fp16 KV cache, split over the context with a log-sum-exp merge.
+ * q [batch][nh*hd] fp32; k, v [batch][ctx][nkv*hd] fp16 (binary16 bits);
+ * out [batch][nh*hd] fp32.  DEVICE pointers. */
+int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
+                        int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream);
+
+/* Device-side error code of the last launch on this model (B2_ERR_TIMEOUT
+ * after a bounded wait gave up), 0 if none; clears it. */
+int b2_device_status(b2_model* m);
+
+/* The cudaStream_t every launch of this model is issued on (for timing with
+ * CUDA events on the launching stream).  No reference counterpart. */
+void* b2_stream_handle(const b2_model* m);
+
+/* Test hook for failure detection without a GPU fault: the next decode launch
+ * waits for `skew` more grid arrivals than will ever come, so its bounded
+ * waits run out (about 2 s) and it reports B2_ERR_TIMEOUT through
+ * b2_device_status while the context stays usable.  0 disables.  No
+ * reference counterpart. */
+int b2_debug_wait_skew(b2_model* m, int32_t skew);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
