@@ -96,6 +96,7 @@ SIGNATURES = {
     "b2_attention_decode": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_device_status": (C.c_int, [_P]),
     "b2_stream_handle": (_P, [_P]),
+    "b2_trace_step": (C.c_int, [_P, _i32, C.POINTER(_i64), _i64, _i32p, _i32p]),
     "b2_debug_wait_skew": (C.c_int, [_P, _i32]),
 }
 
@@ -229,6 +230,16 @@ class Model:
 
     def device_status(self) -> int:
         return lib().b2_device_status(self._h)
+
+    def trace_step(self, token: int) -> np.ndarray:
+        """[phases, 6, ctas] globaltimer stamps (ns) of one decode step."""
+        P = 5 * self.cfg["num_layers"] + 1
+        cap = P * 6 * 1024
+        out = np.zeros(cap, dtype=np.int64)
+        npz, nc = C.c_int32(), C.c_int32()
+        _check(lib().b2_trace_step(self._h, int(token), out.ctypes.data_as(C.POINTER(_i64)), cap, C.byref(npz),
+                                   C.byref(nc)))
+        return out[: npz.value * 6 * nc.value].reshape(npz.value, 6, nc.value)
 
     def stream_handle(self) -> int:
         return lib().b2_stream_handle(self._h) or 0

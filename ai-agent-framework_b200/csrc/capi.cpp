@@ -413,6 +413,26 @@ int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, fl
     return ret(rc, err);
 }
 
+int b2_trace_step(b2_model* m, int32_t token, int64_t* out_ns, int64_t cap, int32_t* n_phases, int32_t* n_ctas) {
+    if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
+    if (!out_ns || !n_phases || !n_ctas) return ret(B2_ERR_BAD_ARG, "null argument");
+    const int P = b2::kPhasesPerLayer * m->dev.L + 1;
+    const int64_t need = (int64_t)P * b2::kTraceSlots * m->grid;
+    *n_phases = P;
+    *n_ctas = m->grid;
+    if (cap < need) return ret(B2_ERR_BAD_ARG, "trace buffer too small: need " + std::to_string(need));
+    std::string err;
+    unsigned long long* d = nullptr;
+    if (!cuda_ok(cudaMalloc(&d, need * sizeof(int64_t)), &err)) return ret(B2_ERR_OOM, err);
+    cudaMemsetAsync(d, 0, need * sizeof(int64_t), m->stream);
+    int rc = b2::run_traced_step(m, token, d, &err);
+    if (!rc && !cuda_ok(cudaMemcpyAsync(out_ns, d, need * sizeof(int64_t), cudaMemcpyDeviceToHost, m->stream), &err))
+        rc = B2_ERR_CUDA;
+    if (!rc) rc = sync_and_check(m, &err);
+    cudaFree(d);
+    return ret(rc, err);
+}
+
 void* b2_stream_handle(const b2_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
 
 int b2_debug_wait_skew(b2_model* m, int32_t skew) {

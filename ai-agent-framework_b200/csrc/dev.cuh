@@ -8,25 +8,33 @@
 namespace b2 {
 
 // One decode token is a fixed sequence of phases; phase p of layer l is
-// 5*l + k with k below, and the lm_head phase is 5*L.  Each phase is a unit of
-// work split over all CTAs; a phase may start only when the previous one is
-// complete everywhere (grid barrier), except that weight bytes of later phases
-// stream into shared memory ahead of time.
+// 5*l + k with k below, and the lm_head phase is 5*L.  Each phase is split
+// over all CTAs.  Phases hand their outputs to the next phase through "LL"
+// words in global memory: 8 bytes = {fp32 value, 32-bit tag}, written with
+// one 8-byte store, so a reader that sees the expected tag also sees the
+// value.  Polling the data itself is the synchronisation; there is no grid
+// barrier.  Weight bytes of later phases stream into shared memory ahead of
+// time because they never depend on activations.
 enum PhaseKind : int {
     PH_QKV = 0,     // rmsnorm(x) -> [Wq|Wk|Wv] rows, bias, RoPE, KV-cache append
     PH_ATTN = 1,    // GQA attention of the new query over the cache, split over context
-    PH_WO = 2,      // attn_out -> Wo rows, residual add into x
+    PH_WO = 2,      // merge attention splits -> Wo rows, residual add
     PH_GATEUP = 3,  // rmsnorm(x) -> gate & up rows, SwiGLU -> act
-    PH_DOWN = 4,    // act -> Wd rows, residual add into x
+    PH_DOWN = 4,    // act -> Wd rows, residual add
     PH_LMHEAD = 5,  // rmsnorm(x) -> lm_head rows, logits + argmax
     PH_MATVEC = 6,  // plain y = W x (kernel-level entry point)
 };
 
 constexpr int kPhasesPerLayer = 5;
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 12;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);  // warp 0 = producer
-constexpr int kBarStride = 32;                        // counters 128 B apart
-constexpr int kMaxSplits = 16;                        // attention context splits per KV head
+constexpr int kMaxSplits = 8;                         // attention context splits per KV head
+constexpr int kAttnTile = 64;                         // positions per attention tile
+constexpr int kMaxOwnRows = 64;                       // residual rows one CTA keeps (H / grid)
+constexpr int kMaxQkvRows = 128;                      // QKV rows one CTA computes ((qd + 2*kvd) / grid)
+// Phase trace slots: consumer phase start, input ready, input staged, work
+// done; producer first and last weight copy issued (globaltimer ns).
+constexpr int kTraceSlots = 6;
 
 struct LayerDev {
     const uint8_t* wqkv;  // [(qd + 2*kvd) rows][rb_h]: Wq rows, then Wk, then Wv
@@ -53,18 +61,17 @@ struct ModelDev {
     void* kcache;             // [L][max_seq][kvd] fp16 or fp32
     void* vcache;
     const LayerDev* layers;   // device array [L]
-    // activations and scratch (device)
-    float* x;                 // [H] residual stream
-    float* q;                 // [qd]
-    float* attn;              // [qd] merged attention output
-    float* part;              // [nh][kMaxSplits][hd + 2] split partials (o, m, l)
-    unsigned* head_ctr;       // [nkv * kBarStride] split arrival counters
-    float* act;               // [FF]
+    // phase hand-off buffers of LL words (uint2 = {value bits, tag})
+    uint2* ll_x1;             // [H]   x after the attention residual
+    uint2* ll_x2;             // [H]   x after the FFN residual
+    uint2* ll_qkv;            // [qd + 2*kvd] q, k (after RoPE), v of the new token
+    uint2* ll_part;           // [nh][kMaxSplits][hd + 2] attention split partials (o, m, l)
+    uint2* ll_act;            // [FF]  SwiGLU output
     float* logits;            // [V]
     float* best_val;          // [grid] argmax partials
     int* best_idx;
     int* token;               // [1] last argmax
-    unsigned* bar;            // [(5L+1) * kBarStride] phase arrival counters
+    unsigned* am_ctr;         // [1] argmax arrivals (self-resetting)
     int* err;                 // device error flag (B2_ERR_* codes)
 };
 
@@ -73,13 +80,14 @@ struct StepArgs {
     const int* tok;      // device pointer to this step's input token
     int pos;             // cache position written by this step
     int p_begin, p_end;  // phase range to run
-    unsigned epoch;      // arrival target multiplier for this launch
-    unsigned skew;       // added to every wait target (test hook; 0 normally)
+    unsigned epoch;      // launch number: LL tags are epoch * 256 + layer + 1
+    unsigned skew;       // added to every awaited tag (test hook; 0 normally)
     int splits;          // attention context splits per KV head
     int* out_ids;        // argmax also written to out_ids[step] when non-null
     int step;
     int eos;             // with done: an argmax equal to eos sets *done
     int* done;           // device flag; a launch that finds it set does no work
+    unsigned long long* trace;  // [phases][kTraceSlots][grid] timestamps, or null
     // PH_MATVEC only
     const uint8_t* mv_w;
     const float* mv_x;
@@ -169,6 +177,66 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
+}
+
+
+// ---- LL words: {fp32 value, tag} in one 8-byte store -----------------------
+__device__ __forceinline__ void ll_store(uint2* p, float v, unsigned tag) {
+    asm volatile("st.relaxed.gpu.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
+                 : "memory");
+}
+// Two adjacent LL words with one 16-byte store (p 16-byte aligned).
+__device__ __forceinline__ void ll_store2(uint2* p, float v0, float v1, unsigned tag) {
+    asm volatile("st.relaxed.gpu.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(v0)), "r"(tag),
+                 "r"(__float_as_uint(v1)), "r"(tag)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ll_load2(const uint2* p) {
+    uint4 r;
+    asm volatile("ld.relaxed.gpu.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+
+// ---- packed fp32x2 arithmetic (sm_100a) -------------------------------------
+__device__ __forceinline__ unsigned long long f2_pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// Four bytes -> two exact float pairs via the 2^23 magic: the byte placed in
+// the low mantissa byte of 0x4B000000 is the float 2^23 + byte.  sub is the
+// pair (2^23 + 128) for int8 after ^0x80, or (2^23 + 8) for Q4_0 nibbles.
+__device__ __forceinline__ void bytes_to_f2(uint32_t u, unsigned long long sub, unsigned long long& p01,
+                                            unsigned long long& p23) {
+    p01 = f2_add(f2_pack(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440)),
+                         __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441))), sub);
+    p23 = f2_add(f2_pack(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442)),
+                         __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443))), sub);
 }
 
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }

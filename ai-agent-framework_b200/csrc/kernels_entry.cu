@@ -190,9 +190,9 @@ int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows,
     const int rb = cols / 32 * bpb;
     m.xs_floats = (cols + 31) & ~31;
     const int need = rb + 32;
-    const int slot = std::max(16384, (need + 1023) & ~1023);
-    int ns = (232448 - 128 - m.xs_floats * 4 - 1024) / slot;
-    if (ns > 16) ns = 16;
+    const int slot = std::max(8192, (need + 1023) & ~1023);
+    int ns = (232448 - 128 - m.xs_floats * 4 - kMaxOwnRows * 4 - 3 * kMaxQkvRows * 4 - 1024) / slot;
+    if (ns > 32) ns = 32;
     if (ns < 2) {
         *err = "matrix rows too wide for the shared-memory ring";
         return B2_ERR_BAD_ARG;

@@ -147,9 +147,12 @@ int check_device_status(b2_model* m, std::string* err) {
     return B2_OK;
 }
 
+// Attention context splits per KV head: one 32-position tile per split while
+// the merge buffer allows it (more splits = more CTAs working, shorter
+// critical path), capped by the grid.
 static int splits_for(const b2_model* m, int ctx) {
-    int s = (ctx + 63) / 64;
-    int cap = std::max(1, std::min(kMaxSplits, m->grid / std::max(1, m->dev.nkv)));
+    int s = (ctx + kAttnTile - 1) / kAttnTile;
+    int cap = std::max(1, std::min(m->max_splits, m->grid / std::max(1, m->dev.nkv)));
     return std::max(1, std::min(s, cap));
 }
 
@@ -182,6 +185,30 @@ int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err)
         if (rc) return rc;
     }
     m->cache_len += n;
+    return B2_OK;
+}
+
+int run_traced_step(b2_model* m, int32_t token, unsigned long long* d_trace, std::string* err) {
+    if (m->cache_len + 1 > m->cfg.max_seq_len) {
+        *err = "context length exceeded";
+        return B2_ERR_CONTEXT;
+    }
+    if (m->pin_pending) cudaEventSynchronize(m->ev_pin);
+    m->h_pinned[0] = token;
+    cudaMemcpyAsync(m->d_tokens, m->h_pinned, sizeof(int32_t), cudaMemcpyHostToDevice, m->stream);
+    cudaEventRecord(m->ev_pin, m->stream);
+    m->pin_pending = true;
+    StepArgs a{};
+    a.tok = m->d_tokens;
+    a.pos = m->cache_len;
+    a.p_begin = 0;
+    a.p_end = kPhasesPerLayer * m->dev.L + 1;
+    a.epoch = ++m->epoch;
+    a.splits = splits_for(m, a.pos + 1);
+    a.trace = d_trace;
+    int rc = launch_decode(m->dev, a, m->grid, m->stream, err);
+    if (rc) return rc;
+    m->cache_len += 1;
     return B2_OK;
 }
 
@@ -404,17 +431,16 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
     m->grid = sms;
 
-    const size_t off_x = take((size_t)H * 4);
-    const size_t off_q = take((size_t)qd * 4);
-    const size_t off_attn = take((size_t)qd * 4);
-    const size_t off_part = take((size_t)nh * kMaxSplits * (hd + 2) * 4);
-    const size_t off_hctr = take((size_t)nkv * kBarStride * 4);
-    const size_t off_act = take((size_t)FF * 4);
+    const size_t off_llx1 = take((size_t)H * 8);
+    const size_t off_llx2 = take((size_t)H * 8);
+    const size_t off_llqkv = take((size_t)(qd + 2 * kvd) * 8);
+    const size_t off_llpart = take((size_t)nh * kMaxSplits * (hd + 2) * 8);
+    const size_t off_llact = take((size_t)FF * 8);
     const size_t off_logits = take((size_t)V * 4);
     const size_t off_bv = take((size_t)m->grid * 4);
     const size_t off_bi = take((size_t)m->grid * 4);
     const size_t off_tok = take(4);
-    const size_t off_bar = take((size_t)(kPhasesPerLayer * L + 2) * kBarStride * 4);
+    const size_t off_amctr = take(4);
     const size_t off_err = take(4);
     const size_t off_toks = take((size_t)S * 4);
     const size_t off_ids = take((size_t)S * 4);
@@ -539,17 +565,16 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.rope_sin = reinterpret_cast<const float*>(A + off_sin);
     d.kcache = A + off_k;
     d.vcache = A + off_v;
-    d.x = reinterpret_cast<float*>(A + off_x);
-    d.q = reinterpret_cast<float*>(A + off_q);
-    d.attn = reinterpret_cast<float*>(A + off_attn);
-    d.part = reinterpret_cast<float*>(A + off_part);
-    d.head_ctr = reinterpret_cast<unsigned*>(A + off_hctr);
-    d.act = reinterpret_cast<float*>(A + off_act);
+    d.ll_x1 = reinterpret_cast<uint2*>(A + off_llx1);
+    d.ll_x2 = reinterpret_cast<uint2*>(A + off_llx2);
+    d.ll_qkv = reinterpret_cast<uint2*>(A + off_llqkv);
+    d.ll_part = reinterpret_cast<uint2*>(A + off_llpart);
+    d.ll_act = reinterpret_cast<uint2*>(A + off_llact);
     d.logits = reinterpret_cast<float*>(A + off_logits);
     d.best_val = reinterpret_cast<float*>(A + off_bv);
     d.best_idx = reinterpret_cast<int*>(A + off_bi);
     d.token = reinterpret_cast<int*>(A + off_tok);
-    d.bar = reinterpret_cast<unsigned*>(A + off_bar);
+    d.am_ctr = reinterpret_cast<unsigned*>(A + off_amctr);
     d.err = reinterpret_cast<int*>(A + off_err);
     m->d_tokens = reinterpret_cast<int*>(A + off_toks);
     m->d_out_ids = reinterpret_cast<int*>(A + off_ids);
@@ -569,20 +594,37 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     cudaMemcpy(m->d_layers, m->layers_host.data(), sizeof(LayerDev) * L, cudaMemcpyHostToDevice);
     d.layers = m->d_layers;
 
-    // Shared-memory ring geometry.
+    // Shared-memory geometry: the ring of weight slots plus one staging area
+    // (xs) that holds, one phase at a time, the phase input vector, the
+    // attention scratch (q, o, scores, K/V tiles), or the Wo input plus all
+    // attention split partials being merged.
     const int grp = nh / nkv;
-    int xs = std::max(std::max(H, FF), qd);
-    xs = std::max(xs, grp * hd * 2 + grp * 64 + 3 * grp + 32);
-    xs = (xs + 31) & ~31;
-    d.xs_floats = xs;
+    const int attn_need = grp * hd * 2 + grp * kAttnTile + 3 * grp + 4 + kAttnTile * (hd + 4) + kAttnTile * hd + 32;
+    const int base_xs = std::max(std::max(std::max(H, FF), qd), attn_need);
     const size_t need_slot = std::max(std::max(2 * rb_h + 192, rb_q + 32), rb_f + 32);
-    int slot = std::max<int>(16384, (int)((need_slot + 1023) & ~size_t(1023)));
-    const int budget = 232448 - 128 - xs * 4 - 1024;
-    int ns = budget / slot;
-    if (ns > 16) ns = 16;
+    const int slot = std::max<int>(8192, (int)((need_slot + 1023) & ~size_t(1023)));
+    auto ring_slots = [&](int xs_f) {
+        const int budget = 232448 - 128 - xs_f * 4 - kMaxOwnRows * 4 - 3 * kMaxQkvRows * 4 - 1024;
+        return std::min(32, budget / slot);
+    };
+    const int merge_full = qd + nh * kMaxSplits * (hd + 2);
+    int xs = base_xs, max_splits;
+    if (ring_slots(std::max(base_xs, merge_full)) >= 2 * kConsumerWarps) {
+        xs = std::max(base_xs, merge_full);
+        max_splits = kMaxSplits;
+    } else {
+        max_splits = std::max(1, std::min(kMaxSplits, (base_xs - qd) / (nh * (hd + 2))));
+    }
+    xs = (xs + 31) & ~31;
+    const int ns = ring_slots(xs);
     if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
+    if ((H + m->grid - 1) / m->grid > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
+    if (2 * (((qd + 2 * kvd) / 2 + m->grid - 1) / m->grid) > kMaxQkvRows)
+        return bail(B2_ERR_UNSUPPORTED_TYPE, "attention projection too large for one GPU");
+    d.xs_floats = xs;
     d.slot_bytes = slot;
     d.nslots = ns;
+    m->max_splits = max_splits;
 
     c.weight_bytes = (int64_t)weight_end;
     {

@@ -50,6 +50,7 @@ struct b2_model {
     cudaStream_t stream = nullptr;
     int grid = 0;
     unsigned epoch = 0;
+    int max_splits = 1;        // attention splits the merge buffer can hold
     unsigned wait_skew = 0;    // test hook: extra arrivals the next launch waits for
     int cache_len = 0;
     int* d_tokens = nullptr;   // [max_seq] step inputs
@@ -80,5 +81,7 @@ int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err)
 int run_greedy(b2_model* m, int32_t first, int n_steps, int32_t eos, int32_t* out_ids, int32_t* n_out,
                std::string* err);
 int check_device_status(b2_model* m, std::string* err);
+// One decode step (with lm_head) that records the phase trace into d_trace.
+int run_traced_step(b2_model* m, int32_t token, unsigned long long* d_trace, std::string* err);
 
 }  // namespace b2

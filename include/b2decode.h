@@ -175,6 +175,15 @@ int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, fl
  * after a bounded wait gave up), 0 if none; clears it. */
 int b2_device_status(b2_model* m);
 
+/* Phase timeline of one decode step (profiling): runs `token` at the current
+ * position like b2_forward_argmax and records globaltimer stamps (ns) for
+ * every phase, slot and CTA into out_ns[phase][6][cta]: slots 0-3 = consumer
+ * wait start, wait done, input staged, work done; 4-5 = producer first and
+ * last weight copy issued (0 when the phase has no weights).  cap is the
+ * capacity of out_ns in elements.  No reference counterpart (the Go engine
+ * only logs durations, transformer.go:305-308). */
+int b2_trace_step(b2_model* m, int32_t token, int64_t* out_ns, int64_t cap, int32_t* n_phases, int32_t* n_ctas);
+
 /* The cudaStream_t every launch of this model is issued on (for timing with
  * CUDA events on the launching stream).  No reference counterpart. */
 void* b2_stream_handle(const b2_model* m);
