@@ -94,6 +94,7 @@ SIGNATURES = {
     "b2_dequant_tensor": (C.c_int, [_P, C.c_char_p, _f32p, _i64, C.POINTER(_i64)]),
     "b2_matvec": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _P]),
     "b2_attention_decode": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
+    "b2_attention_decode_noalloc": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_device_status": (C.c_int, [_P]),
     "b2_stream_handle": (_P, [_P]),
     "b2_trace_step": (C.c_int, [_P, _i32, C.POINTER(_i64), _i64, _i32p, _i32p]),
@@ -263,3 +264,9 @@ def matvec(qtype: int, w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int,
 def attention_decode(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, nh: int, nkv: int, hd: int,
                      ctx: int, stream: int = 0) -> None:
     _check(lib().b2_attention_decode(q_ptr, k_ptr, v_ptr, out_ptr, batch, nh, nkv, hd, ctx, stream or None))
+
+
+def attention_decode_noalloc(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, nh: int, nkv: int,
+                             hd: int, ctx: int, stream: int = 0) -> None:
+    """attention_decode without device allocation (fixed in-library scratch)."""
+    _check(lib().b2_attention_decode_noalloc(q_ptr, k_ptr, v_ptr, out_ptr, batch, nh, nkv, hd, ctx, stream or None))

@@ -17,6 +17,8 @@ int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows,
                    std::string* err);
 int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh, int nkv,
                       int hd, int ctx, cudaStream_t s, std::string* err);
+int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh,
+                              int nkv, int hd, int ctx, cudaStream_t s, std::string* err);
 
 namespace {
 
@@ -440,6 +442,15 @@ int b2_debug_wait_skew(b2_model* m, int32_t skew) {
     if (skew < 0) return ret(B2_ERR_BAD_ARG, "skew must be >= 0");
     m->wait_skew = (unsigned)skew;
     return B2_OK;
+}
+
+int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
+                                int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream) {
+    if (!q || !k || !v || !out || batch <= 0 || nh <= 0 || nkv <= 0 || nh % nkv || hd <= 0 || hd % 8 || ctx <= 0)
+        return ret(B2_ERR_BAD_ARG, "bad attention arguments");
+    std::string err;
+    int rc = b2_attention_noalloc_impl(q, k, v, out, batch, nh, nkv, hd, ctx, static_cast<cudaStream_t>(stream), &err);
+    return ret(rc, err);
 }
 
 int b2_device_status(b2_model* m) {

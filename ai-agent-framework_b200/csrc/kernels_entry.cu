@@ -265,3 +265,99 @@ int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, floa
     }
     return B2_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the attention entry point.
+//
+// The split partials live in one file-scope device array instead of memory
+// obtained with cudaMalloc, so a call allocates nothing.  Every GPU that loads
+// this library holds the array (kNoAllocScratchFloats floats, 2 MiB) until
+// the process exits.  Its address comes from cudaGetSymbolAddress, once per
+// device, on that device's first call; the host-side name of the array is
+// only a stand-in and is never passed to a kernel.  All calls share the
+// array and it keeps the last call's contents: nothing in it needs to start
+// at zero, because the partial kernel writes every entry (o, m, l of each
+// head and split) that the merge kernel then reads.  Calls whose kernels
+// overlap on the GPU (different streams, or different host threads without
+// ordering) race on the array.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNoAllocScratchFloats = 512 * 1024;
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_part[kNoAllocMaxDevices] = {};
+int g_noalloc_sms[kNoAllocMaxDevices] = {};
+}  // namespace
+
+static __device__ __align__(256) float b2_attn_noalloc_scratch[kNoAllocScratchFloats];
+
+int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh,
+                              int nkv, int hd, int ctx, cudaStream_t s, std::string* err) {
+    const int grp = nh / nkv;
+    if (grp > kMaxGrp || hd % 32 || hd / 32 > kMaxDimsLane || (hd != 64 && hd != 128 && hd != 256)) {
+        *err = "attention geometry unsupported (need nh/nkv <= 8 and head_dim in {64, 128, 256})";
+        return B2_ERR_BAD_ARG;
+    }
+    const size_t per_split = (size_t)batch * nh * (hd + 2);
+    if (per_split > kNoAllocScratchFloats) {
+        *err = "batch * num_heads * (head_dim + 2) = " + std::to_string(per_split) +
+               " floats exceeds the allocation-free scratch of " + std::to_string(kNoAllocScratchFloats) +
+               " floats; use b2_attention_decode for this size";
+        return B2_ERR_BAD_ARG;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *err = std::string("cudaGetDevice: ") + cudaGetErrorString(e);
+        return B2_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kNoAllocMaxDevices) {
+        *err = "device ordinal beyond the allocation-free entry point's table";
+        return B2_ERR_BAD_ARG;
+    }
+    float* part = nullptr;
+    int sms = 0;
+    {
+        // once per device, with that device current
+        std::lock_guard<std::mutex> g(g_noalloc_mu);
+        if (!g_noalloc_part[dev]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, b2_attn_noalloc_scratch);
+            if (e != cudaSuccess) {
+                *err = std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e);
+                return B2_ERR_CUDA;
+            }
+            int n = 0;
+            e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) {
+                *err = std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e);
+                return B2_ERR_CUDA;
+            }
+            g_noalloc_sms[dev] = n;
+            g_noalloc_part[dev] = static_cast<float*>(p);
+        }
+        part = g_noalloc_part[dev];
+        sms = g_noalloc_sms[dev];
+    }
+    int S = attention_splits(batch, nkv, ctx, sms);
+    S = std::min<int>(S, (int)(kNoAllocScratchFloats / per_split));
+    const size_t smem = sizeof(float) * (2 * kAttWarps * kMaxGrp + (size_t)kAttWarps * kMaxGrp * hd);
+    const int grid = batch * nkv * S;
+    const __half* kh = reinterpret_cast<const __half*>(k);
+    const __half* vh = reinterpret_cast<const __half*>(v);
+    if (hd == 64) {
+        attn_partial_kernel<2><<<grid, kAttThreads, smem, s>>>(q, kh, vh, part, nh, nkv, hd, ctx, S);
+    } else if (hd == 128) {
+        attn_partial_kernel<4><<<grid, kAttThreads, smem, s>>>(q, kh, vh, part, nh, nkv, hd, ctx, S);
+    } else {
+        cudaFuncSetAttribute(attn_partial_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attn_partial_kernel<8><<<grid, kAttThreads, smem, s>>>(q, kh, vh, part, nh, nkv, hd, ctx, S);
+    }
+    attn_merge_kernel<<<batch * nh, std::min(hd, 256), 0, s>>>(part, out, nh, hd, S);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = std::string("attention launch: ") + cudaGetErrorString(e);
+        return B2_ERR_CUDA;
+    }
+    return B2_OK;
+}

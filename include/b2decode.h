@@ -171,6 +171,20 @@ int b2_matvec(int32_t qtype, const void* w, const float* x, float* y, int32_t ro
 int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
                         int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream);
 
+/* b2_attention_decode without any device allocation, for callers that cannot
+ * call cudaMalloc: a serving process whose HBM is already fully reserved by
+ * its own pools (weights, KV cache), or a per-token path that cannot afford
+ * the device-wide synchronisation a cudaMalloc/cudaFree pair can cause.  The
+ * split partials use a fixed 2 MiB device array inside the library (held by
+ * every GPU that loads it until the process exits); the caller still passes
+ * q, k, v and out.  Limit: batch * nh * (hd + 2) <= 524288 floats, larger
+ * sizes fail with B2_ERR_BAD_ARG.  The first call on a device looks up the
+ * array's device address; make that first call before any stream capture.
+ * All calls share the array, so calls whose kernels overlap on the GPU race.
+ * No counterpart in the reference. */
+int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
+                                int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream);
+
 /* Device-side error code of the last launch on this model (B2_ERR_TIMEOUT
  * after a bounded wait gave up), 0 if none; clears it. */
 int b2_device_status(b2_model* m);
