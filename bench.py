@@ -49,49 +49,91 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clock and throttle reasons during timing."""
+    """Samples the SM clock and the throttle reasons of this process's GPU
+    every 5 ms through NVML (read-only queries) while the timed region runs;
+    falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
 
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, uuid: str | None):
         self.uuid = uuid
-        self.rows = []
+        self.rows = []  # (sm_mhz, max_mhz, reasons bitmask)
         self.proc = None
+        self.stop = threading.Event()
+        self.t = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            u = pynvml.nvmlDeviceGetUUID(h)
+            u = u.decode() if isinstance(u, bytes) else u
+            if self.uuid is None or u == self.uuid:
+                return pynvml, h
+        raise RuntimeError("GPU not found by NVML")
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+            nv, h = self._nvml_handle()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+
+            def poll():
+                while not self.stop.is_set():
+                    try:
+                        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.rows.append((float(sm), float(mx), int(rs)))
+                    except Exception:
+                        pass
+                    self.stop.wait(0.005)
+
+            self.t = threading.Thread(target=poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            pass
+        try:
+            fields = ("uuid,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                      "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                      "clocks_event_reasons.sw_power_cap")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={fields}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t = threading.Thread(target=self._read_smi, daemon=True)
             self.t.start()
         except Exception:
             self.proc = None
         return self
 
-    def _read(self):
+    def _read_smi(self):
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9 and (self.uuid is None or parts[0] == self.uuid):
-                self.rows.append(parts)
+            if len(parts) >= 7 and (self.uuid is None or parts[0] == self.uuid):
+                try:
+                    mask = sum(bit for k, (_, bit) in enumerate(self.REASONS)
+                               if parts[3 + k].lower().startswith("active"))
+                    self.rows.append((float(parts[1]), float(parts[2]), mask))
+                except ValueError:
+                    pass
 
     def __exit__(self, *a):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if self.t:
+            self.t.join(timeout=5)
 
     def summary(self) -> dict:
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+        sm = [r[0] for r in self.rows]
+        reasons = sorted({name for r in self.rows for name, bit in self.REASONS if r[2] & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(r[1] for r in self.rows),
                 "reasons": reasons, "samples": len(self.rows)}
 
 
@@ -115,11 +157,13 @@ def dist_env():
 
 
 def profile_traffic(kernel: str):
-    """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "decode_kernel_qwen05b.json")
+    """DRAM bytes (read + write) per launch of the decode kernel, from the
+    committed ncu summary's `dram_bytes_per_launch:` line."""
+    p = os.path.join(ROOT, "profiles", "decode_kernel_qwen05b_q8_0.md")
     if os.path.exists(p):
-        d = json.load(open(p))
-        return d.get("dram_bytes_per_launch")
+        for line in open(p):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(line.split(":", 1)[1])
     return None
 
 
