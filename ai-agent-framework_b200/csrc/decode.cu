@@ -9,17 +9,25 @@
 //                    with 1-D TMA bulk copies into a ring of shared-memory
 //                    slots.  Weights never depend on activations, so the
 //                    producer runs ahead across phases, limited by the ring.
-//   warps 1..12      consumers: per phase, gather the phase input from the
-//                    previous phase's LL words (the poll is the load), stage it
-//                    in shared memory with RMSNorm / embedding decode /
-//                    attention-split merge fused in, then dequantise their
-//                    chunks in registers and accumulate in fp32, with the
-//                    phase epilogue fused (bias + RoPE + KV append, residual
-//                    add, SwiGLU, logits + argmax).
+//   warps 1..12      consumers, per phase:
+//                    1. stage: gather the phase input from the previous
+//                       phase's LL words (the poll is the load) into shared
+//                       memory, with RMSNorm / embedding decode / attention
+//                       split merge fused in; the phase constants (norm gains,
+//                       QKV bias, RoPE row) arrive by cp.async during the poll;
+//                    2. rows: each warp dequantises its chunks of the CTA's
+//                       weight rows in registers and leaves the fp32 dot
+//                       products in shared memory (ybuf); nothing else is live
+//                       in this loop, so it runs without register spills;
+//                    3. epilogue, one thread per output: bias + RoPE + KV
+//                       append, SwiGLU, residual add, logits + argmax, and the
+//                       LL stores that hand the outputs to the next phase.
+//                    The attention phase instead runs one (query head,
+//                    context split) per CTA over K/V tiles that cp.async
+//                    copies into shared memory while the CTA polls for q.
 // Each CTA keeps the residual-stream rows it owns (the same rows in every Wo
-// and down phase) in shared memory, so residual adds never touch global
-// memory.  Every wait is bounded (globaltimer) and reports B2_ERR_TIMEOUT
-// through the device error flag instead of hanging.
+// and down phase) in shared memory.  Every wait is bounded (globaltimer) and
+// reports B2_ERR_TIMEOUT through the device error flag instead of hanging.
 #include <cuda_runtime.h>
 
 #include "../../include/b2decode.h"
@@ -74,7 +82,7 @@ __device__ __forceinline__ Geom phase_geom(const ModelDev& m, const StepArgs& a,
             g.w = L.wqkv; g.rb = m.rb_h; g.cols = m.H; g.units = (m.qd + 2 * m.kvd) / 2; g.rpu = 2;
             break;
         case PH_ATTN:
-            g.units = m.nkv * a.splits;
+            g.units = m.nh * a.splits;
             break;
         case PH_WO:
             g.w = L.wo; g.rb = m.rb_q; g.cols = m.qd; g.units = m.H; g.rpu = 1;
@@ -150,21 +158,35 @@ __device__ __forceinline__ bool chunk_wait(uint64_t* bar, uint32_t parity, unsig
 
 __device__ __forceinline__ unsigned ll_tag(unsigned epoch, int layer) { return epoch * 256u + (unsigned)layer + 1u; }
 
+// Result of a gather: whether it completed, and the sum of squares of the
+// gathered values (for RMSNorm) when asked for.
+struct GatherRes {
+    float ss;
+    int ok;
+};
+
 // Gathers LL words src[0 .. n) (n even, src 16-byte aligned) once every word
-// carries `tag`, calling put(i, value).  Each consumer thread polls its own
-// words with 16-byte loads, up to 8 in flight; a word whose tag is stale is
-// simply read again.  Bounded: gives up (returns false, error flag set) after
-// kWaitLimitNs or when another CTA already reported an error.
-template <class Put>
-__device__ __forceinline__ bool ll_gather(const uint2* src, int n, unsigned tag, int ct, int* err, Put put) {
+// carries `tag` and stores the values into shared memory at byte address
+// dst: value i goes to float i (us == 0) or to the dot-loop layout of the
+// phase input (us values per lane unit, nu units; see xs_index).  Each
+// consumer thread polls its own words with 16-byte loads, up to 4 in flight;
+// a word whose tag is stale is simply read again.  Bounded: gives up (ok = 0,
+// error flag set) after kWaitLimitNs or when another CTA already reported an
+// error.  Not inlined: its polling state would otherwise add to the register
+// peak of the whole kernel at every one of its call sites.
+__device__ __noinline__ GatherRes ll_gather_s(const uint2* src, int n, unsigned tag, int* err, uint32_t dst, int us,
+                                              int nu, int want_ss) {
+    const int ct = threadIdx.x - 32;
     const int n2 = n >> 1;
+    const int ul = us == 32 ? 5 : 4;
     uint64_t t0 = 0;
-    for (int base = 0; base < n2; base += kConsumerThreads * 8) {
-        uint4 v[8];
+    float ss = 0.0f;
+    for (int base = 0; base < n2; base += kConsumerThreads * 4) {
+        uint4 v[4];
         for (;;) {
             bool ok = true;
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
+            for (int k = 0; k < 4; k++) {
                 const int i = base + ct + k * kConsumerThreads;
                 if (i < n2) {
                     v[k] = ll_load2(src + 2 * i);
@@ -177,20 +199,30 @@ __device__ __forceinline__ bool ll_gather(const uint2* src, int n, unsigned tag,
             if (t0 == 0) t0 = now;
             if (now - t0 > kWaitLimitNs) {
                 set_err(err, B2_ERR_TIMEOUT);
-                return false;
+                return GatherRes{ss, 0};
             }
-            if (*(volatile int*)err) return false;
+            if (*(volatile int*)err) return GatherRes{ss, 0};
         }
 #pragma unroll
-        for (int k = 0; k < 8; k++) {
+        for (int k = 0; k < 4; k++) {
             const int i = base + ct + k * kConsumerThreads;
             if (i < n2) {
-                put(2 * i, __uint_as_float(v[k].x));
-                put(2 * i + 1, __uint_as_float(v[k].z));
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int j = 2 * i + e;
+                    const float val = __uint_as_float(e ? v[k].z : v[k].x);
+                    int idx = j;
+                    if (us) {
+                        const int u = j >> ul, r = j & (us - 1);
+                        idx = ((r >> 2) * nu + u) * 4 + (r & 3);
+                    }
+                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(dst + 4u * (uint32_t)idx), "f"(val) : "memory");
+                    if (want_ss) ss += val * val;
+                }
             }
         }
     }
-    return true;
+    return GatherRes{ss, 1};
 }
 
 // Shared-memory layout of the phase input: element j of lane unit u (US
@@ -334,6 +366,210 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
     return v > bv || (v == bv && i < bi);
 }
 
+// Sums a0 over the warp into lane 0 and a1 into lane 16 (6 shuffles).
+__device__ __forceinline__ float warp_sum2(float a0, float a1, int lane) {
+    const float t0 = __shfl_xor_sync(0xffffffffu, a0, 16);
+    const float t1 = __shfl_xor_sync(0xffffffffu, a1, 16);
+    float v = (lane & 16) ? a1 + t1 : a0 + t0;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Block-wide (consumer threads) max / sum through warp shuffles and red[].
+__device__ __forceinline__ float block_max(float v, float* red, int cw) {
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0) red[cw] = v;
+    named_bar_sync(1, kConsumerThreads);
+    float r = red[0];
+#pragma unroll
+    for (int w = 1; w < kConsumerWarps; w++) r = fmaxf(r, red[w]);
+    named_bar_sync(1, kConsumerThreads);
+    return r;
+}
+__device__ __forceinline__ float block_sum(float v, float* red, int cw) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) red[cw] = v;
+    named_bar_sync(1, kConsumerThreads);
+    float r = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; w++) r += red[w];
+    named_bar_sync(1, kConsumerThreads);
+    return r;
+}
+
+// Offsets in the constant buffer (floats).
+__device__ __forceinline__ int cb_bias(const ModelDev& m) { return m.H; }
+__device__ __forceinline__ int cb_cos(const ModelDev& m) { return m.H + kMaxQkvRows + 4; }
+__device__ __forceinline__ int cb_sin(const ModelDev& m) { return m.H + kMaxQkvRows + 4 + m.hd / 2; }
+
+// The attention phase, transformer.go:658-685, for one query head over one
+// slice [t0, t1) of the context.  Cached K and V rows of a tile go to shared
+// memory by cp.async; the first tile's copies are issued before the poll for
+// q, so they overlap the QKV phase.  The new position's k and v come from the
+// QKV phase's LL words (its cache stores are not ordered with them).  Scores:
+// one thread per position; weighted V sum: thread (chunk vc, group vg) sums 8
+// dims over positions vg, vg + ngrp, ...; online softmax across tiles.  The
+// result is o / l (one split) or the split partial (o, m, l).  Not inlined,
+// so its tiles and gathers do not raise the kernel's register peak.
+template <bool F32>
+__device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, const uint2* vsrc, const uint8_t* kg,
+                                       const uint8_t* vg, uint32_t gs, int hd, int TP, int t0, int t1, int pos,
+                                       unsigned tag_here, unsigned tag_out, uint2* out, int split_out, int* err,
+                                       uint32_t xs_off, uint32_t red_off, int alive) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int ES = F32 ? 4 : 2;
+    const int ct = threadIdx.x - 32, lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 1;
+    float* xs = reinterpret_cast<float*>(smem + xs_off);
+    float* red = reinterpret_cast<float*>(smem + red_off);
+    const int rowb = hd * ES, KS = rowb + 16;  // K rows padded: no bank conflicts across positions
+    float* aq = xs;                    // [hd] q
+    float* akc = aq + hd;              // [hd] k of the new position
+    float* avc = akc + hd;             // [hd] v of the new position
+    float* ao = avc + hd;              // [hd] running output
+    float* asc = ao + hd;              // [TP] probabilities of the tile
+    float* avred = asc + TP;           // [kConsumerWarps][hd] per-warp V sums
+    uint8_t* ktile = reinterpret_cast<uint8_t*>(avred + kConsumerWarps * hd);  // [TP][KS]
+    uint8_t* vtile = ktile + (size_t)TP * KS;                                   // [TP][rowb]
+    const int pieces = rowb / 16;
+    auto load_tile = [&](int tb, int nt) {
+        for (int i = ct; i < nt * pieces; i += kConsumerThreads) {
+            const int t = i / pieces, c = i - t * pieces;
+            if (tb + t == pos) continue;
+            cp_async16(ktile + (size_t)t * KS + c * 16, kg + (size_t)(tb + t) * gs + c * 16);
+            cp_async16(vtile + (size_t)t * rowb + c * 16, vg + (size_t)(tb + t) * gs + c * 16);
+        }
+        cp_async_commit();
+    };
+    if (t1 > t0) load_tile(t0, min(TP, t1 - t0));
+
+    if (alive) alive = ll_gather_s(qsrc, hd, tag_here, err, smem_u32(aq), 0, 0, 0).ok;
+    if (alive && pos >= t0 && pos < t1) {
+        alive = ll_gather_s(ksrc, hd, tag_here, err, smem_u32(akc), 0, 0, 0).ok;
+        if (alive) alive = ll_gather_s(vsrc, hd, tag_here, err, smem_u32(avc), 0, 0, 0).ok;
+    }
+    for (int i = ct; i < hd; i += kConsumerThreads) ao[i] = 0.0f;
+    cp_async_wait();
+    named_bar_sync(1, kConsumerThreads);
+
+    const float scale = (float)(1.0 / sqrt((double)hd));
+    const int hv = hd / 8, ngrp = kConsumerThreads / hv;
+    const int vc = ct % hv, vgi = ct / hv;
+    float mrun = -INFINITY, lrun = 0.0f;
+    for (int tb = t0; tb < t1; tb += TP) {
+        const int nt = min(TP, t1 - tb);
+        if (tb != t0) {
+            load_tile(tb, nt);
+            cp_async_wait();
+            named_bar_sync(1, kConsumerThreads);
+        }
+        // scores (transformer.go:664-671)
+        float sv = -INFINITY;
+        if (ct < nt) {
+            float d0 = 0.0f, d1 = 0.0f;
+            if (tb + ct == pos) {
+                for (int d = 0; d < hd; d += 2) {
+                    d0 = fmaf(aq[d], akc[d], d0);
+                    d1 = fmaf(aq[d + 1], akc[d + 1], d1);
+                }
+            } else if (F32) {
+                const float4* kr = reinterpret_cast<const float4*>(ktile + (size_t)ct * KS);
+                const float4* q4 = reinterpret_cast<const float4*>(aq);
+                for (int i = 0; i < hd / 4; i++) {
+                    const float4 k = kr[i], q = q4[i];
+                    d0 = fmaf(q.x, k.x, d0);
+                    d1 = fmaf(q.y, k.y, d1);
+                    d0 = fmaf(q.z, k.z, d0);
+                    d1 = fmaf(q.w, k.w, d1);
+                }
+            } else {
+                const uint4* kr = reinterpret_cast<const uint4*>(ktile + (size_t)ct * KS);
+                const float4* q4 = reinterpret_cast<const float4*>(aq);
+                for (int i = 0; i < hd / 8; i++) {
+                    const uint4 ku = kr[i];
+                    const __half2* kh = reinterpret_cast<const __half2*>(&ku);
+                    const float4 qa = q4[2 * i], qb = q4[2 * i + 1];
+                    const float2 f0 = __half22float2(kh[0]), f1 = __half22float2(kh[1]);
+                    const float2 f2 = __half22float2(kh[2]), f3 = __half22float2(kh[3]);
+                    d0 = fmaf(qa.x, f0.x, d0);
+                    d1 = fmaf(qa.y, f0.y, d1);
+                    d0 = fmaf(qa.z, f1.x, d0);
+                    d1 = fmaf(qa.w, f1.y, d1);
+                    d0 = fmaf(qb.x, f2.x, d0);
+                    d1 = fmaf(qb.y, f2.y, d1);
+                    d0 = fmaf(qb.z, f3.x, d0);
+                    d1 = fmaf(qb.w, f3.y, d1);
+                }
+            }
+            sv = (d0 + d1) * scale;
+        }
+        // online softmax (transformer.go:673-677)
+        const float mb = block_max(sv, red, cw);
+        const float mnew = fmaxf(mrun, mb);
+        const float pv = (ct < nt) ? expf(sv - mnew) : 0.0f;
+        if (ct < nt) asc[ct] = pv;
+        const float lb = block_sum(pv, red, cw);  // its barriers also publish asc[]
+        const float corr = (mrun == -INFINITY) ? 0.0f : expf(mrun - mnew);
+        lrun = lrun * corr + lb;
+        mrun = mnew;
+        // weighted V sum (transformer.go:679-685)
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) acc[e] = 0.0f;
+        for (int tl = vgi; tl < nt; tl += ngrp) {
+            const float pt = asc[tl];
+            float vf[8];
+            if (tb + tl == pos) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) vf[e] = avc[vc * 8 + e];
+            } else if (F32) {
+                const float4* vr = reinterpret_cast<const float4*>(vtile + (size_t)tl * rowb + vc * 32);
+                const float4 x0 = vr[0], x1 = vr[1];
+                vf[0] = x0.x; vf[1] = x0.y; vf[2] = x0.z; vf[3] = x0.w;
+                vf[4] = x1.x; vf[5] = x1.y; vf[6] = x1.z; vf[7] = x1.w;
+            } else {
+                const uint4 vu = *reinterpret_cast<const uint4*>(vtile + (size_t)tl * rowb + vc * 16);
+                const __half2* vh = reinterpret_cast<const __half2*>(&vu);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float2 f = __half22float2(vh[e]);
+                    vf[2 * e] = f.x;
+                    vf[2 * e + 1] = f.y;
+                }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[e] = fmaf(pt, vf[e], acc[e]);
+        }
+        // lanes of one warp that share a chunk: lane, lane ^ hv, ...
+        for (int o = hv; o < 32; o <<= 1) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
+        }
+        if (lane < hv) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) avred[cw * hd + lane * 8 + e] = acc[e];
+        }
+        named_bar_sync(1, kConsumerThreads);
+        for (int d = ct; d < hd; d += kConsumerThreads) {
+            float o = ao[d] * corr;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; w++) o += avred[w * hd + d];
+            ao[d] = o;
+        }
+        named_bar_sync(1, kConsumerThreads);
+    }
+    if (!split_out) {
+        for (int d = ct; d < hd; d += kConsumerThreads) ll_store(out + d, ao[d] / lrun, tag_out);
+    } else {
+        // split partial (o unnormalised, m, l), laid out [head][split][hd + 2]
+        for (int i = ct; i < hd + 2; i += kConsumerThreads) {
+            const float v = i < hd ? ao[i] : (i == hd ? mrun : lrun);
+            ll_store(out + i, v, tag_out);
+        }
+    }
+    return alive;
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -344,14 +580,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     extern __shared__ __align__(128) uint8_t smem[];
     const int NS = m.nslots;
     const int SB = m.slot_bytes;
+    const SmemOffsets so = smem_offsets(NS, SB, m.xs_floats, m.ybuf_floats, m.cfloats);
     uint8_t* ring = smem;
-    float* xs = reinterpret_cast<float*>(smem + (size_t)NS * SB + 128);
-    float* xres = xs + m.xs_floats;                       // [kMaxOwnRows] residual rows owned
-    float* qconst = xres + kMaxOwnRows;                   // [3][kMaxQkvRows] bias, cos, sin of the QKV rows
-    uint64_t* full = reinterpret_cast<uint64_t*>(qconst + 3 * kMaxQkvRows);
-    uint64_t* empty = full + NS;
-    float* red = reinterpret_cast<float*>(empty + NS);    // 64 floats
-    int* misc = reinterpret_cast<int*>(red + 64);         // 32 ints
+    float* xs = reinterpret_cast<float*>(smem + so.xs);
+    float* xres = reinterpret_cast<float*>(smem + so.xres);
+    float* ybuf = reinterpret_cast<float*>(smem + so.ybuf);
+    float* cb = reinterpret_cast<float*>(smem + so.cbuf);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + so.full);
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + so.empty);
+    float* red = reinterpret_cast<float*>(smem + so.red);
+    int* misc = reinterpret_cast<int*>(smem + so.misc);
     volatile unsigned* pstop = reinterpret_cast<volatile unsigned*>(misc + 31);  // first chunk not issued
     volatile int* dead = misc + 30;  // set by any consumer thread whose wait failed
 
@@ -420,9 +658,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     const int ct = threadIdx.x - 32;      // consumer thread index
     unsigned gbase = 0;                   // chunk index of the phase's first chunk
     bool alive = true;
-    Best best{-INFINITY, 0x7fffffff};
     const int tok = a.mv_w ? 0 : *a.tok;
     const int own0 = (int)((long long)cta * m.H / grid);  // residual rows [own0, own1)
+    const int own1 = (int)((long long)(cta + 1) * m.H / grid);
     // Consumer barrier that also makes `alive` uniform across the CTA: a
     // failed wait in any thread stops the work of all (warp collectives in
     // the row loop must never run with part of a warp).
@@ -435,264 +673,135 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     for (int p = a.p_begin; p < a.p_end; p++) {
         const Geom g = phase_geom(m, a, p);
         const Split s = cta_split(g, cta, grid, SB);
+        const bool has_rows = s.nchunks > 0;
         const size_t tr = (size_t)(p - a.p_begin) * kTraceSlots;
         if (a.trace && ct == 0) a.trace[(tr + 0) * grid + cta] = global_ns();
-
-        // 1+2. gather the phase input (the LL poll) and stage it in shared memory
         const unsigned tag_here = ll_tag(a.epoch, g.layer) + a.skew;
         const unsigned tag_prev = ll_tag(a.epoch, g.layer - 1) + a.skew;
-        const int nu_h = m.H / US;
-        if (g.kind == PH_QKV || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) {
-            // RMSNorm (transformer.go:922-932) fused into the stage; the norm
-            // gains are fetched before the poll so their latency overlaps it.
+
+        // 1. stage the phase input
+        if (g.kind == PH_QKV && g.layer == 0) {
+            // transformer.go:524-531: the residual stream starts at the embedding
+            for (int j = own0 + ct; j < own1; j += kConsumerThreads) xres[j - own0] = embed_elem(m, tok, j);
+        }
+        if ((g.kind == PH_QKV || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) && has_rows) {
+            // constants first (they land while the poll below waits)
             const float* nw = g.kind == PH_QKV ? m.layers[g.layer].attn_norm
                             : (g.kind == PH_GATEUP ? m.layers[g.layer].ffn_norm : m.out_norm);
-            float wreg[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const int j = ct + k * kConsumerThreads;
-                wreg[k] = (j < m.H) ? __ldg(nw + j) : 0.0f;
-            }
+            for (int i = ct; i < m.H / 4; i += kConsumerThreads) cp_async16(cb + 4 * i, nw + 4 * i);
             if (g.kind == PH_QKV) {
-                // this CTA's QKV epilogue constants (bias, RoPE cos/sin at pos),
-                // loaded while the poll below waits
-                const int row0 = 2 * s.u0, nrow = 2 * s.n;
-                const LayerDev& Ld = m.layers[g.layer];
-                for (int i = ct; i < nrow; i += kConsumerThreads) {
-                    const int row = row0 + i;
-                    qconst[i] = Ld.bqkv ? __ldg(Ld.bqkv + row) : 0.0f;
-                    float c = 1.0f, sn = 0.0f;
-                    if (row < m.qd + m.kvd) {
-                        const int pi = (row % m.hd) >> 1;
-                        c = __ldg(m.rope_cos + (size_t)a.pos * (m.hd / 2) + pi);
-                        sn = __ldg(m.rope_sin + (size_t)a.pos * (m.hd / 2) + pi);
-                    }
-                    qconst[kMaxQkvRows + i] = c;
-                    qconst[2 * kMaxQkvRows + i] = sn;
+                const float* bq = m.layers[g.layer].bqkv;
+                const int r0b = (2 * s.u0) & ~3, r1 = 2 * (s.u0 + s.n);
+                if (bq)
+                    for (int i = ct; i < (r1 - r0b + 3) / 4; i += kConsumerThreads)
+                        cp_async16(cb + cb_bias(m) + 4 * i, bq + r0b + 4 * i);
+                const int hh = m.hd / 2;
+                for (int i = ct; i < hh / 4; i += kConsumerThreads) {
+                    cp_async16(cb + cb_cos(m) + 4 * i, m.rope_cos + (size_t)a.pos * hh + 4 * i);
+                    cp_async16(cb + cb_sin(m) + 4 * i, m.rope_sin + (size_t)a.pos * hh + 4 * i);
                 }
             }
+            cp_async_commit();
+            // RMSNorm (transformer.go:922-932) fused into the stage
+            const int nu_h = m.H / US;
             float ss = 0.0f;
             if (g.kind == PH_QKV && g.layer == 0) {
                 for (int j = ct; j < m.H; j += kConsumerThreads) {
                     const float v = embed_elem(m, tok, j);
                     xs[xs_index<US>(j, nu_h)] = v;
-                    if (j >= own0 && j - own0 < kMaxOwnRows) xres[j - own0] = v;
                     ss += v * v;
                 }
             } else if (alive) {
                 const uint2* src = g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2;
                 const unsigned tg = g.kind == PH_GATEUP ? tag_here : tag_prev;
-                alive = ll_gather(src, m.H, tg, ct, m.err, [&](int j, float v) {
-                    xs[xs_index<US>(j, nu_h)] = v;
-                    ss += v * v;
-                });
+                const GatherRes gr = ll_gather_s(src, m.H, tg, m.err, smem_u32(xs), US, nu_h, 1);
+                alive = gr.ok;
+                ss = gr.ss;
             }
             if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-            ss = warp_sum(ss);
-            if (lane == 0) red[cw] = ss;
-            named_bar_sync(1, kConsumerThreads);
-            float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; w++) tot += red[w];
+            cp_async_wait();
+            const float tot = block_sum(ss, red, cw);  // its barriers also publish cb[]
             const float r = (float)(1.0 / sqrt((double)(tot / (float)m.H) + (double)m.eps));
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const int j = ct + k * kConsumerThreads;
-                if (j < m.H) {
-                    float* px = xs + xs_index<US>(j, nu_h);
-                    *px = *px * r * wreg[k];
-                }
-            }
-            for (int j = ct + 8 * kConsumerThreads; j < m.H; j += kConsumerThreads) {
+            for (int j = ct; j < m.H; j += kConsumerThreads) {
                 float* px = xs + xs_index<US>(j, nu_h);
-                *px = *px * r * __ldg(nw + j);
+                *px = *px * r * cb[j];
             }
-        } else if (g.kind == PH_WO) {
-            // merge the attention splits: o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M)
-            const int S = a.splits, hd = m.hd, W2 = hd + 2;
-            float* part = xs + m.qd;  // [nh][S][hd+2] after the qd outputs
-            if (alive)
-                alive = ll_gather(m.ll_part, m.nh * S * W2, tag_here, ct, m.err,
-                                  [&](int i, float v) { part[i] = v; });
-            if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-            named_bar_sync(1, kConsumerThreads);
+        } else if (g.kind == PH_WO && has_rows) {
             const int nu_q = m.qd / US;
-            for (int i = ct; i < m.qd; i += kConsumerThreads) {
-                const int h = i / hd, d = i % hd;
-                const float* ph = part + (size_t)h * S * W2;
-                float M = -INFINITY;
-                for (int s2 = 0; s2 < S; s2++) M = fmaxf(M, ph[s2 * W2 + hd]);
-                float Ls = 0.0f, o = 0.0f;
-                for (int s2 = 0; s2 < S; s2++) {
-                    const float ms = ph[s2 * W2 + hd];
-                    const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-                    Ls = fmaf(ph[s2 * W2 + hd + 1], w, Ls);
-                    o = fmaf(ph[s2 * W2 + d], w, o);
+            if (a.splits == 1) {
+                if (alive)
+                    alive = ll_gather_s(m.ll_attn, m.qd, tag_here, m.err, smem_u32(xs), US, nu_q, 0).ok;
+                if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+            } else {
+                // merge the context splits: o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M)
+                const int S = a.splits, hd = m.hd, W2 = hd + 2;
+                float* part = xs + m.qd;  // [nh][S][hd+2] after the qd outputs
+                if (alive)
+                    alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0, 0, 0).ok;
+                if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+                named_bar_sync(1, kConsumerThreads);
+                for (int i = ct; i < m.qd; i += kConsumerThreads) {
+                    const int hh = i / hd, d = i - hh * hd;
+                    const float* ph = part + (size_t)hh * S * W2;
+                    float M = -INFINITY;
+                    for (int s2 = 0; s2 < S; s2++) M = fmaxf(M, ph[s2 * W2 + hd]);
+                    float Ls = 0.0f, o = 0.0f;
+                    for (int s2 = 0; s2 < S; s2++) {
+                        const float ms = ph[s2 * W2 + hd];
+                        const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+                        Ls = fmaf(ph[s2 * W2 + hd + 1], w, Ls);
+                        o = fmaf(ph[s2 * W2 + d], w, o);
+                    }
+                    xs[xs_index<US>(i, nu_q)] = o / Ls;
                 }
-                xs[xs_index<US>(i, nu_q)] = o / Ls;
             }
-        } else if (g.kind == PH_DOWN) {
+        } else if (g.kind == PH_DOWN && has_rows) {
             const int nu_f = m.FF / US;
             if (alive)
-                alive = ll_gather(m.ll_act, m.FF, tag_here, ct, m.err,
-                                  [&](int j, float v) { xs[xs_index<US>(j, nu_f)] = v; });
-            if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-        } else if (g.kind == PH_ATTN) {
+                alive = ll_gather_s(m.ll_act, m.FF, tag_here, m.err, smem_u32(xs), US, nu_f, 0).ok;
             if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         } else if (g.kind == PH_MATVEC) {
             const int nu = g.cols / US;
             for (int j = ct; j < g.cols; j += kConsumerThreads) xs[xs_index<US>(j, nu)] = a.mv_x[j];
+        } else {
+            if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         }
         sync_alive();
         if (a.trace && ct == 0) a.trace[(tr + 2) * grid + cta] = global_ns();
 
-        // 3. the phase's work
+        float* yb = ybuf + (p & 1) * m.ybuf_floats;  // parity buffers: the next phase's
+                                                      // dots may start before this epilogue ends
         if (g.kind == PH_ATTN) {
-            if (cta < g.units) {
-                // transformer.go:658-685 for the query heads of one KV head over
-                // one slice of the context (online softmax over 32-position
-                // tiles); the slice partial (o, m, l) goes out as LL words and
-                // every CTA merges the slices when it stages the Wo input.
-                const int S = a.splits;
-                const int kvh = cta / S, sidx = cta % S;
-                const int grp = m.nh / m.nkv, hd = m.hd;
+            // 2'. attention, one (query head, split) per CTA
+            if (cta < m.nh * a.splits) {
+                const int S = a.splits, hd = m.hd;
+                const int h = cta / S, sidx = cta - h * S, kvh = h / (m.nh / m.nkv);
                 const int ctx = a.pos + 1;
                 const int t0 = (int)((long long)sidx * ctx / S), t1 = (int)((long long)(sidx + 1) * ctx / S);
-                float* qsm = xs;                       // [grp*hd]
-                float* osm = qsm + grp * hd;           // [grp*hd]
-                float* sc = osm + grp * hd;            // [grp*kAttnTile]
-                float* mrun = sc + grp * kAttnTile;    // [grp]
-                float* lrun = mrun + grp;              // [grp]
-                float* corr = lrun + grp;              // [grp]
-                float* ks = xs + ((grp * hd * 2 + grp * kAttnTile + 3 * grp + 3) & ~3);  // [tile][hd+4]
-                float* vs = ks + kAttnTile * (hd + 4);                                      // [tile][hd]
-                const float scale = (float)(1.0 / sqrt((double)hd));
-                const size_t lay = (size_t)g.layer * m.max_seq * m.kvd;
-                const int hv = hd / 8;  // 8-element vectors per head row
-                // K/V rows of a tile: cached positions come from the cache
-                // (written by earlier launches); the new position's k and v
-                // come from this launch's LL words.
-                auto stage_kv = [&](int tb, int nt) {
-                    for (int i = ct; i < nt * hv; i += kConsumerThreads) {
-                        const int t = i / hv, c8 = i % hv;
-                        if (tb + t == a.pos) continue;
-                        const size_t off = lay + (size_t)(tb + t) * m.kvd + (size_t)kvh * hd + c8 * 8;
-                        float kf[8], vf[8];
-                        if (m.kv_fp32) {
-                            const float4* kp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(m.kcache) + off);
-                            const float4* vp = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(m.vcache) + off);
-                            float4 a0 = __ldcg(kp), a1 = __ldcg(kp + 1), b0 = __ldcg(vp), b1 = __ldcg(vp + 1);
-                            kf[0] = a0.x; kf[1] = a0.y; kf[2] = a0.z; kf[3] = a0.w; kf[4] = a1.x; kf[5] = a1.y; kf[6] = a1.z; kf[7] = a1.w;
-                            vf[0] = b0.x; vf[1] = b0.y; vf[2] = b0.z; vf[3] = b0.w; vf[4] = b1.x; vf[5] = b1.y; vf[6] = b1.z; vf[7] = b1.w;
-                        } else {
-                            const uint4 ku = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(m.kcache) + off));
-                            const uint4 vu = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(m.vcache) + off));
-                            const __half2* kh = reinterpret_cast<const __half2*>(&ku);
-                            const __half2* vh = reinterpret_cast<const __half2*>(&vu);
-#pragma unroll
-                            for (int e = 0; e < 4; e++) {
-                                const float2 f0 = __half22float2(kh[e]), f1 = __half22float2(vh[e]);
-                                kf[2 * e] = f0.x; kf[2 * e + 1] = f0.y; vf[2 * e] = f1.x; vf[2 * e + 1] = f1.y;
-                            }
-                        }
-                        float4* kd = reinterpret_cast<float4*>(ks + t * (hd + 4) + c8 * 8);
-                        float4* vd = reinterpret_cast<float4*>(vs + t * hd + c8 * 8);
-                        kd[0] = make_float4(kf[0], kf[1], kf[2], kf[3]);
-                        kd[1] = make_float4(kf[4], kf[5], kf[6], kf[7]);
-                        vd[0] = make_float4(vf[0], vf[1], vf[2], vf[3]);
-                        vd[1] = make_float4(vf[4], vf[5], vf[6], vf[7]);
-                    }
-                };
-                // the first tile's cached rows load before the q poll
-                if (t1 > t0) stage_kv(t0, min(kAttnTile, t1 - t0));
-                // q of this group's heads, after RoPE (transformer.go:649-650)
-                if (alive)
-                    alive = ll_gather(m.ll_qkv + (size_t)kvh * grp * hd, grp * hd, tag_here, ct, m.err,
-                                      [&](int i, float v) { qsm[i] = v; });
-                for (int i = ct; i < grp * hd; i += kConsumerThreads) osm[i] = 0.0f;
-                if (ct < grp) { mrun[ct] = -INFINITY; lrun[ct] = 0.0f; }
-                for (int tb = t0; tb < t1; tb += kAttnTile) {
-                    const int nt = min(kAttnTile, t1 - tb);
-                    if (tb != t0) {
-                        named_bar_sync(1, kConsumerThreads);  // previous tile fully consumed
-                        stage_kv(tb, nt);
-                    }
-                    if (alive && a.pos >= tb && a.pos < tb + nt) {
-                        // the new position's k and v rows (transformer.go:654-656)
-                        const int t = a.pos - tb;
-                        const uint2* kl = m.ll_qkv + m.qd + (size_t)kvh * hd;
-                        const uint2* vl = m.ll_qkv + m.qd + m.kvd + (size_t)kvh * hd;
-                        alive = ll_gather(kl, hd, tag_here, ct, m.err, [&](int i, float v) { ks[t * (hd + 4) + i] = v; });
-                        if (alive)
-                            alive = ll_gather(vl, hd, tag_here, ct, m.err, [&](int i, float v) { vs[t * hd + i] = v; });
-                    }
-                    named_bar_sync(1, kConsumerThreads);
-                    // scores: warp = query head, lane = position
-                    for (int i = ct; i < grp * kAttnTile; i += kConsumerThreads) {
-                        const int h = i / kAttnTile, t = i % kAttnTile;
-                        if (t < nt) {
-                            const float4* qv = reinterpret_cast<const float4*>(qsm + h * hd);
-                            const float4* kv = reinterpret_cast<const float4*>(ks + t * (hd + 4));
-                            float d0 = 0.0f, d1 = 0.0f;
-                            for (int d4 = 0; d4 < hd / 4; d4 += 2) {
-                                const float4 a0 = qv[d4], b0 = kv[d4], a1 = qv[d4 + 1], b1 = kv[d4 + 1];
-                                d0 = fmaf(a0.x, b0.x, d0); d0 = fmaf(a0.y, b0.y, d0);
-                                d0 = fmaf(a0.z, b0.z, d0); d0 = fmaf(a0.w, b0.w, d0);
-                                d1 = fmaf(a1.x, b1.x, d1); d1 = fmaf(a1.y, b1.y, d1);
-                                d1 = fmaf(a1.z, b1.z, d1); d1 = fmaf(a1.w, b1.w, d1);
-                            }
-                            sc[i] = (d0 + d1) * scale;
-                        } else {
-                            sc[i] = -INFINITY;
-                        }
-                    }
-                    named_bar_sync(1, kConsumerThreads);
-                    // per-head max / exp / sum, one warp per head
-                    for (int h = cw; h < grp; h += kConsumerWarps) {
-                        float mx = -INFINITY;
-                        for (int t = lane; t < kAttnTile; t += 32) mx = fmaxf(mx, sc[h * kAttnTile + t]);
-                        mx = warp_max(mx);
-                        const float mnew = fmaxf(mrun[h], mx);
-                        float sum = 0.0f;
-                        for (int t = lane; t < kAttnTile; t += 32) {
-                            float e = (t < nt) ? expf(sc[h * kAttnTile + t] - mnew) : 0.0f;
-                            sc[h * kAttnTile + t] = e;
-                            sum += e;
-                        }
-                        sum = warp_sum(sum);
-                        if (lane == 0) {
-                            const float c = (mrun[h] == -INFINITY) ? 0.0f : expf(mrun[h] - mnew);
-                            corr[h] = c;
-                            lrun[h] = lrun[h] * c + sum;
-                            mrun[h] = mnew;
-                        }
-                    }
-                    named_bar_sync(1, kConsumerThreads);
-                    for (int i = ct; i < grp * hd; i += kConsumerThreads) {
-                        const int h = i / hd, d = i % hd;
-                        float o = osm[i] * corr[h];
-                        const float* ph = sc + h * kAttnTile;
-                        for (int t = 0; t < nt; t++) o = fmaf(ph[t], vs[t * hd + d], o);
-                        osm[i] = o;
-                    }
-                }
-                named_bar_sync(1, kConsumerThreads);
-                // this slice's partial (o unnormalised, m, l) as LL words,
-                // laid out [head][split][hd + 2]
-                const unsigned tag = ll_tag(a.epoch, g.layer);
-                for (int i = ct; i < grp * (hd + 2); i += kConsumerThreads) {
-                    const int h = i / (hd + 2), d = i % (hd + 2);
-                    const float v = d < hd ? osm[h * hd + d] : (d == hd ? mrun[h] : lrun[h]);
-                    ll_store(m.ll_part + ((size_t)(kvh * grp + h) * S + sidx) * (hd + 2) + d, v, tag);
-                }
+                const int es = m.kv_fp32 ? 4 : 2;
+                const size_t lay = ((size_t)g.layer * m.max_seq * m.kvd + (size_t)kvh * hd) * es;
+                const uint8_t* kg = reinterpret_cast<const uint8_t*>(m.kcache) + lay;
+                const uint8_t* vg = reinterpret_cast<const uint8_t*>(m.vcache) + lay;
+                uint2* out = S == 1 ? m.ll_attn + (size_t)h * hd : m.ll_part + ((size_t)h * S + sidx) * (hd + 2);
+                const uint2* q = m.ll_qkv + (size_t)h * hd;
+                const uint2* kn = m.ll_qkv + m.qd + (size_t)kvh * hd;
+                const uint2* vn = kn + m.kvd;
+                const unsigned tout = ll_tag(a.epoch, g.layer);
+                alive = m.kv_fp32
+                            ? attn_phase<true>(q, kn, vn, kg, vg, (uint32_t)(m.kvd * es), hd, m.attn_tile, t0, t1, a.pos,
+                                               tag_here, tout, out, S != 1, m.err, so.xs, so.red, alive)
+                            : attn_phase<false>(q, kn, vn, kg, vg, (uint32_t)(m.kvd * es), hd, m.attn_tile, t0, t1,
+                                                a.pos, tag_here, tout, out, S != 1, m.err, so.xs, so.red, alive);
             }
         } else {
-            const unsigned tag = ll_tag(a.epoch, g.layer);
+            // 2. rows: dot products of this CTA's weight rows into yb
+            const int rbase = g.rpu * s.u0;
             for (int k = 0; k < s.nchunks; k++) {
                 const unsigned gidx = gbase + k;
                 if ((int)(gidx % kConsumerWarps) != cw) continue;
                 const int slot = gidx % NS;
-                const bool landed = __all_sync(0xffffffffu, chunk_wait(&full[slot], (gidx / NS) & 1, gidx, pstop, m.err));
+                const bool landed =
+                    __all_sync(0xffffffffu, chunk_wait(&full[slot], (gidx / NS) & 1, gidx, pstop, m.err));
                 if (!landed) alive = false;
                 if (alive) {
                     const uint8_t* dst = ring + (size_t)slot * SB;
@@ -701,7 +810,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     const size_t r0 = (size_t)uu0 * g.rpu;
                     const uint8_t* src = g.w + r0 * g.rb;
                     const uint8_t* base1 = dst + (reinterpret_cast<uintptr_t>(src) & 15);
-                    const uint8_t* base2 = nullptr;
+                    const uint8_t* base2 = base1;
                     if (g.w2) {
                         const uintptr_t s2 = reinterpret_cast<uintptr_t>(g.w2 + r0 * g.rb);
                         const uint32_t len1 = (uint32_t)((((uintptr_t)src & 15) + (size_t)nu * g.rb + 15) & ~size_t(15));
@@ -712,84 +821,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     for (int pi = 0; pi < npairs; pi++) {
                         const uint8_t *ra, *rb2;
                         bool two;
-                        int rowa;
+                        int yi;  // output index of the pair's first row in yb
                         if (g.w2) {
                             ra = base1 + (size_t)pi * g.rb;
                             rb2 = base2 + (size_t)pi * g.rb;
                             two = true;
-                            rowa = (int)r0 + pi;
+                            yi = 2 * (uu0 - s.u0 + pi);  // gate, up interleaved
                         } else {
                             ra = base1 + (size_t)(2 * pi) * g.rb;
                             two = (2 * pi + 1) < nrows;
                             rb2 = two ? ra + g.rb : ra;
-                            rowa = (int)r0 + 2 * pi;
+                            yi = (int)r0 - rbase + 2 * pi;
                         }
                         float a0, a1;
                         if (QT == 8) dot2_q8(ra, rb2, two, xs, g.cols, lane, a0, a1);
                         else dot2_q4(ra, rb2, two, xs, g.cols, lane, a0, a1);
-                        a0 = warp_sum(a0);
-                        a1 = warp_sum(a1);
-                        if (lane == 0) {
-                            switch (g.kind) {
-                                case PH_QKV: {
-                                    // bias (transformer.go:632-646), RoPE on interleaved
-                                    // pairs (936-951), KV append (654-656)
-                                    const int qi = rowa - 2 * s.u0;
-                                    a0 += qconst[qi];
-                                    a1 += qconst[qi + 1];
-                                    if (rowa < m.qd + m.kvd) {
-                                        const float rc = qconst[kMaxQkvRows + qi], rs = qconst[2 * kMaxQkvRows + qi];
-                                        const float x0 = a0, x1 = a1;
-                                        a0 = x0 * rc - x1 * rs;
-                                        a1 = x0 * rs + x1 * rc;
-                                    }
-                                    ll_store2(m.ll_qkv + rowa, a0, a1, tag);
-                                    if (rowa >= m.qd) {
-                                        const bool isk = rowa < m.qd + m.kvd;
-                                        const int col = rowa - m.qd - (isk ? 0 : m.kvd);
-                                        const size_t off = ((size_t)g.layer * m.max_seq + a.pos) * m.kvd + col;
-                                        void* cache = isk ? m.kcache : m.vcache;
-                                        if (m.kv_fp32) {
-                                            reinterpret_cast<float*>(cache)[off] = a0;
-                                            reinterpret_cast<float*>(cache)[off + 1] = a1;
-                                        } else {
-                                            *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(cache) + off) =
-                                                __floats2half2_rn(a0, a1);
-                                        }
-                                    }
-                                    break;
-                                }
-                                case PH_GATEUP:
-                                    // SwiGLU (transformer.go:725-727, 954-956)
-                                    ll_store(m.ll_act + rowa, a0 / (1.0f + expf(-a0)) * a1, tag);
-                                    break;
-                                case PH_WO:
-                                case PH_DOWN: {
-                                    // residual (transformer.go:576-578, 591-593)
-                                    uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
-                                    float* xr = xres + (rowa - own0);
-                                    xr[0] += a0;
-                                    ll_store(dstll + rowa, xr[0], tag);
-                                    if (two) {
-                                        xr[1] += a1;
-                                        ll_store(dstll + rowa + 1, xr[1], tag);
-                                    }
-                                    break;
-                                }
-                                case PH_LMHEAD:
-                                    m.logits[rowa] = a0;
-                                    if (better(a0, rowa, best.v, best.i)) { best.v = a0; best.i = rowa; }
-                                    if (two) {
-                                        m.logits[rowa + 1] = a1;
-                                        if (better(a1, rowa + 1, best.v, best.i)) { best.v = a1; best.i = rowa + 1; }
-                                    }
-                                    break;
-                                default:  // PH_MATVEC
-                                    a.mv_y[rowa] = a0;
-                                    if (two) a.mv_y[rowa + 1] = a1;
-                                    break;
-                            }
-                        }
+                        const float v = warp_sum2(a0, a1, lane);
+                        if (lane == 0) yb[yi] = v;
+                        if (lane == 16 && two) yb[yi + 1] = v;
                     }
                 }
                 __syncwarp();
@@ -797,45 +846,124 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             }
             gbase += s.nchunks;
         }
-
-        // 4. this CTA's part of the phase is done
         sync_alive();
-        if (a.trace && ct == 0) a.trace[(tr + 3) * grid + cta] = global_ns();
-        if (g.kind == PH_LMHEAD) {
-            // argmax, first maximum wins (transformer.go:1038-1046)
-            if (lane == 0) { red[cw] = best.v; misc[4 + cw] = best.i; }
-            named_bar_sync(1, kConsumerThreads);
-            if (ct == 0) {
-                Best b{red[0], misc[4]};
-                for (int w = 1; w < kConsumerWarps; w++)
-                    if (better(red[w], misc[4 + w], b.v, b.i)) { b.v = red[w]; b.i = misc[4 + w]; }
-                m.best_val[cta] = b.v;
-                m.best_idx[cta] = b.i;
-                __threadfence();
-                const unsigned old = atom_acq_rel_add(m.am_ctr, 1u);
-                if (old == (unsigned)(grid - 1)) {
-                    Best f{-INFINITY, 0x7fffffff};
-                    for (int c2 = 0; c2 < grid; c2++) {
-                        const float v = __ldcg(m.best_val + c2);
-                        const int i = __ldcg(m.best_idx + c2);
-                        if (better(v, i, f.v, f.i)) { f.v = v; f.i = i; }
+
+        // 3. epilogue, one thread per output
+        const unsigned tag = ll_tag(a.epoch, g.layer);
+        if ((alive && has_rows) || g.kind == PH_LMHEAD) {
+            // (every CTA takes part in the argmax, so its arrival counter
+            // always completes and resets)
+            switch (g.kind) {
+                case PH_QKV: {
+                    // bias (transformer.go:632-646), RoPE on interleaved pairs
+                    // (936-951), KV append (654-656)
+                    const bool bias = m.layers[g.layer].bqkv != nullptr;
+                    const int bias0 = (2 * s.u0) & ~3;
+                    for (int j = ct; j < s.n; j += kConsumerThreads) {
+                        const int row = 2 * (s.u0 + j);
+                        float a0 = yb[2 * j], a1 = yb[2 * j + 1];
+                        if (bias) {
+                            a0 += cb[cb_bias(m) + row - bias0];
+                            a1 += cb[cb_bias(m) + row + 1 - bias0];
+                        }
+                        if (row < m.qd + m.kvd) {
+                            const int pi2 = (row % m.hd) >> 1;
+                            const float rc = cb[cb_cos(m) + pi2], rs = cb[cb_sin(m) + pi2];
+                            const float x0 = a0, x1 = a1;
+                            a0 = x0 * rc - x1 * rs;
+                            a1 = x0 * rs + x1 * rc;
+                        }
+                        ll_store2(m.ll_qkv + row, a0, a1, tag);
+                        if (row >= m.qd) {
+                            const bool isk = row < m.qd + m.kvd;
+                            const int col = row - m.qd - (isk ? 0 : m.kvd);
+                            const size_t off = ((size_t)g.layer * m.max_seq + a.pos) * m.kvd + col;
+                            void* cache = isk ? m.kcache : m.vcache;
+                            if (m.kv_fp32) {
+                                reinterpret_cast<float*>(cache)[off] = a0;
+                                reinterpret_cast<float*>(cache)[off + 1] = a1;
+                            } else {
+                                *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(cache) + off) =
+                                    __floats2half2_rn(a0, a1);
+                            }
+                        }
                     }
-                    if (f.i == 0x7fffffff) f.i = 0;
-                    *m.token = f.i;
-                    if (a.out_ids) a.out_ids[a.step] = f.i;
-                    if (a.done && f.i == a.eos) *a.done = 1;
-                    atomicExch(m.am_ctr, 0u);
+                    break;
                 }
+                case PH_GATEUP:
+                    // SwiGLU (transformer.go:725-727, 954-956)
+                    for (int j = ct; j < s.n; j += kConsumerThreads) {
+                        const float gv = yb[2 * j], uv = yb[2 * j + 1];
+                        ll_store(m.ll_act + s.u0 + j, gv / (1.0f + expf(-gv)) * uv, tag);
+                    }
+                    break;
+                case PH_WO:
+                case PH_DOWN: {
+                    // residual (transformer.go:576-578, 591-593); the rows are
+                    // exactly the residual rows this CTA owns
+                    uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
+                    for (int j = ct; j < s.n; j += kConsumerThreads) {
+                        const int row = s.u0 + j;
+                        const float xr = xres[row - own0] + yb[j];
+                        xres[row - own0] = xr;
+                        ll_store(dstll + row, xr, tag);
+                    }
+                    break;
+                }
+                case PH_LMHEAD: {
+                    // logits + argmax, first maximum wins (transformer.go:1038-1046)
+                    Best best{-INFINITY, 0x7fffffff};
+                    for (int j = ct; alive && j < s.n; j += kConsumerThreads) {
+                        const int row = s.u0 + j;
+                        const float v = yb[j];
+                        m.logits[row] = v;
+                        if (better(v, row, best.v, best.i)) { best.v = v; best.i = row; }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+                        const int oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+                        if (better(ov, oi, best.v, best.i)) { best.v = ov; best.i = oi; }
+                    }
+                    if (lane == 0) { red[cw] = best.v; misc[4 + cw] = best.i; }
+                    named_bar_sync(1, kConsumerThreads);
+                    if (ct == 0) {
+                        Best b{red[0], misc[4]};
+                        for (int w = 1; w < kConsumerWarps; w++)
+                            if (better(red[w], misc[4 + w], b.v, b.i)) { b.v = red[w]; b.i = misc[4 + w]; }
+                        m.best_val[cta] = b.v;
+                        m.best_idx[cta] = b.i;
+                        __threadfence();
+                        const unsigned old = atom_acq_rel_add(m.am_ctr, 1u);
+                        if (old == (unsigned)(grid - 1)) {
+                            Best f{-INFINITY, 0x7fffffff};
+                            for (int c2 = 0; c2 < grid; c2++) {
+                                const float v = __ldcg(m.best_val + c2);
+                                const int i = __ldcg(m.best_idx + c2);
+                                if (better(v, i, f.v, f.i)) { f.v = v; f.i = i; }
+                            }
+                            if (f.i == 0x7fffffff) f.i = 0;
+                            *m.token = f.i;
+                            if (a.out_ids) a.out_ids[a.step] = f.i;
+                            if (a.done && f.i == a.eos) *a.done = 1;
+                            atomicExch(m.am_ctr, 0u);
+                        }
+                    }
+                    break;
+                }
+                default:  // PH_MATVEC
+                    for (int j = ct; j < s.n; j += kConsumerThreads) a.mv_y[s.u0 + j] = yb[j];
+                    break;
             }
         }
+        if (a.trace && ct == 0) a.trace[(tr + 3) * grid + cta] = global_ns();
     }
 }
 
 }  // namespace
 
 size_t decode_smem_bytes(const ModelDev& m) {
-    return (size_t)m.nslots * m.slot_bytes + 128 + (size_t)m.xs_floats * 4 + kMaxOwnRows * 4 + 3 * kMaxQkvRows * 4 +
-           16 * (size_t)m.nslots + 64 * 4 + 32 * 4;
+    return smem_offsets(m.nslots, m.slot_bytes, m.xs_floats, m.ybuf_floats, m.cfloats).total;
 }
 
 int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err) {

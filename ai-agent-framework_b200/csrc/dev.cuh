@@ -29,7 +29,8 @@ constexpr int kPhasesPerLayer = 5;
 constexpr int kConsumerWarps = 12;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);  // warp 0 = producer
 constexpr int kMaxSplits = 8;                         // attention context splits per KV head
-constexpr int kAttnTile = 64;                         // positions per attention tile
+constexpr int kAttnTileBytes = 16384;                 // bytes of cached K (and of V) per attention tile
+constexpr int kMaxAttnTile = 128;                     // positions per attention tile, at most
 constexpr int kMaxOwnRows = 64;                       // residual rows one CTA keeps (H / grid)
 constexpr int kMaxQkvRows = 128;                      // QKV rows one CTA computes ((qd + 2*kvd) / grid)
 // Phase trace slots: consumer phase start, input ready, input staged, work
@@ -52,7 +53,11 @@ struct ModelDev {
     int rb_h, rb_q, rb_f; // row bytes for inputs of width H, qd, FF
     float eps;
     int kv_fp32;
-    int slot_bytes, nslots, xs_floats;  // shared-memory ring geometry
+    int slot_bytes, nslots;   // shared-memory ring geometry
+    int xs_floats;            // phase input / attention scratch (floats)
+    int ybuf_floats;          // phase outputs of one CTA, per buffer (two buffers)
+    int cfloats;              // phase constants: norm gains, QKV bias, RoPE row
+    int attn_tile;            // positions per attention tile
     const uint8_t* tok_embd;  // [V rows][rb_h]
     const uint8_t* lm_head;   // tok_embd when tied
     const float* out_norm;
@@ -66,6 +71,7 @@ struct ModelDev {
     uint2* ll_x2;             // [H]   x after the FFN residual
     uint2* ll_qkv;            // [qd + 2*kvd] q, k (after RoPE), v of the new token
     uint2* ll_part;           // [nh][kMaxSplits][hd + 2] attention split partials (o, m, l)
+    uint2* ll_attn;           // [qd]  attention output when the context is not split
     uint2* ll_act;            // [FF]  SwiGLU output
     float* logits;            // [V]
     float* best_val;          // [grid] argmax partials
@@ -94,6 +100,43 @@ struct StepArgs {
     float* mv_y;
     int mv_rows, mv_cols, mv_rb;
 };
+
+// Dynamic shared-memory layout of the decode kernel (byte offsets).
+//   ring   [nslots][slot_bytes]   weight slots filled by the producer
+//   xs     [xs_floats]            phase input in the dot layout, or the
+//                                 attention scratch (q, k/v tiles, scores)
+//   xres   [kMaxOwnRows]          residual rows this CTA owns
+//   ybuf   [2][ybuf_floats]       dot results of the phase (parity buffers)
+//   cbuf   [cfloats]              phase constants (norm gains, bias, RoPE)
+//   full, empty [nslots] mbarriers; red [64] floats; misc [32] ints
+struct SmemOffsets {
+    uint32_t xs, xres, ybuf, cbuf, full, empty, red, misc, total;
+};
+
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_floats, int cfloats) {
+    SmemOffsets o;
+    uint32_t p = (uint32_t)nslots * (uint32_t)slot_bytes + 128u;
+    o.xs = p;    p += 4u * (uint32_t)xs_floats;
+    o.xres = p;  p += 4u * kMaxOwnRows;
+    o.ybuf = p;  p += 8u * (uint32_t)ybuf_floats;
+    o.cbuf = p;  p += 4u * (uint32_t)cfloats;
+    p = (p + 15u) & ~15u;
+    o.full = p;  p += 8u * (uint32_t)nslots;
+    o.empty = p; p += 8u * (uint32_t)nslots;
+    o.red = p;   p += 4u * 64u;
+    o.misc = p;  p += 4u * 32u;
+    o.total = p;
+    return o;
+}
+
+// Constant buffer layout (floats): [0, H) norm gains; then the QKV bias of
+// this CTA's rows from row (2 * u0) & ~3 (kMaxQkvRows + 4); then hd/2 cos and
+// hd/2 sin of the RoPE row at the current position.
+inline int cb_floats(int H, int hd) { return (H + kMaxQkvRows + 4 + hd + 31) & ~31; }
 
 #ifdef __CUDACC__
 // ---------------------------------------------------------------------------
@@ -162,6 +205,13 @@ __device__ __forceinline__ unsigned atom_acq_rel_add(unsigned* p, unsigned v) {
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
+
+// 16-byte global -> shared copies, completed per thread with cp_async_wait().
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

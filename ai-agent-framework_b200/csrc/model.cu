@@ -147,12 +147,12 @@ int check_device_status(b2_model* m, std::string* err) {
     return B2_OK;
 }
 
-// Attention context splits per KV head: one 32-position tile per split while
-// the merge buffer allows it (more splits = more CTAs working, shorter
-// critical path), capped by the grid.
+// Attention context splits per query head: one K/V tile per split while the
+// merge buffer and the grid allow it (more splits = more CTAs working, a
+// shorter critical path); beyond that a split walks several tiles.
 static int splits_for(const b2_model* m, int ctx) {
-    int s = (ctx + kAttnTile - 1) / kAttnTile;
-    int cap = std::max(1, std::min(m->max_splits, m->grid / std::max(1, m->dev.nkv)));
+    int s = (ctx + m->dev.attn_tile - 1) / m->dev.attn_tile;
+    int cap = std::max(1, std::min(m->max_splits, m->grid / std::max(1, m->dev.nh)));
     return std::max(1, std::min(s, cap));
 }
 
@@ -326,8 +326,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const int nh = c.num_heads, nkv = c.num_kv_heads, hd = c.head_dim;
     const int qd = nh * hd, kvd = nkv * hd;
     if (V <= 0) return bail(B2_ERR_FORMAT, "tokenizer.ggml.tokens missing: vocab size unknown");
-    if (nkv <= 0 || nh % nkv != 0 || hd % 8 != 0 || H % 32 || FF % 32 || qd % 32)
-        return bail(B2_ERR_UNSUPPORTED_TYPE, "unsupported head geometry (need nh % nkv == 0, head_dim % 8 == 0, widths % 32 == 0)");
+    if (nkv <= 0 || nh % nkv != 0 || hd < 8 || hd > 256 || (hd & (hd - 1)) || H % 32 || FF % 32 || qd % 32)
+        return bail(B2_ERR_UNSUPPORTED_TYPE,
+                    "unsupported head geometry (need nh % nkv == 0, head_dim a power of two in [8, 256], widths % 32 == 0)");
     if (c.max_seq_len <= 0) return bail(B2_ERR_FORMAT, "context length is zero");
 
     // Tensor checks (transformer.go:1143-1306 reads the same names).
@@ -435,6 +436,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const size_t off_llx2 = take((size_t)H * 8);
     const size_t off_llqkv = take((size_t)(qd + 2 * kvd) * 8);
     const size_t off_llpart = take((size_t)nh * kMaxSplits * (hd + 2) * 8);
+    const size_t off_llattn = take((size_t)qd * 8);
     const size_t off_llact = take((size_t)FF * 8);
     const size_t off_logits = take((size_t)V * 4);
     const size_t off_bv = take((size_t)m->grid * 4);
@@ -569,6 +571,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.ll_x2 = reinterpret_cast<uint2*>(A + off_llx2);
     d.ll_qkv = reinterpret_cast<uint2*>(A + off_llqkv);
     d.ll_part = reinterpret_cast<uint2*>(A + off_llpart);
+    d.ll_attn = reinterpret_cast<uint2*>(A + off_llattn);
     d.ll_act = reinterpret_cast<uint2*>(A + off_llact);
     d.logits = reinterpret_cast<float*>(A + off_logits);
     d.best_val = reinterpret_cast<float*>(A + off_bv);
@@ -596,20 +599,27 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
 
     // Shared-memory geometry: the ring of weight slots plus one staging area
     // (xs) that holds, one phase at a time, the phase input vector, the
-    // attention scratch (q, o, scores, K/V tiles), or the Wo input plus all
+    // attention scratch (q, k/v of the new position, output, probabilities,
+    // per-warp V sums, one K and one V tile), or the Wo input plus all
     // attention split partials being merged.
-    const int grp = nh / nkv;
-    const int attn_need = grp * hd * 2 + grp * kAttnTile + 3 * grp + 4 + kAttnTile * (hd + 4) + kAttnTile * hd + 32;
+    const int kv_es = o.kv_fp32 ? 4 : 2;
+    const int tile = std::max(1, std::min(kMaxAttnTile, kAttnTileBytes / (hd * kv_es)));
+    const int attn_need = 4 * hd + tile + kConsumerWarps * hd + (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
     const int base_xs = std::max(std::max(std::max(H, FF), qd), attn_need);
+    const int qkv_units = (qd + 2 * kvd) / 2;
+    const auto per_cta = [&](int units) { return (units + m->grid - 1) / m->grid; };
+    const int ybuf = (std::max(std::max(2 * per_cta(qkv_units), 2 * per_cta(FF)), std::max(per_cta(H), per_cta(V))) + 31) & ~31;
+    const int cfloats = cb_floats(H, hd);
     const size_t need_slot = std::max(std::max(2 * rb_h + 192, rb_q + 32), rb_f + 32);
     const int slot = std::max<int>(8192, (int)((need_slot + 1023) & ~size_t(1023)));
     auto ring_slots = [&](int xs_f) {
-        const int budget = 232448 - 128 - xs_f * 4 - kMaxOwnRows * 4 - 3 * kMaxQkvRows * 4 - 1024;
-        return std::min(32, budget / slot);
+        int n = 0;
+        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats).total <= 232448u) n++;
+        return n;
     };
     const int merge_full = qd + nh * kMaxSplits * (hd + 2);
     int xs = base_xs, max_splits;
-    if (ring_slots(std::max(base_xs, merge_full)) >= 2 * kConsumerWarps) {
+    if (ring_slots((std::max(base_xs, merge_full) + 31) & ~31) >= 2 * kConsumerWarps) {
         xs = std::max(base_xs, merge_full);
         max_splits = kMaxSplits;
     } else {
@@ -619,9 +629,12 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const int ns = ring_slots(xs);
     if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
     if ((H + m->grid - 1) / m->grid > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
-    if (2 * (((qd + 2 * kvd) / 2 + m->grid - 1) / m->grid) > kMaxQkvRows)
+    if (2 * per_cta(qkv_units) > kMaxQkvRows)
         return bail(B2_ERR_UNSUPPORTED_TYPE, "attention projection too large for one GPU");
     d.xs_floats = xs;
+    d.ybuf_floats = ybuf;
+    d.cfloats = cfloats;
+    d.attn_tile = tile;
     d.slot_bytes = slot;
     d.nslots = ns;
     m->max_splits = max_splits;
