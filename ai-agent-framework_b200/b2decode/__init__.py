@@ -18,6 +18,7 @@ LIB_PATH = os.path.join(PKG_DIR, "libb2decode.so")
 HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "b2decode.h")
 
 B2_OK = 0
+TRACE_SLOTS = 12  # slots per phase and CTA in trace_step (kTraceSlots)
 ERRORS = {
     -1: "IO", -2: "FORMAT", -3: "UNSUPPORTED_TYPE", -4: "OOM", -5: "CUDA", -6: "NCCL", -7: "TIMEOUT",
     -8: "BAD_ARG", -9: "CONTEXT", -10: "NOT_LOADED",
@@ -233,14 +234,17 @@ class Model:
         return lib().b2_device_status(self._h)
 
     def trace_step(self, token: int) -> np.ndarray:
-        """[phases, 6, ctas] globaltimer stamps (ns) of one decode step."""
+        """[phases, TRACE_SLOTS, ctas] timeline of one decode step: globaltimer
+        stamps (ns) in slots 0-5, consumer chunk-wait ns and slow-wait count in
+        6-7, producer slot-wait ns and chunks issued in 8-9, rows loop done in 10,
+        ns in tile dot products in 11."""
         P = 5 * self.cfg["num_layers"] + 1
-        cap = P * 6 * 1024
+        cap = P * TRACE_SLOTS * 1024
         out = np.zeros(cap, dtype=np.int64)
         npz, nc = C.c_int32(), C.c_int32()
         _check(lib().b2_trace_step(self._h, int(token), out.ctypes.data_as(C.POINTER(_i64)), cap, C.byref(npz),
                                    C.byref(nc)))
-        return out[: npz.value * 6 * nc.value].reshape(npz.value, 6, nc.value)
+        return out[: npz.value * TRACE_SLOTS * nc.value].reshape(npz.value, TRACE_SLOTS, nc.value)
 
     def stream_handle(self) -> int:
         return lib().b2_stream_handle(self._h) or 0

@@ -388,7 +388,7 @@ int b2_dequant_tensor(const b2_model* m, const char* name, float* out, int64_t n
     std::string err;
     float* d = nullptr;
     if (!cuda_ok(cudaMalloc(&d, sizeof(float) * t.elements), &err)) return ret(B2_ERR_OOM, err);
-    int rc = b2::launch_dequant(t.dev, t.type, t.elements, d, m->stream);
+    int rc = b2::launch_dequant(t, d, m->stream);
     if (!rc && !cuda_ok(cudaMemcpyAsync(out, d, sizeof(float) * t.elements, cudaMemcpyDeviceToHost, m->stream), &err))
         rc = B2_ERR_CUDA;
     if (!rc && !cuda_ok(cudaStreamSynchronize(m->stream), &err)) rc = B2_ERR_CUDA;

@@ -4,21 +4,26 @@
 // feedForward) and the Q8_0 matvec of transformer.go:810-892 for B = 1.
 //
 // Layout of one CTA (one per SM):
-//   warp 0, lane 0   producer: walks the static schedule of weight rows this
-//                    CTA owns in every phase of the launch and streams them
-//                    with 1-D TMA bulk copies into a ring of shared-memory
+//   warp 0, lane 0   producer: walks the static schedule of weight chunks
+//                    this CTA owns in every phase of the launch and streams
+//                    them with 1-D TMA bulk copies into a ring of shared-memory
 //                    slots.  Weights never depend on activations, so the
 //                    producer runs ahead across phases, limited by the ring.
 //   warps 1..12      consumers, per phase:
 //                    1. stage: gather the phase input from the previous
 //                       phase's LL words (the poll is the load) into shared
 //                       memory, with RMSNorm / embedding decode / attention
-//                       split merge fused in; the phase constants (norm gains,
-//                       QKV bias, RoPE row) arrive by cp.async during the poll;
-//                    2. rows: each warp dequantises its chunks of the CTA's
-//                       weight rows in registers and leaves the fp32 dot
-//                       products in shared memory (ybuf); nothing else is live
-//                       in this loop, so it runs without register spills;
+//                       split merge fused in, and split it into three int8
+//                       planes per 32-element block (x ~ s * (p0 + p1/128 +
+//                       p2/16384), ~21 significant bits); the phase constants
+//                       (norm gains, QKV bias, RoPE row) arrive by cp.async
+//                       during the poll;
+//                    2. rows: int8 tensor-core dot products (mma m16n8k32):
+//                       the weight tile (8 rows x 32 K-bytes, straight from
+//                       the ring, no dequantisation) is the B operand, the x
+//                       planes the A operand; the int32 per-block sums are
+//                       scaled by the weight block scale and the x block scale
+//                       and accumulated in fp32, one chunk of tiles per warp;
 //                    3. epilogue, one thread per output: bias + RoPE + KV
 //                       append, SwiGLU, residual add, logits + argmax, and the
 //                       LL stores that hand the outputs to the next phase.
@@ -28,6 +33,8 @@
 // Each CTA keeps the residual-stream rows it owns (the same rows in every Wo
 // and down phase) in shared memory.  Every wait is bounded (globaltimer) and
 // reports B2_ERR_TIMEOUT through the device error flag instead of hanging.
+// The kernel-level matvec entry point (ggml block layout, caller memory) runs
+// the same kernel in a one-phase mode with an fp32 dequantising dot.
 #include <cuda_runtime.h>
 
 #include "../../include/b2decode.h"
@@ -42,65 +49,68 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;      // 2 s for any consumer wa
 constexpr uint64_t kProducerLimitNs = 8000000000ull;  // producer slot waits outlast consumer polls
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 
-struct Geom {
+// ---------------------------------------------------------------------------
+// phase geometry
+// ---------------------------------------------------------------------------
+
+// A weight phase of the model: a tiled matrix (plus the up matrix for
+// gate/up), its rows and 32-blocks per row.
+struct TGeom {
     int kind;
     int layer;
     const uint8_t* w;
-    const uint8_t* w2;  // up rows (PH_GATEUP)
-    int rb;
-    int cols;
-    int units;
-    int rpu;  // rows per unit
+    const uint8_t* w2;  // up matrix (PH_GATEUP)
+    int rows;           // real output rows
+    int tiles;          // ceil(rows / kTileRows)
+    int nb;             // K / 32
+    int units;          // PH_ATTN: (query head, split) work items
 };
 
-__device__ __forceinline__ Geom phase_geom(const ModelDev& m, const StepArgs& a, int p) {
-    Geom g{};
-    if (a.mv_w) {
-        g.kind = PH_MATVEC;
-        g.w = a.mv_w;
-        g.rb = a.mv_rb;
-        g.cols = a.mv_cols;
-        g.units = a.mv_rows;
-        g.rpu = 1;
-        return g;
-    }
+__device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const StepArgs& a, int p) {
+    TGeom g{};
     if (p == kPhasesPerLayer * m.L) {
         g.kind = PH_LMHEAD;
         g.layer = m.L;
         g.w = m.lm_head;
-        g.rb = m.rb_h;
-        g.cols = m.H;
-        g.units = m.V;
-        g.rpu = 1;
-        return g;
+        g.rows = m.V;
+        g.nb = m.H / 32;
+    } else {
+        g.layer = p / kPhasesPerLayer;
+        g.kind = p % kPhasesPerLayer;
+        const LayerDev& L = m.layers[g.layer];
+        switch (g.kind) {
+            case PH_QKV: g.w = L.wqkv; g.rows = m.qd + 2 * m.kvd; g.nb = m.H / 32; break;
+            case PH_ATTN: g.units = m.nh * a.splits; break;
+            case PH_WO: g.w = L.wo; g.rows = m.H; g.nb = m.qd / 32; break;
+            case PH_GATEUP:
+                g.w = L.wgu;
+                g.w2 = L.wgu + tiled_bytes(m.FF, m.H, m.qtype);
+                g.rows = m.FF;
+                g.nb = m.H / 32;
+                break;
+            default: g.w = L.wd; g.rows = m.H; g.nb = m.FF / 32; break;  // PH_DOWN
+        }
     }
-    g.layer = p / kPhasesPerLayer;
-    g.kind = p % kPhasesPerLayer;
-    const LayerDev& L = m.layers[g.layer];
-    switch (g.kind) {
-        case PH_QKV:
-            g.w = L.wqkv; g.rb = m.rb_h; g.cols = m.H; g.units = (m.qd + 2 * m.kvd) / 2; g.rpu = 2;
-            break;
-        case PH_ATTN:
-            g.units = m.nh * a.splits;
-            break;
-        case PH_WO:
-            g.w = L.wo; g.rb = m.rb_q; g.cols = m.qd; g.units = m.H; g.rpu = 1;
-            break;
-        case PH_GATEUP:
-            g.w = L.wgu; g.w2 = L.wgu + (size_t)m.FF * m.rb_h; g.rb = m.rb_h; g.cols = m.H; g.units = m.FF;
-            g.rpu = 1;
-            break;
-        default:  // PH_DOWN
-            g.w = L.wd; g.rb = m.rb_f; g.cols = m.FF; g.units = m.H; g.rpu = 1;
-            break;
-    }
+    g.tiles = (g.rows + kTileRows - 1) / kTileRows;
     return g;
 }
 
-// Static split of a phase's units over the grid and of a CTA's share into
-// chunks that fit one ring slot.  Producer and consumers evaluate the same
-// function, so they agree on every chunk without communicating.
+// Bytes of one (tile, block) unit in the ring: 16 rows of quants + 16
+// scales, twice for gate + up.
+__device__ __forceinline__ int tile_unit_bytes(const TGeom& g, int qtype) {
+    return (kTileRows * tile_qb(qtype) + 2 * kTileRows) * (g.w2 ? 2 : 1);
+}
+
+// The matvec entry point's single phase: rows of a ggml-layout matrix.
+struct Geom {
+    const uint8_t* w;
+    int rb;
+    int cols;
+    int units;
+};
+
+// Static split of the matvec rows over the grid and of a CTA's share into
+// chunks that fit one ring slot.
 struct Split {
     int u0, n, cu, nchunks;
 };
@@ -110,13 +120,12 @@ __device__ __forceinline__ Split cta_split(const Geom& g, int cta, int grid, int
     s.u0 = (int)((long long)cta * g.units / grid);
     int u1 = (int)((long long)(cta + 1) * g.units / grid);
     s.n = u1 - s.u0;
-    if (g.w == nullptr || s.n <= 0) {
+    if (s.n <= 0) {
         s.cu = 1;
         s.nchunks = 0;
         return s;
     }
-    int per_unit = g.rpu * g.rb * (g.w2 ? 2 : 1);
-    int max_units = (slot_bytes - (g.w2 ? 192 : 32)) / per_unit;
+    int max_units = (slot_bytes - 32) / g.rb;
     int spread = (s.n + kConsumerWarps - 1) / kConsumerWarps;
     s.cu = max(1, min(max_units, spread));
     s.nchunks = (s.n + s.cu - 1) / s.cu;
@@ -125,11 +134,15 @@ __device__ __forceinline__ Split cta_split(const Geom& g, int cta, int grid, int
 
 __device__ __forceinline__ void set_err(int* err, int code) { atomicCAS(err, 0, code); }
 
-// Producer: bounded wait for a free ring slot.
+// Producer: bounded wait for a free ring slot.  The error flag (a global
+// load, an L2 round trip) is only read while the slot is still taken, so an
+// unblocked producer issues copies back to back; a blocked one gives up as
+// soon as any CTA reported an error.
 __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
     while (!mbar_try_wait(bar, parity)) {
+        if (*(volatile int*)err) return false;
         if (global_ns() - t0 > kProducerLimitNs) {
             set_err(err, B2_ERR_TIMEOUT);
             return false;
@@ -138,14 +151,37 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* e
     return true;
 }
 
-// Consumer: bounded wait for chunk gidx to land.  *pstop is the index of the
-// first chunk the producer did not issue (it stops early only after an
-// error); such chunks are skipped instead of waited for, and every chunk that
-// was issued is waited for, so no bulk copy is left in flight at exit.
+__device__ __forceinline__ unsigned ld_acquire_cta(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.cta.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_cta(unsigned* p, unsigned v) {
+    asm volatile("st.release.cta.shared.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+
+// Consumer: bounded wait for chunk gidx to land.  The chunk must first have
+// been issued (*issued > gidx): only then has its slot's previous round
+// completed, so the parity wait cannot mistake that round for this one (a
+// warp may otherwise reach a slot a full ring round before the producer
+// does).  *pstop is the index of the first chunk the producer did not issue
+// (it stops early only after an error); such chunks are skipped instead of
+// waited for, and every chunk that was issued is waited for, so no bulk copy
+// is left in flight at exit.
 __device__ __forceinline__ bool chunk_wait(uint64_t* bar, uint32_t parity, unsigned gidx, const volatile unsigned* pstop,
-                                           int* err) {
+                                           const unsigned* issued, int* err) {
+    uint64_t t0 = 0;
+    while (ld_acquire_cta(issued) <= gidx) {
+        if (gidx >= *pstop) return false;
+        const uint64_t now = global_ns();
+        if (t0 == 0) t0 = now;
+        if (now - t0 > kWaitLimitNs) {
+            set_err(err, B2_ERR_TIMEOUT);
+            return false;
+        }
+    }
     if (mbar_try_wait(bar, parity)) return true;
-    uint64_t t0 = global_ns();
+    if (t0 == 0) t0 = global_ns();
     for (;;) {
         if (mbar_try_wait(bar, parity)) return true;
         if (gidx >= *pstop) return false;
@@ -340,20 +376,14 @@ __device__ __forceinline__ void dot2_q4(const uint8_t* r0, const uint8_t* r1, bo
 }
 
 // transformer.go:525-531 + gguf.go:540-613: element j of token_embd row tok,
-// decoded from its block (out-of-range ids embed to zero).
+// decoded from its block of the tiled matrix (out-of-range ids embed to zero).
 __device__ __forceinline__ float embed_elem(const ModelDev& m, int tok, int j) {
     if (tok < 0 || tok >= m.V) return 0.0f;
-    const uint8_t* row = m.tok_embd + (size_t)tok * m.rb_h;
-    const int b = j >> 5, e = j & 31;
-    if (m.qtype == 8) {
-        const uint8_t* p = row + 34 * b;
-        float d = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8)));
-        return d * (float)(int8_t)p[2 + e];
-    }
-    const uint8_t* p = row + 18 * b;
-    float d = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8)));
-    uint8_t byte = p[2 + (e & 15)];
-    int nib = (e < 16) ? (byte & 15) : (byte >> 4);
+    const int nb = m.H / 32, b = j >> 5, e = j & 31;
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(m.tok_embd + tiled_soff(tok, b, nb, m.Vp, m.qtype)));
+    if (m.qtype == 8) return d * (float)(int8_t)m.tok_embd[tiled_qoff(tok, b, e, nb, 8)];
+    const uint8_t byte = m.tok_embd[tiled_qoff(tok, b, e & 15, nb, 2)];
+    const int nib = (e < 16) ? (byte & 15) : (byte >> 4);
     return d * (float)(nib - 8);
 }
 
@@ -571,18 +601,215 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
 }
 
 // ---------------------------------------------------------------------------
+// int8 tensor-core tile dot (model phases)
+// ---------------------------------------------------------------------------
+
+// mma.m16n8k32 with int32 accumulate: A = 16 weight rows x 32 (s8 for Q8_0,
+// u8 nibbles for Q4_0), B = x planes in columns 0-2; c01 / c23 start the
+// accumulators of output columns 2t, 2t+1.
+template <bool AU8>
+__device__ __forceinline__ void mma_k32(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                                        uint32_t c0, uint32_t c1, uint32_t& d0, uint32_t& d1, uint32_t& d2,
+                                        uint32_t& d3) {
+    if (AU8)
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+            : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+    else
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+            : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// 1.5 * 2^23 as float bits: an int32 accumulator started here holds the bit
+// pattern of the float 1.5 * 2^23 + P for |P| < 2^22, so P comes back exactly
+// with one subtraction (no int -> float conversion instruction).
+constexpr uint32_t kAccMagic = 0x4B400000u;
+constexpr float kAccMagicF = 12582912.0f;
+
+// Dot products of one 16-row tile over nbc blocks against the x planes of
+// blocks xb0 .. xb0 + nbc.  q: shared address of the tile's quants
+// ([nbc][16 rows][QB]), sc_off: smem offset of its scales ([nbc][16] f16 in
+// (g, g + 8) pairs).  Lane (g, t) accumulates planes 2t, 2t+1 of rows g and
+// g + 8; the planes are weighted (1, 2^-7, 2^-14) and summed over t at the
+// end.  Returns rows g and g + 8 in the lanes with t == 0.  Not inlined: the
+// kernel's other phases then do not share its registers.
+template <int QT>
+__device__ __noinline__ float2 tile_dot(uint32_t q, uint32_t sc_off, int nbc, uint32_t xq_off, uint32_t xsc_off,
+                                        uint32_t xsm_off, int xb0) {
+    constexpr int QB = QT == 8 ? 32 : 16;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint8_t* sc = smem + sc_off;
+    const uint2* xq = reinterpret_cast<const uint2*>(smem + xq_off);
+    const float* xsc = reinterpret_cast<const float*>(smem + xsc_off);
+    const int* xsm = reinterpret_cast<const int*>(smem + xsm_off);
+    const int lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    // ldmatrix row address of this lane
+    uint32_t lo;
+    if (QT == 8) {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8, half = (lane >> 4) & 1;
+        lo = (uint32_t)(row * 32 + ((half ^ ((row >> 2) & 1)) << 4));  // rows with bit 2 set: halves swapped
+    } else {
+        lo = (uint32_t)((lane & 15) * 16);
+    }
+    const unsigned long long m2 = f2_pack(-kAccMagicF, -kAccMagicF);
+    unsigned long long acc0 = f2_pack(0.0f, 0.0f), acc1 = acc0;
+#pragma unroll 2
+    for (int b = 0; b < nbc; b++) {
+        uint32_t a0, a1, a2, a3;
+        uint32_t c0 = kAccMagic, c1 = kAccMagic;
+        if (QT == 8) {
+            ldsm_x4(q + (uint32_t)(b * 16 * QB) + lo, a0, a1, a2, a3);
+        } else {
+            uint32_t w0, w1;
+            ldsm_x2(q + (uint32_t)(b * 16 * QB) + lo, w0, w1);
+            a0 = w0 & 0x0F0F0F0Fu;         // row g, elements 4t .. 4t+3 (low nibbles)
+            a1 = w1 & 0x0F0F0F0Fu;         // row g + 8
+            a2 = (w0 >> 4) & 0x0F0F0F0Fu;  // row g, elements 16+4t .. (high nibbles)
+            a3 = (w1 >> 4) & 0x0F0F0F0Fu;
+            // (q - 8) . p = q . p - 8 sum(p), per plane (output column)
+            if (2 * t < 3) c0 -= 8u * (uint32_t)xsm[(xb0 + b) * 3 + 2 * t];
+            if (2 * t + 1 < 3) c1 -= 8u * (uint32_t)xsm[(xb0 + b) * 3 + 2 * t + 1];
+        }
+        const uint2 bv = lane < 12 ? xq[(xb0 + b) * 12 + lane] : make_uint2(0u, 0u);
+        uint32_t d0, d1, d2, d3;
+        mma_k32<QT != 8>(a0, a1, a2, a3, bv.x, bv.y, c0, c1, d0, d1, d2, d3);
+        const float2 ds = __half22float2(*reinterpret_cast<const __half2*>(sc + b * 32 + 4 * g));  // rows g, g + 8
+        const float xs = xsc[xb0 + b];
+        const float s0 = ds.x * xs, s1 = ds.y * xs;
+        acc0 = f2_fma(f2_pack(s0, s0), f2_add(f2_pack(__uint_as_float(d0), __uint_as_float(d1)), m2), acc0);
+        acc1 = f2_fma(f2_pack(s1, s1), f2_add(f2_pack(__uint_as_float(d2), __uint_as_float(d3)), m2), acc1);
+    }
+    // lane t holds planes 2t, 2t+1: weights 1, 2^-7 (t = 0), 2^-14, 0 (t = 1)
+    const float p0 = t == 0 ? 1.0f : (t == 1 ? 6.103515625e-05f : 0.0f);
+    const float p1 = t == 0 ? 0.0078125f : 0.0f;
+    const float2 u = f2_unpack(acc0), v = f2_unpack(acc1);
+    float y0 = u.x * p0 + u.y * p1, y1 = v.x * p0 + v.y * p1;
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+    y1 += __shfl_xor_sync(0xffffffffu, y1, 1);
+    y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+    y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
+    return make_float2(y0, y1);
+}
+
+// Splits the staged phase input xs[0 .. 32*nbk) into int8 planes: per
+// 32-block, s = max|x| / 127 and x / s = p0 + p1/128 + p2/16384 (rounded to
+// nearest at each step, |p0| <= 127, |p1|, |p2| <= 64).  Four threads per
+// block, eight elements each; rounding by adding 1.5 * 2^23 (the low byte of
+// the sum is the rounded value as int8).  scale(j, x) is applied to x[j]
+// first (RMSNorm: x[j] * r * gain[j], gains at smem offset g_off; no gains
+// when g_off == 0).  All consumer threads call it (it uses warp shuffles).  Not
+// inlined, so its registers do not add to the kernel's peak.
+__device__ __noinline__ void quantize_planes(uint32_t xs_off, int nbk, uint32_t xq_off, uint32_t xsc_off,
+                                             uint32_t xsm_off, float r, uint32_t g_off, int sums) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const float* xs = reinterpret_cast<const float*>(smem + xs_off);
+    uint8_t* xqb = smem + xq_off;
+    float* xsc = reinterpret_cast<float*>(smem + xsc_off);
+    int* xsm = reinterpret_cast<int*>(smem + xsm_off);
+    const float* gain = reinterpret_cast<const float*>(smem + g_off);
+    const int ct = threadIdx.x - 32;
+    const float M = kAccMagicF;
+    for (int base = 0; base < 4 * nbk; base += kConsumerThreads) {
+        const int i = base + ct;
+        const bool on = i < 4 * nbk;
+        const int b = i >> 2, sub = i & 3;
+        float v[8];
+        float amax = 0.0f;
+        if (on) {
+            const float4 x0 = *reinterpret_cast<const float4*>(xs + b * 32 + sub * 8);
+            const float4 x1 = *reinterpret_cast<const float4*>(xs + b * 32 + sub * 8 + 4);
+            v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+            v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (g_off) v[e] = v[e] * r * gain[b * 32 + sub * 8 + e];
+                amax = fmaxf(amax, fabsf(v[e]));
+            }
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+        uint32_t by[3][8];
+        int sg[3] = {0, 0, 0};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float q = on ? v[e] * inv : 0.0f;
+            const float f0 = q + M, r0 = f0 - M;
+            const float q1 = (q - r0) * 128.0f;
+            const float f1 = q1 + M, r1 = f1 - M;
+            const float f2 = (q1 - r1) * 128.0f + M;
+            by[0][e] = __float_as_uint(f0);
+            by[1][e] = __float_as_uint(f1);
+            by[2][e] = __float_as_uint(f2);
+            if (sums) {
+                sg[0] += (int)r0;
+                sg[1] += (int)r1;
+                sg[2] += (int)(f2 - M);
+            }
+        }
+        if (sums) {
+#pragma unroll
+            for (int gq = 0; gq < 3; gq++) {
+                sg[gq] += __shfl_xor_sync(0xffffffffu, sg[gq], 1);
+                sg[gq] += __shfl_xor_sync(0xffffffffu, sg[gq], 2);
+            }
+        }
+        if (on) {
+            // elements sub*8 + 0..7: word w = sub / 2 (a0 or a2), lane groups
+            // t0 = (sub & 1) * 2 and t0 + 1, bytes e & 3
+            const int w = sub >> 1, t0 = (sub & 1) * 2;
+            uint32_t* xw = reinterpret_cast<uint32_t*>(xqb + b * 96);
+#pragma unroll
+            for (int gq = 0; gq < 3; gq++) {
+                const uint32_t lo = __byte_perm(__byte_perm(by[gq][0], by[gq][1], 0x0040),
+                                                __byte_perm(by[gq][2], by[gq][3], 0x0040), 0x5410);
+                const uint32_t hi = __byte_perm(__byte_perm(by[gq][4], by[gq][5], 0x0040),
+                                                __byte_perm(by[gq][6], by[gq][7], 0x0040), 0x5410);
+                xw[(gq * 4 + t0) * 2 + w] = lo;
+                xw[(gq * 4 + t0 + 1) * 2 + w] = hi;
+            }
+            if (sub == 0) {
+                xsc[b] = amax / 127.0f;
+                if (sums) {
+                    xsm[b * 3 + 0] = sg[0];
+                    xsm[b * 3 + 1] = sg[1];
+                    xsm[b * 3 + 2] = sg[2];
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 
-template <int QT>
+template <int QT, bool MV, bool TR>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, const StepArgs a) {
-    constexpr int US = QT == 8 ? 16 : 32;  // values per lane unit
+    constexpr int US = QT == 8 ? 16 : 32;  // matvec: values per lane unit
+    constexpr int QB = QT == 8 ? 32 : 16;  // tiled: quant bytes per row and block
     extern __shared__ __align__(128) uint8_t smem[];
     const int NS = m.nslots;
     const int SB = m.slot_bytes;
-    const SmemOffsets so = smem_offsets(NS, SB, m.xs_floats, m.ybuf_floats, m.cfloats);
+    const SmemOffsets so = smem_offsets(NS, SB, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx);
     uint8_t* ring = smem;
     float* xs = reinterpret_cast<float*>(smem + so.xs);
+    uint8_t* xqb = smem + so.xq;
+    float* xsc = reinterpret_cast<float*>(smem + so.xsc);
+    int* xsm = reinterpret_cast<int*>(smem + so.xsm);
     float* xres = reinterpret_cast<float*>(smem + so.xres);
     float* ybuf = reinterpret_cast<float*>(smem + so.ybuf);
     float* cb = reinterpret_cast<float*>(smem + so.cbuf);
@@ -592,12 +819,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     int* misc = reinterpret_cast<int*>(smem + so.misc);
     volatile unsigned* pstop = reinterpret_cast<volatile unsigned*>(misc + 31);  // first chunk not issued
     volatile int* dead = misc + 30;  // set by any consumer thread whose wait failed
+    unsigned* issued = reinterpret_cast<unsigned*>(misc + 29);  // chunks the producer has issued
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = blockIdx.x, grid = gridDim.x;
 
     // A device-resident greedy loop that already produced EOS does no work.
-    if (a.done && *(volatile const int*)a.done) return;
+    if (!MV && a.done && *(volatile const int*)a.done) return;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; s++) {
@@ -606,48 +834,120 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         }
         *pstop = 0xffffffffu;
         *dead = 0;
+        *issued = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
 
     // ------------------------------------------------------------ producer
+    // Lanes 0..np-1 of warp 0 each issue one chunk of every batch of np
+    // consecutive chunks: the lanes share one instruction stream, so the warp
+    // issues several chunks for the cost of one (the producer shares its SM
+    // sub-partition with three busy consumer warps).  np <= the ring size, so
+    // no batch holds two chunks of one slot.  Slots, ring rounds, tile groups
+    // and K-slices advance incrementally.
     if (warp == 0) {
-        if (lane == 0) {
-            unsigned gidx = 0;
+        constexpr int kProdLanes = 4;
+        const int np = NS < kProdLanes ? NS : kProdLanes;
+        if (lane < kProdLanes) {
+            unsigned gbase_p = 0;  // global index of the phase's first chunk
             bool ok = true;
-            for (int p = a.p_begin; p < a.p_end && ok; p++) {
-                Geom g = phase_geom(m, a, p);
-                Split s = cta_split(g, cta, grid, SB);
-                for (int k = 0; k < s.nchunks && ok; k++, gidx++) {
-                    if (a.trace && (k == 0 || k == s.nchunks - 1))
-                        a.trace[((size_t)(p - a.p_begin) * kTraceSlots + (k == 0 ? 4 : 5)) * grid + cta] = global_ns();
-                    const int slot = gidx % NS;
-                    const uint32_t round = gidx / NS;
-                    if (*(volatile int*)m.err || !slot_wait(&empty[slot], (round & 1) ^ 1, m.err)) {
-                        *pstop = gidx;  // consumers skip chunks from here on
+            for (int p = a.p_begin; p < a.p_end; p++) {
+                const size_t trp = (size_t)(p - a.p_begin) * kTraceSlots;
+                int nchunks;
+                TGeom g{};
+                TPlan pl{};
+                Geom mg{};
+                Split ms{};
+                if (MV) {
+                    mg = Geom{a.mv_w, a.mv_rb, a.mv_cols, a.mv_rows};
+                    ms = cta_split(mg, cta, grid, SB);
+                    nchunks = ms.nchunks;
+                    pl.nks = 1;
+                } else {
+                    g = phase_geom(m, a, p);
+                    if (!g.w) continue;
+                    pl = tile_plan(g.tiles, g.nb, tile_unit_bytes(g, QT), cta, grid, SB, kConsumerWarps);
+                    nchunks = pl.nchunks;
+                }
+                if (TR && a.trace && lane == 0 && nchunks) a.trace[(trp + 4) * grid + cta] = global_ns();
+                uint64_t waited = 0;
+                const size_t sreg = MV ? 0 : (size_t)g.tiles * kTileRows * g.nb * QB;  // scale region offset
+                // this lane's first chunk k = lane, and its position
+                int slot = (int)((gbase_p + lane) % NS);
+                uint32_t par = (((gbase_p + lane) / NS) & 1u) ^ 1u;  // free-slot wait parity
+                int kt = lane / pl.nks, ks = lane - kt * pl.nks;
+                const int dq = np / pl.nks, dr = np - dq * pl.nks;
+                for (int k0 = 0; k0 < nchunks; k0 += np) {
+                    const int k = k0 + lane;
+                    const bool mine = lane < np && k < nchunks;
+                    // 1. every lane waits for its slot; 2. only lanes before the
+                    // first failed wait issue, so no copy goes out past *pstop
+                    bool got = false;
+                    if (mine) {
+                        const uint64_t t0w = (TR && a.trace) ? global_ns() : 0;
+                        got = slot_wait(&empty[slot], par, m.err);
+                        if (TR && a.trace) waited += global_ns() - t0w;
+                    }
+                    const unsigned bad = __ballot_sync(0xfu, mine && !got);
+                    const int first_bad = bad ? __ffs(bad) - 1 : kProdLanes;
+                    if (mine && lane < first_bad) {
+                        uint8_t* dst = ring + (size_t)slot * SB;
+                        if (MV) {
+                            const int uu0 = ms.u0 + k * ms.cu;
+                            const int nu = min(ms.cu, ms.n - k * ms.cu);
+                            const size_t nbytes = (size_t)nu * mg.rb;
+                            const uint8_t* src = mg.w + (size_t)uu0 * mg.rb;
+                            const uint8_t* sal =
+                                reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15));
+                            const uint32_t len = (uint32_t)(((src - sal) + nbytes + 15) & ~size_t(15));
+                            mbar_arrive_expect_tx(&full[slot], len);
+                            bulk_g2s(dst, sal, len, &full[slot]);
+                        } else {
+                            // chunk k = (tile group kt, K-slice ks)
+                            const int t0 = pl.u0 + kt * pl.nt, ntc = min(pl.nt, pl.u0 + pl.n - t0);
+                            const int bb0 = ks * pl.bpk, nbc = min(pl.bpk, g.nb - bb0);
+                            const size_t unit0 = (size_t)t0 * g.nb + bb0;
+                            const uint32_t qlen = (uint32_t)(ntc * nbc * kTileRows * QB);
+                            const uint32_t slen = (uint32_t)(ntc * nbc * 2 * kTileRows);
+                            mbar_arrive_expect_tx(&full[slot], (qlen + slen) * (g.w2 ? 2u : 1u));
+                            bulk_g2s(dst, g.w + unit0 * kTileRows * QB, qlen, &full[slot]);
+                            bulk_g2s(dst + qlen, g.w + sreg + unit0 * 2 * kTileRows, slen, &full[slot]);
+                            if (g.w2) {
+                                bulk_g2s(dst + qlen + slen, g.w2 + unit0 * kTileRows * QB, qlen, &full[slot]);
+                                bulk_g2s(dst + 2 * qlen + slen, g.w2 + sreg + unit0 * 2 * kTileRows, slen, &full[slot]);
+                            }
+                        }
+                    }
+                    __syncwarp(0xfu);
+                    // publish the chunks issued (in order); after a failed wait,
+                    // consumers skip every chunk from the first one not issued
+                    const int nis = bad ? first_bad : min(np, nchunks - k0);
+                    if (bad && lane == 0) *pstop = gbase_p + (unsigned)(k0 + first_bad);
+                    if (lane == 0) st_release_cta(issued, gbase_p + (unsigned)(k0 + nis));
+                    if (bad) {
                         ok = false;
                         break;
                     }
-                    const int uu0 = s.u0 + k * s.cu;
-                    const int nu = min(s.cu, s.n - k * s.cu);
-                    const size_t r0 = (size_t)uu0 * g.rpu, nbytes = (size_t)nu * g.rpu * g.rb;
-                    const uint8_t* src = g.w + r0 * g.rb;
-                    const uint8_t* sal = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15));
-                    const uint32_t len1 = (uint32_t)(((src - sal) + nbytes + 15) & ~size_t(15));
-                    uint32_t total = len1, len2 = 0, off2 = 0;
-                    const uint8_t* sal2 = nullptr;
-                    if (g.w2) {
-                        const uint8_t* src2 = g.w2 + r0 * g.rb;
-                        sal2 = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src2) & ~uintptr_t(15));
-                        len2 = (uint32_t)(((src2 - sal2) + nbytes + 15) & ~size_t(15));
-                        off2 = (len1 + 127) & ~127u;
-                        total = len1 + len2;
+                    slot += np;
+                    while (slot >= NS) {
+                        slot -= NS;
+                        par ^= 1u;
                     }
-                    uint8_t* dst = ring + (size_t)slot * SB;
-                    mbar_arrive_expect_tx(&full[slot], total);
-                    bulk_g2s(dst, sal, len1, &full[slot]);
-                    if (g.w2) bulk_g2s(dst + off2, sal2, len2, &full[slot]);
+                    ks += dr;
+                    kt += dq;
+                    if (ks >= pl.nks) {
+                        ks -= pl.nks;
+                        kt++;
+                    }
                 }
+                if (TR && a.trace && lane == 0 && nchunks) {
+                    a.trace[(trp + 5) * grid + cta] = global_ns();
+                    a.trace[(trp + 8) * grid + cta] = waited;
+                    a.trace[(trp + 9) * grid + cta] = (unsigned)nchunks;
+                }
+                gbase_p += (unsigned)nchunks;
+                if (!ok) break;
             }
         }
         return;
@@ -658,9 +958,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     const int ct = threadIdx.x - 32;      // consumer thread index
     unsigned gbase = 0;                   // chunk index of the phase's first chunk
     bool alive = true;
-    const int tok = a.mv_w ? 0 : *a.tok;
-    const int own0 = (int)((long long)cta * m.H / grid);  // residual rows [own0, own1)
-    const int own1 = (int)((long long)(cta + 1) * m.H / grid);
+    const int tok = MV ? 0 : *a.tok;
+    // residual rows this CTA owns: its tiles of the H-row phases (Wo, down)
+    const int own0 = kTileRows * (int)((long long)cta * (m.H / kTileRows) / grid);
+    const int own1 = kTileRows * (int)((long long)(cta + 1) * (m.H / kTileRows) / grid);
     // Consumer barrier that also makes `alive` uniform across the CTA: a
     // failed wait in any thread stops the work of all (warp collectives in
     // the row loop must never run with part of a warp).
@@ -670,16 +971,60 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         alive = (*dead == 0);
     };
 
+    if (MV) {
+        // ---- kernel-level matvec: y = W x, ggml rows, fp32 dequantising dot
+        const Geom mg{a.mv_w, a.mv_rb, a.mv_cols, a.mv_rows};
+        const Split s = cta_split(mg, cta, grid, SB);
+        const int nu = mg.cols / US;
+        for (int j = ct; j < mg.cols; j += kConsumerThreads) xs[xs_index<US>(j, nu)] = a.mv_x[j];
+        sync_alive();
+        for (int k = 0; k < s.nchunks; k++) {
+            const unsigned gidx = k;
+            if ((int)(gidx % kConsumerWarps) != cw) continue;
+            const int slot = gidx % NS;
+            const bool landed = __all_sync(0xffffffffu, chunk_wait(&full[slot], (gidx / NS) & 1, gidx, pstop, issued, m.err));
+            if (!landed) alive = false;
+            if (alive) {
+                const int uu0 = s.u0 + k * s.cu;
+                const int nrows = min(s.cu, s.n - k * s.cu);
+                const uint8_t* src = mg.w + (size_t)uu0 * mg.rb;
+                const uint8_t* base1 = ring + (size_t)slot * SB + (reinterpret_cast<uintptr_t>(src) & 15);
+                for (int pi = 0; pi < (nrows + 1) / 2; pi++) {
+                    const uint8_t* ra = base1 + (size_t)(2 * pi) * mg.rb;
+                    const bool two = (2 * pi + 1) < nrows;
+                    const uint8_t* rb2 = two ? ra + mg.rb : ra;
+                    float a0, a1;
+                    if (QT == 8) dot2_q8(ra, rb2, two, xs, mg.cols, lane, a0, a1);
+                    else dot2_q4(ra, rb2, two, xs, mg.cols, lane, a0, a1);
+                    const float v = warp_sum2(a0, a1, lane);
+                    if (lane == 0) a.mv_y[uu0 + 2 * pi] = v;
+                    if (lane == 16 && two) a.mv_y[uu0 + 2 * pi + 1] = v;
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && landed) mbar_arrive(&empty[slot]);
+        }
+        return;
+    }
+
     for (int p = a.p_begin; p < a.p_end; p++) {
-        const Geom g = phase_geom(m, a, p);
-        const Split s = cta_split(g, cta, grid, SB);
-        const bool has_rows = s.nchunks > 0;
+        const TGeom g = phase_geom(m, a, p);
+        const TPlan pl = g.w ? tile_plan(g.tiles, g.nb, tile_unit_bytes(g, QT), cta, grid, SB, kConsumerWarps)
+                             : TPlan{0, 0, 1, 1, 1, 0};
+        const bool has_rows = pl.nchunks > 0;
         const size_t tr = (size_t)(p - a.p_begin) * kTraceSlots;
-        if (a.trace && ct == 0) a.trace[(tr + 0) * grid + cta] = global_ns();
+        if (TR && a.trace && ct == 0) {
+            a.trace[(tr + 0) * grid + cta] = global_ns();
+            misc[20] = 0;
+            misc[21] = 0;
+            misc[22] = 0;
+            misc[23] = 0;
+            misc[24] = 0;
+        }
         const unsigned tag_here = ll_tag(a.epoch, g.layer) + a.skew;
         const unsigned tag_prev = ll_tag(a.epoch, g.layer - 1) + a.skew;
 
-        // 1. stage the phase input
+        // 1. stage the phase input: gather (+ norm / merge) into xs, then planes
         if (g.kind == PH_QKV && g.layer == 0) {
             // transformer.go:524-531: the residual stream starts at the embedding
             for (int j = own0 + ct; j < own1; j += kConsumerThreads) xres[j - own0] = embed_elem(m, tok, j);
@@ -691,7 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             for (int i = ct; i < m.H / 4; i += kConsumerThreads) cp_async16(cb + 4 * i, nw + 4 * i);
             if (g.kind == PH_QKV) {
                 const float* bq = m.layers[g.layer].bqkv;
-                const int r0b = (2 * s.u0) & ~3, r1 = 2 * (s.u0 + s.n);
+                const int r0b = (kTileRows * pl.u0) & ~3, r1 = kTileRows * (pl.u0 + pl.n);
                 if (bq)
                     for (int i = ct; i < (r1 - r0b + 3) / 4; i += kConsumerThreads)
                         cp_async16(cb + cb_bias(m) + 4 * i, bq + r0b + 4 * i);
@@ -703,42 +1048,36 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             }
             cp_async_commit();
             // RMSNorm (transformer.go:922-932) fused into the stage
-            const int nu_h = m.H / US;
             float ss = 0.0f;
             if (g.kind == PH_QKV && g.layer == 0) {
                 for (int j = ct; j < m.H; j += kConsumerThreads) {
                     const float v = embed_elem(m, tok, j);
-                    xs[xs_index<US>(j, nu_h)] = v;
+                    xs[j] = v;
                     ss += v * v;
                 }
             } else if (alive) {
                 const uint2* src = g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2;
                 const unsigned tg = g.kind == PH_GATEUP ? tag_here : tag_prev;
-                const GatherRes gr = ll_gather_s(src, m.H, tg, m.err, smem_u32(xs), US, nu_h, 1);
+                const GatherRes gr = ll_gather_s(src, m.H, tg, m.err, smem_u32(xs), 0, 0, 1);
                 alive = gr.ok;
                 ss = gr.ss;
             }
-            if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+            if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
             cp_async_wait();
-            const float tot = block_sum(ss, red, cw);  // its barriers also publish cb[]
+            const float tot = block_sum(ss, red, cw);  // its barriers also publish xs[] and cb[]
             const float r = (float)(1.0 / sqrt((double)(tot / (float)m.H) + (double)m.eps));
-            for (int j = ct; j < m.H; j += kConsumerThreads) {
-                float* px = xs + xs_index<US>(j, nu_h);
-                *px = *px * r * cb[j];
-            }
+            quantize_planes(so.xs, m.H / 32, so.xq, so.xsc, so.xsm, r, so.cbuf, QT != 8);
         } else if (g.kind == PH_WO && has_rows) {
-            const int nu_q = m.qd / US;
             if (a.splits == 1) {
-                if (alive)
-                    alive = ll_gather_s(m.ll_attn, m.qd, tag_here, m.err, smem_u32(xs), US, nu_q, 0).ok;
-                if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+                if (alive) alive = ll_gather_s(m.ll_attn, m.qd, tag_here, m.err, smem_u32(xs), 0, 0, 0).ok;
+                if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+                named_bar_sync(1, kConsumerThreads);
             } else {
                 // merge the context splits: o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M)
                 const int S = a.splits, hd = m.hd, W2 = hd + 2;
                 float* part = xs + m.qd;  // [nh][S][hd+2] after the qd outputs
-                if (alive)
-                    alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0, 0, 0).ok;
-                if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+                if (alive) alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0, 0, 0).ok;
+                if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
                 named_bar_sync(1, kConsumerThreads);
                 for (int i = ct; i < m.qd; i += kConsumerThreads) {
                     const int hh = i / hd, d = i - hh * hd;
@@ -752,28 +1091,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                         Ls = fmaf(ph[s2 * W2 + hd + 1], w, Ls);
                         o = fmaf(ph[s2 * W2 + d], w, o);
                     }
-                    xs[xs_index<US>(i, nu_q)] = o / Ls;
+                    xs[i] = o / Ls;
                 }
+                named_bar_sync(1, kConsumerThreads);
             }
+            quantize_planes(so.xs, m.qd / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);
         } else if (g.kind == PH_DOWN && has_rows) {
-            const int nu_f = m.FF / US;
-            if (alive)
-                alive = ll_gather_s(m.ll_act, m.FF, tag_here, m.err, smem_u32(xs), US, nu_f, 0).ok;
-            if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-        } else if (g.kind == PH_MATVEC) {
-            const int nu = g.cols / US;
-            for (int j = ct; j < g.cols; j += kConsumerThreads) xs[xs_index<US>(j, nu)] = a.mv_x[j];
+            if (alive) alive = ll_gather_s(m.ll_act, m.FF, tag_here, m.err, smem_u32(xs), 0, 0, 0).ok;
+            if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+            named_bar_sync(1, kConsumerThreads);
+            quantize_planes(so.xs, m.FF / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);
         } else {
-            if (a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
+            if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         }
         sync_alive();
-        if (a.trace && ct == 0) a.trace[(tr + 2) * grid + cta] = global_ns();
+        if (TR && a.trace && ct == 0) a.trace[(tr + 2) * grid + cta] = global_ns();
 
         float* yb = ybuf + (p & 1) * m.ybuf_floats;  // parity buffers: the next phase's
                                                       // dots may start before this epilogue ends
+        const int rc = kTileRows * pl.n * (g.w2 ? 2 : 1);  // outputs of one K-slice in yb
         if (g.kind == PH_ATTN) {
             // 2'. attention, one (query head, split) per CTA
-            if (cta < m.nh * a.splits) {
+            if (cta < g.units) {
                 const int S = a.splits, hd = m.hd;
                 const int h = cta / S, sidx = cta - h * S, kvh = h / (m.nh / m.nkv);
                 const int ctx = a.pos + 1;
@@ -794,62 +1133,89 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                                                 a.pos, tag_here, tout, out, S != 1, m.err, so.xs, so.red, alive);
             }
         } else {
-            // 2. rows: dot products of this CTA's weight rows into yb
-            const int rbase = g.rpu * s.u0;
-            for (int k = 0; k < s.nchunks; k++) {
+            // 2. rows: tensor-core dot products of this CTA's tiles into yb
+            const uint64_t tl0 = (TR && a.trace) ? global_ns() : 0;
+            // this warp's chunks are k = first, first + kConsumerWarps, ... (global
+            // index = cw mod kConsumerWarps); slot, ring round, tile group and
+            // K-slice advance incrementally (no divisions in the loop)
+            const int first = (int)((unsigned)(cw + kConsumerWarps) - gbase % kConsumerWarps) % kConsumerWarps;
+            int slot = (int)((gbase + first) % NS);
+            uint32_t par = ((gbase + first) / NS) & 1u;
+            int kt = first / pl.nks, ks = first - kt * pl.nks;
+            const int dq = kConsumerWarps / pl.nks, dr = kConsumerWarps - dq * pl.nks;
+            for (int k = first; k < pl.nchunks; k += kConsumerWarps) {
                 const unsigned gidx = gbase + k;
-                if ((int)(gidx % kConsumerWarps) != cw) continue;
-                const int slot = gidx % NS;
-                const bool landed =
-                    __all_sync(0xffffffffu, chunk_wait(&full[slot], (gidx / NS) & 1, gidx, pstop, m.err));
+                const uint64_t tw = (TR && a.trace) ? global_ns() : 0;
+                const bool landed = __all_sync(0xffffffffu, chunk_wait(&full[slot], par, gidx, pstop, issued, m.err));
+                if (TR && a.trace && lane == 0) {
+                    const unsigned dt = (unsigned)(global_ns() - tw);
+                    atomicAdd(reinterpret_cast<unsigned*>(misc + 20), dt);
+                    if (dt > 256) atomicAdd(reinterpret_cast<unsigned*>(misc + 21), 1u);
+                }
                 if (!landed) alive = false;
                 if (alive) {
-                    const uint8_t* dst = ring + (size_t)slot * SB;
-                    const int uu0 = s.u0 + k * s.cu;
-                    const int nu = min(s.cu, s.n - k * s.cu);
-                    const size_t r0 = (size_t)uu0 * g.rpu;
-                    const uint8_t* src = g.w + r0 * g.rb;
-                    const uint8_t* base1 = dst + (reinterpret_cast<uintptr_t>(src) & 15);
-                    const uint8_t* base2 = base1;
-                    if (g.w2) {
-                        const uintptr_t s2 = reinterpret_cast<uintptr_t>(g.w2 + r0 * g.rb);
-                        const uint32_t len1 = (uint32_t)((((uintptr_t)src & 15) + (size_t)nu * g.rb + 15) & ~size_t(15));
-                        base2 = dst + ((len1 + 127) & ~127u) + (s2 & 15);
-                    }
-                    const int nrows = nu * g.rpu;
-                    const int npairs = g.w2 ? nrows : (nrows + 1) / 2;
-                    for (int pi = 0; pi < npairs; pi++) {
-                        const uint8_t *ra, *rb2;
-                        bool two;
-                        int yi;  // output index of the pair's first row in yb
+                    const int lt0 = kt * pl.nt, ntc = min(pl.nt, pl.n - lt0);
+                    const int bb0 = ks * pl.bpk, nbc = min(pl.bpk, g.nb - bb0);
+                    const int qlen = ntc * nbc * kTileRows * QB, slen = ntc * nbc * 2 * kTileRows;
+                    float* yk = yb + ks * rc;
+                    for (int tl = 0; tl < ntc; tl++) {
+                        const uint32_t qa = (uint32_t)(slot * SB + tl * nbc * kTileRows * QB);
+                        const uint32_t sa = (uint32_t)(slot * SB + qlen + tl * nbc * 2 * kTileRows);
+                        const uint64_t td0 = (TR && a.trace) ? global_ns() : 0;
+                        const float2 y = tile_dot<QT>(smem_u32(smem) + qa, sa, nbc, so.xq, so.xsc, so.xsm, bb0);
+                        if (TR && a.trace && lane == 0) atomicAdd(reinterpret_cast<unsigned*>(misc + 22), (unsigned)(global_ns() - td0));
+                        const int lr = (lt0 + tl) * kTileRows + (lane >> 2);  // local row of y.x; y.y is lr + 8
                         if (g.w2) {
-                            ra = base1 + (size_t)pi * g.rb;
-                            rb2 = base2 + (size_t)pi * g.rb;
-                            two = true;
-                            yi = 2 * (uu0 - s.u0 + pi);  // gate, up interleaved
-                        } else {
-                            ra = base1 + (size_t)(2 * pi) * g.rb;
-                            two = (2 * pi + 1) < nrows;
-                            rb2 = two ? ra + g.rb : ra;
-                            yi = (int)r0 - rbase + 2 * pi;
+                            const uint32_t o2 = (uint32_t)(qlen + slen);
+                            const float2 u = tile_dot<QT>(smem_u32(smem) + qa + o2, sa + o2, nbc, so.xq, so.xsc, so.xsm, bb0);
+                            if ((lane & 3) == 0) {
+                                yk[2 * lr] = y.x;
+                                yk[2 * lr + 1] = u.x;
+                                yk[2 * (lr + 8)] = y.y;
+                                yk[2 * (lr + 8) + 1] = u.y;
+                            }
+                        } else if ((lane & 3) == 0) {
+                            yk[lr] = y.x;
+                            yk[lr + 8] = y.y;
                         }
-                        float a0, a1;
-                        if (QT == 8) dot2_q8(ra, rb2, two, xs, g.cols, lane, a0, a1);
-                        else dot2_q4(ra, rb2, two, xs, g.cols, lane, a0, a1);
-                        const float v = warp_sum2(a0, a1, lane);
-                        if (lane == 0) yb[yi] = v;
-                        if (lane == 16 && two) yb[yi + 1] = v;
                     }
                 }
                 __syncwarp();
                 if (lane == 0 && landed) mbar_arrive(&empty[slot]);
+                slot += kConsumerWarps;
+                while (slot >= NS) {
+                    slot -= NS;
+                    par ^= 1u;
+                }
+                ks += dr;
+                kt += dq;
+                if (ks >= pl.nks) {
+                    ks -= pl.nks;
+                    kt++;
+                }
             }
-            gbase += s.nchunks;
+            gbase += pl.nchunks;
+            if (TR && a.trace && lane == 0) {
+                const unsigned dl = (unsigned)(global_ns() - tl0);
+                atomicAdd(reinterpret_cast<unsigned*>(misc + 23), dl);
+                atomicMax(reinterpret_cast<unsigned*>(misc + 24), dl);
+            }
         }
         sync_alive();
+        if (TR && a.trace && ct == 0) {
+            a.trace[(tr + 10) * grid + cta] = global_ns();
+            a.trace[(tr + 11) * grid + cta] = (unsigned)misc[22] | ((unsigned long long)(unsigned)misc[23] << 32);
+            a.trace[(tr + 9) * grid + cta] |= (unsigned long long)(unsigned)misc[24] << 32;
+        }
 
-        // 3. epilogue, one thread per output
+        // 3. epilogue, one thread per output; K-slice partials summed in order
         const unsigned tag = ll_tag(a.epoch, g.layer);
+        const int row0 = kTileRows * pl.u0;
+        auto ysum = [&](int i) {
+            float v = yb[i];
+            for (int ks = 1; ks < pl.nks; ks++) v += yb[ks * rc + i];
+            return v;
+        };
         if ((alive && has_rows) || g.kind == PH_LMHEAD) {
             // (every CTA takes part in the argmax, so its arrival counter
             // always completes and resets)
@@ -858,20 +1224,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     // bias (transformer.go:632-646), RoPE on interleaved pairs
                     // (936-951), KV append (654-656)
                     const bool bias = m.layers[g.layer].bqkv != nullptr;
-                    const int bias0 = (2 * s.u0) & ~3;
-                    for (int j = ct; j < s.n; j += kConsumerThreads) {
-                        const int row = 2 * (s.u0 + j);
-                        float a0 = yb[2 * j], a1 = yb[2 * j + 1];
+                    const int bias0 = row0 & ~3;
+                    for (int j = ct; j < kTileRows / 2 * pl.n; j += kConsumerThreads) {
+                        const int row = row0 + 2 * j;
+                        float a0 = ysum(2 * j), a1 = ysum(2 * j + 1);
                         if (bias) {
                             a0 += cb[cb_bias(m) + row - bias0];
                             a1 += cb[cb_bias(m) + row + 1 - bias0];
                         }
                         if (row < m.qd + m.kvd) {
                             const int pi2 = (row % m.hd) >> 1;
-                            const float rc = cb[cb_cos(m) + pi2], rs = cb[cb_sin(m) + pi2];
+                            const float rc2 = cb[cb_cos(m) + pi2], rs = cb[cb_sin(m) + pi2];
                             const float x0 = a0, x1 = a1;
-                            a0 = x0 * rc - x1 * rs;
-                            a1 = x0 * rs + x1 * rc;
+                            a0 = x0 * rc2 - x1 * rs;
+                            a1 = x0 * rs + x1 * rc2;
                         }
                         ll_store2(m.ll_qkv + row, a0, a1, tag);
                         if (row >= m.qd) {
@@ -892,9 +1258,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 }
                 case PH_GATEUP:
                     // SwiGLU (transformer.go:725-727, 954-956)
-                    for (int j = ct; j < s.n; j += kConsumerThreads) {
-                        const float gv = yb[2 * j], uv = yb[2 * j + 1];
-                        ll_store(m.ll_act + s.u0 + j, gv / (1.0f + expf(-gv)) * uv, tag);
+                    for (int j = ct; j < kTileRows * pl.n && row0 + j < g.rows; j += kConsumerThreads) {
+                        const float gv = ysum(2 * j), uv = ysum(2 * j + 1);
+                        ll_store(m.ll_act + row0 + j, gv / (1.0f + expf(-gv)) * uv, tag);
                     }
                     break;
                 case PH_WO:
@@ -902,20 +1268,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     // residual (transformer.go:576-578, 591-593); the rows are
                     // exactly the residual rows this CTA owns
                     uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
-                    for (int j = ct; j < s.n; j += kConsumerThreads) {
-                        const int row = s.u0 + j;
-                        const float xr = xres[row - own0] + yb[j];
-                        xres[row - own0] = xr;
-                        ll_store(dstll + row, xr, tag);
+                    for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
+                        const float xr = xres[j] + ysum(j);
+                        xres[j] = xr;
+                        ll_store(dstll + row0 + j, xr, tag);
                     }
                     break;
                 }
-                case PH_LMHEAD: {
+                default: {  // PH_LMHEAD
                     // logits + argmax, first maximum wins (transformer.go:1038-1046)
                     Best best{-INFINITY, 0x7fffffff};
-                    for (int j = ct; alive && j < s.n; j += kConsumerThreads) {
-                        const int row = s.u0 + j;
-                        const float v = yb[j];
+                    for (int j = ct; alive && j < kTileRows * pl.n; j += kConsumerThreads) {
+                        const int row = row0 + j;
+                        if (row >= g.rows) break;
+                        const float v = ysum(j);
                         m.logits[row] = v;
                         if (better(v, row, best.v, best.i)) { best.v = v; best.i = row; }
                     }
@@ -931,47 +1297,56 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                         Best b{red[0], misc[4]};
                         for (int w = 1; w < kConsumerWarps; w++)
                             if (better(red[w], misc[4 + w], b.v, b.i)) { b.v = red[w]; b.i = misc[4 + w]; }
-                        m.best_val[cta] = b.v;
-                        m.best_idx[cta] = b.i;
+                        // one atomic max per CTA on (order-preserving value bits, ~index):
+                        // the largest value wins, and among equal values the lowest index
+                        if (b.i != 0x7fffffff) {
+                            const uint32_t u = __float_as_uint(b.v);
+                            const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+                            atomicMax(m.am_key, ((unsigned long long)ord << 32) | (uint32_t)~(uint32_t)b.i);
+                        }
                         __threadfence();
                         const unsigned old = atom_acq_rel_add(m.am_ctr, 1u);
                         if (old == (unsigned)(grid - 1)) {
-                            Best f{-INFINITY, 0x7fffffff};
-                            for (int c2 = 0; c2 < grid; c2++) {
-                                const float v = __ldcg(m.best_val + c2);
-                                const int i = __ldcg(m.best_idx + c2);
-                                if (better(v, i, f.v, f.i)) { f.v = v; f.i = i; }
-                            }
-                            if (f.i == 0x7fffffff) f.i = 0;
-                            *m.token = f.i;
-                            if (a.out_ids) a.out_ids[a.step] = f.i;
-                            if (a.done && f.i == a.eos) *a.done = 1;
+                            // last CTA: every other CTA's max is in am_key
+                            const unsigned long long key = atomicExch(m.am_key, 0ull);
+                            const int f = key ? (int)~(uint32_t)key : 0;
+                            *m.token = f;
+                            if (a.out_ids) a.out_ids[a.step] = f;
+                            if (a.done && f == a.eos) *a.done = 1;
                             atomicExch(m.am_ctr, 0u);
                         }
                     }
                     break;
                 }
-                default:  // PH_MATVEC
-                    for (int j = ct; j < s.n; j += kConsumerThreads) a.mv_y[s.u0 + j] = yb[j];
-                    break;
             }
         }
-        if (a.trace && ct == 0) a.trace[(tr + 3) * grid + cta] = global_ns();
+        if (TR && a.trace && ct == 0) {
+            a.trace[(tr + 3) * grid + cta] = global_ns();
+            a.trace[(tr + 6) * grid + cta] = (unsigned)misc[20];
+            a.trace[(tr + 7) * grid + cta] = (unsigned)misc[21];
+        }
     }
 }
 
 }  // namespace
 
 size_t decode_smem_bytes(const ModelDev& m) {
-    return smem_offsets(m.nslots, m.slot_bytes, m.xs_floats, m.ybuf_floats, m.cfloats).total;
+    return smem_offsets(m.nslots, m.slot_bytes, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx).total;
 }
 
 int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err) {
     const size_t smem = decode_smem_bytes(m);
     void* args[] = {(void*)&m, (void*)&a};
-    const void* fn = m.qtype == 8 ? (const void*)decode_kernel<8> : (const void*)decode_kernel<2>;
-    static bool attr_done[2] = {false, false};
-    const int ti = m.qtype == 8 ? 0 : 1;
+    // instantiations: (Q8_0, Q4_0) x (model, matvec) x (plain, traced); the
+    // plain kernels carry no trace code at all (smaller instruction footprint)
+    const bool mv = a.mv_w != nullptr;
+    const int ti = (m.qtype == 8 ? 0 : 1) + (mv ? 2 : 0) + (a.trace ? 4 : 0);
+    const void* fns[8] = {(const void*)decode_kernel<8, false, false>, (const void*)decode_kernel<2, false, false>,
+                          (const void*)decode_kernel<8, true, false>,  (const void*)decode_kernel<2, true, false>,
+                          (const void*)decode_kernel<8, false, true>,  (const void*)decode_kernel<2, false, true>,
+                          (const void*)decode_kernel<8, true, true>,   (const void*)decode_kernel<2, true, true>};
+    const void* fn = fns[ti];
+    static bool attr_done[8] = {false, false, false, false, false, false, false, false};
     if (!attr_done[ti]) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
         if (e != cudaSuccess) {

@@ -34,14 +34,120 @@ constexpr int kMaxAttnTile = 128;                     // positions per attention
 constexpr int kMaxOwnRows = 64;                       // residual rows one CTA keeps (H / grid)
 constexpr int kMaxQkvRows = 128;                      // QKV rows one CTA computes ((qd + 2*kvd) / grid)
 // Phase trace slots: consumer phase start, input ready, input staged, work
-// done; producer first and last weight copy issued (globaltimer ns).
-constexpr int kTraceSlots = 6;
+// done; producer first and last weight copy issued (globaltimer ns); total ns
+// the consumer warps spent waiting for weight chunks, and how many of those
+// waits took longer than 256 ns; ns the producer waited for free ring slots,
+// and the chunks it issued; consumer rows loop done (before the epilogue);
+// total ns the consumer warps spent in tile dot products.
+constexpr int kTraceSlots = 12;
+
+// Weight matrices live in HBM in a tiled form of their ggml blocks, made at
+// load time (same bytes per weight as the GGUF file):
+//   quants [Rp/16 tiles][nb blocks][16 rows][QB bytes]   QB = 32 (Q8_0) or 16 (Q4_0)
+//   scales [Rp/16 tiles][nb blocks][16] f16              right after the quants
+// Rp = rows rounded up to 16 (padding rows are zero).  A (tile, block) unit
+// is contiguous, so any range of tiles x blocks is two 16-byte aligned copies,
+// and in shared memory it is the 16 x 32-byte A operand of one int8
+// mma.m16n8k32 (ldmatrix).  For Q8_0, rows with bit 2 set store their two
+// 16-byte halves swapped, so ldmatrix reads any 8 rows of either half
+// without bank conflicts.  The 16 scales of a unit are stored in the order
+// rows 0, 8, 1, 9, ..., 7, 15: the mma lane that owns rows g and g + 8 reads
+// both with one 32-bit load.
+constexpr int kTileRows = 16;
+
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+int tile_qb(int qtype) { return qtype == 8 ? 32 : 16; }
+
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+int64_t tiled_rows(int64_t rows) { return (rows + kTileRows - 1) / kTileRows * kTileRows; }
+
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+size_t tiled_bytes(int64_t rows, int64_t cols, int qtype) {
+    return (size_t)(tiled_rows(rows) * (cols / 32) * (tile_qb(qtype) + 2));
+}
+
+// Byte offset of quant byte e (0..31 for Q8_0, 0..15 for Q4_0) of row r, block b.
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+size_t tiled_qoff(int64_t r, int64_t b, int e, int64_t nb, int qtype) {
+    const int qb = tile_qb(qtype);
+    const int rr = (int)(r & (kTileRows - 1));
+    const int ee = qtype == 8 ? (e ^ ((rr & 4) << 2)) : e;
+    return (size_t)((((r / kTileRows) * nb + b) * kTileRows + rr) * qb + ee);
+}
+// Byte offset of the f16 scale of row r, block b (rp = tiled_rows(rows)).
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+size_t tiled_soff(int64_t r, int64_t b, int64_t nb, int64_t rp, int qtype) {
+    const int rr = (int)(r & (kTileRows - 1));
+    const int pos = 2 * (rr & 7) + (rr >> 3);
+    return (size_t)(rp * nb * tile_qb(qtype) + (((r / kTileRows) * nb + b) * kTileRows + pos) * 2);
+}
+
+// Static work plan of one CTA in one weight phase: its tiles [u0, u0 + n),
+// cut into chunks of nt tiles x one K-slice of bpk blocks (nks slices), each
+// chunk small enough for one ring slot.  K is split when a tile's blocks do
+// not fit a slot, or to give more warps work when the CTA has few tiles.
+// Producer, consumers and the host evaluate the same function.
+struct TPlan {
+    int u0, n;      // tiles of this CTA
+    int nks, bpk;   // K-slices and blocks per slice
+    int nt;         // tiles per chunk
+    int nchunks;    // = ceil(n / nt) * nks
+};
+
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+TPlan tile_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, int warps) {
+    // tbb: bytes of one (tile, block) unit incl. scales (x2 for gate + up)
+    TPlan t;
+    t.u0 = (int)((long long)cta * tiles / grid);
+    t.n = (int)((long long)(cta + 1) * tiles / grid) - t.u0;
+    if (t.n <= 0) {
+        t.n = 0; t.nks = 1; t.bpk = nb; t.nt = 1; t.nchunks = 0;
+        return t;
+    }
+    const int fit = slot_bytes / tbb;                 // blocks per slot
+    int nks = (nb + fit - 1) / fit;                   // slices needed to fit a slot
+    int want = (warps + t.n - 1) / t.n;               // slices that keep the warps busy
+    const int cap = nb / 4 > 0 ? nb / 4 : 1;          // at least 4 blocks per slice
+    if (want > cap) want = cap;
+    if (want > nks) nks = want;
+    t.nks = nks;
+    t.bpk = (nb + nks - 1) / nks;
+    t.nks = (nb + t.bpk - 1) / t.bpk;
+    if (t.nks == 1) {
+        int nt = fit / nb;                            // whole tiles per slot
+        const int spread = (t.n + warps - 1) / warps;
+        if (nt > spread) nt = spread;
+        t.nt = nt < 1 ? 1 : nt;
+    } else {
+        t.nt = 1;
+    }
+    t.nchunks = (t.n + t.nt - 1) / t.nt * t.nks;
+    return t;
+}
 
 struct LayerDev {
-    const uint8_t* wqkv;  // [(qd + 2*kvd) rows][rb_h]: Wq rows, then Wk, then Wv
-    const uint8_t* wo;    // [H rows][rb_q]
-    const uint8_t* wgu;   // [2*FF rows][rb_h]: gate rows, then up rows
-    const uint8_t* wd;    // [H rows][rb_f]
+    const uint8_t* wqkv;  // tiled [(qd + 2*kvd) rows][H]: Wq rows, then Wk, then Wv
+    const uint8_t* wo;    // tiled [H rows][qd]
+    const uint8_t* wgu;   // tiled [FF rows][H] gate, then tiled [FF rows][H] up
+    const uint8_t* wd;    // tiled [H rows][FF]
     const float* attn_norm;
     const float* ffn_norm;
     const float* bqkv;    // [qd + 2*kvd] or null
@@ -58,7 +164,9 @@ struct ModelDev {
     int ybuf_floats;          // phase outputs of one CTA, per buffer (two buffers)
     int cfloats;              // phase constants: norm gains, QKV bias, RoPE row
     int attn_tile;            // positions per attention tile
-    const uint8_t* tok_embd;  // [V rows][rb_h]
+    int nbx;                  // 32-blocks of the widest phase input (xq planes)
+    int Vp;                   // vocab rows rounded up to kTileRows (tiled lm_head / embedding)
+    const uint8_t* tok_embd;  // tiled [V rows][H]
     const uint8_t* lm_head;   // tok_embd when tied
     const float* out_norm;
     const float* rope_cos;    // [max_seq][hd/2]
@@ -74,8 +182,7 @@ struct ModelDev {
     uint2* ll_attn;           // [qd]  attention output when the context is not split
     uint2* ll_act;            // [FF]  SwiGLU output
     float* logits;            // [V]
-    float* best_val;          // [grid] argmax partials
-    int* best_idx;
+    unsigned long long* am_key;  // [1] argmax so far: order-preserving value bits << 32 | ~index (self-resetting)
     int* token;               // [1] last argmax
     unsigned* am_ctr;         // [1] argmax arrivals (self-resetting)
     int* err;                 // device error flag (B2_ERR_* codes)
@@ -110,17 +217,24 @@ struct StepArgs {
 //   cbuf   [cfloats]              phase constants (norm gains, bias, RoPE)
 //   full, empty [nslots] mbarriers; red [64] floats; misc [32] ints
 struct SmemOffsets {
-    uint32_t xs, xres, ybuf, cbuf, full, empty, red, misc, total;
+    uint32_t xs, xq, xsc, xsm, xres, ybuf, cbuf, full, empty, red, misc, total;
 };
 
+// xq holds the phase input as three int8 planes in the operand layout of
+// mma.m16n8k32: per 32-element block, 12 lanes x {a0, a2} words (96 bytes);
+// xsc the per-block scales (fp32) and xsm the per-block plane sums (int32 x3).
 inline
 #ifdef __CUDACC__
 __host__ __device__
 #endif
-SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_floats, int cfloats) {
+SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_floats, int cfloats, int nbx) {
     SmemOffsets o;
     uint32_t p = (uint32_t)nslots * (uint32_t)slot_bytes + 128u;
     o.xs = p;    p += 4u * (uint32_t)xs_floats;
+    o.xq = p;    p += 96u * (uint32_t)nbx;
+    o.xsc = p;   p += 4u * (uint32_t)nbx;
+    o.xsm = p;   p += 12u * (uint32_t)nbx;
+    p = (p + 15u) & ~15u;
     o.xres = p;  p += 4u * kMaxOwnRows;
     o.ybuf = p;  p += 8u * (uint32_t)ybuf_floats;
     o.cbuf = p;  p += 4u * (uint32_t)cfloats;

@@ -2,11 +2,12 @@
 //
 // Load follows transformer.go:215-310 (Engine.Load) and 1122-1335
 // (loadWeights) for what is read and how it is interpreted, but nothing is
-// dequantised on the host: Q8_0 / Q4_0 blocks are copied byte for byte into
-// one HBM arena.  Placement is chosen for the decode kernel: Wq, Wk and Wv
-// rows are adjacent (one fused [qd + 2*kvd] x H matrix), gate rows are
-// followed by up rows, every region starts on a 256-byte boundary and is
-// padded so 16-byte bulk copies never leave the arena.
+// dequantised: the Q8_0 / Q4_0 blocks of every weight matrix are uploaded and
+// rearranged on the device into the tiled layout of the decode kernel
+// (dev.cuh: 8-row tiles, quants and f16 scales in separate regions, the same
+// bytes per weight).  Wq, Wk and Wv form one [qd + 2*kvd] x H matrix, the gate
+// matrix is followed by the up matrix, every region starts on a 256-byte
+// boundary and is padded so 16-byte bulk copies never leave the arena.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -52,24 +53,52 @@ float f16_to_f32(uint16_t h) {
     return o;
 }
 
-struct Region {
-    std::string tensor;  // source tensor name
-    size_t off;          // destination offset in the arena
+// A weight matrix of the decode kernel: GGUF tensors stacked by rows,
+// tiled into the arena at `off`.
+struct MatGroup {
+    std::vector<std::string> tensors;
+    size_t off;
+    int64_t rows, cols;
 };
 
-__global__ void dequant_kernel(const uint8_t* src, uint32_t type, uint64_t n, float* dst) {
-    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+// One thread per (row, block) of the padded matrix: ggml block -> tiled
+// quants + scale (padding rows become zero).
+__global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, int64_t rp, int64_t nb, int qtype) {
+    const int bpb = qtype == 8 ? 34 : 18, qb = tile_qb(qtype);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rp * nb; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / nb, b = i - r * nb;
+        uint8_t* sd = dst + tiled_soff(r, b, nb, rp, qtype);
+        if (r >= rows) {
+            sd[0] = sd[1] = 0;
+            for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = 0;
+            continue;
+        }
+        const uint8_t* src = raw + (r * nb + b) * bpb;
+        sd[0] = src[0];
+        sd[1] = src[1];
+        for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = src[2 + e];
+    }
+}
+
+// Element (r, j) of a tiled Q8_0 / Q4_0 matrix (gguf.go:540-582; Q4_0 in
+// the ggml element order).
+__device__ __forceinline__ float tiled_elem(const uint8_t* base, int64_t r, int64_t j, int64_t nb, int64_t rp, int qtype) {
+    const int64_t b = j >> 5;
+    const int e = (int)(j & 31);
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(base + tiled_soff(r, b, nb, rp, qtype)));
+    if (qtype == 8) return d * (float)(int8_t)base[tiled_qoff(r, b, e, nb, 8)];
+    const uint8_t byte = base[tiled_qoff(r, b, e & 15, nb, 2)];
+    return d * (float)(((e < 16) ? (byte & 15) : (byte >> 4)) - 8);
+}
+
+__global__ void dequant_kernel(TensorLoc t, float* dst) {
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < t.elements; i += (uint64_t)gridDim.x * blockDim.x) {
         float v;
-        if (type == 8) {  // gguf.go:540-582
-            const uint8_t* p = src + (i >> 5) * 34;
-            v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(int8_t)p[2 + (i & 31)];
-        } else if (type == 2) {  // ggml Q4_0 order
-            const uint8_t* p = src + (i >> 5) * 18;
-            const int e = (int)(i & 31);
-            const uint8_t byte = p[2 + (e & 15)];
-            v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(((e < 16) ? (byte & 15) : (byte >> 4)) - 8);
+        if (t.type == 8 || t.type == 2) {
+            const int64_t r = (int64_t)(i / (uint64_t)t.cols), j = (int64_t)(i % (uint64_t)t.cols);
+            v = tiled_elem(static_cast<const uint8_t*>(t.dev), t.row0 + r, j, t.cols / 32, t.rp, (int)t.type);
         } else {
-            v = reinterpret_cast<const float*>(src)[i];
+            v = static_cast<const float*>(t.dev)[i];
         }
         dst[i] = v;
     }
@@ -86,18 +115,7 @@ __global__ void embed_mean_kernel(const ModelDev m, const int* toks, int n, floa
         for (int t = 0; t < n; t++) {
             const int tok = toks[t];
             if (tok < 0 || tok >= m.V) continue;
-            const uint8_t* row = m.tok_embd + (size_t)tok * m.rb_h;
-            const int b = j >> 5, k = j & 31;
-            float v;
-            if (m.qtype == 8) {
-                const uint8_t* p = row + 34 * b;
-                v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(int8_t)p[2 + k];
-            } else {
-                const uint8_t* p = row + 18 * b;
-                const uint8_t byte = p[2 + (k & 15)];
-                v = f16_bits_to_f32((uint16_t)(p[0] | (p[1] << 8))) * (float)(((k < 16) ? (byte & 15) : (byte >> 4)) - 8);
-            }
-            e += v;
+            e += tiled_elem(m.tok_embd, tok, j, m.H / 32, m.Vp, m.qtype);
         }
         e *= scale;
         out[j] = e;
@@ -118,10 +136,10 @@ __global__ void embed_mean_kernel(const ModelDev m, const int* toks, int n, floa
 
 }  // namespace
 
-int launch_dequant(const void* src, uint32_t type, uint64_t n, float* dst, cudaStream_t s) {
-    int blocks = (int)std::min<uint64_t>((n + 255) / 256, 148 * 16);
+int launch_dequant(const TensorLoc& t, float* dst, cudaStream_t s) {
+    int blocks = (int)std::min<uint64_t>((t.elements + 255) / 256, 148 * 16);
     if (blocks < 1) blocks = 1;
-    dequant_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t*>(src), type, n, dst);
+    dequant_kernel<<<blocks, 256, 0, s>>>(t, dst);
     return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
@@ -376,32 +394,32 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         off += up256(bytes + 16);
         return o2;
     };
-    std::vector<Region> regions;
+    std::vector<MatGroup> groups;
     std::vector<std::pair<std::string, size_t>> small;  // f32 vectors: name -> offset
-    const size_t off_embd = take((size_t)V * rb_h);
-    regions.push_back({"token_embd.weight", off_embd});
+    const int qti = qt == GGML_Q8_0 ? 8 : 2;
+    auto take_mat = [&](std::vector<std::string> names, int64_t rows, int64_t cols) {
+        const size_t o2 = take(tiled_bytes(rows, cols, qti));
+        groups.push_back({std::move(names), o2, rows, cols});
+        return o2;
+    };
+    const size_t off_embd = take_mat({"token_embd.weight"}, V, H);
     size_t off_out = off_embd;
-    if (ow) {
-        off_out = take((size_t)V * rb_h);
-        regions.push_back({"output.weight", off_out});
-    }
+    if (ow) off_out = take_mat({"output.weight"}, V, H);
     const size_t off_onorm = take((size_t)H * 4);
     small.push_back({"output_norm.weight", off_onorm});
     struct LOff { size_t qkv, wo, gu, wd, an, fn, b; };
     std::vector<LOff> lo(L);
     for (int l = 0; l < L; l++) {
         const std::string p = "blk." + std::to_string(l) + ".";
-        lo[l].qkv = take((size_t)(qd + 2 * kvd) * rb_h);
-        regions.push_back({p + "attn_q.weight", lo[l].qkv});
-        regions.push_back({p + "attn_k.weight", lo[l].qkv + (size_t)qd * rb_h});
-        regions.push_back({p + "attn_v.weight", lo[l].qkv + (size_t)(qd + kvd) * rb_h});
-        lo[l].wo = take((size_t)H * rb_q);
-        regions.push_back({p + "attn_output.weight", lo[l].wo});
-        lo[l].gu = take((size_t)2 * FF * rb_h);
-        regions.push_back({p + "ffn_gate.weight", lo[l].gu});
-        regions.push_back({p + "ffn_up.weight", lo[l].gu + (size_t)FF * rb_h});
-        lo[l].wd = take((size_t)H * rb_f);
-        regions.push_back({p + "ffn_down.weight", lo[l].wd});
+        lo[l].qkv = take_mat({p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, qd + 2 * kvd, H);
+        lo[l].wo = take_mat({p + "attn_output.weight"}, H, qd);
+        // gate, then up right behind it (the kernel finds up at gate + tiled_bytes)
+        lo[l].gu = off;
+        groups.push_back({{p + "ffn_gate.weight"}, off, FF, H});
+        off += tiled_bytes(FF, H, qti);
+        groups.push_back({{p + "ffn_up.weight"}, off, FF, H});
+        off += up256(tiled_bytes(FF, H, qti) + 16);
+        lo[l].wd = take_mat({p + "ffn_down.weight"}, H, FF);
         lo[l].an = take((size_t)H * 4);
         small.push_back({p + "attn_norm.weight", lo[l].an});
         lo[l].fn = take((size_t)H * 4);
@@ -439,8 +457,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const size_t off_llattn = take((size_t)qd * 8);
     const size_t off_llact = take((size_t)FF * 8);
     const size_t off_logits = take((size_t)V * 4);
-    const size_t off_bv = take((size_t)m->grid * 4);
-    const size_t off_bi = take((size_t)m->grid * 4);
+    const size_t off_amkey = take(8);
     const size_t off_tok = take(4);
     const size_t off_amctr = take(4);
     const size_t off_err = take(4);
@@ -481,25 +498,50 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     bool sev_used[2] = {false, false};
     int which = 0;
     bool io_ok = true;
-    // Verbatim block copies: file -> pinned stage -> HBM, double-buffered.
-    for (const Region& r : regions) {
-        const GgufTensor* t = g.find(r.tensor);
-        uint64_t left = t->bytes(), src = g.data_offset + t->offset, dst = r.off;
-        if (fseeko(f, (off_t)src, SEEK_SET) != 0) { io_ok = false; break; }
-        while (left > 0 && io_ok) {
-            const size_t nb = (size_t)std::min<uint64_t>(left, stage_bytes);
-            if (sev_used[which]) cudaEventSynchronize(sev[which]);
-            if (fread(stage[which], 1, nb, f) != nb) { io_ok = false; break; }
-            cudaMemcpyAsync(A + dst, stage[which], nb, cudaMemcpyHostToDevice, m->stream);
-            cudaEventRecord(sev[which], m->stream);
-            sev_used[which] = true;
-            which ^= 1;
-            left -= nb;
-            dst += nb;
+    // Weight matrices: file -> pinned stage -> raw device buffer (double-
+    // buffered), then one repack launch per matrix into the arena.
+    size_t raw_max = 0;
+    for (const MatGroup& gr : groups) raw_max = std::max(raw_max, (size_t)gr.rows * (size_t)(gr.cols / 32 * bpb));
+    void* raw = nullptr;
+    if (dev_malloc(&raw, raw_max) != 0) {
+        fclose(f);
+        cudaFreeHost(stage[0]);
+        cudaFreeHost(stage[1]);
+        return bail(B2_ERR_OOM, "device allocation of the " + std::to_string(raw_max) + "-byte upload buffer failed");
+    }
+    for (const MatGroup& gr : groups) {
+        size_t dst = 0;
+        int64_t row0 = 0;
+        for (const std::string& name : gr.tensors) {
+            const GgufTensor* t = g.find(name);
+            uint64_t left = t->bytes(), src = g.data_offset + t->offset;
+            if (fseeko(f, (off_t)src, SEEK_SET) != 0) { io_ok = false; break; }
+            while (left > 0 && io_ok) {
+                const size_t nb = (size_t)std::min<uint64_t>(left, stage_bytes);
+                if (sev_used[which]) cudaEventSynchronize(sev[which]);
+                if (fread(stage[which], 1, nb, f) != nb) { io_ok = false; break; }
+                cudaMemcpyAsync(static_cast<uint8_t*>(raw) + dst, stage[which], nb, cudaMemcpyHostToDevice, m->stream);
+                cudaEventRecord(sev[which], m->stream);
+                sev_used[which] = true;
+                which ^= 1;
+                left -= nb;
+                dst += nb;
+            }
+            if (!io_ok) break;
+            TensorLoc tl{A + gr.off, t->type, t->elements()};
+            tl.row0 = row0;
+            tl.cols = gr.cols;
+            tl.rp = tiled_rows(gr.rows);
+            m->tensors[name] = tl;
+            row0 += (int64_t)t->dims[1];
         }
         if (!io_ok) break;
-        m->tensors[r.tensor] = TensorLoc{A + r.off, t->type, t->elements()};
+        const int64_t rp = tiled_rows(gr.rows), nbk = gr.cols / 32;
+        const int blocks = (int)std::min<int64_t>((rp * nbk + 255) / 256, 148 * 32);
+        repack_kernel<<<blocks, 256, 0, m->stream>>>(static_cast<const uint8_t*>(raw), A + gr.off, gr.rows, rp, nbk, qti);
     }
+    cudaStreamSynchronize(m->stream);
+    cudaFree(raw);
     // Small vectors (norm gains, biases) as fp32; F16/BF16 widened on the host
     // exactly as gguf.go:510-536 does.
     std::vector<float> buf;
@@ -560,6 +602,8 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.rb_h = (int)rb_h; d.rb_q = (int)rb_q; d.rb_f = (int)rb_f;
     d.eps = c.rms_norm_eps;
     d.kv_fp32 = o.kv_fp32 ? 1 : 0;
+    d.Vp = (int)tiled_rows(V);
+    d.nbx = std::max(std::max(H, qd), FF) / 32;
     d.tok_embd = A + off_embd;
     d.lm_head = A + off_out;
     d.out_norm = reinterpret_cast<const float*>(A + off_onorm);
@@ -574,8 +618,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.ll_attn = reinterpret_cast<uint2*>(A + off_llattn);
     d.ll_act = reinterpret_cast<uint2*>(A + off_llact);
     d.logits = reinterpret_cast<float*>(A + off_logits);
-    d.best_val = reinterpret_cast<float*>(A + off_bv);
-    d.best_idx = reinterpret_cast<int*>(A + off_bi);
+    d.am_key = reinterpret_cast<unsigned long long*>(A + off_amkey);
     d.token = reinterpret_cast<int*>(A + off_tok);
     d.am_ctr = reinterpret_cast<unsigned*>(A + off_amctr);
     d.err = reinterpret_cast<int*>(A + off_err);
@@ -606,15 +649,29 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const int tile = std::max(1, std::min(kMaxAttnTile, kAttnTileBytes / (hd * kv_es)));
     const int attn_need = 4 * hd + tile + kConsumerWarps * hd + (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
     const int base_xs = std::max(std::max(std::max(H, FF), qd), attn_need);
-    const int qkv_units = (qd + 2 * kvd) / 2;
-    const auto per_cta = [&](int units) { return (units + m->grid - 1) / m->grid; };
-    const int ybuf = (std::max(std::max(2 * per_cta(qkv_units), 2 * per_cta(FF)), std::max(per_cta(H), per_cta(V))) + 31) & ~31;
+    const int slot = 8192;
+    // Outputs one CTA keeps per phase (all K-slices): from the same work plan
+    // the kernel uses, over every CTA.
+    const int qb = tile_qb(qti);
+    auto ybuf_need = [&](int rows, int nbk, bool pair) {
+        const int tiles = (int)(tiled_rows(rows) / kTileRows), tbb = (kTileRows * qb + 2 * kTileRows) * (pair ? 2 : 1);
+        int need = 0;
+        for (int cta = 0; cta < m->grid; cta++) {
+            const TPlan pl = tile_plan(tiles, nbk, tbb, cta, m->grid, slot, kConsumerWarps);
+            need = std::max(need, pl.nks * kTileRows * pl.n * (pair ? 2 : 1));
+        }
+        return need;
+    };
+    const int ybuf = (std::max(std::max(ybuf_need(qd + 2 * kvd, H / 32, false), ybuf_need(H, qd / 32, false)),
+                               std::max(std::max(ybuf_need(FF, H / 32, true), ybuf_need(H, FF / 32, false)),
+                                        ybuf_need(V, H / 32, false))) + 31) & ~31;
+    const auto rows_per_cta = [&](int rows) {
+        return kTileRows * (int)((tiled_rows(rows) / kTileRows + m->grid - 1) / m->grid);
+    };
     const int cfloats = cb_floats(H, hd);
-    const size_t need_slot = std::max(std::max(2 * rb_h + 192, rb_q + 32), rb_f + 32);
-    const int slot = std::max<int>(8192, (int)((need_slot + 1023) & ~size_t(1023)));
     auto ring_slots = [&](int xs_f) {
         int n = 0;
-        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats).total <= 232448u) n++;
+        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qd), FF) / 32).total <= 232448u) n++;
         return n;
     };
     const int merge_full = qd + nh * kMaxSplits * (hd + 2);
@@ -628,8 +685,8 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     xs = (xs + 31) & ~31;
     const int ns = ring_slots(xs);
     if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
-    if ((H + m->grid - 1) / m->grid > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
-    if (2 * per_cta(qkv_units) > kMaxQkvRows)
+    if (rows_per_cta(H) > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
+    if (rows_per_cta(qd + 2 * kvd) > kMaxQkvRows)
         return bail(B2_ERR_UNSUPPORTED_TYPE, "attention projection too large for one GPU");
     d.xs_floats = xs;
     d.ybuf_floats = ybuf;

@@ -14,9 +14,12 @@
 namespace b2 {
 
 struct TensorLoc {
-    void* dev = nullptr;     // device address of the first block / element
+    void* dev = nullptr;     // F32: first element; Q8_0 / Q4_0: base of the tiled matrix
     uint32_t type = 0;       // ggml type as resident (F32 for the small vectors)
     uint64_t elements = 0;
+    int64_t row0 = 0;        // first row of this tensor in the tiled matrix
+    int64_t cols = 0;        // row length (elements)
+    int64_t rp = 0;          // rows of the tiled matrix, rounded up to 8
 };
 
 // PredictStream state (transformer.go:385-442) for the iterator form.
@@ -70,7 +73,7 @@ size_t decode_smem_bytes(const ModelDev& m);
 int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err);
 
 // Kernel-level entry points (matvec.cu / attention.cu / model.cu).
-int launch_dequant(const void* src, uint32_t type, uint64_t n, float* dst, cudaStream_t s);
+int launch_dequant(const TensorLoc& t, float* dst, cudaStream_t s);
 int launch_embed_mean(const b2_model* m, const int* d_tokens, int n, float* d_out, cudaStream_t s);
 
 // Runs n tokens through the model from the current cache position (prefill
