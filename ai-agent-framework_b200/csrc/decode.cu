@@ -463,6 +463,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
     uint8_t* vtile = ktile + (size_t)TP * KS;                                   // [TP][rowb]
     const int pieces = rowb / 16;
     auto load_tile = [&](int tb, int nt) {
+        #pragma unroll 1
         for (int i = ct; i < nt * pieces; i += kConsumerThreads) {
             const int t = i / pieces, c = i - t * pieces;
             if (tb + t == pos) continue;
@@ -478,6 +479,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
         alive = ll_gather_s(ksrc, hd, tag_here, err, smem_u32(akc), 0, 0, 0).ok;
         if (alive) alive = ll_gather_s(vsrc, hd, tag_here, err, smem_u32(avc), 0, 0, 0).ok;
     }
+    #pragma unroll 1
     for (int i = ct; i < hd; i += kConsumerThreads) ao[i] = 0.0f;
     cp_async_wait();
     named_bar_sync(1, kConsumerThreads);
@@ -486,6 +488,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
     const int hv = hd / 8, ngrp = kConsumerThreads / hv;
     const int vc = ct % hv, vgi = ct / hv;
     float mrun = -INFINITY, lrun = 0.0f;
+    #pragma unroll 1
     for (int tb = t0; tb < t1; tb += TP) {
         const int nt = min(TP, t1 - tb);
         if (tb != t0) {
@@ -498,6 +501,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
         if (ct < nt) {
             float d0 = 0.0f, d1 = 0.0f;
             if (tb + ct == pos) {
+                #pragma unroll 1
                 for (int d = 0; d < hd; d += 2) {
                     d0 = fmaf(aq[d], akc[d], d0);
                     d1 = fmaf(aq[d + 1], akc[d + 1], d1);
@@ -505,6 +509,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
             } else if (F32) {
                 const float4* kr = reinterpret_cast<const float4*>(ktile + (size_t)ct * KS);
                 const float4* q4 = reinterpret_cast<const float4*>(aq);
+                #pragma unroll 1
                 for (int i = 0; i < hd / 4; i++) {
                     const float4 k = kr[i], q = q4[i];
                     d0 = fmaf(q.x, k.x, d0);
@@ -515,6 +520,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
             } else {
                 const uint4* kr = reinterpret_cast<const uint4*>(ktile + (size_t)ct * KS);
                 const float4* q4 = reinterpret_cast<const float4*>(aq);
+                #pragma unroll 1
                 for (int i = 0; i < hd / 8; i++) {
                     const uint4 ku = kr[i];
                     const __half2* kh = reinterpret_cast<const __half2*>(&ku);
@@ -546,6 +552,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
         float acc[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) acc[e] = 0.0f;
+        #pragma unroll 1
         for (int tl = vgi; tl < nt; tl += ngrp) {
             const float pt = asc[tl];
             float vf[8];
@@ -571,6 +578,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
             for (int e = 0; e < 8; e++) acc[e] = fmaf(pt, vf[e], acc[e]);
         }
         // lanes of one warp that share a chunk: lane, lane ^ hv, ...
+        #pragma unroll 1
         for (int o = hv; o < 32; o <<= 1) {
 #pragma unroll
             for (int e = 0; e < 8; e++) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
@@ -580,6 +588,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
             for (int e = 0; e < 8; e++) avred[cw * hd + lane * 8 + e] = acc[e];
         }
         named_bar_sync(1, kConsumerThreads);
+        #pragma unroll 1
         for (int d = ct; d < hd; d += kConsumerThreads) {
             float o = ao[d] * corr;
 #pragma unroll
@@ -589,9 +598,11 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
         named_bar_sync(1, kConsumerThreads);
     }
     if (!split_out) {
+        #pragma unroll 1
         for (int d = ct; d < hd; d += kConsumerThreads) ll_store(out + d, ao[d] / lrun, tag_out);
     } else {
         // split partial (o unnormalised, m, l), laid out [head][split][hd + 2]
+        #pragma unroll 1
         for (int i = ct; i < hd + 2; i += kConsumerThreads) {
             const float v = i < hd ? ao[i] : (i == hd ? mrun : lrun);
             ll_store(out + i, v, tag_out);
@@ -976,8 +987,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         const Geom mg{a.mv_w, a.mv_rb, a.mv_cols, a.mv_rows};
         const Split s = cta_split(mg, cta, grid, SB);
         const int nu = mg.cols / US;
+        #pragma unroll 1
         for (int j = ct; j < mg.cols; j += kConsumerThreads) xs[xs_index<US>(j, nu)] = a.mv_x[j];
         sync_alive();
+        #pragma unroll 1
         for (int k = 0; k < s.nchunks; k++) {
             const unsigned gidx = k;
             if ((int)(gidx % kConsumerWarps) != cw) continue;
@@ -989,6 +1002,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 const int nrows = min(s.cu, s.n - k * s.cu);
                 const uint8_t* src = mg.w + (size_t)uu0 * mg.rb;
                 const uint8_t* base1 = ring + (size_t)slot * SB + (reinterpret_cast<uintptr_t>(src) & 15);
+                #pragma unroll 1
                 for (int pi = 0; pi < (nrows + 1) / 2; pi++) {
                     const uint8_t* ra = base1 + (size_t)(2 * pi) * mg.rb;
                     const bool two = (2 * pi + 1) < nrows;
@@ -1007,6 +1021,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         return;
     }
 
+    #pragma unroll 1
     for (int p = a.p_begin; p < a.p_end; p++) {
         const TGeom g = phase_geom(m, a, p);
         const TPlan pl = g.w ? tile_plan(g.tiles, g.nb, tile_unit_bytes(g, QT), cta, grid, SB, kConsumerWarps)
@@ -1027,20 +1042,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         // 1. stage the phase input: gather (+ norm / merge) into xs, then planes
         if (g.kind == PH_QKV && g.layer == 0) {
             // transformer.go:524-531: the residual stream starts at the embedding
+            #pragma unroll 1
             for (int j = own0 + ct; j < own1; j += kConsumerThreads) xres[j - own0] = embed_elem(m, tok, j);
         }
         if ((g.kind == PH_QKV || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) && has_rows) {
             // constants first (they land while the poll below waits)
             const float* nw = g.kind == PH_QKV ? m.layers[g.layer].attn_norm
                             : (g.kind == PH_GATEUP ? m.layers[g.layer].ffn_norm : m.out_norm);
+            #pragma unroll 1
             for (int i = ct; i < m.H / 4; i += kConsumerThreads) cp_async16(cb + 4 * i, nw + 4 * i);
             if (g.kind == PH_QKV) {
                 const float* bq = m.layers[g.layer].bqkv;
                 const int r0b = (kTileRows * pl.u0) & ~3, r1 = kTileRows * (pl.u0 + pl.n);
                 if (bq)
+                    #pragma unroll 1
                     for (int i = ct; i < (r1 - r0b + 3) / 4; i += kConsumerThreads)
                         cp_async16(cb + cb_bias(m) + 4 * i, bq + r0b + 4 * i);
                 const int hh = m.hd / 2;
+                #pragma unroll 1
                 for (int i = ct; i < hh / 4; i += kConsumerThreads) {
                     cp_async16(cb + cb_cos(m) + 4 * i, m.rope_cos + (size_t)a.pos * hh + 4 * i);
                     cp_async16(cb + cb_sin(m) + 4 * i, m.rope_sin + (size_t)a.pos * hh + 4 * i);
@@ -1050,6 +1069,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             // RMSNorm (transformer.go:922-932) fused into the stage
             float ss = 0.0f;
             if (g.kind == PH_QKV && g.layer == 0) {
+                #pragma unroll 1
                 for (int j = ct; j < m.H; j += kConsumerThreads) {
                     const float v = embed_elem(m, tok, j);
                     xs[j] = v;
@@ -1079,12 +1099,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 if (alive) alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0, 0, 0).ok;
                 if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
                 named_bar_sync(1, kConsumerThreads);
+                #pragma unroll 1
                 for (int i = ct; i < m.qd; i += kConsumerThreads) {
                     const int hh = i / hd, d = i - hh * hd;
                     const float* ph = part + (size_t)hh * S * W2;
                     float M = -INFINITY;
+                    #pragma unroll 1
                     for (int s2 = 0; s2 < S; s2++) M = fmaxf(M, ph[s2 * W2 + hd]);
                     float Ls = 0.0f, o = 0.0f;
+                    #pragma unroll 1
                     for (int s2 = 0; s2 < S; s2++) {
                         const float ms = ph[s2 * W2 + hd];
                         const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
@@ -1143,6 +1166,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             uint32_t par = ((gbase + first) / NS) & 1u;
             int kt = first / pl.nks, ks = first - kt * pl.nks;
             const int dq = kConsumerWarps / pl.nks, dr = kConsumerWarps - dq * pl.nks;
+            #pragma unroll 1
             for (int k = first; k < pl.nchunks; k += kConsumerWarps) {
                 const unsigned gidx = gbase + k;
                 const uint64_t tw = (TR && a.trace) ? global_ns() : 0;
@@ -1158,6 +1182,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     const int bb0 = ks * pl.bpk, nbc = min(pl.bpk, g.nb - bb0);
                     const int qlen = ntc * nbc * kTileRows * QB, slen = ntc * nbc * 2 * kTileRows;
                     float* yk = yb + ks * rc;
+                    #pragma unroll 1
                     for (int tl = 0; tl < ntc; tl++) {
                         const uint32_t qa = (uint32_t)(slot * SB + tl * nbc * kTileRows * QB);
                         const uint32_t sa = (uint32_t)(slot * SB + qlen + tl * nbc * 2 * kTileRows);
@@ -1213,6 +1238,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         const int row0 = kTileRows * pl.u0;
         auto ysum = [&](int i) {
             float v = yb[i];
+            #pragma unroll 1
             for (int ks = 1; ks < pl.nks; ks++) v += yb[ks * rc + i];
             return v;
         };
@@ -1225,6 +1251,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     // (936-951), KV append (654-656)
                     const bool bias = m.layers[g.layer].bqkv != nullptr;
                     const int bias0 = row0 & ~3;
+                    #pragma unroll 1
                     for (int j = ct; j < kTileRows / 2 * pl.n; j += kConsumerThreads) {
                         const int row = row0 + 2 * j;
                         float a0 = ysum(2 * j), a1 = ysum(2 * j + 1);
@@ -1258,6 +1285,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 }
                 case PH_GATEUP:
                     // SwiGLU (transformer.go:725-727, 954-956)
+                    #pragma unroll 1
                     for (int j = ct; j < kTileRows * pl.n && row0 + j < g.rows; j += kConsumerThreads) {
                         const float gv = ysum(2 * j), uv = ysum(2 * j + 1);
                         ll_store(m.ll_act + row0 + j, gv / (1.0f + expf(-gv)) * uv, tag);
@@ -1268,6 +1296,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     // residual (transformer.go:576-578, 591-593); the rows are
                     // exactly the residual rows this CTA owns
                     uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
+                    #pragma unroll 1
                     for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
                         const float xr = xres[j] + ysum(j);
                         xres[j] = xr;
@@ -1278,6 +1307,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 default: {  // PH_LMHEAD
                     // logits + argmax, first maximum wins (transformer.go:1038-1046)
                     Best best{-INFINITY, 0x7fffffff};
+                    #pragma unroll 1
                     for (int j = ct; alive && j < kTileRows * pl.n; j += kConsumerThreads) {
                         const int row = row0 + j;
                         if (row >= g.rows) break;
@@ -1295,6 +1325,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     named_bar_sync(1, kConsumerThreads);
                     if (ct == 0) {
                         Best b{red[0], misc[4]};
+                        #pragma unroll 1
                         for (int w = 1; w < kConsumerWarps; w++)
                             if (better(red[w], misc[4 + w], b.v, b.i)) { b.v = red[w]; b.i = misc[4 + w]; }
                         // one atomic max per CTA on (order-preserving value bits, ~index):
