@@ -377,11 +377,12 @@ __device__ __forceinline__ void dot2_q4(const uint8_t* r0, const uint8_t* r1, bo
 
 // transformer.go:525-531 + gguf.go:540-613: element j of token_embd row tok,
 // decoded from its block of the tiled matrix (out-of-range ids embed to zero).
+template <int QT>
 __device__ __forceinline__ float embed_elem(const ModelDev& m, int tok, int j) {
     if (tok < 0 || tok >= m.V) return 0.0f;
     const int nb = m.H / 32, b = j >> 5, e = j & 31;
-    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(m.tok_embd + tiled_soff(tok, b, nb, m.Vp, m.qtype)));
-    if (m.qtype == 8) return d * (float)(int8_t)m.tok_embd[tiled_qoff(tok, b, e, nb, 8)];
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(m.tok_embd + tiled_soff(tok, b, nb, m.Vp, QT)));
+    if (QT == 8) return d * (float)(int8_t)m.tok_embd[tiled_qoff(tok, b, e, nb, 8)];
     const uint8_t byte = m.tok_embd[tiled_qoff(tok, b, e & 15, nb, 2)];
     const int nib = (e < 16) ? (byte & 15) : (byte >> 4);
     return d * (float)(nib - 8);
@@ -808,7 +809,7 @@ __device__ __noinline__ void quantize_planes(uint32_t xs_off, int nbk, uint32_t 
 // the kernel
 // ---------------------------------------------------------------------------
 
-template <int QT, bool MV, bool TR>
+template <int QT, bool MV, bool TR, bool KV32>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, const StepArgs a) {
     constexpr int US = QT == 8 ? 16 : 32;  // matvec: values per lane unit
     constexpr int QB = QT == 8 ? 32 : 16;  // tiled: quant bytes per row and block
@@ -1043,7 +1044,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         if (g.kind == PH_QKV && g.layer == 0) {
             // transformer.go:524-531: the residual stream starts at the embedding
             #pragma unroll 1
-            for (int j = own0 + ct; j < own1; j += kConsumerThreads) xres[j - own0] = embed_elem(m, tok, j);
+            for (int j = own0 + ct; j < own1; j += kConsumerThreads) xres[j - own0] = embed_elem<QT>(m, tok, j);
         }
         if ((g.kind == PH_QKV || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) && has_rows) {
             // constants first (they land while the poll below waits)
@@ -1071,7 +1072,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             if (g.kind == PH_QKV && g.layer == 0) {
                 #pragma unroll 1
                 for (int j = ct; j < m.H; j += kConsumerThreads) {
-                    const float v = embed_elem(m, tok, j);
+                    const float v = embed_elem<QT>(m, tok, j);
                     xs[j] = v;
                     ss += v * v;
                 }
@@ -1140,7 +1141,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 const int h = cta / S, sidx = cta - h * S, kvh = h / (m.nh / m.nkv);
                 const int ctx = a.pos + 1;
                 const int t0 = (int)((long long)sidx * ctx / S), t1 = (int)((long long)(sidx + 1) * ctx / S);
-                const int es = m.kv_fp32 ? 4 : 2;
+                const int es = KV32 ? 4 : 2;
                 const size_t lay = ((size_t)g.layer * m.max_seq * m.kvd + (size_t)kvh * hd) * es;
                 const uint8_t* kg = reinterpret_cast<const uint8_t*>(m.kcache) + lay;
                 const uint8_t* vg = reinterpret_cast<const uint8_t*>(m.vcache) + lay;
@@ -1149,11 +1150,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 const uint2* kn = m.ll_qkv + m.qd + (size_t)kvh * hd;
                 const uint2* vn = kn + m.kvd;
                 const unsigned tout = ll_tag(a.epoch, g.layer);
-                alive = m.kv_fp32
-                            ? attn_phase<true>(q, kn, vn, kg, vg, (uint32_t)(m.kvd * es), hd, m.attn_tile, t0, t1, a.pos,
-                                               tag_here, tout, out, S != 1, m.err, so.xs, so.red, alive)
-                            : attn_phase<false>(q, kn, vn, kg, vg, (uint32_t)(m.kvd * es), hd, m.attn_tile, t0, t1,
-                                                a.pos, tag_here, tout, out, S != 1, m.err, so.xs, so.red, alive);
+                alive = attn_phase<KV32>(q, kn, vn, kg, vg, (uint32_t)(m.kvd * es), hd, m.attn_tile, t0, t1, a.pos,
+                                         tag_here, tout, out, S != 1, m.err, so.xs, so.red, alive);
             }
         } else {
             // 2. rows: tensor-core dot products of this CTA's tiles into yb
@@ -1272,7 +1270,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                             const int col = row - m.qd - (isk ? 0 : m.kvd);
                             const size_t off = ((size_t)g.layer * m.max_seq + a.pos) * m.kvd + col;
                             void* cache = isk ? m.kcache : m.vcache;
-                            if (m.kv_fp32) {
+                            if (KV32) {
                                 reinterpret_cast<float*>(cache)[off] = a0;
                                 reinterpret_cast<float*>(cache)[off + 1] = a1;
                             } else {
@@ -1370,14 +1368,19 @@ int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t s
     void* args[] = {(void*)&m, (void*)&a};
     // instantiations: (Q8_0, Q4_0) x (model, matvec) x (plain, traced); the
     // plain kernels carry no trace code at all (smaller instruction footprint)
-    const bool mv = a.mv_w != nullptr;
-    const int ti = (m.qtype == 8 ? 0 : 1) + (mv ? 2 : 0) + (a.trace ? 4 : 0);
-    const void* fns[8] = {(const void*)decode_kernel<8, false, false>, (const void*)decode_kernel<2, false, false>,
-                          (const void*)decode_kernel<8, true, false>,  (const void*)decode_kernel<2, true, false>,
-                          (const void*)decode_kernel<8, false, true>,  (const void*)decode_kernel<2, false, true>,
-                          (const void*)decode_kernel<8, true, true>,   (const void*)decode_kernel<2, true, true>};
+    // model kernels: (Q8_0, Q4_0) x (plain, traced) x (fp16, fp32 KV cache);
+    // matvec kernels: (Q8_0, Q4_0).  Each kernel carries only its own paths
+    // (the instruction cache is the limit at B = 1).
+    static const void* const fns[10] = {
+        (const void*)decode_kernel<8, false, false, false>, (const void*)decode_kernel<2, false, false, false>,
+        (const void*)decode_kernel<8, false, true, false>,  (const void*)decode_kernel<2, false, true, false>,
+        (const void*)decode_kernel<8, false, false, true>,  (const void*)decode_kernel<2, false, false, true>,
+        (const void*)decode_kernel<8, false, true, true>,   (const void*)decode_kernel<2, false, true, true>,
+        (const void*)decode_kernel<8, true, false, false>,  (const void*)decode_kernel<2, true, false, false>};
+    const int q = m.qtype == 8 ? 0 : 1;
+    const int ti = a.mv_w ? 8 + q : q + (a.trace ? 2 : 0) + (m.kv_fp32 ? 4 : 0);
     const void* fn = fns[ti];
-    static bool attr_done[8] = {false, false, false, false, false, false, false, false};
+    static bool attr_done[10] = {false, false, false, false, false, false, false, false, false, false};
     if (!attr_done[ti]) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
         if (e != cudaSuccess) {
