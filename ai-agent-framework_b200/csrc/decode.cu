@@ -202,21 +202,20 @@ struct GatherRes {
 };
 
 // Gathers LL words src[0 .. n) (n even, src 16-byte aligned) once every word
-// carries `tag` and stores the values into shared memory at byte address
-// dst: value i goes to float i (us == 0) or to the dot-loop layout of the
-// phase input (us values per lane unit, nu units; see xs_index).  Each
-// consumer thread polls its own words with 16-byte loads, up to 4 in flight;
-// a word whose tag is stale is simply read again.  Bounded: gives up (ok = 0,
-// error flag set) after kWaitLimitNs or when another CTA already reported an
-// error.  Not inlined: its polling state would otherwise add to the register
-// peak of the whole kernel at every one of its call sites.
-__device__ __noinline__ GatherRes ll_gather_s(const uint2* src, int n, unsigned tag, int* err, uint32_t dst, int us,
-                                              int nu, int want_ss) {
+// carries `tag` and stores value i as float i at shared byte address dst.
+// Each consumer thread polls its own words with 16-byte loads, up to 4 in
+// flight; a word whose tag is stale is simply read again.  Bounded: gives up
+// (ok = 0, error flag set) after kWaitLimitNs or when another CTA already
+// reported an error.  Also returns the sum of squares (for RMSNorm) when asked.
+// Not inlined: its polling state would otherwise add to the register peak of
+// the whole kernel at every one of its call sites.
+__device__ __noinline__ GatherRes ll_gather_s(const uint2* src, int n, unsigned tag, int* err, uint32_t dst,
+                                              int want_ss) {
     const int ct = threadIdx.x - 32;
     const int n2 = n >> 1;
-    const int ul = us == 32 ? 5 : 4;
     uint64_t t0 = 0;
     float ss = 0.0f;
+#pragma unroll 1
     for (int base = 0; base < n2; base += kConsumerThreads * 4) {
         uint4 v[4];
         for (;;) {
@@ -243,18 +242,9 @@ __device__ __noinline__ GatherRes ll_gather_s(const uint2* src, int n, unsigned 
         for (int k = 0; k < 4; k++) {
             const int i = base + ct + k * kConsumerThreads;
             if (i < n2) {
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    const int j = 2 * i + e;
-                    const float val = __uint_as_float(e ? v[k].z : v[k].x);
-                    int idx = j;
-                    if (us) {
-                        const int u = j >> ul, r = j & (us - 1);
-                        idx = ((r >> 2) * nu + u) * 4 + (r & 3);
-                    }
-                    asm volatile("st.shared.f32 [%0], %1;" ::"r"(dst + 4u * (uint32_t)idx), "f"(val) : "memory");
-                    if (want_ss) ss += val * val;
-                }
+                const float a0 = __uint_as_float(v[k].x), a1 = __uint_as_float(v[k].z);
+                asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(dst + 8u * (uint32_t)i), "f"(a0), "f"(a1) : "memory");
+                if (want_ss) ss += a0 * a0 + a1 * a1;
             }
         }
     }
@@ -475,10 +465,10 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
     };
     if (t1 > t0) load_tile(t0, min(TP, t1 - t0));
 
-    if (alive) alive = ll_gather_s(qsrc, hd, tag_here, err, smem_u32(aq), 0, 0, 0).ok;
+    if (alive) alive = ll_gather_s(qsrc, hd, tag_here, err, smem_u32(aq), 0).ok;
     if (alive && pos >= t0 && pos < t1) {
-        alive = ll_gather_s(ksrc, hd, tag_here, err, smem_u32(akc), 0, 0, 0).ok;
-        if (alive) alive = ll_gather_s(vsrc, hd, tag_here, err, smem_u32(avc), 0, 0, 0).ok;
+        alive = ll_gather_s(ksrc, hd, tag_here, err, smem_u32(akc), 0).ok;
+        if (alive) alive = ll_gather_s(vsrc, hd, tag_here, err, smem_u32(avc), 0).ok;
     }
     #pragma unroll 1
     for (int i = ct; i < hd; i += kConsumerThreads) ao[i] = 0.0f;
@@ -753,7 +743,9 @@ __device__ __noinline__ void quantize_planes(uint32_t xs_off, int nbk, uint32_t 
         }
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+        // approximate reciprocal (no IEEE division): the planes represent x * inv
+        // against the stored scale amax / 127, a 1-ulp mismatch is 6e-8 relative
+        const float inv = amax > 0.0f ? __fdividef(127.0f, amax) : 0.0f;
         uint32_t by[3][8];
         int sg[3] = {0, 0, 0};
 #pragma unroll
@@ -794,7 +786,7 @@ __device__ __noinline__ void quantize_planes(uint32_t xs_off, int nbk, uint32_t 
                 xw[(gq * 4 + t0 + 1) * 2 + w] = hi;
             }
             if (sub == 0) {
-                xsc[b] = amax / 127.0f;
+                xsc[b] = amax * (1.0f / 127.0f);
                 if (sums) {
                     xsm[b * 3 + 0] = sg[0];
                     xsm[b * 3 + 1] = sg[1];
@@ -1079,7 +1071,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             } else if (alive) {
                 const uint2* src = g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2;
                 const unsigned tg = g.kind == PH_GATEUP ? tag_here : tag_prev;
-                const GatherRes gr = ll_gather_s(src, m.H, tg, m.err, smem_u32(xs), 0, 0, 1);
+                const GatherRes gr = ll_gather_s(src, m.H, tg, m.err, smem_u32(xs), 1);
                 alive = gr.ok;
                 ss = gr.ss;
             }
@@ -1090,14 +1082,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             quantize_planes(so.xs, m.H / 32, so.xq, so.xsc, so.xsm, r, so.cbuf, QT != 8);
         } else if (g.kind == PH_WO && has_rows) {
             if (a.splits == 1) {
-                if (alive) alive = ll_gather_s(m.ll_attn, m.qd, tag_here, m.err, smem_u32(xs), 0, 0, 0).ok;
+                if (alive) alive = ll_gather_s(m.ll_attn, m.qd, tag_here, m.err, smem_u32(xs), 0).ok;
                 if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
                 named_bar_sync(1, kConsumerThreads);
             } else {
                 // merge the context splits: o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M)
                 const int S = a.splits, hd = m.hd, W2 = hd + 2;
                 float* part = xs + m.qd;  // [nh][S][hd+2] after the qd outputs
-                if (alive) alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0, 0, 0).ok;
+                if (alive) alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0).ok;
                 if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
                 named_bar_sync(1, kConsumerThreads);
                 #pragma unroll 1
@@ -1121,7 +1113,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             }
             quantize_planes(so.xs, m.qd / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);
         } else if (g.kind == PH_DOWN && has_rows) {
-            if (alive) alive = ll_gather_s(m.ll_act, m.FF, tag_here, m.err, smem_u32(xs), 0, 0, 0).ok;
+            if (alive) alive = ll_gather_s(m.ll_act, m.FF, tag_here, m.err, smem_u32(xs), 0).ok;
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
             named_bar_sync(1, kConsumerThreads);
             quantize_planes(so.xs, m.FF / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);

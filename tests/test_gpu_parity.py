@@ -207,6 +207,29 @@ def test_matvec_config1_shapes(built_lib, oracle_lib, torch_cuda, kind, rows, co
     assert np.max(np.abs(got - want)) <= 1e-4 * np.max(np.abs(want)) + 1e-6
 
 
+@pytest.mark.parametrize("kind,rows,cols", [("q8_0", 300, 32768), ("q4_0", 300, 32768)])
+def test_matvec_small_ring(built_lib, oracle_lib, torch_cuda, kind, rows, cols):
+    """Rows so wide that the shared-memory ring has fewer slots (2 for Q8_0) than
+    the producer has lanes and the kernel has consumer warps: checks that the
+    producer never puts two chunks of one slot in a batch and that consumers
+    wait for a chunk to be issued before waiting on its slot."""
+    torch = torch_cuda
+    rng = np.random.default_rng(rows + cols)
+    w = rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02)
+    raw = gw.quantize(w, gw.TYPE_NAMES[kind])
+    x = rng.standard_normal(cols, dtype=np.float32)
+    want = goref.matvec(kind, raw, x, rows, cols)
+    dw = torch.from_numpy(raw).cuda()
+    dx = torch.from_numpy(x).cuda()
+    for _ in range(2):
+        dy = torch.full((rows,), float("nan"), device="cuda")
+        b2decode.matvec(8 if kind == "q8_0" else 2, dw.data_ptr(), dx.data_ptr(), dy.data_ptr(), rows, cols)
+        torch.cuda.synchronize()
+        got = dy.cpu().numpy()
+        assert np.isfinite(got).all()
+        assert rel_l2(got, want) < 1e-5
+
+
 @pytest.mark.parametrize("batch,ctx", [(1, 1), (1, 7), (2, 65), (1, 4096), (8, 4096), (1, 16384), (1, 32768)])
 def test_attention_config3(built_lib, oracle_lib, torch_cuda, batch, ctx):
     torch = torch_cuda
