@@ -18,7 +18,8 @@ LIB_PATH = os.path.join(PKG_DIR, "libb2decode.so")
 HEADER = os.path.join(os.path.dirname(PKG_DIR), "include", "b2decode.h")
 
 B2_OK = 0
-TRACE_SLOTS = 12  # slots per phase and CTA in trace_step (kTraceSlots)
+TRACE_SLOTS = 13  # slots per phase and CTA in trace_step (kTraceSlots)
+PHASES_PER_LAYER = 4  # decode phases per layer (kPhasesPerLayer)
 ERRORS = {
     -1: "IO", -2: "FORMAT", -3: "UNSUPPORTED_TYPE", -4: "OOM", -5: "CUDA", -6: "NCCL", -7: "TIMEOUT",
     -8: "BAD_ARG", -9: "CONTEXT", -10: "NOT_LOADED",
@@ -237,8 +238,8 @@ class Model:
         """[phases, TRACE_SLOTS, ctas] timeline of one decode step: globaltimer
         stamps (ns) in slots 0-5, consumer chunk-wait ns and slow-wait count in
         6-7, producer slot-wait ns and chunks issued in 8-9, rows loop done in 10,
-        ns in tile dot products in 11."""
-        P = 5 * self.cfg["num_layers"] + 1
+        ns in tile dot products in 11, epilogue constants ready in 12."""
+        P = PHASES_PER_LAYER * self.cfg["num_layers"] + 1
         cap = P * TRACE_SLOTS * 1024
         out = np.zeros(cap, dtype=np.int64)
         npz, nc = C.c_int32(), C.c_int32()

@@ -63,10 +63,9 @@ struct TGeom {
     int rows;           // real output rows
     int tiles;          // ceil(rows / kTileRows)
     int nb;             // K / 32
-    int units;          // PH_ATTN: (query head, split) work items
 };
 
-__device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const StepArgs& a, int p) {
+__device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const LayerDev* layers, int p) {
     TGeom g{};
     if (p == kPhasesPerLayer * m.L) {
         g.kind = PH_LMHEAD;
@@ -77,10 +76,9 @@ __device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const StepArgs& a
     } else {
         g.layer = p / kPhasesPerLayer;
         g.kind = p % kPhasesPerLayer;
-        const LayerDev& L = m.layers[g.layer];
+        const LayerDev& L = layers[g.layer];
         switch (g.kind) {
-            case PH_QKV: g.w = L.wqkv; g.rows = m.qd + 2 * m.kvd; g.nb = m.H / 32; break;
-            case PH_ATTN: g.units = m.nh * a.splits; break;
+            case PH_QA: g.w = L.wqkv; g.rows = m.qd + 2 * m.kvd; g.nb = m.H / 32; break;
             case PH_WO: g.w = L.wo; g.rows = m.H; g.nb = m.qd / 32; break;
             case PH_GATEUP:
                 g.w = L.wgu;
@@ -99,6 +97,11 @@ __device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const StepArgs& a
 // scales, twice for gate + up.
 __device__ __forceinline__ int tile_unit_bytes(const TGeom& g, int qtype) {
     return (kTileRows * tile_qb(qtype) + 2 * kTileRows) * (g.w2 ? 2 : 1);
+}
+
+// This CTA's work plan in weight phase g (precomputed on the host).
+__device__ __forceinline__ TPlan phase_plan(const TPlan* plans, const TGeom& g, int S) {
+    return plans[plan_slot(g.kind, S)];
 }
 
 // The matvec entry point's single phase: rows of a ggml-layout matrix.
@@ -368,14 +371,18 @@ __device__ __forceinline__ void dot2_q4(const uint8_t* r0, const uint8_t* r1, bo
 // transformer.go:525-531 + gguf.go:540-613: element j of token_embd row tok,
 // decoded from its block of the tiled matrix (out-of-range ids embed to zero).
 template <int QT>
-__device__ __forceinline__ float embed_elem(const ModelDev& m, int tok, int j) {
-    if (tok < 0 || tok >= m.V) return 0.0f;
-    const int nb = m.H / 32, b = j >> 5, e = j & 31;
-    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(m.tok_embd + tiled_soff(tok, b, nb, m.Vp, QT)));
-    if (QT == 8) return d * (float)(int8_t)m.tok_embd[tiled_qoff(tok, b, e, nb, 8)];
-    const uint8_t byte = m.tok_embd[tiled_qoff(tok, b, e & 15, nb, 2)];
+__device__ __forceinline__ float embed_val(const uint8_t* embd, int V, int H, int Vp, int tok, int j) {
+    if (tok < 0 || tok >= V) return 0.0f;
+    const int nb = H / 32, b = j >> 5, e = j & 31;
+    const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(embd + tiled_soff(tok, b, nb, Vp, QT)));
+    if (QT == 8) return d * (float)(int8_t)embd[tiled_qoff(tok, b, e, nb, 8)];
+    const uint8_t byte = embd[tiled_qoff(tok, b, e & 15, nb, 2)];
     const int nib = (e < 16) ? (byte & 15) : (byte >> 4);
     return d * (float)(nib - 8);
+}
+template <int QT>
+__device__ __forceinline__ float embed_elem(const ModelDev& m, int tok, int j) {
+    return embed_val<QT>(m.tok_embd, m.V, m.H, m.Vp, tok, j);
 }
 
 struct Best {
@@ -424,66 +431,81 @@ __device__ __forceinline__ int cb_bias(const ModelDev& m) { return m.H; }
 __device__ __forceinline__ int cb_cos(const ModelDev& m) { return m.H + kMaxQkvRows + 4; }
 __device__ __forceinline__ int cb_sin(const ModelDev& m) { return m.H + kMaxQkvRows + 4 + m.hd / 2; }
 
-// The attention phase, transformer.go:658-685, for one query head over one
-// slice [t0, t1) of the context.  Cached K and V rows of a tile go to shared
-// memory by cp.async; the first tile's copies are issued before the poll for
-// q, so they overlap the QKV phase.  The new position's k and v come from the
-// QKV phase's LL words (its cache stores are not ordered with them).  Scores:
-// one thread per position; weighted V sum: thread (chunk vc, group vg) sums 8
-// dims over positions vg, vg + ngrp, ...; online softmax across tiles.  The
-// result is o / l (one split) or the split partial (o, m, l).  Not inlined,
-// so its tiles and gathers do not raise the kernel's register peak.
+// Attention scratch (floats, at smem offset so.xs + 4 * attn_off): q [hd],
+// running output [hd], probabilities [TP], per-warp V sums
+// [kConsumerWarps][hd], then one K tile [TP][hd*ES + 16 bytes] and one V tile
+// [TP][hd*ES].  K rows are padded: no bank conflicts across positions.
+struct AttnMap {
+    float* aq;
+    float* ao;
+    float* asc;
+    float* avred;
+    uint8_t* ktile;
+    uint8_t* vtile;
+};
+template <int ES>
+__device__ __forceinline__ AttnMap attn_map(float* base, int hd, int TP) {
+    AttnMap r;
+    r.aq = base;
+    r.ao = r.aq + hd;
+    r.asc = r.ao + hd;
+    r.avred = r.asc + TP;
+    r.ktile = reinterpret_cast<uint8_t*>(r.avred + kConsumerWarps * hd);
+    r.vtile = r.ktile + (size_t)TP * (hd * ES + 16);
+    return r;
+}
+
+// cp.async copies of the cached K and V rows of positions [tb, tb + nt) into
+// the tile buffers (one committed group).
 template <bool F32>
-__device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, const uint2* vsrc, const uint8_t* kg,
-                                       const uint8_t* vg, uint32_t gs, int hd, int TP, int t0, int t1, int pos,
-                                       unsigned tag_here, unsigned tag_out, uint2* out, int split_out, int* err,
-                                       uint32_t xs_off, uint32_t red_off, int alive) {
+__device__ __noinline__ void attn_load_tile(const uint8_t* kg, const uint8_t* vg, uint32_t gs, int hd, int TP, int tb,
+                                            int nt, uint32_t scratch_off) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int ES = F32 ? 4 : 2;
+    const AttnMap am = attn_map<ES>(reinterpret_cast<float*>(smem + scratch_off), hd, TP);
+    const int ct = threadIdx.x - 32;
+    const int rowb = hd * ES, KS = rowb + 16, pieces = rowb / 16;
+#pragma unroll 1
+    for (int i = ct; i < nt * pieces; i += kConsumerThreads) {
+        const int t = i / pieces, c = i - t * pieces;
+        cp_async16(am.ktile + (size_t)t * KS + c * 16, kg + (size_t)(tb + t) * gs + c * 16);
+        cp_async16(am.vtile + (size_t)t * rowb + c * 16, vg + (size_t)(tb + t) * gs + c * 16);
+    }
+    cp_async_commit();
+}
+
+// The attention of one query head over the cached positions [t0, t1) (one
+// context split), transformer.go:658-685.  q (after RoPE) is already in the
+// scratch; the first tile's copies were issued before the phase's input
+// poll, so they overlapped the hand-off and the q projection.  Scores: one
+// thread per position; weighted V sum: thread (8-dim chunk vc, group vg) sums
+// over positions vg, vg + ngrp, ...; online softmax across tiles.  Writes
+// the split partial (o unnormalised, m, l) as LL words: the Wo phase merges
+// the splits with the new position's own term.  Not inlined, so its tiles do
+// not raise the kernel's register peak.
+template <bool F32>
+__device__ __noinline__ void attn_phase(const uint8_t* kg, const uint8_t* vg, uint32_t gs, int hd, int TP, int t0,
+                                        int t1, unsigned tag_out, uint2* out, uint32_t scratch_off, uint32_t red_off) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int ES = F32 ? 4 : 2;
     const int ct = threadIdx.x - 32, lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 1;
-    float* xs = reinterpret_cast<float*>(smem + xs_off);
+    const AttnMap am = attn_map<ES>(reinterpret_cast<float*>(smem + scratch_off), hd, TP);
     float* red = reinterpret_cast<float*>(smem + red_off);
-    const int rowb = hd * ES, KS = rowb + 16;  // K rows padded: no bank conflicts across positions
-    float* aq = xs;                    // [hd] q
-    float* akc = aq + hd;              // [hd] k of the new position
-    float* avc = akc + hd;             // [hd] v of the new position
-    float* ao = avc + hd;              // [hd] running output
-    float* asc = ao + hd;              // [TP] probabilities of the tile
-    float* avred = asc + TP;           // [kConsumerWarps][hd] per-warp V sums
-    uint8_t* ktile = reinterpret_cast<uint8_t*>(avred + kConsumerWarps * hd);  // [TP][KS]
-    uint8_t* vtile = ktile + (size_t)TP * KS;                                   // [TP][rowb]
-    const int pieces = rowb / 16;
-    auto load_tile = [&](int tb, int nt) {
-        #pragma unroll 1
-        for (int i = ct; i < nt * pieces; i += kConsumerThreads) {
-            const int t = i / pieces, c = i - t * pieces;
-            if (tb + t == pos) continue;
-            cp_async16(ktile + (size_t)t * KS + c * 16, kg + (size_t)(tb + t) * gs + c * 16);
-            cp_async16(vtile + (size_t)t * rowb + c * 16, vg + (size_t)(tb + t) * gs + c * 16);
-        }
-        cp_async_commit();
-    };
-    if (t1 > t0) load_tile(t0, min(TP, t1 - t0));
-
-    if (alive) alive = ll_gather_s(qsrc, hd, tag_here, err, smem_u32(aq), 0).ok;
-    if (alive && pos >= t0 && pos < t1) {
-        alive = ll_gather_s(ksrc, hd, tag_here, err, smem_u32(akc), 0).ok;
-        if (alive) alive = ll_gather_s(vsrc, hd, tag_here, err, smem_u32(avc), 0).ok;
-    }
-    #pragma unroll 1
-    for (int i = ct; i < hd; i += kConsumerThreads) ao[i] = 0.0f;
+    const int rowb = hd * ES, KS = rowb + 16;
+#pragma unroll 1
+    for (int i = ct; i < hd; i += kConsumerThreads) am.ao[i] = 0.0f;
     cp_async_wait();
     named_bar_sync(1, kConsumerThreads);
 
-    const float scale = (float)(1.0 / sqrt((double)hd));
+    const float scale = 1.0f / sqrtf((float)hd);
     const int hv = hd / 8, ngrp = kConsumerThreads / hv;
     const int vc = ct % hv, vgi = ct / hv;
     float mrun = -INFINITY, lrun = 0.0f;
-    #pragma unroll 1
+#pragma unroll 1
     for (int tb = t0; tb < t1; tb += TP) {
         const int nt = min(TP, t1 - tb);
         if (tb != t0) {
-            load_tile(tb, nt);
+            attn_load_tile<F32>(kg, vg, gs, hd, TP, tb, nt, scratch_off);
             cp_async_wait();
             named_bar_sync(1, kConsumerThreads);
         }
@@ -491,16 +513,10 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
         float sv = -INFINITY;
         if (ct < nt) {
             float d0 = 0.0f, d1 = 0.0f;
-            if (tb + ct == pos) {
-                #pragma unroll 1
-                for (int d = 0; d < hd; d += 2) {
-                    d0 = fmaf(aq[d], akc[d], d0);
-                    d1 = fmaf(aq[d + 1], akc[d + 1], d1);
-                }
-            } else if (F32) {
-                const float4* kr = reinterpret_cast<const float4*>(ktile + (size_t)ct * KS);
-                const float4* q4 = reinterpret_cast<const float4*>(aq);
-                #pragma unroll 1
+            if (F32) {
+                const float4* kr = reinterpret_cast<const float4*>(am.ktile + (size_t)ct * KS);
+                const float4* q4 = reinterpret_cast<const float4*>(am.aq);
+#pragma unroll 1
                 for (int i = 0; i < hd / 4; i++) {
                     const float4 k = kr[i], q = q4[i];
                     d0 = fmaf(q.x, k.x, d0);
@@ -509,9 +525,9 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
                     d1 = fmaf(q.w, k.w, d1);
                 }
             } else {
-                const uint4* kr = reinterpret_cast<const uint4*>(ktile + (size_t)ct * KS);
-                const float4* q4 = reinterpret_cast<const float4*>(aq);
-                #pragma unroll 1
+                const uint4* kr = reinterpret_cast<const uint4*>(am.ktile + (size_t)ct * KS);
+                const float4* q4 = reinterpret_cast<const float4*>(am.aq);
+#pragma unroll 1
                 for (int i = 0; i < hd / 8; i++) {
                     const uint4 ku = kr[i];
                     const __half2* kh = reinterpret_cast<const __half2*>(&ku);
@@ -534,7 +550,7 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
         const float mb = block_max(sv, red, cw);
         const float mnew = fmaxf(mrun, mb);
         const float pv = (ct < nt) ? expf(sv - mnew) : 0.0f;
-        if (ct < nt) asc[ct] = pv;
+        if (ct < nt) am.asc[ct] = pv;
         const float lb = block_sum(pv, red, cw);  // its barriers also publish asc[]
         const float corr = (mrun == -INFINITY) ? 0.0f : expf(mrun - mnew);
         lrun = lrun * corr + lb;
@@ -543,20 +559,17 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
         float acc[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) acc[e] = 0.0f;
-        #pragma unroll 1
+#pragma unroll 1
         for (int tl = vgi; tl < nt; tl += ngrp) {
-            const float pt = asc[tl];
+            const float pt = am.asc[tl];
             float vf[8];
-            if (tb + tl == pos) {
-#pragma unroll
-                for (int e = 0; e < 8; e++) vf[e] = avc[vc * 8 + e];
-            } else if (F32) {
-                const float4* vr = reinterpret_cast<const float4*>(vtile + (size_t)tl * rowb + vc * 32);
+            if (F32) {
+                const float4* vr = reinterpret_cast<const float4*>(am.vtile + (size_t)tl * rowb + vc * 32);
                 const float4 x0 = vr[0], x1 = vr[1];
                 vf[0] = x0.x; vf[1] = x0.y; vf[2] = x0.z; vf[3] = x0.w;
                 vf[4] = x1.x; vf[5] = x1.y; vf[6] = x1.z; vf[7] = x1.w;
             } else {
-                const uint4 vu = *reinterpret_cast<const uint4*>(vtile + (size_t)tl * rowb + vc * 16);
+                const uint4 vu = *reinterpret_cast<const uint4*>(am.vtile + (size_t)tl * rowb + vc * 16);
                 const __half2* vh = reinterpret_cast<const __half2*>(&vu);
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
@@ -569,42 +582,32 @@ __device__ __noinline__ int attn_phase(const uint2* qsrc, const uint2* ksrc, con
             for (int e = 0; e < 8; e++) acc[e] = fmaf(pt, vf[e], acc[e]);
         }
         // lanes of one warp that share a chunk: lane, lane ^ hv, ...
-        #pragma unroll 1
+#pragma unroll 1
         for (int o = hv; o < 32; o <<= 1) {
 #pragma unroll
             for (int e = 0; e < 8; e++) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
         }
         if (lane < hv) {
 #pragma unroll
-            for (int e = 0; e < 8; e++) avred[cw * hd + lane * 8 + e] = acc[e];
+            for (int e = 0; e < 8; e++) am.avred[cw * hd + lane * 8 + e] = acc[e];
         }
         named_bar_sync(1, kConsumerThreads);
-        #pragma unroll 1
+#pragma unroll 1
         for (int d = ct; d < hd; d += kConsumerThreads) {
-            float o = ao[d] * corr;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; w++) o += avred[w * hd + d];
-            ao[d] = o;
+            float o = am.ao[d] * corr;
+#pragma unroll 1
+            for (int w = 0; w < kConsumerWarps; w++) o += am.avred[w * hd + d];
+            am.ao[d] = o;
         }
         named_bar_sync(1, kConsumerThreads);
     }
-    if (!split_out) {
-        #pragma unroll 1
-        for (int d = ct; d < hd; d += kConsumerThreads) ll_store(out + d, ao[d] / lrun, tag_out);
-    } else {
-        // split partial (o unnormalised, m, l), laid out [head][split][hd + 2]
-        #pragma unroll 1
-        for (int i = ct; i < hd + 2; i += kConsumerThreads) {
-            const float v = i < hd ? ao[i] : (i == hd ? mrun : lrun);
-            ll_store(out + i, v, tag_out);
-        }
+    // split partial (o unnormalised, m, l); an empty split gives (0, -inf, 0)
+#pragma unroll 1
+    for (int i = ct; i < hd + 2; i += kConsumerThreads) {
+        const float v = i < hd ? am.ao[i] : (i == hd ? mrun : lrun);
+        ll_store(out + i, v, tag_out);
     }
-    return alive;
 }
-
-// ---------------------------------------------------------------------------
-// int8 tensor-core tile dot (model phases)
-// ---------------------------------------------------------------------------
 
 // mma.m16n8k32 with int32 accumulate: A = 16 weight rows x 32 (s8 for Q8_0,
 // u8 nibbles for Q4_0), B = x planes in columns 0-2; c01 / c23 start the
@@ -704,6 +707,147 @@ __device__ __noinline__ float2 tile_dot(uint32_t q, uint32_t sc_off, int nbc, ui
     y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
     y1 += __shfl_xor_sync(0xffffffffu, y1, 2);
     return make_float2(y0, y1);
+}
+
+// Quarter-block of 8 values -> int8 planes (see quantize_planes); the four
+// threads of a block (consecutive lanes) agree on its max with two shuffles.
+// Every lane of the warp must call it.
+__device__ __forceinline__ void planes8(const float* v, bool on, int b, int sub, uint8_t* xqb, float* xsc, int* xsm,
+                                        bool sums) {
+    const float M = kAccMagicF;
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) amax = fmaxf(amax, on ? fabsf(v[e]) : 0.0f);
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float inv = amax > 0.0f ? __fdividef(127.0f, amax) : 0.0f;
+    uint32_t by[3][8];
+    int sg[3] = {0, 0, 0};
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const float q = on ? v[e] * inv : 0.0f;
+        const float f0 = q + M, r0 = f0 - M;
+        const float q1 = (q - r0) * 128.0f;
+        const float f1 = q1 + M, r1 = f1 - M;
+        const float f2 = (q1 - r1) * 128.0f + M;
+        by[0][e] = __float_as_uint(f0);
+        by[1][e] = __float_as_uint(f1);
+        by[2][e] = __float_as_uint(f2);
+        if (sums) {
+            sg[0] += (int)r0;
+            sg[1] += (int)r1;
+            sg[2] += (int)(f2 - M);
+        }
+    }
+    if (sums) {
+#pragma unroll
+        for (int gq = 0; gq < 3; gq++) {
+            sg[gq] += __shfl_xor_sync(0xffffffffu, sg[gq], 1);
+            sg[gq] += __shfl_xor_sync(0xffffffffu, sg[gq], 2);
+        }
+    }
+    if (on) {
+        // elements sub*8 + 0..7: word w = sub / 2 (a0 or a2), lane groups
+        // t0 = (sub & 1) * 2 and t0 + 1, bytes e & 3
+        const int w = sub >> 1, t0 = (sub & 1) * 2;
+        uint32_t* xw = reinterpret_cast<uint32_t*>(xqb + b * 96);
+#pragma unroll
+        for (int gq = 0; gq < 3; gq++) {
+            const uint32_t lo = __byte_perm(__byte_perm(by[gq][0], by[gq][1], 0x0040),
+                                            __byte_perm(by[gq][2], by[gq][3], 0x0040), 0x5410);
+            const uint32_t hi = __byte_perm(__byte_perm(by[gq][4], by[gq][5], 0x0040),
+                                            __byte_perm(by[gq][6], by[gq][7], 0x0040), 0x5410);
+            xw[(gq * 4 + t0) * 2 + w] = lo;
+            xw[(gq * 4 + t0 + 1) * 2 + w] = hi;
+        }
+        if (sub == 0) {
+            xsc[b] = amax * (1.0f / 127.0f);
+            if (sums) {
+                xsm[b * 3 + 0] = sg[0];
+                xsm[b * 3 + 1] = sg[1];
+                xsm[b * 3 + 2] = sg[2];
+            }
+        }
+    }
+}
+
+// The phase input straight into int8 planes, without staging it as floats:
+// each thread polls the LL words of whole quarter-blocks (8 values = four
+// 16-byte loads), multiplies them by the norm gains (global `gain`; none when
+// null) and splits them (planes8).  The RMSNorm scale is one scalar per
+// token, so it is applied to the dot products instead (the dot is linear); the
+// sum of squares of the raw values is returned for it.  With `embed` set the
+// values are the embedding of token tok (layer 0; an id outside the
+// vocabulary embeds to zero) instead of LL words.  A
+// failed or timed-out poll sets ok = 0 but the loop runs to the end, so every
+// lane reaches every shuffle.  Not inlined (register peak, code size).
+template <int QT>
+__device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsigned tag, int* err, int embed, int tok,
+                                                const uint8_t* embd, int V, int H, int Vp, uint32_t xq_off,
+                                                uint32_t xsc_off, uint32_t xsm_off, const float* gain, int sums) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* xqb = smem + xq_off;
+    float* xsc = reinterpret_cast<float*>(smem + xsc_off);
+    int* xsm = reinterpret_cast<int*>(smem + xsm_off);
+    const int ct = threadIdx.x - 32;
+    bool ok = true;
+    uint64_t t0 = 0;
+    float ss = 0.0f;
+#pragma unroll 1
+    for (int base = 0; base < 4 * nbk; base += kConsumerThreads) {
+        const int i = base + ct;
+        const bool on = i < 4 * nbk;
+        const int b = i >> 2, sub = i & 3, j0 = b * 32 + sub * 8;
+        float v[8];
+        float4 g0 = make_float4(1.0f, 1.0f, 1.0f, 1.0f), g1 = g0;
+        if (on && gain) {  // issued before the poll, so their latency overlaps it
+            g0 = __ldg(reinterpret_cast<const float4*>(gain + j0));
+            g1 = __ldg(reinterpret_cast<const float4*>(gain + j0 + 4));
+        }
+        if (on && embed) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = embed_val<QT>(embd, V, H, Vp, tok, j0 + e);
+        } else if (on) {
+            const uint2* sp = src + j0;
+            uint4 w[4];
+            for (;;) {
+                bool got = true;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    w[k] = ll_load2(sp + 2 * k);
+                    got &= (w[k].y == tag) & (w[k].w == tag);
+                }
+                if (got || !ok) break;
+                __nanosleep(64);  // back off: thousands of pollers share these lines
+                const uint64_t now = global_ns();
+                if (t0 == 0) t0 = now;
+                if (now - t0 > kWaitLimitNs) {
+                    set_err(err, B2_ERR_TIMEOUT);
+                    ok = false;
+                } else if (*(volatile int*)err) {
+                    ok = false;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                v[2 * k] = __uint_as_float(w[k].x);
+                v[2 * k + 1] = __uint_as_float(w[k].z);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = 0.0f;
+        }
+        if (on) {
+            const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                ss += v[e] * v[e];
+                v[e] *= gg[e];
+            }
+        }
+        planes8(v, on, b, sub, xqb, xsc, xsm, sums != 0);
+    }
+    return GatherRes{ss, ok ? 1 : 0};
 }
 
 // Splits the staged phase input xs[0 .. 32*nbk) into int8 planes: per
@@ -808,7 +952,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     extern __shared__ __align__(128) uint8_t smem[];
     const int NS = m.nslots;
     const int SB = m.slot_bytes;
-    const SmemOffsets so = smem_offsets(NS, SB, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx);
+    const SmemOffsets so = smem_offsets(NS, SB, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx, MV ? 0 : m.L);
     uint8_t* ring = smem;
     float* xs = reinterpret_cast<float*>(smem + so.xs);
     uint8_t* xqb = smem + so.xq;
@@ -821,6 +965,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + so.empty);
     float* red = reinterpret_cast<float*>(smem + so.red);
     int* misc = reinterpret_cast<int*>(smem + so.misc);
+    const TPlan* plans = reinterpret_cast<const TPlan*>(smem + so.plan);       // this CTA's work plans
+    const LayerDev* layers = reinterpret_cast<const LayerDev*>(smem + so.lay);  // the layer table
     volatile unsigned* pstop = reinterpret_cast<volatile unsigned*>(misc + 31);  // first chunk not issued
     volatile int* dead = misc + 30;  // set by any consumer thread whose wait failed
     unsigned* issued = reinterpret_cast<unsigned*>(misc + 29);  // chunks the producer has issued
@@ -831,6 +977,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     // A device-resident greedy loop that already produced EOS does no work.
     if (!MV && a.done && *(volatile const int*)a.done) return;
 
+    if (!MV) {
+        // this CTA's plans and the layer table, for the whole launch
+        const uint2* ps = reinterpret_cast<const uint2*>(m.plans + (size_t)cta * kPlanSlots);
+        uint2* pd = reinterpret_cast<uint2*>(smem + so.plan);
+        #pragma unroll 1
+        for (int i = threadIdx.x; i < (int)(kPlanSlots * sizeof(TPlan) / 8); i += blockDim.x) pd[i] = ps[i];
+        const uint2* ls = reinterpret_cast<const uint2*>(m.layers);
+        uint2* ld = reinterpret_cast<uint2*>(smem + so.lay);
+        #pragma unroll 1
+        for (int i = threadIdx.x; i < (int)(m.L * sizeof(LayerDev) / 8); i += blockDim.x) ld[i] = ls[i];
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; s++) {
             mbar_init(&full[s], 1);
@@ -869,9 +1026,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     nchunks = ms.nchunks;
                     pl.nks = 1;
                 } else {
-                    g = phase_geom(m, a, p);
-                    if (!g.w) continue;
-                    pl = tile_plan(g.tiles, g.nb, tile_unit_bytes(g, QT), cta, grid, SB, kConsumerWarps);
+                    g = phase_geom(m, layers, p);
+                    pl = phase_plan(plans, g, a.splits);
                     nchunks = pl.nchunks;
                 }
                 if (TR && a.trace && lane == 0 && nchunks) a.trace[(trp + 4) * grid + cta] = global_ns();
@@ -1016,10 +1172,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
 
     #pragma unroll 1
     for (int p = a.p_begin; p < a.p_end; p++) {
-        const TGeom g = phase_geom(m, a, p);
-        const TPlan pl = g.w ? tile_plan(g.tiles, g.nb, tile_unit_bytes(g, QT), cta, grid, SB, kConsumerWarps)
-                             : TPlan{0, 0, 1, 1, 1, 0};
+        const TGeom g = phase_geom(m, layers, p);
+        const TPlan pl = phase_plan(plans, g, a.splits);
         const bool has_rows = pl.nchunks > 0;
+        const bool qa = g.kind == PH_QA;
+        const int S = a.splits;
+        const bool qcta = qa && cta < m.nh * S;  // q + attention role in the QA phase
         const size_t tr = (size_t)(p - a.p_begin) * kTraceSlots;
         if (TR && a.trace && ct == 0) {
             a.trace[(tr + 0) * grid + cta] = global_ns();
@@ -1031,27 +1189,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         }
         const unsigned tag_here = ll_tag(a.epoch, g.layer) + a.skew;
         const unsigned tag_prev = ll_tag(a.epoch, g.layer - 1) + a.skew;
+        // attention work of a q CTA: head h, split sidx over the cached positions [0, pos)
+        const int hd = m.hd, TP = m.attn_tile;
+        const int h = qcta ? cta / S : 0, sidx = qcta ? cta - h * S : 0, kvh = h / (m.nh / m.nkv);
+        const int at0 = (int)((long long)sidx * a.pos / S), at1 = (int)((long long)(sidx + 1) * a.pos / S);
+        const int es = KV32 ? 4 : 2;
+        const size_t lay = ((size_t)g.layer * m.max_seq * m.kvd + (size_t)kvh * hd) * es;
+        const uint8_t* kg = reinterpret_cast<const uint8_t*>(m.kcache) + lay;
+        const uint8_t* vg = reinterpret_cast<const uint8_t*>(m.vcache) + lay;
+        const uint32_t attn_off = so.xs + 4u * (uint32_t)((m.H + 31) & ~31);  // after the QA input
 
         // 1. stage the phase input: gather (+ norm / merge) into xs, then planes
-        if (g.kind == PH_QKV && g.layer == 0) {
+        if (qa && g.layer == 0) {
             // transformer.go:524-531: the residual stream starts at the embedding
             #pragma unroll 1
             for (int j = own0 + ct; j < own1; j += kConsumerThreads) xres[j - own0] = embed_elem<QT>(m, tok, j);
         }
-        if ((g.kind == PH_QKV || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) && has_rows) {
-            // constants first (they land while the poll below waits)
-            const float* nw = g.kind == PH_QKV ? m.layers[g.layer].attn_norm
-                            : (g.kind == PH_GATEUP ? m.layers[g.layer].ffn_norm : m.out_norm);
-            #pragma unroll 1
-            for (int i = ct; i < m.H / 4; i += kConsumerThreads) cp_async16(cb + 4 * i, nw + 4 * i);
-            if (g.kind == PH_QKV) {
-                const float* bq = m.layers[g.layer].bqkv;
+        if ((qa || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) && has_rows) {
+            // QKV constants first (they land while the poll below waits)
+            if (qa) {
+                const float* bq = layers[g.layer].bqkv;
                 const int r0b = (kTileRows * pl.u0) & ~3, r1 = kTileRows * (pl.u0 + pl.n);
                 if (bq)
                     #pragma unroll 1
                     for (int i = ct; i < (r1 - r0b + 3) / 4; i += kConsumerThreads)
                         cp_async16(cb + cb_bias(m) + 4 * i, bq + r0b + 4 * i);
-                const int hh = m.hd / 2;
+                const int hh = hd / 2;
                 #pragma unroll 1
                 for (int i = ct; i < hh / 4; i += kConsumerThreads) {
                     cp_async16(cb + cb_cos(m) + 4 * i, m.rope_cos + (size_t)a.pos * hh + 4 * i);
@@ -1059,64 +1222,81 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 }
             }
             cp_async_commit();
-            // RMSNorm (transformer.go:922-932) fused into the stage
+            // a q CTA's first cached K/V tile goes out now too (its own group,
+            // waited for in the attention): it overlaps the poll and the dot
+            if (qcta && at1 > at0)
+                attn_load_tile<KV32>(kg, vg, (uint32_t)(m.kvd * es), hd, TP, at0, min(TP, at1 - at0), attn_off);
+            // RMSNorm (transformer.go:922-932): x * gain goes into the planes here,
+            // the scale 1/rms multiplies the dot products in the epilogue
+            const float* nw = qa ? layers[g.layer].attn_norm
+                                 : (g.kind == PH_GATEUP ? layers[g.layer].ffn_norm : m.out_norm);
             float ss = 0.0f;
-            if (g.kind == PH_QKV && g.layer == 0) {
-                #pragma unroll 1
-                for (int j = ct; j < m.H; j += kConsumerThreads) {
-                    const float v = embed_elem<QT>(m, tok, j);
-                    xs[j] = v;
-                    ss += v * v;
-                }
-            } else if (alive) {
-                const uint2* src = g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2;
-                const unsigned tg = g.kind == PH_GATEUP ? tag_here : tag_prev;
-                const GatherRes gr = ll_gather_s(src, m.H, tg, m.err, smem_u32(xs), 1);
+            if (alive) {
+                const GatherRes gr = gather_planes<QT>(g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2, m.H / 32,
+                                                       g.kind == PH_GATEUP ? tag_here : tag_prev, m.err,
+                                                       qa && g.layer == 0, tok, m.tok_embd, m.V, m.H, m.Vp,
+                                                       so.xq, so.xsc, so.xsm, nw, QT != 8);
                 alive = gr.ok;
                 ss = gr.ss;
             }
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-            cp_async_wait();
-            const float tot = block_sum(ss, red, cw);  // its barriers also publish xs[] and cb[]
-            const float r = (float)(1.0 / sqrt((double)(tot / (float)m.H) + (double)m.eps));
-            quantize_planes(so.xs, m.H / 32, so.xq, so.xsc, so.xsm, r, so.cbuf, QT != 8);
+            if (qcta && at1 > at0) cp_async_wait_1();  // the constants (not the K/V tile)
+            else cp_async_wait();
+            ss = warp_sum(ss);
+            if (lane == 0) red[32 + cw] = ss;  // summed after the rows barrier
         } else if (g.kind == PH_WO && has_rows) {
-            if (a.splits == 1) {
-                if (alive) alive = ll_gather_s(m.ll_attn, m.qd, tag_here, m.err, smem_u32(xs), 0).ok;
-                if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-                named_bar_sync(1, kConsumerThreads);
-            } else {
-                // merge the context splits: o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M)
-                const int S = a.splits, hd = m.hd, W2 = hd + 2;
-                float* part = xs + m.qd;  // [nh][S][hd+2] after the qd outputs
-                if (alive) alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0).ok;
-                if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-                named_bar_sync(1, kConsumerThreads);
-                #pragma unroll 1
-                for (int i = ct; i < m.qd; i += kConsumerThreads) {
-                    const int hh = i / hd, d = i - hh * hd;
-                    const float* ph = part + (size_t)hh * S * W2;
-                    float M = -INFINITY;
-                    #pragma unroll 1
-                    for (int s2 = 0; s2 < S; s2++) M = fmaxf(M, ph[s2 * W2 + hd]);
-                    float Ls = 0.0f, o = 0.0f;
-                    #pragma unroll 1
-                    for (int s2 = 0; s2 < S; s2++) {
-                        const float ms = ph[s2 * W2 + hd];
-                        const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-                        Ls = fmaf(ph[s2 * W2 + hd + 1], w, Ls);
-                        o = fmaf(ph[s2 * W2 + d], w, o);
-                    }
-                    xs[i] = o / Ls;
-                }
-                named_bar_sync(1, kConsumerThreads);
-            }
-            quantize_planes(so.xs, m.qd / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);
-        } else if (g.kind == PH_DOWN && has_rows) {
-            if (alive) alive = ll_gather_s(m.ll_act, m.FF, tag_here, m.err, smem_u32(xs), 0).ok;
+            // Merge the attention of every head: S split partials over the
+            // cached positions plus the new position's own term (score q.k_new,
+            // value v_new), transformer.go:664-685 over all ctx positions:
+            // o = (sum_s o_s e^(m_s - M) + v_new e^(s_new - M)) / (sum_s l_s e^(m_s - M) + e^(s_new - M))
+            const int W2 = hd + 2;
+            float* snew = xs + m.qd;                      // [nh][S + 1] merge weights
+            float* part = snew + ((m.nh * (kMaxSplits + 1) + 3) & ~3);  // [nh][S][hd+2]
+            float* qv = part + ((m.nh * S * W2 + 3) & ~3);  // [qd] q
+            float* kvn = qv + m.qd;                       // [2*kvd] k, v of the new position
+            if (alive) alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0).ok;
+            if (alive) alive = ll_gather_s(m.ll_qkv, m.qd + 2 * m.kvd, tag_here, m.err, smem_u32(qv), 0).ok;
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
             named_bar_sync(1, kConsumerThreads);
-            quantize_planes(so.xs, m.FF / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);
+            // per head (one warp): the new position's score, M = the largest of it
+            // and the split maxima, and the weights e^(m - M) / L of every term
+            const float scale = 1.0f / sqrtf((float)hd);
+            #pragma unroll 1
+            for (int hh = cw; hh < m.nh; hh += kConsumerWarps) {
+                const float* qh = qv + (size_t)hh * hd;
+                const float* kh = kvn + (size_t)(hh / (m.nh / m.nkv)) * hd;
+                float d = 0.0f;
+                #pragma unroll 1
+                for (int i = lane; i < hd; i += 32) d = fmaf(qh[i], kh[i], d);
+                d = warp_sum(d) * scale;
+                // lanes 0..S-1 hold split s, lane S the new position
+                const float* ph = part + (size_t)hh * S * W2;
+                const float ms = lane < S ? ph[lane * W2 + hd] : (lane == S ? d : -INFINITY);
+                const float ls = lane < S ? ph[lane * W2 + hd + 1] : (lane == S ? 1.0f : 0.0f);
+                const float M = warp_max(ms);
+                const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+                const float L = warp_sum(ls * w);
+                if (lane <= S) snew[hh * (S + 1) + lane] = w / L;
+            }
+            named_bar_sync(1, kConsumerThreads);
+            const int hsh = __ffs(hd) - 1, grp = m.nh / m.nkv;  // hd is a power of two
+            #pragma unroll 1
+            for (int i = ct; i < m.qd; i += kConsumerThreads) {
+                const int hh = i >> hsh, d = i & (hd - 1);
+                const float* c = snew + hh * (S + 1);
+                const float* ph = part + (size_t)hh * S * W2 + d;
+                float o = kvn[m.kvd + (hh / grp) * hd + d] * c[S];
+                #pragma unroll 1
+                for (int s2 = 0; s2 < S; s2++) o = fmaf(ph[s2 * W2], c[s2], o);
+                xs[i] = o;
+            }
+            named_bar_sync(1, kConsumerThreads);
+            quantize_planes(so.xs, m.qd / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);
+        } else if (g.kind == PH_DOWN && has_rows) {
+            if (alive)
+                alive = gather_planes<QT>(m.ll_act, m.FF / 32, tag_here, m.err, 0, 0, m.tok_embd, m.V, m.H, m.Vp, so.xq,
+                                          so.xsc, so.xsm, nullptr, QT != 8).ok;
+            if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         } else {
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         }
@@ -1126,26 +1306,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         float* yb = ybuf + (p & 1) * m.ybuf_floats;  // parity buffers: the next phase's
                                                       // dots may start before this epilogue ends
         const int rc = kTileRows * pl.n * (g.w2 ? 2 : 1);  // outputs of one K-slice in yb
-        if (g.kind == PH_ATTN) {
-            // 2'. attention, one (query head, split) per CTA
-            if (cta < g.units) {
-                const int S = a.splits, hd = m.hd;
-                const int h = cta / S, sidx = cta - h * S, kvh = h / (m.nh / m.nkv);
-                const int ctx = a.pos + 1;
-                const int t0 = (int)((long long)sidx * ctx / S), t1 = (int)((long long)(sidx + 1) * ctx / S);
-                const int es = KV32 ? 4 : 2;
-                const size_t lay = ((size_t)g.layer * m.max_seq * m.kvd + (size_t)kvh * hd) * es;
-                const uint8_t* kg = reinterpret_cast<const uint8_t*>(m.kcache) + lay;
-                const uint8_t* vg = reinterpret_cast<const uint8_t*>(m.vcache) + lay;
-                uint2* out = S == 1 ? m.ll_attn + (size_t)h * hd : m.ll_part + ((size_t)h * S + sidx) * (hd + 2);
-                const uint2* q = m.ll_qkv + (size_t)h * hd;
-                const uint2* kn = m.ll_qkv + m.qd + (size_t)kvh * hd;
-                const uint2* vn = kn + m.kvd;
-                const unsigned tout = ll_tag(a.epoch, g.layer);
-                alive = attn_phase<KV32>(q, kn, vn, kg, vg, (uint32_t)(m.kvd * es), hd, m.attn_tile, t0, t1, a.pos,
-                                         tag_here, tout, out, S != 1, m.err, so.xs, so.red, alive);
-            }
-        } else {
+        {
             // 2. rows: tensor-core dot products of this CTA's tiles into yb
             const uint64_t tl0 = (TR && a.trace) ? global_ns() : 0;
             // this warp's chunks are k = first, first + kConsumerWarps, ... (global
@@ -1225,6 +1386,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
 
         // 3. epilogue, one thread per output; K-slice partials summed in order
         const unsigned tag = ll_tag(a.epoch, g.layer);
+        float rms = 1.0f;  // RMSNorm scale of the norm phases (transformer.go:922-932)
+        if (qa || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) {
+            float tot = 0.0f;
+            #pragma unroll 1
+            for (int w = 0; w < kConsumerWarps; w++) tot += red[32 + w];
+            // in fp32 (Go rounds a float64 result to float32: within an ulp; a
+            // double-precision sqrt and divide cost ~0.8 us on this path)
+            rms = 1.0f / sqrtf(tot / (float)m.H + m.eps);
+        }
+        if (TR && a.trace && ct == 0) a.trace[(tr + 12) * grid + cta] = global_ns();
         const int row0 = kTileRows * pl.u0;
         auto ysum = [&](int i) {
             float v = yb[i];
@@ -1236,39 +1407,45 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             // (every CTA takes part in the argmax, so its arrival counter
             // always completes and resets)
             switch (g.kind) {
-                case PH_QKV: {
+                case PH_QA: {
                     // bias (transformer.go:632-646), RoPE on interleaved pairs
-                    // (936-951), KV append (654-656)
-                    const bool bias = m.layers[g.layer].bqkv != nullptr;
+                    // (936-951); q rows stay in this CTA for its attention (split 0
+                    // also publishes them for the Wo merge), k / v rows are published
+                    // and appended to the KV cache (654-656)
+                    const bool bias = layers[g.layer].bqkv != nullptr;
                     const int bias0 = row0 & ~3;
+                    float* aq = reinterpret_cast<float*>(smem + attn_off);
                     #pragma unroll 1
                     for (int j = ct; j < kTileRows / 2 * pl.n; j += kConsumerThreads) {
                         const int row = row0 + 2 * j;
-                        float a0 = ysum(2 * j), a1 = ysum(2 * j + 1);
+                        float a0 = ysum(2 * j) * rms, a1 = ysum(2 * j + 1) * rms;
                         if (bias) {
                             a0 += cb[cb_bias(m) + row - bias0];
                             a1 += cb[cb_bias(m) + row + 1 - bias0];
                         }
                         if (row < m.qd + m.kvd) {
-                            const int pi2 = (row % m.hd) >> 1;
+                            const int pi2 = (row % hd) >> 1;
                             const float rc2 = cb[cb_cos(m) + pi2], rs = cb[cb_sin(m) + pi2];
                             const float x0 = a0, x1 = a1;
                             a0 = x0 * rc2 - x1 * rs;
                             a1 = x0 * rs + x1 * rc2;
                         }
+                        if (row < m.qd) {
+                            aq[row - h * hd] = a0;
+                            aq[row - h * hd + 1] = a1;
+                            if (sidx == 0) ll_store2(m.ll_qkv + row, a0, a1, tag);
+                            continue;
+                        }
                         ll_store2(m.ll_qkv + row, a0, a1, tag);
-                        if (row >= m.qd) {
-                            const bool isk = row < m.qd + m.kvd;
-                            const int col = row - m.qd - (isk ? 0 : m.kvd);
-                            const size_t off = ((size_t)g.layer * m.max_seq + a.pos) * m.kvd + col;
-                            void* cache = isk ? m.kcache : m.vcache;
-                            if (KV32) {
-                                reinterpret_cast<float*>(cache)[off] = a0;
-                                reinterpret_cast<float*>(cache)[off + 1] = a1;
-                            } else {
-                                *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(cache) + off) =
-                                    __floats2half2_rn(a0, a1);
-                            }
+                        const bool isk = row < m.qd + m.kvd;
+                        const int col = row - m.qd - (isk ? 0 : m.kvd);
+                        const size_t off = ((size_t)g.layer * m.max_seq + a.pos) * m.kvd + col;
+                        void* cache = isk ? m.kcache : m.vcache;
+                        if (KV32) {
+                            reinterpret_cast<float*>(cache)[off] = a0;
+                            reinterpret_cast<float*>(cache)[off + 1] = a1;
+                        } else {
+                            *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(cache) + off) = __floats2half2_rn(a0, a1);
                         }
                     }
                     break;
@@ -1277,7 +1454,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     // SwiGLU (transformer.go:725-727, 954-956)
                     #pragma unroll 1
                     for (int j = ct; j < kTileRows * pl.n && row0 + j < g.rows; j += kConsumerThreads) {
-                        const float gv = ysum(2 * j), uv = ysum(2 * j + 1);
+                        const float gv = ysum(2 * j) * rms, uv = ysum(2 * j + 1) * rms;
                         ll_store(m.ll_act + row0 + j, gv / (1.0f + expf(-gv)) * uv, tag);
                     }
                     break;
@@ -1301,7 +1478,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     for (int j = ct; alive && j < kTileRows * pl.n; j += kConsumerThreads) {
                         const int row = row0 + j;
                         if (row >= g.rows) break;
-                        const float v = ysum(j);
+                        const float v = ysum(j) * rms;
                         m.logits[row] = v;
                         if (better(v, row, best.v, best.i)) { best.v = v; best.i = row; }
                     }
@@ -1341,18 +1518,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 }
             }
         }
+        if (qcta) {
+            // 2'. the head's attention over the cached positions (q is in the scratch)
+            named_bar_sync(1, kConsumerThreads);
+            if (alive)
+                attn_phase<KV32>(kg, vg, (uint32_t)(m.kvd * es), hd, TP, at0, at1, tag,
+                                 m.ll_part + ((size_t)h * S + sidx) * (hd + 2), attn_off, so.red);
+            else
+                cp_async_wait();  // the prefetched tile, before the scratch is reused
+        }
         if (TR && a.trace && ct == 0) {
             a.trace[(tr + 3) * grid + cta] = global_ns();
             a.trace[(tr + 6) * grid + cta] = (unsigned)misc[20];
             a.trace[(tr + 7) * grid + cta] = (unsigned)misc[21];
         }
     }
+    cp_async_wait();
 }
 
 }  // namespace
 
 size_t decode_smem_bytes(const ModelDev& m) {
-    return smem_offsets(m.nslots, m.slot_bytes, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx).total;
+    return smem_offsets(m.nslots, m.slot_bytes, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx, m.plans ? m.L : 0).total;
 }
 
 int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err) {

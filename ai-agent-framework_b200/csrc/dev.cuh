@@ -8,38 +8,39 @@
 namespace b2 {
 
 // One decode token is a fixed sequence of phases; phase p of layer l is
-// 5*l + k with k below, and the lm_head phase is 5*L.  Each phase is split
-// over all CTAs.  Phases hand their outputs to the next phase through "LL"
-// words in global memory: 8 bytes = {fp32 value, 32-bit tag}, written with
-// one 8-byte store, so a reader that sees the expected tag also sees the
-// value.  Polling the data itself is the synchronisation; there is no grid
-// barrier.  Weight bytes of later phases stream into shared memory ahead of
-// time because they never depend on activations.
+// 4*l + k with k below, and the lm_head phase is 4*L.  Phases hand their
+// outputs to the next phase through "LL" words in global memory: 8 bytes =
+// {fp32 value, 32-bit tag}, written with one 8-byte store, so a reader that
+// sees the expected tag also sees the value.  Polling the data itself is the
+// synchronisation; there is no grid barrier.  Weight bytes of later phases
+// stream into shared memory ahead of time because they never depend on
+// activations.
 enum PhaseKind : int {
-    PH_QKV = 0,     // rmsnorm(x) -> [Wq|Wk|Wv] rows, bias, RoPE, KV-cache append
-    PH_ATTN = 1,    // GQA attention of the new query over the cache, split over context
-    PH_WO = 2,      // merge attention splits -> Wo rows, residual add
-    PH_GATEUP = 3,  // rmsnorm(x) -> gate & up rows, SwiGLU -> act
-    PH_DOWN = 4,    // act -> Wd rows, residual add
-    PH_LMHEAD = 5,  // rmsnorm(x) -> lm_head rows, logits + argmax
-    PH_MATVEC = 6,  // plain y = W x (kernel-level entry point)
+    PH_QA = 0,      // rmsnorm(x) -> q rows of one head + attention over the cached context (q CTAs);
+                    //   k, v rows + KV-cache append (kv CTAs)
+    PH_WO = 1,      // merge attention splits and the new position -> Wo rows, residual add
+    PH_GATEUP = 2,  // rmsnorm(x) -> gate & up rows, SwiGLU -> act
+    PH_DOWN = 3,    // act -> Wd rows, residual add
+    PH_LMHEAD = 4,  // rmsnorm(x) -> lm_head rows, logits + argmax
+    PH_MATVEC = 5,  // plain y = W x (kernel-level entry point)
 };
 
-constexpr int kPhasesPerLayer = 5;
+constexpr int kPhasesPerLayer = 4;
 constexpr int kConsumerWarps = 12;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);  // warp 0 = producer
 constexpr int kMaxSplits = 8;                         // attention context splits per KV head
 constexpr int kAttnTileBytes = 16384;                 // bytes of cached K (and of V) per attention tile
 constexpr int kMaxAttnTile = 128;                     // positions per attention tile, at most
 constexpr int kMaxOwnRows = 64;                       // residual rows one CTA keeps (H / grid)
-constexpr int kMaxQkvRows = 128;                      // QKV rows one CTA computes ((qd + 2*kvd) / grid)
+constexpr int kMaxQkvRows = 256;                      // QA-phase rows one CTA computes (hd, or its k/v share)
 // Phase trace slots: consumer phase start, input ready, input staged, work
 // done; producer first and last weight copy issued (globaltimer ns); total ns
 // the consumer warps spent waiting for weight chunks, and how many of those
 // waits took longer than 256 ns; ns the producer waited for free ring slots,
 // and the chunks it issued; consumer rows loop done (before the epilogue);
-// total ns the consumer warps spent in tile dot products.
-constexpr int kTraceSlots = 12;
+// total ns the consumer warps spent in tile dot products; epilogue constants
+// ready.
+constexpr int kTraceSlots = 13;
 
 // Weight matrices live in HBM in a tiled form of their ggml blocks, made at
 // load time (same bytes per weight as the GGUF file):
@@ -109,15 +110,16 @@ struct TPlan {
     int nchunks;    // = ceil(n / nt) * nks
 };
 
+// Plan of the tile range [u0, u0 + n) (see TPlan).
 inline
 #ifdef __CUDACC__
 __host__ __device__
 #endif
-TPlan tile_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, int warps) {
+TPlan tile_plan_range(int u0, int n, int nb, int tbb, int slot_bytes, int warps) {
     // tbb: bytes of one (tile, block) unit incl. scales (x2 for gate + up)
     TPlan t;
-    t.u0 = (int)((long long)cta * tiles / grid);
-    t.n = (int)((long long)(cta + 1) * tiles / grid) - t.u0;
+    t.u0 = u0;
+    t.n = n;
     if (t.n <= 0) {
         t.n = 0; t.nks = 1; t.bpk = nb; t.nt = 1; t.nchunks = 0;
         return t;
@@ -128,7 +130,6 @@ TPlan tile_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, i
     const int cap = nb / 4 > 0 ? nb / 4 : 1;          // at least 4 blocks per slice
     if (want > cap) want = cap;
     if (want > nks) nks = want;
-    t.nks = nks;
     t.bpk = (nb + nks - 1) / nks;
     t.nks = (nb + t.bpk - 1) / t.bpk;
     if (t.nks == 1) {
@@ -142,6 +143,45 @@ TPlan tile_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, i
     t.nchunks = (t.n + t.nt - 1) / t.nt * t.nks;
     return t;
 }
+
+// Even split of `tiles` over the grid.
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+TPlan tile_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, int warps) {
+    const int u0 = (int)((long long)cta * tiles / grid);
+    const int n = (int)((long long)(cta + 1) * tiles / grid) - u0;
+    return tile_plan_range(u0, n, nb, tbb, slot_bytes, warps);
+}
+
+// QA phase roles: q CTAs 0 .. nh*S - 1 (head h = cta / S, split cta % S) each
+// compute the hd / kTileRows q tiles of their head; the kv CTAs nh*S ..
+// grid - 1 share the k and v tiles evenly.  Returns the tile range.
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+void qa_tiles(int nh, int hd, int qd, int kvd, int S, int cta, int grid, int* u0, int* n) {
+    const int nq = nh * S, tph = hd / kTileRows;
+    if (cta < nq) {
+        *u0 = (cta / S) * tph;
+        *n = tph;
+        return;
+    }
+    const int kv0 = qd / kTileRows, nkv = 2 * kvd / kTileRows, J = grid - nq, j = cta - nq;
+    *u0 = kv0 + (int)((long long)j * nkv / J);
+    *n = kv0 + (int)((long long)(j + 1) * nkv / J) - *u0;
+}
+
+// Work plans of one CTA, computed on the host at load time (no divisions in
+// the kernel): Wo, gate/up, down, lm_head, then QA for S = 1 .. kMaxSplits.
+constexpr int kPlanSlots = 4 + kMaxSplits;
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+int plan_slot(int kind, int S) { return kind == PH_QA ? 4 + S - 1 : kind - 1; }
 
 struct LayerDev {
     const uint8_t* wqkv;  // tiled [(qd + 2*kvd) rows][H]: Wq rows, then Wk, then Wv
@@ -165,6 +205,7 @@ struct ModelDev {
     int cfloats;              // phase constants: norm gains, QKV bias, RoPE row
     int attn_tile;            // positions per attention tile
     int nbx;                  // 32-blocks of the widest phase input (xq planes)
+    const TPlan* plans;       // [grid][kPlanSlots] work plans (plan_slot)
     int Vp;                   // vocab rows rounded up to kTileRows (tiled lm_head / embedding)
     const uint8_t* tok_embd;  // tiled [V rows][H]
     const uint8_t* lm_head;   // tok_embd when tied
@@ -216,8 +257,10 @@ struct StepArgs {
 //   ybuf   [2][ybuf_floats]       dot results of the phase (parity buffers)
 //   cbuf   [cfloats]              phase constants (norm gains, bias, RoPE)
 //   full, empty [nslots] mbarriers; red [64] floats; misc [32] ints
+//   plan   [kPlanSlots] TPlan     this CTA's work plans (copied at launch)
+//   lay    [L] LayerDev           the layer table (copied at launch)
 struct SmemOffsets {
-    uint32_t xs, xq, xsc, xsm, xres, ybuf, cbuf, full, empty, red, misc, total;
+    uint32_t xs, xq, xsc, xsm, xres, ybuf, cbuf, full, empty, red, misc, plan, lay, total;
 };
 
 // xq holds the phase input as three int8 planes in the operand layout of
@@ -227,7 +270,8 @@ inline
 #ifdef __CUDACC__
 __host__ __device__
 #endif
-SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_floats, int cfloats, int nbx) {
+SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_floats, int cfloats, int nbx,
+                         int nlayers) {
     SmemOffsets o;
     uint32_t p = (uint32_t)nslots * (uint32_t)slot_bytes + 128u;
     o.xs = p;    p += 4u * (uint32_t)xs_floats;
@@ -243,6 +287,10 @@ SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_flo
     o.empty = p; p += 8u * (uint32_t)nslots;
     o.red = p;   p += 4u * 64u;
     o.misc = p;  p += 4u * 32u;
+    o.plan = p;  p += (uint32_t)(kPlanSlots * sizeof(TPlan));
+    p = (p + 15u) & ~15u;
+    o.lay = p;   p += (uint32_t)(nlayers * sizeof(LayerDev));
+    p = (p + 15u) & ~15u;
     o.total = p;
     return o;
 }
@@ -326,6 +374,8 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// all but the most recent committed group
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

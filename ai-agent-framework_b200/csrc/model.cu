@@ -165,12 +165,13 @@ int check_device_status(b2_model* m, std::string* err) {
     return B2_OK;
 }
 
-// Attention context splits per query head: one K/V tile per split while the
-// merge buffer and the grid allow it (more splits = more CTAs working, a
-// shorter critical path); beyond that a split walks several tiles.
-static int splits_for(const b2_model* m, int ctx) {
-    int s = (ctx + m->dev.attn_tile - 1) / m->dev.attn_tile;
-    int cap = std::max(1, std::min(m->max_splits, m->grid / std::max(1, m->dev.nh)));
+// Attention context splits per query head over the `cached` positions before
+// the new one: one K/V tile per split while the merge buffer and the grid
+// allow it (more q CTAs = a shorter critical path); beyond that a split walks
+// several tiles.  The cap keeps CTAs free for the k / v rows.
+static int splits_for(const b2_model* m, int cached) {
+    int s = (cached + m->dev.attn_tile - 1) / m->dev.attn_tile;
+    int cap = std::max(1, std::min(m->max_splits, (m->grid - 1) / std::max(1, m->dev.nh)));
     return std::max(1, std::min(s, cap));
 }
 
@@ -198,7 +199,7 @@ int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err)
         a.epoch = ++m->epoch;
         a.skew = m->wait_skew;
         m->wait_skew = 0;
-        a.splits = splits_for(m, a.pos + 1);
+        a.splits = splits_for(m, a.pos);
         int rc = launch_decode(m->dev, a, m->grid, m->stream, err);
         if (rc) return rc;
     }
@@ -222,7 +223,7 @@ int run_traced_step(b2_model* m, int32_t token, unsigned long long* d_trace, std
     a.p_begin = 0;
     a.p_end = kPhasesPerLayer * m->dev.L + 1;
     a.epoch = ++m->epoch;
-    a.splits = splits_for(m, a.pos + 1);
+    a.splits = splits_for(m, a.pos);
     a.trace = d_trace;
     int rc = launch_decode(m->dev, a, m->grid, m->stream, err);
     if (rc) return rc;
@@ -255,7 +256,7 @@ int run_greedy(b2_model* m, int32_t first, int n_steps, int32_t eos, int32_t* ou
         a.epoch = ++m->epoch;
         a.skew = m->wait_skew;
         m->wait_skew = 0;
-        a.splits = splits_for(m, a.pos + 1);
+        a.splits = splits_for(m, a.pos);
         a.out_ids = m->d_out_ids;
         a.step = i;
         a.eos = eos;
@@ -344,9 +345,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const int nh = c.num_heads, nkv = c.num_kv_heads, hd = c.head_dim;
     const int qd = nh * hd, kvd = nkv * hd;
     if (V <= 0) return bail(B2_ERR_FORMAT, "tokenizer.ggml.tokens missing: vocab size unknown");
-    if (nkv <= 0 || nh % nkv != 0 || hd < 8 || hd > 256 || (hd & (hd - 1)) || H % 32 || FF % 32 || qd % 32)
+    if (nkv <= 0 || nh % nkv != 0 || hd < 16 || hd > 256 || (hd & (hd - 1)) || H % 32 || FF % 32 || qd % 32)
         return bail(B2_ERR_UNSUPPORTED_TYPE,
-                    "unsupported head geometry (need nh % nkv == 0, head_dim a power of two in [8, 256], widths % 32 == 0)");
+                    "unsupported head geometry (need nh % nkv == 0, head_dim a power of two in [16, 256], widths % 32 == 0)");
     if (c.max_seq_len <= 0) return bail(B2_ERR_FORMAT, "context length is zero");
 
     // Tensor checks (transformer.go:1143-1306 reads the same names).
@@ -450,6 +451,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
     m->grid = sms;
 
+    const size_t off_plans = take((size_t)m->grid * kPlanSlots * sizeof(TPlan));
     const size_t off_llx1 = take((size_t)H * 8);
     const size_t off_llx2 = take((size_t)H * 8);
     const size_t off_llqkv = take((size_t)(qd + 2 * kvd) * 8);
@@ -647,14 +649,25 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // attention split partials being merged.
     const int kv_es = o.kv_fp32 ? 4 : 2;
     const int tile = std::max(1, std::min(kMaxAttnTile, kAttnTileBytes / (hd * kv_es)));
-    const int attn_need = 4 * hd + tile + kConsumerWarps * hd + (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
+    // QA phase: the input x (H floats), then a q CTA's attention scratch (q,
+    // output, probabilities, per-warp V sums, one K and one V tile)
+    const int attn_need = ((H + 31) & ~31) + 2 * hd + tile + kConsumerWarps * hd +
+                          (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
     const int base_xs = std::max(std::max(std::max(H, FF), qd), attn_need);
+    // WO stage: the merged outputs, the new position's scores, all split
+    // partials, q and the new k, v
+    auto merge_need = [&](int S) {
+        return qd + ((nh * (kMaxSplits + 1) + 3) & ~3) + ((nh * S * (hd + 2) + 3) & ~3) + qd + 2 * kvd;
+    };
+    // q CTAs (nh per split) must leave at least one CTA for the k / v rows
+    const int split_cap = std::max(1, std::min(kMaxSplits, (m->grid - 1) / nh));
     const int slot = 8192;
     // Outputs one CTA keeps per phase (all K-slices): from the same work plan
-    // the kernel uses, over every CTA.
+    // the kernel uses, over every CTA (and every split count for the QA phase).
     const int qb = tile_qb(qti);
+    const int tbb1 = kTileRows * qb + 2 * kTileRows;
     auto ybuf_need = [&](int rows, int nbk, bool pair) {
-        const int tiles = (int)(tiled_rows(rows) / kTileRows), tbb = (kTileRows * qb + 2 * kTileRows) * (pair ? 2 : 1);
+        const int tiles = (int)(tiled_rows(rows) / kTileRows), tbb = tbb1 * (pair ? 2 : 1);
         int need = 0;
         for (int cta = 0; cta < m->grid; cta++) {
             const TPlan pl = tile_plan(tiles, nbk, tbb, cta, m->grid, slot, kConsumerWarps);
@@ -662,7 +675,16 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         }
         return need;
     };
-    const int ybuf = (std::max(std::max(ybuf_need(qd + 2 * kvd, H / 32, false), ybuf_need(H, qd / 32, false)),
+    int qa_need = 0, qa_rows = 0;
+    for (int S = 1; S <= split_cap; S++)
+        for (int cta = 0; cta < m->grid; cta++) {
+            int u0 = 0, n = 0;
+            qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n);
+            const TPlan pl = tile_plan_range(u0, n, H / 32, tbb1, slot, kConsumerWarps);
+            qa_need = std::max(qa_need, pl.nks * kTileRows * pl.n);
+            qa_rows = std::max(qa_rows, kTileRows * n);
+        }
+    const int ybuf = (std::max(std::max(qa_need, ybuf_need(H, qd / 32, false)),
                                std::max(std::max(ybuf_need(FF, H / 32, true), ybuf_need(H, FF / 32, false)),
                                         ybuf_need(V, H / 32, false))) + 31) & ~31;
     const auto rows_per_cta = [&](int rows) {
@@ -671,23 +693,41 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const int cfloats = cb_floats(H, hd);
     auto ring_slots = [&](int xs_f) {
         int n = 0;
-        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qd), FF) / 32).total <= 232448u) n++;
+        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qd), FF) / 32, L).total <= 232448u) n++;
         return n;
     };
-    const int merge_full = qd + nh * kMaxSplits * (hd + 2);
-    int xs = base_xs, max_splits;
-    if (ring_slots((std::max(base_xs, merge_full) + 31) & ~31) >= 2 * kConsumerWarps) {
-        xs = std::max(base_xs, merge_full);
-        max_splits = kMaxSplits;
+    int xs = base_xs, max_splits = split_cap;
+    if (ring_slots((std::max(base_xs, merge_need(split_cap)) + 31) & ~31) >= 2 * kConsumerWarps) {
+        xs = std::max(base_xs, merge_need(split_cap));
     } else {
-        max_splits = std::max(1, std::min(kMaxSplits, (base_xs - qd) / (nh * (hd + 2))));
+        while (max_splits > 1 && merge_need(max_splits) > base_xs) max_splits--;
+        xs = std::max(base_xs, merge_need(max_splits));
     }
     xs = (xs + 31) & ~31;
     const int ns = ring_slots(xs);
     if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
     if (rows_per_cta(H) > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
-    if (rows_per_cta(qd + 2 * kvd) > kMaxQkvRows)
+    if (qa_rows > kMaxQkvRows || nh >= m->grid)
         return bail(B2_ERR_UNSUPPORTED_TYPE, "attention projection too large for one GPU");
+    // every CTA's work plans (plan_slot order), so the kernel needs no divisions
+    {
+        std::vector<TPlan> plans((size_t)m->grid * kPlanSlots, TPlan{0, 0, 1, 1, 1, 0});
+        const int Vp = (int)tiled_rows(V);
+        for (int cta = 0; cta < m->grid; cta++) {
+            TPlan* pc = plans.data() + (size_t)cta * kPlanSlots;
+            pc[plan_slot(PH_WO, 1)] = tile_plan(H / kTileRows, qd / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_GATEUP, 1)] = tile_plan(FF / kTileRows, H / 32, 2 * tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_DOWN, 1)] = tile_plan(H / kTileRows, FF / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_LMHEAD, 1)] = tile_plan(Vp / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            for (int S = 1; S <= kMaxSplits && nh * S < m->grid; S++) {
+                int u0 = 0, n = 0;
+                qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n);
+                pc[plan_slot(PH_QA, S)] = tile_plan_range(u0, n, H / 32, tbb1, slot, kConsumerWarps);
+            }
+        }
+        cudaMemcpy(A + off_plans, plans.data(), plans.size() * sizeof(TPlan), cudaMemcpyHostToDevice);
+        d.plans = reinterpret_cast<const TPlan*>(A + off_plans);
+    }
     d.xs_floats = xs;
     d.ybuf_floats = ybuf;
     d.cfloats = cfloats;

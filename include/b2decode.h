@@ -191,13 +191,14 @@ int b2_device_status(b2_model* m);
 
 /* Phase timeline of one decode step (profiling): runs `token` at the current
  * position like b2_forward_argmax and records globaltimer stamps (ns) for
- * every phase, slot and CTA into out_ns[phase][12][cta]: slots 0-3 = consumer
+ * every phase, slot and CTA into out_ns[phase][13][cta]: slots 0-3 = consumer
  * wait start, wait done, input staged, work done; 4-5 = producer first and
  * last weight copy issued (0 when the phase has no weights); 6 = total ns the
  * CTA's consumer warps spent waiting for weight chunks, 7 = how many of those
  * waits took longer than 256 ns; 8 = ns the producer waited for free ring
  * slots, 9 = weight chunks it issued; 10 = consumer rows loop done; 11 = total
- * ns the consumer warps spent in tile dot products.  cap is the
+ * ns the consumer warps spent in tile dot products; 12 = epilogue constants
+ * ready.  cap is the
  * capacity of out_ns in elements.  No reference counterpart (the Go engine
  * only logs durations, transformer.go:305-308). */
 int b2_trace_step(b2_model* m, int32_t token, int64_t* out_ns, int64_t cap, int32_t* n_phases, int32_t* n_ctas);
