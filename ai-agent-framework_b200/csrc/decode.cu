@@ -3,33 +3,34 @@
 // Replaces transformer.go:519-739 (forward / transformerLayer / selfAttention /
 // feedForward) and the Q8_0 matvec of transformer.go:810-892 for B = 1.
 //
-// Layout of one CTA (one per SM):
-//   warp 0, lane 0   producer: walks the static schedule of weight chunks
-//                    this CTA owns in every phase of the launch and streams
-//                    them with 1-D TMA bulk copies into a ring of shared-memory
-//                    slots.  Weights never depend on activations, so the
-//                    producer runs ahead across phases, limited by the ring.
+// Per layer four phases: QA (q, k, v rows + attention), WO, GATEUP, DOWN;
+// then the LM head.  Layout of one CTA (one per SM):
+//   warp 0, lanes 0-3 producer: walks the static work plan of every phase of
+//                    the launch (per-CTA plans in shared memory) and streams
+//                    this CTA's chunks of the tiled weights with 1-D TMA bulk
+//                    copies into a ring of shared-memory slots.  Weights never
+//                    depend on activations, so it runs ahead across phases,
+//                    limited by the ring.
 //   warps 1..12      consumers, per phase:
 //                    1. stage: gather the phase input from the previous
-//                       phase's LL words (the poll is the load) into shared
-//                       memory, with RMSNorm / embedding decode / attention
-//                       split merge fused in, and split it into three int8
-//                       planes per 32-element block (x ~ s * (p0 + p1/128 +
-//                       p2/16384), ~21 significant bits); the phase constants
-//                       (norm gains, QKV bias, RoPE row) arrive by cp.async
-//                       during the poll;
+//                       phase's LL words (the poll is the load), multiplied by
+//                       the RMSNorm gain, or decode the embedding row, or
+//                       merge the attention splits, and split it as it
+//                       arrives into three int8 planes per 32-element block
+//                       (x ~ s * (p0 + p1/128 + p2/16384), ~21 significant
+//                       bits); the QKV bias and RoPE row arrive by cp.async;
 //                    2. rows: int8 tensor-core dot products (mma m16n8k32):
-//                       the weight tile (8 rows x 32 K-bytes, straight from
-//                       the ring, no dequantisation) is the B operand, the x
-//                       planes the A operand; the int32 per-block sums are
-//                       scaled by the weight block scale and the x block scale
-//                       and accumulated in fp32, one chunk of tiles per warp;
-//                    3. epilogue, one thread per output: bias + RoPE + KV
-//                       append, SwiGLU, residual add, logits + argmax, and the
-//                       LL stores that hand the outputs to the next phase.
-//                    The attention phase instead runs one (query head,
-//                    context split) per CTA over K/V tiles that cp.async
-//                    copies into shared memory while the CTA polls for q.
+//                       the 16-row weight tile straight from the ring (A
+//                       operand, no dequantisation) times the x planes (B
+//                       operand); the int32 per-block sums are scaled by the
+//                       weight and x block scales and accumulated in fp32;
+//                    3. epilogue, one thread per output: RMSNorm scale, bias +
+//                       RoPE + KV append, SwiGLU, residual add, logits +
+//                       argmax, and the LL stores that hand the outputs on.
+//                    In the QA phase the q CTAs (one per query head and
+//                    context split) then attend over K/V tiles that cp.async
+//                    copied into shared memory during the phase; the last
+//                    split also takes the new position.
 // Each CTA keeps the residual-stream rows it owns (the same rows in every Wo
 // and down phase) in shared memory.  Every wait is bounded (globaltimer) and
 // reports B2_ERR_TIMEOUT through the device error flag instead of hanging.
@@ -204,55 +205,6 @@ struct GatherRes {
     int ok;
 };
 
-// Gathers LL words src[0 .. n) (n even, src 16-byte aligned) once every word
-// carries `tag` and stores value i as float i at shared byte address dst.
-// Each consumer thread polls its own words with 16-byte loads, up to 4 in
-// flight; a word whose tag is stale is simply read again.  Bounded: gives up
-// (ok = 0, error flag set) after kWaitLimitNs or when another CTA already
-// reported an error.  Also returns the sum of squares (for RMSNorm) when asked.
-// Not inlined: its polling state would otherwise add to the register peak of
-// the whole kernel at every one of its call sites.
-__device__ __noinline__ GatherRes ll_gather_s(const uint2* src, int n, unsigned tag, int* err, uint32_t dst,
-                                              int want_ss) {
-    const int ct = threadIdx.x - 32;
-    const int n2 = n >> 1;
-    uint64_t t0 = 0;
-    float ss = 0.0f;
-#pragma unroll 1
-    for (int base = 0; base < n2; base += kConsumerThreads * 4) {
-        uint4 v[4];
-        for (;;) {
-            bool ok = true;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int i = base + ct + k * kConsumerThreads;
-                if (i < n2) {
-                    v[k] = ll_load2(src + 2 * i);
-                    ok &= (v[k].y == tag) & (v[k].w == tag);
-                }
-            }
-            if (ok) break;
-            __nanosleep(64);  // back off: thousands of pollers share these lines
-            const uint64_t now = global_ns();
-            if (t0 == 0) t0 = now;
-            if (now - t0 > kWaitLimitNs) {
-                set_err(err, B2_ERR_TIMEOUT);
-                return GatherRes{ss, 0};
-            }
-            if (*(volatile int*)err) return GatherRes{ss, 0};
-        }
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int i = base + ct + k * kConsumerThreads;
-            if (i < n2) {
-                const float a0 = __uint_as_float(v[k].x), a1 = __uint_as_float(v[k].z);
-                asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(dst + 8u * (uint32_t)i), "f"(a0), "f"(a1) : "memory");
-                if (want_ss) ss += a0 * a0 + a1 * a1;
-            }
-        }
-    }
-    return GatherRes{ss, 1};
-}
 
 // Shared-memory layout of the phase input: element j of lane unit u (US
 // values per unit) lives in float4 column (j % US) / 4; columns are stored
@@ -479,13 +431,18 @@ __device__ __noinline__ void attn_load_tile(const uint8_t* kg, const uint8_t* vg
 // scratch; the first tile's copies were issued before the phase's input
 // poll, so they overlapped the hand-off and the q projection.  Scores: one
 // thread per position; weighted V sum: thread (8-dim chunk vc, group vg) sums
-// over positions vg, vg + ngrp, ...; online softmax across tiles.  Writes
-// the split partial (o unnormalised, m, l) as LL words: the Wo phase merges
-// the splits with the new position's own term.  Not inlined, so its tiles do
-// not raise the kernel's register peak.
+// over positions vg, vg + ngrp, ...; online softmax across tiles.  The last
+// split (`last`) also takes the new position, whose k (after RoPE) and v are
+// the LL words knew[0 .. hd) and knew[kvd .. kvd + hd) that the k / v CTAs
+// publish in this phase (exact fp32, as the reference attends to them).
+// Writes the split partial (o unnormalised, m, l) as LL words for the Wo
+// phase's merge.  Returns 0 if the new position's words never came (error
+// flag set).  Not inlined, so its tiles do not raise the kernel's register
+// peak.
 template <bool F32>
-__device__ __noinline__ void attn_phase(const uint8_t* kg, const uint8_t* vg, uint32_t gs, int hd, int TP, int t0,
-                                        int t1, unsigned tag_out, uint2* out, uint32_t scratch_off, uint32_t red_off) {
+__device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uint32_t gs, int hd, int TP, int t0,
+                                       int t1, unsigned tag_out, uint2* out, uint32_t scratch_off, uint32_t red_off,
+                                       const uint2* knew, int kvd, int last, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int ES = F32 ? 4 : 2;
     const int ct = threadIdx.x - 32, lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 1;
@@ -601,12 +558,50 @@ __device__ __noinline__ void attn_phase(const uint8_t* kg, const uint8_t* vg, ui
         }
         named_bar_sync(1, kConsumerThreads);
     }
+    int ok = 1;
+    if (last) {
+        // the new position: thread ct < hd / 2 holds dims 2ct, 2ct + 1
+        uint4 kw = make_uint4(0u, 0u, 0u, 0u), vw = kw;
+        if (ct < hd / 2) {
+            uint64_t w0 = 0;
+            for (;;) {
+                kw = ll_load2(knew + 2 * ct);
+                vw = ll_load2(knew + kvd + 2 * ct);
+                if ((kw.y == tag_out) & (kw.w == tag_out) & (vw.y == tag_out) & (vw.w == tag_out)) break;
+                const uint64_t now = global_ns();
+                if (w0 == 0) w0 = now;
+                if (now - w0 > kWaitLimitNs) {
+                    set_err(err, B2_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+                if (*(volatile int*)err) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        const float2 qp = ct < hd / 2 ? *reinterpret_cast<const float2*>(am.aq + 2 * ct) : make_float2(0.0f, 0.0f);
+        const float sn = block_sum(fmaf(qp.x, __uint_as_float(kw.x), qp.y * __uint_as_float(kw.z)), red, cw) * scale;
+        const float mnew = fmaxf(mrun, sn);
+        const float corr = (mrun == -INFINITY) ? 0.0f : expf(mrun - mnew);
+        const float pn = expf(sn - mnew);
+        if (ct < hd / 2) {
+            float2* o2 = reinterpret_cast<float2*>(am.ao + 2 * ct);
+            const float2 o = *o2;
+            *o2 = make_float2(fmaf(o.x, corr, pn * __uint_as_float(vw.x)), fmaf(o.y, corr, pn * __uint_as_float(vw.z)));
+        }
+        lrun = fmaf(lrun, corr, pn);
+        mrun = mnew;
+        named_bar_sync(1, kConsumerThreads);
+    }
     // split partial (o unnormalised, m, l); an empty split gives (0, -inf, 0)
 #pragma unroll 1
     for (int i = ct; i < hd + 2; i += kConsumerThreads) {
         const float v = i < hd ? am.ao[i] : (i == hd ? mrun : lrun);
         ll_store(out + i, v, tag_out);
     }
+    return ok;
 }
 
 // mma.m16n8k32 with int32 accumulate: A = 16 weight rows x 32 (s8 for Q8_0,
@@ -850,95 +845,84 @@ __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsig
     return GatherRes{ss, ok ? 1 : 0};
 }
 
-// Splits the staged phase input xs[0 .. 32*nbk) into int8 planes: per
-// 32-block, s = max|x| / 127 and x / s = p0 + p1/128 + p2/16384 (rounded to
-// nearest at each step, |p0| <= 127, |p1|, |p2| <= 64).  Four threads per
-// block, eight elements each; rounding by adding 1.5 * 2^23 (the low byte of
-// the sum is the rounded value as int8).  scale(j, x) is applied to x[j]
-// first (RMSNorm: x[j] * r * gain[j], gains at smem offset g_off; no gains
-// when g_off == 0).  All consumer threads call it (it uses warp shuffles).  Not
-// inlined, so its registers do not add to the kernel's peak.
-__device__ __noinline__ void quantize_planes(uint32_t xs_off, int nbk, uint32_t xq_off, uint32_t xsc_off,
-                                             uint32_t xsm_off, float r, uint32_t g_off, int sums) {
+// The Wo phase input straight into int8 planes: the attention output of
+// every head, merged from its S context-split partials (o unnormalised, m, l;
+// LL words [nh][S][hd + 2]) as transformer.go:664-685 over all positions:
+// o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M), M = max_s m_s (the new
+// position is part of the last split, so the sum is positive).  Each thread
+// merges the 8 outputs of one quarter-block (one head, hd >= 16) two splits
+// per poll, rescaling as the maximum grows, and splits them (planes8).  Polls
+// and fails like gather_planes (every lane reaches every shuffle).  Not
+// inlined (register peak, code size).
+__device__ __noinline__ int merge_planes(const uint2* part, int nbk, int S, int hsh, unsigned tag, int* err,
+                                         uint32_t xq_off, uint32_t xsc_off, uint32_t xsm_off, int sums) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const float* xs = reinterpret_cast<const float*>(smem + xs_off);
     uint8_t* xqb = smem + xq_off;
     float* xsc = reinterpret_cast<float*>(smem + xsc_off);
     int* xsm = reinterpret_cast<int*>(smem + xsm_off);
-    const float* gain = reinterpret_cast<const float*>(smem + g_off);
-    const int ct = threadIdx.x - 32;
-    const float M = kAccMagicF;
+    const int ct = threadIdx.x - 32, hd = 1 << hsh, W2 = hd + 2;
+    bool ok = true;
+    uint64_t t0 = 0;
+#pragma unroll 1
     for (int base = 0; base < 4 * nbk; base += kConsumerThreads) {
         const int i = base + ct;
         const bool on = i < 4 * nbk;
-        const int b = i >> 2, sub = i & 3;
+        const int b = i >> 2, sub = i & 3, j0 = b * 32 + sub * 8;
         float v[8];
-        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = 0.0f;
         if (on) {
-            const float4 x0 = *reinterpret_cast<const float4*>(xs + b * 32 + sub * 8);
-            const float4 x1 = *reinterpret_cast<const float4*>(xs + b * 32 + sub * 8 + 4);
-            v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
-            v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+            const uint2* ph = part + (size_t)(j0 >> hsh) * S * W2 + (j0 & (hd - 1));
+            float M = -INFINITY, L = 0.0f;
+#pragma unroll 1
+            for (int s0 = 0; s0 < S; s0 += 2) {
+                const bool two = s0 + 1 < S;
+                uint4 w[2][5];
+                for (;;) {
+                    bool got = true;
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                if (g_off) v[e] = v[e] * r * gain[b * 32 + sub * 8 + e];
-                amax = fmaxf(amax, fabsf(v[e]));
-            }
-        }
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        // approximate reciprocal (no IEEE division): the planes represent x * inv
-        // against the stored scale amax / 127, a 1-ulp mismatch is 6e-8 relative
-        const float inv = amax > 0.0f ? __fdividef(127.0f, amax) : 0.0f;
-        uint32_t by[3][8];
-        int sg[3] = {0, 0, 0};
+                    for (int u = 0; u < 2; u++) {
+                        const uint2* pp = ph + (size_t)(two ? s0 + u : s0) * W2;
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const float q = on ? v[e] * inv : 0.0f;
-            const float f0 = q + M, r0 = f0 - M;
-            const float q1 = (q - r0) * 128.0f;
-            const float f1 = q1 + M, r1 = f1 - M;
-            const float f2 = (q1 - r1) * 128.0f + M;
-            by[0][e] = __float_as_uint(f0);
-            by[1][e] = __float_as_uint(f1);
-            by[2][e] = __float_as_uint(f2);
-            if (sums) {
-                sg[0] += (int)r0;
-                sg[1] += (int)r1;
-                sg[2] += (int)(f2 - M);
-            }
-        }
-        if (sums) {
+                        for (int k = 0; k < 4; k++) w[u][k] = ll_load2(pp + 2 * k);
+                        w[u][4] = ll_load2(pp - (j0 & (hd - 1)) + hd);  // (m, l)
 #pragma unroll
-            for (int gq = 0; gq < 3; gq++) {
-                sg[gq] += __shfl_xor_sync(0xffffffffu, sg[gq], 1);
-                sg[gq] += __shfl_xor_sync(0xffffffffu, sg[gq], 2);
-            }
-        }
-        if (on) {
-            // elements sub*8 + 0..7: word w = sub / 2 (a0 or a2), lane groups
-            // t0 = (sub & 1) * 2 and t0 + 1, bytes e & 3
-            const int w = sub >> 1, t0 = (sub & 1) * 2;
-            uint32_t* xw = reinterpret_cast<uint32_t*>(xqb + b * 96);
+                        for (int k = 0; k < 5; k++) got &= (w[u][k].y == tag) & (w[u][k].w == tag);
+                    }
+                    if (got || !ok) break;
+                    __nanosleep(64);
+                    const uint64_t now = global_ns();
+                    if (t0 == 0) t0 = now;
+                    if (now - t0 > kWaitLimitNs) {
+                        set_err(err, B2_ERR_TIMEOUT);
+                        ok = false;
+                    } else if (*(volatile int*)err) {
+                        ok = false;
+                    }
+                }
 #pragma unroll
-            for (int gq = 0; gq < 3; gq++) {
-                const uint32_t lo = __byte_perm(__byte_perm(by[gq][0], by[gq][1], 0x0040),
-                                                __byte_perm(by[gq][2], by[gq][3], 0x0040), 0x5410);
-                const uint32_t hi = __byte_perm(__byte_perm(by[gq][4], by[gq][5], 0x0040),
-                                                __byte_perm(by[gq][6], by[gq][7], 0x0040), 0x5410);
-                xw[(gq * 4 + t0) * 2 + w] = lo;
-                xw[(gq * 4 + t0 + 1) * 2 + w] = hi;
-            }
-            if (sub == 0) {
-                xsc[b] = amax * (1.0f / 127.0f);
-                if (sums) {
-                    xsm[b * 3 + 0] = sg[0];
-                    xsm[b * 3 + 1] = sg[1];
-                    xsm[b * 3 + 2] = sg[2];
+                for (int u = 0; u < 2; u++) {
+                    if (u == 1 && !two) break;
+                    const float ms = __uint_as_float(w[u][4].x), ls = __uint_as_float(w[u][4].z);
+                    const float Mn = fmaxf(M, ms);
+                    const float co = M == -INFINITY ? 0.0f : expf(M - Mn);
+                    const float cn = ms == -INFINITY ? 0.0f : expf(ms - Mn);
+                    L = fmaf(L, co, ls * cn);
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        v[2 * k] = fmaf(v[2 * k], co, __uint_as_float(w[u][k].x) * cn);
+                        v[2 * k + 1] = fmaf(v[2 * k + 1], co, __uint_as_float(w[u][k].z) * cn);
+                    }
+                    M = Mn;
                 }
             }
+            const float rl = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] *= rl;
         }
+        planes8(v, on, b, sub, xqb, xsc, xsm, sums != 0);
     }
+    return ok ? 1 : 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -1245,53 +1229,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             ss = warp_sum(ss);
             if (lane == 0) red[32 + cw] = ss;  // summed after the rows barrier
         } else if (g.kind == PH_WO && has_rows) {
-            // Merge the attention of every head: S split partials over the
-            // cached positions plus the new position's own term (score q.k_new,
-            // value v_new), transformer.go:664-685 over all ctx positions:
-            // o = (sum_s o_s e^(m_s - M) + v_new e^(s_new - M)) / (sum_s l_s e^(m_s - M) + e^(s_new - M))
-            const int W2 = hd + 2;
-            float* snew = xs + m.qd;                      // [nh][S + 1] merge weights
-            float* part = snew + ((m.nh * (kMaxSplits + 1) + 3) & ~3);  // [nh][S][hd+2]
-            float* qv = part + ((m.nh * S * W2 + 3) & ~3);  // [qd] q
-            float* kvn = qv + m.qd;                       // [2*kvd] k, v of the new position
-            if (alive) alive = ll_gather_s(m.ll_part, m.nh * S * W2, tag_here, m.err, smem_u32(part), 0).ok;
-            if (alive) alive = ll_gather_s(m.ll_qkv, m.qd + 2 * m.kvd, tag_here, m.err, smem_u32(qv), 0).ok;
+            // the attention of every head, merged from its split partials
+            if (alive)
+                alive = merge_planes(m.ll_part, m.qd / 32, S, __ffs(hd) - 1, tag_here, m.err, so.xq, so.xsc, so.xsm,
+                                     QT != 8) != 0;
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
-            named_bar_sync(1, kConsumerThreads);
-            // per head (one warp): the new position's score, M = the largest of it
-            // and the split maxima, and the weights e^(m - M) / L of every term
-            const float scale = 1.0f / sqrtf((float)hd);
-            #pragma unroll 1
-            for (int hh = cw; hh < m.nh; hh += kConsumerWarps) {
-                const float* qh = qv + (size_t)hh * hd;
-                const float* kh = kvn + (size_t)(hh / (m.nh / m.nkv)) * hd;
-                float d = 0.0f;
-                #pragma unroll 1
-                for (int i = lane; i < hd; i += 32) d = fmaf(qh[i], kh[i], d);
-                d = warp_sum(d) * scale;
-                // lanes 0..S-1 hold split s, lane S the new position
-                const float* ph = part + (size_t)hh * S * W2;
-                const float ms = lane < S ? ph[lane * W2 + hd] : (lane == S ? d : -INFINITY);
-                const float ls = lane < S ? ph[lane * W2 + hd + 1] : (lane == S ? 1.0f : 0.0f);
-                const float M = warp_max(ms);
-                const float w = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-                const float L = warp_sum(ls * w);
-                if (lane <= S) snew[hh * (S + 1) + lane] = w / L;
-            }
-            named_bar_sync(1, kConsumerThreads);
-            const int hsh = __ffs(hd) - 1, grp = m.nh / m.nkv;  // hd is a power of two
-            #pragma unroll 1
-            for (int i = ct; i < m.qd; i += kConsumerThreads) {
-                const int hh = i >> hsh, d = i & (hd - 1);
-                const float* c = snew + hh * (S + 1);
-                const float* ph = part + (size_t)hh * S * W2 + d;
-                float o = kvn[m.kvd + (hh / grp) * hd + d] * c[S];
-                #pragma unroll 1
-                for (int s2 = 0; s2 < S; s2++) o = fmaf(ph[s2 * W2], c[s2], o);
-                xs[i] = o;
-            }
-            named_bar_sync(1, kConsumerThreads);
-            quantize_planes(so.xs, m.qd / 32, so.xq, so.xsc, so.xsm, 1.0f, 0u, QT != 8);
         } else if (g.kind == PH_DOWN && has_rows) {
             if (alive)
                 alive = gather_planes<QT>(m.ll_act, m.FF / 32, tag_here, m.err, 0, 0, m.tok_embd, m.V, m.H, m.Vp, so.xq,
@@ -1409,9 +1351,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             switch (g.kind) {
                 case PH_QA: {
                     // bias (transformer.go:632-646), RoPE on interleaved pairs
-                    // (936-951); q rows stay in this CTA for its attention (split 0
-                    // also publishes them for the Wo merge), k / v rows are published
-                    // and appended to the KV cache (654-656)
+                    // (936-951); q rows stay in this CTA for its attention, k / v rows
+                    // are published (the q CTAs' new position) and appended to the KV
+                    // cache (654-656)
                     const bool bias = layers[g.layer].bqkv != nullptr;
                     const int bias0 = row0 & ~3;
                     float* aq = reinterpret_cast<float*>(smem + attn_off);
@@ -1433,7 +1375,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                         if (row < m.qd) {
                             aq[row - h * hd] = a0;
                             aq[row - h * hd + 1] = a1;
-                            if (sidx == 0) ll_store2(m.ll_qkv + row, a0, a1, tag);
                             continue;
                         }
                         ll_store2(m.ll_qkv + row, a0, a1, tag);
@@ -1519,11 +1460,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             }
         }
         if (qcta) {
-            // 2'. the head's attention over the cached positions (q is in the scratch)
+            // 2'. the head's attention over its split of the positions (q is in the scratch)
             named_bar_sync(1, kConsumerThreads);
             if (alive)
-                attn_phase<KV32>(kg, vg, (uint32_t)(m.kvd * es), hd, TP, at0, at1, tag,
-                                 m.ll_part + ((size_t)h * S + sidx) * (hd + 2), attn_off, so.red);
+                alive = attn_phase<KV32>(kg, vg, (uint32_t)(m.kvd * es), hd, TP, at0, at1, tag,
+                                         m.ll_part + ((size_t)h * S + sidx) * (hd + 2), attn_off, so.red,
+                                         m.ll_qkv + m.qd + (size_t)kvh * hd, m.kvd, sidx == S - 1, m.err) != 0;
             else
                 cp_async_wait();  // the prefetched tile, before the scratch is reused
         }

@@ -643,22 +643,15 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.layers = m->d_layers;
 
     // Shared-memory geometry: the ring of weight slots plus one staging area
-    // (xs) that holds, one phase at a time, the phase input vector, the
-    // attention scratch (q, k/v of the new position, output, probabilities,
-    // per-warp V sums, one K and one V tile), or the Wo input plus all
-    // attention split partials being merged.
+    // (xs) that holds, one phase at a time, the phase input vector (the matvec
+    // mode) or the QA phase's attention scratch (q, output, probabilities,
+    // per-warp V sums, one K and one V tile).
     const int kv_es = o.kv_fp32 ? 4 : 2;
     const int tile = std::max(1, std::min(kMaxAttnTile, kAttnTileBytes / (hd * kv_es)));
-    // QA phase: the input x (H floats), then a q CTA's attention scratch (q,
-    // output, probabilities, per-warp V sums, one K and one V tile)
+    // the scratch sits after H floats (the QA input area)
     const int attn_need = ((H + 31) & ~31) + 2 * hd + tile + kConsumerWarps * hd +
                           (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
     const int base_xs = std::max(std::max(std::max(H, FF), qd), attn_need);
-    // WO stage: the merged outputs, the new position's scores, all split
-    // partials, q and the new k, v
-    auto merge_need = [&](int S) {
-        return qd + ((nh * (kMaxSplits + 1) + 3) & ~3) + ((nh * S * (hd + 2) + 3) & ~3) + qd + 2 * kvd;
-    };
     // q CTAs (nh per split) must leave at least one CTA for the k / v rows
     const int split_cap = std::max(1, std::min(kMaxSplits, (m->grid - 1) / nh));
     const int slot = 8192;
@@ -696,14 +689,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qd), FF) / 32, L).total <= 232448u) n++;
         return n;
     };
-    int xs = base_xs, max_splits = split_cap;
-    if (ring_slots((std::max(base_xs, merge_need(split_cap)) + 31) & ~31) >= 2 * kConsumerWarps) {
-        xs = std::max(base_xs, merge_need(split_cap));
-    } else {
-        while (max_splits > 1 && merge_need(max_splits) > base_xs) max_splits--;
-        xs = std::max(base_xs, merge_need(max_splits));
-    }
-    xs = (xs + 31) & ~31;
+    const int xs = (base_xs + 31) & ~31, max_splits = split_cap;
     const int ns = ring_slots(xs);
     if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
     if (rows_per_cta(H) > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
