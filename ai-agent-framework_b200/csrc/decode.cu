@@ -383,15 +383,13 @@ __device__ __forceinline__ int cb_bias(const ModelDev& m) { return m.H; }
 __device__ __forceinline__ int cb_cos(const ModelDev& m) { return m.H + kMaxQkvRows + 4; }
 __device__ __forceinline__ int cb_sin(const ModelDev& m) { return m.H + kMaxQkvRows + 4 + m.hd / 2; }
 
-// Attention scratch (floats, at smem offset so.xs + 4 * attn_off): q [hd],
-// running output [hd], probabilities [TP], per-warp V sums
-// [kConsumerWarps][hd], then one K tile [TP][hd*ES + 16 bytes] and one V tile
-// [TP][hd*ES].  K rows are padded: no bank conflicts across positions.
+// Attention scratch (at the shared byte offset the QA phase passes): q [hd]
+// floats, the per-warp partials [kConsumerWarps][hd + 2] floats (o, m, l),
+// their merge weights [16] floats, the new position's k and v LL words
+// [2 * hd], then one K tile [TP][hd*ES + 16 bytes] and one V tile [TP][hd*ES].
 struct AttnMap {
     float* aq;
-    float* ao;
-    float* asc;
-    float* avred;
+    float* wpart;
     uint8_t* ktile;
     uint8_t* vtile;
 };
@@ -399,10 +397,8 @@ template <int ES>
 __device__ __forceinline__ AttnMap attn_map(float* base, int hd, int TP) {
     AttnMap r;
     r.aq = base;
-    r.ao = r.aq + hd;
-    r.asc = r.ao + hd;
-    r.avred = r.asc + TP;
-    r.ktile = reinterpret_cast<uint8_t*>(r.avred + kConsumerWarps * hd);
+    r.wpart = r.aq + hd;
+    r.ktile = reinterpret_cast<uint8_t*>(r.wpart + kConsumerWarps * (hd + 2) + 16 + 4 * hd);
     r.vtile = r.ktile + (size_t)TP * (hd * ES + 16);
     return r;
 }
@@ -426,180 +422,202 @@ __device__ __noinline__ void attn_load_tile(const uint8_t* kg, const uint8_t* vg
     cp_async_commit();
 }
 
+// N consecutive K or V elements of one cached row (fp16 or fp32) as floats.
+template <bool F32, int N>
+__device__ __forceinline__ void attn_row(const uint8_t* p, float* f) {
+    if (F32) {
+#pragma unroll
+        for (int e = 0; e < N; e++) f[e] = reinterpret_cast<const float*>(p)[e];
+    } else if (N % 8 == 0) {
+#pragma unroll
+        for (int e = 0; e < N; e += 8) {
+            const uint4 u = *reinterpret_cast<const uint4*>(p + 2 * e);
+            const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float2 a = __half22float2(h[k]);
+                f[e + 2 * k] = a.x;
+                f[e + 2 * k + 1] = a.y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < N; e++) f[e] = __half2float(reinterpret_cast<const __half*>(p)[e]);
+    }
+}
+
 // The attention of one query head over the cached positions [t0, t1) (one
-// context split), transformer.go:658-685.  q (after RoPE) is already in the
-// scratch; the first tile's copies were issued before the phase's input
-// poll, so they overlapped the hand-off and the q projection.  Scores: one
-// thread per position; weighted V sum: thread (8-dim chunk vc, group vg) sums
-// over positions vg, vg + ngrp, ...; online softmax across tiles.  The last
-// split (`last`) also takes the new position, whose k (after RoPE) and v are
-// the LL words knew[0 .. hd) and knew[kvd .. kvd + hd) that the k / v CTAs
-// publish in this phase (exact fp32, as the reference attends to them).
-// Writes the split partial (o unnormalised, m, l) as LL words for the Wo
-// phase's merge.  Returns 0 if the new position's words never came (error
-// flag set).  Not inlined, so its tiles do not raise the kernel's register
-// peak.
-template <bool F32>
-__device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uint32_t gs, int hd, int TP, int t0,
-                                       int t1, unsigned tag_out, uint2* out, uint32_t scratch_off, uint32_t red_off,
-                                       const uint2* knew, int kvd, int last, int* err) {
+// context split), transformer.go:658-685, for head dimension HD.  q (after
+// RoPE) is already in the scratch; the first tile's copies were issued before
+// the phase's input poll, so they overlapped the hand-off and the q
+// projection.  Each warp takes G positions per step: a group of LP lanes per
+// position holds 16 elements of q . k each (reduced over the group); the step
+// updates the warp's running softmax (max and sum over its groups by
+// shuffles), then the lanes switch to head dimensions (DV each) to add the G
+// weighted V rows.  The warps' streams are merged at the end through shared
+// memory.  The last split (`last`) also takes the new position, whose k
+// (after RoPE) and v are the LL words knew[0 .. HD) and knew[kvd .. kvd + HD)
+// that the k / v CTAs publish in this phase (exact fp32, as the reference
+// attends to them); their loads are issued before the tile loop.  Writes the
+// split partial (o unnormalised, m, l) as LL words for the Wo phase's merge.
+// Returns 0 if the new position's words never came (error flag set).  Not
+// inlined, so its registers do not add to the kernel's peak.
+template <bool F32, int HD>
+__device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uint32_t gs, int TP, int t0, int t1,
+                                       unsigned tag_out, uint2* out, uint32_t scratch_off, const uint2* knew, int kvd,
+                                       int last, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int ES = F32 ? 4 : 2;
+    constexpr int DL = 16, LP = HD / DL, G = 32 / LP;          // score lanes per position, positions per step
+    constexpr int DV = HD >= 32 ? HD / 32 : 1, NV = HD / DV;  // V elements per lane, V lanes
     const int ct = threadIdx.x - 32, lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 1;
-    const AttnMap am = attn_map<ES>(reinterpret_cast<float*>(smem + scratch_off), hd, TP);
-    float* red = reinterpret_cast<float*>(smem + red_off);
-    const int rowb = hd * ES, KS = rowb + 16;
+    const AttnMap am = attn_map<ES>(reinterpret_cast<float*>(smem + scratch_off), HD, TP);
+    constexpr int rowb = HD * ES, KS = rowb + 16;
+    const float scale = 1.0f / sqrtf((float)HD);
+    const int grp = lane / LP, d0 = (lane % LP) * DL, vl = lane < NV ? lane : 0;
+    float q[DL], o[DV];
+#pragma unroll
+    for (int k = 0; k < DL; k++) q[k] = am.aq[d0 + k] * scale;
+#pragma unroll
+    for (int e = 0; e < DV; e++) o[e] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+    // the new position's words (last split): copied now (cp.async, through
+    // L2) into the scratch and checked after the tiles
+    const bool nw = last && cw == 0;
+    uint2* kn_s = reinterpret_cast<uint2*>(am.wpart + kConsumerWarps * (HD + 2) + 16);  // [2 * HD] words
+    if (nw) {
 #pragma unroll 1
-    for (int i = ct; i < hd; i += kConsumerThreads) am.ao[i] = 0.0f;
-    cp_async_wait();
+        for (int i = lane; i < HD; i += 32)
+            cp_async16(kn_s + 2 * i, knew + 2 * (i % (HD / 2)) + (i < HD / 2 ? 0 : kvd));
+    }
+    cp_async_commit();
+    cp_async_wait_1();  // the first K/V tile (issued at phase start), not these words
     named_bar_sync(1, kConsumerThreads);
-
-    const float scale = 1.0f / sqrtf((float)hd);
-    const int hv = hd / 8, ngrp = kConsumerThreads / hv;
-    const int vc = ct % hv, vgi = ct / hv;
-    float mrun = -INFINITY, lrun = 0.0f;
 #pragma unroll 1
     for (int tb = t0; tb < t1; tb += TP) {
         const int nt = min(TP, t1 - tb);
         if (tb != t0) {
-            attn_load_tile<F32>(kg, vg, gs, hd, TP, tb, nt, scratch_off);
+            named_bar_sync(1, kConsumerThreads);  // the previous tile is no longer read
+            attn_load_tile<F32>(kg, vg, gs, HD, TP, tb, nt, scratch_off);
             cp_async_wait();
             named_bar_sync(1, kConsumerThreads);
         }
-        // scores (transformer.go:664-671)
-        float sv = -INFINITY;
-        if (ct < nt) {
-            float d0 = 0.0f, d1 = 0.0f;
-            if (F32) {
-                const float4* kr = reinterpret_cast<const float4*>(am.ktile + (size_t)ct * KS);
-                const float4* q4 = reinterpret_cast<const float4*>(am.aq);
 #pragma unroll 1
-                for (int i = 0; i < hd / 4; i++) {
-                    const float4 k = kr[i], q = q4[i];
-                    d0 = fmaf(q.x, k.x, d0);
-                    d1 = fmaf(q.y, k.y, d1);
-                    d0 = fmaf(q.z, k.z, d0);
-                    d1 = fmaf(q.w, k.w, d1);
-                }
-            } else {
-                const uint4* kr = reinterpret_cast<const uint4*>(am.ktile + (size_t)ct * KS);
-                const float4* q4 = reinterpret_cast<const float4*>(am.aq);
-#pragma unroll 1
-                for (int i = 0; i < hd / 8; i++) {
-                    const uint4 ku = kr[i];
-                    const __half2* kh = reinterpret_cast<const __half2*>(&ku);
-                    const float4 qa = q4[2 * i], qb = q4[2 * i + 1];
-                    const float2 f0 = __half22float2(kh[0]), f1 = __half22float2(kh[1]);
-                    const float2 f2 = __half22float2(kh[2]), f3 = __half22float2(kh[3]);
-                    d0 = fmaf(qa.x, f0.x, d0);
-                    d1 = fmaf(qa.y, f0.y, d1);
-                    d0 = fmaf(qa.z, f1.x, d0);
-                    d1 = fmaf(qa.w, f1.y, d1);
-                    d0 = fmaf(qb.x, f2.x, d0);
-                    d1 = fmaf(qb.y, f2.y, d1);
-                    d0 = fmaf(qb.z, f3.x, d0);
-                    d1 = fmaf(qb.w, f3.y, d1);
+        for (int tw = cw * G; tw < nt; tw += kConsumerWarps * G) {  // warp-uniform trip count
+            const int tp = tw + grp;
+            const bool on = tp < nt;
+            float kf[DL];
+            attn_row<F32, DL>(am.ktile + (size_t)(on ? tp : tw) * KS + d0 * ES, kf);
+            float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+            for (int k = 0; k < DL; k += 2) {
+                s0 = fmaf(q[k], kf[k], s0);
+                s1 = fmaf(q[k + 1], kf[k + 1], s1);
+            }
+            float sc = s0 + s1;
+#pragma unroll
+            for (int off = 1; off < LP; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+            sc = on ? sc : -INFINITY;
+            float mx = sc;
+#pragma unroll
+            for (int off = LP; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m, mx);  // finite: position tw is on
+            const float c = __expf(m - mn), pr = __expf(sc - mn);
+            float ps = pr;
+#pragma unroll
+            for (int off = LP; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            l = fmaf(l, c, ps);
+#pragma unroll
+            for (int e = 0; e < DV; e++) o[e] *= c;
+#pragma unroll 4
+            for (int j = 0; j < G; j++) {
+                const float pj = __shfl_sync(0xffffffffu, pr, j * LP);
+                if (tw + j < nt) {
+                    float vf[DV];
+                    attn_row<F32, DV>(am.vtile + (size_t)(tw + j) * rowb + vl * DV * ES, vf);
+#pragma unroll
+                    for (int e = 0; e < DV; e++) o[e] = fmaf(pj, vf[e], o[e]);
                 }
             }
-            sv = (d0 + d1) * scale;
+            m = mn;
         }
-        // online softmax (transformer.go:673-677)
-        const float mb = block_max(sv, red, cw);
-        const float mnew = fmaxf(mrun, mb);
-        const float pv = (ct < nt) ? expf(sv - mnew) : 0.0f;
-        if (ct < nt) am.asc[ct] = pv;
-        const float lb = block_sum(pv, red, cw);  // its barriers also publish asc[]
-        const float corr = (mrun == -INFINITY) ? 0.0f : expf(mrun - mnew);
-        lrun = lrun * corr + lb;
-        mrun = mnew;
-        // weighted V sum (transformer.go:679-685)
-        float acc[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) acc[e] = 0.0f;
-#pragma unroll 1
-        for (int tl = vgi; tl < nt; tl += ngrp) {
-            const float pt = am.asc[tl];
-            float vf[8];
-            if (F32) {
-                const float4* vr = reinterpret_cast<const float4*>(am.vtile + (size_t)tl * rowb + vc * 32);
-                const float4 x0 = vr[0], x1 = vr[1];
-                vf[0] = x0.x; vf[1] = x0.y; vf[2] = x0.z; vf[3] = x0.w;
-                vf[4] = x1.x; vf[5] = x1.y; vf[6] = x1.z; vf[7] = x1.w;
-            } else {
-                const uint4 vu = *reinterpret_cast<const uint4*>(am.vtile + (size_t)tl * rowb + vc * 16);
-                const __half2* vh = reinterpret_cast<const __half2*>(&vu);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float2 f = __half22float2(vh[e]);
-                    vf[2 * e] = f.x;
-                    vf[2 * e + 1] = f.y;
-                }
-            }
-#pragma unroll
-            for (int e = 0; e < 8; e++) acc[e] = fmaf(pt, vf[e], acc[e]);
-        }
-        // lanes of one warp that share a chunk: lane, lane ^ hv, ...
-#pragma unroll 1
-        for (int o = hv; o < 32; o <<= 1) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], o);
-        }
-        if (lane < hv) {
-#pragma unroll
-            for (int e = 0; e < 8; e++) am.avred[cw * hd + lane * 8 + e] = acc[e];
-        }
-        named_bar_sync(1, kConsumerThreads);
-#pragma unroll 1
-        for (int d = ct; d < hd; d += kConsumerThreads) {
-            float o = am.ao[d] * corr;
-#pragma unroll 1
-            for (int w = 0; w < kConsumerWarps; w++) o += am.avred[w * hd + d];
-            am.ao[d] = o;
-        }
-        named_bar_sync(1, kConsumerThreads);
     }
     int ok = 1;
-    if (last) {
-        // the new position: thread ct < hd / 2 holds dims 2ct, 2ct + 1
-        uint4 kw = make_uint4(0u, 0u, 0u, 0u), vw = kw;
-        if (ct < hd / 2) {
-            uint64_t w0 = 0;
-            for (;;) {
-                kw = ll_load2(knew + 2 * ct);
-                vw = ll_load2(knew + kvd + 2 * ct);
-                if ((kw.y == tag_out) & (kw.w == tag_out) & (vw.y == tag_out) & (vw.w == tag_out)) break;
-                const uint64_t now = global_ns();
-                if (w0 == 0) w0 = now;
-                if (now - w0 > kWaitLimitNs) {
-                    set_err(err, B2_ERR_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-                if (*(volatile int*)err) {
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        const float2 qp = ct < hd / 2 ? *reinterpret_cast<const float2*>(am.aq + 2 * ct) : make_float2(0.0f, 0.0f);
-        const float sn = block_sum(fmaf(qp.x, __uint_as_float(kw.x), qp.y * __uint_as_float(kw.z)), red, cw) * scale;
-        const float mnew = fmaxf(mrun, sn);
-        const float corr = (mrun == -INFINITY) ? 0.0f : expf(mrun - mnew);
-        const float pn = expf(sn - mnew);
-        if (ct < hd / 2) {
-            float2* o2 = reinterpret_cast<float2*>(am.ao + 2 * ct);
-            const float2 o = *o2;
-            *o2 = make_float2(fmaf(o.x, corr, pn * __uint_as_float(vw.x)), fmaf(o.y, corr, pn * __uint_as_float(vw.z)));
-        }
-        lrun = fmaf(lrun, corr, pn);
-        mrun = mnew;
-        named_bar_sync(1, kConsumerThreads);
-    }
-    // split partial (o unnormalised, m, l); an empty split gives (0, -inf, 0)
+    if (nw) {
+        // the new position: every lane group holds the same score; stale words
+        // are read again from global memory
+        cp_async_wait();
+        __syncwarp();
+        uint64_t w0 = 0;
+        for (;;) {
+            bool got = true;
 #pragma unroll 1
-    for (int i = ct; i < hd + 2; i += kConsumerThreads) {
-        const float v = i < hd ? am.ao[i] : (i == hd ? mrun : lrun);
-        ll_store(out + i, v, tag_out);
+            for (int i = lane; i < 2 * HD; i += 32) got &= kn_s[i].y == tag_out;
+            if (__all_sync(0xffffffffu, got)) break;
+            const uint64_t now = global_ns();
+            if (w0 == 0) w0 = now;
+            if (now - w0 > kWaitLimitNs) {
+                set_err(err, B2_ERR_TIMEOUT);
+                ok = 0;
+                break;
+            }
+            if (*(volatile int*)err) {
+                ok = 0;
+                break;
+            }
+            __syncwarp();
+            for (int i = lane; i < HD; i += 32) {
+                const uint4 kw = ll_load2(knew + 2 * (i % (HD / 2)) + (i < HD / 2 ? 0 : kvd));
+                kn_s[2 * i] = make_uint2(kw.x, kw.y);
+                kn_s[2 * i + 1] = make_uint2(kw.z, kw.w);
+            }
+            __syncwarp();
+        }
+        float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+        for (int k = 0; k < DL; k += 2) {
+            s0 = fmaf(q[k], __uint_as_float(kn_s[d0 + k].x), s0);
+            s1 = fmaf(q[k + 1], __uint_as_float(kn_s[d0 + k + 1].x), s1);
+        }
+        float sc = s0 + s1;
+#pragma unroll
+        for (int off = 1; off < LP; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+        const float mn = fmaxf(m, sc);
+        const float c = __expf(m - mn), pr = __expf(sc - mn);
+        l = fmaf(l, c, pr);
+#pragma unroll
+        for (int e = 0; e < DV; e++) o[e] = fmaf(o[e], c, pr * __uint_as_float(kn_s[HD + vl * DV + e].x));
+        m = mn;
+    }
+    // publish the warp's stream, then merge the warps: weights e^(m_w - M)
+    // (one thread per warp), then the split partial (o unnormalised, m, l);
+    // an empty split gives (0, -inf, 0)
+    float* wp = am.wpart + cw * (HD + 2);
+    if (lane < NV) {
+#pragma unroll
+        for (int e = 0; e < DV; e++) wp[lane * DV + e] = o[e];
+    }
+    if (lane == 0) {
+        wp[HD] = m;
+        wp[HD + 1] = l;
+    }
+    named_bar_sync(1, kConsumerThreads);
+    float* wc = am.wpart + kConsumerWarps * (HD + 2);  // [kConsumerWarps] weights, then M
+    if (ct < kConsumerWarps) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; w++) mx = fmaxf(mx, am.wpart[w * (HD + 2) + HD]);
+        const float mw = am.wpart[ct * (HD + 2) + HD];
+        wc[ct] = mw == -INFINITY ? 0.0f : __expf(mw - mx);
+        if (ct == 0) wc[kConsumerWarps] = mx;
+    }
+    named_bar_sync(1, kConsumerThreads);
+    if (ct < HD + 2) {
+        const int col = ct == HD ? HD + 1 : ct;  // (the m slot carries M instead)
+        float acc = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; w++) acc = fmaf(am.wpart[w * (HD + 2) + col], wc[w], acc);
+        ll_store(out + ct, ct == HD ? wc[kConsumerWarps] : acc, tag_out);
     }
     return ok;
 }
@@ -1331,17 +1349,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         float rms = 1.0f;  // RMSNorm scale of the norm phases (transformer.go:922-932)
         if (qa || g.kind == PH_GATEUP || g.kind == PH_LMHEAD) {
             float tot = 0.0f;
-            #pragma unroll 1
+            #pragma unroll
             for (int w = 0; w < kConsumerWarps; w++) tot += red[32 + w];
-            // in fp32 (Go rounds a float64 result to float32: within an ulp; a
-            // double-precision sqrt and divide cost ~0.8 us on this path)
-            rms = 1.0f / sqrtf(tot / (float)m.H + m.eps);
+            // in fp32 with the fast divide and reciprocal square root (Go
+            // rounds a float64 result to float32; these are within 2 ulp of
+            // it, and the IEEE forms cost a long dependent chain here)
+            rms = rsqrtf(__fdividef(tot, (float)m.H) + m.eps);
         }
         if (TR && a.trace && ct == 0) a.trace[(tr + 12) * grid + cta] = global_ns();
         const int row0 = kTileRows * pl.u0;
         auto ysum = [&](int i) {
             float v = yb[i];
-            #pragma unroll 1
+            #pragma unroll 4
             for (int ks = 1; ks < pl.nks; ks++) v += yb[ks * rc + i];
             return v;
         };
@@ -1396,7 +1415,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     #pragma unroll 1
                     for (int j = ct; j < kTileRows * pl.n && row0 + j < g.rows; j += kConsumerThreads) {
                         const float gv = ysum(2 * j) * rms, uv = ysum(2 * j + 1) * rms;
-                        ll_store(m.ll_act + row0 + j, gv / (1.0f + expf(-gv)) * uv, tag);
+                        ll_store(m.ll_act + row0 + j, __fdividef(gv, 1.0f + __expf(-gv)) * uv, tag);
                     }
                     break;
                 case PH_WO:
@@ -1462,10 +1481,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         if (qcta) {
             // 2'. the head's attention over its split of the positions (q is in the scratch)
             named_bar_sync(1, kConsumerThreads);
-            if (alive)
-                alive = attn_phase<KV32>(kg, vg, (uint32_t)(m.kvd * es), hd, TP, at0, at1, tag,
-                                         m.ll_part + ((size_t)h * S + sidx) * (hd + 2), attn_off, so.red,
-                                         m.ll_qkv + m.qd + (size_t)kvh * hd, m.kvd, sidx == S - 1, m.err) != 0;
+            if (alive) {
+                uint2* po = m.ll_part + ((size_t)h * S + sidx) * (hd + 2);
+                const uint2* kn = m.ll_qkv + m.qd + (size_t)kvh * hd;
+                const uint32_t gsb = (uint32_t)(m.kvd * es);
+                const int lst = sidx == S - 1;
+                int r;
+                switch (hd) {
+                    case 16: r = attn_phase<KV32, 16>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    case 32: r = attn_phase<KV32, 32>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    case 64: r = attn_phase<KV32, 64>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    case 128: r = attn_phase<KV32, 128>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    default: r = attn_phase<KV32, 256>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                }
+                alive = r != 0;
+            }
             else
                 cp_async_wait();  // the prefetched tile, before the scratch is reused
         }

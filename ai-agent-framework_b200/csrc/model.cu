@@ -644,12 +644,12 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
 
     // Shared-memory geometry: the ring of weight slots plus one staging area
     // (xs) that holds, one phase at a time, the phase input vector (the matvec
-    // mode) or the QA phase's attention scratch (q, output, probabilities,
-    // per-warp V sums, one K and one V tile).
+    // mode) or the QA phase's attention scratch (q, the per-warp partials, one
+    // K and one V tile).
     const int kv_es = o.kv_fp32 ? 4 : 2;
     const int tile = std::max(1, std::min(kMaxAttnTile, kAttnTileBytes / (hd * kv_es)));
     // the scratch sits after H floats (the QA input area)
-    const int attn_need = ((H + 31) & ~31) + 2 * hd + tile + kConsumerWarps * hd +
+    const int attn_need = ((H + 31) & ~31) + hd + kConsumerWarps * (hd + 2) + 16 + 4 * hd +
                           (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
     const int base_xs = std::max(std::max(std::max(H, FF), qd), attn_need);
     // q CTAs (nh per split) must leave at least one CTA for the k / v rows
