@@ -1122,8 +1122,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     bool alive = true;
     const int tok = MV ? 0 : *a.tok;
     // residual rows this CTA owns: its tiles of the H-row phases (Wo, down)
-    const int own0 = kTileRows * (int)((long long)cta * (m.H / kTileRows) / grid);
-    const int own1 = kTileRows * (int)((long long)(cta + 1) * (m.H / kTileRows) / grid);
+    int own_u0 = 0, own_n = 0;
+    own_tiles(m.H / kTileRows, cta, grid, &own_u0, &own_n);
+    const int own0 = kTileRows * own_u0, own1 = own0 + kTileRows * own_n;
     // Consumer barrier that also makes `alive` uniform across the CTA: a
     // failed wait in any thread stops the work of all (warp collectives in
     // the row loop must never run with part of a warp).

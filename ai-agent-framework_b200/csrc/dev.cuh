@@ -155,6 +155,36 @@ TPlan tile_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, i
     return tile_plan_range(u0, n, nb, tbb, slot_bytes, warps);
 }
 
+// The residual-stream rows a CTA owns (the tiles of the H-row phases, Wo
+// and down, and the rows it keeps in shared memory across them).  With no
+// more tiles than CTAs they go to the last CTAs of the grid, one each, so the
+// first CTAs (the QA phase's q CTAs, whose attention ends the QA phase last)
+// own none and the Wo phase does not wait for them twice; otherwise an even
+// split.
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+void own_tiles(int tiles, int cta, int grid, int* u0, int* n) {
+    if (tiles <= grid) {
+        const int first = grid - tiles;
+        *n = cta >= first ? 1 : 0;
+        *u0 = cta >= first ? cta - first : 0;
+        return;
+    }
+    *u0 = (int)((long long)cta * tiles / grid);
+    *n = (int)((long long)(cta + 1) * tiles / grid) - *u0;
+}
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+TPlan own_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, int warps) {
+    int u0 = 0, n = 0;
+    own_tiles(tiles, cta, grid, &u0, &n);
+    return tile_plan_range(u0, n, nb, tbb, slot_bytes, warps);
+}
+
 // QA phase roles: q CTAs 0 .. nh*S - 1 (head h = cta / S, split cta % S) each
 // compute the hd / kTileRows q tiles of their head; the kv CTAs nh*S ..
 // grid - 1 share the k and v tiles evenly.  Returns the tile range.

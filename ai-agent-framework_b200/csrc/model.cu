@@ -659,11 +659,12 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // the kernel uses, over every CTA (and every split count for the QA phase).
     const int qb = tile_qb(qti);
     const int tbb1 = kTileRows * qb + 2 * kTileRows;
-    auto ybuf_need = [&](int rows, int nbk, bool pair) {
+    auto ybuf_need = [&](int rows, int nbk, bool pair, bool own = false) {
         const int tiles = (int)(tiled_rows(rows) / kTileRows), tbb = tbb1 * (pair ? 2 : 1);
         int need = 0;
         for (int cta = 0; cta < m->grid; cta++) {
-            const TPlan pl = tile_plan(tiles, nbk, tbb, cta, m->grid, slot, kConsumerWarps);
+            const TPlan pl = own ? own_plan(tiles, nbk, tbb, cta, m->grid, slot, kConsumerWarps)
+                                 : tile_plan(tiles, nbk, tbb, cta, m->grid, slot, kConsumerWarps);
             need = std::max(need, pl.nks * kTileRows * pl.n * (pair ? 2 : 1));
         }
         return need;
@@ -677,8 +678,8 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             qa_need = std::max(qa_need, pl.nks * kTileRows * pl.n);
             qa_rows = std::max(qa_rows, kTileRows * n);
         }
-    const int ybuf = (std::max(std::max(qa_need, ybuf_need(H, qd / 32, false)),
-                               std::max(std::max(ybuf_need(FF, H / 32, true), ybuf_need(H, FF / 32, false)),
+    const int ybuf = (std::max(std::max(qa_need, ybuf_need(H, qd / 32, false, true)),
+                               std::max(std::max(ybuf_need(FF, H / 32, true), ybuf_need(H, FF / 32, false, true)),
                                         ybuf_need(V, H / 32, false))) + 31) & ~31;
     const auto rows_per_cta = [&](int rows) {
         return kTileRows * (int)((tiled_rows(rows) / kTileRows + m->grid - 1) / m->grid);
@@ -701,9 +702,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         const int Vp = (int)tiled_rows(V);
         for (int cta = 0; cta < m->grid; cta++) {
             TPlan* pc = plans.data() + (size_t)cta * kPlanSlots;
-            pc[plan_slot(PH_WO, 1)] = tile_plan(H / kTileRows, qd / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_WO, 1)] = own_plan(H / kTileRows, qd / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             pc[plan_slot(PH_GATEUP, 1)] = tile_plan(FF / kTileRows, H / 32, 2 * tbb1, cta, m->grid, slot, kConsumerWarps);
-            pc[plan_slot(PH_DOWN, 1)] = tile_plan(H / kTileRows, FF / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_DOWN, 1)] = own_plan(H / kTileRows, FF / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             pc[plan_slot(PH_LMHEAD, 1)] = tile_plan(Vp / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             for (int S = 1; S <= kMaxSplits && nh * S < m->grid; S++) {
                 int u0 = 0, n = 0;
