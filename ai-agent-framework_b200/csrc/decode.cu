@@ -810,6 +810,7 @@ __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsig
     for (int base = 0; base < 4 * nbk; base += kConsumerThreads) {
         const int i = base + ct;
         const bool on = i < 4 * nbk;
+        if (!__any_sync(0xffffffffu, on)) continue;  // (warp-uniform: planes8 shuffles)
         const int b = i >> 2, sub = i & 3, j0 = b * 32 + sub * 8;
         float v[8];
         float4 g0 = make_float4(1.0f, 1.0f, 1.0f, 1.0f), g1 = g0;
@@ -831,7 +832,6 @@ __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsig
                     got &= (w[k].y == tag) & (w[k].w == tag);
                 }
                 if (got || !ok) break;
-                __nanosleep(64);  // back off: thousands of pollers share these lines
                 const uint64_t now = global_ns();
                 if (t0 == 0) t0 = now;
                 if (now - t0 > kWaitLimitNs) {
@@ -885,6 +885,7 @@ __device__ __noinline__ int merge_planes(const uint2* part, int nbk, int S, int 
     for (int base = 0; base < 4 * nbk; base += kConsumerThreads) {
         const int i = base + ct;
         const bool on = i < 4 * nbk;
+        if (!__any_sync(0xffffffffu, on)) continue;  // (warp-uniform: planes8 shuffles)
         const int b = i >> 2, sub = i & 3, j0 = b * 32 + sub * 8;
         float v[8];
 #pragma unroll
@@ -908,7 +909,6 @@ __device__ __noinline__ int merge_planes(const uint2* part, int nbk, int S, int 
                         for (int k = 0; k < 5; k++) got &= (w[u][k].y == tag) & (w[u][k].w == tag);
                     }
                     if (got || !ok) break;
-                    __nanosleep(64);
                     const uint64_t now = global_ns();
                     if (t0 == 0) t0 = now;
                     if (now - t0 > kWaitLimitNs) {
