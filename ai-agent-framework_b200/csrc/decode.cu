@@ -54,14 +54,14 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 // phase geometry
 // ---------------------------------------------------------------------------
 
-// A weight phase of the model: a tiled matrix (plus the up matrix for
-// gate/up), its rows and 32-blocks per row.
+// A weight phase of the model: a tiled matrix, its rows and 32-blocks per
+// row.  The gate/up matrix has 2*FF rows (gate and up interleaved 8 rows at
+// a time: tile t = gate rows 8t .. 8t+7, then up rows 8t .. 8t+7).
 struct TGeom {
     int kind;
     int layer;
     const uint8_t* w;
-    const uint8_t* w2;  // up matrix (PH_GATEUP)
-    int rows;           // real output rows
+    int rows;           // real matrix rows
     int tiles;          // ceil(rows / kTileRows)
     int nb;             // K / 32
 };
@@ -81,23 +81,12 @@ __device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const LayerDev* l
         switch (g.kind) {
             case PH_QA: g.w = L.wqkv; g.rows = m.qd + 2 * m.kvd; g.nb = m.H / 32; break;
             case PH_WO: g.w = L.wo; g.rows = m.H; g.nb = m.qd / 32; break;
-            case PH_GATEUP:
-                g.w = L.wgu;
-                g.w2 = L.wgu + tiled_bytes(m.FF, m.H, m.qtype);
-                g.rows = m.FF;
-                g.nb = m.H / 32;
-                break;
+            case PH_GATEUP: g.w = L.wgu; g.rows = 2 * m.FF; g.nb = m.H / 32; break;
             default: g.w = L.wd; g.rows = m.H; g.nb = m.FF / 32; break;  // PH_DOWN
         }
     }
     g.tiles = (g.rows + kTileRows - 1) / kTileRows;
     return g;
-}
-
-// Bytes of one (tile, block) unit in the ring: 16 rows of quants + 16
-// scales, twice for gate + up.
-__device__ __forceinline__ int tile_unit_bytes(const TGeom& g, int qtype) {
-    return (kTileRows * tile_qb(qtype) + 2 * kTileRows) * (g.w2 ? 2 : 1);
 }
 
 // This CTA's work plan in weight phase g (precomputed on the host).
@@ -1072,13 +1061,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                             const size_t unit0 = (size_t)t0 * g.nb + bb0;
                             const uint32_t qlen = (uint32_t)(ntc * nbc * kTileRows * QB);
                             const uint32_t slen = (uint32_t)(ntc * nbc * 2 * kTileRows);
-                            mbar_arrive_expect_tx(&full[slot], (qlen + slen) * (g.w2 ? 2u : 1u));
+                            mbar_arrive_expect_tx(&full[slot], qlen + slen);
                             bulk_g2s(dst, g.w + unit0 * kTileRows * QB, qlen, &full[slot]);
                             bulk_g2s(dst + qlen, g.w + sreg + unit0 * 2 * kTileRows, slen, &full[slot]);
-                            if (g.w2) {
-                                bulk_g2s(dst + qlen + slen, g.w2 + unit0 * kTileRows * QB, qlen, &full[slot]);
-                                bulk_g2s(dst + 2 * qlen + slen, g.w2 + sreg + unit0 * 2 * kTileRows, slen, &full[slot]);
-                            }
                         }
                     }
                     __syncwarp(0xfu);
@@ -1266,7 +1251,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
 
         float* yb = ybuf + (p & 1) * m.ybuf_floats;  // parity buffers: the next phase's
                                                       // dots may start before this epilogue ends
-        const int rc = kTileRows * pl.n * (g.w2 ? 2 : 1);  // outputs of one K-slice in yb
+        const int rc = kTileRows * pl.n;  // outputs of one K-slice in yb
         {
             // 2. rows: tensor-core dot products of this CTA's tiles into yb
             const uint64_t tl0 = (TR && a.trace) ? global_ns() : 0;
@@ -1302,16 +1287,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                         const float2 y = tile_dot<QT>(smem_u32(smem) + qa, sa, nbc, so.xq, so.xsc, so.xsm, bb0);
                         if (TR && a.trace && lane == 0) atomicAdd(reinterpret_cast<unsigned*>(misc + 22), (unsigned)(global_ns() - td0));
                         const int lr = (lt0 + tl) * kTileRows + (lane >> 2);  // local row of y.x; y.y is lr + 8
-                        if (g.w2) {
-                            const uint32_t o2 = (uint32_t)(qlen + slen);
-                            const float2 u = tile_dot<QT>(smem_u32(smem) + qa + o2, sa + o2, nbc, so.xq, so.xsc, so.xsm, bb0);
-                            if ((lane & 3) == 0) {
-                                yk[2 * lr] = y.x;
-                                yk[2 * lr + 1] = u.x;
-                                yk[2 * (lr + 8)] = y.y;
-                                yk[2 * (lr + 8) + 1] = u.y;
-                            }
-                        } else if ((lane & 3) == 0) {
+                        if ((lane & 3) == 0) {
                             yk[lr] = y.x;
                             yk[lr + 8] = y.y;
                         }
@@ -1412,11 +1388,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     break;
                 }
                 case PH_GATEUP:
-                    // SwiGLU (transformer.go:725-727, 954-956)
+                    // SwiGLU (transformer.go:725-727, 954-956): output j of tile
+                    // t has its gate at row 16t + j % 8 and its up 8 rows below
                     #pragma unroll 1
-                    for (int j = ct; j < kTileRows * pl.n && row0 + j < g.rows; j += kConsumerThreads) {
-                        const float gv = ysum(2 * j) * rms, uv = ysum(2 * j + 1) * rms;
-                        ll_store(m.ll_act + row0 + j, __fdividef(gv, 1.0f + __expf(-gv)) * uv, tag);
+                    for (int j = ct; j < kTileRows / 2 * pl.n; j += kConsumerThreads) {
+                        const int r = (j >> 3) * kTileRows + (j & 7);
+                        const float gv = ysum(r) * rms, uv = ysum(r + 8) * rms;
+                        ll_store(m.ll_act + row0 / 2 + j, __fdividef(gv, 1.0f + __expf(-gv)) * uv, tag);
                     }
                     break;
                 case PH_WO:

@@ -216,7 +216,7 @@ int plan_slot(int kind, int S) { return kind == PH_QA ? 4 + S - 1 : kind - 1; }
 struct LayerDev {
     const uint8_t* wqkv;  // tiled [(qd + 2*kvd) rows][H]: Wq rows, then Wk, then Wv
     const uint8_t* wo;    // tiled [H rows][qd]
-    const uint8_t* wgu;   // tiled [FF rows][H] gate, then tiled [FF rows][H] up
+    const uint8_t* wgu;   // tiled [2*FF rows][H]: gate and up interleaved 8 rows at a time
     const uint8_t* wd;    // tiled [H rows][FF]
     const float* attn_norm;
     const float* ffn_norm;

@@ -59,11 +59,22 @@ struct MatGroup {
     std::vector<std::string> tensors;
     size_t off;
     int64_t rows, cols;
+    int64_t half_rows = 0;  // gate/up: rows of each tensor (8-row interleave)
 };
+
+// Row of the stacked source tensors that row r of a tiled matrix holds.  The
+// gate/up matrix (half_rows = FF) interleaves them 8 rows at a time, so one
+// 16-row tile carries the gate and up rows of the same 8 outputs: tile t =
+// gate rows 8t .. 8t+7, then up rows 8t .. 8t+7 (stacked at FF + ...).
+__host__ __device__ inline int64_t src_row(int64_t r, int64_t half_rows) {
+    if (half_rows == 0) return r;
+    return (r >> 4) * 8 + (r & 7) + ((r & 8) ? half_rows : 0);
+}
 
 // One thread per (row, block) of the padded matrix: ggml block -> tiled
 // quants + scale (padding rows become zero).
-__global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, int64_t rp, int64_t nb, int qtype) {
+__global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, int64_t rp, int64_t nb, int qtype,
+                              int64_t half_rows) {
     const int bpb = qtype == 8 ? 34 : 18, qb = tile_qb(qtype);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rp * nb; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / nb, b = i - r * nb;
@@ -73,7 +84,7 @@ __global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, in
             for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = 0;
             continue;
         }
-        const uint8_t* src = raw + (r * nb + b) * bpb;
+        const uint8_t* src = raw + (src_row(r, half_rows) * nb + b) * bpb;
         sd[0] = src[0];
         sd[1] = src[1];
         for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = src[2 + e];
@@ -96,7 +107,9 @@ __global__ void dequant_kernel(TensorLoc t, float* dst) {
         float v;
         if (t.type == 8 || t.type == 2) {
             const int64_t r = (int64_t)(i / (uint64_t)t.cols), j = (int64_t)(i % (uint64_t)t.cols);
-            v = tiled_elem(static_cast<const uint8_t*>(t.dev), t.row0 + r, j, t.cols / 32, t.rp, (int)t.type);
+            // gate / up halves of the interleaved gate/up matrix (src_row inverse)
+            const int64_t tr = t.half ? (r >> 3) * 16 + (r & 7) + (t.half == 2 ? 8 : 0) : t.row0 + r;
+            v = tiled_elem(static_cast<const uint8_t*>(t.dev), tr, j, t.cols / 32, t.rp, (int)t.type);
         } else {
             v = static_cast<const float*>(t.dev)[i];
         }
@@ -395,7 +408,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         off += up256(bytes + 16);
         return o2;
     };
-    std::vector<MatGroup> groups;
+    std::vector<MatGroup> groups;  // (half_rows: the interleaved gate/up matrix)
     std::vector<std::pair<std::string, size_t>> small;  // f32 vectors: name -> offset
     const int qti = qt == GGML_Q8_0 ? 8 : 2;
     auto take_mat = [&](std::vector<std::string> names, int64_t rows, int64_t cols) {
@@ -414,12 +427,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         const std::string p = "blk." + std::to_string(l) + ".";
         lo[l].qkv = take_mat({p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, qd + 2 * kvd, H);
         lo[l].wo = take_mat({p + "attn_output.weight"}, H, qd);
-        // gate, then up right behind it (the kernel finds up at gate + tiled_bytes)
-        lo[l].gu = off;
-        groups.push_back({{p + "ffn_gate.weight"}, off, FF, H});
-        off += tiled_bytes(FF, H, qti);
-        groups.push_back({{p + "ffn_up.weight"}, off, FF, H});
-        off += up256(tiled_bytes(FF, H, qti) + 16);
+        // gate and up in one matrix of 2*FF rows, interleaved 8 rows at a time
+        lo[l].gu = take(tiled_bytes(2 * FF, H, qti));
+        groups.push_back({{p + "ffn_gate.weight", p + "ffn_up.weight"}, lo[l].gu, 2 * FF, H, FF});
         lo[l].wd = take_mat({p + "ffn_down.weight"}, H, FF);
         lo[l].an = take((size_t)H * 4);
         small.push_back({p + "attn_norm.weight", lo[l].an});
@@ -534,13 +544,15 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             tl.row0 = row0;
             tl.cols = gr.cols;
             tl.rp = tiled_rows(gr.rows);
+            tl.half = gr.half_rows ? (row0 == 0 ? 1 : 2) : 0;
             m->tensors[name] = tl;
             row0 += (int64_t)t->dims[1];
         }
         if (!io_ok) break;
         const int64_t rp = tiled_rows(gr.rows), nbk = gr.cols / 32;
         const int blocks = (int)std::min<int64_t>((rp * nbk + 255) / 256, 148 * 32);
-        repack_kernel<<<blocks, 256, 0, m->stream>>>(static_cast<const uint8_t*>(raw), A + gr.off, gr.rows, rp, nbk, qti);
+        repack_kernel<<<blocks, 256, 0, m->stream>>>(static_cast<const uint8_t*>(raw), A + gr.off, gr.rows, rp, nbk, qti,
+                                                     gr.half_rows);
     }
     cudaStreamSynchronize(m->stream);
     cudaFree(raw);
@@ -659,13 +671,13 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // the kernel uses, over every CTA (and every split count for the QA phase).
     const int qb = tile_qb(qti);
     const int tbb1 = kTileRows * qb + 2 * kTileRows;
-    auto ybuf_need = [&](int rows, int nbk, bool pair, bool own = false) {
-        const int tiles = (int)(tiled_rows(rows) / kTileRows), tbb = tbb1 * (pair ? 2 : 1);
+    auto ybuf_need = [&](int rows, int nbk, bool own) {
+        const int tiles = (int)(tiled_rows(rows) / kTileRows);
         int need = 0;
         for (int cta = 0; cta < m->grid; cta++) {
-            const TPlan pl = own ? own_plan(tiles, nbk, tbb, cta, m->grid, slot, kConsumerWarps)
-                                 : tile_plan(tiles, nbk, tbb, cta, m->grid, slot, kConsumerWarps);
-            need = std::max(need, pl.nks * kTileRows * pl.n * (pair ? 2 : 1));
+            const TPlan pl = own ? own_plan(tiles, nbk, tbb1, cta, m->grid, slot, kConsumerWarps)
+                                 : tile_plan(tiles, nbk, tbb1, cta, m->grid, slot, kConsumerWarps);
+            need = std::max(need, pl.nks * kTileRows * pl.n);
         }
         return need;
     };
@@ -678,8 +690,8 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             qa_need = std::max(qa_need, pl.nks * kTileRows * pl.n);
             qa_rows = std::max(qa_rows, kTileRows * n);
         }
-    const int ybuf = (std::max(std::max(qa_need, ybuf_need(H, qd / 32, false, true)),
-                               std::max(std::max(ybuf_need(FF, H / 32, true), ybuf_need(H, FF / 32, false, true)),
+    const int ybuf = (std::max(std::max(qa_need, ybuf_need(H, qd / 32, true)),
+                               std::max(std::max(ybuf_need(2 * FF, H / 32, false), ybuf_need(H, FF / 32, true)),
                                         ybuf_need(V, H / 32, false))) + 31) & ~31;
     const auto rows_per_cta = [&](int rows) {
         return kTileRows * (int)((tiled_rows(rows) / kTileRows + m->grid - 1) / m->grid);
@@ -703,7 +715,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         for (int cta = 0; cta < m->grid; cta++) {
             TPlan* pc = plans.data() + (size_t)cta * kPlanSlots;
             pc[plan_slot(PH_WO, 1)] = own_plan(H / kTileRows, qd / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
-            pc[plan_slot(PH_GATEUP, 1)] = tile_plan(FF / kTileRows, H / 32, 2 * tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_GATEUP, 1)] = tile_plan(2 * FF / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             pc[plan_slot(PH_DOWN, 1)] = own_plan(H / kTileRows, FF / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             pc[plan_slot(PH_LMHEAD, 1)] = tile_plan(Vp / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             for (int S = 1; S <= kMaxSplits && nh * S < m->grid; S++) {

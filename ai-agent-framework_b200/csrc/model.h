@@ -20,6 +20,7 @@ struct TensorLoc {
     int64_t row0 = 0;        // first row of this tensor in the tiled matrix
     int64_t cols = 0;        // row length (elements)
     int64_t rp = 0;          // rows of the tiled matrix, rounded up to 8
+    int half = 0;            // gate/up matrix: 1 = gate rows, 2 = up rows (8-row interleave)
 };
 
 // PredictStream state (transformer.go:385-442) for the iterator form.
