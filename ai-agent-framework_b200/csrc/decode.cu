@@ -411,27 +411,30 @@ __device__ __noinline__ void attn_load_tile(const uint8_t* kg, const uint8_t* vg
     cp_async_commit();
 }
 
-// N consecutive K or V elements of one cached row (fp16 or fp32) as floats.
+// N (a multiple of 4) consecutive K or V elements of one cached row (fp16 or
+// fp32) as floats.
 template <bool F32, int N>
 __device__ __forceinline__ void attn_row(const uint8_t* p, float* f) {
     if (F32) {
 #pragma unroll
-        for (int e = 0; e < N; e++) f[e] = reinterpret_cast<const float*>(p)[e];
-    } else if (N % 8 == 0) {
-#pragma unroll
-        for (int e = 0; e < N; e += 8) {
-            const uint4 u = *reinterpret_cast<const uint4*>(p + 2 * e);
-            const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float2 a = __half22float2(h[k]);
-                f[e + 2 * k] = a.x;
-                f[e + 2 * k + 1] = a.y;
-            }
+        for (int e = 0; e < N; e += 4) {
+            const float4 x = *reinterpret_cast<const float4*>(p + 4 * e);
+            f[e] = x.x;
+            f[e + 1] = x.y;
+            f[e + 2] = x.z;
+            f[e + 3] = x.w;
         }
     } else {
 #pragma unroll
-        for (int e = 0; e < N; e++) f[e] = __half2float(reinterpret_cast<const __half*>(p)[e]);
+        for (int e = 0; e < N; e += 4) {
+            const uint2 u = *reinterpret_cast<const uint2*>(p + 2 * e);
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            f[e] = a.x;
+            f[e + 1] = a.y;
+            f[e + 2] = b.x;
+            f[e + 3] = b.y;
+        }
     }
 }
 
@@ -439,36 +442,39 @@ __device__ __forceinline__ void attn_row(const uint8_t* p, float* f) {
 // context split), transformer.go:658-685, for head dimension HD.  q (after
 // RoPE) is already in the scratch; the first tile's copies were issued before
 // the phase's input poll, so they overlapped the hand-off and the q
-// projection.  Each warp takes G positions per step: a group of LP lanes per
-// position holds 16 elements of q . k each (reduced over the group); the step
-// updates the warp's running softmax (max and sum over its groups by
-// shuffles), then the lanes switch to head dimensions (DV each) to add the G
-// weighted V rows.  The warps' streams are merged at the end through shared
-// memory.  The last split (`last`) also takes the new position, whose k
-// (after RoPE) and v are the LL words knew[0 .. HD) and knew[kvd .. kvd + HD)
-// that the k / v CTAs publish in this phase (exact fp32, as the reference
-// attends to them); their loads are issued before the tile loop.  Writes the
-// split partial (o unnormalised, m, l) as LL words for the Wo phase's merge.
-// Returns 0 if the new position's words never came (error flag set).  Not
-// inlined, so its registers do not add to the kernel's peak.
-template <bool F32, int HD>
+// projection.  A group of LP = HD / DL lanes takes one position at a time
+// and keeps its own online softmax: each lane holds DL elements of q, of the
+// position's k and v rows and of the running output, so a step needs only
+// the LP-lane reduction of q . k (a warp advances 32 / LP positions per
+// step; DL = 8 measured best for HD 64 and 128: fewer groups to merge at the
+// end than with 16 lanes of 4, shorter steps than with 4 lanes of 16).  The streams are merged at the end, first across the groups of a
+// warp (shuffles), then across warps (shared memory, one barrier).  The last
+// split (`last`) also takes the new position, whose k (after RoPE) and v are
+// the LL words knew[0 .. HD) and knew[kvd .. kvd + HD) that the k / v CTAs
+// publish in this phase (exact fp32, as the reference attends to them); they
+// are copied into the scratch before the tile loop.  Writes the split partial
+// (o unnormalised, m, l) as LL words for the Wo phase's merge.  Returns 0 if
+// the new position's words never came (error flag set).  Not inlined, so its
+// registers do not add to the kernel's peak.
+template <bool F32, int HD, int DL>
 __device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uint32_t gs, int TP, int t0, int t1,
                                        unsigned tag_out, uint2* out, uint32_t scratch_off, const uint2* knew, int kvd,
                                        int last, int* err) {
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int ES = F32 ? 4 : 2;
-    constexpr int DL = 16, LP = HD / DL, G = 32 / LP;          // score lanes per position, positions per step
-    constexpr int DV = HD >= 32 ? HD / 32 : 1, NV = HD / DV;  // V elements per lane, V lanes
+    constexpr int LP = HD / DL, G = 32 / LP;  // lanes per position, positions per step
+    static_assert(LP >= 1 && LP <= 32, "lanes per position");
     const int ct = threadIdx.x - 32, lane = threadIdx.x & 31, cw = (threadIdx.x >> 5) - 1;
     const AttnMap am = attn_map<ES>(reinterpret_cast<float*>(smem + scratch_off), HD, TP);
     constexpr int rowb = HD * ES, KS = rowb + 16;
     const float scale = 1.0f / sqrtf((float)HD);
-    const int grp = lane / LP, d0 = (lane % LP) * DL, vl = lane < NV ? lane : 0;
-    float q[DL], o[DV];
+    const int grp = lane / LP, d0 = (lane % LP) * DL;
+    float q[DL], o[DL];
 #pragma unroll
-    for (int k = 0; k < DL; k++) q[k] = am.aq[d0 + k] * scale;
-#pragma unroll
-    for (int e = 0; e < DV; e++) o[e] = 0.0f;
+    for (int k = 0; k < DL; k++) {
+        q[k] = am.aq[d0 + k] * scale;
+        o[k] = 0.0f;
+    }
     float m = -INFINITY, l = 0.0f;
     // the new position's words (last split): copied now (cp.async, through
     // L2) into the scratch and checked after the tiles
@@ -495,8 +501,10 @@ __device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uin
         for (int tw = cw * G; tw < nt; tw += kConsumerWarps * G) {  // warp-uniform trip count
             const int tp = tw + grp;
             const bool on = tp < nt;
-            float kf[DL];
-            attn_row<F32, DL>(am.ktile + (size_t)(on ? tp : tw) * KS + d0 * ES, kf);
+            const int tr = on ? tp : tw;
+            float kf[DL], vf[DL];
+            attn_row<F32, DL>(am.ktile + (size_t)tr * KS + d0 * ES, kf);
+            attn_row<F32, DL>(am.vtile + (size_t)tr * rowb + d0 * ES, vf);
             float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
             for (int k = 0; k < DL; k += 2) {
@@ -506,35 +514,22 @@ __device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uin
             float sc = s0 + s1;
 #pragma unroll
             for (int off = 1; off < LP; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
-            sc = on ? sc : -INFINITY;
-            float mx = sc;
+            if (on) {
+                // one exponential per position: the larger of (m, sc) keeps weight 1
+                const float e = __expf(-fabsf(sc - m));  // m = -inf: e = 0
+                const bool up = sc > m;
+                const float c = up ? e : 1.0f, pr = up ? 1.0f : e;
+                l = fmaf(l, c, pr);
 #pragma unroll
-            for (int off = LP; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float mn = fmaxf(m, mx);  // finite: position tw is on
-            const float c = __expf(m - mn), pr = __expf(sc - mn);
-            float ps = pr;
-#pragma unroll
-            for (int off = LP; off < 32; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            l = fmaf(l, c, ps);
-#pragma unroll
-            for (int e = 0; e < DV; e++) o[e] *= c;
-#pragma unroll 4
-            for (int j = 0; j < G; j++) {
-                const float pj = __shfl_sync(0xffffffffu, pr, j * LP);
-                if (tw + j < nt) {
-                    float vf[DV];
-                    attn_row<F32, DV>(am.vtile + (size_t)(tw + j) * rowb + vl * DV * ES, vf);
-#pragma unroll
-                    for (int e = 0; e < DV; e++) o[e] = fmaf(pj, vf[e], o[e]);
-                }
+                for (int k = 0; k < DL; k++) o[k] = fmaf(pr, vf[k], o[k] * c);
+                m = up ? sc : m;
             }
-            m = mn;
         }
     }
     int ok = 1;
     if (nw) {
-        // the new position: every lane group holds the same score; stale words
-        // are read again from global memory
+        // the new position, in warp 0's first lane group; stale words are read
+        // again from global memory
         cp_async_wait();
         __syncwarp();
         uint64_t w0 = 0;
@@ -571,24 +566,35 @@ __device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uin
         float sc = s0 + s1;
 #pragma unroll
         for (int off = 1; off < LP; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
-        const float mn = fmaxf(m, sc);
-        const float c = __expf(m - mn), pr = __expf(sc - mn);
-        l = fmaf(l, c, pr);
+        if (grp == 0) {
+            const float e = __expf(-fabsf(sc - m));
+            const bool up = sc > m;
+            const float c = up ? e : 1.0f, pr = up ? 1.0f : e;
+            l = fmaf(l, c, pr);
 #pragma unroll
-        for (int e = 0; e < DV; e++) o[e] = fmaf(o[e], c, pr * __uint_as_float(kn_s[HD + vl * DV + e].x));
-        m = mn;
+            for (int k = 0; k < DL; k++) o[k] = fmaf(pr, __uint_as_float(kn_s[HD + d0 + k].x), o[k] * c);
+            m = up ? sc : m;
+        }
     }
-    // publish the warp's stream, then merge the warps: weights e^(m_w - M)
-    // (one thread per warp), then the split partial (o unnormalised, m, l);
-    // an empty split gives (0, -inf, 0)
+    // merge the lane groups of this warp, then publish the warp's stream
+#pragma unroll
+    for (int off = LP; off < 32; off <<= 1) {
+        const float mo = __shfl_xor_sync(0xffffffffu, m, off), lo = __shfl_xor_sync(0xffffffffu, l, off);
+        const float mx = fmaxf(m, mo);
+        const float c1 = m == -INFINITY ? 0.0f : __expf(m - mx), c2 = mo == -INFINITY ? 0.0f : __expf(mo - mx);
+        l = l * c1 + lo * c2;
+#pragma unroll
+        for (int k = 0; k < DL; k++) o[k] = o[k] * c1 + __shfl_xor_sync(0xffffffffu, o[k], off) * c2;
+        m = mx;
+    }
     float* wp = am.wpart + cw * (HD + 2);
-    if (lane < NV) {
+    if (grp == 0) {
 #pragma unroll
-        for (int e = 0; e < DV; e++) wp[lane * DV + e] = o[e];
-    }
-    if (lane == 0) {
-        wp[HD] = m;
-        wp[HD + 1] = l;
+        for (int k = 0; k < DL; k++) wp[d0 + k] = o[k];
+        if (lane == 0) {
+            wp[HD] = m;
+            wp[HD + 1] = l;
+        }
     }
     named_bar_sync(1, kConsumerThreads);
     float* wc = am.wpart + kConsumerWarps * (HD + 2);  // [kConsumerWarps] weights, then M
@@ -1467,11 +1473,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 const int lst = sidx == S - 1;
                 int r;
                 switch (hd) {
-                    case 16: r = attn_phase<KV32, 16>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
-                    case 32: r = attn_phase<KV32, 32>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
-                    case 64: r = attn_phase<KV32, 64>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
-                    case 128: r = attn_phase<KV32, 128>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
-                    default: r = attn_phase<KV32, 256>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    case 16: r = attn_phase<KV32, 16, 8>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    case 32: r = attn_phase<KV32, 32, 8>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    case 64: r = attn_phase<KV32, 64, 8>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    case 128: r = attn_phase<KV32, 128, 8>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
+                    default: r = attn_phase<KV32, 256, 8>(kg, vg, gsb, TP, at0, at1, tag, po, attn_off, kn, m.kvd, lst, m.err); break;
                 }
                 alive = r != 0;
             }
