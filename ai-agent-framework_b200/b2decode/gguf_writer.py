@@ -257,8 +257,17 @@ def _kv_str_array(b, k, items):
         _s(b, it)
 
 
-def write_model(path: str, shape: ModelShape, seed: int = 0) -> dict:
-    """Writes a GGUF v3 file; returns {"bytes": size, "sha256": digest}."""
+def _tensor_bytes(args) -> bytes:
+    """All quantised bytes of one tensor (a pool worker's unit)."""
+    spec, seed = args
+    return b"".join(quantize(v, spec.gtype).tobytes() for v in tensor_values(spec, seed))
+
+
+def write_model(path: str, shape: ModelShape, seed: int = 0, workers: int = 1) -> dict:
+    """Writes a GGUF v3 file; returns {"bytes": size, "sha256": digest}.
+    workers > 1 generates tensors in a process pool (spawned, so it is safe
+    after CUDA initialisation); the file is identical either way, as every
+    tensor has its own seed."""
     specs = tensor_plan(shape)
     arch = shape.arch
     meta = bytearray()
@@ -313,14 +322,24 @@ def write_model(path: str, shape: ModelShape, seed: int = 0) -> dict:
         pad = (-pos) % ALIGNMENT
         w(b"\0" * pad)
         written = 0
-        for s, off in zip(specs, offsets):
-            if written < off:
-                w(b"\0" * (off - written))
-                written = off
-            for vals in tensor_values(s, seed):
-                buf = quantize(vals, s.gtype).tobytes()
+        pool = None
+        if workers > 1:
+            import multiprocessing as mp
+            pool = mp.get_context("spawn").Pool(workers)
+            chunks = pool.imap(_tensor_bytes, [(sp, seed) for sp in specs])
+        else:
+            chunks = (b"".join(quantize(v, sp.gtype).tobytes() for v in tensor_values(sp, seed)) for sp in specs)
+        try:
+            for off, buf in zip(offsets, chunks):
+                if written < off:
+                    w(b"\0" * (off - written))
+                    written = off
                 w(buf)
                 written += len(buf)
+        finally:
+            if pool is not None:
+                pool.close()
+                pool.join()
         tail = (-written) % ALIGNMENT
         w(b"\0" * tail)
         size = f.tell()

@@ -368,9 +368,9 @@ __device__ __forceinline__ float block_sum(float v, float* red, int cw) {
 }
 
 // Offsets in the constant buffer (floats).
-__device__ __forceinline__ int cb_bias(const ModelDev& m) { return m.H; }
-__device__ __forceinline__ int cb_cos(const ModelDev& m) { return m.H + kMaxQkvRows + 4; }
-__device__ __forceinline__ int cb_sin(const ModelDev& m) { return m.H + kMaxQkvRows + 4 + m.hd / 2; }
+__device__ __forceinline__ int cb_bias(const ModelDev&) { return 0; }
+__device__ __forceinline__ int cb_cos(const ModelDev&) { return kMaxQkvRows + 4; }
+__device__ __forceinline__ int cb_sin(const ModelDev& m) { return kMaxQkvRows + 4 + m.hd / 2; }
 
 // Attention scratch (at the shared byte offset the QA phase passes): q [hd]
 // floats, the per-warp partials [kConsumerWarps][hd + 2] floats (o, m, l),
@@ -949,7 +949,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
     extern __shared__ __align__(128) uint8_t smem[];
     const int NS = m.nslots;
     const int SB = m.slot_bytes;
-    const SmemOffsets so = smem_offsets(NS, SB, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx, MV ? 0 : m.L);
+    const SmemOffsets so = smem_offsets(NS, SB, m.xs_floats, m.ybuf_floats + m.ybuf_odd, m.cfloats, m.nbx, MV ? 0 : m.L);
     uint8_t* ring = smem;
     float* xs = reinterpret_cast<float*>(smem + so.xs);
     uint8_t* xqb = smem + so.xq;
@@ -1191,7 +1191,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         const size_t lay = ((size_t)g.layer * m.max_seq * m.kvd + (size_t)kvh * hd) * es;
         const uint8_t* kg = reinterpret_cast<const uint8_t*>(m.kcache) + lay;
         const uint8_t* vg = reinterpret_cast<const uint8_t*>(m.vcache) + lay;
-        const uint32_t attn_off = so.xs + 4u * (uint32_t)((m.H + 31) & ~31);  // after the QA input
+        const uint32_t attn_off = so.xs;  // the attention scratch
 
         // 1. stage the phase input: gather (+ norm / merge) into xs, then planes
         if (qa && g.layer == 0) {
@@ -1255,7 +1255,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         sync_alive();
         if (TR && a.trace && ct == 0) a.trace[(tr + 2) * grid + cta] = global_ns();
 
-        float* yb = ybuf + (p & 1) * m.ybuf_floats;  // parity buffers: the next phase's
+        float* yb = ybuf + ((p & 1) ? m.ybuf_floats : 0);  // parity buffers: the next phase's
                                                       // dots may start before this epilogue ends
         const int rc = kTileRows * pl.n;  // outputs of one K-slice in yb
         {
@@ -1496,7 +1496,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
 }  // namespace
 
 size_t decode_smem_bytes(const ModelDev& m) {
-    return smem_offsets(m.nslots, m.slot_bytes, m.xs_floats, m.ybuf_floats, m.cfloats, m.nbx, m.plans ? m.L : 0).total;
+    return smem_offsets(m.nslots, m.slot_bytes, m.xs_floats, m.ybuf_floats + m.ybuf_odd, m.cfloats, m.nbx,
+                        m.plans ? m.L : 0).total;
 }
 
 int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err) {

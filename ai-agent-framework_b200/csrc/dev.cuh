@@ -231,7 +231,8 @@ struct ModelDev {
     int kv_fp32;
     int slot_bytes, nslots;   // shared-memory ring geometry
     int xs_floats;            // phase input / attention scratch (floats)
-    int ybuf_floats;          // phase outputs of one CTA, per buffer (two buffers)
+    int ybuf_floats;          // phase outputs of one CTA: even phases' buffer (QA, gate/up, LM head)
+    int ybuf_odd;             // ... and the odd phases' buffer (Wo, down) right after it
     int cfloats;              // phase constants: norm gains, QKV bias, RoPE row
     int attn_tile;            // positions per attention tile
     int nbx;                  // 32-blocks of the widest phase input (xq planes)
@@ -281,10 +282,11 @@ struct StepArgs {
 
 // Dynamic shared-memory layout of the decode kernel (byte offsets).
 //   ring   [nslots][slot_bytes]   weight slots filled by the producer
-//   xs     [xs_floats]            phase input in the dot layout, or the
-//                                 attention scratch (q, k/v tiles, scores)
+//   xs     [xs_floats]            the matvec mode's input vector, or the
+//                                 QA phase's attention scratch
 //   xres   [kMaxOwnRows]          residual rows this CTA owns
-//   ybuf   [2][ybuf_floats]       dot results of the phase (parity buffers)
+//   ybuf   [ybuf_floats]          dot results of the phase (parity buffers,
+//                                 even phases first, then the odd ones)
 //   cbuf   [cfloats]              phase constants (norm gains, bias, RoPE)
 //   full, empty [nslots] mbarriers; red [64] floats; misc [32] ints
 //   plan   [kPlanSlots] TPlan     this CTA's work plans (copied at launch)
@@ -310,7 +312,7 @@ SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_flo
     o.xsm = p;   p += 12u * (uint32_t)nbx;
     p = (p + 15u) & ~15u;
     o.xres = p;  p += 4u * kMaxOwnRows;
-    o.ybuf = p;  p += 8u * (uint32_t)ybuf_floats;
+    o.ybuf = p;  p += 4u * (uint32_t)ybuf_floats;
     o.cbuf = p;  p += 4u * (uint32_t)cfloats;
     p = (p + 15u) & ~15u;
     o.full = p;  p += 8u * (uint32_t)nslots;
@@ -325,10 +327,10 @@ SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_flo
     return o;
 }
 
-// Constant buffer layout (floats): [0, H) norm gains; then the QKV bias of
-// this CTA's rows from row (2 * u0) & ~3 (kMaxQkvRows + 4); then hd/2 cos and
-// hd/2 sin of the RoPE row at the current position.
-inline int cb_floats(int H, int hd) { return (H + kMaxQkvRows + 4 + hd + 31) & ~31; }
+// Constant buffer layout (floats): the QKV bias of this CTA's rows from row
+// (16 * u0) & ~3 (kMaxQkvRows + 4); then hd/2 cos and hd/2 sin of the RoPE
+// row at the current position.
+inline int cb_floats(int hd) { return (kMaxQkvRows + 4 + hd + 31) & ~31; }
 
 #ifdef __CUDACC__
 // ---------------------------------------------------------------------------

@@ -190,12 +190,13 @@ int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows,
     const int rb = cols / 32 * bpb;
     m.xs_floats = (cols + 31) & ~31;
     m.ybuf_floats = ((rows + sc->sms - 1) / sc->sms + 31) & ~31;
+    m.ybuf_odd = m.ybuf_floats;
     m.cfloats = 32;
     m.nbx = 0;
     const int need = rb + 32;
     const int slot = std::max(8192, (need + 1023) & ~1023);
     int ns = 0;
-    while (ns < 32 && smem_offsets(ns + 1, slot, m.xs_floats, m.ybuf_floats, m.cfloats, 0, 0).total <= 232448u) ns++;
+    while (ns < 32 && smem_offsets(ns + 1, slot, m.xs_floats, m.ybuf_floats + m.ybuf_odd, m.cfloats, 0, 0).total <= 232448u) ns++;
     if (ns < 2) {
         *err = "matrix rows too wide for the shared-memory ring";
         return B2_ERR_BAD_ARG;

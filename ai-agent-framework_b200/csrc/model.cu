@@ -654,16 +654,15 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     cudaMemcpy(m->d_layers, m->layers_host.data(), sizeof(LayerDev) * L, cudaMemcpyHostToDevice);
     d.layers = m->d_layers;
 
-    // Shared-memory geometry: the ring of weight slots plus one staging area
-    // (xs) that holds, one phase at a time, the phase input vector (the matvec
-    // mode) or the QA phase's attention scratch (q, the per-warp partials, one
-    // K and one V tile).
+    // Shared-memory geometry: the ring of weight slots plus the QA phase's
+    // attention scratch (xs: q, the per-warp partials and merge weights, the
+    // new position's words, one K and one V tile); the phase inputs go
+    // straight into the int8 planes.
     const int kv_es = o.kv_fp32 ? 4 : 2;
     const int tile = std::max(1, std::min(kMaxAttnTile, kAttnTileBytes / (hd * kv_es)));
-    // the scratch sits after H floats (the QA input area)
-    const int attn_need = ((H + 31) & ~31) + hd + kConsumerWarps * (hd + 2) + 16 + 4 * hd +
+    const int attn_need = hd + kConsumerWarps * (hd + 2) + 16 + 4 * hd +
                           (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
-    const int base_xs = std::max(std::max(std::max(H, FF), qd), attn_need);
+    const int base_xs = attn_need;
     // q CTAs (nh per split) must leave at least one CTA for the k / v rows
     const int split_cap = std::max(1, std::min(kMaxSplits, (m->grid - 1) / nh));
     const int slot = 8192;
@@ -690,13 +689,17 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             qa_need = std::max(qa_need, pl.nks * kTileRows * pl.n);
             qa_rows = std::max(qa_rows, kTileRows * n);
         }
-    const int ybuf = (std::max(std::max(qa_need, ybuf_need(H, qd / 32, true)),
-                               std::max(std::max(ybuf_need(2 * FF, H / 32, false), ybuf_need(H, FF / 32, true)),
-                                        ybuf_need(V, H / 32, false))) + 31) & ~31;
+    // even phases (QA, gate/up, LM head) and odd phases (Wo, down) alternate
+    // between two buffers, so the next phase's dots may start before this
+    // phase's epilogue ends
+    const int ybuf_even = (std::max(std::max(qa_need, ybuf_need(2 * FF, H / 32, false)), ybuf_need(V, H / 32, false)) +
+                           31) & ~31;
+    const int ybuf_odd = (std::max(ybuf_need(H, qd / 32, true), ybuf_need(H, FF / 32, true)) + 31) & ~31;
+    const int ybuf = ybuf_even + ybuf_odd;
     const auto rows_per_cta = [&](int rows) {
         return kTileRows * (int)((tiled_rows(rows) / kTileRows + m->grid - 1) / m->grid);
     };
-    const int cfloats = cb_floats(H, hd);
+    const int cfloats = cb_floats(hd);
     auto ring_slots = [&](int xs_f) {
         int n = 0;
         while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qd), FF) / 32, L).total <= 232448u) n++;
@@ -728,7 +731,8 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         d.plans = reinterpret_cast<const TPlan*>(A + off_plans);
     }
     d.xs_floats = xs;
-    d.ybuf_floats = ybuf;
+    d.ybuf_floats = ybuf_even;
+    d.ybuf_odd = ybuf_odd;
     d.cfloats = cfloats;
     d.attn_tile = tile;
     d.slot_bytes = slot;

@@ -7,6 +7,7 @@ quantised to Q8_0; prompt = BOS + 128 ids uniform over the vocab (seed 0);
 prefill, then greedy decode.  One step = one decode token.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload qwen05b|llama3-8b|matvec|attention]
 
 value: decode tok/s over all ranks, device-timed with CUDA events on the
 engine's stream (inputs resident in HBM).  e2e: the same tok/s through the C
@@ -16,6 +17,18 @@ host memory and the next id read back every step, wall-clock timed.  With
 shard), scaling "weak".  --impl reference times the reference's own CPU
 implementation (its C++ engine compiled from the reference sources into
 oracle/_ref, else the Go restatement in oracle/) on the host cores.
+
+The other workloads (one GPU, one JSON line per case; not the driver's line):
+  llama3-8b  Llama-3-8B-shape Q4_0 greedy decode at batch 1 (hidden 4096, 32
+             layers, 32/8 heads, head_dim 128, FFN 14336, vocab 128256, untied),
+             prompt 512 ids, then K decode tokens;
+  matvec     y = W x through b2_matvec for the Q8_0 and Q4_0 shapes 4096x4096,
+             14336x4096, 4096x14336, 128256x4096 (GGUF block layout, W N(0,0.02),
+             x N(0,1)), batch 1, with >= 256 MB of distinct weight copies rotated
+             so that L2 does not serve repeats;
+  attention  b2_attention_decode, 32 query / 8 KV heads, head_dim 128, fp16 KV
+             N(0,1), contexts 4096 / 16384 / 32768, batch 1 and 8, KV copies
+             rotated past L2 in the same way.
 """
 from __future__ import annotations
 
@@ -144,9 +157,18 @@ def ensure_model(shape_name: str) -> str:
     path = os.path.join(d, f"{shape_name}-s0.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        gw.write_model(tmp, gw.SHAPES[shape_name], seed=0)
+        shape = gw.SHAPES[shape_name]
+        big = shape.hidden * shape.layers > 1 << 16  # multi-GB files: one worker per host core
+        gw.write_model(tmp, shape, seed=0, workers=(os.cpu_count() or 1) if big else 1)
         os.replace(tmp, path)
     return path
+
+
+# The decode workloads: shape, prompt length, description.
+MODELS = {
+    "qwen05b": ("qwen2.5-0.5b", 128, WORKLOAD),
+    "llama3-8b": ("llama3-8b", 512, "llama-3-8b-shape q4_0 greedy decode, batch 1, prompt 512 ids"),
+}
 
 
 def dist_env():
@@ -167,14 +189,15 @@ def profile_traffic(kernel: str):
     return None
 
 
-def cpu_baseline_goref(path: str, seconds: float = 12.0) -> dict:
+def cpu_baseline_goref(path: str, shape_name: str = "qwen2.5-0.5b", seconds: float = 12.0,
+                       prefill: int = 16) -> dict:
     """Decode tok/s of the oracle (the Go engine restated, its worker pool with
     one thread per host core) on a bounded sample of the same workload."""
     import goref
     from b2decode import gguf_writer as gw
-    shape = gw.SHAPES["qwen2.5-0.5b"]
+    shape = gw.SHAPES[shape_name]
     g = goref.GoRef(path, num_ctx=512, n_threads=0)
-    prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, 16, seed=0)]).astype(np.int32)
+    prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, prefill, seed=0)]).astype(np.int32)
     t = int(np.argmax(g.forward(prompt)))
     n, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds and n < 256:
@@ -182,7 +205,7 @@ def cpu_baseline_goref(path: str, seconds: float = 12.0) -> dict:
         n += 1
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": "tok/s", "cores": g.threads, "kind": "port",
-            "sample": f"{n} greedy decode tokens after a 17-token prefill, same synthetic GGUF, "
+            "sample": f"{n} greedy decode tokens after a {len(prompt)}-token prefill, same synthetic GGUF, "
                       f"{dt:.1f} s, goref worker pool with {g.threads} threads"}
 
 
@@ -257,14 +280,15 @@ def run_b200(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    shape = gw.SHAPES["qwen2.5-0.5b"]
+    shape_name, n_prompt, workload = MODELS[args.workload]
+    shape = gw.SHAPES[shape_name]
     if rank == 0 or local == 0:
-        path = ensure_model("qwen2.5-0.5b")
+        path = ensure_model(shape_name)
     barrier()
-    path = ensure_model("qwen2.5-0.5b")
+    path = ensure_model(shape_name)
     K, W = args.steps, args.warmup
     e2e_steps = min(K, 64)
-    prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, 128, seed=0)]).astype(np.int32)
+    prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, n_prompt, seed=0)]).astype(np.int32)
     num_ctx = len(prompt) + W + K + e2e_steps + 8
     m = b2decode.Model(path, num_ctx=num_ctx, device=local)
     stream = torch.cuda.ExternalStream(m.stream_handle())
@@ -316,7 +340,8 @@ def run_b200(args) -> None:
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_baseline_goref(path)
+            cpu = (cpu_baseline_goref(path) if args.workload == "qwen05b"
+                   else cpu_baseline_goref(path, shape_name, seconds=20.0, prefill=0))
         except Exception as exc:  # the baseline must not sink the GPU line
             cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {exc}"}
     if rank == 0:
@@ -324,14 +349,15 @@ def run_b200(args) -> None:
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "weights": "N(0,0.02) quantised Q8_0, seed 0",
+            "config": {"workload": workload, "weights": f"N(0,0.02) quantised {shape.wtype.upper()}, seed 0",
                        "prompt_tokens": int(len(prompt)), "decode_tokens_timed": K,
                        "ctx_range": [int(len(prompt) + W), int(len(prompt) + W + K)],
-                       "l2": "no flush needed: each token streams 525 MB of weights, > 126 MB L2",
+                       "l2": f"no flush needed: each token streams {bytes_tok / 1e6:.0f} MB of weights, > 126 MB L2",
                        "parallelism": f"replicas x{ws}" if ws > 1 else "single gpu",
                        "prefill_s": prefill_s, "kv_cache": "fp16"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": profile_traffic("decode_kernel"),
+                         "frac": achieved / peak,
+                         "traffic": profile_traffic("decode_kernel") if args.workload == "qwen05b" else None,
                          "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
                          "algorithmic_bytes_per_token": bytes_tok, "kv_bytes_per_token": kv_bytes},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
@@ -346,6 +372,100 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
+def _rotations(nbytes: int) -> int:
+    """Distinct copies so that one pass over them exceeds 256 MB (2x the L2)."""
+    return max(1, -(-(256 << 20) // max(nbytes, 1)))
+
+
+def _timed(torch, stream, fn, copies: int, iters: int) -> float:
+    """Mean ms per call of fn(i) over `iters` calls cycling through the copies,
+    CUDA events on `stream` after 3 warm-up passes."""
+    for i in range(3 * copies):
+        fn(i % copies)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(iters):
+        fn(i % copies)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def run_matvec(args) -> None:
+    """Config-1 dequant-matvec microbench through b2_matvec (batch 1)."""
+    import torch
+
+    import b2decode
+    from b2decode import gguf_writer as gw
+    torch.cuda.set_device(0)
+    st = torch.cuda.Stream()
+    peak, peak_kind = peaks()
+    for kind, qt in (("q8_0", 8), ("q4_0", 2)):
+        for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
+            rng = np.random.default_rng(rows * 7 + cols)
+            base = gw.quantize(rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02),
+                               gw.TYPE_NAMES[kind])
+            ncp = _rotations(base.nbytes)
+            w0 = torch.from_numpy(base).cuda()
+            ws = [w0] + [w0.clone() for _ in range(ncp - 1)]
+            x = torch.from_numpy(rng.standard_normal(cols, dtype=np.float32)).cuda()
+            y = torch.empty(rows, device="cuda")
+            with torch.cuda.stream(st):
+                ms = _timed(torch, st, lambda i: b2decode.matvec(qt, ws[i].data_ptr(), x.data_ptr(), y.data_ptr(),
+                                                                 rows, cols, st.cuda_stream),
+                            ncp, max(args.steps, 2 * ncp))
+            nbytes = base.nbytes + 4 * (rows + cols)
+            gbs = nbytes / (ms / 1000.0) / 1e9
+            print(json.dumps({
+                "metric": "dequant-matvec GB/s (B=1)", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+                "higher_is_better": True, "dtype": "fp32", "data": "synthetic",
+                "config": {"workload": f"matvec {kind} {rows}x{cols}, batch 1", "us_per_call": ms * 1000.0,
+                           "weight_bytes": int(base.nbytes), "l2": f"{ncp} weight copies rotated"},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "peak_source": peak_kind},
+            }), flush=True)
+            del ws, w0
+            torch.cuda.empty_cache()
+    print(json.dumps({"metric": "dequant-matvec GB/s (B=8)", "unavailable": "batched matvec (B>1) is not built"}),
+          flush=True)
+
+
+def run_attention(args) -> None:
+    """Config-3 GQA decode attention through b2_attention_decode."""
+    import torch
+
+    import b2decode
+    torch.cuda.set_device(0)
+    st = torch.cuda.Stream()
+    peak, peak_kind = peaks()
+    nh, nkv, hd = 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for ctx in (4096, 16384, 32768):
+        for B in (1, 8):
+            kvbytes = 2 * B * ctx * nkv * hd * 2
+            ncp = _rotations(kvbytes)
+            ks = [torch.randn(B * ctx * nkv * hd, generator=g, device="cuda").half() for _ in range(ncp)]
+            vs = [torch.randn(B * ctx * nkv * hd, generator=g, device="cuda").half() for _ in range(ncp)]
+            q = torch.randn(B * nh * hd, generator=g, device="cuda")
+            out = torch.empty(B * nh * hd, device="cuda")
+            with torch.cuda.stream(st):
+                ms = _timed(torch, st, lambda i: b2decode.attention_decode(
+                    q.data_ptr(), ks[i].data_ptr(), vs[i].data_ptr(), out.data_ptr(), B, nh, nkv, hd, ctx,
+                    st.cuda_stream), ncp, max(args.steps, 2 * ncp))
+            gbs = kvbytes / (ms / 1000.0) / 1e9
+            print(json.dumps({
+                "metric": "GQA decode attention GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+                "higher_is_better": True, "dtype": "fp16 KV, fp32 math", "data": "synthetic",
+                "config": {"workload": f"attention nh {nh} nkv {nkv} hd {hd} ctx {ctx} batch {B}",
+                           "us_per_call": ms * 1000.0, "kv_bytes": kvbytes, "l2": f"{ncp} KV copies rotated"},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "peak_source": peak_kind},
+            }), flush=True)
+            del ks, vs
+            torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -353,11 +473,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="qwen05b", choices=["qwen05b", "llama3-8b", "matvec", "attention"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "matvec":
+        run_matvec(args)
+    elif args.workload == "attention":
+        run_attention(args)
     else:
         run_b200(args)
 
