@@ -263,11 +263,13 @@ def _tensor_bytes(args) -> bytes:
     return b"".join(quantize(v, spec.gtype).tobytes() for v in tensor_values(spec, seed))
 
 
-def write_model(path: str, shape: ModelShape, seed: int = 0, workers: int = 1) -> dict:
+def write_model(path: str, shape: ModelShape, seed: int = 0, workers: int = 1, processes: bool = False) -> dict:
     """Writes a GGUF v3 file; returns {"bytes": size, "sha256": digest}.
-    workers > 1 generates tensors in a process pool (spawned, so it is safe
-    after CUDA initialisation); the file is identical either way, as every
-    tensor has its own seed."""
+    workers > 1 generates tensors in a thread pool (numpy's generator and
+    array loops release the GIL; threads never re-import the caller's
+    script), or with processes=True in a spawned process pool (faster; only
+    from an import-safe main module, as this file's command line is); the
+    file is identical either way, as every tensor has its own seed."""
     specs = tensor_plan(shape)
     arch = shape.arch
     meta = bytearray()
@@ -324,11 +326,16 @@ def write_model(path: str, shape: ModelShape, seed: int = 0, workers: int = 1) -
         written = 0
         pool = None
         if workers > 1:
-            import multiprocessing as mp
-            pool = mp.get_context("spawn").Pool(workers)
-            chunks = pool.imap(_tensor_bytes, [(sp, seed) for sp in specs])
+            from concurrent.futures import ProcessPoolExecutor, ThreadPoolExecutor
+            if processes:
+                import multiprocessing as mp
+                pool = ProcessPoolExecutor(workers, mp_context=mp.get_context("spawn"))
+            else:
+                pool = ThreadPoolExecutor(workers)
+            futs = [pool.submit(_tensor_bytes, (sp, seed)) for sp in specs]
+            chunks = (f.result() for f in futs)
         else:
-            chunks = (b"".join(quantize(v, sp.gtype).tobytes() for v in tensor_values(sp, seed)) for sp in specs)
+            chunks = (_tensor_bytes((sp, seed)) for sp in specs)
         try:
             for off, buf in zip(offsets, chunks):
                 if written < off:
@@ -338,8 +345,7 @@ def write_model(path: str, shape: ModelShape, seed: int = 0, workers: int = 1) -
                 written += len(buf)
         finally:
             if pool is not None:
-                pool.close()
-                pool.join()
+                pool.shutdown(wait=True, cancel_futures=True)
         tail = (-written) % ALIGNMENT
         w(b"\0" * tail)
         size = f.tell()
@@ -364,3 +370,17 @@ def algorithmic_bytes_per_token(shape: ModelShape) -> dict:
     total = shape.layers * (layer + small) + lm + 4 * H
     return {"layers": shape.layers * layer, "lm_head": lm, "small": shape.layers * small + 4 * H,
             "total": total}
+
+
+if __name__ == "__main__":
+    # python -m b2decode.gguf_writer SHAPE OUT [--seed S] [--workers N]
+    import argparse
+    import os
+    ap = argparse.ArgumentParser(description="write a synthetic GGUF of a named shape")
+    ap.add_argument("shape", choices=sorted(SHAPES))
+    ap.add_argument("out")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--workers", type=int, default=os.cpu_count() or 1)
+    a = ap.parse_args()
+    r = write_model(a.out, SHAPES[a.shape], seed=a.seed, workers=a.workers, processes=a.workers > 1)
+    print(r["bytes"], r["sha256"])

@@ -692,9 +692,13 @@ __device__ __noinline__ float2 tile_dot(uint32_t q, uint32_t sc_off, int nbc, ui
             a1 = w1 & 0x0F0F0F0Fu;         // row g + 8
             a2 = (w0 >> 4) & 0x0F0F0F0Fu;  // row g, elements 16+4t .. (high nibbles)
             a3 = (w1 >> 4) & 0x0F0F0F0Fu;
-            // (q - 8) . p = q . p - 8 sum(p), per plane (output column)
-            if (2 * t < 3) c0 -= 8u * (uint32_t)xsm[(xb0 + b) * 3 + 2 * t];
-            if (2 * t + 1 < 3) c1 -= 8u * (uint32_t)xsm[(xb0 + b) * 3 + 2 * t + 1];
+            // (q - 8) . p = q . p - 8 sum(p): the accumulator starts of planes
+            // 2t, 2t + 1 were stored with the planes
+            if (t < 2) {
+                const uint2 cs = *reinterpret_cast<const uint2*>(xsm + (xb0 + b) * 4 + 2 * t);
+                c0 = cs.x;
+                c1 = cs.y;
+            }
         }
         const uint2 bv = lane < 12 ? xq[(xb0 + b) * 12 + lane] : make_uint2(0u, 0u);
         uint32_t d0, d1, d2, d3;
@@ -771,9 +775,10 @@ __device__ __forceinline__ void planes8(const float* v, bool on, int b, int sub,
         if (sub == 0) {
             xsc[b] = amax * (1.0f / 127.0f);
             if (sums) {
-                xsm[b * 3 + 0] = sg[0];
-                xsm[b * 3 + 1] = sg[1];
-                xsm[b * 3 + 2] = sg[2];
+                // Q4_0 accumulator starts: (q - 8) . p = q . p - 8 sum(p)
+                *reinterpret_cast<uint4*>(xsm + b * 4) =
+                    make_uint4(kAccMagic - 8u * (uint32_t)sg[0], kAccMagic - 8u * (uint32_t)sg[1],
+                               kAccMagic - 8u * (uint32_t)sg[2], kAccMagic);
             }
         }
     }
@@ -1353,9 +1358,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             switch (g.kind) {
                 case PH_QA: {
                     // bias (transformer.go:632-646), RoPE on interleaved pairs
-                    // (936-951); q rows stay in this CTA for its attention, k / v rows
-                    // are published (the q CTAs' new position) and appended to the KV
-                    // cache (654-656)
+                    // (936-951); q rows stay in this CTA for its attention (published
+                    // in the distributed form), k / v rows are published (the q CTAs'
+                    // new position) and appended to the KV cache (654-656)
                     const bool bias = layers[g.layer].bqkv != nullptr;
                     const int bias0 = row0 & ~3;
                     float* aq = reinterpret_cast<float*>(smem + attn_off);
@@ -1374,12 +1379,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                             a0 = x0 * rc2 - x1 * rs;
                             a1 = x0 * rs + x1 * rc2;
                         }
-                        if (row < m.qd) {
+                        if (row < m.qd && !m.qa_dist) {
                             aq[row - h * hd] = a0;
                             aq[row - h * hd + 1] = a1;
                             continue;
                         }
                         ll_store2(m.ll_qkv + row, a0, a1, tag);
+                        if (row < m.qd) continue;
                         const bool isk = row < m.qd + m.kvd;
                         const int col = row - m.qd - (isk ? 0 : m.kvd);
                         const size_t off = ((size_t)g.layer * m.max_seq + a.pos) * m.kvd + col;
@@ -1464,8 +1470,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             }
         }
         if (qcta) {
-            // 2'. the head's attention over its split of the positions (q is in the scratch)
-            named_bar_sync(1, kConsumerThreads);
+            // 2'. the head's attention over its split of the positions (q is in the
+            // scratch; the distributed form reads it back from the LL words)
+            if (m.qa_dist && alive && ct < hd / 2) {
+                float* aq = reinterpret_cast<float*>(smem + attn_off);
+                const uint2* src = m.ll_qkv + (size_t)h * hd + 2 * ct;
+                uint64_t w0 = 0;
+                for (;;) {
+                    const uint4 w = ll_load2(src);
+                    if ((w.y == tag) & (w.w == tag)) {
+                        aq[2 * ct] = __uint_as_float(w.x);
+                        aq[2 * ct + 1] = __uint_as_float(w.z);
+                        break;
+                    }
+                    const uint64_t now = global_ns();
+                    if (w0 == 0) w0 = now;
+                    if (now - w0 > kWaitLimitNs) {
+                        set_err(m.err, B2_ERR_TIMEOUT);
+                        alive = false;
+                        break;
+                    }
+                    if (*(volatile int*)m.err) {
+                        alive = false;
+                        break;
+                    }
+                }
+            }
+            sync_alive();
             if (alive) {
                 uint2* po = m.ll_part + ((size_t)h * S + sidx) * (hd + 2);
                 const uint2* kn = m.ll_qkv + m.qd + (size_t)kvh * hd;

@@ -185,15 +185,24 @@ TPlan own_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, in
     return tile_plan_range(u0, n, nb, tbb, slot_bytes, warps);
 }
 
-// QA phase roles: q CTAs 0 .. nh*S - 1 (head h = cta / S, split cta % S) each
-// compute the hd / kTileRows q tiles of their head; the kv CTAs nh*S ..
-// grid - 1 share the k and v tiles evenly.  Returns the tile range.
+// QA phase rows.  Fused form: q CTAs 0 .. nh*S - 1 (head h = cta / S, split
+// cta % S) each compute the hd / kTileRows q tiles of their head and keep
+// them; the kv CTAs nh*S .. grid - 1 share the k and v tiles evenly.
+// Distributed form (`dist`, for heads whose q rows are too much work for one
+// CTA): every CTA takes an even share of all q, k, v tiles and publishes
+// them; the q CTAs then read their head's q back.  Returns the tile range.
 inline
 #ifdef __CUDACC__
 __host__ __device__
 #endif
-void qa_tiles(int nh, int hd, int qd, int kvd, int S, int cta, int grid, int* u0, int* n) {
+void qa_tiles(int nh, int hd, int qd, int kvd, int S, int cta, int grid, int* u0, int* n, int dist) {
     const int nq = nh * S, tph = hd / kTileRows;
+    if (dist) {
+        const int tiles = (qd + 2 * kvd) / kTileRows;
+        *u0 = (int)((long long)cta * tiles / grid);
+        *n = (int)((long long)(cta + 1) * tiles / grid) - *u0;
+        return;
+    }
     if (cta < nq) {
         *u0 = (cta / S) * tph;
         *n = tph;
@@ -235,6 +244,7 @@ struct ModelDev {
     int ybuf_odd;             // ... and the odd phases' buffer (Wo, down) right after it
     int cfloats;              // phase constants: norm gains, QKV bias, RoPE row
     int attn_tile;            // positions per attention tile
+    int qa_dist;              // QA rows spread over all CTAs (q published, read back by the q CTAs)
     int nbx;                  // 32-blocks of the widest phase input (xq planes)
     const TPlan* plans;       // [grid][kPlanSlots] work plans (plan_slot)
     int Vp;                   // vocab rows rounded up to kTileRows (tiled lm_head / embedding)
@@ -297,7 +307,8 @@ struct SmemOffsets {
 
 // xq holds the phase input as three int8 planes in the operand layout of
 // mma.m16n8k32: per 32-element block, 12 lanes x {a0, a2} words (96 bytes);
-// xsc the per-block scales (fp32) and xsm the per-block plane sums (int32 x3).
+// xsc the per-block scales (fp32) and xsm, for Q4_0, the per-block int32
+// accumulator starts of planes 0-2 (1.5 * 2^23 - 8 * plane sum) and 1.5 * 2^23.
 inline
 #ifdef __CUDACC__
 __host__ __device__
@@ -309,7 +320,8 @@ SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_flo
     o.xs = p;    p += 4u * (uint32_t)xs_floats;
     o.xq = p;    p += 96u * (uint32_t)nbx;
     o.xsc = p;   p += 4u * (uint32_t)nbx;
-    o.xsm = p;   p += 12u * (uint32_t)nbx;
+    p = (p + 15u) & ~15u;
+    o.xsm = p;   p += 16u * (uint32_t)nbx;
     p = (p + 15u) & ~15u;
     o.xres = p;  p += 4u * kMaxOwnRows;
     o.ybuf = p;  p += 4u * (uint32_t)ybuf_floats;

@@ -680,11 +680,15 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         }
         return need;
     };
+    // QA rows: fused with the attention (each q CTA computes its head's q) unless
+    // one head's q rows are a large matrix share (> 256 tile-blocks: e.g. head
+    // dim 128 over K = 4096), then spread over all CTAs and handed on
+    const int qa_dist = (hd / kTileRows) * (H / 32) > 256 ? 1 : 0;
     int qa_need = 0, qa_rows = 0;
     for (int S = 1; S <= split_cap; S++)
         for (int cta = 0; cta < m->grid; cta++) {
             int u0 = 0, n = 0;
-            qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n);
+            qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n, qa_dist);
             const TPlan pl = tile_plan_range(u0, n, H / 32, tbb1, slot, kConsumerWarps);
             qa_need = std::max(qa_need, pl.nks * kTileRows * pl.n);
             qa_rows = std::max(qa_rows, kTileRows * n);
@@ -723,7 +727,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             pc[plan_slot(PH_LMHEAD, 1)] = tile_plan(Vp / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             for (int S = 1; S <= kMaxSplits && nh * S < m->grid; S++) {
                 int u0 = 0, n = 0;
-                qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n);
+                qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n, qa_dist);
                 pc[plan_slot(PH_QA, S)] = tile_plan_range(u0, n, H / 32, tbb1, slot, kConsumerWarps);
             }
         }
@@ -735,6 +739,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.ybuf_odd = ybuf_odd;
     d.cfloats = cfloats;
     d.attn_tile = tile;
+    d.qa_dist = qa_dist;
     d.slot_bytes = slot;
     d.nslots = ns;
     m->max_splits = max_splits;

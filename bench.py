@@ -158,8 +158,14 @@ def ensure_model(shape_name: str) -> str:
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
         shape = gw.SHAPES[shape_name]
-        big = shape.hidden * shape.layers > 1 << 16  # multi-GB files: one worker per host core
-        gw.write_model(tmp, shape, seed=0, workers=(os.cpu_count() or 1) if big else 1)
+        if shape.hidden * shape.layers > 1 << 16:
+            # multi-GB files: the writer's own process with one worker per host
+            # core (fork + exec, so safe after CUDA initialisation)
+            env = dict(os.environ, PYTHONPATH=os.path.join(ROOT, "ai-agent-framework_b200"))
+            subprocess.run([sys.executable, "-m", "b2decode.gguf_writer", shape_name, tmp], check=True, env=env,
+                           stdout=subprocess.DEVNULL)
+        else:
+            gw.write_model(tmp, shape, seed=0)
         os.replace(tmp, path)
     return path
 
@@ -196,7 +202,10 @@ def cpu_baseline_goref(path: str, shape_name: str = "qwen2.5-0.5b", seconds: flo
     import goref
     from b2decode import gguf_writer as gw
     shape = gw.SHAPES[shape_name]
-    g = goref.GoRef(path, num_ctx=512, n_threads=0)
+    # Q4_0 models: the oracle's ggml-order Q4_0 (the Go engine reads Q4_0
+    # matrices as Q8_0 rows and cannot run them)
+    mode = goref.MODE_GGML_Q4 if shape.wtype == "q4_0" else goref.MODE_GO
+    g = goref.GoRef(path, num_ctx=512, n_threads=0, mode=mode)
     prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, prefill, seed=0)]).astype(np.int32)
     t = int(np.argmax(g.forward(prompt)))
     n, t0 = 0, time.perf_counter()

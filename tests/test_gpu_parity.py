@@ -265,3 +265,25 @@ def test_qwen05b_shape_parity(built_lib, oracle_lib, write_model):
     want = g.predict(prompt, 12, temperature=0.001)
     got, _ = m.predict(prompt, b2decode.sample_opts(temperature=0.001, num_predict=12))
     assert got.tolist() == want.tolist()
+
+
+@pytest.mark.parametrize("arch,wtype,bias", [("llama", "q4_0", False), ("qwen2", "q8_0", True)])
+def test_wide_heads_distributed_qa(built_lib, oracle_lib, write_model, arch, wtype, bias):
+    """Head dim 128 over hidden 2048: one head's q rows exceed the fused QA
+    phase's share, so the q, k, v rows are spread over all CTAs and each q CTA
+    reads its head's q back; context past one attention tile (64 positions),
+    so several splits.  Teacher-forced logits and greedy ids vs the oracle."""
+    shape = gw.ModelShape(arch, 2048, 2, 16, 4, 1024, 1024, 512, 1e-5, 5e5, bias, not bias, wtype, 1, 2)
+    path = write_model(f"wide-{arch}-{wtype}", shape)
+    m = b2decode.Model(path, num_ctx=256)
+    mode = goref.MODE_GGML_Q4 if wtype == "q4_0" else goref.MODE_GO
+    g = goref.GoRef(path, num_ctx=256, n_threads=0, mode=mode)
+    prompt = gw.make_prompt(shape.vocab, 70, seed=5)
+    toks = np.concatenate([[shape.bos_id], prompt, gw.make_prompt(shape.vocab, 12, seed=6)]).astype(np.int32)
+    pairs = teacher_forced(m.forward, g.forward, toks, 71)
+    errs = [rel_l2(a, b) for a, b in pairs]
+    assert max(errs) < LOGIT_TOL, errs
+    assert np.mean([int(np.argmax(a)) == int(np.argmax(b)) for a, b in pairs]) >= 0.99
+    want = g.predict(prompt, 8, temperature=0.001)
+    got, _ = m.predict(prompt, b2decode.sample_opts(temperature=0.001, num_predict=8))
+    assert got.tolist() == want.tolist()
