@@ -35,8 +35,8 @@ class B2Error(RuntimeError):
 
 
 class LoadOpts(C.Structure):
-    _fields_ = [("num_ctx", C.c_int32), ("device", C.c_int32), ("kv_fp32", C.c_int32), ("reserved0", C.c_int32),
-                ("reserved1", C.c_int32), ("reserved2", C.c_int32)]
+    _fields_ = [("num_ctx", C.c_int32), ("device", C.c_int32), ("kv_fp32", C.c_int32), ("tp_size", C.c_int32),
+                ("tp_rank", C.c_int32), ("reserved2", C.c_int32)]
 
 
 class Config(C.Structure):
@@ -45,7 +45,8 @@ class Config(C.Structure):
                 ("num_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("max_seq_len", C.c_int32),
                 ("rms_norm_eps", C.c_float), ("rope_theta", C.c_float), ("tied_embeddings", C.c_int32),
                 ("has_qkv_bias", C.c_int32), ("weight_type", C.c_int32), ("bos_id", C.c_int32),
-                ("eos_id", C.c_int32), ("weight_bytes", C.c_int64), ("stream_bytes_per_token", C.c_int64)]
+                ("eos_id", C.c_int32), ("weight_bytes", C.c_int64), ("stream_bytes_per_token", C.c_int64),
+                ("tp_size", C.c_int32), ("tp_rank", C.c_int32), ("vocab_begin", C.c_int32), ("vocab_local", C.c_int32)]
 
 
 class Timings(C.Structure):
@@ -101,6 +102,8 @@ SIGNATURES = {
     "b2_stream_handle": (_P, [_P]),
     "b2_trace_step": (C.c_int, [_P, _i32, C.POINTER(_i64), _i64, _i32p, _i32p]),
     "b2_debug_wait_skew": (C.c_int, [_P, _i32]),
+    "b2_tp_handle": (C.c_int, [_P, C.c_char_p]),
+    "b2_tp_connect": (C.c_int, [_P, C.c_char_p]),
 }
 
 
@@ -140,11 +143,14 @@ def sample_opts(temperature=0.0, top_k=0, top_p=0.0, repeat_penalty=1.0, num_pre
 
 
 class Model:
-    """One loaded GGUF model on one GPU (a b2_model handle)."""
+    """One loaded GGUF model on one GPU (a b2_model handle).  With tp_size > 1
+    it is rank tp_rank's share of a tensor-parallel model: connect all ranks
+    (tp.connect) before the first forward call."""
 
-    def __init__(self, path: str, num_ctx: int = 0, device: int = 0, kv_fp32: bool = False):
+    def __init__(self, path: str, num_ctx: int = 0, device: int = 0, kv_fp32: bool = False, tp_size: int = 1,
+                 tp_rank: int = 0):
         L = lib()
-        opts = LoadOpts(int(num_ctx), int(device), 1 if kv_fp32 else 0, 0, 0, 0)
+        opts = LoadOpts(int(num_ctx), int(device), 1 if kv_fp32 else 0, int(tp_size), int(tp_rank), 0)
         h = _P()
         _check(L.b2_load(path.encode(), C.byref(opts), C.byref(h)))
         self._h = h
@@ -153,6 +159,19 @@ class Model:
         self.cfg = {k: getattr(c, k) for k, _ in Config._fields_}
         self.cfg["arch"] = c.arch.decode()
         self.vocab = c.vocab_size
+
+    def tp_handle(self) -> bytes:
+        """64-byte IPC handle of this rank's exchange buffer."""
+        buf = C.create_string_buffer(64)
+        _check(lib().b2_tp_handle(self._h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """Maps every rank's exchange buffer (handles in rank order)."""
+        blob = b"".join(bytes(h) for h in handles)
+        if len(blob) != 64 * len(handles):
+            raise ValueError("handles must be 64 bytes each")
+        _check(lib().b2_tp_connect(self._h, blob))
 
     # engine.go Unload
     def close(self) -> None:
@@ -180,8 +199,10 @@ class Model:
         return n.value
 
     def forward(self, tokens) -> np.ndarray:
+        """Logits of the last token: the whole vocabulary, or this rank's share
+        (cfg vocab_begin .. + vocab_local) of a tensor-parallel model."""
         arr, p = _ids(tokens)
-        out = np.empty(self.vocab, dtype=np.float32)
+        out = np.empty(self.cfg["vocab_local"], dtype=np.float32)
         _check(lib().b2_forward(self._h, p, len(arr), out.ctypes.data_as(_f32p)))
         return out
 

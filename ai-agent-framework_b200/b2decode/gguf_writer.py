@@ -86,6 +86,9 @@ SHAPES = {
     "tiny": ModelShape("qwen2", 128, 2, 4, 2, 256, 512, 256, 1e-6, 1e6, True, True, "q8_0", 1, 2),
     "tiny-llama-q4": ModelShape("llama", 128, 2, 4, 1, 320, 384, 256, 1e-5, 5e5, False, False, "q4_0", 1, 2),
 }
+# The 72B shape cut to 4 layers (a 6.4 GB file instead of 77 GB): per-layer
+# and lm_head costs of the tensor-parallel decode at the real widths.
+SHAPES["qwen2.5-72b-4l"] = SHAPES["qwen2.5-72b"].with_(layers=4)
 
 
 # ---------------------------------------------------------------------------

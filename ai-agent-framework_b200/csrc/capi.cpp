@@ -130,6 +130,10 @@ float uniform01(std::mt19937_64& g) { return (float)((g() >> 40) * (1.0 / 167772
 int sample_from_device(b2_model* m, const b2_sample_opts& o, const std::vector<int32_t>& generated, int32_t* next,
                        std::string* err) {
     const int V = m->cfg.vocab_size;
+    if (m->cfg.tp_size > 1) {
+        *err = "sampling needs the whole vocabulary's logits: greedy only on a tensor-parallel model";
+        return B2_ERR_BAD_ARG;
+    }
     if (!cuda_ok(cudaMemcpyAsync(m->h_logits, m->dev.logits, sizeof(float) * V, cudaMemcpyDeviceToHost, m->stream), err))
         return B2_ERR_CUDA;
     int rc = sync_and_check(m, err);
@@ -194,7 +198,7 @@ int b2_forward(b2_model* m, const int32_t* tokens, int32_t n, float* logits_out)
     int rc = b2::run_tokens(m, tokens, n, &err);
     if (rc) return ret(rc, err);
     if (logits_out) {
-        const int V = m->cfg.vocab_size;
+        const int V = m->cfg.vocab_local;  // the whole vocabulary unless tensor-parallel
         if (!cuda_ok(cudaMemcpyAsync(m->h_logits, m->dev.logits, sizeof(float) * V, cudaMemcpyDeviceToHost, m->stream), &err))
             return ret(B2_ERR_CUDA, err);
         rc = sync_and_check(m, &err);
@@ -458,6 +462,20 @@ int b2_device_status(b2_model* m) {
     std::string err;
     int rc = b2::check_device_status(m, &err);
     return ret(rc, err);
+}
+
+int b2_tp_handle(const b2_model* m, void* handle_out) {
+    if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
+    if (!handle_out) return ret(B2_ERR_BAD_ARG, "null argument");
+    std::string err;
+    return ret(b2::b2_tp_handle_impl(m, handle_out, &err), err);
+}
+
+int b2_tp_connect(b2_model* m, const void* handles) {
+    if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
+    if (!handles) return ret(B2_ERR_BAD_ARG, "null argument");
+    std::string err;
+    return ret(b2::b2_tp_connect_impl(m, handles, &err), err);
 }
 
 }  // extern "C"

@@ -323,7 +323,7 @@ __device__ __forceinline__ float embed_val(const uint8_t* embd, int V, int H, in
 }
 template <int QT>
 __device__ __forceinline__ float embed_elem(const ModelDev& m, int tok, int j) {
-    return embed_val<QT>(m.tok_embd, m.V, m.H, m.Vp, tok, j);
+    return embed_val<QT>(m.tok_embd, m.Vemb, m.H, m.Vp_emb, tok, j);
 }
 
 struct Best {
@@ -1233,7 +1233,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             if (alive) {
                 const GatherRes gr = gather_planes<QT>(g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2, m.H / 32,
                                                        g.kind == PH_GATEUP ? tag_here : tag_prev, m.err,
-                                                       qa && g.layer == 0, tok, m.tok_embd, m.V, m.H, m.Vp,
+                                                       qa && g.layer == 0, tok, m.tok_embd, m.Vemb, m.H, m.Vp_emb,
                                                        so.xq, so.xsc, so.xsm, nw, QT != 8);
                 alive = gr.ok;
                 ss = gr.ss;
@@ -1251,7 +1251,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         } else if (g.kind == PH_DOWN && has_rows) {
             if (alive)
-                alive = gather_planes<QT>(m.ll_act, m.FF / 32, tag_here, m.err, 0, 0, m.tok_embd, m.V, m.H, m.Vp, so.xq,
+                alive = gather_planes<QT>(m.ll_act, m.FF / 32, tag_here, m.err, 0, 0, m.tok_embd, m.Vemb, m.H, m.Vp_emb, so.xq,
                                           so.xsc, so.xsm, nullptr, QT != 8).ok;
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         } else {
@@ -1414,6 +1414,51 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     // residual (transformer.go:576-578, 591-593); the rows are
                     // exactly the residual rows this CTA owns
                     uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
+                    if (m.tp > 1) {
+                        // tensor parallel: this rank's partial sums of these rows go to
+                        // every rank's exchange buffer (peer stores over NVLink), then
+                        // the partials of all ranks are added in rank order, so every
+                        // rank holds the same residual stream
+                        const size_t xo = g.kind == PH_WO ? 0 : xch_dn(m.H, m.tp);
+                        const size_t mine = xo + ((size_t)m.tp_rank * m.H + row0) * 8;
+                        #pragma unroll 1
+                        for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
+                            const float d = ysum(j);
+                            #pragma unroll 1
+                            for (int q = 0; q < m.tp; q++) ll_store_sys(reinterpret_cast<uint2*>(m.xpeer[q] + mine) + j, d, tag);
+                        }
+                        #pragma unroll 1
+                        for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
+                            float xr = xres[j];
+                            #pragma unroll 1
+                            for (int q = 0; q < m.tp && alive; q++) {
+                                const uint2* src = reinterpret_cast<const uint2*>(
+                                    m.xpeer[m.tp_rank] + xo + ((size_t)q * m.H + row0) * 8) + j;
+                                uint64_t w0 = 0;
+                                for (;;) {
+                                    const uint2 w = ll_load_sys(src);
+                                    if (w.y == tag) {
+                                        xr += __uint_as_float(w.x);
+                                        break;
+                                    }
+                                    const uint64_t now = global_ns();
+                                    if (w0 == 0) w0 = now;
+                                    if (now - w0 > kWaitLimitNs) {
+                                        set_err(m.err, B2_ERR_TIMEOUT);
+                                        alive = false;
+                                        break;
+                                    }
+                                    if (*(volatile int*)m.err) {
+                                        alive = false;
+                                        break;
+                                    }
+                                }
+                            }
+                            xres[j] = xr;
+                            ll_store(dstll + row0 + j, xr, tag);
+                        }
+                        break;
+                    }
                     #pragma unroll 1
                     for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
                         const float xr = xres[j] + ysum(j);
@@ -1424,6 +1469,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                 }
                 default: {  // PH_LMHEAD
                     // logits + argmax, first maximum wins (transformer.go:1038-1046)
+                    // (indices are vocab ids: this rank's share starts at v_off)
                     Best best{-INFINITY, 0x7fffffff};
                     #pragma unroll 1
                     for (int j = ct; alive && j < kTileRows * pl.n; j += kConsumerThreads) {
@@ -1431,7 +1477,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                         if (row >= g.rows) break;
                         const float v = ysum(j) * rms;
                         m.logits[row] = v;
-                        if (better(v, row, best.v, best.i)) { best.v = v; best.i = row; }
+                        if (better(v, row + m.v_off, best.v, best.i)) { best.v = v; best.i = row + m.v_off; }
                     }
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
@@ -1457,7 +1503,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                         const unsigned old = atom_acq_rel_add(m.am_ctr, 1u);
                         if (old == (unsigned)(grid - 1)) {
                             // last CTA: every other CTA's max is in am_key
-                            const unsigned long long key = atomicExch(m.am_key, 0ull);
+                            unsigned long long key = atomicExch(m.am_key, 0ull);
+                            if (m.tp > 1) {
+                                // every rank's key to every rank, then the largest of all
+                                // (the same on every rank)
+                                const size_t xa = xch_am(m.H, m.tp);
+                                const uint4 kw = make_uint4((uint32_t)(key >> 32), tag, (uint32_t)key, tag);
+                                for (int q = 0; q < m.tp; q++)
+                                    st4_sys(reinterpret_cast<uint4*>(m.xpeer[q] + xa) + m.tp_rank, kw);
+                                const uint4* mine = reinterpret_cast<const uint4*>(m.xpeer[m.tp_rank] + xa);
+                                for (int q = 0; q < m.tp; q++) {
+                                    uint64_t w0 = 0;
+                                    for (;;) {
+                                        const uint4 w = ld4_sys(mine + q);
+                                        if (w.y == tag && w.w == tag) {
+                                            const unsigned long long kq = ((unsigned long long)w.x << 32) | w.z;
+                                            if (kq > key) key = kq;
+                                            break;
+                                        }
+                                        const uint64_t now = global_ns();
+                                        if (w0 == 0) w0 = now;
+                                        if (now - w0 > kWaitLimitNs || *(volatile int*)m.err) {
+                                            set_err(m.err, B2_ERR_TIMEOUT);
+                                            break;
+                                        }
+                                    }
+                                }
+                            }
                             const int f = key ? (int)~(uint32_t)key : 0;
                             *m.token = f;
                             if (a.out_ids) a.out_ids[a.step] = f;
@@ -1532,6 +1604,11 @@ size_t decode_smem_bytes(const ModelDev& m) {
 }
 
 int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err) {
+    for (int p = 0; p < m.tp && m.tp > 1; p++)
+        if (!m.xpeer[p]) {
+            *err = "tensor-parallel model not connected (b2_tp_connect)";
+            return B2_ERR_BAD_ARG;
+        }
     const size_t smem = decode_smem_bytes(m);
     void* args[] = {(void*)&m, (void*)&a};
     // instantiations: (Q8_0, Q4_0) x (model, matvec) x (plain, traced); the

@@ -29,6 +29,7 @@ constexpr int kPhasesPerLayer = 4;
 constexpr int kConsumerWarps = 12;
 constexpr int kThreads = 32 * (kConsumerWarps + 1);  // warp 0 = producer
 constexpr int kMaxSplits = 8;                         // attention context splits per KV head
+constexpr int kMaxTp = 8;                             // tensor-parallel ranks (GPUs of one box)
 constexpr int kAttnTileBytes = 16384;                 // bytes of cached K (and of V) per attention tile
 constexpr int kMaxAttnTile = 128;                     // positions per attention tile, at most
 constexpr int kMaxOwnRows = 64;                       // residual rows one CTA keeps (H / grid)
@@ -247,9 +248,11 @@ struct ModelDev {
     int qa_dist;              // QA rows spread over all CTAs (q published, read back by the q CTAs)
     int nbx;                  // 32-blocks of the widest phase input (xq planes)
     const TPlan* plans;       // [grid][kPlanSlots] work plans (plan_slot)
-    int Vp;                   // vocab rows rounded up to kTileRows (tiled lm_head / embedding)
-    const uint8_t* tok_embd;  // tiled [V rows][H]
-    const uint8_t* lm_head;   // tok_embd when tied
+    int Vp;                   // lm_head rows (this rank's vocab share) rounded up to kTileRows
+    int Vemb, Vp_emb;         // embedding rows (the whole vocab) and rounded up
+    int v_off;                // first vocab row of this rank's lm_head share
+    const uint8_t* tok_embd;  // tiled [Vemb rows][H]
+    const uint8_t* lm_head;   // tiled [V rows][H] (tok_embd when tied on one GPU)
     const float* out_norm;
     const float* rope_cos;    // [max_seq][hd/2]
     const float* rope_sin;
@@ -261,14 +264,34 @@ struct ModelDev {
     uint2* ll_x2;             // [H]   x after the FFN residual
     uint2* ll_qkv;            // [qd + 2*kvd] q, k (after RoPE), v of the new token
     uint2* ll_part;           // [nh][kMaxSplits][hd + 2] attention split partials (o, m, l)
-    uint2* ll_attn;           // [qd]  attention output when the context is not split
     uint2* ll_act;            // [FF]  SwiGLU output
     float* logits;            // [V]
     unsigned long long* am_key;  // [1] argmax so far: order-preserving value bits << 32 | ~index (self-resetting)
     int* token;               // [1] last argmax
     unsigned* am_ctr;         // [1] argmax arrivals (self-resetting)
     int* err;                 // device error flag (B2_ERR_* codes)
+    // tensor parallelism: this rank's heads, FFN rows and vocab share are the
+    // dims above; the Wo and down partial sums and the argmax keys go through
+    // every rank's exchange buffer (xpeer[tp_rank] is this rank's own)
+    int tp, tp_rank;
+    uint8_t* xpeer[kMaxTp];
 };
+
+// Tensor-parallel exchange buffer (one per rank, the same layout on all;
+// peers map it through CUDA IPC): the Wo and the down partial rows of every
+// rank [tp][H] LL words each, then every rank's LM-head argmax key (16 bytes:
+// order-preserving value bits, tag, ~index, tag).
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+size_t xch_dn(int H, int tp) { return (size_t)tp * H * 8; }
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+size_t xch_am(int H, int tp) { return 2 * (size_t)tp * H * 8; }
+inline size_t xch_bytes(int H, int tp) { return xch_am(H, tp) + 16 * (size_t)tp; }
 
 // Per-launch arguments of the decode kernel.
 struct StepArgs {
@@ -448,6 +471,30 @@ __device__ __forceinline__ void ll_store2(uint2* p, float v0, float v1, unsigned
     asm volatile("st.relaxed.gpu.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(__float_as_uint(v0)), "r"(tag),
                  "r"(__float_as_uint(v1)), "r"(tag)
                  : "memory");
+}
+// System-scope LL words for the tensor-parallel exchange buffers (written by
+// peer GPUs over NVLink, polled by the owner).
+__device__ __forceinline__ void ll_store_sys(uint2* p, float v, unsigned tag) {
+    asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag)
+                 : "memory");
+}
+__device__ __forceinline__ uint2 ll_load_sys(const uint2* p) {
+    uint2 r;
+    asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+    return r;
+}
+__device__ __forceinline__ void st4_sys(uint4* p, uint4 v) {
+    asm volatile("st.relaxed.sys.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ld4_sys(const uint4* p) {
+    uint4 r;
+    asm volatile("ld.relaxed.sys.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
 }
 __device__ __forceinline__ uint4 ll_load2(const uint2* p) {
     uint4 r;

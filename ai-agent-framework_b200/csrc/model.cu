@@ -55,11 +55,16 @@ float f16_to_f32(uint16_t h) {
 
 // A weight matrix of the decode kernel: GGUF tensors stacked by rows,
 // tiled into the arena at `off`.
+struct MatPart {
+    std::string name;
+    int64_t row0, rows;  // source rows of the tensor that go in
+};
 struct MatGroup {
-    std::vector<std::string> tensors;
+    std::vector<MatPart> parts;  // stacked in order
     size_t off;
-    int64_t rows, cols;
-    int64_t half_rows = 0;  // gate/up: rows of each tensor (8-row interleave)
+    int64_t rows, cols;          // the tiled matrix (this rank's share)
+    int64_t half_rows = 0;       // gate/up: rows of each part (8-row interleave)
+    int64_t cb0 = 0, nb_src = 0; // column blocks [cb0, cb0 + cols / 32) of source rows of nb_src blocks
 };
 
 // Row of the stacked source tensors that row r of a tiled matrix holds.  The
@@ -72,9 +77,10 @@ __host__ __device__ inline int64_t src_row(int64_t r, int64_t half_rows) {
 }
 
 // One thread per (row, block) of the padded matrix: ggml block -> tiled
-// quants + scale (padding rows become zero).
+// quants + scale (padding rows become zero).  Source rows have nb_src blocks,
+// of which blocks cb0 .. cb0 + nb go in (a tensor-parallel column share).
 __global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, int64_t rp, int64_t nb, int qtype,
-                              int64_t half_rows) {
+                              int64_t half_rows, int64_t nb_src, int64_t cb0) {
     const int bpb = qtype == 8 ? 34 : 18, qb = tile_qb(qtype);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rp * nb; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / nb, b = i - r * nb;
@@ -84,7 +90,7 @@ __global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, in
             for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = 0;
             continue;
         }
-        const uint8_t* src = raw + (src_row(r, half_rows) * nb + b) * bpb;
+        const uint8_t* src = raw + (src_row(r, half_rows) * nb_src + cb0 + b) * bpb;
         sd[0] = src[0];
         sd[1] = src[1];
         for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = src[2 + e];
@@ -127,8 +133,8 @@ __global__ void embed_mean_kernel(const ModelDev m, const int* toks, int n, floa
         float e = 0.0f;
         for (int t = 0; t < n; t++) {
             const int tok = toks[t];
-            if (tok < 0 || tok >= m.V) continue;
-            e += tiled_elem(m.tok_embd, tok, j, m.H / 32, m.Vp, m.qtype);
+            if (tok < 0 || tok >= m.Vemb) continue;
+            e += tiled_elem(m.tok_embd, tok, j, m.H / 32, m.Vp_emb, m.qtype);
         }
         e *= scale;
         out[j] = e;
@@ -315,7 +321,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     *out = nullptr;
     b2_load_opts o{};
     if (opts) o = *opts;
-    if (o.reserved0 > 1) return fail(err, B2_ERR_BAD_ARG, "tensor-parallel degree > 1 is not supported by b2_load");
+    const int tp = o.tp_size > 1 ? o.tp_size : 1, rank = tp > 1 ? o.tp_rank : 0;
+    if (tp > kMaxTp || rank < 0 || rank >= tp)
+        return fail(err, B2_ERR_BAD_ARG, "tensor-parallel degree must be 1 .. 8 and the rank below it");
     auto m = new b2_model();
     auto bail = [&](int code, const std::string& msg) {
         *err = msg;
@@ -399,48 +407,68 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     }
     c.weight_type = (int)qt;
 
+    // ---------------------------------------------------------- tensor-parallel shares
+    // Megatron layout: q / k / v rows and Wo columns by heads, gate / up rows
+    // and down columns by FFN 32-blocks (uneven shares allowed), lm_head rows
+    // by vocab; norms replicated.  From here on the dims are this rank's (the
+    // whole model when tp == 1).
+    if (nh % tp || nkv % tp)
+        return bail(B2_ERR_UNSUPPORTED_TYPE, "tensor parallelism needs the heads and KV heads divisible by the degree");
+    const int nhl = nh / tp, nkvl = nkv / tp, qdl = nhl * hd, kvdl = nkvl * hd;
+    const int fb0 = (int)((int64_t)rank * (FF / 32) / tp), fb1 = (int)((int64_t)(rank + 1) * (FF / 32) / tp);
+    const int FFl = 32 * (fb1 - fb0), ff0 = 32 * fb0;
+    const int v0 = (int)((int64_t)rank * V / tp), Vl = (int)((int64_t)(rank + 1) * V / tp) - v0;
+    if (FFl == 0 || Vl == 0) return bail(B2_ERR_UNSUPPORTED_TYPE, "tensor-parallel degree too large for this model");
+
     // ---------------------------------------------------------- arena plan
     const size_t bpb = qt == GGML_Q8_0 ? 34 : 18;
-    const size_t rb_h = H / 32 * bpb, rb_q = qd / 32 * bpb, rb_f = FF / 32 * bpb;
+    const size_t rb_h = H / 32 * bpb, rb_q = qdl / 32 * bpb, rb_f = FFl / 32 * bpb;
     size_t off = 0;
     auto take = [&](size_t bytes) {
         size_t o2 = off;
         off += up256(bytes + 16);
         return o2;
     };
-    std::vector<MatGroup> groups;  // (half_rows: the interleaved gate/up matrix)
-    std::vector<std::pair<std::string, size_t>> small;  // f32 vectors: name -> offset
+    std::vector<MatGroup> groups;
+    // f32 vectors: name, arena offset, first element and count of this rank's share
+    struct SmallVec { std::string name; size_t off; int64_t e0, n, total; };
+    std::vector<SmallVec> small;
     const int qti = qt == GGML_Q8_0 ? 8 : 2;
-    auto take_mat = [&](std::vector<std::string> names, int64_t rows, int64_t cols) {
+    auto take_mat = [&](std::vector<MatPart> parts, int64_t rows, int64_t cols, int64_t half_rows = 0,
+                        int64_t cb0 = 0, int64_t nb_src = 0) {
         const size_t o2 = take(tiled_bytes(rows, cols, qti));
-        groups.push_back({std::move(names), o2, rows, cols});
+        groups.push_back({std::move(parts), o2, rows, cols, half_rows, cb0, nb_src ? nb_src : cols / 32});
         return o2;
     };
-    const size_t off_embd = take_mat({"token_embd.weight"}, V, H);
+    // the embedding lookup needs every row; the lm_head only this rank's vocab share
+    const size_t off_embd = take_mat({{"token_embd.weight", 0, V}}, V, H);
     size_t off_out = off_embd;
-    if (ow) off_out = take_mat({"output.weight"}, V, H);
+    if (ow) off_out = take_mat({{"output.weight", v0, Vl}}, Vl, H);
+    else if (tp > 1) off_out = take_mat({{"token_embd.weight", v0, Vl}}, Vl, H);
     const size_t off_onorm = take((size_t)H * 4);
-    small.push_back({"output_norm.weight", off_onorm});
+    small.push_back({"output_norm.weight", off_onorm, 0, H, H});
     struct LOff { size_t qkv, wo, gu, wd, an, fn, b; };
     std::vector<LOff> lo(L);
     for (int l = 0; l < L; l++) {
         const std::string p = "blk." + std::to_string(l) + ".";
-        lo[l].qkv = take_mat({p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, qd + 2 * kvd, H);
-        lo[l].wo = take_mat({p + "attn_output.weight"}, H, qd);
-        // gate and up in one matrix of 2*FF rows, interleaved 8 rows at a time
-        lo[l].gu = take(tiled_bytes(2 * FF, H, qti));
-        groups.push_back({{p + "ffn_gate.weight", p + "ffn_up.weight"}, lo[l].gu, 2 * FF, H, FF});
-        lo[l].wd = take_mat({p + "ffn_down.weight"}, H, FF);
+        lo[l].qkv = take_mat({{p + "attn_q.weight", (int64_t)rank * qdl, qdl},
+                              {p + "attn_k.weight", (int64_t)rank * kvdl, kvdl},
+                              {p + "attn_v.weight", (int64_t)rank * kvdl, kvdl}}, qdl + 2 * kvdl, H);
+        // Wo: this rank's heads' input columns; down: its FFN blocks' columns
+        lo[l].wo = take_mat({{p + "attn_output.weight", 0, H}}, H, qdl, 0, (int64_t)rank * qdl / 32, qd / 32);
+        // gate and up in one matrix of 2*FFl rows, interleaved 8 rows at a time
+        lo[l].gu = take_mat({{p + "ffn_gate.weight", ff0, FFl}, {p + "ffn_up.weight", ff0, FFl}}, 2 * FFl, H, FFl);
+        lo[l].wd = take_mat({{p + "ffn_down.weight", 0, H}}, H, FFl, 0, fb0, FF / 32);
         lo[l].an = take((size_t)H * 4);
-        small.push_back({p + "attn_norm.weight", lo[l].an});
+        small.push_back({p + "attn_norm.weight", lo[l].an, 0, H, H});
         lo[l].fn = take((size_t)H * 4);
-        small.push_back({p + "ffn_norm.weight", lo[l].fn});
+        small.push_back({p + "ffn_norm.weight", lo[l].fn, 0, H, H});
         lo[l].b = 0;
         if (c.has_qkv_bias) {
-            lo[l].b = take((size_t)(qd + 2 * kvd) * 4);
-            small.push_back({p + "attn_q.bias", lo[l].b});
-            small.push_back({p + "attn_k.bias", lo[l].b + (size_t)qd * 4});
-            small.push_back({p + "attn_v.bias", lo[l].b + (size_t)(qd + kvd) * 4});
+            lo[l].b = take((size_t)(qdl + 2 * kvdl) * 4);
+            small.push_back({p + "attn_q.bias", lo[l].b, (int64_t)rank * qdl, qdl, qd});
+            small.push_back({p + "attn_k.bias", lo[l].b + (size_t)qdl * 4, (int64_t)rank * kvdl, kvdl, kvd});
+            small.push_back({p + "attn_v.bias", lo[l].b + (size_t)(qdl + kvdl) * 4, (int64_t)rank * kvdl, kvdl, kvd});
         }
     }
     const size_t weight_end = off;
@@ -448,8 +476,8 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const size_t off_cos = take((size_t)S * (hd / 2) * 4);
     const size_t off_sin = take((size_t)S * (hd / 2) * 4);
     const size_t kv_el = o.kv_fp32 ? 4 : 2;
-    const size_t off_k = take((size_t)L * S * kvd * kv_el);
-    const size_t off_v = take((size_t)L * S * kvd * kv_el);
+    const size_t off_k = take((size_t)L * S * kvdl * kv_el);
+    const size_t off_v = take((size_t)L * S * kvdl * kv_el);
 
     int dev_count = 0;
     if (cudaGetDeviceCount(&dev_count) != cudaSuccess || dev_count == 0)
@@ -464,11 +492,10 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const size_t off_plans = take((size_t)m->grid * kPlanSlots * sizeof(TPlan));
     const size_t off_llx1 = take((size_t)H * 8);
     const size_t off_llx2 = take((size_t)H * 8);
-    const size_t off_llqkv = take((size_t)(qd + 2 * kvd) * 8);
-    const size_t off_llpart = take((size_t)nh * kMaxSplits * (hd + 2) * 8);
-    const size_t off_llattn = take((size_t)qd * 8);
-    const size_t off_llact = take((size_t)FF * 8);
-    const size_t off_logits = take((size_t)V * 4);
+    const size_t off_llqkv = take((size_t)(qdl + 2 * kvdl) * 8);
+    const size_t off_llpart = take((size_t)nhl * kMaxSplits * (hd + 2) * 8);
+    const size_t off_llact = take((size_t)FFl * 8);
+    const size_t off_logits = take((size_t)Vl * 4);
     const size_t off_amkey = take(8);
     const size_t off_tok = take(4);
     const size_t off_amctr = take(4);
@@ -478,6 +505,16 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const size_t off_done = take(4);
     const size_t off_layers = take(sizeof(LayerDev) * L);
     m->arena_bytes = off;
+    // the tensor-parallel exchange buffer: its own allocation, so that its IPC
+    // mapping covers nothing else and its layout is the same on every rank
+    if (tp > 1) {
+        m->xch_bytes = xch_bytes(H, tp);
+        if (cudaMalloc(&m->xch, m->xch_bytes) != cudaSuccess) {
+            m->xch = nullptr;
+            return bail(B2_ERR_OOM, "device allocation of the exchange buffer failed");
+        }
+        cudaMemset(m->xch, 0, m->xch_bytes);
+    }
 
     if (dev_malloc(&m->arena, m->arena_bytes) != 0) {
         m->arena = nullptr;
@@ -491,7 +528,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     cudaEventCreateWithFlags(&m->ev_pin, cudaEventDisableTiming);
     cudaMemsetAsync(A + weight_end, 0, m->arena_bytes - weight_end, m->stream);
     if (cudaMallocHost(&m->h_pinned, sizeof(int32_t) * std::max(S, 16)) != cudaSuccess ||
-        cudaMallocHost(&m->h_logits, sizeof(float) * V) != cudaSuccess)
+        cudaMallocHost(&m->h_logits, sizeof(float) * Vl) != cudaSuccess)
         return bail(B2_ERR_OOM, "pinned host allocation failed");
 
     // ---------------------------------------------------------- upload
@@ -513,7 +550,11 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // Weight matrices: file -> pinned stage -> raw device buffer (double-
     // buffered), then one repack launch per matrix into the arena.
     size_t raw_max = 0;
-    for (const MatGroup& gr : groups) raw_max = std::max(raw_max, (size_t)gr.rows * (size_t)(gr.cols / 32 * bpb));
+    for (const MatGroup& gr : groups) {
+        int64_t r = 0;
+        for (const MatPart& pt : gr.parts) r += pt.rows;
+        raw_max = std::max(raw_max, (size_t)r * (size_t)gr.nb_src * bpb);
+    }
     void* raw = nullptr;
     if (dev_malloc(&raw, raw_max) != 0) {
         fclose(f);
@@ -524,9 +565,11 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     for (const MatGroup& gr : groups) {
         size_t dst = 0;
         int64_t row0 = 0;
-        for (const std::string& name : gr.tensors) {
+        for (const MatPart& pt : gr.parts) {
+            const std::string& name = pt.name;
             const GgufTensor* t = g.find(name);
-            uint64_t left = t->bytes(), src = g.data_offset + t->offset;
+            const uint64_t rb_src = (uint64_t)gr.nb_src * bpb;  // source row bytes
+            uint64_t left = (uint64_t)pt.rows * rb_src, src = g.data_offset + t->offset + (uint64_t)pt.row0 * rb_src;
             if (fseeko(f, (off_t)src, SEEK_SET) != 0) { io_ok = false; break; }
             while (left > 0 && io_ok) {
                 const size_t nb = (size_t)std::min<uint64_t>(left, stage_bytes);
@@ -540,48 +583,48 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
                 dst += nb;
             }
             if (!io_ok) break;
-            TensorLoc tl{A + gr.off, t->type, t->elements()};
+            // this rank's share of the tensor (b2_dequant_tensor decodes it)
+            TensorLoc tl{A + gr.off, t->type, (uint64_t)pt.rows * (uint64_t)gr.cols};
             tl.row0 = row0;
             tl.cols = gr.cols;
             tl.rp = tiled_rows(gr.rows);
             tl.half = gr.half_rows ? (row0 == 0 ? 1 : 2) : 0;
-            m->tensors[name] = tl;
-            row0 += (int64_t)t->dims[1];
+            if (!m->tensors.count(name)) m->tensors[name] = tl;
+            row0 += pt.rows;
         }
         if (!io_ok) break;
         const int64_t rp = tiled_rows(gr.rows), nbk = gr.cols / 32;
         const int blocks = (int)std::min<int64_t>((rp * nbk + 255) / 256, 148 * 32);
         repack_kernel<<<blocks, 256, 0, m->stream>>>(static_cast<const uint8_t*>(raw), A + gr.off, gr.rows, rp, nbk, qti,
-                                                     gr.half_rows);
+                                                     gr.half_rows, gr.nb_src, gr.cb0);
     }
     cudaStreamSynchronize(m->stream);
     cudaFree(raw);
     // Small vectors (norm gains, biases) as fp32; F16/BF16 widened on the host
     // exactly as gguf.go:510-536 does.
     std::vector<float> buf;
-    for (const auto& s : small) {
+    for (const SmallVec& sv : small) {
         if (!io_ok) break;
-        const GgufTensor* t = g.find(s.first);
+        const GgufTensor* t = g.find(sv.name);
         const size_t n = t ? (size_t)t->elements() : 0;
-        const int64_t expect = s.first.find("attn_q.bias") != std::string::npos ? qd
-                             : (s.first.find("attn_k.bias") != std::string::npos || s.first.find("attn_v.bias") != std::string::npos) ? kvd : H;
-        buf.assign(expect, 0.0f);  // an absent optional bias stays zero (transformer.go:632-646)
+        buf.assign(sv.n, 0.0f);  // an absent optional bias stays zero (transformer.go:632-646)
         if (t) {
-            if ((int64_t)n != expect) { fclose(f); return bail(B2_ERR_FORMAT, s.first + ": unexpected length"); }
+            if ((int64_t)n != sv.total) { fclose(f); return bail(B2_ERR_FORMAT, sv.name + ": unexpected length"); }
             std::vector<uint8_t> raw(t->bytes());
             if (fseeko(f, (off_t)(g.data_offset + t->offset), SEEK_SET) != 0 || fread(raw.data(), 1, raw.size(), f) != raw.size()) {
                 io_ok = false;
                 break;
             }
-            for (size_t i = 0; i < n; i++) {
-                if (t->type == GGML_F32) memcpy(&buf[i], &raw[i * 4], 4);
-                else if (t->type == GGML_F16) buf[i] = f16_to_f32((uint16_t)(raw[2 * i] | (raw[2 * i + 1] << 8)));
-                else if (t->type == GGML_BF16) { uint32_t bits = (uint32_t)(raw[2 * i] | (raw[2 * i + 1] << 8)) << 16; memcpy(&buf[i], &bits, 4); }
-                else { fclose(f); return bail(B2_ERR_UNSUPPORTED_TYPE, s.first + ": vectors must be F32, F16 or BF16"); }
+            for (int64_t k = 0; k < sv.n; k++) {
+                const size_t i = (size_t)(sv.e0 + k);
+                if (t->type == GGML_F32) memcpy(&buf[k], &raw[i * 4], 4);
+                else if (t->type == GGML_F16) buf[k] = f16_to_f32((uint16_t)(raw[2 * i] | (raw[2 * i + 1] << 8)));
+                else if (t->type == GGML_BF16) { uint32_t bits = (uint32_t)(raw[2 * i] | (raw[2 * i + 1] << 8)) << 16; memcpy(&buf[k], &bits, 4); }
+                else { fclose(f); return bail(B2_ERR_UNSUPPORTED_TYPE, sv.name + ": vectors must be F32, F16 or BF16"); }
             }
-            m->tensors[s.first] = TensorLoc{A + s.second, GGML_F32, n};
+            m->tensors[sv.name] = TensorLoc{A + sv.off, GGML_F32, (uint64_t)sv.n};
         }
-        cudaMemcpyAsync(A + s.second, buf.data(), buf.size() * 4, cudaMemcpyHostToDevice, m->stream);
+        cudaMemcpyAsync(A + sv.off, buf.data(), buf.size() * 4, cudaMemcpyHostToDevice, m->stream);
         cudaStreamSynchronize(m->stream);
     }
     fclose(f);
@@ -610,14 +653,19 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
 
     // ---------------------------------------------------------- device view
     ModelDev& d = m->dev;
-    d.H = H; d.FF = FF; d.V = V; d.L = L; d.nh = nh; d.nkv = nkv; d.hd = hd; d.qd = qd; d.kvd = kvd;
+    d.H = H; d.FF = FFl; d.V = Vl; d.L = L; d.nh = nhl; d.nkv = nkvl; d.hd = hd; d.qd = qdl; d.kvd = kvdl;
     d.max_seq = S;
     d.qtype = (int)qt;
     d.rb_h = (int)rb_h; d.rb_q = (int)rb_q; d.rb_f = (int)rb_f;
     d.eps = c.rms_norm_eps;
     d.kv_fp32 = o.kv_fp32 ? 1 : 0;
-    d.Vp = (int)tiled_rows(V);
-    d.nbx = std::max(std::max(H, qd), FF) / 32;
+    d.Vp = (int)tiled_rows(Vl);
+    d.Vemb = V;
+    d.Vp_emb = (int)tiled_rows(V);
+    d.v_off = v0;
+    d.tp = tp;
+    d.tp_rank = rank;
+    d.nbx = std::max(std::max(H, qdl), FFl) / 32;
     d.tok_embd = A + off_embd;
     d.lm_head = A + off_out;
     d.out_norm = reinterpret_cast<const float*>(A + off_onorm);
@@ -629,7 +677,6 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.ll_x2 = reinterpret_cast<uint2*>(A + off_llx2);
     d.ll_qkv = reinterpret_cast<uint2*>(A + off_llqkv);
     d.ll_part = reinterpret_cast<uint2*>(A + off_llpart);
-    d.ll_attn = reinterpret_cast<uint2*>(A + off_llattn);
     d.ll_act = reinterpret_cast<uint2*>(A + off_llact);
     d.logits = reinterpret_cast<float*>(A + off_logits);
     d.am_key = reinterpret_cast<unsigned long long*>(A + off_amkey);
@@ -656,15 +703,15 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
 
     // Shared-memory geometry: the ring of weight slots plus the QA phase's
     // attention scratch (xs: q, the per-warp partials and merge weights, the
-    // new position's words, one K and one V tile); the phase inputs go
+    // new position's words, one K and one Vl tile); the phase inputs go
     // straight into the int8 planes.
     const int kv_es = o.kv_fp32 ? 4 : 2;
     const int tile = std::max(1, std::min(kMaxAttnTile, kAttnTileBytes / (hd * kv_es)));
     const int attn_need = hd + kConsumerWarps * (hd + 2) + 16 + 4 * hd +
                           (tile * (hd * kv_es + 16) + tile * hd * kv_es) / 4;
     const int base_xs = attn_need;
-    // q CTAs (nh per split) must leave at least one CTA for the k / v rows
-    const int split_cap = std::max(1, std::min(kMaxSplits, (m->grid - 1) / nh));
+    // q CTAs (nhl per split) must leave at least one CTA for the k / v rows
+    const int split_cap = std::max(1, std::min(kMaxSplits, (m->grid - 1) / nhl));
     const int slot = 8192;
     // Outputs one CTA keeps per phase (all K-slices): from the same work plan
     // the kernel uses, over every CTA (and every split count for the QA phase).
@@ -688,7 +735,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     for (int S = 1; S <= split_cap; S++)
         for (int cta = 0; cta < m->grid; cta++) {
             int u0 = 0, n = 0;
-            qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n, qa_dist);
+            qa_tiles(nhl, hd, qdl, kvdl, S, cta, m->grid, &u0, &n, qa_dist);
             const TPlan pl = tile_plan_range(u0, n, H / 32, tbb1, slot, kConsumerWarps);
             qa_need = std::max(qa_need, pl.nks * kTileRows * pl.n);
             qa_rows = std::max(qa_rows, kTileRows * n);
@@ -696,9 +743,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // even phases (QA, gate/up, LM head) and odd phases (Wo, down) alternate
     // between two buffers, so the next phase's dots may start before this
     // phase's epilogue ends
-    const int ybuf_even = (std::max(std::max(qa_need, ybuf_need(2 * FF, H / 32, false)), ybuf_need(V, H / 32, false)) +
+    const int ybuf_even = (std::max(std::max(qa_need, ybuf_need(2 * FFl, H / 32, false)), ybuf_need(Vl, H / 32, false)) +
                            31) & ~31;
-    const int ybuf_odd = (std::max(ybuf_need(H, qd / 32, true), ybuf_need(H, FF / 32, true)) + 31) & ~31;
+    const int ybuf_odd = (std::max(ybuf_need(H, qdl / 32, true), ybuf_need(H, FFl / 32, true)) + 31) & ~31;
     const int ybuf = ybuf_even + ybuf_odd;
     const auto rows_per_cta = [&](int rows) {
         return kTileRows * (int)((tiled_rows(rows) / kTileRows + m->grid - 1) / m->grid);
@@ -706,28 +753,28 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const int cfloats = cb_floats(hd);
     auto ring_slots = [&](int xs_f) {
         int n = 0;
-        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qd), FF) / 32, L).total <= 232448u) n++;
+        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qdl), FFl) / 32, L).total <= 232448u) n++;
         return n;
     };
     const int xs = (base_xs + 31) & ~31, max_splits = split_cap;
     const int ns = ring_slots(xs);
     if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
     if (rows_per_cta(H) > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
-    if (qa_rows > kMaxQkvRows || nh >= m->grid)
+    if (qa_rows > kMaxQkvRows || nhl >= m->grid)
         return bail(B2_ERR_UNSUPPORTED_TYPE, "attention projection too large for one GPU");
     // every CTA's work plans (plan_slot order), so the kernel needs no divisions
     {
         std::vector<TPlan> plans((size_t)m->grid * kPlanSlots, TPlan{0, 0, 1, 1, 1, 0});
-        const int Vp = (int)tiled_rows(V);
+        const int Vp = (int)tiled_rows(Vl);
         for (int cta = 0; cta < m->grid; cta++) {
             TPlan* pc = plans.data() + (size_t)cta * kPlanSlots;
-            pc[plan_slot(PH_WO, 1)] = own_plan(H / kTileRows, qd / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
-            pc[plan_slot(PH_GATEUP, 1)] = tile_plan(2 * FF / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
-            pc[plan_slot(PH_DOWN, 1)] = own_plan(H / kTileRows, FF / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_WO, 1)] = own_plan(H / kTileRows, qdl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_GATEUP, 1)] = tile_plan(2 * FFl / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_DOWN, 1)] = own_plan(H / kTileRows, FFl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             pc[plan_slot(PH_LMHEAD, 1)] = tile_plan(Vp / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
-            for (int S = 1; S <= kMaxSplits && nh * S < m->grid; S++) {
+            for (int S = 1; S <= kMaxSplits && nhl * S < m->grid; S++) {
                 int u0 = 0, n = 0;
-                qa_tiles(nh, hd, qd, kvd, S, cta, m->grid, &u0, &n, qa_dist);
+                qa_tiles(nhl, hd, qdl, kvdl, S, cta, m->grid, &u0, &n, qa_dist);
                 pc[plan_slot(PH_QA, S)] = tile_plan_range(u0, n, H / 32, tbb1, slot, kConsumerWarps);
             }
         }
@@ -745,10 +792,14 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     m->max_splits = max_splits;
 
     c.weight_bytes = (int64_t)weight_end;
+    c.tp_size = tp;
+    c.tp_rank = rank;
+    c.vocab_begin = v0;
+    c.vocab_local = Vl;
     {
-        int64_t layer = (int64_t)(qd + 2 * kvd) * rb_h + (int64_t)H * rb_q + (int64_t)2 * FF * rb_h + (int64_t)H * rb_f;
-        int64_t smallb = 4 * (2 * (int64_t)H + (c.has_qkv_bias ? (qd + 2 * kvd) : 0));
-        c.stream_bytes_per_token = (int64_t)L * (layer + smallb) + (int64_t)V * rb_h + 4 * (int64_t)H;
+        int64_t layer = (int64_t)(qdl + 2 * kvdl) * rb_h + (int64_t)H * rb_q + (int64_t)2 * FFl * rb_h + (int64_t)H * rb_f;
+        int64_t smallb = 4 * (2 * (int64_t)H + (c.has_qkv_bias ? (qdl + 2 * kvdl) : 0));
+        c.stream_bytes_per_token = (int64_t)L * (layer + smallb) + (int64_t)Vl * rb_h + 4 * (int64_t)H;
     }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return bail(B2_ERR_CUDA, std::string("CUDA: ") + cudaGetErrorString(e));
@@ -759,6 +810,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
 void b2_free_impl(b2_model* m) {
     if (!m) return;
     if (m->stream) cudaStreamSynchronize(m->stream);
+    for (int p = 0; p < kMaxTp; p++)
+        if (m->xch_peer[p] && m->xch_peer[p] != m->xch) cudaIpcCloseMemHandle(m->xch_peer[p]);
+    if (m->xch) cudaFree(m->xch);
     if (m->arena) cudaFree(m->arena);
     if (m->h_pinned) cudaFreeHost(m->h_pinned);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -768,3 +822,49 @@ void b2_free_impl(b2_model* m) {
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
+
+namespace b2 {
+
+// Tensor parallelism: the IPC handle of this rank's exchange buffer, and the
+// mapping of every rank's buffer (handles in rank order, 64 bytes each).
+int b2_tp_handle_impl(const b2_model* m, void* out, std::string* err) {
+    if (m->dev.tp < 2 || !m->xch) { *err = "not a tensor-parallel model"; return B2_ERR_BAD_ARG; }
+    cudaSetDevice(m->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, m->xch);
+    if (e != cudaSuccess) { *err = std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(e); return B2_ERR_CUDA; }
+    static_assert(sizeof(h) == 64, "IPC handle size");
+    memcpy(out, &h, sizeof h);
+    return B2_OK;
+}
+
+int b2_tp_connect_impl(b2_model* m, const void* handles, std::string* err) {
+    const int tp = m->dev.tp;
+    if (tp < 2 || !m->xch) { *err = "not a tensor-parallel model"; return B2_ERR_BAD_ARG; }
+    if (m->tp_connected) { *err = "already connected"; return B2_ERR_BAD_ARG; }
+    cudaSetDevice(m->device);
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (int p = 0; p < tp; p++) {
+        if (p == m->dev.tp_rank) {
+            m->xch_peer[p] = m->xch;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + 64 * p, sizeof h);
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            *err = "cudaIpcOpenMemHandle (rank " + std::to_string(p) + "): " + cudaGetErrorString(e);
+            for (int q = 0; q < p; q++)
+                if (m->xch_peer[q] && m->xch_peer[q] != m->xch) cudaIpcCloseMemHandle(m->xch_peer[q]);
+            for (int q = 0; q < kMaxTp; q++) m->xch_peer[q] = nullptr;
+            return B2_ERR_CUDA;
+        }
+        m->xch_peer[p] = ptr;
+    }
+    for (int p = 0; p < tp; p++) m->dev.xpeer[p] = static_cast<uint8_t*>(m->xch_peer[p]);
+    m->tp_connected = true;
+    return B2_OK;
+}
+
+}  // namespace b2

@@ -66,6 +66,12 @@ struct b2_model {
     cudaEvent_t ev_pin = nullptr;  // last H2D copy out of h_pinned
     bool pin_pending = false;
     b2::StreamState st;
+    // tensor parallelism: this rank's exchange buffer and the peers' (mapped
+    // through CUDA IPC by b2_tp_connect; launches need the connection first)
+    void* xch = nullptr;
+    size_t xch_bytes = 0;
+    void* xch_peer[b2::kMaxTp] = {};
+    bool tp_connected = false;
 };
 
 namespace b2 {
@@ -81,6 +87,10 @@ int launch_embed_mean(const b2_model* m, const int* d_tokens, int n, float* d_ou
 // when n > 1).  Logits of the last token stay in dev.logits and its argmax in
 // dev.token.  Returns B2_* codes.
 int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err);
+// Tensor parallelism: this rank's exchange-buffer IPC handle (64 bytes), and
+// the mapping of all ranks' buffers from their handles in rank order.
+int b2_tp_handle_impl(const b2_model* m, void* out, std::string* err);
+int b2_tp_connect_impl(b2_model* m, const void* handles, std::string* err);
 // Device-resident greedy loop; see b2_decode_greedy.
 int run_greedy(b2_model* m, int32_t first, int n_steps, int32_t eos, int32_t* out_ids, int32_t* n_out,
                std::string* err);

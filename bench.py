@@ -7,7 +7,7 @@ quantised to Q8_0; prompt = BOS + 128 ids uniform over the vocab (seed 0);
 prefill, then greedy decode.  One step = one decode token.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload qwen05b|llama3-8b|matvec|attention]
+                    [--workload qwen05b|llama3-8b|qwen72b|matvec|attention]
 
 value: decode tok/s over all ranks, device-timed with CUDA events on the
 engine's stream (inputs resident in HBM).  e2e: the same tok/s through the C
@@ -22,6 +22,12 @@ The other workloads (one GPU, one JSON line per case; not the driver's line):
   llama3-8b  Llama-3-8B-shape Q4_0 greedy decode at batch 1 (hidden 4096, 32
              layers, 32/8 heads, head_dim 128, FFN 14336, vocab 128256, untied),
              prompt 512 ids, then K decode tokens;
+  qwen72b    Qwen2.5-72B-shape Q8_0 (hidden 8192, 64/8 heads of 128, FFN 29568,
+             vocab 152064, untied) cut to 4 of its 80 layers, tensor-parallel
+             over the --gpus N ranks (one process per GPU under torchrun,
+             partial sums exchanged by peer stores over NVLink inside the
+             decode kernel), prompt 256 ids; value = tok/s of the one model
+             (strong scaling), ms_per_step = per-token latency;
   matvec     y = W x through b2_matvec for the Q8_0 and Q4_0 shapes 4096x4096,
              14336x4096, 4096x14336, 128256x4096 (GGUF block layout, W N(0,0.02),
              x N(0,1)), batch 1, with >= 256 MB of distinct weight copies rotated
@@ -174,6 +180,8 @@ def ensure_model(shape_name: str) -> str:
 MODELS = {
     "qwen05b": ("qwen2.5-0.5b", 128, WORKLOAD),
     "llama3-8b": ("llama3-8b", 512, "llama-3-8b-shape q4_0 greedy decode, batch 1, prompt 512 ids"),
+    "qwen72b": ("qwen2.5-72b-4l", 256, "qwen2.5-72b-shape q8_0 (4 of its 80 layers, full widths) tensor-parallel "
+                "greedy decode, batch 1, prompt 256 ids"),
 }
 
 
@@ -299,7 +307,11 @@ def run_b200(args) -> None:
     e2e_steps = min(K, 64)
     prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, n_prompt, seed=0)]).astype(np.int32)
     num_ctx = len(prompt) + W + K + e2e_steps + 8
-    m = b2decode.Model(path, num_ctx=num_ctx, device=local)
+    tpn = ws if args.workload == "qwen72b" else 1  # tensor-parallel degree (else replicas)
+    m = b2decode.Model(path, num_ctx=num_ctx, device=local, tp_size=tpn, tp_rank=rank if tpn > 1 else 0)
+    if tpn > 1:
+        from b2decode import tp as tpmod
+        tpmod.connect(m)
     stream = torch.cuda.ExternalStream(m.stream_handle())
     cfg = m.cfg
 
@@ -326,7 +338,8 @@ def run_b200(args) -> None:
     ms_max = max_over_ranks(ms)
     if len(ids) != K:
         raise RuntimeError(f"decode produced {len(ids)} of {K} tokens")
-    value = ws * K / (ms_max / 1000.0)
+    reps = ws // tpn  # independent model copies decoding at once
+    value = reps * K / (ms_max / 1000.0)
     ms_tok = ms / K
 
     # e2e through the C ABI: one call per token, host in / host out
@@ -338,7 +351,7 @@ def run_b200(args) -> None:
         tok = m.forward_argmax([tok])
     e2e_s = time.perf_counter() - t0
     e2e_s = max_over_ranks(e2e_s)
-    e2e = ws * e2e_steps / e2e_s
+    e2e = reps * e2e_steps / e2e_s
 
     peak, peak_kind = peaks()
     bytes_tok = int(cfg["stream_bytes_per_token"])
@@ -356,13 +369,14 @@ def run_b200(args) -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
-            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong" if tpn > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "fp32", "data": "synthetic",
             "config": {"workload": workload, "weights": f"N(0,0.02) quantised {shape.wtype.upper()}, seed 0",
                        "prompt_tokens": int(len(prompt)), "decode_tokens_timed": K,
                        "ctx_range": [int(len(prompt) + W), int(len(prompt) + W + K)],
                        "l2": f"no flush needed: each token streams {bytes_tok / 1e6:.0f} MB of weights, > 126 MB L2",
-                       "parallelism": f"replicas x{ws}" if ws > 1 else "single gpu",
+                       "parallelism": (f"tp{tpn}" if tpn > 1 else (f"replicas x{ws}" if ws > 1 else "single gpu")),
                        "prefill_s": prefill_s, "kv_cache": "fp16"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
@@ -482,7 +496,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="qwen05b", choices=["qwen05b", "llama3-8b", "matvec", "attention"])
+    ap.add_argument("--workload", default="qwen05b", choices=["qwen05b", "llama3-8b", "qwen72b", "matvec", "attention"])
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -45,8 +45,8 @@ typedef struct {
     int32_t num_ctx;    /* LoadOptions.NumCtx: caps context_length when > 0 (transformer.go:233-235) */
     int32_t device;     /* CUDA device ordinal */
     int32_t kv_fp32;    /* 0: fp16 KV cache (default); 1: fp32 KV cache as in the Go engine */
-    int32_t reserved0;  /* LoadOptions.NumGPU / tensor-parallel degree; must be 0 or 1 here */
-    int32_t reserved1;
+    int32_t tp_size;    /* LoadOptions.NumGPU: tensor-parallel degree (0 or 1: one GPU; up to 8) */
+    int32_t tp_rank;    /* this process's rank, 0 .. tp_size - 1 (one process per GPU) */
     int32_t reserved2;
 } b2_load_opts;
 
@@ -68,8 +68,12 @@ typedef struct {
     int32_t weight_type;       /* ggml type of the layer matrices: 8 = Q8_0, 2 = Q4_0 */
     int32_t bos_id;            /* tokenizer.ggml.bos_token_id (bpe.go:48,105) */
     int32_t eos_id;            /* tokenizer.ggml.eos_token_id (bpe.go:49,108) */
-    int64_t weight_bytes;      /* bytes of weights resident in HBM */
-    int64_t stream_bytes_per_token; /* algorithmic HBM bytes one B=1 decode token reads */
+    int64_t weight_bytes;      /* bytes of weights resident in HBM (this rank's) */
+    int64_t stream_bytes_per_token; /* algorithmic HBM bytes one B=1 decode token reads (this rank's) */
+    int32_t tp_size;           /* tensor-parallel degree and this rank */
+    int32_t tp_rank;
+    int32_t vocab_begin;       /* this rank's share of the lm_head rows: logits of */
+    int32_t vocab_local;       /* vocab ids vocab_begin .. vocab_begin + vocab_local - 1 */
 } b2_config;
 
 /* Real phase timings (the Go engine reports fixed 1/3 and 2/3 splits,
@@ -184,6 +188,25 @@ int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, fl
  * No counterpart in the reference. */
 int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
                                 int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream);
+
+/* ---- tensor parallelism (engine.go LoadOptions.NumGPU; no counterpart in the
+ * Go engine, which runs on CPU cores) ----
+ *
+ * One process per GPU loads the same GGUF with b2_load_opts.tp_size = N and
+ * its own tp_rank: it keeps its heads' q / k / v rows and Wo columns, its
+ * share of the FFN (gate / up rows, down columns, at 32-block granularity)
+ * and of the lm_head vocab rows.  After Wo and after down every rank writes
+ * its partial sums into every rank's exchange buffer over NVLink (peer
+ * stores) and sums all ranks' partials in rank order, so the residual stream
+ * is identical on every rank; the argmax is taken over all ranks' vocab
+ * shares the same way.  Before the first forward call, every rank passes the
+ * 64-byte handle from b2_tp_handle to the others (any host channel) and calls
+ * b2_tp_connect with all N handles in rank order.  Every rank must then make
+ * the same sequence of forward calls with the same tokens.  b2_forward's
+ * logits_out receives this rank's vocab share (b2_config.vocab_begin /
+ * vocab_local); sampling other than greedy is not available. */
+int b2_tp_handle(const b2_model* m, void* handle_out);
+int b2_tp_connect(b2_model* m, const void* handles);
 
 /* Device-side error code of the last launch on this model (B2_ERR_TIMEOUT
  * after a bounded wait gave up), 0 if none; clears it. */
