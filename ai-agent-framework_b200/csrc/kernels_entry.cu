@@ -47,103 +47,167 @@ constexpr int kAttWarps = kAttThreads / 32;
 constexpr int kMaxGrp = 8;      // query heads per KV head handled in registers
 constexpr int kMaxDimsLane = 8; // head_dim up to 256
 
-// One CTA = one (sequence, KV head, context slice).  Warps take positions
-// round-robin; within a warp the lanes split the head dimension.  Each warp
-// keeps an online softmax (m, l, o) per query head; the CTA merges its warps
-// and writes one partial (o unnormalised, m, l) per query head.
-template <int DPL>  // dims per lane = hd / 32
-__global__ void __launch_bounds__(kAttThreads) attn_partial_kernel(const float* __restrict__ q, const __half* __restrict__ k,
-                                                                   const __half* __restrict__ v, float* __restrict__ part,
-                                                                   int nh, int nkv, int hd, int ctx, int S) {
+// One CTA = one (sequence, KV head, context slice), GRP query heads of head
+// dimension HD.  A group of LP = HD / 8 lanes takes one position at a time
+// (8 elements of k and v per lane, 16-byte loads) and keeps its own online
+// softmax per query head, so a step needs only the LP-lane reduction of
+// q . k; a warp advances 32 / LP positions per step and issues the loads of
+// U steps before using them, so enough bytes are in flight to stream the
+// cache.  Groups merge by shuffles, warps through shared memory; the CTA
+// writes one partial (o unnormalised, m, l) per query head.
+template <int HD, int GRP>
+__global__ void __launch_bounds__(kAttThreads, (GRP <= 4 ? 2 : 1))
+    attn_split_kernel(const float* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
+                      float* __restrict__ part, int nh, int nkv, int ctx, int S) {
+    constexpr int DL = 8, LP = HD / DL, G = 32 / LP, U = GRP <= 3 ? 4 : (GRP == 4 ? 3 : 2);
     extern __shared__ float sm[];
-    const int grp = nh / nkv;
     const int cta = blockIdx.x;
     const int s = cta % S, g = (cta / S) % nkv, b = cta / (S * nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = lane / LP, d0 = (lane % LP) * DL;
     const int t0 = (int)((long long)s * ctx / S), t1 = (int)((long long)(s + 1) * ctx / S);
-    const size_t kvd = (size_t)nkv * hd;
-    const __half* kb = k + (size_t)b * ctx * kvd + (size_t)g * hd + lane * DPL;
-    const __half* vb = v + (size_t)b * ctx * kvd + (size_t)g * hd + lane * DPL;
-    const float scale = (float)(1.0 / sqrt((double)hd));
-
-    float qr[kMaxGrp][DPL];
+    const size_t kvd = (size_t)nkv * HD;
+    const __half* kb = k + (size_t)b * ctx * kvd + (size_t)g * HD + d0;
+    const __half* vb = v + (size_t)b * ctx * kvd + (size_t)g * HD + d0;
+    const float scale = (float)(1.0 / sqrt((double)HD));
+    float qr[GRP][DL], o[GRP][DL], mr[GRP], lr[GRP];
 #pragma unroll
-    for (int h = 0; h < kMaxGrp; h++)
+    for (int h = 0; h < GRP; h++) {
+        const float* qh = q + ((size_t)b * nh + (size_t)g * GRP + h) * HD + d0;
+        const float4 x0 = *reinterpret_cast<const float4*>(qh), x1 = *reinterpret_cast<const float4*>(qh + 4);
+        qr[h][0] = x0.x * scale; qr[h][1] = x0.y * scale; qr[h][2] = x0.z * scale; qr[h][3] = x0.w * scale;
+        qr[h][4] = x1.x * scale; qr[h][5] = x1.y * scale; qr[h][6] = x1.z * scale; qr[h][7] = x1.w * scale;
+        mr[h] = -INFINITY;
+        lr[h] = 0.0f;
 #pragma unroll
-        for (int d = 0; d < DPL; d++)
-            qr[h][d] = (h < grp) ? q[((size_t)b * nh + g * grp + h) * hd + lane * DPL + d] : 0.0f;
-
-    float mrun[kMaxGrp], lrun[kMaxGrp], o[kMaxGrp][DPL];
-#pragma unroll
-    for (int h = 0; h < kMaxGrp; h++) {
-        mrun[h] = -INFINITY;
-        lrun[h] = 0.0f;
-#pragma unroll
-        for (int d = 0; d < DPL; d++) o[h][d] = 0.0f;
+        for (int e = 0; e < DL; e++) o[h][e] = 0.0f;
     }
-
-    for (int t = t0 + warp; t < t1; t += kAttWarps) {
-        float kf[DPL], vf[DPL];
-        if (DPL == 4) {
-            const uint2 ku = __ldg(reinterpret_cast<const uint2*>(kb + (size_t)t * kvd));
-            const uint2 vu = __ldg(reinterpret_cast<const uint2*>(vb + (size_t)t * kvd));
-            const __half2* kh = reinterpret_cast<const __half2*>(&ku);
-            const __half2* vh = reinterpret_cast<const __half2*>(&vu);
+    constexpr int step = kAttWarps * G;  // positions per CTA step
+    for (int base = t0 + warp * G; base < t1; base += step * U) {
+        uint4 kr[U], vr[U];
+        bool on[U];
 #pragma unroll
-            for (int e = 0; e < DPL / 2; e++) {
-                float2 a = __half22float2(kh[e]), c = __half22float2(vh[e]);
+        for (int u = 0; u < U; u++) {
+            const int t = base + u * step + grp;
+            on[u] = t < t1;
+            const size_t tt = (size_t)(on[u] ? t : t0);
+            kr[u] = __ldg(reinterpret_cast<const uint4*>(kb + tt * kvd));
+            vr[u] = __ldg(reinterpret_cast<const uint4*>(vb + tt * kvd));
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            if (!__any_sync(0xffffffffu, on[u])) break;  // warp-uniform
+            float kf[DL], vf[DL];
+            const __half2* kh = reinterpret_cast<const __half2*>(&kr[u]);
+            const __half2* vh = reinterpret_cast<const __half2*>(&vr[u]);
+#pragma unroll
+            for (int e = 0; e < DL / 2; e++) {
+                const float2 a = __half22float2(kh[e]), c = __half22float2(vh[e]);
                 kf[2 * e] = a.x; kf[2 * e + 1] = a.y; vf[2 * e] = c.x; vf[2 * e + 1] = c.y;
             }
-        } else {
 #pragma unroll
-            for (int e = 0; e < DPL; e += 2) {
-                float2 a = __half22float2(*reinterpret_cast<const __half2*>(kb + (size_t)t * kvd + e));
-                float2 c = __half22float2(*reinterpret_cast<const __half2*>(vb + (size_t)t * kvd + e));
-                kf[e] = a.x; kf[e + 1] = a.y; vf[e] = c.x; vf[e + 1] = c.y;
+            for (int h = 0; h < GRP; h++) {
+                float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+                for (int e = 0; e < DL; e += 2) {
+                    s0 = fmaf(qr[h][e], kf[e], s0);
+                    s1 = fmaf(qr[h][e + 1], kf[e + 1], s1);
+                }
+                float sc = s0 + s1;
+#pragma unroll
+                for (int off = 1; off < LP; off <<= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+                if (on[u]) {
+                    // one exponential per position: the larger of (m, sc) keeps weight 1
+                    const float ex = __expf(-fabsf(sc - mr[h]));  // m = -inf: 0
+                    const bool up = sc > mr[h];
+                    const float cf = up ? ex : 1.0f, pr = up ? 1.0f : ex;
+                    lr[h] = fmaf(lr[h], cf, pr);
+#pragma unroll
+                    for (int e = 0; e < DL; e++) o[h][e] = fmaf(pr, vf[e], o[h][e] * cf);
+                    mr[h] = up ? sc : mr[h];
+                }
             }
         }
+    }
+    // merge the lane groups of this warp
 #pragma unroll
-        for (int h = 0; h < kMaxGrp; h++) {
-            if (h >= grp) break;
-            float dot = 0.0f;
+    for (int off = LP; off < 32; off <<= 1) {
 #pragma unroll
-            for (int d = 0; d < DPL; d++) dot = fmaf(qr[h][d], kf[d], dot);
-            dot = warp_sum(dot) * scale;
-            const float mn = fmaxf(mrun[h], dot);
-            const float c = expf(mrun[h] - mn);  // exp(-inf) = 0 on the first position
-            const float p = expf(dot - mn);
-            lrun[h] = lrun[h] * c + p;
-            mrun[h] = mn;
+        for (int h = 0; h < GRP; h++) {
+            const float mo = __shfl_xor_sync(0xffffffffu, mr[h], off), lo = __shfl_xor_sync(0xffffffffu, lr[h], off);
+            const float mx = fmaxf(mr[h], mo);
+            const float c1 = mr[h] == -INFINITY ? 0.0f : __expf(mr[h] - mx);
+            const float c2 = mo == -INFINITY ? 0.0f : __expf(mo - mx);
+            lr[h] = lr[h] * c1 + lo * c2;
 #pragma unroll
-            for (int d = 0; d < DPL; d++) o[h][d] = fmaf(p, vf[d], o[h][d] * c);
+            for (int e = 0; e < DL; e++) o[h][e] = o[h][e] * c1 + __shfl_xor_sync(0xffffffffu, o[h][e], off) * c2;
+            mr[h] = mx;
         }
     }
-
-    // merge the warps of this CTA
-    float* wm = sm;                                  // [warps][grp]
-    float* wl = wm + kAttWarps * kMaxGrp;            // [warps][grp]
-    float* wo = wl + kAttWarps * kMaxGrp;            // [warps][grp][hd]
-    for (int h = 0; h < grp; h++) {
-        if (lane == 0) { wm[warp * kMaxGrp + h] = mrun[h]; wl[warp * kMaxGrp + h] = lrun[h]; }
+    // merge the warps of this CTA: [warp][GRP][HD + 2] (o, m, l)
+    float* wp = sm + (size_t)warp * GRP * (HD + 2);
+    if (grp == 0) {
 #pragma unroll
-        for (int d = 0; d < DPL; d++) wo[((size_t)warp * kMaxGrp + h) * hd + lane * DPL + d] = o[h][d];
+        for (int h = 0; h < GRP; h++) {
+#pragma unroll
+            for (int e = 0; e < DL; e++) wp[h * (HD + 2) + d0 + e] = o[h][e];
+            if (lane == 0) {
+                wp[h * (HD + 2) + HD] = mr[h];
+                wp[h * (HD + 2) + HD + 1] = lr[h];
+            }
+        }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < grp * (hd + 2); i += kAttThreads) {
-        const int h = i / (hd + 2), d = i % (hd + 2);
+    for (int i = threadIdx.x; i < GRP * (HD + 2); i += kAttThreads) {
+        const int h = i / (HD + 2), d = i - h * (HD + 2);
         float M = -INFINITY;
-        for (int w = 0; w < kAttWarps; w++) M = fmaxf(M, wm[w * kMaxGrp + h]);
-        float val = 0.0f;
-        if (d == hd) {
-            val = M;
-        } else {
+#pragma unroll
+        for (int w = 0; w < kAttWarps; w++) M = fmaxf(M, sm[((size_t)w * GRP + h) * (HD + 2) + HD]);
+        float val = M;
+        if (d != HD) {
+            val = 0.0f;
+#pragma unroll
             for (int w = 0; w < kAttWarps; w++) {
-                const float mw = wm[w * kMaxGrp + h];
-                const float f = (mw == -INFINITY) ? 0.0f : expf(mw - M);
-                val = fmaf(d < hd ? wo[((size_t)w * kMaxGrp + h) * hd + d] : wl[w * kMaxGrp + h], f, val);
+                const float* pw = sm + ((size_t)w * GRP + h) * (HD + 2);
+                const float f = pw[HD] == -INFINITY ? 0.0f : __expf(pw[HD] - M);
+                val = fmaf(pw[d], f, val);
             }
         }
-        part[(((size_t)b * nh + g * grp + h) * S + s) * (hd + 2) + d] = val;
+        part[(((size_t)b * nh + (size_t)g * GRP + h) * S + s) * (HD + 2) + d] = val;
+    }
+}
+
+// Launches attn_split_kernel for head dimension hd (64, 128, 256) and group
+// size grp (1 .. 8); returns false for other geometries.
+template <int HD>
+bool launch_split_hd(int grp, int grid, cudaStream_t st, const float* q, const __half* k, const __half* v, float* part,
+                     int nh, int nkv, int ctx, int S) {
+    auto go = [&](auto kern, int g) {
+        const size_t smem = sizeof(float) * (size_t)kAttWarps * g * (HD + 2);
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        kern<<<grid, kAttThreads, smem, st>>>(q, k, v, part, nh, nkv, ctx, S);
+        return true;
+    };
+    switch (grp) {
+        case 1: return go(attn_split_kernel<HD, 1>, 1);
+        case 2: return go(attn_split_kernel<HD, 2>, 2);
+        case 3: return go(attn_split_kernel<HD, 3>, 3);
+        case 4: return go(attn_split_kernel<HD, 4>, 4);
+        case 5: return go(attn_split_kernel<HD, 5>, 5);
+        case 6: return go(attn_split_kernel<HD, 6>, 6);
+        case 7: return go(attn_split_kernel<HD, 7>, 7);
+        case 8: return go(attn_split_kernel<HD, 8>, 8);
+        default: return false;
+    }
+}
+
+bool launch_split(int hd, int grp, int grid, cudaStream_t st, const float* q, const __half* k, const __half* v,
+                  float* part, int nh, int nkv, int ctx, int S) {
+    switch (hd) {
+        case 64: return launch_split_hd<64>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S);
+        case 128: return launch_split_hd<128>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S);
+        case 256: return launch_split_hd<256>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S);
+        default: return false;
     }
 }
 
@@ -223,6 +287,10 @@ int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, floa
         *err = "attention geometry unsupported (need nh/nkv <= 8 and head_dim in {64, 128, 256})";
         return B2_ERR_BAD_ARG;
     }
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) {
+        *err = "q, k and v must be 16-byte aligned";
+        return B2_ERR_BAD_ARG;
+    }
     DeviceScratch* sc = scratch_for_current(err);
     if (!sc) return B2_ERR_CUDA;
     const int S = attention_splits(batch, nkv, ctx, sc->sms);
@@ -240,26 +308,12 @@ int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, floa
             sc->part_floats = need;
         }
     }
-    const size_t smem = sizeof(float) * (2 * kAttWarps * kMaxGrp + (size_t)kAttWarps * kMaxGrp * hd);
     const int grid = batch * nkv * S;
     const __half* kh = reinterpret_cast<const __half*>(k);
     const __half* vh = reinterpret_cast<const __half*>(v);
-    switch (hd / 32) {
-        case 2:
-            cudaFuncSetAttribute(attn_partial_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            attn_partial_kernel<2><<<grid, kAttThreads, smem, s>>>(q, kh, vh, sc->part, nh, nkv, hd, ctx, S);
-            break;
-        case 4:
-            cudaFuncSetAttribute(attn_partial_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            attn_partial_kernel<4><<<grid, kAttThreads, smem, s>>>(q, kh, vh, sc->part, nh, nkv, hd, ctx, S);
-            break;
-        case 8:
-            cudaFuncSetAttribute(attn_partial_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            attn_partial_kernel<8><<<grid, kAttThreads, smem, s>>>(q, kh, vh, sc->part, nh, nkv, hd, ctx, S);
-            break;
-        default:
-            *err = "head_dim must be 64, 128 or 256";
-            return B2_ERR_BAD_ARG;
+    if (!launch_split(hd, grp, grid, s, q, kh, vh, sc->part, nh, nkv, ctx, S)) {
+        *err = "head_dim must be 64, 128 or 256";
+        return B2_ERR_BAD_ARG;
     }
     attn_merge_kernel<<<batch * nh, std::min(hd, 256), 0, s>>>(sc->part, out, nh, hd, S);
     cudaError_t e = cudaGetLastError();
@@ -300,6 +354,10 @@ int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t*
     const int grp = nh / nkv;
     if (grp > kMaxGrp || hd % 32 || hd / 32 > kMaxDimsLane || (hd != 64 && hd != 128 && hd != 256)) {
         *err = "attention geometry unsupported (need nh/nkv <= 8 and head_dim in {64, 128, 256})";
+        return B2_ERR_BAD_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) & 15) {
+        *err = "q, k and v must be 16-byte aligned";
         return B2_ERR_BAD_ARG;
     }
     const size_t per_split = (size_t)batch * nh * (hd + 2);
@@ -345,18 +403,10 @@ int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t*
     }
     int S = attention_splits(batch, nkv, ctx, sms);
     S = std::min<int>(S, (int)(kNoAllocScratchFloats / per_split));
-    const size_t smem = sizeof(float) * (2 * kAttWarps * kMaxGrp + (size_t)kAttWarps * kMaxGrp * hd);
     const int grid = batch * nkv * S;
     const __half* kh = reinterpret_cast<const __half*>(k);
     const __half* vh = reinterpret_cast<const __half*>(v);
-    if (hd == 64) {
-        attn_partial_kernel<2><<<grid, kAttThreads, smem, s>>>(q, kh, vh, part, nh, nkv, hd, ctx, S);
-    } else if (hd == 128) {
-        attn_partial_kernel<4><<<grid, kAttThreads, smem, s>>>(q, kh, vh, part, nh, nkv, hd, ctx, S);
-    } else {
-        cudaFuncSetAttribute(attn_partial_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attn_partial_kernel<8><<<grid, kAttThreads, smem, s>>>(q, kh, vh, part, nh, nkv, hd, ctx, S);
-    }
+    launch_split(hd, grp, grid, s, q, kh, vh, part, nh, nkv, ctx, S);
     attn_merge_kernel<<<batch * nh, std::min(hd, 256), 0, s>>>(part, out, nh, hd, S);
     e = cudaGetLastError();
     if (e != cudaSuccess) {
