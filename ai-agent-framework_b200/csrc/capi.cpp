@@ -422,7 +422,7 @@ int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, fl
 int b2_trace_step(b2_model* m, int32_t token, int64_t* out_ns, int64_t cap, int32_t* n_phases, int32_t* n_ctas) {
     if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
     if (!out_ns || !n_phases || !n_ctas) return ret(B2_ERR_BAD_ARG, "null argument");
-    const int P = b2::kPhasesPerLayer * m->dev.L + 1;
+    const int P = b2::kPhasesPerLayer * m->dev.L + m->dev.n_lm;
     const int64_t need = (int64_t)P * b2::kTraceSlots * m->grid;
     *n_phases = P;
     *n_ctas = m->grid;

@@ -60,6 +60,7 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 struct TGeom {
     int kind;
     int layer;
+    int sub;            // lm_head sub-phase
     const uint8_t* w;
     int rows;           // real matrix rows
     int tiles;          // ceil(rows / kTileRows)
@@ -68,9 +69,10 @@ struct TGeom {
 
 __device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const LayerDev* layers, int p) {
     TGeom g{};
-    if (p == kPhasesPerLayer * m.L) {
+    if (p >= kPhasesPerLayer * m.L) {
         g.kind = PH_LMHEAD;
         g.layer = m.L;
+        g.sub = p - kPhasesPerLayer * m.L;
         g.w = m.lm_head;
         g.rows = m.V;
         g.nb = m.H / 32;
@@ -91,7 +93,7 @@ __device__ __forceinline__ TGeom phase_geom(const ModelDev& m, const LayerDev* l
 
 // This CTA's work plan in weight phase g (precomputed on the host).
 __device__ __forceinline__ TPlan phase_plan(const TPlan* plans, const TGeom& g, int S) {
-    return plans[plan_slot(g.kind, S)];
+    return plans[plan_slot(g.kind, g.kind == PH_LMHEAD ? g.sub : S)];
 }
 
 // The matvec entry point's single phase: rows of a ggml-layout matrix.
@@ -1260,8 +1262,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
         sync_alive();
         if (TR && a.trace && ct == 0) a.trace[(tr + 2) * grid + cta] = global_ns();
 
-        float* yb = ybuf + ((p & 1) ? m.ybuf_floats : 0);  // parity buffers: the next phase's
-                                                      // dots may start before this epilogue ends
+        // parity buffers (even phases' one first, sized for the lm_head); every
+        // lm_head sub-phase uses the even one, whatever its parity (the stage
+        // barrier of each phase orders its dots after the previous epilogue)
+        float* yb = ybuf + (((p & 1) && g.kind != PH_LMHEAD) ? m.ybuf_floats : 0);
         const int rc = kTileRows * pl.n;  // outputs of one K-slice in yb
         {
             // 2. rows: tensor-core dot products of this CTA's tiles into yb
@@ -1499,6 +1503,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                             const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
                             atomicMax(m.am_key, ((unsigned long long)ord << 32) | (uint32_t)~(uint32_t)b.i);
                         }
+                        // (the arrivals, and the key's read and reset, in the last sub-phase)
+                        if (g.sub == m.n_lm - 1) {
                         __threadfence();
                         const unsigned old = atom_acq_rel_add(m.am_ctr, 1u);
                         if (old == (unsigned)(grid - 1)) {
@@ -1535,6 +1541,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                             if (a.out_ids) a.out_ids[a.step] = f;
                             if (a.done && f == a.eos) *a.done = 1;
                             atomicExch(m.am_ctr, 0u);
+                        }
                         }
                     }
                     break;

@@ -215,13 +215,19 @@ void qa_tiles(int nh, int hd, int qd, int kvd, int S, int cta, int grid, int* u0
 }
 
 // Work plans of one CTA, computed on the host at load time (no divisions in
-// the kernel): Wo, gate/up, down, lm_head, then QA for S = 1 .. kMaxSplits.
-constexpr int kPlanSlots = 4 + kMaxSplits;
+// the kernel): Wo, gate/up, down, the lm_head's sub-phases 0 .. kMaxLmSub - 1
+// (consecutive parts of the CTA's lm_head tiles, so that one part's K-slice
+// results fit the phase buffer), then QA for S = 1 .. kMaxSplits.
+constexpr int kMaxLmSub = 8;
+constexpr int kPlanSlots = 3 + kMaxLmSub + kMaxSplits;
+// S: the QA phase's split count (1 ..), or the lm_head's sub-phase (0 ..)
 inline
 #ifdef __CUDACC__
 __host__ __device__
 #endif
-int plan_slot(int kind, int S) { return kind == PH_QA ? 4 + S - 1 : kind - 1; }
+int plan_slot(int kind, int S) {
+    return kind == PH_QA ? 3 + kMaxLmSub + S - 1 : (kind == PH_LMHEAD ? 3 + S : kind - 1);
+}
 
 struct LayerDev {
     const uint8_t* wqkv;  // tiled [(qd + 2*kvd) rows][H]: Wq rows, then Wk, then Wv
@@ -246,6 +252,7 @@ struct ModelDev {
     int cfloats;              // phase constants: norm gains, QKV bias, RoPE row
     int attn_tile;            // positions per attention tile
     int qa_dist;              // QA rows spread over all CTAs (q published, read back by the q CTAs)
+    int n_lm;                 // lm_head sub-phases (phases 4L .. 4L + n_lm - 1)
     int nbx;                  // 32-blocks of the widest phase input (xq planes)
     const TPlan* plans;       // [grid][kPlanSlots] work plans (plan_slot)
     int Vp;                   // lm_head rows (this rank's vocab share) rounded up to kTileRows

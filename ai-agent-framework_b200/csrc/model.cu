@@ -214,7 +214,7 @@ int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err)
         a.pos = m->cache_len + i;
         a.p_begin = 0;
         // transformer.go:545-555: logits are needed for the last token only.
-        a.p_end = (i == n - 1) ? P + 1 : P;
+        a.p_end = (i == n - 1) ? P + m->dev.n_lm : P;
         a.epoch = ++m->epoch;
         a.skew = m->wait_skew;
         m->wait_skew = 0;
@@ -240,7 +240,7 @@ int run_traced_step(b2_model* m, int32_t token, unsigned long long* d_trace, std
     a.tok = m->d_tokens;
     a.pos = m->cache_len;
     a.p_begin = 0;
-    a.p_end = kPhasesPerLayer * m->dev.L + 1;
+    a.p_end = kPhasesPerLayer * m->dev.L + m->dev.n_lm;
     a.epoch = ++m->epoch;
     a.splits = splits_for(m, a.pos);
     a.trace = d_trace;
@@ -271,7 +271,7 @@ int run_greedy(b2_model* m, int32_t first, int n_steps, int32_t eos, int32_t* ou
         a.tok = (i == 0) ? m->d_tokens : m->dev.token;
         a.pos = m->cache_len + i;
         a.p_begin = 0;
-        a.p_end = P + 1;
+        a.p_end = P + m->dev.n_lm;
         a.epoch = ++m->epoch;
         a.skew = m->wait_skew;
         m->wait_skew = 0;
@@ -740,24 +740,55 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             qa_need = std::max(qa_need, pl.nks * kTileRows * pl.n);
             qa_rows = std::max(qa_rows, kTileRows * n);
         }
+    // The lm_head's share of a CTA, cut into n_lm consecutive sub-phases: the
+    // K-slice results of one sub-phase must fit the phase buffer.
+    const int lm_tiles = (int)(tiled_rows(Vl) / kTileRows);
+    auto lm_plan = [&](int cta, int sub, int n_lm) {
+        const int u0 = (int)((long long)cta * lm_tiles / m->grid);
+        const int n = (int)((long long)(cta + 1) * lm_tiles / m->grid) - u0;
+        const int a = u0 + (int)((long long)sub * n / n_lm), b = u0 + (int)((long long)(sub + 1) * n / n_lm);
+        return tile_plan_range(a, b - a, H / 32, tbb1, slot, kConsumerWarps);
+    };
+    auto lm_need = [&](int n_lm) {
+        int need = 0;
+        for (int cta = 0; cta < m->grid; cta++)
+            for (int sub = 0; sub < n_lm; sub++) {
+                const TPlan pl = lm_plan(cta, sub, n_lm);
+                need = std::max(need, pl.nks * kTileRows * pl.n);
+            }
+        return need;
+    };
     // even phases (QA, gate/up, LM head) and odd phases (Wo, down) alternate
     // between two buffers, so the next phase's dots may start before this
     // phase's epilogue ends
-    const int ybuf_even = (std::max(std::max(qa_need, ybuf_need(2 * FFl, H / 32, false)), ybuf_need(Vl, H / 32, false)) +
-                           31) & ~31;
+    const int even_layers = std::max(qa_need, ybuf_need(2 * FFl, H / 32, false));
     const int ybuf_odd = (std::max(ybuf_need(H, qdl / 32, true), ybuf_need(H, FFl / 32, true)) + 31) & ~31;
+    const int cfloats = cb_floats(hd);
+    const int xs = (base_xs + 31) & ~31, max_splits = split_cap;
+    auto ring_slots = [&](int ybuf_total) {
+        int n = 0;
+        while (n < 32 &&
+               smem_offsets(n + 1, slot, xs, ybuf_total, cfloats, std::max(std::max(H, qdl), FFl) / 32, L).total <= 232448u)
+            n++;
+        return n;
+    };
+    // fewest lm_head sub-phases that leave 8 ring slots (each one more costs a
+    // gather of the final norm's input)
+    int n_lm = 1, ybuf_even = 0, ns = 0;
+    for (int k = 1; k <= kMaxLmSub; k++) {
+        const int ev = (std::max(even_layers, lm_need(k)) + 31) & ~31;
+        const int nsk = ring_slots(ev + ybuf_odd);
+        if (k == 1 || nsk > ns) {
+            n_lm = k;
+            ybuf_even = ev;
+            ns = nsk;
+        }
+        if (ns >= 8) break;
+    }
     const int ybuf = ybuf_even + ybuf_odd;
     const auto rows_per_cta = [&](int rows) {
         return kTileRows * (int)((tiled_rows(rows) / kTileRows + m->grid - 1) / m->grid);
     };
-    const int cfloats = cb_floats(hd);
-    auto ring_slots = [&](int xs_f) {
-        int n = 0;
-        while (n < 32 && smem_offsets(n + 1, slot, xs_f, ybuf, cfloats, std::max(std::max(H, qdl), FFl) / 32, L).total <= 232448u) n++;
-        return n;
-    };
-    const int xs = (base_xs + 31) & ~31, max_splits = split_cap;
-    const int ns = ring_slots(xs);
     if (ns < 2) return bail(B2_ERR_UNSUPPORTED_TYPE, "rows too wide for the shared-memory ring");
     if (rows_per_cta(H) > kMaxOwnRows) return bail(B2_ERR_UNSUPPORTED_TYPE, "hidden size too large for one GPU");
     if (qa_rows > kMaxQkvRows || nhl >= m->grid)
@@ -765,13 +796,12 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // every CTA's work plans (plan_slot order), so the kernel needs no divisions
     {
         std::vector<TPlan> plans((size_t)m->grid * kPlanSlots, TPlan{0, 0, 1, 1, 1, 0});
-        const int Vp = (int)tiled_rows(Vl);
         for (int cta = 0; cta < m->grid; cta++) {
             TPlan* pc = plans.data() + (size_t)cta * kPlanSlots;
             pc[plan_slot(PH_WO, 1)] = own_plan(H / kTileRows, qdl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             pc[plan_slot(PH_GATEUP, 1)] = tile_plan(2 * FFl / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             pc[plan_slot(PH_DOWN, 1)] = own_plan(H / kTileRows, FFl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
-            pc[plan_slot(PH_LMHEAD, 1)] = tile_plan(Vp / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            for (int sub = 0; sub < n_lm; sub++) pc[plan_slot(PH_LMHEAD, sub)] = lm_plan(cta, sub, n_lm);
             for (int S = 1; S <= kMaxSplits && nhl * S < m->grid; S++) {
                 int u0 = 0, n = 0;
                 qa_tiles(nhl, hd, qdl, kvdl, S, cta, m->grid, &u0, &n, qa_dist);
@@ -782,6 +812,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         d.plans = reinterpret_cast<const TPlan*>(A + off_plans);
     }
     d.xs_floats = xs;
+    d.n_lm = n_lm;
     d.ybuf_floats = ybuf_even;
     d.ybuf_odd = ybuf_odd;
     d.cfloats = cfloats;
