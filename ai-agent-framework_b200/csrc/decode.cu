@@ -949,8 +949,93 @@ __device__ __noinline__ int merge_planes(const uint2* part, int nbk, int S, int 
 // the kernel
 // ---------------------------------------------------------------------------
 
+// Tensor parallel, after the Wo or the down dots: this rank's partial sums of
+// residual rows row0 .. row0 + n (K-slices summed from the phase buffer at
+// shared offset yb_off, rc = n outputs per slice) go to slot [tp_rank] of
+// every rank's exchange region xo (peer stores over NVLink); then the N
+// ranks' partials of these rows are read back from this rank's own buffer and
+// added to the residual (shared offset xres_off) in rank order, so every rank
+// holds the same residual stream; the sums are published as LL words.
+// Returns 0 if a partial never came (error flag set).  Not inlined (the
+// one-GPU path does not carry its code and registers).
+__device__ __noinline__ int tp_reduce_rows(const ModelDev& m, size_t xo, int row0, int n, int nks, uint32_t yb_off,
+                                           uint32_t xres_off, uint2* dstll, unsigned tag) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const float* yb = reinterpret_cast<const float*>(smem + yb_off);
+    float* xres = reinterpret_cast<float*>(smem + xres_off);
+    const int ct = threadIdx.x - 32;
+    const size_t mine = xo + ((size_t)m.tp_rank * m.H + row0) * 8;
+    int ok = 1;
+#pragma unroll 1
+    for (int j = ct; j < n; j += kConsumerThreads) {
+        float d = yb[j];
+#pragma unroll 1
+        for (int ks = 1; ks < nks; ks++) d += yb[ks * n + j];
+#pragma unroll 1
+        for (int q = 0; q < m.tp; q++) ll_store_sys(reinterpret_cast<uint2*>(m.xpeer[q] + mine) + j, d, tag);
+    }
+#pragma unroll 1
+    for (int j = ct; j < n; j += kConsumerThreads) {
+        float xr = xres[j];
+#pragma unroll 1
+        for (int q = 0; q < m.tp && ok; q++) {
+            const uint2* src = reinterpret_cast<const uint2*>(m.xpeer[m.tp_rank] + xo + ((size_t)q * m.H + row0) * 8) + j;
+            uint64_t w0 = 0;
+            for (;;) {
+                const uint2 w = ll_load_sys(src);
+                if (w.y == tag) {
+                    xr += __uint_as_float(w.x);
+                    break;
+                }
+                const uint64_t now = global_ns();
+                if (w0 == 0) w0 = now;
+                if (now - w0 > kWaitLimitNs) {
+                    set_err(m.err, B2_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+                if (*(volatile int*)m.err) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        xres[j] = xr;
+        ll_store(dstll + row0 + j, xr, tag);
+    }
+    return ok;
+}
+
+// Tensor parallel, the lm_head's last CTA: this rank's argmax key goes to
+// every rank's exchange buffer; returns the largest of all ranks' keys (the
+// same on every rank).
+__device__ __noinline__ unsigned long long tp_argmax_key(const ModelDev& m, unsigned long long key, unsigned tag) {
+    const size_t xa = xch_am(m.H, m.tp);
+    const uint4 kw = make_uint4((uint32_t)(key >> 32), tag, (uint32_t)key, tag);
+    for (int q = 0; q < m.tp; q++) st4_sys(reinterpret_cast<uint4*>(m.xpeer[q] + xa) + m.tp_rank, kw);
+    const uint4* mine = reinterpret_cast<const uint4*>(m.xpeer[m.tp_rank] + xa);
+    for (int q = 0; q < m.tp; q++) {
+        uint64_t w0 = 0;
+        for (;;) {
+            const uint4 w = ld4_sys(mine + q);
+            if (w.y == tag && w.w == tag) {
+                const unsigned long long kq = ((unsigned long long)w.x << 32) | w.z;
+                if (kq > key) key = kq;
+                break;
+            }
+            const uint64_t now = global_ns();
+            if (w0 == 0) w0 = now;
+            if (now - w0 > kWaitLimitNs || *(volatile int*)m.err) {
+                set_err(m.err, B2_ERR_TIMEOUT);
+                break;
+            }
+        }
+    }
+    return key;
+}
+
 template <int QT, bool MV, bool TR, bool KV32>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, const StepArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ ModelDev m, const StepArgs a) {
     constexpr int US = QT == 8 ? 16 : 32;  // matvec: values per lane unit
     constexpr int QB = QT == 8 ? 32 : 16;  // tiled: quant bytes per row and block
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1419,48 +1504,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                     // exactly the residual rows this CTA owns
                     uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
                     if (m.tp > 1) {
-                        // tensor parallel: this rank's partial sums of these rows go to
-                        // every rank's exchange buffer (peer stores over NVLink), then
-                        // the partials of all ranks are added in rank order, so every
-                        // rank holds the same residual stream
-                        const size_t xo = g.kind == PH_WO ? 0 : xch_dn(m.H, m.tp);
-                        const size_t mine = xo + ((size_t)m.tp_rank * m.H + row0) * 8;
-                        #pragma unroll 1
-                        for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
-                            const float d = ysum(j);
-                            #pragma unroll 1
-                            for (int q = 0; q < m.tp; q++) ll_store_sys(reinterpret_cast<uint2*>(m.xpeer[q] + mine) + j, d, tag);
-                        }
-                        #pragma unroll 1
-                        for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
-                            float xr = xres[j];
-                            #pragma unroll 1
-                            for (int q = 0; q < m.tp && alive; q++) {
-                                const uint2* src = reinterpret_cast<const uint2*>(
-                                    m.xpeer[m.tp_rank] + xo + ((size_t)q * m.H + row0) * 8) + j;
-                                uint64_t w0 = 0;
-                                for (;;) {
-                                    const uint2 w = ll_load_sys(src);
-                                    if (w.y == tag) {
-                                        xr += __uint_as_float(w.x);
-                                        break;
-                                    }
-                                    const uint64_t now = global_ns();
-                                    if (w0 == 0) w0 = now;
-                                    if (now - w0 > kWaitLimitNs) {
-                                        set_err(m.err, B2_ERR_TIMEOUT);
-                                        alive = false;
-                                        break;
-                                    }
-                                    if (*(volatile int*)m.err) {
-                                        alive = false;
-                                        break;
-                                    }
-                                }
-                            }
-                            xres[j] = xr;
-                            ll_store(dstll + row0 + j, xr, tag);
-                        }
+                        if (!tp_reduce_rows(m, g.kind == PH_WO ? 0 : xch_dn(m.H, m.tp), row0, kTileRows * pl.n, pl.nks,
+                                            smem_u32(yb), smem_u32(xres), dstll, tag))
+                            alive = false;
                         break;
                     }
                     #pragma unroll 1
@@ -1510,32 +1556,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const ModelDev m, c
                         if (old == (unsigned)(grid - 1)) {
                             // last CTA: every other CTA's max is in am_key
                             unsigned long long key = atomicExch(m.am_key, 0ull);
-                            if (m.tp > 1) {
-                                // every rank's key to every rank, then the largest of all
-                                // (the same on every rank)
-                                const size_t xa = xch_am(m.H, m.tp);
-                                const uint4 kw = make_uint4((uint32_t)(key >> 32), tag, (uint32_t)key, tag);
-                                for (int q = 0; q < m.tp; q++)
-                                    st4_sys(reinterpret_cast<uint4*>(m.xpeer[q] + xa) + m.tp_rank, kw);
-                                const uint4* mine = reinterpret_cast<const uint4*>(m.xpeer[m.tp_rank] + xa);
-                                for (int q = 0; q < m.tp; q++) {
-                                    uint64_t w0 = 0;
-                                    for (;;) {
-                                        const uint4 w = ld4_sys(mine + q);
-                                        if (w.y == tag && w.w == tag) {
-                                            const unsigned long long kq = ((unsigned long long)w.x << 32) | w.z;
-                                            if (kq > key) key = kq;
-                                            break;
-                                        }
-                                        const uint64_t now = global_ns();
-                                        if (w0 == 0) w0 = now;
-                                        if (now - w0 > kWaitLimitNs || *(volatile int*)m.err) {
-                                            set_err(m.err, B2_ERR_TIMEOUT);
-                                            break;
-                                        }
-                                    }
-                                }
-                            }
+                            if (m.tp > 1) key = tp_argmax_key(m, key, tag);
                             const int f = key ? (int)~(uint32_t)key : 0;
                             *m.token = f;
                             if (a.out_ids) a.out_ids[a.step] = f;
