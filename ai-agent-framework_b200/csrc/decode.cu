@@ -956,6 +956,8 @@ __device__ __noinline__ int merge_planes(const uint2* part, int nbk, int S, int 
 // ranks' partials of these rows are read back from this rank's own buffer and
 // added to the residual (shared offset xres_off) in rank order, so every rank
 // holds the same residual stream; the sums are published as LL words.
+// yb_off and xres_off are byte offsets from the dynamic shared array (not
+// shared-window addresses: the array does not start at address 0).
 // Returns 0 if a partial never came (error flag set).  Not inlined (the
 // one-GPU path does not carry its code and registers).
 __device__ __noinline__ int tp_reduce_rows(const ModelDev& m, size_t xo, int row0, int n, int nks, uint32_t yb_off,
@@ -1504,8 +1506,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                     // exactly the residual rows this CTA owns
                     uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
                     if (m.tp > 1) {
+                        // (byte offsets from the dynamic shared array, like every helper's)
                         if (!tp_reduce_rows(m, g.kind == PH_WO ? 0 : xch_dn(m.H, m.tp), row0, kTileRows * pl.n, pl.nks,
-                                            smem_u32(yb), smem_u32(xres), dstll, tag))
+                                            (uint32_t)(reinterpret_cast<uint8_t*>(yb) - smem),
+                                            (uint32_t)(reinterpret_cast<uint8_t*>(xres) - smem), dstll, tag))
                             alive = false;
                         break;
                     }
