@@ -158,7 +158,9 @@ int b2_embed(b2_model* m, const int32_t* tokens, int32_t n, float* out);
 
 /* gguf.go:491-508 Dequantize of one named tensor, decoded on the device from
  * the resident blocks (Q4_0 in the ggml element order).  n = capacity of out
- * in floats; returns 0 and writes *n_out elements. */
+ * in floats; returns 0 and writes *n_out elements.  On a tensor-parallel rank
+ * a sharded tensor yields this rank's share (its rows, or its columns of each
+ * row, in the order of the GGUF tensor). */
 int b2_dequant_tensor(const b2_model* m, const char* name, float* out, int64_t n, int64_t* n_out);
 
 /* transformer.go:810-865 matVecMulQ8Chunk over all rows, on the device:
