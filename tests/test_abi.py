@@ -106,3 +106,33 @@ def test_host_sampler_matches_go_sample(built_lib, oracle_lib, seed):
             want = goref.sample(lg, temp, k, p, rp, gen, r)
             got = b2decode.sample_logits(lg, b2decode.sample_opts(temp, k, p, rp), gen, r)
             assert got == want, (temp, k, p, rp, r)
+
+
+def _tp_load_err(path, tp_size, tp_rank):
+    try:
+        b2decode.Model(path, tp_size=tp_size, tp_rank=tp_rank)
+    except b2decode.B2Error as e:
+        return e.code, str(e)
+    return 0, ""
+
+
+def test_tensor_parallel_options_checked_before_any_device_work(built_lib, tiny_gguf):
+    # degree above 8, rank outside the degree: bad arguments
+    assert _tp_load_err(tiny_gguf, 9, 0)[0] == -8
+    assert _tp_load_err(tiny_gguf, 2, 2)[0] == -8
+    assert _tp_load_err(tiny_gguf, 2, -1)[0] == -8
+    # the tiny model has 2 KV heads: 4 ranks cannot share them
+    code, msg = _tp_load_err(tiny_gguf, 4, 1)
+    assert code == -3 and "divisible" in msg
+
+
+@pytest.mark.skipif(has_gpu(), reason="the CPU-only path")
+def test_tensor_parallel_load_needs_a_gpu(built_lib, tiny_gguf):
+    code, msg = _tp_load_err(tiny_gguf, 2, 1)
+    assert code == -5 and "no CUDA device" in msg
+
+
+def test_tp_entry_points_reject_null(built_lib):
+    L = b2decode.lib()
+    assert L.b2_tp_handle(None, b"\0" * 64) == -10
+    assert L.b2_tp_connect(None, b"\0" * 64) == -10
