@@ -178,3 +178,19 @@ def test_embed_restatement(oracle_lib, tiny_gguf):
     e *= np.float32(1.0 / len(toks))
     e /= np.float32(np.sqrt(np.float64((e * e).sum(dtype=np.float32))))
     assert np.isfinite(e).all() and abs(np.linalg.norm(e) - 1) < 1e-5
+
+
+def test_writer_command_line_writes_the_same_bytes(tmp_path):
+    """The writer's command line (a process pool, used by the bench for the
+    multi-GB shapes) writes the same file as the in-process writer."""
+    import subprocess
+    import sys
+    pkg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "ai-agent-framework_b200")
+    out = tmp_path / "cli.gguf"
+    r = subprocess.run([sys.executable, "-m", "b2decode.gguf_writer", "tiny-llama-q4", str(out), "--workers", "2"],
+                       env=dict(os.environ, PYTHONPATH=pkg), capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    ref = gw.write_model(str(tmp_path / "lib.gguf"), gw.SHAPES["tiny-llama-q4"], seed=0)
+    size, digest = r.stdout.split()
+    assert int(size) == ref["bytes"] and digest == ref["sha256"]
+    assert out.read_bytes() == (tmp_path / "lib.gguf").read_bytes()
