@@ -96,6 +96,7 @@ SIGNATURES = {
     "b2_embed": (C.c_int, [_P, _i32p, _i32, _f32p]),
     "b2_dequant_tensor": (C.c_int, [_P, C.c_char_p, _f32p, _i64, C.POINTER(_i64)]),
     "b2_matvec": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _P]),
+    "b2_matvec_batch": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _i32, _P]),
     "b2_attention_decode": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_attention_decode_noalloc": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_device_status": (C.c_int, [_P]),
@@ -285,6 +286,12 @@ def sample_logits(logits, opts: SampleOpts, generated=(), r: float = 0.5) -> int
 def matvec(qtype: int, w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:
     """y = W x on the device; pointers are device addresses (e.g. tensor.data_ptr())."""
     _check(lib().b2_matvec(qtype, w_ptr, x_ptr, y_ptr, rows, cols, stream or None))
+
+
+def matvec_batch(qtype: int, w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, nvec: int,
+                 stream: int = 0) -> None:
+    """Y = W X for nvec (1..8) vectors in one pass over W: x [nvec][cols], y [nvec][rows] fp32, device addresses."""
+    _check(lib().b2_matvec_batch(qtype, w_ptr, x_ptr, y_ptr, rows, cols, nvec, stream or None))
 
 
 def attention_decode(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, nh: int, nkv: int, hd: int,

@@ -15,6 +15,8 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
 void b2_free_impl(b2_model* m);
 int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows, int cols, cudaStream_t s,
                    std::string* err);
+int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int rows, int cols, int nvec,
+                         cudaStream_t s, std::string* err);
 int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh, int nkv,
                       int hd, int ctx, cudaStream_t s, std::string* err);
 int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh,
@@ -407,6 +409,17 @@ int b2_matvec(int32_t qtype, const void* w, const float* x, float* y, int32_t ro
     if (qtype != 8 && qtype != 2) return ret(B2_ERR_UNSUPPORTED_TYPE, "qtype must be 8 (Q8_0) or 2 (Q4_0)");
     std::string err;
     int rc = b2_matvec_impl(qtype, w, x, y, rows, cols, static_cast<cudaStream_t>(stream), &err);
+    return ret(rc, err);
+}
+
+int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int32_t rows, int32_t cols,
+                    int32_t nvec, void* stream) {
+    if (!w || !x || !y || rows <= 0 || cols <= 0) return ret(B2_ERR_BAD_ARG, "bad matvec arguments");
+    if (cols % 256) return ret(B2_ERR_BAD_ARG, "batched matvec needs cols to be a multiple of 256");
+    if (nvec < 1 || nvec > 8) return ret(B2_ERR_BAD_ARG, "batched matvec takes 1 to 8 vectors");
+    if (qtype != 8 && qtype != 2) return ret(B2_ERR_UNSUPPORTED_TYPE, "qtype must be 8 (Q8_0) or 2 (Q4_0)");
+    std::string err;
+    int rc = b2_matvec_batch_impl(qtype, w, x, y, rows, cols, nvec, static_cast<cudaStream_t>(stream), &err);
     return ret(rc, err);
 }
 

@@ -1,0 +1,468 @@
+// Batched dequantising matvec: Y = W X for up to eight fp32 vectors in one
+// pass over a GGUF-layout Q8_0 / Q4_0 matrix.
+//
+// The reference evaluates one vector at a time (transformer.go:810-865
+// matVecMulQ8Chunk, driven over row ranges by matVecMulQ8Pooled at
+// transformer.go:868-892: per 32-block, q * d against x in fp32; Q4_0 blocks
+// take the same dot with (q - 8) * d, the ggml block layout).  Here the weights stream from HBM once for
+// all vectors and the products run on the int8 tensor-core path:
+//
+//   * Each vector is split per 32-block into three int8 planes,
+//     x ~= s * (p0 + p1 / 2^7 + p2 / 2^14) with s = max|x| / 127 (about 22
+//     bits of precision relative to the block maximum, i.e. fp32-grade
+//     dots).  The planes sit in global memory in the B-fragment order of
+//     mma.m16n8k32, one column per vector, one mma per plane.
+//   * A warp owns a unit = (16-row tile, slice of the 32-blocks).  Its raw
+//     GGUF row bytes stream through warp-private shared-memory stages filled
+//     with cp.async (16 B, L1-bypassing); the fragments are read from the raw
+//     34- / 18-byte blocks with aligned 32-bit loads and byte permutes.
+//   * Each 32-block gives, per plane, the exact int32 dot in an accumulator
+//     started at the float bits of 1.5 * 2^23 (Q4_0: minus 8 * the plane
+//     sum, so (q - 8) . p comes out), read back with one subtraction, then
+//     scaled by d_w * s_x and accumulated in fp32.
+//   * With fewer tiles than warps the blocks are split into KS slices; every
+//     unit writes its partial sums and the last unit of a tile to arrive
+//     (an atomic counter, reset by that unit) adds the slices in slice
+//     order, so results do not depend on timing.
+//
+// Nothing in this file waits on a flag: the only waits are cp.async
+// completions of the warp's own copies.
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/b2decode.h"
+#include "dev.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kMvbVec = 8;                    // vectors per pass (mma N)
+constexpr int kMvbWarps = 8;                  // warps per CTA
+constexpr int kMvbThreads = kMvbWarps * 32;
+constexpr int kMvbKc = 8;                     // 32-blocks per chunk
+constexpr int kMvbMaxSlices = 8;
+constexpr uint32_t kMvbMagic = 0x4B400000u;   // 1.5 * 2^23 as float bits
+constexpr float kMvbMagicF = 12582912.0f;
+
+template <int QT> struct MvbGeom {
+    static constexpr int bpb = QT == 8 ? 34 : 18;        // bytes per 32-block
+    static constexpr int rc = kMvbKc * bpb;              // row bytes of one chunk (16-B multiple)
+    static constexpr int tile = 16 * rc;                 // one stage: 16 rows of one chunk
+    static constexpr int stages = QT == 8 ? 3 : 5;
+    static constexpr int smem = kMvbWarps * stages * tile;
+};
+
+// Byte position of element k (0..31) of vector v inside one plane record
+// (256 bytes = 32 lanes x the 8 bytes of their B fragment {b0, b1}).
+// Lane (g, t) holds column g; Q4_0 keeps the natural k slots of the fragment
+// (b0: k = 4t..4t+3, b1: 16+4t..), Q8_0 assigns lane t the eight contiguous
+// elements 8t..8t+7 (b0 then b1), which its A operand mirrors.
+template <int QT> __device__ __forceinline__ int plane_pos(int v, int k) {
+    if (QT == 8) return v * 32 + k;
+    const int kk = k & 15;
+    return v * 32 + 8 * (kk >> 2) + (k >= 16 ? 4 : 0) + (kk & 3);
+}
+
+// One warp per (32-block kb, vector v): lane = element.  Vectors v >= nvec
+// become zero planes with scale 0.  xst (Q4_0 only) holds, per block and
+// plane, the accumulator start 1.5 * 2^23 - 8 * sum(plane) of each vector.
+template <int QT>
+__global__ void __launch_bounds__(kMvbThreads)
+    mvb_planes_kernel(const float* __restrict__ x, int nvec, int cols, uint8_t* __restrict__ planes,
+                      float* __restrict__ xsc, uint32_t* __restrict__ xst) {
+    const int kb = blockIdx.x, v = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float val = v < nvec ? x[(size_t)v * cols + (size_t)kb * 32 + lane] : 0.0f;
+    float amax = fabsf(val);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+    const float M = kMvbMagicF;
+    const float q = val * inv;
+    const float f0 = q + M, r0 = f0 - M;
+    const float q1 = (q - r0) * 128.0f;
+    const float f1 = q1 + M, r1 = f1 - M;
+    const float f2 = (q1 - r1) * 128.0f + M, r2 = f2 - M;
+    const int pos = plane_pos<QT>(v, lane);
+    uint8_t* rec = planes + (size_t)kb * 3 * 256;
+    rec[pos] = (uint8_t)__float_as_uint(f0);
+    rec[256 + pos] = (uint8_t)__float_as_uint(f1);
+    rec[512 + pos] = (uint8_t)__float_as_uint(f2);
+    if (lane == 0) xsc[kb * kMvbVec + v] = amax * (1.0f / 127.0f);
+    if (QT != 8) {
+        int s0 = (int)r0, s1 = (int)r1, s2 = (int)r2;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+        if (lane == 0) {
+            uint32_t* st = xst + (size_t)kb * 3 * kMvbVec + v;
+            st[0] = kMvbMagic - 8u * (uint32_t)s0;
+            st[kMvbVec] = kMvbMagic - 8u * (uint32_t)s1;
+            st[2 * kMvbVec] = kMvbMagic - 8u * (uint32_t)s2;
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <bool U4>
+__device__ __forceinline__ void mma_i8(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                                       uint32_t c0, uint32_t c1, uint32_t& d0, uint32_t& d1, uint32_t& d2,
+                                       uint32_t& d3) {
+    if (U4) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%10, %11, %12, %13};"
+            : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c0), "r"(c1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+            "{%10, %11, %12, %13};"
+            : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3)
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1), "r"(c0), "r"(c1));
+    }
+}
+
+// Two A-operand words of one row of block b from its raw bytes in shared
+// memory (blk = the block's first byte, the fp16 scale).  Q8_0: elements
+// 8t..8t+7 (quants start 2 bytes in); Q4_0: the nibble bytes 4t..4t+3,
+// low nibbles = elements 4t.., high nibbles = 16+4t..  A stage row starts
+// on a 16-byte boundary, so the quants of even blocks start 2 bytes off a
+// 4-byte boundary: those read the aligned words around them and permute.
+template <int QT, int B>
+__device__ __forceinline__ void a_words(const uint8_t* blk, int t, uint32_t& lo, uint32_t& hi) {
+    if (QT == 8) {
+        if (B & 1) {
+            lo = *reinterpret_cast<const uint32_t*>(blk + 2 + 8 * t);
+            hi = *reinterpret_cast<const uint32_t*>(blk + 6 + 8 * t);
+        } else {
+            const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk + 8 * t);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t*>(blk + 4 + 8 * t);
+            const uint32_t w2 = *reinterpret_cast<const uint32_t*>(blk + 8 + 8 * t);
+            lo = __byte_perm(w0, w1, 0x5432);
+            hi = __byte_perm(w1, w2, 0x5432);
+        }
+    } else {
+        uint32_t w;
+        if (B & 1) {
+            w = *reinterpret_cast<const uint32_t*>(blk + 2 + 4 * t);
+        } else {
+            const uint32_t w0 = *reinterpret_cast<const uint32_t*>(blk + 4 * t);
+            const uint32_t w1 = *reinterpret_cast<const uint32_t*>(blk + 4 + 4 * t);
+            w = __byte_perm(w0, w1, 0x5432);
+        }
+        lo = w & 0x0F0F0F0Fu;
+        hi = (w >> 4) & 0x0F0F0F0Fu;
+    }
+}
+
+// The sequence of (unit, chunk) items of one warp: units u = first,
+// first + stride, ... in slice-major order (u = slice * ntiles + tile), the
+// chunks of the unit's slice in order.
+struct MvbIter {
+    int u, tile, slice, c, c1;
+    __device__ __forceinline__ void enter(int total, int ntiles, int nch, int ks) {
+        if (u >= total) return;
+        slice = u / ntiles;
+        tile = u - slice * ntiles;
+        c = (int)((long long)slice * nch / ks);
+        c1 = (int)((long long)(slice + 1) * nch / ks);
+    }
+    __device__ __forceinline__ void next(int stride, int total, int ntiles, int nch, int ks) {
+        if (++c < c1) return;
+        u += stride;
+        enter(total, ntiles, nch, ks);
+    }
+};
+
+template <int QT>
+__global__ void __launch_bounds__(kMvbThreads, 1)
+    mvb_kernel(const uint8_t* __restrict__ w, int rows, int rb, int nch, int ntiles, int ks,
+               const uint8_t* __restrict__ planes, const float* __restrict__ xsc, const uint32_t* __restrict__ xst,
+               float* __restrict__ y, int nvec, float* __restrict__ part, int* __restrict__ cnt) {
+    using G = MvbGeom<QT>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    uint8_t* stage0 = smem + (size_t)warp * G::stages * G::tile;
+    const uint32_t stage0_s = smem_u32(stage0);
+    const int stride = gridDim.x * kMvbWarps;
+    const int total = ntiles * ks;
+    const int rows_pad = ntiles * 16;
+
+    MvbIter pf, cs;
+    pf.u = blockIdx.x * kMvbWarps + warp;
+    pf.tile = pf.slice = pf.c = pf.c1 = 0;
+    pf.enter(total, ntiles, nch, ks);
+    cs = pf;
+
+    // 16-byte copies of one stage: 16 rows x G::rc / 16 pieces
+    constexpr int kPieces = G::rc / 16;
+    auto issue = [&](const MvbIter& it, int st) {
+        if (it.u < total) {
+            const uint32_t dst0 = stage0_s + (uint32_t)(st * G::tile);
+            const size_t coff = (size_t)it.c * G::rc;
+            for (int j = lane; j < 16 * kPieces; j += 32) {
+                const int row = j / kPieces, piece = j - row * kPieces;
+                const int r = min(it.tile * 16 + row, rows - 1);
+                cp_async16(dst0 + (uint32_t)(row * G::rc + piece * 16), w + (size_t)r * rb + coff + piece * 16);
+            }
+        }
+        cp_async_commit();
+    };
+
+#pragma unroll
+    for (int i = 0; i < G::stages - 1; i++) {
+        issue(pf, i);
+        pf.next(stride, total, ntiles, nch, ks);
+    }
+
+    const unsigned long long mneg = f2_pack(-kMvbMagicF, -kMvbMagicF);
+    const unsigned long long c7 = f2_pack(0.0078125f, 0.0078125f);
+    const unsigned long long c14 = f2_pack(6.103515625e-05f, 6.103515625e-05f);
+    unsigned long long acc_g = f2_pack(0.0f, 0.0f), acc_h = acc_g;
+    int st = 0;
+#pragma unroll 1
+    while (cs.u < total) {
+        issue(pf, st == 0 ? G::stages - 1 : st - 1);
+        pf.next(stride, total, ntiles, nch, ks);
+        cp_async_wait<G::stages - 1>();
+        __syncwarp();
+
+        const uint8_t* rg = stage0 + st * G::tile + g * G::rc;
+        const uint8_t* rh = rg + 8 * G::rc;
+        const int kb0 = cs.c * kMvbKc;
+#pragma unroll
+        for (int bb = 0; bb < kMvbKc; bb++) {
+            const int kb = kb0 + bb;
+            const uint2* rec = reinterpret_cast<const uint2*>(planes + (size_t)kb * 3 * 256) + lane;
+            const uint2 p0 = __ldg(rec), p1 = __ldg(rec + 32), p2 = __ldg(rec + 64);
+            const float2 sx = __ldg(reinterpret_cast<const float2*>(xsc + kb * kMvbVec + 2 * t));
+            uint32_t s0a = kMvbMagic, s0b = kMvbMagic, s1a = kMvbMagic, s1b = kMvbMagic, s2a = kMvbMagic,
+                     s2b = kMvbMagic;
+            if (QT != 8) {
+                const uint2* sp = reinterpret_cast<const uint2*>(xst + (size_t)kb * 3 * kMvbVec + 2 * t);
+                const uint2 v0 = __ldg(sp), v1 = __ldg(sp + 4), v2 = __ldg(sp + 8);
+                s0a = v0.x; s0b = v0.y; s1a = v1.x; s1b = v1.y; s2a = v2.x; s2b = v2.y;
+            }
+            const uint8_t* bg = rg + bb * G::bpb;
+            const uint8_t* bh = rh + bb * G::bpb;
+            uint32_t a0, a1, a2, a3;
+            switch (bb) {  // bb is a constant after unrolling: the parity picks the load pattern
+                case 0: a_words<QT, 0>(bg, t, a0, a2); a_words<QT, 0>(bh, t, a1, a3); break;
+                case 1: a_words<QT, 1>(bg, t, a0, a2); a_words<QT, 1>(bh, t, a1, a3); break;
+                case 2: a_words<QT, 2>(bg, t, a0, a2); a_words<QT, 2>(bh, t, a1, a3); break;
+                case 3: a_words<QT, 3>(bg, t, a0, a2); a_words<QT, 3>(bh, t, a1, a3); break;
+                case 4: a_words<QT, 4>(bg, t, a0, a2); a_words<QT, 4>(bh, t, a1, a3); break;
+                case 5: a_words<QT, 5>(bg, t, a0, a2); a_words<QT, 5>(bh, t, a1, a3); break;
+                case 6: a_words<QT, 6>(bg, t, a0, a2); a_words<QT, 6>(bh, t, a1, a3); break;
+                default: a_words<QT, 7>(bg, t, a0, a2); a_words<QT, 7>(bh, t, a1, a3); break;
+            }
+            const float dg = __half2float(*reinterpret_cast<const __half*>(bg));
+            const float dh = __half2float(*reinterpret_cast<const __half*>(bh));
+            uint32_t e0, e1, e2, e3, f0, f1, f2, f3, h0, h1, h2, h3;
+            mma_i8<QT != 8>(a0, a1, a2, a3, p0.x, p0.y, s0a, s0b, e0, e1, e2, e3);
+            mma_i8<QT != 8>(a0, a1, a2, a3, p1.x, p1.y, s1a, s1b, f0, f1, f2, f3);
+            mma_i8<QT != 8>(a0, a1, a2, a3, p2.x, p2.y, s2a, s2b, h0, h1, h2, h3);
+            const unsigned long long sxp = f2_pack(sx.x, sx.y);
+            // rows g (d0, d1) and g + 8 (d2, d3), vectors 2t and 2t + 1
+            unsigned long long tg = f2_add(f2_pack(__uint_as_float(e0), __uint_as_float(e1)), mneg);
+            tg = f2_fma(f2_add(f2_pack(__uint_as_float(f0), __uint_as_float(f1)), mneg), c7, tg);
+            tg = f2_fma(f2_add(f2_pack(__uint_as_float(h0), __uint_as_float(h1)), mneg), c14, tg);
+            unsigned long long th = f2_add(f2_pack(__uint_as_float(e2), __uint_as_float(e3)), mneg);
+            th = f2_fma(f2_add(f2_pack(__uint_as_float(f2), __uint_as_float(f3)), mneg), c7, th);
+            th = f2_fma(f2_add(f2_pack(__uint_as_float(h2), __uint_as_float(h3)), mneg), c14, th);
+            acc_g = f2_fma(f2_mul(f2_pack(dg, dg), sxp), tg, acc_g);
+            acc_h = f2_fma(f2_mul(f2_pack(dh, dh), sxp), th, acc_h);
+        }
+
+        if (cs.c + 1 == cs.c1) {
+            // unit done: rows tile*16 + g, + 8; vectors 2t, 2t + 1
+            const float2 vg = f2_unpack(acc_g), vh = f2_unpack(acc_h);
+            const int r0 = cs.tile * 16 + g, r1 = r0 + 8, v0 = 2 * t, v1 = v0 + 1;
+            if (ks == 1) {
+                if (r0 < rows) {
+                    if (v0 < nvec) y[(size_t)v0 * rows + r0] = vg.x;
+                    if (v1 < nvec) y[(size_t)v1 * rows + r0] = vg.y;
+                }
+                if (r1 < rows) {
+                    if (v0 < nvec) y[(size_t)v0 * rows + r1] = vh.x;
+                    if (v1 < nvec) y[(size_t)v1 * rows + r1] = vh.y;
+                }
+            } else {
+                float* ps = part + (size_t)cs.slice * kMvbVec * rows_pad;
+                ps[(size_t)v0 * rows_pad + r0] = vg.x;
+                ps[(size_t)v1 * rows_pad + r0] = vg.y;
+                ps[(size_t)v0 * rows_pad + r1] = vh.x;
+                ps[(size_t)v1 * rows_pad + r1] = vh.y;
+                __threadfence();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) last = atomicAdd(cnt + cs.tile, 1) == ks - 1;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __threadfence();
+                    float s00 = 0.0f, s01 = 0.0f, s10 = 0.0f, s11 = 0.0f;
+                    for (int s = 0; s < ks; s++) {
+                        const float* q = part + (size_t)s * kMvbVec * rows_pad;
+                        s00 += __ldcg(q + (size_t)v0 * rows_pad + r0);
+                        s01 += __ldcg(q + (size_t)v1 * rows_pad + r0);
+                        s10 += __ldcg(q + (size_t)v0 * rows_pad + r1);
+                        s11 += __ldcg(q + (size_t)v1 * rows_pad + r1);
+                    }
+                    if (r0 < rows) {
+                        if (v0 < nvec) y[(size_t)v0 * rows + r0] = s00;
+                        if (v1 < nvec) y[(size_t)v1 * rows + r0] = s01;
+                    }
+                    if (r1 < rows) {
+                        if (v0 < nvec) y[(size_t)v0 * rows + r1] = s10;
+                        if (v1 < nvec) y[(size_t)v1 * rows + r1] = s11;
+                    }
+                    if (lane == 0) cnt[cs.tile] = 0;  // every unit of the tile has arrived
+                }
+            }
+            acc_g = f2_pack(0.0f, 0.0f);
+            acc_h = acc_g;
+        }
+        __syncwarp();  // every lane is done with this stage before it is refilled
+        st = st + 1 == G::stages ? 0 : st + 1;
+        cs.next(stride, total, ntiles, nch, ks);
+    }
+    cp_async_wait<0>();
+}
+
+// Per-device scratch of the batched matvec: the per-tile arrival counters
+// (zero between calls: the last unit of a tile resets its counter), the x
+// planes, their scales and Q4_0 accumulator starts, the slice partials.
+// Calls that overlap on the GPU (different streams) race on it.
+struct MvbScratch {
+    uint8_t* buf = nullptr;
+    size_t bytes = 0;
+    int sms = 0;
+    bool attr_set = false;
+};
+std::mutex g_mvb_mu;
+std::vector<MvbScratch> g_mvb;
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int rows, int cols, int nvec,
+                         cudaStream_t s, std::string* err) {
+    if (reinterpret_cast<uintptr_t>(w) & 15) {
+        *err = "weight pointer must be 16-byte aligned";
+        return B2_ERR_BAD_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(x) & 3 || reinterpret_cast<uintptr_t>(y) & 3) {
+        *err = "x and y must be 4-byte aligned";
+        return B2_ERR_BAD_ARG;
+    }
+    const bool q8 = qtype == 8;
+    const int bpb = q8 ? 34 : 18;
+    const int nbk = cols / 32;
+    const int nch = nbk / kMvbKc;
+    const int rb = nbk * bpb;
+    const int ntiles = (rows + 15) / 16;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        *err = "no CUDA device";
+        return B2_ERR_CUDA;
+    }
+    MvbScratch* sc = nullptr;
+    int ks = 1;
+    uint8_t *planes = nullptr, *base = nullptr;
+    float *xsc = nullptr, *part = nullptr;
+    uint32_t* xst = nullptr;
+    int* cnt = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_mvb_mu);
+        if ((int)g_mvb.size() <= dev) g_mvb.resize(dev + 1);
+        sc = &g_mvb[dev];
+        if (!sc->sms && cudaDeviceGetAttribute(&sc->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            *err = "cudaDeviceGetAttribute failed";
+            return B2_ERR_CUDA;
+        }
+        if (!sc->attr_set) {
+            cudaError_t e1 = cudaFuncSetAttribute(mvb_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  MvbGeom<8>::smem);
+            cudaError_t e2 = cudaFuncSetAttribute(mvb_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  MvbGeom<2>::smem);
+            if (e1 != cudaSuccess || e2 != cudaSuccess) {
+                *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e1 != cudaSuccess ? e1 : e2);
+                return B2_ERR_CUDA;
+            }
+            // the rest of the 256 KB stays L1 for the x planes (read through the texture path)
+            cudaFuncSetAttribute(mvb_kernel<8>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+            cudaFuncSetAttribute(mvb_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+            sc->attr_set = true;
+        }
+        // slices: the fewest (up to 8, at most one per chunk) giving every
+        // warp of the grid two units
+        const int warps = sc->sms * kMvbWarps;
+        ks = 1;
+        while (ks < kMvbMaxSlices && ks < nch && (long long)ntiles * ks < 2LL * warps) ks++;
+        // Arrival counters first: ks > 1 only when ntiles * (ks - 1) < 2 * warps,
+        // so 2 * warps counters cover every split call.  They are zeroed when
+        // the buffer is allocated and each split call leaves them zero.
+        const size_t b_cnt = align256((size_t)2 * warps * 4);
+        const size_t b_planes = align256((size_t)nbk * 3 * 256);
+        const size_t b_xsc = align256((size_t)nbk * kMvbVec * 4);
+        const size_t b_xst = align256((size_t)nbk * 3 * kMvbVec * 4);
+        const size_t b_part = ks > 1 ? align256((size_t)ks * kMvbVec * ntiles * 16 * 4) : 0;
+        const size_t need = b_cnt + b_planes + b_xsc + b_xst + b_part;
+        if (sc->bytes < need) {
+            if (sc->buf) cudaFree(sc->buf);
+            sc->buf = nullptr;
+            sc->bytes = 0;
+            if (cudaMalloc(&sc->buf, need) != cudaSuccess) {
+                *err = "scratch allocation failed";
+                return B2_ERR_OOM;
+            }
+            if (cudaMemsetAsync(sc->buf, 0, b_cnt, s) != cudaSuccess) {
+                *err = "scratch clear failed";
+                return B2_ERR_CUDA;
+            }
+            sc->bytes = need;
+        }
+        base = sc->buf;
+        cnt = reinterpret_cast<int*>(base);
+        planes = base + b_cnt;
+        xsc = reinterpret_cast<float*>(planes + b_planes);
+        xst = reinterpret_cast<uint32_t*>(planes + b_planes + b_xsc);
+        part = ks > 1 ? reinterpret_cast<float*>(planes + b_planes + b_xsc + b_xst) : nullptr;
+        const int units = ntiles * ks;
+        const int grid = std::min(sc->sms, (units + kMvbWarps - 1) / kMvbWarps);
+        const uint8_t* wb = static_cast<const uint8_t*>(w);
+        if (q8) {
+            mvb_planes_kernel<8><<<nbk, kMvbThreads, 0, s>>>(x, nvec, cols, planes, xsc, xst);
+            mvb_kernel<8><<<grid, kMvbThreads, MvbGeom<8>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes, xsc,
+                                                                     xst, y, nvec, part, cnt);
+        } else {
+            mvb_planes_kernel<2><<<nbk, kMvbThreads, 0, s>>>(x, nvec, cols, planes, xsc, xst);
+            mvb_kernel<2><<<grid, kMvbThreads, MvbGeom<2>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes, xsc,
+                                                                     xst, y, nvec, part, cnt);
+        }
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = std::string("batched matvec launch: ") + cudaGetErrorString(e);
+        return B2_ERR_CUDA;
+    }
+    return B2_OK;
+}

@@ -28,10 +28,11 @@ The other workloads (one GPU, one JSON line per case; not the driver's line):
              partial sums exchanged by peer stores over NVLink inside the
              decode kernel), prompt 256 ids; value = tok/s of the one model
              (strong scaling), ms_per_step = per-token latency;
-  matvec     y = W x through b2_matvec for the Q8_0 and Q4_0 shapes 4096x4096,
-             14336x4096, 4096x14336, 128256x4096 (GGUF block layout, W N(0,0.02),
-             x N(0,1)), batch 1, with >= 256 MB of distinct weight copies rotated
-             so that L2 does not serve repeats;
+  matvec     y = W x through b2_matvec (batch 1) and b2_matvec_batch (batch 8)
+             for the Q8_0 and Q4_0 shapes 4096x4096, 14336x4096, 4096x14336,
+             128256x4096 (GGUF block layout, W N(0,0.02), x N(0,1)), with
+             >= 256 MB of distinct weight copies rotated so that L2 does not
+             serve repeats;
   attention  b2_attention_decode, 32 query / 8 KV heads, head_dim 128, fp16 KV
              N(0,1), contexts 4096 / 16384 / 32768, batch 1 and 8, KV copies
              rotated past L2 in the same way.
@@ -416,7 +417,8 @@ def _timed(torch, stream, fn, copies: int, iters: int) -> float:
 
 
 def run_matvec(args) -> None:
-    """Config-1 dequant-matvec microbench through b2_matvec (batch 1)."""
+    """Config-1 dequant-matvec microbench: b2_matvec (batch 1) and
+    b2_matvec_batch (batch 8, one pass over W for all eight vectors)."""
     import torch
 
     import b2decode
@@ -424,34 +426,39 @@ def run_matvec(args) -> None:
     torch.cuda.set_device(0)
     st = torch.cuda.Stream()
     peak, peak_kind = peaks()
-    for kind, qt in (("q8_0", 8), ("q4_0", 2)):
-        for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
-            rng = np.random.default_rng(rows * 7 + cols)
-            base = gw.quantize(rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02),
-                               gw.TYPE_NAMES[kind])
-            ncp = _rotations(base.nbytes)
-            w0 = torch.from_numpy(base).cuda()
-            ws = [w0] + [w0.clone() for _ in range(ncp - 1)]
-            x = torch.from_numpy(rng.standard_normal(cols, dtype=np.float32)).cuda()
-            y = torch.empty(rows, device="cuda")
-            with torch.cuda.stream(st):
-                ms = _timed(torch, st, lambda i: b2decode.matvec(qt, ws[i].data_ptr(), x.data_ptr(), y.data_ptr(),
-                                                                 rows, cols, st.cuda_stream),
-                            ncp, max(args.steps, 2 * ncp))
-            nbytes = base.nbytes + 4 * (rows + cols)
-            gbs = nbytes / (ms / 1000.0) / 1e9
-            print(json.dumps({
-                "metric": "dequant-matvec GB/s (B=1)", "value": gbs, "unit": "GB/s", "n_gpus": 1,
-                "higher_is_better": True, "dtype": "fp32", "data": "synthetic",
-                "config": {"workload": f"matvec {kind} {rows}x{cols}, batch 1", "us_per_call": ms * 1000.0,
-                           "weight_bytes": int(base.nbytes), "l2": f"{ncp} weight copies rotated"},
-                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                             "peak_source": peak_kind},
-            }), flush=True)
-            del ws, w0
-            torch.cuda.empty_cache()
-    print(json.dumps({"metric": "dequant-matvec GB/s (B=8)", "unavailable": "batched matvec (B>1) is not built"}),
-          flush=True)
+    for batch in (1, 8):
+        for kind, qt in (("q8_0", 8), ("q4_0", 2)):
+            for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
+                rng = np.random.default_rng(rows * 7 + cols)
+                base = gw.quantize(rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02),
+                                   gw.TYPE_NAMES[kind])
+                ncp = _rotations(base.nbytes)
+                w0 = torch.from_numpy(base).cuda()
+                ws = [w0] + [w0.clone() for _ in range(ncp - 1)]
+                x = torch.from_numpy(rng.standard_normal((batch, cols), dtype=np.float32)).cuda()
+                y = torch.empty((batch, rows), device="cuda")
+                if batch == 1:
+                    def call(i):
+                        b2decode.matvec(qt, ws[i].data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, st.cuda_stream)
+                else:
+                    def call(i):
+                        b2decode.matvec_batch(qt, ws[i].data_ptr(), x.data_ptr(), y.data_ptr(), rows, cols, batch,
+                                              st.cuda_stream)
+                with torch.cuda.stream(st):
+                    ms = _timed(torch, st, call, ncp, max(args.steps, 2 * ncp))
+                nbytes = base.nbytes + 4 * batch * (rows + cols)
+                gbs = nbytes / (ms / 1000.0) / 1e9
+                print(json.dumps({
+                    "metric": f"dequant-matvec GB/s (B={batch})", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+                    "higher_is_better": True, "dtype": "fp32" if batch == 1 else "s8x3 planes, fp32 accumulate",
+                    "data": "synthetic",
+                    "config": {"workload": f"matvec {kind} {rows}x{cols}, batch {batch}", "us_per_call": ms * 1000.0,
+                               "weight_bytes": int(base.nbytes), "l2": f"{ncp} weight copies rotated"},
+                    "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                                 "peak_source": peak_kind},
+                }), flush=True)
+                del ws, w0
+                torch.cuda.empty_cache()
 
 
 def run_attention(args) -> None:

@@ -170,6 +170,16 @@ int b2_dequant_tensor(const b2_model* m, const char* name, float* out, int64_t n
 int b2_matvec(int32_t qtype, const void* w, const float* x, float* y, int32_t rows, int32_t cols,
               void* stream);
 
+/* transformer.go:810-892 (matVecMulQ8Chunk / matVecMulQ8Pooled) for nvec
+ * vectors at once, reading the matrix from HBM once: y[v][r] = sum_b d_rb *
+ * sum_j q_rbj * x[v][32b+j] for v < nvec.  x [nvec][cols] and y [nvec][rows]
+ * fp32, w GGUF block rows (16-byte aligned); all DEVICE pointers.
+ * 1 <= nvec <= 8; cols a multiple of 256.  qtype 8 = Q8_0, 2 = Q4_0.  Uses a
+ * per-device scratch buffer (grown with cudaMalloc when a call needs more),
+ * so calls on different streams must not overlap. */
+int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int32_t rows, int32_t cols,
+                    int32_t nvec, void* stream);
+
 /* transformer.go:663-685 attention of one query token per sequence over an
  * fp16 KV cache, split over the context with a log-sum-exp merge.
  * q [batch][nh*hd] fp32; k, v [batch][ctx][nkv*hd] fp16 (binary16 bits);

@@ -136,3 +136,29 @@ def test_tp_entry_points_reject_null(built_lib):
     L = b2decode.lib()
     assert L.b2_tp_handle(None, b"\0" * 64) == -10
     assert L.b2_tp_connect(None, b"\0" * 64) == -10
+
+
+@pytest.mark.parametrize("qtype,rows,cols,nvec,code,text", [
+    (8, 64, 4096, 0, -8, "1 to 8 vectors"),
+    (8, 64, 4096, 9, -8, "1 to 8 vectors"),
+    (8, 64, 4000, 8, -8, "multiple of 256"),
+    (2, 64, 288, 8, -8, "multiple of 256"),
+    (8, 0, 4096, 8, -8, "bad matvec arguments"),
+    (3, 64, 4096, 8, -3, "qtype"),
+])
+def test_batched_matvec_arguments_checked_before_any_device_work(built_lib, qtype, rows, cols, nvec, code, text):
+    """Bad shapes are rejected by the C ABI itself: the (never dereferenced)
+    device addresses below would fault if any of these reached a kernel."""
+    L = b2decode.lib()
+    assert L.b2_matvec_batch(qtype, 4096, 8192, 16384, rows, cols, nvec, None) == code
+    assert text in b2decode.last_error()
+    assert L.b2_matvec_batch(8, None, 8192, 16384, 64, 4096, 8, None) == -8
+
+
+def test_batched_matvec_alignment_and_no_gpu(built_lib):
+    L = b2decode.lib()
+    assert L.b2_matvec_batch(8, 4100, 8192, 16384, 64, 4096, 8, None) == -8
+    assert "16-byte aligned" in b2decode.last_error()
+    if not has_gpu():
+        assert L.b2_matvec_batch(8, 4096, 8192, 16384, 64, 4096, 8, None) == -5
+        assert "no CUDA device" in b2decode.last_error()
