@@ -290,7 +290,7 @@ def matvec(qtype: int, w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int,
 
 def matvec_batch(qtype: int, w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, nvec: int,
                  stream: int = 0) -> None:
-    """Y = W X for nvec (1..8) vectors in one pass over W: x [nvec][cols], y [nvec][rows] fp32, device addresses."""
+    """Y = W X for nvec (1..16) vectors in one pass over W: x [nvec][cols], y [nvec][rows] fp32, device addresses."""
     _check(lib().b2_matvec_batch(qtype, w_ptr, x_ptr, y_ptr, rows, cols, nvec, stream or None))
 
 

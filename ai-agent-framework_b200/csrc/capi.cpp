@@ -416,7 +416,7 @@ int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int3
                     int32_t nvec, void* stream) {
     if (!w || !x || !y || rows <= 0 || cols <= 0) return ret(B2_ERR_BAD_ARG, "bad matvec arguments");
     if (cols % 256) return ret(B2_ERR_BAD_ARG, "batched matvec needs cols to be a multiple of 256");
-    if (nvec < 1 || nvec > 8) return ret(B2_ERR_BAD_ARG, "batched matvec takes 1 to 8 vectors");
+    if (nvec < 1 || nvec > 16) return ret(B2_ERR_BAD_ARG, "batched matvec takes 1 to 16 vectors");
     if (qtype != 8 && qtype != 2) return ret(B2_ERR_UNSUPPORTED_TYPE, "qtype must be 8 (Q8_0) or 2 (Q4_0)");
     std::string err;
     int rc = b2_matvec_batch_impl(qtype, w, x, y, rows, cols, nvec, static_cast<cudaStream_t>(stream), &err);

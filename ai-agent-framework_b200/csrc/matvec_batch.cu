@@ -1,4 +1,4 @@
-// Batched dequantising matvec: Y = W X for up to eight fp32 vectors in one
+// Batched dequantising matvec: Y = W X for up to sixteen fp32 vectors in one
 // pass over a GGUF-layout Q8_0 / Q4_0 matrix.
 //
 // The reference evaluates one vector at a time (transformer.go:810-865
@@ -11,7 +11,8 @@
 //     x ~= s * (p0 + p1 / 2^7 + p2 / 2^14) with s = max|x| / 127 (about 22
 //     bits of precision relative to the block maximum, i.e. fp32-grade
 //     dots).  The planes sit in global memory in the B-fragment order of
-//     mma.m16n8k32, one column per vector, one mma per plane.
+//     mma.m16n8k32, one column per vector, one mma per plane and group of
+//     eight vectors (NT = 1 or 2 column tiles share each A fragment).
 //   * A warp owns a unit = (16-row tile, slice of the 32-blocks).  Its raw
 //     GGUF row bytes stream through warp-private shared-memory stages filled
 //     with cp.async (16 B, L1-bypassing); the fragments are read from the raw
@@ -39,7 +40,8 @@
 namespace b2 {
 namespace {
 
-constexpr int kMvbVec = 8;                    // vectors per pass (mma N)
+constexpr int kMvbVec = 8;                    // vectors per column tile (mma N)
+constexpr int kMvbMaxNt = 2;                  // column tiles per pass (up to 16 vectors)
 constexpr int kMvbWarps = 8;                  // warps per CTA
 constexpr int kMvbThreads = kMvbWarps * 32;
 constexpr int kMvbKc = 8;                     // 32-blocks per chunk
@@ -66,14 +68,17 @@ template <int QT> __device__ __forceinline__ int plane_pos(int v, int k) {
     return v * 32 + 8 * (kk >> 2) + (k >= 16 ? 4 : 0) + (kk & 3);
 }
 
-// One warp per (32-block kb, vector v): lane = element.  Vectors v >= nvec
-// become zero planes with scale 0.  xst (Q4_0 only) holds, per block and
-// plane, the accumulator start 1.5 * 2^23 - 8 * sum(plane) of each vector.
+// One CTA per (32-block kb, column tile n), one warp per vector v of the
+// tile, lane = element.  Record gi = kb * NT + n: planes at gi * 768 bytes
+// (three 256-byte plane records), scales at gi * 8, and (Q4_0) the
+// accumulator starts 1.5 * 2^23 - 8 * sum(plane) at gi * 24 + plane * 8.
+// Vectors v >= nvec become zero planes with scale 0.
 template <int QT>
 __global__ void __launch_bounds__(kMvbThreads)
-    mvb_planes_kernel(const float* __restrict__ x, int nvec, int cols, uint8_t* __restrict__ planes,
+    mvb_planes_kernel(const float* __restrict__ x, int nvec, int cols, int nt, uint8_t* __restrict__ planes,
                       float* __restrict__ xsc, uint32_t* __restrict__ xst) {
-    const int kb = blockIdx.x, v = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gi = blockIdx.x, kb = gi / nt, n = gi - kb * nt;
+    const int vl = threadIdx.x >> 5, lane = threadIdx.x & 31, v = n * kMvbVec + vl;
     const float val = v < nvec ? x[(size_t)v * cols + (size_t)kb * 32 + lane] : 0.0f;
     float amax = fabsf(val);
 #pragma unroll
@@ -85,12 +90,12 @@ __global__ void __launch_bounds__(kMvbThreads)
     const float q1 = (q - r0) * 128.0f;
     const float f1 = q1 + M, r1 = f1 - M;
     const float f2 = (q1 - r1) * 128.0f + M, r2 = f2 - M;
-    const int pos = plane_pos<QT>(v, lane);
-    uint8_t* rec = planes + (size_t)kb * 3 * 256;
+    const int pos = plane_pos<QT>(vl, lane);
+    uint8_t* rec = planes + (size_t)gi * 3 * 256;
     rec[pos] = (uint8_t)__float_as_uint(f0);
     rec[256 + pos] = (uint8_t)__float_as_uint(f1);
     rec[512 + pos] = (uint8_t)__float_as_uint(f2);
-    if (lane == 0) xsc[kb * kMvbVec + v] = amax * (1.0f / 127.0f);
+    if (lane == 0) xsc[gi * kMvbVec + vl] = amax * (1.0f / 127.0f);
     if (QT != 8) {
         int s0 = (int)r0, s1 = (int)r1, s2 = (int)r2;
 #pragma unroll
@@ -100,7 +105,7 @@ __global__ void __launch_bounds__(kMvbThreads)
             s2 += __shfl_xor_sync(0xffffffffu, s2, o);
         }
         if (lane == 0) {
-            uint32_t* st = xst + (size_t)kb * 3 * kMvbVec + v;
+            uint32_t* st = xst + (size_t)gi * 3 * kMvbVec + vl;
             st[0] = kMvbMagic - 8u * (uint32_t)s0;
             st[kMvbVec] = kMvbMagic - 8u * (uint32_t)s1;
             st[2 * kMvbVec] = kMvbMagic - 8u * (uint32_t)s2;
@@ -187,12 +192,28 @@ struct MvbIter {
     }
 };
 
-template <int QT>
+// Output of one lane for one column tile: rows g, g + 8 of the tile,
+// vectors 2t, 2t + 1 of the column tile.
+__device__ __forceinline__ void mvb_store(float* y, int rows, int nvec, int r0, int v0, float a, float b, float c,
+                                          float d) {
+    const int r1 = r0 + 8, v1 = v0 + 1;
+    if (r0 < rows) {
+        if (v0 < nvec) y[(size_t)v0 * rows + r0] = a;
+        if (v1 < nvec) y[(size_t)v1 * rows + r0] = b;
+    }
+    if (r1 < rows) {
+        if (v0 < nvec) y[(size_t)v0 * rows + r1] = c;
+        if (v1 < nvec) y[(size_t)v1 * rows + r1] = d;
+    }
+}
+
+template <int QT, int NT>
 __global__ void __launch_bounds__(kMvbThreads, 1)
     mvb_kernel(const uint8_t* __restrict__ w, int rows, int rb, int nch, int ntiles, int ks,
                const uint8_t* __restrict__ planes, const float* __restrict__ xsc, const uint32_t* __restrict__ xst,
                float* __restrict__ y, int nvec, float* __restrict__ part, int* __restrict__ cnt) {
     using G = MvbGeom<QT>;
+    constexpr int NV = NT * kMvbVec;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -232,7 +253,9 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
     const unsigned long long mneg = f2_pack(-kMvbMagicF, -kMvbMagicF);
     const unsigned long long c7 = f2_pack(0.0078125f, 0.0078125f);
     const unsigned long long c14 = f2_pack(6.103515625e-05f, 6.103515625e-05f);
-    unsigned long long acc_g = f2_pack(0.0f, 0.0f), acc_h = acc_g;
+    unsigned long long acc_g[NT], acc_h[NT];
+#pragma unroll
+    for (int n = 0; n < NT; n++) acc_g[n] = acc_h[n] = f2_pack(0.0f, 0.0f);
     int st = 0;
 #pragma unroll 1
     while (cs.u < total) {
@@ -247,16 +270,6 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
 #pragma unroll
         for (int bb = 0; bb < kMvbKc; bb++) {
             const int kb = kb0 + bb;
-            const uint2* rec = reinterpret_cast<const uint2*>(planes + (size_t)kb * 3 * 256) + lane;
-            const uint2 p0 = __ldg(rec), p1 = __ldg(rec + 32), p2 = __ldg(rec + 64);
-            const float2 sx = __ldg(reinterpret_cast<const float2*>(xsc + kb * kMvbVec + 2 * t));
-            uint32_t s0a = kMvbMagic, s0b = kMvbMagic, s1a = kMvbMagic, s1b = kMvbMagic, s2a = kMvbMagic,
-                     s2b = kMvbMagic;
-            if (QT != 8) {
-                const uint2* sp = reinterpret_cast<const uint2*>(xst + (size_t)kb * 3 * kMvbVec + 2 * t);
-                const uint2 v0 = __ldg(sp), v1 = __ldg(sp + 4), v2 = __ldg(sp + 8);
-                s0a = v0.x; s0b = v0.y; s1a = v1.x; s1b = v1.y; s2a = v2.x; s2b = v2.y;
-            }
             const uint8_t* bg = rg + bb * G::bpb;
             const uint8_t* bh = rh + bb * G::bpb;
             uint32_t a0, a1, a2, a3;
@@ -272,41 +285,57 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
             }
             const float dg = __half2float(*reinterpret_cast<const __half*>(bg));
             const float dh = __half2float(*reinterpret_cast<const __half*>(bh));
-            uint32_t e0, e1, e2, e3, f0, f1, f2, f3, h0, h1, h2, h3;
-            mma_i8<QT != 8>(a0, a1, a2, a3, p0.x, p0.y, s0a, s0b, e0, e1, e2, e3);
-            mma_i8<QT != 8>(a0, a1, a2, a3, p1.x, p1.y, s1a, s1b, f0, f1, f2, f3);
-            mma_i8<QT != 8>(a0, a1, a2, a3, p2.x, p2.y, s2a, s2b, h0, h1, h2, h3);
-            const unsigned long long sxp = f2_pack(sx.x, sx.y);
-            // rows g (d0, d1) and g + 8 (d2, d3), vectors 2t and 2t + 1
-            unsigned long long tg = f2_add(f2_pack(__uint_as_float(e0), __uint_as_float(e1)), mneg);
-            tg = f2_fma(f2_add(f2_pack(__uint_as_float(f0), __uint_as_float(f1)), mneg), c7, tg);
-            tg = f2_fma(f2_add(f2_pack(__uint_as_float(h0), __uint_as_float(h1)), mneg), c14, tg);
-            unsigned long long th = f2_add(f2_pack(__uint_as_float(e2), __uint_as_float(e3)), mneg);
-            th = f2_fma(f2_add(f2_pack(__uint_as_float(f2), __uint_as_float(f3)), mneg), c7, th);
-            th = f2_fma(f2_add(f2_pack(__uint_as_float(h2), __uint_as_float(h3)), mneg), c14, th);
-            acc_g = f2_fma(f2_mul(f2_pack(dg, dg), sxp), tg, acc_g);
-            acc_h = f2_fma(f2_mul(f2_pack(dh, dh), sxp), th, acc_h);
+            const unsigned long long dgp = f2_pack(dg, dg), dhp = f2_pack(dh, dh);
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                const int gi = kb * NT + n;
+                const uint2* rec = reinterpret_cast<const uint2*>(planes + (size_t)gi * 3 * 256) + lane;
+                const uint2 p0 = __ldg(rec), p1 = __ldg(rec + 32), p2 = __ldg(rec + 64);
+                const float2 sx = __ldg(reinterpret_cast<const float2*>(xsc + gi * kMvbVec + 2 * t));
+                uint32_t s0a = kMvbMagic, s0b = kMvbMagic, s1a = kMvbMagic, s1b = kMvbMagic, s2a = kMvbMagic,
+                         s2b = kMvbMagic;
+                if (QT != 8) {
+                    const uint2* sp = reinterpret_cast<const uint2*>(xst + (size_t)gi * 3 * kMvbVec + 2 * t);
+                    const uint2 v0 = __ldg(sp), v1 = __ldg(sp + 4), v2 = __ldg(sp + 8);
+                    s0a = v0.x; s0b = v0.y; s1a = v1.x; s1b = v1.y; s2a = v2.x; s2b = v2.y;
+                }
+                uint32_t e0, e1, e2, e3, f0, f1, f2, f3, h0, h1, h2, h3;
+                mma_i8<QT != 8>(a0, a1, a2, a3, p0.x, p0.y, s0a, s0b, e0, e1, e2, e3);
+                mma_i8<QT != 8>(a0, a1, a2, a3, p1.x, p1.y, s1a, s1b, f0, f1, f2, f3);
+                mma_i8<QT != 8>(a0, a1, a2, a3, p2.x, p2.y, s2a, s2b, h0, h1, h2, h3);
+                const unsigned long long sxp = f2_pack(sx.x, sx.y);
+                // rows g (d0, d1) and g + 8 (d2, d3), vectors 2t and 2t + 1 of column tile n
+                unsigned long long tg = f2_add(f2_pack(__uint_as_float(e0), __uint_as_float(e1)), mneg);
+                tg = f2_fma(f2_add(f2_pack(__uint_as_float(f0), __uint_as_float(f1)), mneg), c7, tg);
+                tg = f2_fma(f2_add(f2_pack(__uint_as_float(h0), __uint_as_float(h1)), mneg), c14, tg);
+                unsigned long long th = f2_add(f2_pack(__uint_as_float(e2), __uint_as_float(e3)), mneg);
+                th = f2_fma(f2_add(f2_pack(__uint_as_float(f2), __uint_as_float(f3)), mneg), c7, th);
+                th = f2_fma(f2_add(f2_pack(__uint_as_float(h2), __uint_as_float(h3)), mneg), c14, th);
+                acc_g[n] = f2_fma(f2_mul(dgp, sxp), tg, acc_g[n]);
+                acc_h[n] = f2_fma(f2_mul(dhp, sxp), th, acc_h[n]);
+            }
         }
 
         if (cs.c + 1 == cs.c1) {
-            // unit done: rows tile*16 + g, + 8; vectors 2t, 2t + 1
-            const float2 vg = f2_unpack(acc_g), vh = f2_unpack(acc_h);
-            const int r0 = cs.tile * 16 + g, r1 = r0 + 8, v0 = 2 * t, v1 = v0 + 1;
+            // unit done: rows tile*16 + g, + 8; vectors n*8 + 2t, + 1
+            const int r0 = cs.tile * 16 + g, r1 = r0 + 8;
             if (ks == 1) {
-                if (r0 < rows) {
-                    if (v0 < nvec) y[(size_t)v0 * rows + r0] = vg.x;
-                    if (v1 < nvec) y[(size_t)v1 * rows + r0] = vg.y;
-                }
-                if (r1 < rows) {
-                    if (v0 < nvec) y[(size_t)v0 * rows + r1] = vh.x;
-                    if (v1 < nvec) y[(size_t)v1 * rows + r1] = vh.y;
+#pragma unroll
+                for (int n = 0; n < NT; n++) {
+                    const float2 vg = f2_unpack(acc_g[n]), vh = f2_unpack(acc_h[n]);
+                    mvb_store(y, rows, nvec, r0, n * kMvbVec + 2 * t, vg.x, vg.y, vh.x, vh.y);
                 }
             } else {
-                float* ps = part + (size_t)cs.slice * kMvbVec * rows_pad;
-                ps[(size_t)v0 * rows_pad + r0] = vg.x;
-                ps[(size_t)v1 * rows_pad + r0] = vg.y;
-                ps[(size_t)v0 * rows_pad + r1] = vh.x;
-                ps[(size_t)v1 * rows_pad + r1] = vh.y;
+                float* ps = part + (size_t)cs.slice * NV * rows_pad;
+#pragma unroll
+                for (int n = 0; n < NT; n++) {
+                    const float2 vg = f2_unpack(acc_g[n]), vh = f2_unpack(acc_h[n]);
+                    const int v0 = n * kMvbVec + 2 * t, v1 = v0 + 1;
+                    ps[(size_t)v0 * rows_pad + r0] = vg.x;
+                    ps[(size_t)v1 * rows_pad + r0] = vg.y;
+                    ps[(size_t)v0 * rows_pad + r1] = vh.x;
+                    ps[(size_t)v1 * rows_pad + r1] = vh.y;
+                }
                 __threadfence();
                 __syncwarp();
                 int last = 0;
@@ -314,27 +343,24 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
-                    float s00 = 0.0f, s01 = 0.0f, s10 = 0.0f, s11 = 0.0f;
-                    for (int s = 0; s < ks; s++) {
-                        const float* q = part + (size_t)s * kMvbVec * rows_pad;
-                        s00 += __ldcg(q + (size_t)v0 * rows_pad + r0);
-                        s01 += __ldcg(q + (size_t)v1 * rows_pad + r0);
-                        s10 += __ldcg(q + (size_t)v0 * rows_pad + r1);
-                        s11 += __ldcg(q + (size_t)v1 * rows_pad + r1);
-                    }
-                    if (r0 < rows) {
-                        if (v0 < nvec) y[(size_t)v0 * rows + r0] = s00;
-                        if (v1 < nvec) y[(size_t)v1 * rows + r0] = s01;
-                    }
-                    if (r1 < rows) {
-                        if (v0 < nvec) y[(size_t)v0 * rows + r1] = s10;
-                        if (v1 < nvec) y[(size_t)v1 * rows + r1] = s11;
+#pragma unroll
+                    for (int n = 0; n < NT; n++) {
+                        const int v0 = n * kMvbVec + 2 * t, v1 = v0 + 1;
+                        float s00 = 0.0f, s01 = 0.0f, s10 = 0.0f, s11 = 0.0f;
+                        for (int s = 0; s < ks; s++) {
+                            const float* q = part + (size_t)s * NV * rows_pad;
+                            s00 += __ldcg(q + (size_t)v0 * rows_pad + r0);
+                            s01 += __ldcg(q + (size_t)v1 * rows_pad + r0);
+                            s10 += __ldcg(q + (size_t)v0 * rows_pad + r1);
+                            s11 += __ldcg(q + (size_t)v1 * rows_pad + r1);
+                        }
+                        mvb_store(y, rows, nvec, r0, v0, s00, s01, s10, s11);
                     }
                     if (lane == 0) cnt[cs.tile] = 0;  // every unit of the tile has arrived
                 }
             }
-            acc_g = f2_pack(0.0f, 0.0f);
-            acc_h = acc_g;
+#pragma unroll
+            for (int n = 0; n < NT; n++) acc_g[n] = acc_h[n] = f2_pack(0.0f, 0.0f);
         }
         __syncwarp();  // every lane is done with this stage before it is refilled
         st = st + 1 == G::stages ? 0 : st + 1;
@@ -373,12 +399,17 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
         *err = "x and y must be 4-byte aligned";
         return B2_ERR_BAD_ARG;
     }
+    if (nvec < 1 || nvec > kMvbMaxNt * kMvbVec || cols % (32 * kMvbKc)) {
+        *err = "batched matvec takes 1 to 16 vectors and cols a multiple of 256";
+        return B2_ERR_BAD_ARG;
+    }
     const bool q8 = qtype == 8;
     const int bpb = q8 ? 34 : 18;
     const int nbk = cols / 32;
     const int nch = nbk / kMvbKc;
     const int rb = nbk * bpb;
     const int ntiles = (rows + 15) / 16;
+    const int nt = (nvec + kMvbVec - 1) / kMvbVec;  // column tiles: 1 or 2
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         *err = "no CUDA device";
@@ -399,17 +430,22 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
             return B2_ERR_CUDA;
         }
         if (!sc->attr_set) {
-            cudaError_t e1 = cudaFuncSetAttribute(mvb_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  MvbGeom<8>::smem);
-            cudaError_t e2 = cudaFuncSetAttribute(mvb_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  MvbGeom<2>::smem);
-            if (e1 != cudaSuccess || e2 != cudaSuccess) {
-                *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e1 != cudaSuccess ? e1 : e2);
-                return B2_ERR_CUDA;
+            const cudaError_t es[4] = {
+                cudaFuncSetAttribute(mvb_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<8>::smem),
+                cudaFuncSetAttribute(mvb_kernel<8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<8>::smem),
+                cudaFuncSetAttribute(mvb_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<2>::smem),
+                cudaFuncSetAttribute(mvb_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<2>::smem)};
+            for (cudaError_t e : es) {
+                if (e != cudaSuccess) {
+                    *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+                    return B2_ERR_CUDA;
+                }
             }
             // the rest of the 256 KB stays L1 for the x planes (read through the texture path)
-            cudaFuncSetAttribute(mvb_kernel<8>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
-            cudaFuncSetAttribute(mvb_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+            cudaFuncSetAttribute(mvb_kernel<8, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+            cudaFuncSetAttribute(mvb_kernel<8, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+            cudaFuncSetAttribute(mvb_kernel<2, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+            cudaFuncSetAttribute(mvb_kernel<2, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
             sc->attr_set = true;
         }
         // slices: the fewest (up to 8, at most one per chunk) giving every
@@ -421,10 +457,11 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
         // so 2 * warps counters cover every split call.  They are zeroed when
         // the buffer is allocated and each split call leaves them zero.
         const size_t b_cnt = align256((size_t)2 * warps * 4);
-        const size_t b_planes = align256((size_t)nbk * 3 * 256);
-        const size_t b_xsc = align256((size_t)nbk * kMvbVec * 4);
-        const size_t b_xst = align256((size_t)nbk * 3 * kMvbVec * 4);
-        const size_t b_part = ks > 1 ? align256((size_t)ks * kMvbVec * ntiles * 16 * 4) : 0;
+        const size_t ng = (size_t)nbk * nt;  // plane record groups
+        const size_t b_planes = align256(ng * 3 * 256);
+        const size_t b_xsc = align256(ng * kMvbVec * 4);
+        const size_t b_xst = align256(ng * 3 * kMvbVec * 4);
+        const size_t b_part = ks > 1 ? align256((size_t)ks * nt * kMvbVec * ntiles * 16 * 4) : 0;
         const size_t need = b_cnt + b_planes + b_xsc + b_xst + b_part;
         if (sc->bytes < need) {
             if (sc->buf) cudaFree(sc->buf);
@@ -449,14 +486,23 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
         const int units = ntiles * ks;
         const int grid = std::min(sc->sms, (units + kMvbWarps - 1) / kMvbWarps);
         const uint8_t* wb = static_cast<const uint8_t*>(w);
+        const int ngrid = (int)ng;
         if (q8) {
-            mvb_planes_kernel<8><<<nbk, kMvbThreads, 0, s>>>(x, nvec, cols, planes, xsc, xst);
-            mvb_kernel<8><<<grid, kMvbThreads, MvbGeom<8>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes, xsc,
-                                                                     xst, y, nvec, part, cnt);
+            mvb_planes_kernel<8><<<ngrid, kMvbThreads, 0, s>>>(x, nvec, cols, nt, planes, xsc, xst);
+            if (nt == 1)
+                mvb_kernel<8, 1><<<grid, kMvbThreads, MvbGeom<8>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
+                                                                            xsc, xst, y, nvec, part, cnt);
+            else
+                mvb_kernel<8, 2><<<grid, kMvbThreads, MvbGeom<8>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
+                                                                            xsc, xst, y, nvec, part, cnt);
         } else {
-            mvb_planes_kernel<2><<<nbk, kMvbThreads, 0, s>>>(x, nvec, cols, planes, xsc, xst);
-            mvb_kernel<2><<<grid, kMvbThreads, MvbGeom<2>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes, xsc,
-                                                                     xst, y, nvec, part, cnt);
+            mvb_planes_kernel<2><<<ngrid, kMvbThreads, 0, s>>>(x, nvec, cols, nt, planes, xsc, xst);
+            if (nt == 1)
+                mvb_kernel<2, 1><<<grid, kMvbThreads, MvbGeom<2>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
+                                                                            xsc, xst, y, nvec, part, cnt);
+            else
+                mvb_kernel<2, 2><<<grid, kMvbThreads, MvbGeom<2>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
+                                                                            xsc, xst, y, nvec, part, cnt);
         }
     }
     cudaError_t e = cudaGetLastError();

@@ -174,7 +174,8 @@ int b2_matvec(int32_t qtype, const void* w, const float* x, float* y, int32_t ro
  * vectors at once, reading the matrix from HBM once: y[v][r] = sum_b d_rb *
  * sum_j q_rbj * x[v][32b+j] for v < nvec.  x [nvec][cols] and y [nvec][rows]
  * fp32, w GGUF block rows (16-byte aligned); all DEVICE pointers.
- * 1 <= nvec <= 8; cols a multiple of 256.  qtype 8 = Q8_0, 2 = Q4_0.  Uses a
+ * 1 <= nvec <= 16 (vectors 8..15 share the pass over w with 0..7); cols a
+ * multiple of 256.  qtype 8 = Q8_0, 2 = Q4_0.  Uses a
  * per-device scratch buffer (grown with cudaMalloc when a call needs more),
  * so calls on different streams must not overlap. */
 int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int32_t rows, int32_t cols,

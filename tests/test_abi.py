@@ -139,8 +139,8 @@ def test_tp_entry_points_reject_null(built_lib):
 
 
 @pytest.mark.parametrize("qtype,rows,cols,nvec,code,text", [
-    (8, 64, 4096, 0, -8, "1 to 8 vectors"),
-    (8, 64, 4096, 9, -8, "1 to 8 vectors"),
+    (8, 64, 4096, 0, -8, "1 to 16 vectors"),
+    (8, 64, 4096, 17, -8, "1 to 16 vectors"),
     (8, 64, 4000, 8, -8, "multiple of 256"),
     (2, 64, 288, 8, -8, "multiple of 256"),
     (8, 0, 4096, 8, -8, "bad matvec arguments"),

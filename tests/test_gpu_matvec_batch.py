@@ -1,4 +1,4 @@
-"""b2_matvec_batch (up to eight vectors per pass over W) against the oracle's
+"""b2_matvec_batch (up to sixteen vectors per pass over W) against the oracle's
 restatement of the Go Q8_0 / Q4_0 matvec, one vector at a time.
 
 The kernel splits each vector into three int8 planes (about 22 bits relative
@@ -72,11 +72,12 @@ def test_config1_shapes_batch8(built_lib, oracle_lib, torch_cuda, kind, rows, co
 
 
 @pytest.mark.parametrize("kind", ["q8_0", "q4_0"])
-@pytest.mark.parametrize("rows,cols,nvec", [(17, 256, 3), (40, 512, 8), (33, 768, 5), (1000, 2048, 1), (16, 256, 2)])
+@pytest.mark.parametrize("rows,cols,nvec", [(17, 256, 3), (40, 512, 8), (33, 768, 5), (1000, 2048, 1), (16, 256, 2),
+                                            (24, 512, 16), (17, 256, 12), (4096, 4096, 16), (300, 14336, 9)])
 def test_ragged_rows_and_partial_batches(built_lib, oracle_lib, torch_cuda, kind, rows, cols, nvec):
-    """Row counts off the 16-row tile, fewer than eight vectors, and shapes
-    small enough that the blocks are split into slices merged by the last
-    unit of each tile."""
+    """Row counts off the 16-row tile, partial column tiles (fewer than 8, or
+    9..16 vectors in two column tiles), and shapes small enough that the
+    blocks are split into slices merged by the last unit of each tile."""
     raw, x = _case(kind, rows, cols, nvec, rows * 31 + cols + nvec)
     x[0, :32] *= 1e-3       # a block of tiny values
     if nvec > 2:
@@ -89,7 +90,7 @@ def test_ragged_rows_and_partial_batches(built_lib, oracle_lib, torch_cuda, kind
 def test_calls_in_a_row_are_independent_and_deterministic(built_lib, oracle_lib, torch_cuda, kind):
     """The slice counters are reset by each call (a second split call, and one
     after an unsplit call, are still right) and equal inputs give equal bits."""
-    shapes = [(300, 4096, 8), (128256, 4096, 8), (300, 4096, 8), (40, 512, 6)]
+    shapes = [(300, 4096, 8), (128256, 4096, 8), (300, 4096, 8), (40, 512, 6), (300, 4096, 16), (40, 512, 6)]
     first = {}
     for i, (rows, cols, nvec) in enumerate(shapes):
         raw, x = _case(kind, rows, cols, nvec, 7 + rows)
