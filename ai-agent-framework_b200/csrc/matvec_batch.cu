@@ -441,11 +441,16 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
                     return B2_ERR_CUDA;
                 }
             }
-            // the rest of the 256 KB stays L1 for the x planes (read through the texture path)
-            cudaFuncSetAttribute(mvb_kernel<8, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
-            cudaFuncSetAttribute(mvb_kernel<8, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
-            cudaFuncSetAttribute(mvb_kernel<2, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
-            cudaFuncSetAttribute(mvb_kernel<2, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0);
+            // the rest of the 256 KB stays L1 for the x planes (read through the
+            // texture path).  Only a hint: a refusal is cleared so that the
+            // launch check below does not report it.
+            const cudaError_t hints[4] = {
+                cudaFuncSetAttribute(mvb_kernel<8, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0),
+                cudaFuncSetAttribute(mvb_kernel<8, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0),
+                cudaFuncSetAttribute(mvb_kernel<2, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0),
+                cudaFuncSetAttribute(mvb_kernel<2, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0)};
+            for (cudaError_t e : hints)
+                if (e != cudaSuccess) (void)cudaGetLastError();
             sc->attr_set = true;
         }
         // slices: the fewest (up to 8, at most one per chunk) giving every
