@@ -378,7 +378,9 @@ def run_b200(args) -> None:
                        "ctx_range": [int(len(prompt) + W), int(len(prompt) + W + K)],
                        "l2": f"no flush needed: each token streams {bytes_tok / 1e6:.0f} MB of weights, > 126 MB L2",
                        "parallelism": (f"tp{tpn}" if tpn > 1 else (f"replicas x{ws}" if ws > 1 else "single gpu")),
-                       "prefill_s": prefill_s, "kv_cache": "fp16"},
+                       "prefill_s": prefill_s,
+                       "prefill_path": "the decode kernel once per prompt token (no batched GEMM prefill yet)",
+                       "kv_cache": "fp16"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": profile_traffic("decode_kernel") if args.workload == "qwen05b" else None,
