@@ -97,6 +97,7 @@ SIGNATURES = {
     "b2_dequant_tensor": (C.c_int, [_P, C.c_char_p, _f32p, _i64, C.POINTER(_i64)]),
     "b2_matvec": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _P]),
     "b2_matvec_batch": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _i32, _P]),
+    "b2_model_matvec": (C.c_int, [_P, C.c_char_p, _P, _P, _i32, _P]),
     "b2_attention_decode": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_attention_decode_noalloc": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_device_status": (C.c_int, [_P]),
@@ -252,6 +253,11 @@ class Model:
         got = C.c_int64()
         _check(lib().b2_dequant_tensor(self._h, name.encode(), out.ctypes.data_as(_f32p), n, C.byref(got)))
         return out[: got.value]
+
+    def matvec(self, name: str, x_ptr: int, y_ptr: int, nvec: int, stream: int = 0) -> None:
+        """Y = W X over the resident tensor `name` for nvec (1..16) vectors:
+        x [nvec][cols], y [nvec][rows] fp32 at device addresses."""
+        _check(lib().b2_model_matvec(self._h, name.encode(), x_ptr, y_ptr, nvec, stream or None))
 
     def device_status(self) -> int:
         return lib().b2_device_status(self._h)

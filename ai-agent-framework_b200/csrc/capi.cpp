@@ -17,6 +17,8 @@ int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows,
                    std::string* err);
 int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int rows, int cols, int nvec,
                          cudaStream_t s, std::string* err);
+int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
+                               const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
 int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh, int nkv,
                       int hd, int ctx, cudaStream_t s, std::string* err);
 int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh,
@@ -420,6 +422,25 @@ int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int3
     if (qtype != 8 && qtype != 2) return ret(B2_ERR_UNSUPPORTED_TYPE, "qtype must be 8 (Q8_0) or 2 (Q4_0)");
     std::string err;
     int rc = b2_matvec_batch_impl(qtype, w, x, y, rows, cols, nvec, static_cast<cudaStream_t>(stream), &err);
+    return ret(rc, err);
+}
+
+int b2_model_matvec(const b2_model* m, const char* name, const float* x, float* y, int32_t nvec, void* stream) {
+    if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
+    if (!name || !x || !y) return ret(B2_ERR_BAD_ARG, "null argument");
+    if (nvec < 1 || nvec > 16) return ret(B2_ERR_BAD_ARG, "batched matvec takes 1 to 16 vectors");
+    auto it = m->tensors.find(name);
+    if (it == m->tensors.end()) return ret(B2_ERR_BAD_ARG, std::string("tensor not found: ") + name);
+    const b2::TensorLoc& t = it->second;
+    if (t.type != 8 && t.type != 2) return ret(B2_ERR_UNSUPPORTED_TYPE, std::string(name) + " is not a Q8_0 / Q4_0 matrix");
+    if (t.half) return ret(B2_ERR_BAD_ARG, std::string(name) + ": gate and up rows are interleaved in the resident matrix");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device)
+        return ret(B2_ERR_BAD_ARG, "the model's device must be the current device");
+    std::string err;
+    const int rows = (int)(t.elements / (uint64_t)t.cols);
+    int rc = b2_tiled_matvec_batch_impl((int)t.type, t.dev, t.rp, t.row0, rows, (int)t.cols, x, y, nvec,
+                                        stream ? static_cast<cudaStream_t>(stream) : m->stream, &err);
     return ret(rc, err);
 }
 

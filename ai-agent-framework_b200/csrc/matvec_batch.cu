@@ -49,21 +49,28 @@ constexpr int kMvbMaxSlices = 8;
 constexpr uint32_t kMvbMagic = 0x4B400000u;   // 1.5 * 2^23 as float bits
 constexpr float kMvbMagicF = 12582912.0f;
 
+// One stage holds 16 rows x one chunk of 8 blocks: raw GGUF rows (16 rows of
+// rc bytes), or in the tiled layout the chunk's 8 (tile, block) units of
+// 16 x qb quant bytes followed by their 8 x 16 f16 scales -- the same bytes.
 template <int QT> struct MvbGeom {
     static constexpr int bpb = QT == 8 ? 34 : 18;        // bytes per 32-block
+    static constexpr int qb = QT == 8 ? 32 : 16;         // quant bytes of one row's block
     static constexpr int rc = kMvbKc * bpb;              // row bytes of one chunk (16-B multiple)
-    static constexpr int tile = 16 * rc;                 // one stage: 16 rows of one chunk
+    static constexpr int tile = 16 * rc;                 // one stage
+    static constexpr int tsc = kMvbKc * 16 * qb;         // tiled: offset of the scales in a stage
     static constexpr int stages = QT == 8 ? 3 : 5;
     static constexpr int smem = kMvbWarps * stages * tile;
+    static_assert(tsc + kMvbKc * 32 == tile, "tiled stage = raw stage bytes");
 };
 
 // Byte position of element k (0..31) of vector v inside one plane record
 // (256 bytes = 32 lanes x the 8 bytes of their B fragment {b0, b1}).
-// Lane (g, t) holds column g; Q4_0 keeps the natural k slots of the fragment
-// (b0: k = 4t..4t+3, b1: 16+4t..), Q8_0 assigns lane t the eight contiguous
-// elements 8t..8t+7 (b0 then b1), which its A operand mirrors.
-template <int QT> __device__ __forceinline__ int plane_pos(int v, int k) {
-    if (QT == 8) return v * 32 + k;
+// Lane (g, t) holds column g.  The natural order keeps the k slots of the
+// fragment (b0: k = 4t..4t+3, b1: 16+4t..): Q4_0 rows and the tiled layout
+// (ldmatrix) use it.  PERM assigns lane t the eight contiguous elements
+// 8t..8t+7 (b0 then b1), which the A operand of raw Q8_0 rows mirrors.
+template <bool PERM> __device__ __forceinline__ int plane_pos(int v, int k) {
+    if (PERM) return v * 32 + k;
     const int kk = k & 15;
     return v * 32 + 8 * (kk >> 2) + (k >= 16 ? 4 : 0) + (kk & 3);
 }
@@ -73,7 +80,7 @@ template <int QT> __device__ __forceinline__ int plane_pos(int v, int k) {
 // (three 256-byte plane records), scales at gi * 8, and (Q4_0) the
 // accumulator starts 1.5 * 2^23 - 8 * sum(plane) at gi * 24 + plane * 8.
 // Vectors v >= nvec become zero planes with scale 0.
-template <int QT>
+template <bool PERM, bool STARTS>
 __global__ void __launch_bounds__(kMvbThreads)
     mvb_planes_kernel(const float* __restrict__ x, int nvec, int cols, int nt, uint8_t* __restrict__ planes,
                       float* __restrict__ xsc, uint32_t* __restrict__ xst) {
@@ -90,13 +97,13 @@ __global__ void __launch_bounds__(kMvbThreads)
     const float q1 = (q - r0) * 128.0f;
     const float f1 = q1 + M, r1 = f1 - M;
     const float f2 = (q1 - r1) * 128.0f + M, r2 = f2 - M;
-    const int pos = plane_pos<QT>(vl, lane);
+    const int pos = plane_pos<PERM>(vl, lane);
     uint8_t* rec = planes + (size_t)gi * 3 * 256;
     rec[pos] = (uint8_t)__float_as_uint(f0);
     rec[256 + pos] = (uint8_t)__float_as_uint(f1);
     rec[512 + pos] = (uint8_t)__float_as_uint(f2);
     if (lane == 0) xsc[gi * kMvbVec + vl] = amax * (1.0f / 127.0f);
-    if (QT != 8) {
+    if (STARTS) {
         int s0 = (int)r0, s1 = (int)r1, s2 = (int)r2;
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
@@ -207,11 +214,31 @@ __device__ __forceinline__ void mvb_store(float* y, int rows, int nvec, int r0, 
     }
 }
 
-template <int QT, int NT>
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+
+// The matrix: raw GGUF rows (w, row bytes rb), or (TILED) the decode
+// kernel's tiled layout -- quants at w, scales at ws, nb blocks per row --
+// of which this call reads the `rows` rows from tile tile0 on.
+struct MvbMat {
+    const uint8_t* w;
+    const uint8_t* ws;
+    int rows, rb, nb, tile0;
+};
+
+template <int QT, int NT, bool TILED>
 __global__ void __launch_bounds__(kMvbThreads, 1)
-    mvb_kernel(const uint8_t* __restrict__ w, int rows, int rb, int nch, int ntiles, int ks,
+    mvb_kernel(const MvbMat mat, int nch, int ntiles, int ks,
                const uint8_t* __restrict__ planes, const float* __restrict__ xsc, const uint32_t* __restrict__ xst,
                float* __restrict__ y, int nvec, float* __restrict__ part, int* __restrict__ cnt) {
+    const uint8_t* __restrict__ w = mat.w;
+    const int rows = mat.rows, rb = mat.rb, nb = mat.nb;
     using G = MvbGeom<QT>;
     constexpr int NV = NT * kMvbVec;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -229,20 +256,41 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
     pf.enter(total, ntiles, nch, ks);
     cs = pf;
 
-    // 16-byte copies of one stage: 16 rows x G::rc / 16 pieces
+    // 16-byte copies of one stage.  Raw: 16 rows x G::rc / 16 pieces (rows
+    // past the end repeat the last row; their outputs are dropped).  Tiled:
+    // the chunk's units (nblk x 16 x qb bytes) and scales (nblk x 32 bytes),
+    // each one contiguous range.
     constexpr int kPieces = G::rc / 16;
     auto issue = [&](const MvbIter& it, int st) {
         if (it.u < total) {
             const uint32_t dst0 = stage0_s + (uint32_t)(st * G::tile);
-            const size_t coff = (size_t)it.c * G::rc;
-            for (int j = lane; j < 16 * kPieces; j += 32) {
-                const int row = j / kPieces, piece = j - row * kPieces;
-                const int r = min(it.tile * 16 + row, rows - 1);
-                cp_async16(dst0 + (uint32_t)(row * G::rc + piece * 16), w + (size_t)r * rb + coff + piece * 16);
+            if (TILED) {
+                const int kb0 = it.c * kMvbKc, nblk = min(kMvbKc, nb - kb0);
+                const size_t unit0 = (size_t)(mat.tile0 + it.tile) * nb + kb0;
+                const uint8_t* qsrc = w + unit0 * 16 * G::qb;
+                const uint8_t* ssrc = mat.ws + unit0 * 32;
+                for (int j = lane; j < nblk * G::qb; j += 32) cp_async16(dst0 + (uint32_t)(j * 16), qsrc + (size_t)j * 16);
+                for (int j = lane; j < nblk * 2; j += 32)
+                    cp_async16(dst0 + (uint32_t)(G::tsc + j * 16), ssrc + (size_t)j * 16);
+            } else {
+                const size_t coff = (size_t)it.c * G::rc;
+                for (int j = lane; j < 16 * kPieces; j += 32) {
+                    const int row = j / kPieces, piece = j - row * kPieces;
+                    const int r = min(it.tile * 16 + row, rows - 1);
+                    cp_async16(dst0 + (uint32_t)(row * G::rc + piece * 16), w + (size_t)r * rb + coff + piece * 16);
+                }
             }
         }
         cp_async_commit();
     };
+    // tiled Q8_0: this lane's ldmatrix row address in a unit (rows with bit 2
+    // set hold their 16-byte halves swapped); Q4_0: rows 0..15, one 16-byte row each
+    uint32_t lo8;
+    {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8, half = (lane >> 4) & 1;
+        lo8 = (uint32_t)(row * 32 + ((half ^ ((row >> 2) & 1)) << 4));
+    }
+    const uint32_t lo4 = (uint32_t)((lane & 15) * 16);
 
 #pragma unroll
     for (int i = 0; i < G::stages - 1; i++) {
@@ -266,25 +314,47 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
 
         const uint8_t* rg = stage0 + st * G::tile + g * G::rc;
         const uint8_t* rh = rg + 8 * G::rc;
+        const uint32_t sq = stage0_s + (uint32_t)(st * G::tile);
+        const uint8_t* ssc = stage0 + st * G::tile + G::tsc;
         const int kb0 = cs.c * kMvbKc;
+        const int nblk = TILED ? min(kMvbKc, nb - kb0) : kMvbKc;
 #pragma unroll
         for (int bb = 0; bb < kMvbKc; bb++) {
+            if (TILED && bb >= nblk) break;  // warp-uniform: a short last chunk
             const int kb = kb0 + bb;
-            const uint8_t* bg = rg + bb * G::bpb;
-            const uint8_t* bh = rh + bb * G::bpb;
             uint32_t a0, a1, a2, a3;
-            switch (bb) {  // bb is a constant after unrolling: the parity picks the load pattern
-                case 0: a_words<QT, 0>(bg, t, a0, a2); a_words<QT, 0>(bh, t, a1, a3); break;
-                case 1: a_words<QT, 1>(bg, t, a0, a2); a_words<QT, 1>(bh, t, a1, a3); break;
-                case 2: a_words<QT, 2>(bg, t, a0, a2); a_words<QT, 2>(bh, t, a1, a3); break;
-                case 3: a_words<QT, 3>(bg, t, a0, a2); a_words<QT, 3>(bh, t, a1, a3); break;
-                case 4: a_words<QT, 4>(bg, t, a0, a2); a_words<QT, 4>(bh, t, a1, a3); break;
-                case 5: a_words<QT, 5>(bg, t, a0, a2); a_words<QT, 5>(bh, t, a1, a3); break;
-                case 6: a_words<QT, 6>(bg, t, a0, a2); a_words<QT, 6>(bh, t, a1, a3); break;
-                default: a_words<QT, 7>(bg, t, a0, a2); a_words<QT, 7>(bh, t, a1, a3); break;
+            float dg, dh;
+            if (TILED) {
+                if (QT == 8) {
+                    ldsm_x4(sq + (uint32_t)(bb * 16 * G::qb) + lo8, a0, a1, a2, a3);
+                } else {
+                    uint32_t w0, w1;
+                    ldsm_x2(sq + (uint32_t)(bb * 16 * G::qb) + lo4, w0, w1);
+                    a0 = w0 & 0x0F0F0F0Fu;         // row g, elements 4t.. (low nibbles)
+                    a1 = w1 & 0x0F0F0F0Fu;         // row g + 8
+                    a2 = (w0 >> 4) & 0x0F0F0F0Fu;  // row g, elements 16+4t.. (high nibbles)
+                    a3 = (w1 >> 4) & 0x0F0F0F0Fu;
+                }
+                // scales of rows g and g + 8: one word (order 0, 8, 1, 9, ...)
+                const float2 d2 = __half22float2(*reinterpret_cast<const __half2*>(ssc + bb * 32 + 4 * g));
+                dg = d2.x;
+                dh = d2.y;
+            } else {
+                const uint8_t* bg = rg + bb * G::bpb;
+                const uint8_t* bh = rh + bb * G::bpb;
+                switch (bb) {  // bb is a constant after unrolling: the parity picks the load pattern
+                    case 0: a_words<QT, 0>(bg, t, a0, a2); a_words<QT, 0>(bh, t, a1, a3); break;
+                    case 1: a_words<QT, 1>(bg, t, a0, a2); a_words<QT, 1>(bh, t, a1, a3); break;
+                    case 2: a_words<QT, 2>(bg, t, a0, a2); a_words<QT, 2>(bh, t, a1, a3); break;
+                    case 3: a_words<QT, 3>(bg, t, a0, a2); a_words<QT, 3>(bh, t, a1, a3); break;
+                    case 4: a_words<QT, 4>(bg, t, a0, a2); a_words<QT, 4>(bh, t, a1, a3); break;
+                    case 5: a_words<QT, 5>(bg, t, a0, a2); a_words<QT, 5>(bh, t, a1, a3); break;
+                    case 6: a_words<QT, 6>(bg, t, a0, a2); a_words<QT, 6>(bh, t, a1, a3); break;
+                    default: a_words<QT, 7>(bg, t, a0, a2); a_words<QT, 7>(bh, t, a1, a3); break;
+                }
+                dg = __half2float(*reinterpret_cast<const __half*>(bg));
+                dh = __half2float(*reinterpret_cast<const __half*>(bh));
             }
-            const float dg = __half2float(*reinterpret_cast<const __half*>(bg));
-            const float dh = __half2float(*reinterpret_cast<const __half*>(bh));
             const unsigned long long dgp = f2_pack(dg, dg), dhp = f2_pack(dh, dh);
 #pragma unroll
             for (int n = 0; n < NT; n++) {
@@ -384,6 +454,123 @@ std::vector<MvbScratch> g_mvb;
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
+template <int QT, bool TILED>
+cudaError_t set_smem_attrs() {
+    using G = MvbGeom<QT>;
+    cudaError_t e = cudaFuncSetAttribute(mvb_kernel<QT, 1, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::smem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(mvb_kernel<QT, 2, TILED>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::smem);
+    // the rest of the 256 KB stays L1 for the x planes (read through the
+    // texture path).  Only a hint: a refusal is cleared so that the launch
+    // check does not report it.
+    if (cudaFuncSetAttribute(mvb_kernel<QT, 1, TILED>, cudaFuncAttributePreferredSharedMemoryCarveout, 0) != cudaSuccess)
+        (void)cudaGetLastError();
+    if (cudaFuncSetAttribute(mvb_kernel<QT, 2, TILED>, cudaFuncAttributePreferredSharedMemoryCarveout, 0) != cudaSuccess)
+        (void)cudaGetLastError();
+    return e;
+}
+
+template <int QT, bool TILED>
+void launch_mvb(int nt, int grid, cudaStream_t s, const MvbMat& mat, int nch, int ntiles, int ks,
+                const uint8_t* planes, const float* xsc, const uint32_t* xst, float* y, int nvec, float* part,
+                int* cnt) {
+    using G = MvbGeom<QT>;
+    if (nt == 1)
+        mvb_kernel<QT, 1, TILED><<<grid, kMvbThreads, G::smem, s>>>(mat, nch, ntiles, ks, planes, xsc, xst, y, nvec,
+                                                                    part, cnt);
+    else
+        mvb_kernel<QT, 2, TILED><<<grid, kMvbThreads, G::smem, s>>>(mat, nch, ntiles, ks, planes, xsc, xst, y, nvec,
+                                                                    part, cnt);
+}
+
+// Both layouts: plane split of x, then the tile dots.  nb = 32-blocks per row.
+int mvb_run(bool q8, bool tiled, const MvbMat& mat, const float* x, float* y, int nvec, cudaStream_t s,
+            std::string* err) {
+    const int nbk = mat.nb;
+    const int nch = (nbk + kMvbKc - 1) / kMvbKc;
+    const int ntiles = (mat.rows + 15) / 16;
+    const int nt = (nvec + kMvbVec - 1) / kMvbVec;  // column tiles: 1 or 2
+    const int cols = nbk * 32;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        *err = "no CUDA device";
+        return B2_ERR_CUDA;
+    }
+    std::lock_guard<std::mutex> lk(g_mvb_mu);
+    if ((int)g_mvb.size() <= dev) g_mvb.resize(dev + 1);
+    MvbScratch* sc = &g_mvb[dev];
+    if (!sc->sms && cudaDeviceGetAttribute(&sc->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        *err = "cudaDeviceGetAttribute failed";
+        return B2_ERR_CUDA;
+    }
+    if (!sc->attr_set) {
+        const cudaError_t es[4] = {set_smem_attrs<8, false>(), set_smem_attrs<2, false>(), set_smem_attrs<8, true>(),
+                                   set_smem_attrs<2, true>()};
+        for (cudaError_t e : es) {
+            if (e != cudaSuccess) {
+                *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
+                return B2_ERR_CUDA;
+            }
+        }
+        sc->attr_set = true;
+    }
+    // slices: the fewest (up to 8, at most one per chunk) giving every
+    // warp of the grid two units
+    const int warps = sc->sms * kMvbWarps;
+    int ks = 1;
+    while (ks < kMvbMaxSlices && ks < nch && (long long)ntiles * ks < 2LL * warps) ks++;
+    // Arrival counters first: ks > 1 only when ntiles * (ks - 1) < 2 * warps,
+    // so 2 * warps counters cover every split call.  They are zeroed when
+    // the buffer is allocated and each split call leaves them zero.
+    const size_t b_cnt = align256((size_t)2 * warps * 4);
+    const size_t ng = (size_t)nbk * nt;  // plane record groups
+    const size_t b_planes = align256(ng * 3 * 256);
+    const size_t b_xsc = align256(ng * kMvbVec * 4);
+    const size_t b_xst = align256(ng * 3 * kMvbVec * 4);
+    const size_t b_part = ks > 1 ? align256((size_t)ks * nt * kMvbVec * ntiles * 16 * 4) : 0;
+    const size_t need = b_cnt + b_planes + b_xsc + b_xst + b_part;
+    if (sc->bytes < need) {
+        if (sc->buf) cudaFree(sc->buf);
+        sc->buf = nullptr;
+        sc->bytes = 0;
+        if (cudaMalloc(&sc->buf, need) != cudaSuccess) {
+            *err = "scratch allocation failed";
+            return B2_ERR_OOM;
+        }
+        if (cudaMemsetAsync(sc->buf, 0, b_cnt, s) != cudaSuccess) {
+            *err = "scratch clear failed";
+            return B2_ERR_CUDA;
+        }
+        sc->bytes = need;
+    }
+    uint8_t* base = sc->buf;
+    int* cnt = reinterpret_cast<int*>(base);
+    uint8_t* planes = base + b_cnt;
+    float* xsc = reinterpret_cast<float*>(planes + b_planes);
+    uint32_t* xst = reinterpret_cast<uint32_t*>(planes + b_planes + b_xsc);
+    float* part = ks > 1 ? reinterpret_cast<float*>(planes + b_planes + b_xsc + b_xst) : nullptr;
+    const int units = ntiles * ks;
+    const int grid = std::min(sc->sms, (units + kMvbWarps - 1) / kMvbWarps);
+    const int ngrid = (int)ng;
+    // plane order: raw Q8_0 rows take the permuted order, everything else the natural one
+    if (q8 && !tiled)
+        mvb_planes_kernel<true, false><<<ngrid, kMvbThreads, 0, s>>>(x, nvec, cols, nt, planes, xsc, xst);
+    else if (q8)
+        mvb_planes_kernel<false, false><<<ngrid, kMvbThreads, 0, s>>>(x, nvec, cols, nt, planes, xsc, xst);
+    else
+        mvb_planes_kernel<false, true><<<ngrid, kMvbThreads, 0, s>>>(x, nvec, cols, nt, planes, xsc, xst);
+    if (q8 && tiled) launch_mvb<8, true>(nt, grid, s, mat, nch, ntiles, ks, planes, xsc, xst, y, nvec, part, cnt);
+    else if (q8) launch_mvb<8, false>(nt, grid, s, mat, nch, ntiles, ks, planes, xsc, xst, y, nvec, part, cnt);
+    else if (tiled) launch_mvb<2, true>(nt, grid, s, mat, nch, ntiles, ks, planes, xsc, xst, y, nvec, part, cnt);
+    else launch_mvb<2, false>(nt, grid, s, mat, nch, ntiles, ks, planes, xsc, xst, y, nvec, part, cnt);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        *err = std::string("batched matvec launch: ") + cudaGetErrorString(e);
+        return B2_ERR_CUDA;
+    }
+    return B2_OK;
+}
+
 }  // namespace
 }  // namespace b2
 
@@ -404,116 +591,31 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
         return B2_ERR_BAD_ARG;
     }
     const bool q8 = qtype == 8;
-    const int bpb = q8 ? 34 : 18;
     const int nbk = cols / 32;
-    const int nch = nbk / kMvbKc;
-    const int rb = nbk * bpb;
-    const int ntiles = (rows + 15) / 16;
-    const int nt = (nvec + kMvbVec - 1) / kMvbVec;  // column tiles: 1 or 2
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) {
-        *err = "no CUDA device";
-        return B2_ERR_CUDA;
+    const MvbMat mat{static_cast<const uint8_t*>(w), nullptr, rows, nbk * (q8 ? 34 : 18), nbk, 0};
+    return mvb_run(q8, false, mat, x, y, nvec, s, err);
+}
+
+// The same dots over a matrix resident in the decode kernel's tiled layout
+// (base = the tiled matrix, rp = its padded row count): rows [row0, row0 +
+// rows) of it, row0 a multiple of 16.
+int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
+                               const float* x, float* y, int nvec, cudaStream_t s, std::string* err) {
+    if (reinterpret_cast<uintptr_t>(x) & 3 || reinterpret_cast<uintptr_t>(y) & 3) {
+        *err = "x and y must be 4-byte aligned";
+        return B2_ERR_BAD_ARG;
     }
-    MvbScratch* sc = nullptr;
-    int ks = 1;
-    uint8_t *planes = nullptr, *base = nullptr;
-    float *xsc = nullptr, *part = nullptr;
-    uint32_t* xst = nullptr;
-    int* cnt = nullptr;
-    {
-        std::lock_guard<std::mutex> lk(g_mvb_mu);
-        if ((int)g_mvb.size() <= dev) g_mvb.resize(dev + 1);
-        sc = &g_mvb[dev];
-        if (!sc->sms && cudaDeviceGetAttribute(&sc->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-            *err = "cudaDeviceGetAttribute failed";
-            return B2_ERR_CUDA;
-        }
-        if (!sc->attr_set) {
-            const cudaError_t es[4] = {
-                cudaFuncSetAttribute(mvb_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<8>::smem),
-                cudaFuncSetAttribute(mvb_kernel<8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<8>::smem),
-                cudaFuncSetAttribute(mvb_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<2>::smem),
-                cudaFuncSetAttribute(mvb_kernel<2, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, MvbGeom<2>::smem)};
-            for (cudaError_t e : es) {
-                if (e != cudaSuccess) {
-                    *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e);
-                    return B2_ERR_CUDA;
-                }
-            }
-            // the rest of the 256 KB stays L1 for the x planes (read through the
-            // texture path).  Only a hint: a refusal is cleared so that the
-            // launch check below does not report it.
-            const cudaError_t hints[4] = {
-                cudaFuncSetAttribute(mvb_kernel<8, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0),
-                cudaFuncSetAttribute(mvb_kernel<8, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0),
-                cudaFuncSetAttribute(mvb_kernel<2, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, 0),
-                cudaFuncSetAttribute(mvb_kernel<2, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, 0)};
-            for (cudaError_t e : hints)
-                if (e != cudaSuccess) (void)cudaGetLastError();
-            sc->attr_set = true;
-        }
-        // slices: the fewest (up to 8, at most one per chunk) giving every
-        // warp of the grid two units
-        const int warps = sc->sms * kMvbWarps;
-        ks = 1;
-        while (ks < kMvbMaxSlices && ks < nch && (long long)ntiles * ks < 2LL * warps) ks++;
-        // Arrival counters first: ks > 1 only when ntiles * (ks - 1) < 2 * warps,
-        // so 2 * warps counters cover every split call.  They are zeroed when
-        // the buffer is allocated and each split call leaves them zero.
-        const size_t b_cnt = align256((size_t)2 * warps * 4);
-        const size_t ng = (size_t)nbk * nt;  // plane record groups
-        const size_t b_planes = align256(ng * 3 * 256);
-        const size_t b_xsc = align256(ng * kMvbVec * 4);
-        const size_t b_xst = align256(ng * 3 * kMvbVec * 4);
-        const size_t b_part = ks > 1 ? align256((size_t)ks * nt * kMvbVec * ntiles * 16 * 4) : 0;
-        const size_t need = b_cnt + b_planes + b_xsc + b_xst + b_part;
-        if (sc->bytes < need) {
-            if (sc->buf) cudaFree(sc->buf);
-            sc->buf = nullptr;
-            sc->bytes = 0;
-            if (cudaMalloc(&sc->buf, need) != cudaSuccess) {
-                *err = "scratch allocation failed";
-                return B2_ERR_OOM;
-            }
-            if (cudaMemsetAsync(sc->buf, 0, b_cnt, s) != cudaSuccess) {
-                *err = "scratch clear failed";
-                return B2_ERR_CUDA;
-            }
-            sc->bytes = need;
-        }
-        base = sc->buf;
-        cnt = reinterpret_cast<int*>(base);
-        planes = base + b_cnt;
-        xsc = reinterpret_cast<float*>(planes + b_planes);
-        xst = reinterpret_cast<uint32_t*>(planes + b_planes + b_xsc);
-        part = ks > 1 ? reinterpret_cast<float*>(planes + b_planes + b_xsc + b_xst) : nullptr;
-        const int units = ntiles * ks;
-        const int grid = std::min(sc->sms, (units + kMvbWarps - 1) / kMvbWarps);
-        const uint8_t* wb = static_cast<const uint8_t*>(w);
-        const int ngrid = (int)ng;
-        if (q8) {
-            mvb_planes_kernel<8><<<ngrid, kMvbThreads, 0, s>>>(x, nvec, cols, nt, planes, xsc, xst);
-            if (nt == 1)
-                mvb_kernel<8, 1><<<grid, kMvbThreads, MvbGeom<8>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
-                                                                            xsc, xst, y, nvec, part, cnt);
-            else
-                mvb_kernel<8, 2><<<grid, kMvbThreads, MvbGeom<8>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
-                                                                            xsc, xst, y, nvec, part, cnt);
-        } else {
-            mvb_planes_kernel<2><<<ngrid, kMvbThreads, 0, s>>>(x, nvec, cols, nt, planes, xsc, xst);
-            if (nt == 1)
-                mvb_kernel<2, 1><<<grid, kMvbThreads, MvbGeom<2>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
-                                                                            xsc, xst, y, nvec, part, cnt);
-            else
-                mvb_kernel<2, 2><<<grid, kMvbThreads, MvbGeom<2>::smem, s>>>(wb, rows, rb, nch, ntiles, ks, planes,
-                                                                            xsc, xst, y, nvec, part, cnt);
-        }
+    if (nvec < 1 || nvec > kMvbMaxNt * kMvbVec || cols % 32 || cols <= 0 || rows <= 0) {
+        *err = "batched matvec takes 1 to 16 vectors and cols a multiple of 32";
+        return B2_ERR_BAD_ARG;
     }
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) {
-        *err = std::string("batched matvec launch: ") + cudaGetErrorString(e);
-        return B2_ERR_CUDA;
+    if (row0 % 16 || row0 + rows > rp) {
+        *err = "tensor does not start on a 16-row tile of its matrix";
+        return B2_ERR_BAD_ARG;
     }
-    return B2_OK;
+    const bool q8 = qtype == 8;
+    const int nbk = cols / 32;
+    const uint8_t* w = static_cast<const uint8_t*>(base);
+    const MvbMat mat{w, w + (size_t)rp * nbk * (q8 ? 32 : 16), rows, 0, nbk, (int)(row0 / 16)};
+    return mvb_run(q8, true, mat, x, y, nvec, s, err);
 }

@@ -180,6 +180,15 @@ int b2_matvec(int32_t qtype, const void* w, const float* x, float* y, int32_t ro
  * so calls on different streams must not overlap. */
 int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int32_t rows, int32_t cols,
                     int32_t nvec, void* stream);
+/* The same batched dots (transformer.go:810-892 for nvec vectors) over a
+ * weight matrix of the loaded model, read from its resident tiled blocks:
+ * y[v][r] = sum_j W[r][j] * x[v][j] for the tensor `name` (this rank's share
+ * under tensor parallelism, rows and columns as b2_dequant_tensor returns
+ * them).  x [nvec][cols], y [nvec][rows] fp32 DEVICE pointers, 1 <= nvec <=
+ * 16; the model's device must be current.  stream NULL = the model's own
+ * stream.  The gate and up matrices are stored interleaved and are rejected.
+ * Shares the per-device scratch of b2_matvec_batch. */
+int b2_model_matvec(const b2_model* m, const char* name, const float* x, float* y, int32_t nvec, void* stream);
 
 /* transformer.go:663-685 attention of one query token per sequence over an
  * fp16 KV cache, split over the context with a log-sum-exp merge.

@@ -132,6 +132,10 @@ def test_tensor_parallel_load_needs_a_gpu(built_lib, tiny_gguf):
     assert code == -5 and "no CUDA device" in msg
 
 
+def test_model_matvec_rejects_null_model(built_lib):
+    assert b2decode.lib().b2_model_matvec(None, b"token_embd.weight", 4096, 8192, 8, None) == -10
+
+
 def test_tp_entry_points_reject_null(built_lib):
     L = b2decode.lib()
     assert L.b2_tp_handle(None, b"\0" * 64) == -10

@@ -113,3 +113,46 @@ def test_batch1_agrees_with_b2_matvec(built_lib, oracle_lib, torch_cuda):
     b2decode.matvec(8, dw.data_ptr(), dx.data_ptr(), dy.data_ptr(), rows, cols)
     torch.cuda.synchronize()
     assert rel_l2(got, dy.cpu().numpy()) < 2 * TOL
+
+
+MODEL_SHAPES = {
+    "tiny-q8": gw.SHAPES["tiny"],
+    "tiny-llama-q4": gw.SHAPES["tiny-llama-q4"],
+    "wide-q4": gw.ModelShape("llama", 1024, 1, 8, 2, 2816, 1000, 256, 1e-5, 5e5, False, False, "q4_0", 1, 2),
+    "wide-q8": gw.ModelShape("qwen2", 1024, 1, 8, 2, 2816, 1000, 256, 1e-6, 1e6, True, False, "q8_0", 1, 2),
+}
+
+
+@pytest.mark.parametrize("key", list(MODEL_SHAPES))
+def test_model_matvec_over_resident_tiled_weights(built_lib, oracle_lib, torch_cuda, write_model, key):
+    """b2_model_matvec reads the loader's tiled blocks: every projection of
+    layer 0 (k and v start inside the fused QKV matrix), the embedding and
+    the untied lm_head, against the dequantised tensor (bit-exact with the
+    oracle) times x in float64."""
+    torch = torch_cuda
+    shape = MODEL_SHAPES[key]
+    m = b2decode.Model(write_model(key, shape), num_ctx=64)
+    H, qd, kvd, ff, V = shape.hidden, shape.hidden, shape.kv_dim, shape.ffn, shape.vocab
+    dims = {"blk.0.attn_q.weight": (qd, H), "blk.0.attn_k.weight": (kvd, H), "blk.0.attn_v.weight": (kvd, H),
+            "blk.0.attn_output.weight": (H, qd), "blk.0.ffn_down.weight": (H, ff), "token_embd.weight": (V, H)}
+    if not shape.tied:
+        dims["output.weight"] = (V, H)
+    rng = np.random.default_rng(3)
+    for name, (rows, cols) in dims.items():
+        w = m.dequant(name, rows * cols).reshape(rows, cols).astype(np.float64)
+        for nvec in (1, 8, 13):
+            x = rng.standard_normal((nvec, cols), dtype=np.float32)
+            dx = torch.from_numpy(x).cuda()
+            dy = torch.full((nvec, rows), float("nan"), device="cuda")
+            m.matvec(name, dx.data_ptr(), dy.data_ptr(), nvec)
+            torch.cuda.synchronize()
+            got = dy.cpu().numpy()
+            want = x.astype(np.float64) @ w.T
+            for v in range(nvec):
+                assert rel_l2(got[v], want[v]) < TOL, (name, nvec, v, rel_l2(got[v], want[v]))
+    x = torch.zeros((1, H), device="cuda")
+    y = torch.zeros((1, ff), device="cuda")
+    with pytest.raises(b2decode.B2Error) as e:
+        m.matvec("blk.0.ffn_gate.weight", x.data_ptr(), y.data_ptr(), 1)
+    assert e.value.code == -8
+    m.close()
