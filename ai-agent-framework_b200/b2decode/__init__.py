@@ -98,6 +98,11 @@ SIGNATURES = {
     "b2_matvec": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _P]),
     "b2_matvec_batch": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _i32, _P]),
     "b2_model_matvec": (C.c_int, [_P, C.c_char_p, _P, _P, _i32, _P]),
+    "b2_batch_create": (C.c_int, [_P, _i32, C.POINTER(_P)]),
+    "b2_batch_free": (None, [_P]),
+    "b2_batch_prefill": (C.c_int, [_P, _i32, _i32p, _i32, C.POINTER(_i32)]),
+    "b2_batch_step": (C.c_int, [_P, _i32p, _i32p]),
+    "b2_batch_logits": (C.c_int, [_P, _f32p]),
     "b2_attention_decode": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_attention_decode_noalloc": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_device_status": (C.c_int, [_P]),
@@ -287,6 +292,50 @@ def sample_logits(logits, opts: SampleOpts, generated=(), r: float = 0.5) -> int
     g, gp = _ids(list(generated) or [0])
     return int(lib().b2_sample_logits(lg.ctypes.data_as(_f32p), lg.size, C.byref(opts), gp, len(generated),
                                       float(r)))
+
+
+class Batch:
+    """Batched greedy decode over a loaded single-GPU Model: `batch` slots,
+    each a sequence with its own KV cache, advancing one token per step
+    together (b2_batch_*)."""
+
+    def __init__(self, model: "Model", batch: int):
+        h = _P()
+        _check(lib().b2_batch_create(model._h, int(batch), C.byref(h)))
+        self._h, self.model, self.batch = h, model, int(batch)
+        self.vocab = int(model.vocab)
+
+    def prefill(self, slot: int, prompt) -> int:
+        """Runs the prompt into the slot; returns the argmax after it."""
+        arr, p = _ids(prompt)
+        nxt = C.c_int32()
+        _check(lib().b2_batch_prefill(self._h, int(slot), p, len(arr), C.byref(nxt)))
+        return nxt.value
+
+    def step(self, tokens) -> np.ndarray:
+        """Feeds one token per slot; returns the next id of every slot."""
+        arr, p = _ids(tokens)
+        if len(arr) != self.batch:
+            raise ValueError("one token per slot")
+        out = np.zeros(self.batch, dtype=np.int32)
+        _check(lib().b2_batch_step(self._h, p, out.ctypes.data_as(_i32p)))
+        return out
+
+    def logits(self) -> np.ndarray:
+        out = np.empty((self.batch, self.vocab), dtype=np.float32)
+        _check(lib().b2_batch_logits(self._h, out.ctypes.data_as(_f32p)))
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            lib().b2_batch_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def matvec(qtype: int, w_ptr: int, x_ptr: int, y_ptr: int, rows: int, cols: int, stream: int = 0) -> None:

@@ -19,6 +19,11 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
                          cudaStream_t s, std::string* err);
 int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
+int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err);
+void b2_batch_free_impl(b2_batch* bt);
+int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, int32_t* next_out, std::string* err);
+int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, std::string* err);
+int b2_batch_logits_impl(const b2_batch* bt, float* out, std::string* err);
 int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh, int nkv,
                       int hd, int ctx, cudaStream_t s, std::string* err);
 int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh,
@@ -442,6 +447,37 @@ int b2_model_matvec(const b2_model* m, const char* name, const float* x, float* 
     int rc = b2_tiled_matvec_batch_impl((int)t.type, t.dev, t.rp, t.row0, rows, (int)t.cols, x, y, nvec,
                                         stream ? static_cast<cudaStream_t>(stream) : m->stream, &err);
     return ret(rc, err);
+}
+
+int b2_batch_create(b2_model* m, int32_t batch, b2_batch** out) {
+    if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
+    if (!out) return ret(B2_ERR_BAD_ARG, "null argument");
+    *out = nullptr;
+    std::string err;
+    return ret(b2_batch_create_impl(m, batch, out, &err), err);
+}
+
+void b2_batch_free(b2_batch* b) { b2_batch_free_impl(b); }
+
+int b2_batch_prefill(b2_batch* b, int32_t slot, const int32_t* prompt, int32_t n, int32_t* next_out) {
+    if (!b) return ret(B2_ERR_NOT_LOADED, "no batch");
+    if (!prompt || !next_out) return ret(B2_ERR_BAD_ARG, "null argument");
+    std::string err;
+    return ret(b2_batch_prefill_impl(b, slot, prompt, n, next_out, &err), err);
+}
+
+int b2_batch_step(b2_batch* b, const int32_t* tokens, int32_t* next_out) {
+    if (!b) return ret(B2_ERR_NOT_LOADED, "no batch");
+    if (!tokens || !next_out) return ret(B2_ERR_BAD_ARG, "null argument");
+    std::string err;
+    return ret(b2_batch_step_impl(b, tokens, next_out, &err), err);
+}
+
+int b2_batch_logits(const b2_batch* b, float* out) {
+    if (!b) return ret(B2_ERR_NOT_LOADED, "no batch");
+    if (!out) return ret(B2_ERR_BAD_ARG, "null argument");
+    std::string err;
+    return ret(b2_batch_logits_impl(b, out, &err), err);
 }
 
 int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch, int32_t nh,

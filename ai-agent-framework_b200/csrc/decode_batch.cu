@@ -1,0 +1,406 @@
+// Batched greedy decode: up to 16 sequences advance one token per step
+// together, each at its own position in a KV cache of its own, so a step
+// reads every weight byte once for all of them (transformer.go:519-739, the
+// forward of one new token, for B sequences at a time; argmax
+// transformer.go:1038-1046).
+//
+// A step is a sequence of launches on the model's stream:
+//   embedding rows of the B tokens (the tiled token_embd, decoded on the fly)
+//   per layer: RMSNorm -> batched tile dot over [Wq; Wk; Wv] -> bias, RoPE
+//   and the KV append at each sequence's position -> attention over each
+//   sequence's own length -> Wo tile dot -> residual add -> RMSNorm ->
+//   gate/up tile dot (interleaved 8 rows at a time) -> SwiGLU -> down tile dot
+//   -> residual add
+//   final RMSNorm -> lm_head tile dot -> argmax per sequence (first maximum).
+// The tile dots are the batched matvec over the resident tiled weights
+// (matvec_batch.cu); prefill of a sequence runs on the single-sequence
+// decode kernel and its KV rows are copied into the sequence's slot.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "../../include/b2decode.h"
+#include "dev.cuh"
+#include "model.h"
+
+int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
+                               const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
+int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, float* part, size_t part_floats,
+                             float* out, int batch, int nh, int nkv, int hd, const int* lens, int add, int stride,
+                             int max_len, int sms, cudaStream_t s);
+
+constexpr int kBatchMax = 16;
+constexpr int kBatchSplits = 32;  // attention splits the partial buffer holds
+
+struct b2_batch {
+    b2_model* m = nullptr;
+    int B = 0;
+    int max_seq = 0;
+    void* arena = nullptr;
+    __half* kc = nullptr;  // [L][B][max_seq][kvd]
+    __half* vc = nullptr;
+    float *x = nullptr, *xn = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr;
+    float *gu = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+    size_t part_floats = 0;
+    int *d_pos = nullptr, *d_tok = nullptr, *d_next = nullptr;  // [B]
+    int* h_io = nullptr;                                        // pinned [2B]
+    std::vector<int> pos;                                       // positions (host copy)
+};
+
+namespace b2 {
+namespace {
+
+constexpr int kBdThreads = 256;
+
+// Row `tok` of the tiled embedding (gguf.go:540-582 dequant, Q4_0 in the
+// ggml element order); an id outside the vocabulary embeds to zero.
+__global__ void bd_embed_kernel(const uint8_t* __restrict__ emb, int V, int64_t rp, int H, int qt,
+                                const int* __restrict__ tok, float* __restrict__ x) {
+    const int b = blockIdx.x, t = tok[b];
+    const int64_t nb = H / 32;
+    for (int j = threadIdx.x; j < H; j += blockDim.x) {
+        float v = 0.0f;
+        if (t >= 0 && t < V) {
+            const int64_t blk = j >> 5;
+            const int e = j & 31;
+            const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(emb + tiled_soff(t, blk, nb, rp, qt)));
+            if (qt == 8) {
+                v = d * (float)(int8_t)emb[tiled_qoff(t, blk, e, nb, 8)];
+            } else {
+                const uint8_t byte = emb[tiled_qoff(t, blk, e & 15, nb, 2)];
+                v = d * (float)(((e < 16) ? (byte & 15) : (byte >> 4)) - 8);
+            }
+        }
+        x[(size_t)b * H + j] = v;
+    }
+}
+
+// transformer.go:922-932 rmsNorm of each sequence's row: x * r * w with
+// r = 1 / sqrt(mean(x^2) + eps) (the root in double, as the Go code).
+__global__ void bd_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
+                                  int H, float eps) {
+    __shared__ float red[kBdThreads / 32];
+    __shared__ float rs;
+    const int b = blockIdx.x;
+    const float* xb = x + (size_t)b * H;
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < H; j += blockDim.x) ss = fmaf(xb[j], xb[j], ss);
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < kBdThreads / 32; i++) t += red[i];
+        rs = (float)(1.0 / sqrt((double)(t / (float)H) + (double)eps));
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < H; j += blockDim.x) out[(size_t)b * H + j] = xb[j] * rs * w[j];
+}
+
+// transformer.go:632-656: bias, RoPE on interleaved pairs of every q and k
+// head at the sequence's position (936-951, the model's cos / sin table),
+// then k and v appended to the sequence's cache slot; q kept for attention.
+__global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, const float* __restrict__ bias,
+                                  const float* __restrict__ cosT, const float* __restrict__ sinT,
+                                  const int* __restrict__ pos, float* __restrict__ q, __half* __restrict__ kc,
+                                  __half* __restrict__ vc, int qd, int kvd, int hd, int B, int max_seq) {
+    const int b = blockIdx.x, p = pos[b], n = qd + 2 * kvd, hh = hd / 2;
+    const float* row = qkv + (size_t)b * n;
+    for (int j = threadIdx.x; j < n / 2; j += blockDim.x) {
+        const int r = 2 * j;
+        float a0 = row[r], a1 = row[r + 1];
+        if (bias) {
+            a0 += bias[r];
+            a1 += bias[r + 1];
+        }
+        if (r < qd + kvd) {
+            const int pi2 = (r % hd) >> 1;
+            const float c = cosT[(size_t)p * hh + pi2], s = sinT[(size_t)p * hh + pi2];
+            const float x0 = a0, x1 = a1;
+            a0 = x0 * c - x1 * s;
+            a1 = x0 * s + x1 * c;
+        }
+        if (r < qd) {
+            q[(size_t)b * qd + r] = a0;
+            q[(size_t)b * qd + r + 1] = a1;
+        } else {
+            const bool isk = r < qd + kvd;
+            const int col = r - qd - (isk ? 0 : kvd);
+            __half* cache = isk ? kc : vc;
+            *reinterpret_cast<__half2*>(cache + ((size_t)b * max_seq + p) * kvd + col) = __floats2half2_rn(a0, a1);
+        }
+    }
+}
+
+__global__ void bd_add_kernel(float* __restrict__ x, const float* __restrict__ y, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) x[i] += y[i];
+}
+
+// transformer.go:725-727, 954-956 SwiGLU over the interleaved gate/up
+// output: output j of tile t has its gate at row 16t + j % 8, its up 8 rows
+// below.
+__global__ void bd_swiglu_kernel(const float* __restrict__ gu, float* __restrict__ act, int FF, int B) {
+    const int n = B * FF;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int b = i / FF, j = i - b * FF;
+        const float* g = gu + (size_t)b * 2 * FF + (size_t)(j >> 3) * 16 + (j & 7);
+        const float gv = g[0], uv = g[8];
+        act[i] = gv / (1.0f + expf(-gv)) * uv;
+    }
+}
+
+// transformer.go:1038-1046 argmax per sequence (the first maximum wins);
+// then the sequence's position moves past the token just appended.
+__global__ void bd_argmax_kernel(const float* __restrict__ logits, int V, int* __restrict__ next,
+                                 int* __restrict__ pos) {
+    __shared__ float bv[kBdThreads];
+    __shared__ int bi[kBdThreads];
+    const int b = blockIdx.x;
+    const float* lb = logits + (size_t)b * V;
+    float best = -INFINITY;
+    int idx = V;
+    for (int j = threadIdx.x; j < V; j += blockDim.x)
+        if (lb[j] > best) {
+            best = lb[j];
+            idx = j;
+        }
+    bv[threadIdx.x] = best;
+    bi[threadIdx.x] = idx;
+    __syncthreads();
+    for (int o = kBdThreads / 2; o; o >>= 1) {
+        if ((int)threadIdx.x < o) {
+            const float v2 = bv[threadIdx.x + o];
+            const int i2 = bi[threadIdx.x + o];
+            if (v2 > bv[threadIdx.x] || (v2 == bv[threadIdx.x] && i2 < bi[threadIdx.x])) {
+                bv[threadIdx.x] = v2;
+                bi[threadIdx.x] = i2;
+            }
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        next[b] = bi[0] < V ? bi[0] : 0;
+        pos[b] += 1;
+    }
+}
+
+bool ok(cudaError_t e, std::string* err, const char* what) {
+    if (e == cudaSuccess) return true;
+    *err = std::string(what) + ": " + cudaGetErrorString(e);
+    return false;
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
+    const ModelDev& d = m->dev;
+    if (B < 1 || B > kBatchMax) {
+        *err = "batch size must be 1 to 16";
+        return B2_ERR_BAD_ARG;
+    }
+    if (d.tp > 1 || d.kv_fp32) {
+        *err = "batched decode needs a single-GPU model with the fp16 KV cache";
+        return B2_ERR_BAD_ARG;
+    }
+    if ((d.hd != 64 && d.hd != 128 && d.hd != 256) || d.nh / d.nkv > 8) {
+        *err = "batched decode attention needs head_dim 64, 128 or 256 and at most 8 query heads per KV head";
+        return B2_ERR_UNSUPPORTED_TYPE;
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device) {
+        *err = "the model's device must be the current device";
+        return B2_ERR_BAD_ARG;
+    }
+    b2_batch* bt = new b2_batch;
+    bt->m = m;
+    bt->B = B;
+    bt->max_seq = d.max_seq;
+    bt->pos.assign(B, 0);
+    const size_t kv = (size_t)d.L * B * d.max_seq * d.kvd;
+    const int n_qkv = d.qd + 2 * d.kvd;
+    bt->part_floats = (size_t)B * d.nh * kBatchSplits * (d.hd + 2);
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 255) & ~size_t(255);
+        return o;
+    };
+    const size_t o_kc = take(kv * 2), o_vc = take(kv * 2);
+    const size_t o_x = take((size_t)B * d.H * 4), o_xn = take((size_t)B * d.H * 4), o_y = take((size_t)B * d.H * 4);
+    const size_t o_qkv = take((size_t)B * n_qkv * 4), o_q = take((size_t)B * d.qd * 4);
+    const size_t o_att = take((size_t)B * d.qd * 4);
+    const size_t o_gu = take((size_t)B * 2 * d.FF * 4), o_act = take((size_t)B * d.FF * 4);
+    const size_t o_lg = take((size_t)B * d.V * 4), o_part = take(bt->part_floats * 4);
+    const size_t o_pos = take((size_t)B * 4), o_tok = take((size_t)B * 4), o_next = take((size_t)B * 4);
+    if (cudaMalloc(&bt->arena, off) != cudaSuccess) {
+        delete bt;
+        *err = "device allocation of the batch state failed";
+        return B2_ERR_OOM;
+    }
+    if (cudaMallocHost(&bt->h_io, sizeof(int) * 2 * B) != cudaSuccess) {
+        cudaFree(bt->arena);
+        delete bt;
+        *err = "pinned host allocation failed";
+        return B2_ERR_OOM;
+    }
+    uint8_t* A = static_cast<uint8_t*>(bt->arena);
+    bt->kc = reinterpret_cast<__half*>(A + o_kc);
+    bt->vc = reinterpret_cast<__half*>(A + o_vc);
+    bt->x = reinterpret_cast<float*>(A + o_x);
+    bt->xn = reinterpret_cast<float*>(A + o_xn);
+    bt->y = reinterpret_cast<float*>(A + o_y);
+    bt->qkv = reinterpret_cast<float*>(A + o_qkv);
+    bt->q = reinterpret_cast<float*>(A + o_q);
+    bt->att = reinterpret_cast<float*>(A + o_att);
+    bt->gu = reinterpret_cast<float*>(A + o_gu);
+    bt->act = reinterpret_cast<float*>(A + o_act);
+    bt->logits = reinterpret_cast<float*>(A + o_lg);
+    bt->part = reinterpret_cast<float*>(A + o_part);
+    bt->d_pos = reinterpret_cast<int*>(A + o_pos);
+    bt->d_tok = reinterpret_cast<int*>(A + o_tok);
+    bt->d_next = reinterpret_cast<int*>(A + o_next);
+    if (!ok(cudaMemsetAsync(bt->arena, 0, off, m->stream), err, "clear") ||
+        !ok(cudaStreamSynchronize(m->stream), err, "clear")) {
+        cudaFreeHost(bt->h_io);
+        cudaFree(bt->arena);
+        delete bt;
+        return B2_ERR_CUDA;
+    }
+    *out = bt;
+    return B2_OK;
+}
+
+void b2_batch_free_impl(b2_batch* bt) {
+    if (!bt) return;
+    if (bt->m && bt->m->stream) cudaStreamSynchronize(bt->m->stream);
+    if (bt->h_io) cudaFreeHost(bt->h_io);
+    if (bt->arena) cudaFree(bt->arena);
+    delete bt;
+}
+
+// The slot's sequence: prefill on the single-sequence path (which leaves the
+// model's own cache holding the prompt), then its KV rows copied into the slot.
+int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, int32_t* next_out, std::string* err) {
+    b2_model* m = bt->m;
+    const ModelDev& d = m->dev;
+    if (slot < 0 || slot >= bt->B) {
+        *err = "slot outside the batch";
+        return B2_ERR_BAD_ARG;
+    }
+    if (n < 1 || n >= bt->max_seq) {
+        *err = "prompt length must be 1 .. max_seq - 1";
+        return B2_ERR_CONTEXT;
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device) {
+        *err = "the model's device must be the current device";
+        return B2_ERR_BAD_ARG;
+    }
+    int rc = b2_reset(m);
+    if (rc == B2_OK) rc = b2_forward_argmax(m, prompt, n, next_out);
+    if (rc) {
+        *err = b2_last_error();
+        return rc;
+    }
+    const size_t row = (size_t)d.kvd * sizeof(__half);
+    for (int l = 0; l < d.L; l++) {
+        const size_t dst = ((size_t)l * bt->B + slot) * bt->max_seq * d.kvd;
+        const size_t src = (size_t)l * d.max_seq * d.kvd;
+        if (!ok(cudaMemcpyAsync(bt->kc + dst, static_cast<const __half*>(d.kcache) + src, row * n,
+                                cudaMemcpyDeviceToDevice, m->stream), err, "KV copy") ||
+            !ok(cudaMemcpyAsync(bt->vc + dst, static_cast<const __half*>(d.vcache) + src, row * n,
+                                cudaMemcpyDeviceToDevice, m->stream), err, "KV copy"))
+            return B2_ERR_CUDA;
+    }
+    bt->pos[slot] = n;
+    bt->h_io[0] = n;
+    if (!ok(cudaMemcpyAsync(bt->d_pos + slot, bt->h_io, sizeof(int), cudaMemcpyHostToDevice, m->stream), err,
+            "position") ||
+        !ok(cudaStreamSynchronize(m->stream), err, "prefill"))
+        return B2_ERR_CUDA;
+    return B2_OK;
+}
+
+int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, std::string* err) {
+    b2_model* m = bt->m;
+    const ModelDev& d = m->dev;
+    const int B = bt->B;
+    cudaStream_t s = m->stream;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device) {
+        *err = "the model's device must be the current device";
+        return B2_ERR_BAD_ARG;
+    }
+    int max_len = 0;
+    for (int b = 0; b < B; b++) {
+        if (bt->pos[b] + 1 > bt->max_seq) {
+            *err = "a sequence of the batch is at the KV-cache capacity";
+            return B2_ERR_CONTEXT;
+        }
+        max_len = std::max(max_len, bt->pos[b] + 1);
+    }
+    for (int b = 0; b < B; b++) bt->h_io[b] = tokens[b];
+    if (!ok(cudaMemcpyAsync(bt->d_tok, bt->h_io, sizeof(int) * B, cudaMemcpyHostToDevice, s), err, "tokens"))
+        return B2_ERR_CUDA;
+    const int H = d.H, qt = d.qtype, n_qkv = d.qd + 2 * d.kvd;
+    bd_embed_kernel<<<B, kBdThreads, 0, s>>>(d.tok_embd, d.Vemb, d.Vp_emb, H, qt, bt->d_tok, bt->x);
+    const int ew_blocks = std::max(1, std::min(m->grid * 4, (B * 2 * d.FF + kBdThreads - 1) / kBdThreads));
+    const size_t kv_layer = (size_t)B * bt->max_seq * d.kvd;
+    int rc = B2_OK;
+    for (int l = 0; l < d.L && rc == B2_OK; l++) {
+        const LayerDev& ld = m->layers_host[l];
+        bd_rmsnorm_kernel<<<B, kBdThreads, 0, s>>>(bt->x, ld.attn_norm, bt->xn, H, d.eps);
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wqkv, tiled_rows(n_qkv), 0, n_qkv, H, bt->xn, bt->qkv, B, s, err);
+        if (rc) break;
+        __half* kc = bt->kc + (size_t)l * kv_layer;
+        __half* vc = bt->vc + (size_t)l * kv_layer;
+        bd_rope_kv_kernel<<<B, kBdThreads, 0, s>>>(bt->qkv, ld.bqkv, d.rope_cos, d.rope_sin, bt->d_pos, bt->q, kc, vc,
+                                                   d.qd, d.kvd, d.hd, B, bt->max_seq);
+        rc = b2_attention_seqs_launch(bt->q, kc, vc, bt->part, bt->part_floats, bt->att, B, d.nh, d.nkv, d.hd,
+                                      bt->d_pos, 1, bt->max_seq, max_len, m->grid, s);
+        if (rc) {
+            *err = "batched attention launch failed";
+            break;
+        }
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wo, tiled_rows(H), 0, H, d.qd, bt->att, bt->y, B, s, err);
+        if (rc) break;
+        bd_add_kernel<<<std::max(1, (B * H + kBdThreads - 1) / kBdThreads), kBdThreads, 0, s>>>(bt->x, bt->y, B * H);
+        bd_rmsnorm_kernel<<<B, kBdThreads, 0, s>>>(bt->x, ld.ffn_norm, bt->xn, H, d.eps);
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wgu, tiled_rows(2 * d.FF), 0, 2 * d.FF, H, bt->xn, bt->gu, B, s, err);
+        if (rc) break;
+        bd_swiglu_kernel<<<ew_blocks, kBdThreads, 0, s>>>(bt->gu, bt->act, d.FF, B);
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wd, tiled_rows(H), 0, H, d.FF, bt->act, bt->y, B, s, err);
+        if (rc) break;
+        bd_add_kernel<<<std::max(1, (B * H + kBdThreads - 1) / kBdThreads), kBdThreads, 0, s>>>(bt->x, bt->y, B * H);
+    }
+    if (rc) return rc;
+    bd_rmsnorm_kernel<<<B, kBdThreads, 0, s>>>(bt->x, d.out_norm, bt->xn, H, d.eps);
+    rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn, bt->logits, B, s, err);
+    if (rc) return rc;
+    bd_argmax_kernel<<<B, kBdThreads, 0, s>>>(bt->logits, d.V, bt->d_next, bt->d_pos);
+    if (!ok(cudaGetLastError(), err, "batched decode launch") ||
+        !ok(cudaMemcpyAsync(bt->h_io + B, bt->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, s), err, "ids") ||
+        !ok(cudaStreamSynchronize(s), err, "batched decode"))
+        return B2_ERR_CUDA;
+    for (int b = 0; b < B; b++) {
+        next_out[b] = bt->h_io[B + b];
+        bt->pos[b] += 1;
+    }
+    return B2_OK;
+}
+
+// Logits of the last step, [B][vocab] floats.
+int b2_batch_logits_impl(const b2_batch* bt, float* out, std::string* err) {
+    const size_t n = (size_t)bt->B * bt->m->dev.V;
+    if (!ok(cudaMemcpyAsync(out, bt->logits, n * sizeof(float), cudaMemcpyDeviceToHost, bt->m->stream), err,
+            "logits") ||
+        !ok(cudaStreamSynchronize(bt->m->stream), err, "logits"))
+        return B2_ERR_CUDA;
+    return B2_OK;
+}

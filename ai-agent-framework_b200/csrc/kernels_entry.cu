@@ -55,20 +55,30 @@ constexpr int kMaxDimsLane = 8; // head_dim up to 256
 // U steps before using them, so enough bytes are in flight to stream the
 // cache.  Groups merge by shuffles, warps through shared memory; the CTA
 // writes one partial (o unnormalised, m, l) per query head.
-template <int HD, int GRP>
+// VAR: sequences of their own lengths (lens[b] + add positions) in caches
+// `stride` positions apart (a batch of decode sequences); otherwise every
+// sequence has ctx positions, stored back to back.
+struct AttnSeqs {
+    const int* lens;
+    int add, stride;
+};
+
+template <int HD, int GRP, bool VAR>
 __global__ void __launch_bounds__(kAttThreads, (GRP <= 4 ? 2 : 1))
     attn_split_kernel(const float* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
-                      float* __restrict__ part, int nh, int nkv, int ctx, int S) {
+                      float* __restrict__ part, int nh, int nkv, int ctx, int S, const AttnSeqs seqs) {
     constexpr int DL = 8, LP = HD / DL, G = 32 / LP, U = GRP <= 3 ? 4 : (GRP == 4 ? 3 : 2);
     extern __shared__ float sm[];
     const int cta = blockIdx.x;
     const int s = cta % S, g = (cta / S) % nkv, b = cta / (S * nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grp = lane / LP, d0 = (lane % LP) * DL;
-    const int t0 = (int)((long long)s * ctx / S), t1 = (int)((long long)(s + 1) * ctx / S);
+    const int len = VAR ? __ldg(seqs.lens + b) + seqs.add : ctx;
+    const int t0 = (int)((long long)s * len / S), t1 = (int)((long long)(s + 1) * len / S);
     const size_t kvd = (size_t)nkv * HD;
-    const __half* kb = k + (size_t)b * ctx * kvd + (size_t)g * HD + d0;
-    const __half* vb = v + (size_t)b * ctx * kvd + (size_t)g * HD + d0;
+    const size_t bstride = VAR ? (size_t)seqs.stride : (size_t)ctx;
+    const __half* kb = k + (size_t)b * bstride * kvd + (size_t)g * HD + d0;
+    const __half* vb = v + (size_t)b * bstride * kvd + (size_t)g * HD + d0;
     const float scale = (float)(1.0 / sqrt((double)HD));
     float qr[GRP][DL], o[GRP][DL], mr[GRP], lr[GRP];
 #pragma unroll
@@ -179,34 +189,42 @@ __global__ void __launch_bounds__(kAttThreads, (GRP <= 4 ? 2 : 1))
 
 // Launches attn_split_kernel for head dimension hd (64, 128, 256) and group
 // size grp (1 .. 8); returns false for other geometries.
-template <int HD>
+template <int HD, bool VAR>
 bool launch_split_hd(int grp, int grid, cudaStream_t st, const float* q, const __half* k, const __half* v, float* part,
-                     int nh, int nkv, int ctx, int S) {
+                     int nh, int nkv, int ctx, int S, const AttnSeqs& seqs) {
     auto go = [&](auto kern, int g) {
         const size_t smem = sizeof(float) * (size_t)kAttWarps * g * (HD + 2);
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, kAttThreads, smem, st>>>(q, k, v, part, nh, nkv, ctx, S);
+        kern<<<grid, kAttThreads, smem, st>>>(q, k, v, part, nh, nkv, ctx, S, seqs);
         return true;
     };
     switch (grp) {
-        case 1: return go(attn_split_kernel<HD, 1>, 1);
-        case 2: return go(attn_split_kernel<HD, 2>, 2);
-        case 3: return go(attn_split_kernel<HD, 3>, 3);
-        case 4: return go(attn_split_kernel<HD, 4>, 4);
-        case 5: return go(attn_split_kernel<HD, 5>, 5);
-        case 6: return go(attn_split_kernel<HD, 6>, 6);
-        case 7: return go(attn_split_kernel<HD, 7>, 7);
-        case 8: return go(attn_split_kernel<HD, 8>, 8);
+        case 1: return go(attn_split_kernel<HD, 1, VAR>, 1);
+        case 2: return go(attn_split_kernel<HD, 2, VAR>, 2);
+        case 3: return go(attn_split_kernel<HD, 3, VAR>, 3);
+        case 4: return go(attn_split_kernel<HD, 4, VAR>, 4);
+        case 5: return go(attn_split_kernel<HD, 5, VAR>, 5);
+        case 6: return go(attn_split_kernel<HD, 6, VAR>, 6);
+        case 7: return go(attn_split_kernel<HD, 7, VAR>, 7);
+        case 8: return go(attn_split_kernel<HD, 8, VAR>, 8);
         default: return false;
     }
 }
 
+// seqs null: every sequence has ctx positions stored back to back.
 bool launch_split(int hd, int grp, int grid, cudaStream_t st, const float* q, const __half* k, const __half* v,
-                  float* part, int nh, int nkv, int ctx, int S) {
+                  float* part, int nh, int nkv, int ctx, int S, const AttnSeqs* seqs = nullptr) {
+    const AttnSeqs none{nullptr, 0, 0};
     switch (hd) {
-        case 64: return launch_split_hd<64>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S);
-        case 128: return launch_split_hd<128>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S);
-        case 256: return launch_split_hd<256>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S);
+        case 64:
+            return seqs ? launch_split_hd<64, true>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, *seqs)
+                        : launch_split_hd<64, false>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, none);
+        case 128:
+            return seqs ? launch_split_hd<128, true>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, *seqs)
+                        : launch_split_hd<128, false>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, none);
+        case 256:
+            return seqs ? launch_split_hd<256, true>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, *seqs)
+                        : launch_split_hd<256, false>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, none);
         default: return false;
     }
 }
@@ -322,6 +340,24 @@ int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, floa
         return B2_ERR_CUDA;
     }
     return B2_OK;
+}
+
+// Attention of a batch of decode sequences with lengths of their own: q
+// [batch][nh*hd]; sequence b has lens[b] + add cached positions at k, v +
+// b * stride * nkv * hd (fp16).  part holds part_floats floats for the split
+// partials (the split count is capped to fit).  Used by the batched decode.
+int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, float* part, size_t part_floats,
+                             float* out, int batch, int nh, int nkv, int hd, const int* lens, int add, int stride,
+                             int max_len, int sms, cudaStream_t s) {
+    const int grp = nh / nkv;
+    if (grp > kMaxGrp || (hd != 64 && hd != 128 && hd != 256)) return B2_ERR_UNSUPPORTED_TYPE;
+    int S = attention_splits(batch, nkv, max_len, sms);
+    const size_t per_split = (size_t)batch * nh * (hd + 2);
+    S = (int)std::max<size_t>(1, std::min<size_t>((size_t)S, part_floats / per_split));
+    const AttnSeqs seqs{lens, add, stride};
+    if (!launch_split(hd, grp, batch * nkv * S, s, q, k, v, part, nh, nkv, 0, S, &seqs)) return B2_ERR_UNSUPPORTED_TYPE;
+    attn_merge_kernel<<<batch * nh, std::min(hd, 256), 0, s>>>(part, out, nh, hd, S);
+    return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
 // ---------------------------------------------------------------------------

@@ -39,6 +39,7 @@ extern "C" {
 #define B2_ERR_NOT_LOADED (-10)      /* model handle is NULL or unloaded */
 
 typedef struct b2_model b2_model;
+typedef struct b2_batch b2_batch;
 
 /* engine.go:42-47 LoadOptions, plus device placement. */
 typedef struct {
@@ -210,6 +211,25 @@ int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, fl
  * No counterpart in the reference. */
 int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
                                 int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream);
+
+/* ---- batched greedy decode (config: Llama-3-8B at batch 16) ----
+ *
+ * Up to 16 sequences, each with a KV-cache slot of its own (max_seq = the
+ * model's num_ctx, fp16), advance one token per b2_batch_step together, each
+ * at its own position, so every weight byte is read once per step for all of
+ * them: the forward of transformer.go:519-739 and argmax 1038-1046 for B
+ * sequences at a time.  b2_batch_prefill runs a slot's prompt on the model's
+ * single-sequence path (it resets the model's own cache) and copies its KV
+ * rows into the slot; next_out is the argmax after the prompt.  b2_batch_step
+ * feeds tokens[B] (one per slot, every slot) and writes the B argmax ids;
+ * b2_batch_logits copies the last step's logits, [B][vocab_size].  Needs a
+ * single-GPU model with the fp16 cache; the model's device must be current.
+ * No single counterpart in the reference (its engine runs one sequence). */
+int b2_batch_create(b2_model* m, int32_t batch, b2_batch** out);
+void b2_batch_free(b2_batch* b);
+int b2_batch_prefill(b2_batch* b, int32_t slot, const int32_t* prompt, int32_t n, int32_t* next_out);
+int b2_batch_step(b2_batch* b, const int32_t* tokens, int32_t* next_out);
+int b2_batch_logits(const b2_batch* b, float* out);
 
 /* ---- tensor parallelism (engine.go LoadOptions.NumGPU; no counterpart in the
  * Go engine, which runs on CPU cores) ----

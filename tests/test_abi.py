@@ -136,6 +136,17 @@ def test_model_matvec_rejects_null_model(built_lib):
     assert b2decode.lib().b2_model_matvec(None, b"token_embd.weight", 4096, 8192, 8, None) == -10
 
 
+def test_batch_entry_points_reject_null(built_lib):
+    L = b2decode.lib()
+    h = b2decode._P()
+    assert L.b2_batch_create(None, 4, b2decode.C.byref(h)) == -10
+    toks = (b2decode.C.c_int32 * 4)()
+    assert L.b2_batch_step(None, toks, toks) == -10
+    assert L.b2_batch_prefill(None, 0, toks, 4, toks) == -10
+    assert L.b2_batch_logits(None, None) == -10
+    L.b2_batch_free(None)
+
+
 def test_tp_entry_points_reject_null(built_lib):
     L = b2decode.lib()
     assert L.b2_tp_handle(None, b"\0" * 64) == -10
