@@ -36,6 +36,10 @@ The other workloads (one GPU, one JSON line per case; not the driver's line):
   attention  b2_attention_decode, 32 query / 8 KV heads, head_dim 128, fp16 KV
              N(0,1), contexts 4096 / 16384 / 32768, batch 1 and 8, KV copies
              rotated past L2 in the same way.
+With --batch B > 1 (qwen05b or llama3-8b, one GPU) the model workload runs as
+batched greedy decode (b2_batch_*): B sequences, each prefilled with a prompt
+of its own, then K steps of all of them; value = tokens of all sequences per
+second.
 """
 from __future__ import annotations
 
@@ -498,6 +502,69 @@ def run_attention(args) -> None:
             torch.cuda.empty_cache()
 
 
+def run_batch(args) -> None:
+    """Batched greedy decode (b2_batch_*) of --batch sequences of a model
+    workload: each sequence prefilled with its own prompt on the
+    single-sequence path, then K steps of all sequences at once; value =
+    tokens of all sequences per second."""
+    import torch
+
+    import b2decode
+    from b2decode import gguf_writer as gw
+    if dist_env()[0] > 1 or args.workload not in ("qwen05b", "llama3-8b"):
+        raise SystemExit("--batch runs the qwen05b or llama3-8b workload on one GPU")
+    torch.cuda.set_device(0)
+    shape_name, n_prompt, _ = MODELS[args.workload]
+    shape = gw.SHAPES[shape_name]
+    path = ensure_model(shape_name)
+    B, K, W = args.batch, args.steps, args.warmup
+    m = b2decode.Model(path, num_ctx=n_prompt + 1 + W + K + 8)
+    stream = torch.cuda.ExternalStream(m.stream_handle())
+    bt = b2decode.Batch(m, B)
+    t0 = time.perf_counter()
+    nxt = [bt.prefill(b, np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, n_prompt, seed=b)])
+                      .astype(np.int32)) for b in range(B)]
+    prefill_s = time.perf_counter() - t0
+    for _ in range(W):
+        nxt = bt.step(nxt)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dev_uuid = None
+    try:
+        dev_uuid = "GPU-" + str(torch.cuda.get_device_properties(0).uuid)
+    except Exception:
+        pass
+    with Clocks(dev_uuid) as clk:
+        e0.record(stream)
+        t_host = time.perf_counter()
+        for _ in range(K):
+            nxt = bt.step(nxt)  # host ids in and out every step
+        t_host = time.perf_counter() - t_host
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    peak, peak_kind = peaks()
+    bytes_step = int(m.cfg["stream_bytes_per_token"])
+    achieved = bytes_step / (ms / K / 1000.0) / 1e9
+    print(json.dumps({
+        "metric": f"batched decode tok/s (B={B})", "value": B * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": 1,
+        "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (int8 planes x Q weights)", "data": "synthetic",
+        "config": {"workload": f"{shape_name}-shape {shape.wtype} batched greedy decode, batch {B}, "
+                               f"prompt {n_prompt} ids per sequence",
+                   "prompt_tokens": n_prompt + 1, "prefill_s": prefill_s,
+                   "prefill_path": "the decode kernel once per prompt token, per sequence",
+                   "l2": f"no flush needed: each step streams {bytes_step / 1e6:.0f} MB of weights"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "algorithmic_bytes_per_step": bytes_step},
+        "e2e": {"value": B * K / t_host, "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
+                "api": "b2_batch_step per step"},
+        "clocks": clk.summary(),
+    }), flush=True)
+    bt.close()
+    m.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -506,6 +573,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="qwen05b", choices=["qwen05b", "llama3-8b", "qwen72b", "matvec", "attention"])
+    ap.add_argument("--batch", type=int, default=1,
+                    help="> 1: batched greedy decode of that many sequences (qwen05b / llama3-8b workloads)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -515,6 +584,8 @@ def main():
         run_matvec(args)
     elif args.workload == "attention":
         run_attention(args)
+    elif args.batch > 1:
+        run_batch(args)
     else:
         run_b200(args)
 
