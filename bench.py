@@ -545,6 +545,14 @@ def run_batch(args) -> None:
     ms = e0.elapsed_time(e1)
     peak, peak_kind = peaks()
     bytes_step = int(m.cfg["stream_bytes_per_token"])
+    cpu = None
+    if not args.no_cpu_baseline:
+        # the reference engine serves one sequence at a time: its rate over B
+        # sequences is its single-sequence rate
+        try:
+            cpu = cpu_baseline_goref(path, shape_name, seconds=20.0, prefill=0)
+        except Exception as exc:  # the baseline must not sink the GPU line
+            cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {exc}"}
     achieved = bytes_step / (ms / K / 1000.0) / 1e9
     print(json.dumps({
         "metric": f"batched decode tok/s (B={B})", "value": B * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": 1,
@@ -560,6 +568,7 @@ def run_batch(args) -> None:
         "e2e": {"value": B * K / t_host, "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
                 "api": "b2_batch_step per step"},
         "clocks": clk.summary(),
+        "cpu_baseline": cpu,
     }), flush=True)
     bt.close()
     m.close()
