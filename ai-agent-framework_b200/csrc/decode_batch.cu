@@ -4,7 +4,8 @@
 // forward of one new token, for B sequences at a time; argmax
 // transformer.go:1038-1046).
 //
-// A step is a sequence of launches on the model's stream:
+// A step (and each prompt chunk of a slot's prefill) is a sequence of
+// launches on the model's stream:
 //   embedding rows of the B tokens (the tiled token_embd, decoded on the fly)
 //   per layer: RMSNorm -> batched tile dot over [Wq; Wk; Wv] -> bias, RoPE
 //   and the KV append at each sequence's position -> attention over each
@@ -13,8 +14,8 @@
 //   -> residual add
 //   final RMSNorm -> lm_head tile dot -> argmax per sequence (first maximum).
 // The tile dots are the batched matvec over the resident tiled weights
-// (matvec_batch.cu); prefill of a sequence runs on the single-sequence
-// decode kernel and its KV rows are copied into the sequence's slot.
+// (matvec_batch.cu).  A slot's prompt runs through the same launches in
+// chunks of up to 16 of its tokens.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -45,8 +46,9 @@ struct b2_batch {
     float *x = nullptr, *xn = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr;
     float *gu = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
     size_t part_floats = 0;
-    int *d_pos = nullptr, *d_tok = nullptr, *d_next = nullptr;  // [B]
-    int* h_io = nullptr;                                        // pinned [2B]
+    int *d_pos = nullptr, *d_tok = nullptr, *d_next = nullptr;  // [kBatchMax]
+    int* d_ppos = nullptr;                                      // [kBatchMax] prefill chunk positions
+    int* h_io = nullptr;                                        // pinned [3 * kBatchMax]
     std::vector<int> pos;                                       // positions (host copy)
 };
 
@@ -101,12 +103,13 @@ __global__ void bd_rmsnorm_kernel(const float* __restrict__ x, const float* __re
 }
 
 // transformer.go:632-656: bias, RoPE on interleaved pairs of every q and k
-// head at the sequence's position (936-951, the model's cos / sin table),
-// then k and v appended to the sequence's cache slot; q kept for attention.
+// head at the row's position (936-951, the model's cos / sin table), then k
+// and v appended to the row's cache slot (rows slot_stride positions apart;
+// 0 when all rows are tokens of one sequence); q kept for attention.
 __global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, const float* __restrict__ bias,
                                   const float* __restrict__ cosT, const float* __restrict__ sinT,
                                   const int* __restrict__ pos, float* __restrict__ q, __half* __restrict__ kc,
-                                  __half* __restrict__ vc, int qd, int kvd, int hd, int B, int max_seq) {
+                                  __half* __restrict__ vc, int qd, int kvd, int hd, int slot_stride) {
     const int b = blockIdx.x, p = pos[b], n = qd + 2 * kvd, hh = hd / 2;
     const float* row = qkv + (size_t)b * n;
     for (int j = threadIdx.x; j < n / 2; j += blockDim.x) {
@@ -130,7 +133,8 @@ __global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, const float* __
             const bool isk = r < qd + kvd;
             const int col = r - qd - (isk ? 0 : kvd);
             __half* cache = isk ? kc : vc;
-            *reinterpret_cast<__half2*>(cache + ((size_t)b * max_seq + p) * kvd + col) = __floats2half2_rn(a0, a1);
+            *reinterpret_cast<__half2*>(cache + ((size_t)b * slot_stride + p) * kvd + col) =
+                __floats2half2_rn(a0, a1);
         }
     }
 }
@@ -224,7 +228,10 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
     bt->pos.assign(B, 0);
     const size_t kv = (size_t)d.L * B * d.max_seq * d.kvd;
     const int n_qkv = d.qd + 2 * d.kvd;
-    bt->part_floats = (size_t)B * d.nh * kBatchSplits * (d.hd + 2);
+    // activations for R rows: the B slots of a step, or up to kBatchMax
+    // tokens of one sequence in a prefill chunk
+    const size_t R = kBatchMax;
+    bt->part_floats = R * d.nh * kBatchSplits * (d.hd + 2);
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -232,18 +239,18 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
         return o;
     };
     const size_t o_kc = take(kv * 2), o_vc = take(kv * 2);
-    const size_t o_x = take((size_t)B * d.H * 4), o_xn = take((size_t)B * d.H * 4), o_y = take((size_t)B * d.H * 4);
-    const size_t o_qkv = take((size_t)B * n_qkv * 4), o_q = take((size_t)B * d.qd * 4);
-    const size_t o_att = take((size_t)B * d.qd * 4);
-    const size_t o_gu = take((size_t)B * 2 * d.FF * 4), o_act = take((size_t)B * d.FF * 4);
-    const size_t o_lg = take((size_t)B * d.V * 4), o_part = take(bt->part_floats * 4);
-    const size_t o_pos = take((size_t)B * 4), o_tok = take((size_t)B * 4), o_next = take((size_t)B * 4);
+    const size_t o_x = take(R * d.H * 4), o_xn = take(R * d.H * 4), o_y = take(R * d.H * 4);
+    const size_t o_qkv = take(R * n_qkv * 4), o_q = take(R * d.qd * 4);
+    const size_t o_att = take(R * d.qd * 4);
+    const size_t o_gu = take(R * 2 * d.FF * 4), o_act = take(R * d.FF * 4);
+    const size_t o_lg = take(R * d.V * 4), o_part = take(bt->part_floats * 4);
+    const size_t o_pos = take(R * 4), o_tok = take(R * 4), o_next = take(R * 4), o_ppos = take(R * 4);
     if (cudaMalloc(&bt->arena, off) != cudaSuccess) {
         delete bt;
         *err = "device allocation of the batch state failed";
         return B2_ERR_OOM;
     }
-    if (cudaMallocHost(&bt->h_io, sizeof(int) * 2 * B) != cudaSuccess) {
+    if (cudaMallocHost(&bt->h_io, sizeof(int) * 3 * kBatchMax) != cudaSuccess) {
         cudaFree(bt->arena);
         delete bt;
         *err = "pinned host allocation failed";
@@ -265,6 +272,7 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
     bt->d_pos = reinterpret_cast<int*>(A + o_pos);
     bt->d_tok = reinterpret_cast<int*>(A + o_tok);
     bt->d_next = reinterpret_cast<int*>(A + o_next);
+    bt->d_ppos = reinterpret_cast<int*>(A + o_ppos);
     if (!ok(cudaMemsetAsync(bt->arena, 0, off, m->stream), err, "clear") ||
         !ok(cudaStreamSynchronize(m->stream), err, "clear")) {
         cudaFreeHost(bt->h_io);
@@ -284,8 +292,70 @@ void b2_batch_free_impl(b2_batch* bt) {
     delete bt;
 }
 
-// The slot's sequence: prefill on the single-sequence path (which leaves the
-// model's own cache holding the prompt), then its KV rows copied into the slot.
+namespace {
+
+// R rows through the whole model: row r is token d_tok[r] at position
+// d_rpos[r], its K / V rows going to kc / vc + r * slot_stride positions
+// (per layer, plus kv_off); its attention covers positions 0 .. d_rpos[r].
+// Writes the argmax of every row to d_next and moves d_rpos on by one.
+int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err) {
+    b2_model* m = bt->m;
+    const ModelDev& d = m->dev;
+    cudaStream_t s = m->stream;
+    const int H = d.H, qt = d.qtype, n_qkv = d.qd + 2 * d.kvd;
+    bd_embed_kernel<<<R, kBdThreads, 0, s>>>(d.tok_embd, d.Vemb, d.Vp_emb, H, qt, bt->d_tok, bt->x);
+    const int ew_blocks = std::max(1, std::min(m->grid * 4, (R * 2 * d.FF + kBdThreads - 1) / kBdThreads));
+    const int add_blocks = std::max(1, (R * H + kBdThreads - 1) / kBdThreads);
+    const size_t kv_layer = (size_t)bt->B * bt->max_seq * d.kvd;
+    int rc = B2_OK;
+    for (int l = 0; l < d.L && rc == B2_OK; l++) {
+        const LayerDev& ld = m->layers_host[l];
+        bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, ld.attn_norm, bt->xn, H, d.eps);
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wqkv, tiled_rows(n_qkv), 0, n_qkv, H, bt->xn, bt->qkv, R, s, err);
+        if (rc) break;
+        __half* kc = bt->kc + (size_t)l * kv_layer + kv_off;
+        __half* vc = bt->vc + (size_t)l * kv_layer + kv_off;
+        bd_rope_kv_kernel<<<R, kBdThreads, 0, s>>>(bt->qkv, ld.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc, vc,
+                                                   d.qd, d.kvd, d.hd, slot_stride);
+        rc = b2_attention_seqs_launch(bt->q, kc, vc, bt->part, bt->part_floats, bt->att, R, d.nh, d.nkv, d.hd, d_rpos,
+                                      1, slot_stride, max_len, m->grid, s);
+        if (rc) {
+            *err = "batched attention launch failed";
+            break;
+        }
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wo, tiled_rows(H), 0, H, d.qd, bt->att, bt->y, R, s, err);
+        if (rc) break;
+        bd_add_kernel<<<add_blocks, kBdThreads, 0, s>>>(bt->x, bt->y, R * H);
+        bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, ld.ffn_norm, bt->xn, H, d.eps);
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wgu, tiled_rows(2 * d.FF), 0, 2 * d.FF, H, bt->xn, bt->gu, R, s, err);
+        if (rc) break;
+        bd_swiglu_kernel<<<ew_blocks, kBdThreads, 0, s>>>(bt->gu, bt->act, d.FF, R);
+        rc = b2_tiled_matvec_batch_impl(qt, ld.wd, tiled_rows(H), 0, H, d.FF, bt->act, bt->y, R, s, err);
+        if (rc) break;
+        bd_add_kernel<<<add_blocks, kBdThreads, 0, s>>>(bt->x, bt->y, R * H);
+    }
+    if (rc) return rc;
+    bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, d.out_norm, bt->xn, H, d.eps);
+    rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn, bt->logits, R, s, err);
+    if (rc) return rc;
+    bd_argmax_kernel<<<R, kBdThreads, 0, s>>>(bt->logits, d.V, bt->d_next, d_rpos);
+    return ok(cudaGetLastError(), err, "batched decode launch") ? B2_OK : B2_ERR_CUDA;
+}
+
+bool device_current(const b2_model* m, std::string* err) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device) {
+        *err = "the model's device must be the current device";
+        return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+// The slot's sequence: its prompt in chunks of up to kBatchMax tokens, each
+// chunk one pass over the weights (rows = the chunk's tokens, all appending to
+// and attending over this slot, token i over positions 0 .. p0 + i).
 int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, int32_t* next_out, std::string* err) {
     b2_model* m = bt->m;
     const ModelDev& d = m->dev;
@@ -297,33 +367,32 @@ int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, 
         *err = "prompt length must be 1 .. max_seq - 1";
         return B2_ERR_CONTEXT;
     }
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device) {
-        *err = "the model's device must be the current device";
-        return B2_ERR_BAD_ARG;
-    }
-    int rc = b2_reset(m);
-    if (rc == B2_OK) rc = b2_forward_argmax(m, prompt, n, next_out);
-    if (rc) {
-        *err = b2_last_error();
-        return rc;
-    }
-    const size_t row = (size_t)d.kvd * sizeof(__half);
-    for (int l = 0; l < d.L; l++) {
-        const size_t dst = ((size_t)l * bt->B + slot) * bt->max_seq * d.kvd;
-        const size_t src = (size_t)l * d.max_seq * d.kvd;
-        if (!ok(cudaMemcpyAsync(bt->kc + dst, static_cast<const __half*>(d.kcache) + src, row * n,
-                                cudaMemcpyDeviceToDevice, m->stream), err, "KV copy") ||
-            !ok(cudaMemcpyAsync(bt->vc + dst, static_cast<const __half*>(d.vcache) + src, row * n,
-                                cudaMemcpyDeviceToDevice, m->stream), err, "KV copy"))
+    if (!device_current(m, err)) return B2_ERR_BAD_ARG;
+    cudaStream_t s = m->stream;
+    int c = 0;
+    for (int p0 = 0; p0 < n; p0 += kBatchMax) {
+        c = std::min(kBatchMax, n - p0);
+        for (int i = 0; i < c; i++) {
+            bt->h_io[i] = prompt[p0 + i];
+            bt->h_io[kBatchMax + i] = p0 + i;
+        }
+        if (!ok(cudaMemcpyAsync(bt->d_tok, bt->h_io, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens") ||
+            !ok(cudaMemcpyAsync(bt->d_ppos, bt->h_io + kBatchMax, sizeof(int) * c, cudaMemcpyHostToDevice, s), err,
+                "positions"))
             return B2_ERR_CUDA;
+        const int rc = forward_rows(bt, c, bt->d_ppos, (size_t)slot * bt->max_seq * d.kvd, 0, p0 + c, err);
+        if (rc) return rc;
+        // the pinned staging is reused by the next chunk
+        if (!ok(cudaStreamSynchronize(s), err, "prefill")) return B2_ERR_CUDA;
     }
     bt->pos[slot] = n;
     bt->h_io[0] = n;
-    if (!ok(cudaMemcpyAsync(bt->d_pos + slot, bt->h_io, sizeof(int), cudaMemcpyHostToDevice, m->stream), err,
-            "position") ||
-        !ok(cudaStreamSynchronize(m->stream), err, "prefill"))
+    if (!ok(cudaMemcpyAsync(bt->d_pos + slot, bt->h_io, sizeof(int), cudaMemcpyHostToDevice, s), err, "position") ||
+        !ok(cudaMemcpyAsync(bt->h_io + 2 * kBatchMax, bt->d_next + (c - 1), sizeof(int), cudaMemcpyDeviceToHost, s),
+            err, "id") ||
+        !ok(cudaStreamSynchronize(s), err, "prefill"))
         return B2_ERR_CUDA;
+    *next_out = bt->h_io[2 * kBatchMax];
     return B2_OK;
 }
 
@@ -332,11 +401,7 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
     const ModelDev& d = m->dev;
     const int B = bt->B;
     cudaStream_t s = m->stream;
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device) {
-        *err = "the model's device must be the current device";
-        return B2_ERR_BAD_ARG;
-    }
+    if (!device_current(m, err)) return B2_ERR_BAD_ARG;
     int max_len = 0;
     for (int b = 0; b < B; b++) {
         if (bt->pos[b] + 1 > bt->max_seq) {
@@ -348,44 +413,10 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
     for (int b = 0; b < B; b++) bt->h_io[b] = tokens[b];
     if (!ok(cudaMemcpyAsync(bt->d_tok, bt->h_io, sizeof(int) * B, cudaMemcpyHostToDevice, s), err, "tokens"))
         return B2_ERR_CUDA;
-    const int H = d.H, qt = d.qtype, n_qkv = d.qd + 2 * d.kvd;
-    bd_embed_kernel<<<B, kBdThreads, 0, s>>>(d.tok_embd, d.Vemb, d.Vp_emb, H, qt, bt->d_tok, bt->x);
-    const int ew_blocks = std::max(1, std::min(m->grid * 4, (B * 2 * d.FF + kBdThreads - 1) / kBdThreads));
-    const size_t kv_layer = (size_t)B * bt->max_seq * d.kvd;
-    int rc = B2_OK;
-    for (int l = 0; l < d.L && rc == B2_OK; l++) {
-        const LayerDev& ld = m->layers_host[l];
-        bd_rmsnorm_kernel<<<B, kBdThreads, 0, s>>>(bt->x, ld.attn_norm, bt->xn, H, d.eps);
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wqkv, tiled_rows(n_qkv), 0, n_qkv, H, bt->xn, bt->qkv, B, s, err);
-        if (rc) break;
-        __half* kc = bt->kc + (size_t)l * kv_layer;
-        __half* vc = bt->vc + (size_t)l * kv_layer;
-        bd_rope_kv_kernel<<<B, kBdThreads, 0, s>>>(bt->qkv, ld.bqkv, d.rope_cos, d.rope_sin, bt->d_pos, bt->q, kc, vc,
-                                                   d.qd, d.kvd, d.hd, B, bt->max_seq);
-        rc = b2_attention_seqs_launch(bt->q, kc, vc, bt->part, bt->part_floats, bt->att, B, d.nh, d.nkv, d.hd,
-                                      bt->d_pos, 1, bt->max_seq, max_len, m->grid, s);
-        if (rc) {
-            *err = "batched attention launch failed";
-            break;
-        }
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wo, tiled_rows(H), 0, H, d.qd, bt->att, bt->y, B, s, err);
-        if (rc) break;
-        bd_add_kernel<<<std::max(1, (B * H + kBdThreads - 1) / kBdThreads), kBdThreads, 0, s>>>(bt->x, bt->y, B * H);
-        bd_rmsnorm_kernel<<<B, kBdThreads, 0, s>>>(bt->x, ld.ffn_norm, bt->xn, H, d.eps);
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wgu, tiled_rows(2 * d.FF), 0, 2 * d.FF, H, bt->xn, bt->gu, B, s, err);
-        if (rc) break;
-        bd_swiglu_kernel<<<ew_blocks, kBdThreads, 0, s>>>(bt->gu, bt->act, d.FF, B);
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wd, tiled_rows(H), 0, H, d.FF, bt->act, bt->y, B, s, err);
-        if (rc) break;
-        bd_add_kernel<<<std::max(1, (B * H + kBdThreads - 1) / kBdThreads), kBdThreads, 0, s>>>(bt->x, bt->y, B * H);
-    }
+    const int rc = forward_rows(bt, B, bt->d_pos, 0, bt->max_seq, max_len, err);
     if (rc) return rc;
-    bd_rmsnorm_kernel<<<B, kBdThreads, 0, s>>>(bt->x, d.out_norm, bt->xn, H, d.eps);
-    rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn, bt->logits, B, s, err);
-    if (rc) return rc;
-    bd_argmax_kernel<<<B, kBdThreads, 0, s>>>(bt->logits, d.V, bt->d_next, bt->d_pos);
-    if (!ok(cudaGetLastError(), err, "batched decode launch") ||
-        !ok(cudaMemcpyAsync(bt->h_io + B, bt->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, s), err, "ids") ||
+    (void)d;
+    if (!ok(cudaMemcpyAsync(bt->h_io + B, bt->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, s), err, "ids") ||
         !ok(cudaStreamSynchronize(s), err, "batched decode"))
         return B2_ERR_CUDA;
     for (int b = 0; b < B; b++) {

@@ -504,9 +504,9 @@ def run_attention(args) -> None:
 
 def run_batch(args) -> None:
     """Batched greedy decode (b2_batch_*) of --batch sequences of a model
-    workload: each sequence prefilled with its own prompt on the
-    single-sequence path, then K steps of all sequences at once; value =
-    tokens of all sequences per second."""
+    workload: each sequence prefilled with its own prompt (16-token chunks),
+    then K steps of all sequences at once; value = tokens of all sequences
+    per second."""
     import torch
 
     import b2decode
@@ -561,7 +561,7 @@ def run_batch(args) -> None:
         "config": {"workload": f"{shape_name}-shape {shape.wtype} batched greedy decode, batch {B}, "
                                f"prompt {n_prompt} ids per sequence",
                    "prompt_tokens": n_prompt + 1, "prefill_s": prefill_s,
-                   "prefill_path": "the decode kernel once per prompt token, per sequence",
+                   "prefill_path": "b2_batch_prefill: chunks of 16 prompt tokens, one weight pass each",
                    "l2": f"no flush needed: each step streams {bytes_step / 1e6:.0f} MB of weights"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "algorithmic_bytes_per_step": bytes_step},

@@ -218,9 +218,10 @@ int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_
  * model's num_ctx, fp16), advance one token per b2_batch_step together, each
  * at its own position, so every weight byte is read once per step for all of
  * them: the forward of transformer.go:519-739 and argmax 1038-1046 for B
- * sequences at a time.  b2_batch_prefill runs a slot's prompt on the model's
- * single-sequence path (it resets the model's own cache) and copies its KV
- * rows into the slot; next_out is the argmax after the prompt.  b2_batch_step
+ * sequences at a time.  b2_batch_prefill runs a slot's prompt into the slot
+ * in chunks of up to 16 tokens, each chunk one pass over the weights (the
+ * model's own single-sequence cache is not touched); next_out is the argmax
+ * after the prompt.  b2_batch_step
  * feeds tokens[B] (one per slot, every slot) and writes the B argmax ids;
  * b2_batch_logits copies the last step's logits, [B][vocab_size].  Needs a
  * single-GPU model with the fp16 cache; the model's device must be current.
