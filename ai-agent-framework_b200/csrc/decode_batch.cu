@@ -284,9 +284,10 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
     return B2_OK;
 }
 
+// Touches nothing of the model (which may already be freed): cudaFree waits
+// for the device's outstanding work before releasing the arena.
 void b2_batch_free_impl(b2_batch* bt) {
     if (!bt) return;
-    if (bt->m && bt->m->stream) cudaStreamSynchronize(bt->m->stream);
     if (bt->h_io) cudaFreeHost(bt->h_io);
     if (bt->arena) cudaFree(bt->arena);
     delete bt;

@@ -225,6 +225,8 @@ int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_
  * feeds tokens[B] (one per slot, every slot) and writes the B argmax ids;
  * b2_batch_logits copies the last step's logits, [B][vocab_size].  Needs a
  * single-GPU model with the fp16 cache; the model's device must be current.
+ * A batch is used only while its model is loaded; b2_batch_free may come
+ * before or after b2_free of the model.
  * No single counterpart in the reference (its engine runs one sequence). */
 int b2_batch_create(b2_model* m, int32_t batch, b2_batch** out);
 void b2_batch_free(b2_batch* b);
