@@ -103,6 +103,7 @@ SIGNATURES = {
     "b2_batch_prefill": (C.c_int, [_P, _i32, _i32p, _i32, C.POINTER(_i32)]),
     "b2_batch_step": (C.c_int, [_P, _i32p, _i32p]),
     "b2_batch_logits": (C.c_int, [_P, _f32p]),
+    "b2_batch_use_graph": (C.c_int, [_P, _i32]),
     "b2_attention_decode": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_attention_decode_noalloc": (C.c_int, [_P, _P, _P, _P, _i32, _i32, _i32, _i32, _i32, _P]),
     "b2_device_status": (C.c_int, [_P]),
@@ -320,6 +321,10 @@ class Batch:
         out = np.zeros(self.batch, dtype=np.int32)
         _check(lib().b2_batch_step(self._h, p, out.ctypes.data_as(_i32p)))
         return out
+
+    def use_graph(self, on: bool = True) -> None:
+        """Replay steps from a captured CUDA graph (b2_batch_use_graph)."""
+        _check(lib().b2_batch_use_graph(self._h, 1 if on else 0))
 
     def logits(self) -> np.ndarray:
         out = np.empty((self.batch, self.vocab), dtype=np.float32)

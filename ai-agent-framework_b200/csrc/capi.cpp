@@ -24,6 +24,7 @@ void b2_batch_free_impl(b2_batch* bt);
 int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, int32_t* next_out, std::string* err);
 int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, std::string* err);
 int b2_batch_logits_impl(const b2_batch* bt, float* out, std::string* err);
+int b2_batch_use_graph_impl(b2_batch* bt, int on);
 int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh, int nkv,
                       int hd, int ctx, cudaStream_t s, std::string* err);
 int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh,
@@ -471,6 +472,11 @@ int b2_batch_step(b2_batch* b, const int32_t* tokens, int32_t* next_out) {
     if (!tokens || !next_out) return ret(B2_ERR_BAD_ARG, "null argument");
     std::string err;
     return ret(b2_batch_step_impl(b, tokens, next_out, &err), err);
+}
+
+int b2_batch_use_graph(b2_batch* b, int32_t on) {
+    if (!b) return ret(B2_ERR_NOT_LOADED, "no batch");
+    return b2_batch_use_graph_impl(b, on);
 }
 
 int b2_batch_logits(const b2_batch* b, float* out) {

@@ -29,6 +29,7 @@
 
 int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
+unsigned long long b2_mvb_scratch_generation();
 int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, float* part, size_t part_floats,
                              float* out, int batch, int nh, int nkv, int hd, const int* lens, int add, int stride,
                              int max_len, int sms, cudaStream_t s);
@@ -50,6 +51,9 @@ struct b2_batch {
     int* d_ppos = nullptr;                                      // [kBatchMax] prefill chunk positions
     int* h_io = nullptr;                                        // pinned [3 * kBatchMax]
     std::vector<int> pos;                                       // positions (host copy)
+    bool use_graph = false;                  // replay steps from a captured CUDA graph
+    cudaGraphExec_t exec = nullptr;          // the step's launches (tokens and ids copied outside)
+    unsigned long long exec_gen = 0;         // matvec scratch generation it captured
 };
 
 namespace b2 {
@@ -288,6 +292,7 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
 // for the device's outstanding work before releasing the arena.
 void b2_batch_free_impl(b2_batch* bt) {
     if (!bt) return;
+    if (bt->exec) cudaGraphExecDestroy(bt->exec);
     if (bt->h_io) cudaFreeHost(bt->h_io);
     if (bt->arena) cudaFree(bt->arena);
     delete bt;
@@ -414,15 +419,54 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
     for (int b = 0; b < B; b++) bt->h_io[b] = tokens[b];
     if (!ok(cudaMemcpyAsync(bt->d_tok, bt->h_io, sizeof(int) * B, cudaMemcpyHostToDevice, s), err, "tokens"))
         return B2_ERR_CUDA;
-    const int rc = forward_rows(bt, B, bt->d_pos, 0, bt->max_seq, max_len, err);
-    if (rc) return rc;
     (void)d;
+    if (bt->exec && bt->exec_gen != b2_mvb_scratch_generation()) {  // the scratch moved since the capture
+        cudaGraphExecDestroy(bt->exec);
+        bt->exec = nullptr;
+    }
+    if (bt->use_graph && bt->exec) {
+        if (!ok(cudaGraphLaunch(bt->exec, s), err, "graph launch")) return B2_ERR_CUDA;
+    } else {
+        const int rc = forward_rows(bt, B, bt->d_pos, 0, bt->max_seq, max_len, err);
+        if (rc) return rc;
+    }
     if (!ok(cudaMemcpyAsync(bt->h_io + B, bt->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, s), err, "ids") ||
         !ok(cudaStreamSynchronize(s), err, "batched decode"))
         return B2_ERR_CUDA;
+    if (bt->use_graph && !bt->exec) {
+        // Capture the launches of a step for the next ones (capturing runs
+        // nothing).  This step ran them eagerly, so the matvec scratch is
+        // already sized and no allocation happens inside the capture.  The
+        // attention split count is fixed for the full cache length; every
+        // row's length is still read on the device.  A capture that fails
+        // leaves the batch stepping eagerly.
+        cudaGraph_t graph = nullptr;
+        std::string cerr;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int crc = forward_rows(bt, B, bt->d_pos, 0, bt->max_seq, bt->max_seq, &cerr);
+            const cudaError_t ce = cudaStreamEndCapture(s, &graph);
+            if (crc == B2_OK && ce == cudaSuccess && graph &&
+                cudaGraphInstantiate(&bt->exec, graph, 0) == cudaSuccess) {
+                bt->exec_gen = b2_mvb_scratch_generation();
+            } else {
+                bt->exec = nullptr;
+            }
+            if (graph) cudaGraphDestroy(graph);
+        }
+        (void)cudaGetLastError();  // a refused capture is not this step's error
+    }
     for (int b = 0; b < B; b++) {
         next_out[b] = bt->h_io[B + b];
         bt->pos[b] += 1;
+    }
+    return B2_OK;
+}
+
+int b2_batch_use_graph_impl(b2_batch* bt, int on) {
+    bt->use_graph = on != 0;
+    if (!bt->use_graph && bt->exec) {
+        cudaGraphExecDestroy(bt->exec);
+        bt->exec = nullptr;
     }
     return B2_OK;
 }

@@ -446,6 +446,7 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
 struct MvbScratch {
     uint8_t* buf = nullptr;
     size_t bytes = 0;
+    unsigned long long gen = 0;  // bumped whenever buf moves (CUDA graphs hold its address)
     int sms = 0;
     bool attr_set = false;
 };
@@ -542,6 +543,7 @@ int mvb_run(bool q8, bool tiled, const MvbMat& mat, const float* x, float* y, in
             return B2_ERR_CUDA;
         }
         sc->bytes = need;
+        sc->gen++;
     }
     uint8_t* base = sc->buf;
     int* cnt = reinterpret_cast<int*>(base);
@@ -618,4 +620,13 @@ int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t 
     const uint8_t* w = static_cast<const uint8_t*>(base);
     const MvbMat mat{w, w + (size_t)rp * nbk * (q8 ? 32 : 16), rows, 0, nbk, (int)(row0 / 16)};
     return mvb_run(q8, true, mat, x, y, nvec, s, err);
+}
+
+// Generation of the current device's scratch buffer: a CUDA graph that
+// captured batched matvecs is valid while this is unchanged.
+unsigned long long b2_mvb_scratch_generation() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(g_mvb_mu);
+    return (int)g_mvb.size() > dev ? g_mvb[dev].gen : 0;
 }

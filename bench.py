@@ -521,6 +521,8 @@ def run_batch(args) -> None:
     m = b2decode.Model(path, num_ctx=n_prompt + 1 + W + K + 8)
     stream = torch.cuda.ExternalStream(m.stream_handle())
     bt = b2decode.Batch(m, B)
+    if args.graph:
+        bt.use_graph(True)  # captured after the first warm-up step
     t0 = time.perf_counter()
     nxt = [bt.prefill(b, np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, n_prompt, seed=b)])
                       .astype(np.int32)) for b in range(B)]
@@ -560,6 +562,7 @@ def run_batch(args) -> None:
         "vs_baseline": None, "dtype": "fp32 (int8 planes x Q weights)", "data": "synthetic",
         "config": {"workload": f"{shape_name}-shape {shape.wtype} batched greedy decode, batch {B}, "
                                f"prompt {n_prompt} ids per sequence",
+                   "launches": "one CUDA graph per step" if args.graph else "eager (about 15 per layer)",
                    "prompt_tokens": n_prompt + 1, "prefill_s": prefill_s,
                    "prefill_path": "b2_batch_prefill: chunks of 16 prompt tokens, one weight pass each",
                    "l2": f"no flush needed: each step streams {bytes_step / 1e6:.0f} MB of weights"},
@@ -584,6 +587,7 @@ def main():
     ap.add_argument("--workload", default="qwen05b", choices=["qwen05b", "llama3-8b", "qwen72b", "matvec", "attention"])
     ap.add_argument("--batch", type=int, default=1,
                     help="> 1: batched greedy decode of that many sequences (qwen05b / llama3-8b workloads)")
+    ap.add_argument("--graph", action="store_true", help="--batch: replay each step from a captured CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

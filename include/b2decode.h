@@ -233,6 +233,11 @@ void b2_batch_free(b2_batch* b);
 int b2_batch_prefill(b2_batch* b, int32_t slot, const int32_t* prompt, int32_t n, int32_t* next_out);
 int b2_batch_step(b2_batch* b, const int32_t* tokens, int32_t* next_out);
 int b2_batch_logits(const b2_batch* b, float* out);
+/* on != 0: replay each step's launches from a CUDA graph, captured after the
+ * first step that runs with the switch on (and again after the batched
+ * matvec's shared scratch has moved); a capture that fails leaves the batch
+ * stepping eagerly.  Off by default. */
+int b2_batch_use_graph(b2_batch* b, int32_t on);
 
 /* ---- tensor parallelism (engine.go LoadOptions.NumGPU; no counterpart in the
  * Go engine, which runs on CPU cores) ----

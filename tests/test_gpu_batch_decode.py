@@ -40,8 +40,10 @@ SHAPES = {
 }
 
 
+@pytest.mark.parametrize("graph", [False, True])
 @pytest.mark.parametrize("key", list(SHAPES))
-def test_batch_decode_matches_oracle_per_sequence(built_lib, oracle_lib, write_model, key):
+def test_batch_decode_matches_oracle_per_sequence(built_lib, oracle_lib, write_model, key, graph):
+    """graph: steps after the first replay a captured CUDA graph."""
     shape = SHAPES[key]
     path = write_model(key, shape)
     m = b2decode.Model(path, num_ctx=128)
@@ -50,6 +52,8 @@ def test_batch_decode_matches_oracle_per_sequence(built_lib, oracle_lib, write_m
     prompts = [np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, n, seed=10 + n)]).astype(np.int32)
                for n in (5, 70, 1)]
     bt = b2decode.Batch(m, len(prompts))
+    if graph:
+        bt.use_graph(True)
     hist = [list(p) for p in prompts]
     nxt = []
     for slot, p in enumerate(prompts):
