@@ -318,9 +318,9 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
         const uint8_t* ssc = stage0 + st * G::tile + G::tsc;
         const int kb0 = cs.c * kMvbKc;
         const int nblk = TILED ? min(kMvbKc, nb - kb0) : kMvbKc;
-#pragma unroll
-        for (int bb = 0; bb < kMvbKc; bb++) {
-            if (TILED && bb >= nblk) break;  // warp-uniform: a short last chunk
+        // one 32-block of the chunk: A fragments, scales, the NT x 3 mma and
+        // their fp32 accumulation
+        auto block = [&](const int bb) {
             const int kb = kb0 + bb;
             uint32_t a0, a1, a2, a3;
             float dg, dh;
@@ -384,6 +384,14 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
                 acc_g[n] = f2_fma(f2_mul(dgp, sxp), tg, acc_g[n]);
                 acc_h[n] = f2_fma(f2_mul(dhp, sxp), th, acc_h[n]);
             }
+        };
+        if (nblk == kMvbKc) {
+            // a full chunk: unrolled, so the loads of later blocks issue early
+#pragma unroll
+            for (int bb = 0; bb < kMvbKc; bb++) block(bb);
+        } else {
+#pragma unroll 1
+            for (int bb = 0; bb < nblk; bb++) block(bb);  // tiled layout only: a short last chunk
         }
 
         if (cs.c + 1 == cs.c1) {
