@@ -564,6 +564,10 @@ def run_batch(args) -> None:
                                f"prompt {n_prompt} ids per sequence",
                    "launches": "one CUDA graph per step" if args.graph else "eager (about 15 per layer)",
                    "prompt_tokens": n_prompt + 1, "prefill_s": prefill_s,
+                   "prefill_tok_s": B * (n_prompt + 1) / prefill_s,
+                   # 2 flops per weight per token; weights = streamed bytes x 32 / (bytes per 32-block)
+                   "prefill_tflops": 2.0 * bytes_step * 32 / (34 if shape.wtype == "q8_0" else 18)
+                                     * B * (n_prompt + 1) / prefill_s / 1e12,
                    "prefill_path": "b2_batch_prefill: chunks of 16 prompt tokens, one weight pass each",
                    "l2": f"no flush needed: each step streams {bytes_step / 1e6:.0f} MB of weights"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
