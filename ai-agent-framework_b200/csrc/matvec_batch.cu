@@ -1,11 +1,14 @@
 // Batched dequantising matvec: Y = W X for up to sixteen fp32 vectors in one
-// pass over a GGUF-layout Q8_0 / Q4_0 matrix.
+// pass over a Q8_0 / Q4_0 matrix, in the GGUF row layout (b2_matvec_batch)
+// or in the decode kernel's tiled layout of a loaded model (b2_model_matvec
+// and the batched decode).
 //
 // The reference evaluates one vector at a time (transformer.go:810-865
 // matVecMulQ8Chunk, driven over row ranges by matVecMulQ8Pooled at
-// transformer.go:868-892: per 32-block, q * d against x in fp32; Q4_0 blocks
-// take the same dot with (q - 8) * d, the ggml block layout).  Here the weights stream from HBM once for
-// all vectors and the products run on the int8 tensor-core path:
+// transformer.go:868-892: per 32-block, q * d against x in fp32; Q4_0
+// blocks take the same dot with (q - 8) * d, the ggml block layout).  Here
+// the weights stream from HBM once for all vectors and the products run on
+// the int8 tensor-core path:
 //
 //   * Each vector is split per 32-block into three int8 planes,
 //     x ~= s * (p0 + p1 / 2^7 + p2 / 2^14) with s = max|x| / 127 (about 22
@@ -13,10 +16,13 @@
 //     dots).  The planes sit in global memory in the B-fragment order of
 //     mma.m16n8k32, one column per vector, one mma per plane and group of
 //     eight vectors (NT = 1 or 2 column tiles share each A fragment).
-//   * A warp owns a unit = (16-row tile, slice of the 32-blocks).  Its raw
-//     GGUF row bytes stream through warp-private shared-memory stages filled
-//     with cp.async (16 B, L1-bypassing); the fragments are read from the raw
-//     34- / 18-byte blocks with aligned 32-bit loads and byte permutes.
+//   * A warp owns a unit = (16-row tile, slice of the 32-blocks).  Its weight
+//     bytes stream through warp-private shared-memory stages filled with
+//     cp.async (16 B, L1-bypassing), 8 blocks of the tile per stage.  Raw
+//     rows: the fragments come from the 34- / 18-byte blocks with aligned
+//     32-bit loads and byte permutes.  Tiled: a stage is the chunk's
+//     (tile, block) units and their scales, and the fragments come by
+//     ldmatrix.
 //   * Each 32-block gives, per plane, the exact int32 dot in an accumulator
 //     started at the float bits of 1.5 * 2^23 (Q4_0: minus 8 * the plane
 //     sum, so (q - 8) . p comes out), read back with one subtraction, then
