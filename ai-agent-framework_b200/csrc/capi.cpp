@@ -249,7 +249,7 @@ int b2_predict(b2_model* m, const int32_t* prompt, int32_t n_prompt, const b2_sa
                b2_timings* timings) {
     // transformer.go:325-382.
     if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
-    if ((n_prompt > 0 && !prompt) || !out_ids || !n_out) return ret(B2_ERR_BAD_ARG, "bad argument");
+    if ((n_prompt > 0 && !prompt) || !out_ids || !n_out || max_out < 0) return ret(B2_ERR_BAD_ARG, "bad argument");
     b2_sample_opts o = opts ? *opts : default_opts();
     const int max_gen = o.num_predict > 0 ? o.num_predict : 256;
     std::vector<int32_t> stop(stop_ids, stop_ids + (stop_ids ? std::max(0, n_stop) : 0));
