@@ -110,6 +110,7 @@ SIGNATURES = {
     "b2_stream_handle": (_P, [_P]),
     "b2_trace_step": (C.c_int, [_P, _i32, C.POINTER(_i64), _i64, _i32p, _i32p]),
     "b2_debug_wait_skew": (C.c_int, [_P, _i32]),
+    "b2_debug_fail_alloc": (C.c_int, [_i32]),
     "b2_tp_handle": (C.c_int, [_P, C.c_char_p]),
     "b2_tp_connect": (C.c_int, [_P, C.c_char_p]),
 }
@@ -286,6 +287,11 @@ class Model:
 
     def debug_wait_skew(self, skew: int) -> None:
         _check(lib().b2_debug_wait_skew(self._h, int(skew)))
+
+
+def debug_fail_alloc(nth: int) -> None:
+    """The nth device allocation of the next loads fails (b2_debug_fail_alloc); 0 disarms."""
+    _check(lib().b2_debug_fail_alloc(int(nth)))
 
 
 def sample_logits(logits, opts: SampleOpts, generated=(), r: float = 0.5) -> int:

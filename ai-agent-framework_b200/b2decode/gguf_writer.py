@@ -89,6 +89,13 @@ SHAPES = {
 # The 72B shape cut to 4 layers (a 6.4 GB file instead of 77 GB): per-layer
 # and lm_head costs of the tensor-parallel decode at the real widths.
 SHAPES["qwen2.5-72b-4l"] = SHAPES["qwen2.5-72b"].with_(layers=4)
+# Untied tiny model: with tied N(0, 0.02) embeddings the greedy next token is
+# the input token itself, so a smoke run needs an untied head to show a
+# changing greedy sequence.
+SHAPES["tiny-untied"] = SHAPES["tiny"].with_(tied=False)
+# Llama-3-8B widths (hidden 4096, FFN 14336, vocab 128256) cut to 4 layers:
+# the config-2 parity case at its real matrix shapes.
+SHAPES["llama3-8b-4l"] = SHAPES["llama3-8b"].with_(layers=4)
 
 
 # ---------------------------------------------------------------------------

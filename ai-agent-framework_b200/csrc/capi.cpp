@@ -524,6 +524,12 @@ int b2_debug_wait_skew(b2_model* m, int32_t skew) {
     return B2_OK;
 }
 
+int b2_debug_fail_alloc(int32_t nth) {
+    if (nth < 0) return ret(B2_ERR_BAD_ARG, "nth must be >= 0");
+    b2::g_fail_left.store(nth);
+    return B2_OK;
+}
+
 int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
                                 int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream) {
     if (!q || !k || !v || !out || batch <= 0 || nh <= 0 || nkv <= 0 || nh % nkv || hd <= 0 || hd % 8 || ctx <= 0)

@@ -29,7 +29,7 @@
 
 int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
-unsigned long long b2_mvb_scratch_generation();
+unsigned long long b2_mvb_scratch_generation(cudaStream_t s);
 int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, float* part, size_t part_floats,
                              float* out, int batch, int nh, int nkv, int hd, const int* lens, int add, int stride,
                              int max_len, int sms, cudaStream_t s);
@@ -420,7 +420,7 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
     if (!ok(cudaMemcpyAsync(bt->d_tok, bt->h_io, sizeof(int) * B, cudaMemcpyHostToDevice, s), err, "tokens"))
         return B2_ERR_CUDA;
     (void)d;
-    if (bt->exec && bt->exec_gen != b2_mvb_scratch_generation()) {  // the scratch moved since the capture
+    if (bt->exec && bt->exec_gen != b2_mvb_scratch_generation(s)) {  // the scratch moved since the capture
         cudaGraphExecDestroy(bt->exec);
         bt->exec = nullptr;
     }
@@ -447,7 +447,7 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
             const cudaError_t ce = cudaStreamEndCapture(s, &graph);
             if (crc == B2_OK && ce == cudaSuccess && graph &&
                 cudaGraphInstantiate(&bt->exec, graph, 0) == cudaSuccess) {
-                bt->exec_gen = b2_mvb_scratch_generation();
+                bt->exec_gen = b2_mvb_scratch_generation(s);
             } else {
                 bt->exec = nullptr;
             }

@@ -442,7 +442,10 @@ int b2_attention_noalloc_impl(const float* q, const uint16_t* k, const uint16_t*
     const int grid = batch * nkv * S;
     const __half* kh = reinterpret_cast<const __half*>(k);
     const __half* vh = reinterpret_cast<const __half*>(v);
-    launch_split(hd, grp, grid, s, q, kh, vh, part, nh, nkv, ctx, S);
+    if (!launch_split(hd, grp, grid, s, q, kh, vh, part, nh, nkv, ctx, S)) {
+        *err = "head_dim must be 64, 128 or 256";
+        return B2_ERR_BAD_ARG;
+    }
     attn_merge_kernel<<<batch * nh, std::min(hd, 256), 0, s>>>(part, out, nh, hd, S);
     e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -36,6 +36,7 @@
 // completions of the warp's own copies.
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -453,10 +454,12 @@ __global__ void __launch_bounds__(kMvbThreads, 1)
     cp_async_wait<0>();
 }
 
-// Per-device scratch of the batched matvec: the per-tile arrival counters
-// (zero between calls: the last unit of a tile resets its counter), the x
-// planes, their scales and Q4_0 accumulator starts, the slice partials.
-// Calls that overlap on the GPU (different streams) race on it.
+// Scratch of the batched matvec, one per (device, stream): the per-tile
+// arrival counters (zero between calls: the last unit of a tile resets its
+// counter), the x planes, their scales and Q4_0 accumulator starts, the slice
+// partials.  Calls on one stream run in order, so they never share it while
+// it is in use; calls on different streams (two models, or two batches of
+// one model on different threads) each get their own.
 struct MvbScratch {
     uint8_t* buf = nullptr;
     size_t bytes = 0;
@@ -465,7 +468,7 @@ struct MvbScratch {
     bool attr_set = false;
 };
 std::mutex g_mvb_mu;
-std::vector<MvbScratch> g_mvb;
+std::map<std::pair<int, cudaStream_t>, MvbScratch> g_mvb;
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
@@ -512,8 +515,7 @@ int mvb_run(bool q8, bool tiled, const MvbMat& mat, const float* x, float* y, in
         return B2_ERR_CUDA;
     }
     std::lock_guard<std::mutex> lk(g_mvb_mu);
-    if ((int)g_mvb.size() <= dev) g_mvb.resize(dev + 1);
-    MvbScratch* sc = &g_mvb[dev];
+    MvbScratch* sc = &g_mvb[{dev, s}];
     if (!sc->sms && cudaDeviceGetAttribute(&sc->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
         *err = "cudaDeviceGetAttribute failed";
         return B2_ERR_CUDA;
@@ -636,11 +638,12 @@ int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t 
     return mvb_run(q8, true, mat, x, y, nvec, s, err);
 }
 
-// Generation of the current device's scratch buffer: a CUDA graph that
-// captured batched matvecs is valid while this is unchanged.
-unsigned long long b2_mvb_scratch_generation() {
+// Generation of the scratch buffer of stream s on the current device: a CUDA
+// graph that captured batched matvecs on s is valid while this is unchanged.
+unsigned long long b2_mvb_scratch_generation(cudaStream_t s) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
     std::lock_guard<std::mutex> lk(g_mvb_mu);
-    return (int)g_mvb.size() > dev ? g_mvb[dev].gen : 0;
+    const auto it = g_mvb.find({dev, s});
+    return it == g_mvb.end() ? 0 : it->second.gen;
 }

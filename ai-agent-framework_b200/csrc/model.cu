@@ -11,6 +11,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -20,12 +21,20 @@
 
 namespace b2 {
 
-int (*g_malloc_hook)(void** p, size_t bytes) = nullptr;
+// Allocation-failure injection (b2_debug_fail_alloc): the device allocation
+// that brings g_fail_left to zero fails.
+std::atomic<int> g_fail_left{0};
 
 namespace {
 
 int dev_malloc(void** p, size_t bytes) {
-    if (g_malloc_hook) return g_malloc_hook(p, bytes);
+    int left = g_fail_left.load();
+    while (left > 0 && !g_fail_left.compare_exchange_weak(left, left - 1)) {
+    }
+    if (left == 1) {
+        *p = nullptr;
+        return -1;
+    }
     return cudaMalloc(p, bytes) == cudaSuccess ? 0 : -1;
 }
 
@@ -509,7 +518,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // mapping covers nothing else and its layout is the same on every rank
     if (tp > 1) {
         m->xch_bytes = xch_bytes(H, tp);
-        if (cudaMalloc(&m->xch, m->xch_bytes) != cudaSuccess) {
+        if (dev_malloc(&m->xch, m->xch_bytes) != 0) {
             m->xch = nullptr;
             return bail(B2_ERR_OOM, "device allocation of the exchange buffer failed");
         }

@@ -1,5 +1,6 @@
 // Host-side model object behind the b2_model handle.
 #pragma once
+#include <atomic>
 #include <cuda_runtime.h>
 
 #include <map>
@@ -35,9 +36,10 @@ struct StreamState {
     std::mt19937_64 rng;
 };
 
-// Process-wide launch hooks for tests of the failure paths (fault injection
-// on the host: a failing allocation is simulated, nothing faults the GPU).
-extern int (*g_malloc_hook)(void** p, size_t bytes);
+// Process-wide hook for tests of the failure paths (fault injection on the
+// host: a failing device allocation is simulated, nothing faults the GPU):
+// the load's device allocation that brings it from 1 to 0 fails.
+extern std::atomic<int> g_fail_left;
 
 }  // namespace b2
 

@@ -208,6 +208,19 @@ def profile_traffic(kernel: str):
     return None
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (/proc/cpuinfo), or the platform string."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or platform.machine()
+
+
 def cpu_baseline_goref(path: str, shape_name: str = "qwen2.5-0.5b", seconds: float = 12.0,
                        prefill: int = 16) -> dict:
     """Decode tok/s of the oracle (the Go engine restated, its worker pool with
@@ -226,8 +239,8 @@ def cpu_baseline_goref(path: str, shape_name: str = "qwen2.5-0.5b", seconds: flo
         t = int(np.argmax(g.forward([t])))
         n += 1
     dt = time.perf_counter() - t0
-    return {"value": n / dt, "unit": "tok/s", "cores": g.threads, "kind": "port",
-            "sample": f"{n} greedy decode tokens after a {len(prompt)}-token prefill, same synthetic GGUF, "
+    return {"value": n / dt, "unit": "tok/s", "cores": g.threads, "kind": "port", "cpu_model": cpu_model(),
+            "logical_cpus": os.cpu_count(), "sample": f"{n} greedy decode tokens after a {len(prompt)}-token prefill, same synthetic GGUF, "
                       f"{dt:.1f} s, goref worker pool with {g.threads} threads"}
 
 
@@ -266,8 +279,8 @@ def run_reference(args) -> None:
         "warmup": args.warmup, "ms_per_step": 1000.0 * dt / max(n, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "prefill_s": t_pref, "engine": who},
-        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind,
-                         "sample": f"{n} greedy decode tokens after the 129-token prefill ({dt:.1f} s)"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": kind, "cpu_model": cpu_model(),
+                         "logical_cpus": os.cpu_count(), "sample": f"{n} greedy decode tokens after the 129-token prefill ({dt:.1f} s)"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

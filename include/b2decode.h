@@ -207,8 +207,10 @@ int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, fl
  * q, k, v and out.  Limit: batch * nh * (hd + 2) <= 524288 floats, larger
  * sizes fail with B2_ERR_BAD_ARG.  The first call on a device looks up the
  * array's device address; make that first call before any stream capture.
- * All calls share the array, so calls whose kernels overlap on the GPU race.
- * No counterpart in the reference. */
+ * The address is cached per device for the life of the process: after a
+ * caller resets a device (cudaDeviceReset) this entry point must not be
+ * called on it again.  All calls share the array, so calls whose kernels
+ * overlap on the GPU race.  No counterpart in the reference. */
 int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
                                 int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream);
 
@@ -223,8 +225,13 @@ int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_
  * model's own single-sequence cache is not touched); next_out is the argmax
  * after the prompt.  b2_batch_step
  * feeds tokens[B] (one per slot, every slot) and writes the B argmax ids;
- * b2_batch_logits copies the last step's logits, [B][vocab_size].  Needs a
+ * b2_batch_logits copies the logits of the last forward of the batch: the B
+ * rows of the last b2_batch_step, or, after a b2_batch_prefill, the rows of
+ * its last prompt chunk (row i = chunk token i), [B][vocab_size].  Needs a
  * single-GPU model with the fp16 cache; the model's device must be current.
+ * Every batch of a model runs on the model's stream and shares its scratch,
+ * so calls on the batches of one model, like calls on the model itself, must
+ * be serialised by the caller; batches of different models are independent.
  * A batch is used only while its model is loaded; b2_batch_free may come
  * before or after b2_free of the model.
  * No single counterpart in the reference (its engine runs one sequence). */
@@ -286,6 +293,14 @@ void* b2_stream_handle(const b2_model* m);
  * b2_device_status while the context stays usable.  0 disables.  No
  * reference counterpart. */
 int b2_debug_wait_skew(b2_model* m, int32_t skew);
+
+/* Test hook for allocation failures: the nth device allocation that
+ * b2_load makes from now on (1 = the next one) fails as if cudaMalloc had
+ * returned an error, so the caller sees B2_ERR_OOM and can check that the
+ * failed load freed everything it had taken.  The hook disarms itself after
+ * firing; 0 disarms it.  Process-wide.  No reference counterpart (the Go
+ * engine's allocations cannot fail short of a runtime panic). */
+int b2_debug_fail_alloc(int32_t nth);
 
 #ifdef __cplusplus
 }

@@ -5,12 +5,7 @@ step's logits of every slot are compared with the oracle run on that
 sequence alone with the same token history (teacher-forced on the batch's
 own ids): within the logits bar of the single-sequence path (1e-2 relative
 L2 per step) and the same argmax on at least 99% of the steps.
-
-Until the batched decode has had its first run on a B200 these tests run
-only with B2_BATCH_DECODE_GPU=1 set.
 """
-import os
-
 import numpy as np
 import pytest
 
@@ -18,11 +13,7 @@ import b2decode
 import goref
 from b2decode import gguf_writer as gw
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("B2_BATCH_DECODE_GPU") != "1",
-                       reason="batched decode not yet run on a B200: set B2_BATCH_DECODE_GPU=1"),
-]
+pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = 1e-2
 

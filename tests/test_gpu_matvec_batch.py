@@ -4,12 +4,7 @@ restatement of the Go Q8_0 / Q4_0 matvec, one vector at a time.
 The kernel splits each vector into three int8 planes (about 22 bits relative
 to the 32-block maximum), so its dots agree with the fp32 loop to rounding:
 the bar is the batch-1 entry point's, 1e-5 relative L2 per vector.
-
-Until the batched kernel has had its first run on a B200 these tests run only
-with B2_MATVEC_BATCH_GPU=1 set.
 """
-import os
-
 import numpy as np
 import pytest
 
@@ -17,11 +12,7 @@ import b2decode
 import goref
 from b2decode import gguf_writer as gw
 
-pytestmark = [
-    pytest.mark.gpu,
-    pytest.mark.skipif(os.environ.get("B2_MATVEC_BATCH_GPU") != "1",
-                       reason="batched matvec not yet run on a B200: set B2_MATVEC_BATCH_GPU=1"),
-]
+pytestmark = pytest.mark.gpu
 
 TOL = 1e-5
 
