@@ -60,6 +60,12 @@ class ModelShape:
     wtype: str = "q8_0"
     bos_id: int = 1
     eos_id: int = 2
+    # > 0: only the first distinct_layers layers have data of their own;
+    # layer i's tensor infos point at the data of layer i % distinct_layers
+    # (GGUF tensor infos may share offsets).  A reader still loads every
+    # layer as a tensor of its own, so the bytes a decode step streams are
+    # those of the full model, from a file a fraction of its size.
+    distinct_layers: int = 0
 
     @property
     def head_dim(self) -> int:
@@ -96,6 +102,10 @@ SHAPES["tiny-untied"] = SHAPES["tiny"].with_(tied=False)
 # Llama-3-8B widths (hidden 4096, FFN 14336, vocab 128256) cut to 4 layers:
 # the config-2 parity case at its real matrix shapes.
 SHAPES["llama3-8b-4l"] = SHAPES["llama3-8b"].with_(layers=4)
+# Qwen2.5-72B at all 80 layers whose tensor infos share one layer's data:
+# 3.6 GB on disk, 75.9 GB of weights once loaded (the tensor-parallel decode
+# benchmark at the full depth).
+SHAPES["qwen2.5-72b-alias"] = SHAPES["qwen2.5-72b"].with_(distinct_layers=1)
 
 
 # ---------------------------------------------------------------------------
@@ -184,6 +194,7 @@ class TensorSpec:
     init: str          # "normal", "ones"
     index: int = 0
     is_vec: bool = False
+    alias_of: int = -1  # index of the tensor whose data this one shares (-1: its own)
 
     @property
     def nbytes(self) -> int:
@@ -223,6 +234,14 @@ def tensor_plan(shape: ModelShape) -> list[TensorSpec]:
         mat(p + "ffn_down.weight", FF, H)
     for i, s in enumerate(specs):
         s.index = i
+    k = shape.distinct_layers
+    if k > 0:
+        first = {sp.name: sp.index for sp in specs}
+        for sp in specs:
+            if sp.name.startswith("blk."):
+                layer = int(sp.name.split(".")[1])
+                if layer >= k:
+                    sp.alias_of = first[sp.name.replace(f"blk.{layer}.", f"blk.{layer % k}.", 1)]
     return specs
 
 
@@ -315,10 +334,14 @@ def write_model(path: str, shape: ModelShape, seed: int = 0, workers: int = 1, p
         infos += struct.pack("<I", len(dims))
         for d in dims:
             infos += struct.pack("<Q", d)
-        infos += struct.pack("<IQ", s.gtype, offset)
-        offsets.append(offset)
-        offset += s.nbytes
-        offset = (offset + ALIGNMENT - 1) // ALIGNMENT * ALIGNMENT
+        own = s.alias_of < 0
+        infos += struct.pack("<IQ", s.gtype, offset if own else offsets[s.alias_of])
+        offsets.append(offset if own else offsets[s.alias_of])
+        if own:
+            offset += s.nbytes
+            offset = (offset + ALIGNMENT - 1) // ALIGNMENT * ALIGNMENT
+    data_specs = [s for s in specs if s.alias_of < 0]
+    data_offsets = [offsets[s.index] for s in data_specs]
 
     header = struct.pack("<IIQQ", GGUF_MAGIC, 3, len(specs), n_kv)
     h = hashlib.sha256()
@@ -342,12 +365,12 @@ def write_model(path: str, shape: ModelShape, seed: int = 0, workers: int = 1, p
                 pool = ProcessPoolExecutor(workers, mp_context=mp.get_context("spawn"))
             else:
                 pool = ThreadPoolExecutor(workers)
-            futs = [pool.submit(_tensor_bytes, (sp, seed)) for sp in specs]
+            futs = [pool.submit(_tensor_bytes, (sp, seed)) for sp in data_specs]
             chunks = (f.result() for f in futs)
         else:
-            chunks = (_tensor_bytes((sp, seed)) for sp in specs)
+            chunks = (_tensor_bytes((sp, seed)) for sp in data_specs)
         try:
-            for off, buf in zip(offsets, chunks):
+            for off, buf in zip(data_offsets, chunks):
                 if written < off:
                     w(b"\0" * (off - written))
                     written = off

@@ -194,3 +194,21 @@ def test_writer_command_line_writes_the_same_bytes(tmp_path):
     size, digest = r.stdout.split()
     assert int(size) == ref["bytes"] and digest == ref["sha256"]
     assert out.read_bytes() == (tmp_path / "lib.gguf").read_bytes()
+
+
+def test_aliased_layers_share_data_and_load(oracle_lib, tmp_path):
+    """A GGUF whose layers >= distinct_layers point at layer 0's data: the file
+    holds one layer's bytes, every layer reads back as layer 0's tensors, and
+    the oracle runs it like any model."""
+    base = gw.SHAPES["tiny"].with_(layers=3, tied=False)
+    a, one = str(tmp_path / "alias.gguf"), str(tmp_path / "one.gguf")
+    ra = gw.write_model(a, base.with_(distinct_layers=1), seed=4)
+    r1 = gw.write_model(one, base.with_(layers=1), seed=4)
+    assert ra["bytes"] - r1["bytes"] < 4096  # only the extra tensor infos
+    n = base.hidden * base.hidden
+    w0 = goref.dequant_tensor(a, "blk.0.attn_q.weight", n)
+    for layer in (1, 2):
+        assert np.array_equal(goref.dequant_tensor(a, f"blk.{layer}.attn_q.weight", n), w0)
+    assert np.array_equal(goref.dequant_tensor(one, "blk.0.attn_q.weight", n), w0)
+    g = goref.GoRef(a, n_threads=2)
+    assert np.isfinite(g.forward([1, 2, 3])).all()
