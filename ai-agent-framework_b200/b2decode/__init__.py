@@ -28,6 +28,12 @@ QTYPE_Q8_0 = 8
 QTYPE_Q4_0 = 2
 
 
+class TpShare(C.Structure):
+    _fields_ = [("q_row0", C.c_int32), ("q_rows", C.c_int32), ("kv_row0", C.c_int32), ("kv_rows", C.c_int32),
+                ("ffn_row0", C.c_int32), ("ffn_rows", C.c_int32), ("vocab_row0", C.c_int32),
+                ("vocab_rows", C.c_int32)]
+
+
 class B2Error(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"B2_ERR_{ERRORS.get(code, code)} ({code}): {msg}")
@@ -98,6 +104,7 @@ SIGNATURES = {
     "b2_matvec": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _P]),
     "b2_matvec_batch": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _i32, _P]),
     "b2_model_matvec": (C.c_int, [_P, C.c_char_p, _P, _P, _i32, _P]),
+    "b2_model_gemm": (C.c_int, [_P, C.c_char_p, _P, _P, _i32, _P]),
     "b2_batch_create": (C.c_int, [_P, _i32, C.POINTER(_P)]),
     "b2_batch_free": (None, [_P]),
     "b2_batch_prefill": (C.c_int, [_P, _i32, _i32p, _i32, C.POINTER(_i32)]),
@@ -111,6 +118,7 @@ SIGNATURES = {
     "b2_trace_step": (C.c_int, [_P, _i32, C.POINTER(_i64), _i64, _i32p, _i32p]),
     "b2_debug_wait_skew": (C.c_int, [_P, _i32]),
     "b2_debug_fail_alloc": (C.c_int, [_i32]),
+    "b2_tp_share_of": (C.c_int, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, C.POINTER(TpShare)]),
     "b2_tp_handle": (C.c_int, [_P, C.c_char_p]),
     "b2_tp_connect": (C.c_int, [_P, C.c_char_p]),
 }
@@ -266,6 +274,11 @@ class Model:
         x [nvec][cols], y [nvec][rows] fp32 at device addresses."""
         _check(lib().b2_model_matvec(self._h, name.encode(), x_ptr, y_ptr, nvec, stream or None))
 
+    def gemm(self, name: str, x_ptr: int, y_ptr: int, ntok: int, stream: int = 0) -> None:
+        """Y = W X over the resident tensor `name` for ntok tokens on the tensor
+        cores: x [ntok][cols], y [ntok][rows] fp32 at device addresses."""
+        _check(lib().b2_model_gemm(self._h, name.encode(), x_ptr, y_ptr, ntok, stream or None))
+
     def device_status(self) -> int:
         return lib().b2_device_status(self._h)
 
@@ -287,6 +300,17 @@ class Model:
 
     def debug_wait_skew(self, skew: int) -> None:
         _check(lib().b2_debug_wait_skew(self._h, int(skew)))
+
+
+def tp_share_of(hidden: int, heads: int, kv_heads: int, ffn: int, vocab: int, tp: int, rank: int) -> dict:
+    """The slices a tensor-parallel rank keeps, computed by the loader's own
+    arithmetic (b2_tp_share_of; host only): (first, end) ranges."""
+    s = TpShare()
+    _check(lib().b2_tp_share_of(hidden, heads, kv_heads, ffn, vocab, tp, rank, C.byref(s)))
+    q = (s.q_row0, s.q_row0 + s.q_rows)
+    f = (s.ffn_row0, s.ffn_row0 + s.ffn_rows)
+    return {"q_rows": q, "kv_rows": (s.kv_row0, s.kv_row0 + s.kv_rows), "wo_cols": q, "ffn_rows": f,
+            "down_cols": f, "vocab_rows": (s.vocab_row0, s.vocab_row0 + s.vocab_rows)}
 
 
 def debug_fail_alloc(nth: int) -> None:

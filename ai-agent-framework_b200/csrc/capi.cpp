@@ -19,6 +19,8 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
                          cudaStream_t s, std::string* err);
 int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
+int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
+                       float* y, int ntok, cudaStream_t s, std::string* err);
 int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err);
 void b2_batch_free_impl(b2_batch* bt);
 int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, int32_t* next_out, std::string* err);
@@ -450,6 +452,25 @@ int b2_model_matvec(const b2_model* m, const char* name, const float* x, float* 
     return ret(rc, err);
 }
 
+int b2_model_gemm(const b2_model* m, const char* name, const float* x, float* y, int32_t ntok, void* stream) {
+    if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
+    if (!name || !x || !y) return ret(B2_ERR_BAD_ARG, "null argument");
+    if (ntok < 1) return ret(B2_ERR_BAD_ARG, "at least one token");
+    auto it = m->tensors.find(name);
+    if (it == m->tensors.end()) return ret(B2_ERR_BAD_ARG, std::string("tensor not found: ") + name);
+    const b2::TensorLoc& t = it->second;
+    if (t.type != 8 && t.type != 2) return ret(B2_ERR_UNSUPPORTED_TYPE, std::string(name) + " is not a Q8_0 / Q4_0 matrix");
+    if (t.half) return ret(B2_ERR_BAD_ARG, std::string(name) + ": gate and up rows are interleaved in the resident matrix");
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device)
+        return ret(B2_ERR_BAD_ARG, "the model's device must be the current device");
+    std::string err;
+    const int rows = (int)(t.elements / (uint64_t)t.cols);
+    int rc = b2_tiled_gemm_impl((int)t.type, t.dev, t.rp, t.row0, rows, (int)t.cols, x, y, ntok,
+                                stream ? static_cast<cudaStream_t>(stream) : m->stream, &err);
+    return ret(rc, err);
+}
+
 int b2_batch_create(b2_model* m, int32_t batch, b2_batch** out) {
     if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
     if (!out) return ret(B2_ERR_BAD_ARG, "null argument");
@@ -522,6 +543,13 @@ int b2_debug_wait_skew(b2_model* m, int32_t skew) {
     if (skew < 0) return ret(B2_ERR_BAD_ARG, "skew must be >= 0");
     m->wait_skew = (unsigned)skew;
     return B2_OK;
+}
+
+int b2_tp_share_of(int32_t hidden, int32_t heads, int32_t kv_heads, int32_t ffn, int32_t vocab, int32_t tp,
+                   int32_t rank, b2_tp_share* out) {
+    if (!out || heads <= 0 || kv_heads <= 0 || hidden <= 0) return ret(B2_ERR_BAD_ARG, "bad model shape");
+    const int rc = b2::tp_share(hidden, heads, kv_heads, ffn, vocab, tp, rank, out);
+    return ret(rc, rc ? "heads must divide by the degree, the rank lie below it and every share be non-empty" : "");
 }
 
 int b2_debug_fail_alloc(int32_t nth) {

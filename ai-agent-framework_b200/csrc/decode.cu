@@ -48,6 +48,13 @@ namespace {
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;      // 2 s for any consumer wait
 constexpr uint64_t kProducerLimitNs = 8000000000ull;  // producer slot waits outlast consumer polls
+// A wait reads the device error flag (another CTA gave up) only once it has
+// lasted this long: the flag is a global load, an L2 round trip that would
+// otherwise sit between two polls of every waiting thread and delay the
+// moment it sees its data.  Normal hand-offs end well within it.
+constexpr uint64_t kErrCheckNs = 20000ull;
+// Attention split partials the Wo stage polls per round (merge_planes).
+constexpr int kMergePerRound = 2;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 
 // ---------------------------------------------------------------------------
@@ -137,8 +144,9 @@ __device__ __forceinline__ bool slot_wait(uint64_t* bar, uint32_t parity, int* e
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (*(volatile int*)err) return false;
-        if (global_ns() - t0 > kProducerLimitNs) {
+        const uint64_t dt = global_ns() - t0;
+        if (dt > kErrCheckNs && *(volatile int*)err) return false;
+        if (dt > kProducerLimitNs) {
             set_err(err, B2_ERR_TIMEOUT);
             return false;
         }
@@ -547,7 +555,7 @@ __device__ __noinline__ int attn_phase(const uint8_t* kg, const uint8_t* vg, uin
                 ok = 0;
                 break;
             }
-            if (*(volatile int*)err) {
+            if (now - w0 > kErrCheckNs && *(volatile int*)err) {
                 ok = 0;
                 break;
             }
@@ -791,15 +799,19 @@ __device__ __forceinline__ void planes8(const float* v, bool on, int b, int sub,
 // 16-byte loads), multiplies them by the norm gains (global `gain`; none when
 // null) and splits them (planes8).  The RMSNorm scale is one scalar per
 // token, so it is applied to the dot products instead (the dot is linear); the
-// sum of squares of the raw values is returned for it.  With `embed` set the
+// sum of squares of the raw values is returned for it.  With NADD > 0 each
+// value is src + add[0] + ... + add[NADD - 1] (arrays add_stride words apart,
+// the same tag, all polled in the same round): the residual stream after a
+// down phase split over K.  With `embed` set the
 // values are the embedding of token tok (layer 0; an id outside the
 // vocabulary embeds to zero) instead of LL words.  A
 // failed or timed-out poll sets ok = 0 but the loop runs to the end, so every
 // lane reaches every shuffle.  Not inlined (register peak, code size).
-template <int QT>
+template <int QT, int NADD>
 __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsigned tag, int* err, int embed, int tok,
                                                 const uint8_t* embd, int V, int H, int Vp, uint32_t xq_off,
-                                                uint32_t xsc_off, uint32_t xsm_off, const float* gain, int sums) {
+                                                uint32_t xsc_off, uint32_t xsm_off, const float* gain, int sums,
+                                                const uint2* add, int add_stride) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* xqb = smem + xq_off;
     float* xsc = reinterpret_cast<float*>(smem + xsc_off);
@@ -825,7 +837,7 @@ __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsig
             for (int e = 0; e < 8; e++) v[e] = embed_val<QT>(embd, V, H, Vp, tok, j0 + e);
         } else if (on) {
             const uint2* sp = src + j0;
-            uint4 w[4];
+            uint4 w[4], wa[NADD > 0 ? NADD : 1][4];
             for (;;) {
                 bool got = true;
 #pragma unroll
@@ -833,13 +845,20 @@ __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsig
                     w[k] = ll_load2(sp + 2 * k);
                     got &= (w[k].y == tag) & (w[k].w == tag);
                 }
+#pragma unroll
+                for (int a = 0; a < NADD; a++)
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        wa[a][k] = ll_load2(add + (size_t)a * add_stride + j0 + 2 * k);
+                        got &= (wa[a][k].y == tag) & (wa[a][k].w == tag);
+                    }
                 if (got || !ok) break;
                 const uint64_t now = global_ns();
                 if (t0 == 0) t0 = now;
                 if (now - t0 > kWaitLimitNs) {
                     set_err(err, B2_ERR_TIMEOUT);
                     ok = false;
-                } else if (*(volatile int*)err) {
+                } else if (now - t0 > kErrCheckNs && *(volatile int*)err) {
                     ok = false;
                 }
             }
@@ -848,6 +867,15 @@ __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsig
                 v[2 * k] = __uint_as_float(w[k].x);
                 v[2 * k + 1] = __uint_as_float(w[k].z);
             }
+            // the down-phase partials, added in slice order (every reader of
+            // the residual stream adds them in this order)
+#pragma unroll
+            for (int a = 0; a < NADD; a++)
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    v[2 * k] += __uint_as_float(wa[a][k].x);
+                    v[2 * k + 1] += __uint_as_float(wa[a][k].z);
+                }
         } else {
 #pragma unroll
             for (int e = 0; e < 8; e++) v[e] = 0.0f;
@@ -870,8 +898,8 @@ __device__ __noinline__ GatherRes gather_planes(const uint2* src, int nbk, unsig
 // LL words [nh][S][hd + 2]) as transformer.go:664-685 over all positions:
 // o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M), M = max_s m_s (the new
 // position is part of the last split, so the sum is positive).  Each thread
-// merges the 8 outputs of one quarter-block (one head, hd >= 16) two splits
-// per poll, rescaling as the maximum grows, and splits them (planes8).  Polls
+// merges the 8 outputs of one quarter-block (one head, hd >= 16) up to
+// kMergePerRound splits per poll, rescaling as the maximum grows, and splits them (planes8).  Polls
 // and fails like gather_planes (every lane reaches every shuffle).  Not
 // inlined (register peak, code size).
 __device__ __noinline__ int merge_planes(const uint2* part, int nbk, int S, int hsh, unsigned tag, int* err,
@@ -896,33 +924,37 @@ __device__ __noinline__ int merge_planes(const uint2* part, int nbk, int S, int 
             const uint2* ph = part + (size_t)(j0 >> hsh) * S * W2 + (j0 & (hd - 1));
             float M = -INFINITY, L = 0.0f;
 #pragma unroll 1
-            for (int s0 = 0; s0 < S; s0 += 2) {
-                const bool two = s0 + 1 < S;
-                uint4 w[2][5];
+            for (int s0 = 0; s0 < S; s0 += kMergePerRound) {
+                // up to kMergePerRound splits per poll round (loads of all of
+                // them in flight at once); a slot past the last split re-reads
+                // the last one and is not merged
+                uint4 w[kMergePerRound][5];
                 for (;;) {
                     bool got = true;
 #pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        const uint2* pp = ph + (size_t)(two ? s0 + u : s0) * W2;
+                    for (int u = 0; u < kMergePerRound; u++) {
+                        const uint2* pp = ph + (size_t)min(s0 + u, S - 1) * W2;
 #pragma unroll
                         for (int k = 0; k < 4; k++) w[u][k] = ll_load2(pp + 2 * k);
                         w[u][4] = ll_load2(pp - (j0 & (hd - 1)) + hd);  // (m, l)
+                    }
+#pragma unroll
+                    for (int u = 0; u < kMergePerRound; u++)
 #pragma unroll
                         for (int k = 0; k < 5; k++) got &= (w[u][k].y == tag) & (w[u][k].w == tag);
-                    }
                     if (got || !ok) break;
                     const uint64_t now = global_ns();
                     if (t0 == 0) t0 = now;
                     if (now - t0 > kWaitLimitNs) {
                         set_err(err, B2_ERR_TIMEOUT);
                         ok = false;
-                    } else if (*(volatile int*)err) {
+                    } else if (now - t0 > kErrCheckNs && *(volatile int*)err) {
                         ok = false;
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    if (u == 1 && !two) break;
+                for (int u = 0; u < kMergePerRound; u++) {
+                    if (s0 + u >= S) break;
                     const float ms = __uint_as_float(w[u][4].x), ls = __uint_as_float(w[u][4].z);
                     const float Mn = fmaxf(M, ms);
                     const float co = M == -INFINITY ? 0.0f : expf(M - Mn);
@@ -996,7 +1028,7 @@ __device__ __noinline__ int tp_reduce_rows(const ModelDev& m, size_t xo, int row
                     ok = 0;
                     break;
                 }
-                if (*(volatile int*)m.err) {
+                if (now - w0 > kErrCheckNs && *(volatile int*)m.err) {
                     ok = 0;
                     break;
                 }
@@ -1027,7 +1059,7 @@ __device__ __noinline__ unsigned long long tp_argmax_key(const ModelDev& m, unsi
             }
             const uint64_t now = global_ns();
             if (w0 == 0) w0 = now;
-            if (now - w0 > kWaitLimitNs || *(volatile int*)m.err) {
+            if (now - w0 > kWaitLimitNs || (now - w0 > kErrCheckNs && *(volatile int*)m.err)) {
                 set_err(m.err, B2_ERR_TIMEOUT);
                 break;
             }
@@ -1157,8 +1189,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                         } else {
                             // chunk k = (tile group kt, K-slice ks)
                             const int t0 = pl.u0 + kt * pl.nt, ntc = min(pl.nt, pl.u0 + pl.n - t0);
-                            const int bb0 = ks * pl.bpk, nbc = min(pl.bpk, g.nb - bb0);
-                            const size_t unit0 = (size_t)t0 * g.nb + bb0;
+                            const int bb0 = ks * pl.bpk, nbc = min(pl.bpk, pl.kbn - bb0);
+                            const size_t unit0 = (size_t)t0 * g.nb + pl.kb0 + bb0;
                             const uint32_t qlen = (uint32_t)(ntc * nbc * kTileRows * QB);
                             const uint32_t slen = (uint32_t)(ntc * nbc * 2 * kTileRows);
                             mbar_arrive_expect_tx(&full[slot], qlen + slen);
@@ -1288,6 +1320,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         const uint32_t attn_off = so.xs;  // the attention scratch
 
         // 1. stage the phase input: gather (+ norm / merge) into xs, then planes
+        if (qa && !has_rows && qcta && at1 > at0) {
+            // a q CTA with no q / k / v rows of its own (the distributed form
+            // with fewer tiles than CTAs) still attends: its first cached K/V
+            // tile goes out now, as in the stage below
+            cp_async_commit();
+            attn_load_tile<KV32>(kg, vg, (uint32_t)(m.kvd * es), hd, TP, at0, min(TP, at1 - at0), attn_off);
+        }
         if (qa && g.layer == 0) {
             // transformer.go:524-531: the residual stream starts at the embedding
             #pragma unroll 1
@@ -1320,10 +1359,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                                  : (g.kind == PH_GATEUP ? layers[g.layer].ffn_norm : m.out_norm);
             float ss = 0.0f;
             if (alive) {
-                const GatherRes gr = gather_planes<QT>(g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2, m.H / 32,
-                                                       g.kind == PH_GATEUP ? tag_here : tag_prev, m.err,
-                                                       qa && g.layer == 0, tok, m.tok_embd, m.Vemb, m.H, m.Vp_emb,
-                                                       so.xq, so.xsc, so.xsm, nw, QT != 8);
+                // QA (after layer 0) and the LM head read the residual stream after
+                // the previous down phase: x2, or with the down phase split over K
+                // x1 plus the down partials of the previous layer
+                GatherRes gr;
+                if (m.dn_split > 1 && g.kind != PH_GATEUP && !(qa && g.layer == 0))
+                    gr = gather_planes<QT, kDownSplit>(m.ll_x1, m.H / 32, tag_prev, m.err, 0, tok, m.tok_embd, m.Vemb,
+                                                       m.H, m.Vp_emb, so.xq, so.xsc, so.xsm, nw, QT != 8,
+                                                       m.ll_dnp + (size_t)((g.layer - 1) & 1) * kDownSplit * m.H, m.H);
+                else
+                    gr = gather_planes<QT, 0>(g.kind == PH_GATEUP ? m.ll_x1 : m.ll_x2, m.H / 32,
+                                              g.kind == PH_GATEUP ? tag_here : tag_prev, m.err, qa && g.layer == 0, tok,
+                                              m.tok_embd, m.Vemb, m.H, m.Vp_emb, so.xq, so.xsc, so.xsm, nw, QT != 8,
+                                              nullptr, 0);
                 alive = gr.ok;
                 ss = gr.ss;
             }
@@ -1333,15 +1381,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             ss = warp_sum(ss);
             if (lane == 0) red[32 + cw] = ss;  // summed after the rows barrier
         } else if (g.kind == PH_WO && has_rows) {
+            // with the down phase split over K, the residual rows this CTA owns
+            // still lack the previous layer's down partials: their words go to
+            // shared memory now (two 16-row slices of LL words, checked in the
+            // epilogue) and land while the merge below polls
+            if (m.dn_split > 1 && g.layer > 0 && ct < 2 * kTileRows / 2)
+                cp_async16(smem + so.dnp + 16 * ct,
+                           m.ll_dnp + ((size_t)(((g.layer - 1) & 1) * kDownSplit + ct / 8)) * m.H + own0 + 2 * (ct % 8));
+            cp_async_commit();
             // the attention of every head, merged from its split partials
             if (alive)
                 alive = merge_planes(m.ll_part, m.qd / 32, S, __ffs(hd) - 1, tag_here, m.err, so.xq, so.xsc, so.xsm,
                                      QT != 8) != 0;
+            cp_async_wait();
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         } else if (g.kind == PH_DOWN && has_rows) {
+            // this CTA's blocks of the SwiGLU output (all of them, or its half of
+            // the row when the phase is split over K)
             if (alive)
-                alive = gather_planes<QT>(m.ll_act, m.FF / 32, tag_here, m.err, 0, 0, m.tok_embd, m.Vemb, m.H, m.Vp_emb, so.xq,
-                                          so.xsc, so.xsm, nullptr, QT != 8).ok;
+                alive = gather_planes<QT, 0>(m.ll_act + 32 * pl.kb0, pl.kbn, tag_here, m.err, 0, 0, m.tok_embd, m.Vemb,
+                                             m.H, m.Vp_emb, so.xq, so.xsc, so.xsm, nullptr, QT != 8, nullptr, 0).ok;
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
         } else {
             if (TR && a.trace && ct == 0) a.trace[(tr + 1) * grid + cta] = global_ns();
@@ -1378,8 +1437,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 if (!landed) alive = false;
                 if (alive) {
                     const int lt0 = kt * pl.nt, ntc = min(pl.nt, pl.n - lt0);
-                    const int bb0 = ks * pl.bpk, nbc = min(pl.bpk, g.nb - bb0);
-                    const int qlen = ntc * nbc * kTileRows * QB, slen = ntc * nbc * 2 * kTileRows;
+                    const int bb0 = ks * pl.bpk, nbc = min(pl.bpk, pl.kbn - bb0);
+                    const int qlen = ntc * nbc * kTileRows * QB;
                     float* yk = yb + ks * rc;
                     #pragma unroll 1
                     for (int tl = 0; tl < ntc; tl++) {
@@ -1502,6 +1561,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                     break;
                 case PH_WO:
                 case PH_DOWN: {
+                    if (g.kind == PH_DOWN && m.dn_split > 1) {
+                        // split over K: this half-row's partial sums of the tile's
+                        // residual rows, for the readers of the residual stream
+                        uint2* dp = m.ll_dnp +
+                                    ((size_t)((g.layer & 1) * kDownSplit + dn_slice_of(cta, grid, m.H / kTileRows))) * m.H +
+                                    row0;
+                        #pragma unroll 1
+                        for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) ll_store(dp + j, ysum(j), tag);
+                        break;
+                    }
+                    if (g.kind == PH_WO && m.dn_split > 1 && g.layer > 0) {
+                        // the owned rows become x2 of the previous layer: x1 plus its
+                        // down partials in slice order (as every gather adds them);
+                        // words the prefetch found stale are polled again
+                        const uint2* dw = reinterpret_cast<const uint2*>(smem + so.dnp);
+                        #pragma unroll 1
+                        for (int j = ct; j < kTileRows * pl.n; j += kConsumerThreads) {
+                            float xr = xres[j];
+                            #pragma unroll
+                            for (int sl = 0; sl < kDownSplit; sl++) {
+                                uint2 w = dw[sl * kTileRows + j];
+                                const uint2* gw = m.ll_dnp +
+                                                  ((size_t)(((g.layer - 1) & 1) * kDownSplit + sl)) * m.H + row0 + j;
+                                uint64_t w0 = 0;
+                                while (w.y != tag_prev && alive) {
+                                    w = ll_load1(gw);
+                                    const uint64_t now = global_ns();
+                                    if (w0 == 0) w0 = now;
+                                    if (now - w0 > kWaitLimitNs) {
+                                        set_err(m.err, B2_ERR_TIMEOUT);
+                                        alive = false;
+                                    }
+                                }
+                                xr += __uint_as_float(w.x);
+                            }
+                            xres[j] = xr;
+                        }
+                    }
                     // residual (transformer.go:576-578, 591-593); the rows are
                     // exactly the residual rows this CTA owns
                     uint2* dstll = g.kind == PH_WO ? m.ll_x1 : m.ll_x2;
@@ -1594,7 +1691,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                         alive = false;
                         break;
                     }
-                    if (*(volatile int*)m.err) {
+                    if (now - w0 > kErrCheckNs && *(volatile int*)m.err) {
                         alive = false;
                         break;
                     }

@@ -29,18 +29,24 @@
 
 int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
+int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
+                       float* y, int ntok, cudaStream_t s, std::string* err);
+int b2_gemm_status(cudaStream_t s);
+unsigned long long b2_gemm_scratch_generation(cudaStream_t s);
 unsigned long long b2_mvb_scratch_generation(cudaStream_t s);
 int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, float* part, size_t part_floats,
                              float* out, int batch, int nh, int nkv, int hd, const int* lens, int add, int stride,
                              int max_len, int sms, cudaStream_t s);
 
 constexpr int kBatchMax = 16;
-constexpr int kBatchSplits = 32;  // attention splits the partial buffer holds
+constexpr int kPrefillChunk = 128;  // prompt tokens per weight pass of a prefill (tensor-core GEMM)
+constexpr int kBatchSplits = 32;    // attention splits the partial buffer holds (for kBatchMax rows)
 
 struct b2_batch {
     b2_model* m = nullptr;
     int B = 0;
     int max_seq = 0;
+    bool model_cache = false;  // kc / vc are the model's own cache (the prompt-prefill workspace)
     void* arena = nullptr;
     __half* kc = nullptr;  // [L][B][max_seq][kvd]
     __half* vc = nullptr;
@@ -53,7 +59,7 @@ struct b2_batch {
     std::vector<int> pos;                                       // positions (host copy)
     bool use_graph = false;                  // replay steps from a captured CUDA graph
     cudaGraphExec_t exec = nullptr;          // the step's launches (tokens and ids copied outside)
-    unsigned long long exec_gen = 0;         // matvec scratch generation it captured
+    unsigned long long exec_gen = 0;         // scratch generation it captured (scratch_generation)
 };
 
 namespace b2 {
@@ -195,6 +201,12 @@ __global__ void bd_argmax_kernel(const float* __restrict__ logits, int V, int* _
     }
 }
 
+// positions p0 .. p0 + n - 1 of a prefill chunk
+__global__ void bd_iota_kernel(int* __restrict__ pos, int n, int p0) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) pos[i] = p0 + i;
+}
+
 bool ok(cudaError_t e, std::string* err, const char* what) {
     if (e == cudaSuccess) return true;
     *err = std::string(what) + ": " + cudaGetErrorString(e);
@@ -206,7 +218,20 @@ bool ok(cudaError_t e, std::string* err, const char* what) {
 
 using namespace b2;
 
+namespace {
+int batch_create(b2_model* m, int B, bool model_cache, b2_batch** out, std::string* err);
+}
+
 int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
+    return batch_create(m, B, false, out, err);
+}
+
+namespace {
+
+// A batch of B slots with KV caches of their own, or (model_cache) one row
+// set over the model's own cache: the workspace of the model's prompt
+// prefill on the tensor cores.
+int batch_create(b2_model* m, int B, bool model_cache, b2_batch** out, std::string* err) {
     const ModelDev& d = m->dev;
     if (B < 1 || B > kBatchMax) {
         *err = "batch size must be 1 to 16";
@@ -229,13 +254,15 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
     bt->m = m;
     bt->B = B;
     bt->max_seq = d.max_seq;
+    bt->model_cache = model_cache;
     bt->pos.assign(B, 0);
-    const size_t kv = (size_t)d.L * B * d.max_seq * d.kvd;
+    const size_t kv = model_cache ? 0 : (size_t)d.L * B * d.max_seq * d.kvd;
     const int n_qkv = d.qd + 2 * d.kvd;
-    // activations for R rows: the B slots of a step, or up to kBatchMax
-    // tokens of one sequence in a prefill chunk
-    const size_t R = kBatchMax;
-    bt->part_floats = R * d.nh * kBatchSplits * (d.hd + 2);
+    // activations for R rows: the B slots of a step, or up to kPrefillChunk
+    // tokens of one sequence in a prefill chunk (whose lm_head runs for its
+    // last token only, so the logits hold kBatchMax rows)
+    const size_t R = std::max(kBatchMax, kPrefillChunk);
+    bt->part_floats = (size_t)kBatchMax * d.nh * kBatchSplits * (d.hd + 2);
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t o = off;
@@ -247,7 +274,7 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
     const size_t o_qkv = take(R * n_qkv * 4), o_q = take(R * d.qd * 4);
     const size_t o_att = take(R * d.qd * 4);
     const size_t o_gu = take(R * 2 * d.FF * 4), o_act = take(R * d.FF * 4);
-    const size_t o_lg = take(R * d.V * 4), o_part = take(bt->part_floats * 4);
+    const size_t o_lg = take((size_t)kBatchMax * d.V * 4), o_part = take(bt->part_floats * 4);
     const size_t o_pos = take(R * 4), o_tok = take(R * 4), o_next = take(R * 4), o_ppos = take(R * 4);
     if (cudaMalloc(&bt->arena, off) != cudaSuccess) {
         delete bt;
@@ -261,8 +288,8 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
         return B2_ERR_OOM;
     }
     uint8_t* A = static_cast<uint8_t*>(bt->arena);
-    bt->kc = reinterpret_cast<__half*>(A + o_kc);
-    bt->vc = reinterpret_cast<__half*>(A + o_vc);
+    bt->kc = model_cache ? static_cast<__half*>(d.kcache) : reinterpret_cast<__half*>(A + o_kc);
+    bt->vc = model_cache ? static_cast<__half*>(d.vcache) : reinterpret_cast<__half*>(A + o_vc);
     bt->x = reinterpret_cast<float*>(A + o_x);
     bt->xn = reinterpret_cast<float*>(A + o_xn);
     bt->y = reinterpret_cast<float*>(A + o_y);
@@ -288,6 +315,8 @@ int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err) {
     return B2_OK;
 }
 
+}  // namespace
+
 // Touches nothing of the model (which may already be freed): cudaFree waits
 // for the device's outstanding work before releasing the arena.
 void b2_batch_free_impl(b2_batch* bt) {
@@ -300,11 +329,30 @@ void b2_batch_free_impl(b2_batch* bt) {
 
 namespace {
 
+// Y = W X for the R rows: the tensor-core GEMM from kGemmMinRows rows on,
+// the batched matvec (one weight pass, int8 planes against the tiled
+// blocks) below.
+constexpr int kGemmMinRows = 2;
+int matmul_rows(int qt, const uint8_t* w, int64_t rp, int rows, int cols, const float* x, float* y, int R,
+                cudaStream_t s, std::string* err) {
+    if (R >= kGemmMinRows && cols % 64 == 0) return b2_tiled_gemm_impl(qt, w, rp, 0, rows, cols, x, y, R, s, err);
+    return b2_tiled_matvec_batch_impl(qt, w, rp, 0, rows, cols, x, y, R, s, err);
+}
+
+// Generation of the scratch buffers a step's launches use (a captured graph
+// holds their addresses).
+unsigned long long scratch_generation(cudaStream_t s) {
+    return b2_mvb_scratch_generation(s) ^ (b2_gemm_scratch_generation(s) << 32);
+}
+
 // R rows through the whole model: row r is token d_tok[r] at position
 // d_rpos[r], its K / V rows going to kc / vc + r * slot_stride positions
 // (per layer, plus kv_off); its attention covers positions 0 .. d_rpos[r].
-// Writes the argmax of every row to d_next and moves d_rpos on by one.
-int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err) {
+// With all_logits the lm_head and argmax run for every row (d_next[r],
+// d_rpos[r] moved on by one); otherwise for the last row only, into logits
+// row 0 and d_next[0] (a prefill chunk needs the argmax after its last token).
+int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err,
+                 bool all_logits = true) {
     b2_model* m = bt->m;
     const ModelDev& d = m->dev;
     cudaStream_t s = m->stream;
@@ -317,7 +365,7 @@ int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_strid
     for (int l = 0; l < d.L && rc == B2_OK; l++) {
         const LayerDev& ld = m->layers_host[l];
         bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, ld.attn_norm, bt->xn, H, d.eps);
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wqkv, tiled_rows(n_qkv), 0, n_qkv, H, bt->xn, bt->qkv, R, s, err);
+        rc = matmul_rows(qt, ld.wqkv, tiled_rows(n_qkv), n_qkv, H, bt->xn, bt->qkv, R, s, err);
         if (rc) break;
         __half* kc = bt->kc + (size_t)l * kv_layer + kv_off;
         __half* vc = bt->vc + (size_t)l * kv_layer + kv_off;
@@ -329,22 +377,23 @@ int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_strid
             *err = "batched attention launch failed";
             break;
         }
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wo, tiled_rows(H), 0, H, d.qd, bt->att, bt->y, R, s, err);
+        rc = matmul_rows(qt, ld.wo, tiled_rows(H), H, d.qd, bt->att, bt->y, R, s, err);
         if (rc) break;
         bd_add_kernel<<<add_blocks, kBdThreads, 0, s>>>(bt->x, bt->y, R * H);
         bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, ld.ffn_norm, bt->xn, H, d.eps);
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wgu, tiled_rows(2 * d.FF), 0, 2 * d.FF, H, bt->xn, bt->gu, R, s, err);
+        rc = matmul_rows(qt, ld.wgu, tiled_rows(2 * d.FF), 2 * d.FF, H, bt->xn, bt->gu, R, s, err);
         if (rc) break;
         bd_swiglu_kernel<<<ew_blocks, kBdThreads, 0, s>>>(bt->gu, bt->act, d.FF, R);
-        rc = b2_tiled_matvec_batch_impl(qt, ld.wd, tiled_rows(H), 0, H, d.FF, bt->act, bt->y, R, s, err);
+        rc = matmul_rows(qt, ld.wd, tiled_rows(H), H, d.FF, bt->act, bt->y, R, s, err);
         if (rc) break;
         bd_add_kernel<<<add_blocks, kBdThreads, 0, s>>>(bt->x, bt->y, R * H);
     }
     if (rc) return rc;
-    bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, d.out_norm, bt->xn, H, d.eps);
-    rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn, bt->logits, R, s, err);
+    const int r_lm = all_logits ? 0 : R - 1, n_lm = all_logits ? R : 1;
+    bd_rmsnorm_kernel<<<n_lm, kBdThreads, 0, s>>>(bt->x + (size_t)r_lm * H, d.out_norm, bt->xn, H, d.eps);
+    rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn, bt->logits, n_lm, s, err);
     if (rc) return rc;
-    bd_argmax_kernel<<<R, kBdThreads, 0, s>>>(bt->logits, d.V, bt->d_next, d_rpos);
+    bd_argmax_kernel<<<n_lm, kBdThreads, 0, s>>>(bt->logits, d.V, bt->d_next, d_rpos + r_lm);
     return ok(cudaGetLastError(), err, "batched decode launch") ? B2_OK : B2_ERR_CUDA;
 }
 
@@ -375,32 +424,79 @@ int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, 
     }
     if (!device_current(m, err)) return B2_ERR_BAD_ARG;
     cudaStream_t s = m->stream;
-    int c = 0;
-    for (int p0 = 0; p0 < n; p0 += kBatchMax) {
-        c = std::min(kBatchMax, n - p0);
-        for (int i = 0; i < c; i++) {
-            bt->h_io[i] = prompt[p0 + i];
-            bt->h_io[kBatchMax + i] = p0 + i;
-        }
-        if (!ok(cudaMemcpyAsync(bt->d_tok, bt->h_io, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens") ||
-            !ok(cudaMemcpyAsync(bt->d_ppos, bt->h_io + kBatchMax, sizeof(int) * c, cudaMemcpyHostToDevice, s), err,
-                "positions"))
+    for (int p0 = 0; p0 < n; p0 += kPrefillChunk) {
+        const int c = std::min(kPrefillChunk, n - p0);
+        if (!ok(cudaMemcpyAsync(bt->d_tok, prompt + p0, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens"))
             return B2_ERR_CUDA;
-        const int rc = forward_rows(bt, c, bt->d_ppos, (size_t)slot * bt->max_seq * d.kvd, 0, p0 + c, err);
+        bd_iota_kernel<<<(c + 255) / 256, 256, 0, s>>>(bt->d_ppos, c, p0);
+        const int rc = forward_rows(bt, c, bt->d_ppos, (size_t)slot * bt->max_seq * d.kvd, 0, p0 + c, err, false);
         if (rc) return rc;
-        // the pinned staging is reused by the next chunk
-        if (!ok(cudaStreamSynchronize(s), err, "prefill")) return B2_ERR_CUDA;
+        // (prompt is pageable host memory: the copy above is complete when the call returns)
     }
     bt->pos[slot] = n;
     bt->h_io[0] = n;
     if (!ok(cudaMemcpyAsync(bt->d_pos + slot, bt->h_io, sizeof(int), cudaMemcpyHostToDevice, s), err, "position") ||
-        !ok(cudaMemcpyAsync(bt->h_io + 2 * kBatchMax, bt->d_next + (c - 1), sizeof(int), cudaMemcpyDeviceToHost, s),
-            err, "id") ||
+        !ok(cudaMemcpyAsync(bt->h_io + 2 * kBatchMax, bt->d_next, sizeof(int), cudaMemcpyDeviceToHost, s), err, "id") ||
         !ok(cudaStreamSynchronize(s), err, "prefill"))
         return B2_ERR_CUDA;
+    if (const int st = b2_gemm_status(s)) {
+        *err = "tensor-core GEMM: a bounded wait gave up";
+        return st;
+    }
     *next_out = bt->h_io[2 * kBatchMax];
     return B2_OK;
 }
+
+namespace b2 {
+
+// Prompts from this many tokens on take the tensor-core prefill.
+constexpr int kGemmPrefillMin = 16;
+
+bool prefill_gemm_ok(const b2_model* m, int n) {
+    const ModelDev& d = m->dev;
+    return n >= kGemmPrefillMin && d.tp == 1 && !d.kv_fp32 && (d.hd == 64 || d.hd == 128 || d.hd == 256) &&
+           d.nh / d.nkv <= 8 && d.H % 64 == 0 && d.qd % 64 == 0 && d.FF % 64 == 0;
+}
+
+void free_prefill_ws(b2_model* m) {
+    if (m->prefill_ws) b2_batch_free_impl(m->prefill_ws);
+    m->prefill_ws = nullptr;
+}
+
+// The prompt in chunks of up to kPrefillChunk tokens, each one pass over the
+// weights on the tensor cores, appending to and attending over the model's
+// own cache (token i of a chunk sees positions 0 .. its own); then the last
+// token's logits and argmax go where the decode kernel leaves them (the
+// model's logits buffer and token), so the next decode step and the forward
+// entry points read them as after a prefill through the decode kernel.
+int prefill_gemm(b2_model* m, const int32_t* tokens, int n, int pos0, std::string* err) {
+    const ModelDev& d = m->dev;
+    if (!m->prefill_ws) {
+        const int rc = batch_create(m, 1, true, &m->prefill_ws, err);
+        if (rc) return rc;
+    }
+    b2_batch* bt = m->prefill_ws;
+    cudaStream_t s = m->stream;
+    for (int p0 = 0; p0 < n; p0 += kPrefillChunk) {
+        const int c = std::min(kPrefillChunk, n - p0);
+        if (!ok(cudaMemcpyAsync(bt->d_tok, tokens + p0, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens"))
+            return B2_ERR_CUDA;
+        bd_iota_kernel<<<(c + 255) / 256, 256, 0, s>>>(bt->d_ppos, c, pos0 + p0);
+        const int rc = forward_rows(bt, c, bt->d_ppos, 0, 0, pos0 + p0 + c, err, false);
+        if (rc) return rc;
+    }
+    if (!ok(cudaMemcpyAsync(d.logits, bt->logits, sizeof(float) * d.V, cudaMemcpyDeviceToDevice, s), err, "logits") ||
+        !ok(cudaMemcpyAsync(d.token, bt->d_next, sizeof(int), cudaMemcpyDeviceToDevice, s), err, "token"))
+        return B2_ERR_CUDA;
+    if (!ok(cudaStreamSynchronize(s), err, "prefill")) return B2_ERR_CUDA;
+    if (const int st = b2_gemm_status(s)) {
+        *err = "tensor-core GEMM: a bounded wait gave up";
+        return st;
+    }
+    return B2_OK;
+}
+
+}  // namespace b2
 
 int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, std::string* err) {
     b2_model* m = bt->m;
@@ -420,7 +516,7 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
     if (!ok(cudaMemcpyAsync(bt->d_tok, bt->h_io, sizeof(int) * B, cudaMemcpyHostToDevice, s), err, "tokens"))
         return B2_ERR_CUDA;
     (void)d;
-    if (bt->exec && bt->exec_gen != b2_mvb_scratch_generation(s)) {  // the scratch moved since the capture
+    if (bt->exec && bt->exec_gen != scratch_generation(s)) {  // the scratch moved since the capture
         cudaGraphExecDestroy(bt->exec);
         bt->exec = nullptr;
     }
@@ -433,6 +529,10 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
     if (!ok(cudaMemcpyAsync(bt->h_io + B, bt->d_next, sizeof(int) * B, cudaMemcpyDeviceToHost, s), err, "ids") ||
         !ok(cudaStreamSynchronize(s), err, "batched decode"))
         return B2_ERR_CUDA;
+    if (const int st = b2_gemm_status(s)) {
+        *err = "tensor-core GEMM: a bounded wait gave up";
+        return st;
+    }
     if (bt->use_graph && !bt->exec) {
         // Capture the launches of a step for the next ones (capturing runs
         // nothing).  This step ran them eagerly, so the matvec scratch is
@@ -447,7 +547,7 @@ int b2_batch_step_impl(b2_batch* bt, const int32_t* tokens, int32_t* next_out, s
             const cudaError_t ce = cudaStreamEndCapture(s, &graph);
             if (crc == B2_OK && ce == cudaSuccess && graph &&
                 cudaGraphInstantiate(&bt->exec, graph, 0) == cudaSuccess) {
-                bt->exec_gen = b2_mvb_scratch_generation(s);
+                bt->exec_gen = scratch_generation(s);
             } else {
                 bt->exec = nullptr;
             }

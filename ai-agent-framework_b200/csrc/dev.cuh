@@ -109,6 +109,7 @@ struct TPlan {
     int nks, bpk;   // K-slices and blocks per slice
     int nt;         // tiles per chunk
     int nchunks;    // = ceil(n / nt) * nks
+    int kb0, kbn;   // the row blocks [kb0, kb0 + kbn) the plan covers (all of them but in a K-split phase)
 };
 
 // Plan of the tile range [u0, u0 + n) (see TPlan).
@@ -121,6 +122,8 @@ TPlan tile_plan_range(int u0, int n, int nb, int tbb, int slot_bytes, int warps)
     TPlan t;
     t.u0 = u0;
     t.n = n;
+    t.kb0 = 0;
+    t.kbn = nb;
     if (t.n <= 0) {
         t.n = 0; t.nks = 1; t.bpk = nb; t.nt = 1; t.nchunks = 0;
         return t;
@@ -186,6 +189,57 @@ TPlan own_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, in
     return tile_plan_range(u0, n, nb, tbb, slot_bytes, warps);
 }
 
+// The down phase split over K (single GPU, when the grid has at least two
+// CTAs per residual tile): tile t of the H / kTileRows down tiles goes to
+// CTAs first + 2t and first + 2t + 1 (first = grid - 2 * h_tiles, so the
+// residual-row owners at the end of the grid take part), each with one half
+// of the row's blocks; they publish partial sums, which the consumers of the
+// residual stream add.  kDownSplit is the number of halves.
+constexpr int kDownSplit = 2;
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+int dn_slice_of(int cta, int grid, int h_tiles) {
+    const int c = cta - (grid - kDownSplit * h_tiles);
+    return c < 0 ? -1 : c % kDownSplit;
+}
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+TPlan dn_split_plan(int h_tiles, int nb, int tbb, int cta, int grid, int slot_bytes, int warps) {
+    const int c = cta - (grid - kDownSplit * h_tiles);
+    if (c < 0) return tile_plan_range(0, 0, nb, tbb, slot_bytes, warps);
+    const int t = c / kDownSplit, s = c % kDownSplit;
+    const int kb0 = s * nb / kDownSplit, kb1 = (s + 1) * nb / kDownSplit;
+    TPlan p = tile_plan_range(t, 1, kb1 - kb0, tbb, slot_bytes, warps);
+    p.kb0 = kb0;
+    return p;
+}
+
+// Gate/up tiles of one CTA.  The CTAs that own residual rows (own_tiles of
+// the H / kTileRows Wo and down tiles) also stream those two matrices every
+// layer, so they take own_pct percent of the gate/up share of the others:
+// the bytes per layer come out close on every CTA, and the owners' ring
+// slots are free to prefetch their down tiles during the gate/up phase.
+// own_pct = 100 is the even split.
+inline
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+TPlan gu_plan(int tiles, int nb, int tbb, int cta, int grid, int slot_bytes, int warps, int h_tiles, int own_pct) {
+    if (h_tiles > grid || own_pct == 100) return tile_plan(tiles, nb, tbb, cta, grid, slot_bytes, warps);
+    const int first = grid - h_tiles;  // first owner CTA
+    const long long W = (long long)first * 100 + (long long)h_tiles * own_pct;
+    auto cum = [&](int c) {
+        return c <= first ? (long long)c * 100 : (long long)first * 100 + (long long)(c - first) * own_pct;
+    };
+    const int u0 = (int)(tiles * cum(cta) / W);
+    const int n = (int)(tiles * cum(cta + 1) / W) - u0;
+    return tile_plan_range(u0, n, nb, tbb, slot_bytes, warps);
+}
+
 // QA phase rows.  Fused form: q CTAs 0 .. nh*S - 1 (head h = cta / S, split
 // cta % S) each compute the hd / kTileRows q tiles of their head and keep
 // them; the kv CTAs nh*S .. grid - 1 share the k and v tiles evenly.
@@ -210,6 +264,15 @@ void qa_tiles(int nh, int hd, int qd, int kvd, int S, int cta, int grid, int* u0
         return;
     }
     const int kv0 = qd / kTileRows, nkv = 2 * kvd / kTileRows, J = grid - nq, j = cta - nq;
+    if (nkv <= J) {
+        // one tile each on the first CTAs after the q CTAs: the residual-row
+        // owners sit at the end of the grid and enter this phase last (they
+        // finish the previous down phase), while every q CTA's last split
+        // waits for these rows
+        *u0 = kv0 + (j < nkv ? j : 0);
+        *n = j < nkv ? 1 : 0;
+        return;
+    }
     *u0 = kv0 + (int)((long long)j * nkv / J);
     *n = kv0 + (int)((long long)(j + 1) * nkv / J) - *u0;
 }
@@ -272,6 +335,8 @@ struct ModelDev {
     uint2* ll_qkv;            // [qd + 2*kvd] q, k (after RoPE), v of the new token
     uint2* ll_part;           // [nh][kMaxSplits][hd + 2] attention split partials (o, m, l)
     uint2* ll_act;            // [FF]  SwiGLU output
+    uint2* ll_dnp;            // [2 (layer parity)][kDownSplit][H] down-phase partial sums (split mode)
+    int dn_split;             // 1: down rows on their residual owners; kDownSplit: split over K (dn_split_plan)
     float* logits;            // [V]
     unsigned long long* am_key;  // [1] argmax so far: order-preserving value bits << 32 | ~index (self-resetting)
     int* token;               // [1] last argmax
@@ -329,10 +394,11 @@ struct StepArgs {
 //                                 even phases first, then the odd ones)
 //   cbuf   [cfloats]              phase constants (norm gains, bias, RoPE)
 //   full, empty [nslots] mbarriers; red [64] floats; misc [32] ints
+//   dnp    [kDownSplit][16] LL    the down partials of an owner's rows (split mode)
 //   plan   [kPlanSlots] TPlan     this CTA's work plans (copied at launch)
 //   lay    [L] LayerDev           the layer table (copied at launch)
 struct SmemOffsets {
-    uint32_t xs, xq, xsc, xsm, xres, ybuf, cbuf, full, empty, red, misc, plan, lay, total;
+    uint32_t xs, xq, xsc, xsm, xres, ybuf, cbuf, full, empty, red, misc, dnp, plan, lay, total;
 };
 
 // xq holds the phase input as three int8 planes in the operand layout of
@@ -361,6 +427,8 @@ SmemOffsets smem_offsets(int nslots, int slot_bytes, int xs_floats, int ybuf_flo
     o.empty = p; p += 8u * (uint32_t)nslots;
     o.red = p;   p += 4u * 64u;
     o.misc = p;  p += 4u * 32u;
+    p = (p + 15u) & ~15u;
+    o.dnp = p;   p += 8u * kTileRows * kDownSplit;
     o.plan = p;  p += (uint32_t)(kPlanSlots * sizeof(TPlan));
     p = (p + 15u) & ~15u;
     o.lay = p;   p += (uint32_t)(nlayers * sizeof(LayerDev));
@@ -501,6 +569,11 @@ __device__ __forceinline__ uint4 ld4_sys(const uint4* p) {
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p)
                  : "memory");
+    return r;
+}
+__device__ __forceinline__ uint2 ll_load1(const uint2* p) {
+    uint2 r;
+    asm volatile("ld.relaxed.gpu.global.v2.b32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
     return r;
 }
 __device__ __forceinline__ uint4 ll_load2(const uint2* p) {

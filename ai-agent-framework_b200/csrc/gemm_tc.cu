@@ -1,0 +1,600 @@
+// Tensor-core GEMM over the resident quantised weights (Blackwell tcgen05).
+//
+// Y[t][r] = sum_k X[t][k] W[r][k] for many tokens t at once: the prefill of
+// a prompt (the forward of transformer.go:519-739 with seqLen > 1, the
+// batched form of the C++ sibling's Transformer::forward_batch,
+// Local-LLM/src/transformer.cpp:540-575, whose mat_mat_mul_tensor
+// Local-LLM/include/tensor.h:354-387 dequantises and multiplies) and the
+// batched decode steps.  W stays in the decode kernel's tiled Q8_0 / Q4_0
+// layout (dev.cuh); nothing is dequantised in HBM.
+//
+// One CTA computes a 128-row x BN-token tile of Y over its K range:
+//   warp 0      producer: TMA tensor loads (cp.async.bulk.tensor.2d, this
+//               GPU's own memory, no multicast) of each K stage's raw quant
+//               and scale blocks of the 128 weight rows and of the BN x 64
+//               fp16 activation tile (128-byte swizzle) into a ring of stages;
+//   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 (M 128,
+//               N BN, K 16) four times per stage, A and B from shared memory
+//               by descriptor, the fp32 accumulator in tensor memory (BN
+//               columns); tcgen05.commit frees each stage;
+//   warps 2..5  dequantisers: thread r decodes weight row r of the stage
+//               (f16 scale x int8 or nibble - 8, rounded once to fp16) into
+//               the 128-byte-swizzled K-major A tile the MMA reads; then
+//               the epilogue: tcgen05.ld of its accumulator row, times the
+//               token's activation scale, to Y (coalesced over rows).
+// Activations are converted once per call to fp16 with a power-of-two scale
+// per token (its largest magnitude maps into [2^14, 2^15)), so they keep 11
+// significant bits without overflow; products accumulate in fp32.  The
+// weight d * q is rounded to fp16 once (at most 2^-12 relative error per
+// weight).  Every wait is bounded (globaltimer) and reports B2_ERR_TIMEOUT
+// through the device error flag; a CTA that gave up stops issuing work,
+// waits (bounded) for the copies and products it issued and frees its
+// tensor memory before it exits.
+//
+// When the row tiles are fewer than the SMs, the K range is split over up to
+// kMaxKSplit CTAs per tile; their partial sums go to a scratch buffer and one
+// more kernel adds them in split order (results do not depend on timing).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "../../include/b2decode.h"
+#include "dev.cuh"
+
+namespace b2 {
+namespace {
+
+constexpr int kGemmThreads = 192;       // 6 warps: producer, MMA, 4 dequant / epilogue
+constexpr int kBM = 128;                // weight rows per CTA (MMA M)
+constexpr int kStageBlocks = 2;         // Q blocks (of 32) per K stage: 64 elements
+constexpr int kMaxKSplit = 8;
+constexpr uint64_t kGemmWaitNs = 2000000000ull;
+constexpr int kGemmSmemMax = 232448;
+
+template <int QT>
+struct QShape {
+    static constexpr int QB = QT == 8 ? 32 : 16;                       // quant bytes per row and block
+    static constexpr int kRawQ = kBM / kTileRows * kStageBlocks * kTileRows * QB;  // quants of a stage
+    static constexpr int kRawS = kBM / kTileRows * kStageBlocks * kTileRows * 2;   // scales of a stage
+};
+
+// Shared-memory plan of one CTA (byte offsets from a 1024-aligned base).
+template <int QT, int BN>
+struct GemmSmem {
+    static constexpr int kA = kBM * 128;  // fp16, 128 rows x 64 K, 128-byte swizzle
+    static constexpr int kB = BN * 128;   // fp16, BN rows x 64 K
+    // (a multiple of 1024, so every stage's A and B tiles stay 1024-aligned)
+    static constexpr int kStage = (kA + kB + QShape<QT>::kRawQ + QShape<QT>::kRawS + 1023) & ~1023;
+    static constexpr int kFixed = 2048;  // alignment slack, then barriers and the TMEM slot
+    static constexpr int kStages = (kGemmSmemMax - kFixed) / kStage > 8 ? 8 : (kGemmSmemMax - kFixed) / kStage;
+    static_assert(kStages >= 2, "a K stage must fit twice");
+    static constexpr int kTotal = kFixed + kStages * kStage;
+};
+
+struct GemmArgs {
+    int nst;            // K stages per CTA (kStageBlocks blocks each)
+    int kst_split;      // stages per split (the last split may take fewer)
+    int tiles_q;        // first 16-row Q tile of the matrix share (row0 / 16)
+    int rows;           // output rows (weight rows) of the share
+    int ntok;           // tokens (valid columns of X)
+    int ldy;            // row stride of Y (floats)
+    float* y;           // [ntok][ldy] (split 1) or partials [split][ntok][rows]
+    const float* tok_scale;  // [ntok_pad] activation scale per token
+    int* err;
+};
+
+__device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kGemmWaitNs) {
+            atomicCAS(err, 0, B2_ERR_TIMEOUT);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (sm_100 shared
+// memory descriptor: start >> 4 in bits 0-13, leading offset (unused with
+// this swizzle) 16-29, stride offset >> 4 in 32-45, version 1 in 46-47,
+// layout type 2 = 128-byte swizzle in 61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+           ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator (bits 4-5 = 1), A
+// and B fp16 (bits 7-9, 10-12 = 0), both K-major (bits 15, 16 = 0), N >> 3 in
+// bits 17-22, M >> 4 in bits 24-28.
+template <int BN>
+__device__ __forceinline__ uint32_t f16_idesc() {
+    return (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+        "[%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 4 signed bytes -> 2 half2 of the exact integers: (b ^ 0x80) in the low
+// byte of the fp16 0x6400 (1024) is 1024 + b + 128.
+__device__ __forceinline__ void s8x4_to_h2(uint32_t w, __half2& lo, __half2& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t a = __byte_perm(u, 0x64646464u, 0x5140), b = __byte_perm(u, 0x64646464u, 0x7362);
+    const __half2 off = __floats2half2_rn(1152.0f, 1152.0f);
+    lo = __hsub2(*reinterpret_cast<const __half2*>(&a), off);
+    hi = __hsub2(*reinterpret_cast<const __half2*>(&b), off);
+}
+// 4 nibbles (one per byte, 0..15) -> 2 half2 of nibble - 8.
+__device__ __forceinline__ void u4x4_to_h2(uint32_t w, __half2& lo, __half2& hi) {
+    const uint32_t a = __byte_perm(w, 0x64646464u, 0x5140), b = __byte_perm(w, 0x64646464u, 0x7362);
+    const __half2 off = __floats2half2_rn(1032.0f, 1032.0f);
+    lo = __hsub2(*reinterpret_cast<const __half2*>(&a), off);
+    hi = __hsub2(*reinterpret_cast<const __half2*>(&b), off);
+}
+
+// Row r (0..127) of a stage: its two Q blocks -> 64 fp16 (d * q) into the
+// swizzled A tile (16-byte chunk c of row r at chunk position c ^ (r & 7)).
+template <int QT>
+__device__ __forceinline__ void dequant_row(const uint8_t* rawq, const uint8_t* raws, uint8_t* a_tile, int r) {
+    constexpr int QB = QShape<QT>::QB;
+    const int t = r >> 4, rr = r & 15;
+    uint8_t* arow = a_tile + r * 128;
+#pragma unroll
+    for (int kb = 0; kb < kStageBlocks; kb++) {
+        // TMA box layout: [tile][block][16 rows][QB]; scales [tile][block][16] in (g, g + 8) order
+        const uint8_t* q = rawq + ((t * kStageBlocks + kb) * kTileRows + rr) * QB;
+        const uint16_t dbits =
+            *reinterpret_cast<const uint16_t*>(raws + ((t * kStageBlocks + kb) * kTileRows + 2 * (rr & 7) + (rr >> 3)) * 2);
+        const __half2 d2 = __halves2half2(__ushort_as_half(dbits), __ushort_as_half(dbits));
+        uint32_t w[8];
+        if (QT == 8) {
+            // rows with bit 2 set hold their two 16-byte halves swapped
+            const uint4 h0 = *reinterpret_cast<const uint4*>(q + ((rr & 4) ? 16 : 0));
+            const uint4 h1 = *reinterpret_cast<const uint4*>(q + ((rr & 4) ? 0 : 16));
+            w[0] = h0.x; w[1] = h0.y; w[2] = h0.z; w[3] = h0.w;
+            w[4] = h1.x; w[5] = h1.y; w[6] = h1.z; w[7] = h1.w;
+        } else {
+            // byte i: low nibble = element i, high nibble = element i + 16
+            const uint4 h = *reinterpret_cast<const uint4*>(q);
+            w[0] = h.x & 0x0F0F0F0Fu; w[1] = h.y & 0x0F0F0F0Fu; w[2] = h.z & 0x0F0F0F0Fu; w[3] = h.w & 0x0F0F0F0Fu;
+            w[4] = (h.x >> 4) & 0x0F0F0F0Fu; w[5] = (h.y >> 4) & 0x0F0F0F0Fu;
+            w[6] = (h.z >> 4) & 0x0F0F0F0Fu; w[7] = (h.w >> 4) & 0x0F0F0F0Fu;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; c++) {  // chunk c of this block: elements 8c .. 8c + 7
+            __half2 h[4];
+            if (QT == 8) {
+                s8x4_to_h2(w[2 * c], h[0], h[1]);
+                s8x4_to_h2(w[2 * c + 1], h[2], h[3]);
+            } else {
+                u4x4_to_h2(w[2 * c], h[0], h[1]);
+                u4x4_to_h2(w[2 * c + 1], h[2], h[3]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) h[i] = __hmul2(h[i], d2);
+            const int chunk = kb * 4 + c;
+            *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
+        }
+    }
+}
+
+template <int QT, int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_s,
+                 const __grid_constant__ CUtensorMap map_x, const GemmArgs a) {
+    using SM = GemmSmem<QT, BN>;
+    constexpr int NS = SM::kStages;
+    extern __shared__ __align__(1024) uint8_t gsm_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stages = base + 1024;  // [NS][A | B | raw q | raw s], A and B 1024-aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(base);
+    uint64_t* adone = full + NS;
+    uint64_t* empty = adone + NS;
+    uint64_t* accum = empty + NS;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = blockIdx.x, nt = blockIdx.y, ks = blockIdx.z;
+    const int st0 = ks * a.kst_split;
+    const int nst = max(0, min(a.kst_split, a.nst - st0));
+    constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&adone[s], 4);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- producer
+        if (lane == 0) {
+            const uint32_t bytes = QShape<QT>::kRawQ + QShape<QT>::kRawS + SM::kB;
+            int issued = 0;
+            for (int it = 0; it < nst; it++) {
+                const int s = it % NS;
+                if (it >= NS && !gemm_wait(&empty[s], ((it / NS) - 1) & 1, a.err, abort_flag)) break;
+                uint8_t* st = stages + (size_t)s * SM::kStage;
+                const int kb = (st0 + it) * kStageBlocks;  // first Q block of the stage
+                mbar_arrive_expect_tx(&full[s], bytes);
+                tma_load_2d(st + SM::kA + SM::kB, &map_q, kb * (kTileRows * QShape<QT>::QB / 8),
+                            a.tiles_q + mt * (kBM / kTileRows), &full[s]);
+                tma_load_2d(st + SM::kA + SM::kB + QShape<QT>::kRawQ, &map_s, kb * (kTileRows * 2 / 8),
+                            a.tiles_q + mt * (kBM / kTileRows), &full[s]);
+                tma_load_2d(st + SM::kA, &map_x, kb * 32, nt * BN, &full[s]);
+                issued = it + 1;
+            }
+            // every copy issued has landed before the CTA may exit
+            for (int it = max(0, issued - NS); it < issued; it++)
+                if (!gemm_wait(&full[it % NS], (it / NS) & 1, a.err, abort_flag)) {
+                    // (already aborted: give the copies a bounded time of their own)
+                    const uint64_t t0 = global_ns();
+                    while (!mbar_try_wait(&full[it % NS], (it / NS) & 1) && global_ns() - t0 < kGemmWaitNs) {
+                    }
+                }
+        }
+    } else if (warp == 1) {
+        // --------------------------------------------------------------- MMA
+        if (lane == 0) {
+            const uint32_t idesc = f16_idesc<BN>();
+            int done = 0;
+            for (int it = 0; it < nst; it++) {
+                const int s = it % NS;
+                if (!gemm_wait(&adone[s], (it / NS) & 1, a.err, abort_flag)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                uint8_t* st = stages + (size_t)s * SM::kStage;
+                const uint32_t sa = smem_u32(st), sb = smem_u32(st + SM::kA);
+#pragma unroll
+                for (int k = 0; k < 4; k++)  // K = 16 per MMA: 32 bytes along the swizzled row
+                    mma_f16(tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc, (it | k) != 0);
+                mma_commit(&empty[s]);
+                done = it + 1;
+            }
+            mma_commit(accum);  // after every MMA issued above
+            (void)done;
+        }
+    } else {
+        // ---------------------------------------------- dequantisers, epilogue
+        const int r = threadIdx.x - 64;  // weight row of the tile, 0..127
+        for (int it = 0; it < nst; it++) {
+            const int s = it % NS;
+            bool ok = gemm_wait(&full[s], (it / NS) & 1, a.err, abort_flag);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            uint8_t* st = stages + (size_t)s * SM::kStage;
+            dequant_row<QT>(st + SM::kA + SM::kB, st + SM::kA + SM::kB + QShape<QT>::kRawQ, st, r);
+            fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&adone[s]);
+        }
+        // epilogue: accumulator row r (TMEM lane r; warp w reads lanes 32 (w % 4) ..)
+        const int q = warp & 3;
+        const int row = 32 * q + lane;
+        bool ok = gemm_wait(accum, 0, a.err, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok && nst > 0) {
+            const int grow = mt * kBM + row;  // output row within the share
+            float* yb = a.y + (size_t)ks * ((size_t)a.ntok * a.rows);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int tok = nt * BN + c0 + j;
+                    if (grow < a.rows && tok < a.ntok)
+                        yb[(size_t)tok * a.ldy + grow] = __uint_as_float(v[j]) * a.tok_scale[tok];
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        // the MMAs this CTA issued are complete (accum barrier, bounded) before
+        // its tensor memory goes back
+        if (lane == 0) {
+            const uint64_t t0 = global_ns();
+            while (!mbar_try_wait(accum, 0) && global_ns() - t0 < kGemmWaitNs) {
+            }
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// X fp32 [ntok][cols] -> fp16 [ntok_pad][cols] scaled by 2^e per token (the
+// largest magnitude into [2^14, 2^15)), scale[t] = 2^-e; rows past ntok zero.
+__global__ void to_f16_scaled_kernel(const float* __restrict__ x, int ntok, int cols, __half* __restrict__ xh,
+                                     float* __restrict__ scale) {
+    __shared__ float red[8];
+    const int t = blockIdx.x;
+    float mx = 0.0f;
+    if (t < ntok)
+        for (int j = threadIdx.x; j < cols; j += blockDim.x) mx = fmaxf(mx, fabsf(x[(size_t)t * cols + j]));
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); i++) mx = fmaxf(mx, red[i]);
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+        int ex;
+        frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+        e = 15 - ex;
+    }
+    const float up = ldexpf(1.0f, e);
+    if (threadIdx.x == 0) scale[t] = ldexpf(1.0f, -e);
+    for (int j = threadIdx.x; j < cols; j += blockDim.x)
+        xh[(size_t)t * cols + j] = __float2half_rn(t < ntok ? x[(size_t)t * cols + j] * up : 0.0f);
+}
+
+// Split-K partials [ks][ntok][rows] -> y[tok][row] (summed in split order).
+__global__ void splitk_sum_kernel(const float* __restrict__ part, int ks, int ntok, int rows, int ldy,
+                                  float* __restrict__ y) {
+    const size_t n = (size_t)ntok * rows;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v = part[i];
+        for (int s = 1; s < ks; s++) v += part[(size_t)s * n + i];
+        const size_t tok = i / rows, row = i - tok * rows;
+        y[tok * ldy + row] = v;
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn(std::string* err) {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) *err = "cuTensorMapEncodeTiled is not available from the driver";
+    return fn;
+}
+
+bool make_map_2d(EncodeTiledFn enc, CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Per (device, stream) scratch: fp16 activations, token scales, split
+// partials, the error flag.  Calls on one stream run in order.
+struct GemmScratch {
+    uint8_t* buf = nullptr;
+    size_t bytes = 0;
+    int* err = nullptr;
+    int sms = 0;
+    unsigned long long gen = 0;
+};
+std::mutex g_gemm_mu;
+std::map<std::pair<int, cudaStream_t>, GemmScratch> g_gemm;
+
+size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
+
+template <int QT, int BN>
+int launch_qgemm(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mx, const GemmArgs& a, dim3 grid,
+                 cudaStream_t s, std::string* err) {
+    static bool attr = false;
+    if (!attr) {
+        if (cudaFuncSetAttribute(qgemm_kernel<QT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 GemmSmem<QT, BN>::kTotal) != cudaSuccess) {
+            *err = "cudaFuncSetAttribute (tensor-core GEMM) failed";
+            return B2_ERR_CUDA;
+        }
+        attr = true;
+    }
+    qgemm_kernel<QT, BN><<<grid, kGemmThreads, GemmSmem<QT, BN>::kTotal, s>>>(mq, ms, mx, a);
+    return B2_OK;
+}
+
+template <int QT>
+int launch_bn(int bn, const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mx, const GemmArgs& a,
+              dim3 grid, cudaStream_t s, std::string* err) {
+    switch (bn) {
+        case 16: return launch_qgemm<QT, 16>(mq, ms, mx, a, grid, s, err);
+        case 32: return launch_qgemm<QT, 32>(mq, ms, mx, a, grid, s, err);
+        case 64: return launch_qgemm<QT, 64>(mq, ms, mx, a, grid, s, err);
+        default: return launch_qgemm<QT, 128>(mq, ms, mx, a, grid, s, err);
+    }
+}
+
+}  // namespace
+}  // namespace b2
+
+using namespace b2;
+
+// Y = W X over rows [row0, row0 + rows) of a tiled Q8_0 / Q4_0 matrix
+// (base: the tiled matrix, rp its padded rows, cols = K) for ntok tokens:
+// x [ntok][cols] fp32, y [ntok][rows] fp32, device memory, stream s.
+int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
+                       float* y, int ntok, cudaStream_t s, std::string* err) {
+    if (qtype != 8 && qtype != 2) {
+        *err = "tensor-core GEMM takes Q8_0 or Q4_0 weights";
+        return B2_ERR_UNSUPPORTED_TYPE;
+    }
+    if (ntok < 1 || rows < 1 || cols < 64 || cols % 64 || row0 % kTileRows || row0 + rows > rp) {
+        *err = "tensor-core GEMM: cols must be a multiple of 64 and rows inside the matrix";
+        return B2_ERR_BAD_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 3) {
+        *err = "x and y must be 4-byte aligned";
+        return B2_ERR_BAD_ARG;
+    }
+    std::string e2;
+    EncodeTiledFn enc = encode_fn(&e2);
+    if (!enc) {
+        *err = e2;
+        return B2_ERR_CUDA;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        *err = "no CUDA device";
+        return B2_ERR_CUDA;
+    }
+    const int bn = ntok <= 16 ? 16 : ntok <= 32 ? 32 : ntok <= 64 ? 64 : 128;
+    const int n_tiles = (ntok + bn - 1) / bn;
+    const int ntok_pad = n_tiles * bn;
+    const int nb = cols / 32;
+    const int nst = nb / kStageBlocks;
+    const int m_tiles = (rows + kBM - 1) / kBM;
+    std::lock_guard<std::mutex> lk(g_gemm_mu);
+    GemmScratch* sc = &g_gemm[{dev, s}];
+    if (!sc->sms && cudaDeviceGetAttribute(&sc->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        *err = "cudaDeviceGetAttribute failed";
+        return B2_ERR_CUDA;
+    }
+    // split K until the tiles cover the SMs (at least 4 stages per split)
+    int ksplit = 1;
+    while (ksplit < kMaxKSplit && (long long)m_tiles * n_tiles * ksplit < sc->sms && nst / (2 * ksplit) >= 4) ksplit *= 2;
+    const int kst = (nst + ksplit - 1) / ksplit;
+    ksplit = (nst + kst - 1) / kst;
+    const size_t b_x = al256((size_t)ntok_pad * cols * 2), b_sc = al256((size_t)ntok_pad * 4);
+    const size_t b_part = ksplit > 1 ? al256((size_t)ksplit * ntok * rows * 4) : 0;
+    const size_t need = 256 + b_x + b_sc + b_part;
+    if (sc->bytes < need) {
+        if (sc->buf) cudaFree(sc->buf);
+        sc->buf = nullptr;
+        sc->bytes = 0;
+        if (cudaMalloc(&sc->buf, need) != cudaSuccess) {
+            *err = "tensor-core GEMM scratch allocation failed";
+            return B2_ERR_OOM;
+        }
+        cudaMemsetAsync(sc->buf, 0, 256, s);
+        sc->bytes = need;
+        sc->err = reinterpret_cast<int*>(sc->buf);
+        sc->gen++;
+    }
+    __half* xh = reinterpret_cast<__half*>(sc->buf + 256);
+    float* tsc = reinterpret_cast<float*>(sc->buf + 256 + b_x);
+    float* part = ksplit > 1 ? reinterpret_cast<float*>(sc->buf + 256 + b_x + b_sc) : nullptr;
+
+    const bool q8 = qtype == 8;
+    const int QB = q8 ? 32 : 16;
+    const int64_t tiles_total = rp / kTileRows;
+    const uint8_t* wq = static_cast<const uint8_t*>(base);
+    const uint8_t* ws = wq + (size_t)rp * nb * QB;
+    CUtensorMap mq, ms, mx;
+    if (!make_map_2d(enc, &mq, CU_TENSOR_MAP_DATA_TYPE_UINT64, wq, (uint64_t)nb * kTileRows * QB / 8, tiles_total,
+                     (uint64_t)nb * kTileRows * QB, kStageBlocks * kTileRows * QB / 8, kBM / kTileRows,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(enc, &ms, CU_TENSOR_MAP_DATA_TYPE_UINT64, ws, (uint64_t)nb * kTileRows * 2 / 8, tiles_total,
+                     (uint64_t)nb * kTileRows * 2, kStageBlocks * kTileRows * 2 / 8, kBM / kTileRows,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(enc, &mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, (uint64_t)cols, (uint64_t)ntok_pad,
+                     (uint64_t)cols * 2, 64, (uint32_t)bn, CU_TENSOR_MAP_SWIZZLE_128B)) {
+        *err = "tensor map encoding failed (alignment)";
+        return B2_ERR_BAD_ARG;
+    }
+    to_f16_scaled_kernel<<<ntok_pad, 256, 0, s>>>(x, ntok, cols, xh, tsc);
+    GemmArgs a{};
+    a.nst = nst;
+    a.kst_split = kst;
+    a.tiles_q = (int)(row0 / kTileRows);
+    a.rows = rows;
+    a.ntok = ntok;
+    a.ldy = rows;
+    a.y = ksplit > 1 ? part : y;
+    a.tok_scale = tsc;
+    a.err = sc->err;
+    const dim3 grid(m_tiles, n_tiles, ksplit);
+    int rc = q8 ? launch_bn<8>(bn, mq, ms, mx, a, grid, s, err) : launch_bn<2>(bn, mq, ms, mx, a, grid, s, err);
+    if (rc) return rc;
+    if (ksplit > 1) {
+        const int blocks = std::min(sc->sms * 4, (int)(((size_t)ntok * rows + 255) / 256));
+        splitk_sum_kernel<<<std::max(blocks, 1), 256, 0, s>>>(part, ksplit, ntok, rows, rows, y);
+    }
+    cudaError_t ce = cudaGetLastError();
+    if (ce != cudaSuccess) {
+        *err = std::string("tensor-core GEMM launch: ") + cudaGetErrorString(ce);
+        return B2_ERR_CUDA;
+    }
+    return B2_OK;
+}
+
+// Device error flag of the GEMM scratch of stream s (0 if none); clears it.
+int b2_gemm_status(cudaStream_t s) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return B2_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_gemm_mu);
+    auto it = g_gemm.find({dev, s});
+    if (it == g_gemm.end() || !it->second.err) return 0;
+    int v = 0;
+    cudaMemcpyAsync(&v, it->second.err, sizeof(int), cudaMemcpyDeviceToHost, s);
+    cudaStreamSynchronize(s);
+    if (v) cudaMemsetAsync(it->second.err, 0, sizeof(int), s);
+    return v;
+}
+
+// Generation of the GEMM scratch of stream s (a CUDA graph that captured a
+// GEMM on s stays valid while it is unchanged).
+unsigned long long b2_gemm_scratch_generation(cudaStream_t s) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lk(g_gemm_mu);
+    const auto it = g_gemm.find({dev, s});
+    return it == g_gemm.end() ? 0 : it->second.gen;
+}

@@ -197,6 +197,30 @@ int check_device_status(b2_model* m, std::string* err) {
 // the new one: one K/V tile per split while the merge buffer and the grid
 // allow it (more q CTAs = a shorter critical path); beyond that a split walks
 // several tiles.  The cap keeps CTAs free for the k / v rows.
+// The slices rank `rank` of a tp-way model keeps (b2_tp_share_of): heads
+// evenly, the FFN by 32-element blocks (the first ranks take the smaller
+// shares when the blocks do not divide), the vocabulary by rows.
+int tp_share(int H, int nh, int nkv, int FF, int V, int tp, int rank, b2_tp_share* s) {
+    if (tp < 1 || rank < 0 || rank >= tp || nh % tp || nkv % tp || H % nh || FF % 32) return B2_ERR_BAD_ARG;
+    const int hd = H / nh, nhl = nh / tp, nkvl = nkv / tp;
+    const int nbf = FF / 32;
+    const int fb0 = (int)((int64_t)rank * nbf / tp), fb1 = (int)((int64_t)(rank + 1) * nbf / tp);
+    const int v0 = (int)((int64_t)rank * V / tp), v1 = (int)((int64_t)(rank + 1) * V / tp);
+    if (fb1 == fb0 || v1 == v0) return B2_ERR_BAD_ARG;
+    s->q_row0 = rank * nhl * hd;
+    s->q_rows = nhl * hd;
+    s->kv_row0 = rank * nkvl * hd;
+    s->kv_rows = nkvl * hd;
+    s->ffn_row0 = 32 * fb0;
+    s->ffn_rows = 32 * (fb1 - fb0);
+    s->vocab_row0 = v0;
+    s->vocab_rows = v1 - v0;
+    return B2_OK;
+}
+
+// Gate/up share of a residual-row owner CTA, in percent of the others' (gu_plan).
+constexpr int kGuOwnerPct = 100;
+
 static int splits_for(const b2_model* m, int cached) {
     int s = (cached + m->dev.attn_tile - 1) / m->dev.attn_tile;
     int cap = std::max(1, std::min(m->max_splits, (m->grid - 1) / std::max(1, m->dev.nh)));
@@ -209,6 +233,13 @@ int run_tokens(b2_model* m, const int32_t* host_tokens, int n, std::string* err)
         *err = "context length exceeded: " + std::to_string(m->cache_len + n) + " > " +
                std::to_string(m->cfg.max_seq_len);
         return B2_ERR_CONTEXT;
+    }
+    if (prefill_gemm_ok(m, n)) {
+        // a prompt: one weight pass per chunk on the tensor cores
+        const int rc = prefill_gemm(m, host_tokens, n, m->cache_len, err);
+        if (rc) return rc;
+        m->cache_len += n;
+        return B2_OK;
     }
     if (m->pin_pending) cudaEventSynchronize(m->ev_pin);  // h_pinned may still feed an earlier copy
     memcpy(m->h_pinned, host_tokens, sizeof(int32_t) * n);
@@ -423,11 +454,12 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // whole model when tp == 1).
     if (nh % tp || nkv % tp)
         return bail(B2_ERR_UNSUPPORTED_TYPE, "tensor parallelism needs the heads and KV heads divisible by the degree");
-    const int nhl = nh / tp, nkvl = nkv / tp, qdl = nhl * hd, kvdl = nkvl * hd;
-    const int fb0 = (int)((int64_t)rank * (FF / 32) / tp), fb1 = (int)((int64_t)(rank + 1) * (FF / 32) / tp);
-    const int FFl = 32 * (fb1 - fb0), ff0 = 32 * fb0;
-    const int v0 = (int)((int64_t)rank * V / tp), Vl = (int)((int64_t)(rank + 1) * V / tp) - v0;
-    if (FFl == 0 || Vl == 0) return bail(B2_ERR_UNSUPPORTED_TYPE, "tensor-parallel degree too large for this model");
+    b2_tp_share sh{};
+    if (tp_share(H, nh, nkv, FF, V, tp, rank, &sh) != B2_OK)
+        return bail(B2_ERR_UNSUPPORTED_TYPE, "tensor-parallel degree too large for this model");
+    const int nhl = nh / tp, nkvl = nkv / tp, qdl = sh.q_rows, kvdl = sh.kv_rows;
+    const int FFl = sh.ffn_rows, ff0 = sh.ffn_row0, fb0 = ff0 / 32;
+    const int v0 = sh.vocab_row0, Vl = sh.vocab_rows;
 
     // ---------------------------------------------------------- arena plan
     const size_t bpb = qt == GGML_Q8_0 ? 34 : 18;
@@ -504,6 +536,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const size_t off_llqkv = take((size_t)(qdl + 2 * kvdl) * 8);
     const size_t off_llpart = take((size_t)nhl * kMaxSplits * (hd + 2) * 8);
     const size_t off_llact = take((size_t)FFl * 8);
+    const size_t off_lldnp = take((size_t)2 * kDownSplit * H * 8);
     const size_t off_logits = take((size_t)Vl * 4);
     const size_t off_amkey = take(8);
     const size_t off_tok = take(4);
@@ -687,6 +720,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.ll_qkv = reinterpret_cast<uint2*>(A + off_llqkv);
     d.ll_part = reinterpret_cast<uint2*>(A + off_llpart);
     d.ll_act = reinterpret_cast<uint2*>(A + off_llact);
+    d.ll_dnp = reinterpret_cast<uint2*>(A + off_lldnp);
     d.logits = reinterpret_cast<float*>(A + off_logits);
     d.am_key = reinterpret_cast<unsigned long long*>(A + off_amkey);
     d.token = reinterpret_cast<int*>(A + off_tok);
@@ -770,8 +804,26 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     // even phases (QA, gate/up, LM head) and odd phases (Wo, down) alternate
     // between two buffers, so the next phase's dots may start before this
     // phase's epilogue ends
-    const int even_layers = std::max(qa_need, ybuf_need(2 * FFl, H / 32, false));
-    const int ybuf_odd = (std::max(ybuf_need(H, qdl / 32, true), ybuf_need(H, FFl / 32, true)) + 31) & ~31;
+    int gu_need = 0;
+    for (int cta = 0; cta < m->grid; cta++) {
+        const TPlan pl = gu_plan(2 * FFl / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps, H / kTileRows,
+                                 kGuOwnerPct);
+        gu_need = std::max(gu_need, pl.nks * kTileRows * pl.n);
+    }
+    const int even_layers = std::max(qa_need, gu_need);
+    // the down phase split over K on one GPU when the grid has two CTAs per
+    // residual tile and the QA / LM gathers can poll the partials with one
+    // thread per quarter-block (dn_split_plan)
+    const int h_tiles = H / kTileRows;
+    const int dn_split = (tp == 1 && kDownSplit * h_tiles <= m->grid && (FFl / 32) % kDownSplit == 0 &&
+                          4 * (H / 32) <= kConsumerWarps * 32) ? kDownSplit : 1;
+    int dn_need = 0;
+    for (int cta = 0; cta < m->grid; cta++) {
+        const TPlan pl = dn_split > 1 ? dn_split_plan(h_tiles, FFl / 32, tbb1, cta, m->grid, slot, kConsumerWarps)
+                                      : own_plan(h_tiles, FFl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+        dn_need = std::max(dn_need, pl.nks * kTileRows * pl.n);
+    }
+    const int ybuf_odd = (std::max(ybuf_need(H, qdl / 32, true), dn_need) + 31) & ~31;
     const int cfloats = cb_floats(hd);
     const int xs = (base_xs + 31) & ~31, max_splits = split_cap;
     auto ring_slots = [&](int ybuf_total) {
@@ -804,12 +856,15 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         return bail(B2_ERR_UNSUPPORTED_TYPE, "attention projection too large for one GPU");
     // every CTA's work plans (plan_slot order), so the kernel needs no divisions
     {
-        std::vector<TPlan> plans((size_t)m->grid * kPlanSlots, TPlan{0, 0, 1, 1, 1, 0});
+        std::vector<TPlan> plans((size_t)m->grid * kPlanSlots, TPlan{0, 0, 1, 1, 1, 0, 0, 0});
         for (int cta = 0; cta < m->grid; cta++) {
             TPlan* pc = plans.data() + (size_t)cta * kPlanSlots;
             pc[plan_slot(PH_WO, 1)] = own_plan(H / kTileRows, qdl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
-            pc[plan_slot(PH_GATEUP, 1)] = tile_plan(2 * FFl / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
-            pc[plan_slot(PH_DOWN, 1)] = own_plan(H / kTileRows, FFl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
+            pc[plan_slot(PH_GATEUP, 1)] = gu_plan(2 * FFl / kTileRows, H / 32, tbb1, cta, m->grid, slot, kConsumerWarps,
+                                                  H / kTileRows, kGuOwnerPct);
+            pc[plan_slot(PH_DOWN, 1)] = dn_split > 1
+                ? dn_split_plan(h_tiles, FFl / 32, tbb1, cta, m->grid, slot, kConsumerWarps)
+                : own_plan(h_tiles, FFl / 32, tbb1, cta, m->grid, slot, kConsumerWarps);
             for (int sub = 0; sub < n_lm; sub++) pc[plan_slot(PH_LMHEAD, sub)] = lm_plan(cta, sub, n_lm);
             for (int S = 1; S <= kMaxSplits && nhl * S < m->grid; S++) {
                 int u0 = 0, n = 0;
@@ -827,6 +882,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     d.cfloats = cfloats;
     d.attn_tile = tile;
     d.qa_dist = qa_dist;
+    d.dn_split = dn_split;
     d.slot_bytes = slot;
     d.nslots = ns;
     m->max_splits = max_splits;
@@ -850,6 +906,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
 void b2_free_impl(b2_model* m) {
     if (!m) return;
     if (m->stream) cudaStreamSynchronize(m->stream);
+    b2::free_prefill_ws(m);
     for (int p = 0; p < kMaxTp; p++)
         if (m->xch_peer[p] && m->xch_peer[p] != m->xch) cudaIpcCloseMemHandle(m->xch_peer[p]);
     if (m->xch) cudaFree(m->xch);

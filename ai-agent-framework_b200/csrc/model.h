@@ -41,6 +41,9 @@ struct StreamState {
 // the load's device allocation that brings it from 1 to 0 fails.
 extern std::atomic<int> g_fail_left;
 
+// The slices a tensor-parallel rank keeps (b2_tp_share_of; the loader's own).
+int tp_share(int H, int nh, int nkv, int FF, int V, int tp, int rank, b2_tp_share* s);
+
 }  // namespace b2
 
 struct b2_model {
@@ -74,11 +77,21 @@ struct b2_model {
     size_t xch_bytes = 0;
     void* xch_peer[b2::kMaxTp] = {};
     bool tp_connected = false;
+    // activations of the tensor-core prompt prefill (a one-row batch over this
+    // model's own KV cache), made on the first long prompt
+    b2_batch* prefill_ws = nullptr;
 };
 
 namespace b2 {
 
 size_t decode_smem_bytes(const ModelDev& m);
+// Prompt prefill on the tensor-core GEMM path (decode_batch.cu): tokens at
+// positions pos0 .. pos0 + n - 1 of the model's cache, the last token's
+// logits and argmax left where the decode kernel leaves them.  prefill_gemm_ok
+// says whether the model can take it (one GPU, fp16 cache, supported shapes).
+bool prefill_gemm_ok(const b2_model* m, int n);
+int prefill_gemm(b2_model* m, const int32_t* tokens, int n, int pos0, std::string* err);
+void free_prefill_ws(b2_model* m);
 int launch_decode(const ModelDev& m, const StepArgs& a, int grid, cudaStream_t stream, std::string* err);
 
 // Kernel-level entry points (matvec.cu / attention.cu / model.cu).

@@ -177,8 +177,9 @@ int b2_matvec(int32_t qtype, const void* w, const float* x, float* y, int32_t ro
  * fp32, w GGUF block rows (16-byte aligned); all DEVICE pointers.
  * 1 <= nvec <= 16 (vectors 8..15 share the pass over w with 0..7); cols a
  * multiple of 256.  qtype 8 = Q8_0, 2 = Q4_0.  Uses a
- * per-device scratch buffer (grown with cudaMalloc when a call needs more),
- * so calls on different streams must not overlap. */
+ * scratch buffer per (device, stream), grown with cudaMalloc when a call
+ * needs more; calls on one stream run in order, calls on different streams
+ * use different buffers. */
 int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int32_t rows, int32_t cols,
                     int32_t nvec, void* stream);
 /* The same batched dots (transformer.go:810-892 for nvec vectors) over a
@@ -188,8 +189,20 @@ int b2_matvec_batch(int32_t qtype, const void* w, const float* x, float* y, int3
  * them).  x [nvec][cols], y [nvec][rows] fp32 DEVICE pointers, 1 <= nvec <=
  * 16; the model's device must be current.  stream NULL = the model's own
  * stream.  The gate and up matrices are stored interleaved and are rejected.
- * Shares the per-device scratch of b2_matvec_batch. */
+ * Shares the per-(device, stream) scratch of b2_matvec_batch. */
 int b2_model_matvec(const b2_model* m, const char* name, const float* x, float* y, int32_t nvec, void* stream);
+/* The same product for any number of tokens on the tensor cores (tcgen05,
+ * TMA-staged tiles): Y = W X for the tensor `name`, x [ntok][cols], y
+ * [ntok][rows] fp32 DEVICE pointers, ntok >= 1, cols a multiple of 64.  The
+ * weights are decoded to fp16 in shared memory (d * q rounded once) and the
+ * activations converted to fp16 with a power-of-two scale per token; products
+ * accumulate in fp32.  This is the dense contraction of a prompt's prefill:
+ * the batched counterpart of the C++ sibling engine's
+ * Local-LLM/include/tensor.h:354-387 mat_mat_mul_tensor (Transformer::
+ * forward_batch, Local-LLM/src/transformer.cpp:540-575).  Asynchronous on
+ * `stream` (NULL = the model's stream), with a per-(device, stream) scratch
+ * grown by cudaMalloc when a call needs more. */
+int b2_model_gemm(const b2_model* m, const char* name, const float* x, float* y, int32_t ntok, void* stream);
 
 /* transformer.go:663-685 attention of one query token per sequence over an
  * fp16 KV cache, split over the context with a log-sum-exp merge.
@@ -221,13 +234,15 @@ int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_
  * at its own position, so every weight byte is read once per step for all of
  * them: the forward of transformer.go:519-739 and argmax 1038-1046 for B
  * sequences at a time.  b2_batch_prefill runs a slot's prompt into the slot
- * in chunks of up to 16 tokens, each chunk one pass over the weights (the
- * model's own single-sequence cache is not touched); next_out is the argmax
- * after the prompt.  b2_batch_step
+ * (the model's own single-sequence cache is not touched); next_out is the
+ * argmax after the prompt.  b2_batch_step
  * feeds tokens[B] (one per slot, every slot) and writes the B argmax ids;
- * b2_batch_logits copies the logits of the last forward of the batch: the B
- * rows of the last b2_batch_step, or, after a b2_batch_prefill, the rows of
- * its last prompt chunk (row i = chunk token i), [B][vocab_size].  Needs a
+ * b2_batch_logits copies the logits of the last forward of the batch,
+ * [B][vocab_size]: the B rows of the last b2_batch_step, or, after a
+ * b2_batch_prefill, the prompt's last token in row 0.  A prompt runs in
+ * chunks of up to 128 of its tokens, each one pass over the weights on the
+ * tensor cores (b2_model_gemm's product) with the chunk's attention over the
+ * slot's cache.  Needs a
  * single-GPU model with the fp16 cache; the model's device must be current.
  * Every batch of a model runs on the model's stream and shares its scratch,
  * so calls on the batches of one model, like calls on the model itself, must
@@ -264,6 +279,23 @@ int b2_batch_use_graph(b2_batch* b, int32_t on);
  * vocab_local); sampling other than greedy is not available. */
 int b2_tp_handle(const b2_model* m, void* handle_out);
 int b2_tp_connect(b2_model* m, const void* handles);
+
+/* The slices of the GGUF tensors that rank `rank` of a tp-way tensor-
+ * parallel model keeps, as b2_load computes them (host arithmetic, no GPU):
+ * query heads and KV heads evenly (rows of attn_q / attn_k / attn_v and
+ * their biases, input columns of attn_output), the FFN at 32-element block
+ * granularity (rows of ffn_gate / ffn_up, input columns of ffn_down; uneven
+ * shares allowed), the lm_head by vocab rows.  Fails with B2_ERR_BAD_ARG
+ * when the heads do not divide by tp or a share would be empty.  No
+ * reference counterpart (the Go engine runs on CPU cores). */
+typedef struct {
+    int32_t q_row0, q_rows;          /* attn_q rows; attn_output input columns */
+    int32_t kv_row0, kv_rows;        /* attn_k / attn_v rows */
+    int32_t ffn_row0, ffn_rows;      /* ffn_gate / ffn_up rows; ffn_down input columns */
+    int32_t vocab_row0, vocab_rows;  /* lm_head (output or token_embd) rows */
+} b2_tp_share;
+int b2_tp_share_of(int32_t hidden, int32_t heads, int32_t kv_heads, int32_t ffn, int32_t vocab, int32_t tp,
+                   int32_t rank, b2_tp_share* out);
 
 /* Device-side error code of the last launch on this model (B2_ERR_TIMEOUT
  * after a bounded wait gave up), 0 if none; clears it. */

@@ -125,6 +125,44 @@ int main(int argc, char** argv) {
                     fail(std::string(ph.name) + ": residual rows not owned by the last CTAs");
     }
 
+    // gate/up with the owners' share cut to own_pct percent (gu_plan)
+    for (int own_pct : {0, 10, 25, 50, 100}) {
+        const int tiles = 2 * FF / kTileRows;
+        std::vector<std::pair<int, int>> r;
+        for (int cta = 0; cta < grid; cta++) {
+            const TPlan p = gu_plan(tiles, H / 32, tbb, cta, grid, slot, warps, H / kTileRows, own_pct);
+            check_plan(p, H / 32, tbb, slot, "gateup own " + std::to_string(own_pct) + " cta " + std::to_string(cta));
+            r.push_back({p.u0, p.n});
+        }
+        check_partition(r, 0, tiles, "gateup own " + std::to_string(own_pct));
+    }
+
+    // down split over K (dn_split_plan): each residual tile's blocks are
+    // covered exactly once by its kDownSplit CTAs, whose slice index matches
+    if (kDownSplit * (H / kTileRows) <= grid) {
+        const int ht = H / kTileRows, nb = FF / 32;
+        std::vector<std::vector<int>> cover(ht, std::vector<int>(nb, 0));
+        for (int cta = 0; cta < grid; cta++) {
+            const TPlan p = dn_split_plan(ht, nb, tbb, cta, grid, slot, warps);
+            const std::string where = "down split cta " + std::to_string(cta);
+            if (p.n == 0) {
+                if (dn_slice_of(cta, grid, ht) >= 0) fail(where + ": slice index without work");
+                continue;
+            }
+            check_plan(p, p.kbn, tbb, slot, where);
+            if (p.n != 1 || p.u0 < 0 || p.u0 >= ht) fail(where + ": not one residual tile");
+            if (p.kb0 != dn_slice_of(cta, grid, ht) * nb / kDownSplit) fail(where + ": slice index mismatch");
+            for (int b = p.kb0; b < p.kb0 + p.kbn; b++) {
+                if (b < 0 || b >= nb) fail(where + ": block out of range");
+                else cover[p.u0][b]++;
+            }
+        }
+        for (int t = 0; t < ht; t++)
+            for (int b = 0; b < nb; b++)
+                if (cover[t][b] != 1) fail("down split: tile " + std::to_string(t) + " block " + std::to_string(b) +
+                                           " covered " + std::to_string(cover[t][b]) + " times");
+    }
+
     // QA phase: every split count the kernel can pick, fused and distributed forms
     const int tph = hd / kTileRows, qtiles = qd / kTileRows, kvtiles = 2 * kvd / kTileRows;
     for (int dist = 0; dist <= 1; dist++)

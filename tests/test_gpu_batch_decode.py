@@ -90,3 +90,30 @@ def test_batch_rejects_what_it_cannot_run(built_lib, write_model):
     assert e.value.code == -9
     bt.close()
     m.close()
+
+
+def test_batch_prefill_long_prompt_chunks(built_lib, oracle_lib, write_model):
+    """A 300-token prompt runs in three chunks (128, 128, 44 tokens) on the
+    tensor-core GEMM, each attending over the cache the earlier chunks
+    wrote: the argmax after the prompt, its logits (row 0) and four steps
+    after it against the oracle."""
+    shape = SHAPES["llama-hd128-q4"].with_(context=512)
+    path = write_model("llama-hd128-q4-ctx512", shape)
+    m = b2decode.Model(path, num_ctx=320)
+    g = goref.GoRef(path, num_ctx=320, n_threads=0, mode=goref.MODE_GGML_Q4)
+    prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, 299, seed=21)]).astype(np.int32)
+    bt = b2decode.Batch(m, 1)
+    first = bt.prefill(0, prompt)
+    want = g.forward(prompt)
+    assert rel_l2(bt.logits()[0], want) < LOGIT_TOL
+    assert first == int(np.argmax(want))
+    nxt, errs = [first], []
+    for _ in range(4):
+        ids = bt.step(nxt)
+        want = g.forward(nxt)
+        errs.append(rel_l2(bt.logits()[0], want))
+        assert int(ids[0]) == int(np.argmax(want))
+        nxt = [int(ids[0])]
+    assert max(errs) < LOGIT_TOL, errs
+    bt.close()
+    m.close()

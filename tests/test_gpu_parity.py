@@ -287,3 +287,21 @@ def test_wide_heads_distributed_qa(built_lib, oracle_lib, write_model, arch, wty
     want = g.predict(prompt, 8, temperature=0.001)
     got, _ = m.predict(prompt, b2decode.sample_opts(temperature=0.001, num_predict=8))
     assert got.tolist() == want.tolist()
+
+
+def test_distributed_qa_with_rowless_q_ctas(built_lib, oracle_lib, write_model):
+    """Head dim 128 over hidden 1280 takes the distributed QA form with only
+    112 q / k / v tiles for the 148 CTAs, so some q CTAs own no rows of the
+    projection and still attend (the shape of a 72B rank at TP8).  Context
+    past two attention tiles; teacher-forced logits and greedy ids vs the
+    oracle."""
+    shape = gw.ModelShape("llama", 1280, 2, 10, 2, 1024, 1024, 512, 1e-5, 5e5, False, False, "q8_0", 1, 2)
+    path = write_model("dist-qa-rowless", shape)
+    m = b2decode.Model(path, num_ctx=512)
+    g = goref.GoRef(path, num_ctx=512, n_threads=0)
+    prompt = gw.make_prompt(shape.vocab, 150, seed=8)
+    toks = np.concatenate([[shape.bos_id], prompt, gw.make_prompt(shape.vocab, 10, seed=9)]).astype(np.int32)
+    pairs = teacher_forced(m.forward, g.forward, toks, 151)
+    errs = [rel_l2(a, b) for a, b in pairs]
+    assert max(errs) < LOGIT_TOL, errs
+    assert np.mean([int(np.argmax(a)) == int(np.argmax(b)) for a, b in pairs]) >= 0.99
