@@ -21,6 +21,8 @@ int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t 
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
 int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
                        float* y, int ntok, cudaStream_t s, std::string* err);
+int b2_tiled_gemm_half_impl(int qtype, const void* base, int64_t rp, int half, int rows, int cols, const float* x,
+                            float* y, int ntok, cudaStream_t s, std::string* err);
 int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err);
 void b2_batch_free_impl(b2_batch* bt);
 int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, int32_t* next_out, std::string* err);
@@ -460,14 +462,14 @@ int b2_model_gemm(const b2_model* m, const char* name, const float* x, float* y,
     if (it == m->tensors.end()) return ret(B2_ERR_BAD_ARG, std::string("tensor not found: ") + name);
     const b2::TensorLoc& t = it->second;
     if (t.type != 8 && t.type != 2) return ret(B2_ERR_UNSUPPORTED_TYPE, std::string(name) + " is not a Q8_0 / Q4_0 matrix");
-    if (t.half) return ret(B2_ERR_BAD_ARG, std::string(name) + ": gate and up rows are interleaved in the resident matrix");
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != m->device)
         return ret(B2_ERR_BAD_ARG, "the model's device must be the current device");
     std::string err;
     const int rows = (int)(t.elements / (uint64_t)t.cols);
-    int rc = b2_tiled_gemm_impl((int)t.type, t.dev, t.rp, t.row0, rows, (int)t.cols, x, y, ntok,
-                                stream ? static_cast<cudaStream_t>(stream) : m->stream, &err);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    int rc = t.half ? b2_tiled_gemm_half_impl((int)t.type, t.dev, t.rp, t.half, rows, (int)t.cols, x, y, ntok, s, &err)
+                    : b2_tiled_gemm_impl((int)t.type, t.dev, t.rp, t.row0, rows, (int)t.cols, x, y, ntok, s, &err);
     return ret(rc, err);
 }
 

@@ -55,6 +55,8 @@ struct b2_batch {
     size_t part_floats = 0;
     int *d_pos = nullptr, *d_tok = nullptr, *d_next = nullptr;  // [kBatchMax]
     int* d_ppos = nullptr;                                      // [kBatchMax] prefill chunk positions
+    float* arg_v = nullptr;                                     // [kBatchMax][kArgParts] argmax parts
+    int* arg_i = nullptr;
     int* h_io = nullptr;                                        // pinned [3 * kBatchMax]
     std::vector<int> pos;                                       // positions (host copy)
     bool use_graph = false;                  // replay steps from a captured CUDA graph
@@ -91,25 +93,53 @@ __global__ void bd_embed_kernel(const uint8_t* __restrict__ emb, int V, int64_t 
 }
 
 // transformer.go:922-932 rmsNorm of each sequence's row: x * r * w with
-// r = 1 / sqrt(mean(x^2) + eps) (the root in double, as the Go code).
-__global__ void bd_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
-                                  int H, float eps) {
-    __shared__ float red[kBdThreads / 32];
+// r = 1 / sqrt(mean(x^2) + eps) (the root in double, as the Go code).  One
+// CTA of kNormThreads per row, the row read once (float4, kept in registers);
+// H a multiple of 4 (the batched path needs H % 64 == 0 for its products).
+constexpr int kNormThreads = 512;
+constexpr int kNormVec = 4;  // float4 per thread in the single pass: H up to 8192
+__global__ void __launch_bounds__(kNormThreads) bd_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                                   float* __restrict__ out, int H, float eps) {
+    __shared__ float red[kNormThreads / 32];
     __shared__ float rs;
-    const int b = blockIdx.x;
-    const float* xb = x + (size_t)b * H;
+    const int b = blockIdx.x, n4 = H / 4;
+    const float4* xb = reinterpret_cast<const float4*>(x + (size_t)b * H);
+    const float4* wv = reinterpret_cast<const float4*>(w);
+    float4* ob = reinterpret_cast<float4*>(out + (size_t)b * H);
+    float4 v[kNormVec];
     float ss = 0.0f;
-    for (int j = threadIdx.x; j < H; j += blockDim.x) ss = fmaf(xb[j], xb[j], ss);
+#pragma unroll
+    for (int k = 0; k < kNormVec; k++) {
+        const int i = threadIdx.x + k * kNormThreads;
+        v[k] = i < n4 ? xb[i] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        ss = fmaf(v[k].x, v[k].x, fmaf(v[k].y, v[k].y, fmaf(v[k].z, v[k].z, fmaf(v[k].w, v[k].w, ss))));
+    }
+    for (int i = threadIdx.x + kNormVec * kNormThreads; i < n4; i += kNormThreads) {
+        const float4 u = xb[i];
+        ss = fmaf(u.x, u.x, fmaf(u.y, u.y, fmaf(u.z, u.z, fmaf(u.w, u.w, ss))));
+    }
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     if (threadIdx.x == 0) {
         float t = 0.0f;
-        for (int i = 0; i < kBdThreads / 32; i++) t += red[i];
+        for (int i = 0; i < kNormThreads / 32; i++) t += red[i];
         rs = (float)(1.0 / sqrt((double)(t / (float)H) + (double)eps));
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < H; j += blockDim.x) out[(size_t)b * H + j] = xb[j] * rs * w[j];
+    const float r = rs;
+#pragma unroll
+    for (int k = 0; k < kNormVec; k++) {
+        const int i = threadIdx.x + k * kNormThreads;
+        if (i < n4) {
+            const float4 g = __ldg(wv + i);
+            ob[i] = make_float4(v[k].x * r * g.x, v[k].y * r * g.y, v[k].z * r * g.z, v[k].w * r * g.w);
+        }
+    }
+    for (int i = threadIdx.x + kNormVec * kNormThreads; i < n4; i += kNormThreads) {
+        const float4 u = xb[i], g = __ldg(wv + i);
+        ob[i] = make_float4(u.x * r * g.x, u.y * r * g.y, u.z * r * g.z, u.w * r * g.w);
+    }
 }
 
 // transformer.go:632-656: bias, RoPE on interleaved pairs of every q and k
@@ -166,37 +196,65 @@ __global__ void bd_swiglu_kernel(const float* __restrict__ gu, float* __restrict
     }
 }
 
-// transformer.go:1038-1046 argmax per sequence (the first maximum wins);
-// then the sequence's position moves past the token just appended.
-__global__ void bd_argmax_kernel(const float* __restrict__ logits, int V, int* __restrict__ next,
-                                 int* __restrict__ pos) {
-    __shared__ float bv[kBdThreads];
-    __shared__ int bi[kBdThreads];
-    const int b = blockIdx.x;
+// transformer.go:1038-1046 argmax per sequence (the first maximum wins), in
+// two levels: kArgParts CTAs per row each keep the best (value, index) of
+// their slice, then one warp per row takes the best of the parts (the lowest
+// index among equal values, as a left-to-right scan does); then the row's
+// position moves past the token just appended.
+constexpr int kArgParts = 32;
+__global__ void bd_argmax_part_kernel(const float* __restrict__ logits, int V, float* __restrict__ pv,
+                                      int* __restrict__ pi) {
+    __shared__ float bv[kBdThreads / 32];
+    __shared__ int bi[kBdThreads / 32];
+    const int b = blockIdx.x / kArgParts, part = blockIdx.x % kArgParts;
+    const int j0 = (int)((long long)part * V / kArgParts), j1 = (int)((long long)(part + 1) * V / kArgParts);
     const float* lb = logits + (size_t)b * V;
     float best = -INFINITY;
     int idx = V;
-    for (int j = threadIdx.x; j < V; j += blockDim.x)
+    for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x)
         if (lb[j] > best) {
             best = lb[j];
             idx = j;
         }
-    bv[threadIdx.x] = best;
-    bi[threadIdx.x] = idx;
-    __syncthreads();
-    for (int o = kBdThreads / 2; o; o >>= 1) {
-        if ((int)threadIdx.x < o) {
-            const float v2 = bv[threadIdx.x + o];
-            const int i2 = bi[threadIdx.x + o];
-            if (v2 > bv[threadIdx.x] || (v2 == bv[threadIdx.x] && i2 < bi[threadIdx.x])) {
-                bv[threadIdx.x] = v2;
-                bi[threadIdx.x] = i2;
-            }
+    for (int o = 16; o; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (v2 > best || (v2 == best && i2 < idx)) {
+            best = v2;
+            idx = i2;
         }
-        __syncthreads();
     }
+    if ((threadIdx.x & 31) == 0) {
+        bv[threadIdx.x >> 5] = best;
+        bi[threadIdx.x >> 5] = idx;
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
-        next[b] = bi[0] < V ? bi[0] : 0;
+        for (int w = 1; w < kBdThreads / 32; w++)
+            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) {
+                best = bv[w];
+                idx = bi[w];
+            }
+        // (bv[0], bi[0] is thread 0's own warp result: already in best / idx)
+        pv[blockIdx.x] = best;
+        pi[blockIdx.x] = idx;
+    }
+}
+__global__ void bd_argmax_final_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int V,
+                                       int* __restrict__ next, int* __restrict__ pos) {
+    const int b = blockIdx.x, lane = threadIdx.x;
+    float best = lane < kArgParts ? pv[b * kArgParts + lane] : -INFINITY;
+    int idx = lane < kArgParts ? pi[b * kArgParts + lane] : V;
+    for (int o = 16; o; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (v2 > best || (v2 == best && i2 < idx)) {
+            best = v2;
+            idx = i2;
+        }
+    }
+    if (lane == 0) {
+        next[b] = idx < V ? idx : 0;
         pos[b] += 1;
     }
 }
@@ -276,6 +334,7 @@ int batch_create(b2_model* m, int B, bool model_cache, b2_batch** out, std::stri
     const size_t o_gu = take(R * 2 * d.FF * 4), o_act = take(R * d.FF * 4);
     const size_t o_lg = take((size_t)kBatchMax * d.V * 4), o_part = take(bt->part_floats * 4);
     const size_t o_pos = take(R * 4), o_tok = take(R * 4), o_next = take(R * 4), o_ppos = take(R * 4);
+    const size_t o_argv = take((size_t)kBatchMax * kArgParts * 4), o_argi = take((size_t)kBatchMax * kArgParts * 4);
     if (cudaMalloc(&bt->arena, off) != cudaSuccess) {
         delete bt;
         *err = "device allocation of the batch state failed";
@@ -304,6 +363,8 @@ int batch_create(b2_model* m, int B, bool model_cache, b2_batch** out, std::stri
     bt->d_tok = reinterpret_cast<int*>(A + o_tok);
     bt->d_next = reinterpret_cast<int*>(A + o_next);
     bt->d_ppos = reinterpret_cast<int*>(A + o_ppos);
+    bt->arg_v = reinterpret_cast<float*>(A + o_argv);
+    bt->arg_i = reinterpret_cast<int*>(A + o_argi);
     if (!ok(cudaMemsetAsync(bt->arena, 0, off, m->stream), err, "clear") ||
         !ok(cudaStreamSynchronize(m->stream), err, "clear")) {
         cudaFreeHost(bt->h_io);
@@ -328,6 +389,13 @@ void b2_batch_free_impl(b2_batch* bt) {
 }
 
 namespace {
+
+// Prompt tokens per weight pass: kPrefillChunk when every product can run
+// on the tensor-core GEMM (widths a multiple of 64), else the batched
+// matvec's kBatchMax.
+int prefill_chunk(const ModelDev& d) {
+    return (d.H % 64 == 0 && d.qd % 64 == 0 && d.FF % 64 == 0) ? kPrefillChunk : kBatchMax;
+}
 
 // Y = W X for the R rows: the tensor-core GEMM from kGemmMinRows rows on,
 // the batched matvec (one weight pass, int8 planes against the tiled
@@ -364,7 +432,7 @@ int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_strid
     int rc = B2_OK;
     for (int l = 0; l < d.L && rc == B2_OK; l++) {
         const LayerDev& ld = m->layers_host[l];
-        bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, ld.attn_norm, bt->xn, H, d.eps);
+        bd_rmsnorm_kernel<<<R, kNormThreads, 0, s>>>(bt->x, ld.attn_norm, bt->xn, H, d.eps);
         rc = matmul_rows(qt, ld.wqkv, tiled_rows(n_qkv), n_qkv, H, bt->xn, bt->qkv, R, s, err);
         if (rc) break;
         __half* kc = bt->kc + (size_t)l * kv_layer + kv_off;
@@ -380,7 +448,7 @@ int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_strid
         rc = matmul_rows(qt, ld.wo, tiled_rows(H), H, d.qd, bt->att, bt->y, R, s, err);
         if (rc) break;
         bd_add_kernel<<<add_blocks, kBdThreads, 0, s>>>(bt->x, bt->y, R * H);
-        bd_rmsnorm_kernel<<<R, kBdThreads, 0, s>>>(bt->x, ld.ffn_norm, bt->xn, H, d.eps);
+        bd_rmsnorm_kernel<<<R, kNormThreads, 0, s>>>(bt->x, ld.ffn_norm, bt->xn, H, d.eps);
         rc = matmul_rows(qt, ld.wgu, tiled_rows(2 * d.FF), 2 * d.FF, H, bt->xn, bt->gu, R, s, err);
         if (rc) break;
         bd_swiglu_kernel<<<ew_blocks, kBdThreads, 0, s>>>(bt->gu, bt->act, d.FF, R);
@@ -390,10 +458,11 @@ int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_strid
     }
     if (rc) return rc;
     const int r_lm = all_logits ? 0 : R - 1, n_lm = all_logits ? R : 1;
-    bd_rmsnorm_kernel<<<n_lm, kBdThreads, 0, s>>>(bt->x + (size_t)r_lm * H, d.out_norm, bt->xn, H, d.eps);
-    rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn, bt->logits, n_lm, s, err);
+    bd_rmsnorm_kernel<<<n_lm, kNormThreads, 0, s>>>(bt->x + (size_t)r_lm * H, d.out_norm, bt->xn, H, d.eps);
+    rc = matmul_rows(qt, d.lm_head, d.Vp, d.V, H, bt->xn, bt->logits, n_lm, s, err);
     if (rc) return rc;
-    bd_argmax_kernel<<<n_lm, kBdThreads, 0, s>>>(bt->logits, d.V, bt->d_next, d_rpos + r_lm);
+    bd_argmax_part_kernel<<<n_lm * kArgParts, kBdThreads, 0, s>>>(bt->logits, d.V, bt->arg_v, bt->arg_i);
+    bd_argmax_final_kernel<<<n_lm, 32, 0, s>>>(bt->arg_v, bt->arg_i, d.V, bt->d_next, d_rpos + r_lm);
     return ok(cudaGetLastError(), err, "batched decode launch") ? B2_OK : B2_ERR_CUDA;
 }
 
@@ -424,8 +493,9 @@ int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, 
     }
     if (!device_current(m, err)) return B2_ERR_BAD_ARG;
     cudaStream_t s = m->stream;
-    for (int p0 = 0; p0 < n; p0 += kPrefillChunk) {
-        const int c = std::min(kPrefillChunk, n - p0);
+    const int chunk = prefill_chunk(d);
+    for (int p0 = 0; p0 < n; p0 += chunk) {
+        const int c = std::min(chunk, n - p0);
         if (!ok(cudaMemcpyAsync(bt->d_tok, prompt + p0, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens"))
             return B2_ERR_CUDA;
         bd_iota_kernel<<<(c + 255) / 256, 256, 0, s>>>(bt->d_ppos, c, p0);

@@ -71,7 +71,12 @@ struct GemmSmem {
     // (a multiple of 1024, so every stage's A and B tiles stay 1024-aligned)
     static constexpr int kStage = (kA + kB + QShape<QT>::kRawQ + QShape<QT>::kRawS + 1023) & ~1023;
     static constexpr int kFixed = 2048;  // alignment slack, then barriers and the TMEM slot
-    static constexpr int kStages = (kGemmSmemMax - kFixed) / kStage > 8 ? 8 : (kGemmSmemMax - kFixed) / kStage;
+    // the decode-step forms (BN <= 32: the stage is mostly the dequantised A
+    // tile) run two CTAs per SM on a 4-stage ring, so twice the warps decode
+    // weights; the prefill forms one CTA with as many stages as fit (<= 8)
+    static constexpr int kCtas = BN <= 32 ? 2 : 1;
+    static constexpr int kFit = (kGemmSmemMax / kCtas - kFixed) / kStage;
+    static constexpr int kStages = kCtas == 2 ? (kFit < 4 ? kFit : 4) : (kFit > 8 ? 8 : kFit);
     static_assert(kStages >= 2, "a K stage must fit twice");
     static constexpr int kTotal = kFixed + kStages * kStage;
 };
@@ -79,11 +84,13 @@ struct GemmSmem {
 struct GemmArgs {
     int nst;            // K stages per CTA (kStageBlocks blocks each)
     int kst_split;      // stages per split (the last split may take fewer)
+    int ksplit;         // splits of K (gridDim.z)
     int tiles_q;        // first 16-row Q tile of the matrix share (row0 / 16)
     int rows;           // output rows (weight rows) of the share
     int ntok;           // tokens (valid columns of X)
     int ldy;            // row stride of Y (floats)
-    float* y;           // [ntok][ldy] (split 1) or partials [split][ntok][rows]
+    float* y;           // [ntok][ldy]
+    float* part;        // split partials [split][ntok][rows] (ksplit > 1)
     const float* tok_scale;  // [ntok_pad] activation scale per token
     int* err;
 };
@@ -214,7 +221,7 @@ __device__ __forceinline__ void dequant_row(const uint8_t* rawq, const uint8_t* 
 }
 
 template <int QT, int BN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
     qgemm_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_s,
                  const __grid_constant__ CUtensorMap map_x, const GemmArgs a) {
     using SM = GemmSmem<QT, BN>;
@@ -322,10 +329,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int row = 32 * q + lane;
         bool ok = gemm_wait(accum, 0, a.err, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
+        // one decision for all four epilogue warps (each arrives here whatever
+        // its waits returned), so the barriers below are met by all or none
+        volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 4);  // [4]
+        if (lane == 0) ep_ok[warp - 2] = ok ? 1 : 0;
+        named_bar_sync(1, 128);
+        ok = ep_ok[0] && ep_ok[1] && ep_ok[2] && ep_ok[3];
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok && nst > 0) {
             const int grow = mt * kBM + row;  // output row within the share
-            float* yb = a.y + (size_t)ks * ((size_t)a.ntok * a.rows);
+            const size_t plane = (size_t)a.ntok * a.rows;
+            float* yb = a.ksplit > 1 ? a.part + (size_t)ks * plane : a.y;
+            const int ld = a.ksplit > 1 ? a.rows : a.ldy;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t v[16];
@@ -334,7 +349,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int j = 0; j < 16; j++) {
                     const int tok = nt * BN + c0 + j;
                     if (grow < a.rows && tok < a.ntok)
-                        yb[(size_t)tok * a.ldy + grow] = __uint_as_float(v[j]) * a.tok_scale[tok];
+                        yb[(size_t)tok * ld + grow] = __uint_as_float(v[j]) * a.tok_scale[tok];
                 }
             }
         }
@@ -357,18 +372,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 // X fp32 [ntok][cols] -> fp16 [ntok_pad][cols] scaled by 2^e per token (the
 // largest magnitude into [2^14, 2^15)), scale[t] = 2^-e; rows past ntok zero.
-__global__ void to_f16_scaled_kernel(const float* __restrict__ x, int ntok, int cols, __half* __restrict__ xh,
-                                     float* __restrict__ scale) {
-    __shared__ float red[8];
-    const int t = blockIdx.x;
+// One CTA of kCvtThreads per token; the row is read once (float4 loads kept
+// in registers for the scaling pass), cols a multiple of 64.
+constexpr int kCvtThreads = 512;
+constexpr int kCvtVec = 8;  // float4 per thread: cols up to 16384 in one pass
+__global__ void __launch_bounds__(kCvtThreads) to_f16_scaled_kernel(const float* __restrict__ x, int ntok, int cols,
+                                                                      __half* __restrict__ xh, float* __restrict__ scale) {
+    __shared__ float red[kCvtThreads / 32];
+    const int t = blockIdx.x, n4 = cols / 4;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * cols);
+    float4 v[kCvtVec];
     float mx = 0.0f;
-    if (t < ntok)
-        for (int j = threadIdx.x; j < cols; j += blockDim.x) mx = fmaxf(mx, fabsf(x[(size_t)t * cols + j]));
+#pragma unroll
+    for (int k = 0; k < kCvtVec; k++) {
+        const int i = threadIdx.x + k * kCvtThreads;
+        v[k] = (t < ntok && i < n4) ? __ldg(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+    }
+    // (columns past kCvtVec * kCvtThreads * 4: a second, rare pass below)
+    for (int i = threadIdx.x + kCvtVec * kCvtThreads; t < ntok && i < n4; i += kCvtThreads) {
+        const float4 w = __ldg(xr + i);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(w.x), fabsf(w.y)), fmaxf(fabsf(w.z), fabsf(w.w))));
+    }
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
     __syncthreads();
     mx = red[0];
-    for (int i = 1; i < (int)(blockDim.x >> 5); i++) mx = fmaxf(mx, red[i]);
+#pragma unroll
+    for (int i = 1; i < kCvtThreads / 32; i++) mx = fmaxf(mx, red[i]);
     int e = 0;
     if (mx > 0.0f && isfinite(mx)) {
         int ex;
@@ -377,19 +408,42 @@ __global__ void to_f16_scaled_kernel(const float* __restrict__ x, int ntok, int 
     }
     const float up = ldexpf(1.0f, e);
     if (threadIdx.x == 0) scale[t] = ldexpf(1.0f, -e);
-    for (int j = threadIdx.x; j < cols; j += blockDim.x)
-        xh[(size_t)t * cols + j] = __float2half_rn(t < ntok ? x[(size_t)t * cols + j] * up : 0.0f);
+    uint2* xo = reinterpret_cast<uint2*>(xh + (size_t)t * cols);
+#pragma unroll
+    for (int k = 0; k < kCvtVec; k++) {
+        const int i = threadIdx.x + k * kCvtThreads;
+        if (i < n4) {
+            const __half2 a = __floats2half2_rn(v[k].x * up, v[k].y * up), b = __floats2half2_rn(v[k].z * up, v[k].w * up);
+            xo[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+        }
+    }
+    for (int i = threadIdx.x + kCvtVec * kCvtThreads; i < n4; i += kCvtThreads) {
+        float4 w = t < ntok ? __ldg(xr + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const __half2 a = __floats2half2_rn(w.x * up, w.y * up), b = __floats2half2_rn(w.z * up, w.w * up);
+        xo[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+    }
 }
 
-// Split-K partials [ks][ntok][rows] -> y[tok][row] (summed in split order).
-__global__ void splitk_sum_kernel(const float* __restrict__ part, int ks, int ntok, int rows, int ldy,
-                                  float* __restrict__ y) {
-    const size_t n = (size_t)ntok * rows;
+// Split-K partials [ks][ntok][rows] -> y [ntok][rows], summed in split order
+// (the same sums whatever order the CTAs finished in): float4 elements when
+// y is 16-byte aligned and the count divides by 4, single floats otherwise.
+__global__ void splitk_sum4_kernel(const float* __restrict__ part, int ks, size_t n4, float* __restrict__ y) {
+    const float4* p = reinterpret_cast<const float4*>(part);
+    float4* o = reinterpret_cast<float4*>(y);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        float4 v = __ldcg(p + i);
+        for (int s = 1; s < ks; s++) {
+            const float4 w = __ldcg(p + (size_t)s * n4 + i);
+            v.x += w.x; v.y += w.y; v.z += w.z; v.w += w.w;
+        }
+        o[i] = v;
+    }
+}
+__global__ void splitk_sum1_kernel(const float* __restrict__ part, int ks, size_t n, float* __restrict__ y) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        float v = part[i];
-        for (int s = 1; s < ks; s++) v += part[(size_t)s * n + i];
-        const size_t tok = i / rows, row = i - tok * rows;
-        y[tok * ldy + row] = v;
+        float v = __ldcg(part + i);
+        for (int s = 1; s < ks; s++) v += __ldcg(part + (size_t)s * n + i);
+        y[i] = v;
     }
 }
 
@@ -480,8 +534,8 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         *err = "tensor-core GEMM: cols must be a multiple of 64 and rows inside the matrix";
         return B2_ERR_BAD_ARG;
     }
-    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 3) {
-        *err = "x and y must be 4-byte aligned";
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 3)) {
+        *err = "x must be 16-byte aligned and y 4-byte aligned";
         return B2_ERR_BAD_ARG;
     }
     std::string e2;
@@ -549,7 +603,7 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         *err = "tensor map encoding failed (alignment)";
         return B2_ERR_BAD_ARG;
     }
-    to_f16_scaled_kernel<<<ntok_pad, 256, 0, s>>>(x, ntok, cols, xh, tsc);
+    to_f16_scaled_kernel<<<ntok_pad, kCvtThreads, 0, s>>>(x, ntok, cols, xh, tsc);
     GemmArgs a{};
     a.nst = nst;
     a.kst_split = kst;
@@ -557,15 +611,21 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
     a.rows = rows;
     a.ntok = ntok;
     a.ldy = rows;
-    a.y = ksplit > 1 ? part : y;
+    a.y = y;
+    a.ksplit = ksplit;
+    a.part = part;
     a.tok_scale = tsc;
     a.err = sc->err;
     const dim3 grid(m_tiles, n_tiles, ksplit);
     int rc = q8 ? launch_bn<8>(bn, mq, ms, mx, a, grid, s, err) : launch_bn<2>(bn, mq, ms, mx, a, grid, s, err);
     if (rc) return rc;
     if (ksplit > 1) {
-        const int blocks = std::min(sc->sms * 4, (int)(((size_t)ntok * rows + 255) / 256));
-        splitk_sum_kernel<<<std::max(blocks, 1), 256, 0, s>>>(part, ksplit, ntok, rows, rows, y);
+        const size_t n = (size_t)ntok * rows;
+        const bool vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;  // (part is 256-aligned)
+        const size_t units = vec ? n / 4 : n;
+        const int blocks = (int)std::min<size_t>((size_t)sc->sms * 8, (units + 255) / 256);
+        if (vec) splitk_sum4_kernel<<<std::max(blocks, 1), 256, 0, s>>>(part, ksplit, units, y);
+        else splitk_sum1_kernel<<<std::max(blocks, 1), 256, 0, s>>>(part, ksplit, units, y);
     }
     cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) {
@@ -573,6 +633,45 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         return B2_ERR_CUDA;
     }
     return B2_OK;
+}
+
+namespace b2 {
+namespace {
+// y[t][j] = fused[t][16 (j / 8) + j % 8 + 8 (half - 1)]: one half (gate 1,
+// up 2) of a gate/up product computed over the interleaved resident matrix.
+__global__ void gather_half_kernel(const float* __restrict__ fused, int ntok, int rows, int half,
+                                   float* __restrict__ y) {
+    const size_t n = (size_t)ntok * rows;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t t = i / rows;
+        const int j = (int)(i - t * rows);
+        y[i] = fused[t * 2 * rows + (size_t)(j >> 3) * 16 + (j & 7) + (half == 2 ? 8 : 0)];
+    }
+}
+}  // namespace
+}  // namespace b2
+
+// The gate or up half (half 1 or 2) of the interleaved gate/up matrix (2 *
+// rows resident rows): the product over the whole matrix into a buffer the
+// call allocates on the stream, then that half's rows.
+int b2_tiled_gemm_half_impl(int qtype, const void* base, int64_t rp, int half, int rows, int cols, const float* x,
+                            float* y, int ntok, cudaStream_t s, std::string* err) {
+    float* fused = nullptr;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&fused), sizeof(float) * (size_t)ntok * 2 * rows, s) != cudaSuccess) {
+        *err = "allocation of the gate/up product failed";
+        return B2_ERR_OOM;
+    }
+    int rc = b2_tiled_gemm_impl(qtype, base, rp, 0, 2 * rows, cols, x, fused, ntok, s, err);
+    if (!rc) {
+        const int blocks = (int)std::min<size_t>(4096, ((size_t)ntok * rows + 255) / 256);
+        gather_half_kernel<<<std::max(blocks, 1), 256, 0, s>>>(fused, ntok, rows, half, y);
+        if (cudaGetLastError() != cudaSuccess) {
+            *err = "gate/up gather launch failed";
+            rc = B2_ERR_CUDA;
+        }
+    }
+    cudaFreeAsync(fused, s);
+    return rc;
 }
 
 // Device error flag of the GEMM scratch of stream s (0 if none); clears it.

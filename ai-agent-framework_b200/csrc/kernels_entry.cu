@@ -42,6 +42,11 @@ DeviceScratch* scratch_for_current(std::string* err) {
 // split over the context (flash-decoding) with a log-sum-exp merge.
 // ---------------------------------------------------------------------------
 
+template <int N>
+__device__ __forceinline__ void cp_async_wait_stages() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 constexpr int kAttThreads = 256;
 constexpr int kAttWarps = kAttThreads / 32;
 constexpr int kMaxGrp = 8;      // query heads per KV head handled in registers
@@ -187,6 +192,274 @@ __global__ void __launch_bounds__(kAttThreads, (GRP <= 4 ? 2 : 1))
     }
 }
 
+// ---------------------------------------------------------------------------
+// The same split attention on the tensor cores (head dimension 64 or 128, up
+// to 16 query heads per KV head).  One CTA = one (sequence, KV head, context
+// slice), 4 warps; the cached K and V rows of the slice stream through a
+// cp.async ring of kMmaStages tiles of kMmaTile positions in 128-byte-swizzled
+// shared memory.  Per 16 positions a warp computes S = Q K^T with
+// mma.m16n8k16 (the group's query heads are the 16 rows of A; rows past the
+// group are zero), keeps an online softmax per row on the accumulator
+// fragments, and adds P V with P taken straight from the S fragments (two
+// n8 accumulator tiles form one k16 A fragment).  Q and P are split into two
+// fp16 terms each (hi + lo, the lo term the rounding remainder), so the
+// products carry about 22 bits: the result matches the fp32 loop of
+// transformer.go:663-685 to ~1e-6, with K and V used exactly.  The four
+// warps' (o, m, l) merge in shared memory into the same partial record as
+// attn_split_kernel writes.
+// ---------------------------------------------------------------------------
+constexpr int kMmaThreads = 128;
+constexpr int kMmaTile = 64;   // positions per ring tile (16 per warp)
+constexpr int kMmaStages = 4;
+constexpr int kMmaMaxGrp = 16;
+
+template <int HD>
+struct MmaSmem {
+    static constexpr int kRow = HD * 2;                    // bytes of one cached row
+    static constexpr int kTile = kMmaTile * kRow;          // one K (or V) tile
+    static constexpr int kQ = 16 * kRow;                   // Q hi (then Q lo) [16 rows][HD] fp16
+    static constexpr int kStages = kMmaStages;
+    static constexpr int kMerge = 4 * 16 * (HD + 2) * 4;   // warps' (o, m, l) for the merge
+    static constexpr int kRing = kStages * 2 * kTile;
+    static constexpr int kTotal = kRing + 2 * kQ + (kMerge > 0 ? 0 : 0);
+};
+
+// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile
+template <int HD>
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+    return (uint32_t)(r * (HD * 2) + ((c ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4_t(uint32_t addr, uint32_t* r) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+// (a, b) -> half2 hi and the half2 of the remainders
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int HD, bool VAR>
+__global__ void __launch_bounds__(kMmaThreads, 1)
+    attn_mma_kernel(const float* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
+                    float* __restrict__ part, int nh, int nkv, int grp, int ctx, int S, const AttnSeqs seqs) {
+    using SM = MmaSmem<HD>;
+    constexpr int KS = HD / 16;        // k16 steps of S = Q K^T
+    constexpr int NT = HD / 8;         // n8 tiles of O
+    constexpr int CH = HD * 2 / 16;    // 16-byte chunks per row
+    extern __shared__ __align__(1024) uint8_t asm_raw[];
+    uint8_t* ring = asm_raw;                         // [stage][K tile | V tile]
+    uint8_t* qh = ring + SM::kRing;                  // [16][HD] fp16, swizzled
+    uint8_t* ql = qh + SM::kQ;
+    const int cta = blockIdx.x;
+    const int s = cta % S, g = (cta / S) % nkv, b = cta / (S * nkv);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, ti = lane & 3;
+    const int len = VAR ? __ldg(seqs.lens + b) + seqs.add : ctx;
+    const int t0 = (int)((long long)s * len / S), t1 = (int)((long long)(s + 1) * len / S);
+    const size_t kvd = (size_t)nkv * HD;
+    const size_t bstride = VAR ? (size_t)seqs.stride : (size_t)ctx;
+    const __half* kb = k + (size_t)b * bstride * kvd + (size_t)g * HD;
+    const __half* vb = v + (size_t)b * bstride * kvd + (size_t)g * HD;
+    const int ntile = (t1 - t0 + kMmaTile - 1) / kMmaTile;
+
+    auto issue = [&](int tile) {
+        if (tile < ntile) {
+            uint8_t* kt = ring + (size_t)(tile % kMmaStages) * 2 * SM::kTile;
+            uint8_t* vt = kt + SM::kTile;
+            for (int i = threadIdx.x; i < kMmaTile * CH; i += kMmaThreads) {
+                const int r = i / CH, c = i - r * CH;
+                const int t = t0 + tile * kMmaTile + r;
+                const bool ok = t < t1;
+                const size_t row = (size_t)(ok ? t : t0) * kvd;
+                cp_async16_zfill(kt + sw_off<HD>(r, c), kb + row + c * 8, ok);
+                cp_async16_zfill(vt + sw_off<HD>(r, c), vb + row + c * 8, ok);
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll 1
+    for (int i = 0; i < kMmaStages - 1; i++) issue(i);
+
+    // Q (scaled by 1 / sqrt(HD)) as hi + lo fp16 rows; rows past the group zero
+    const float scale = (float)(1.0 / sqrt((double)HD));
+    for (int i = threadIdx.x; i < 16 * (HD / 2); i += kMmaThreads) {
+        const int r = i / (HD / 2), c2 = i - r * (HD / 2);  // row, pair of columns
+        float a = 0.0f, bb = 0.0f;
+        if (r < grp) {
+            const float* qr = q + ((size_t)b * nh + (size_t)g * grp + r) * HD + 2 * c2;
+            a = qr[0] * scale;
+            bb = qr[1] * scale;
+        }
+        uint32_t hi, lo;
+        split2(a, bb, hi, lo);
+        const uint32_t off = sw_off<HD>(r, (2 * c2) / 8) + ((2 * c2) % 8) * 2;
+        *reinterpret_cast<uint32_t*>(qh + off) = hi;
+        *reinterpret_cast<uint32_t*>(ql + off) = lo;
+    }
+
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;  // rows gi, gi + 8
+    const uint32_t qh_s = smem_u32(qh), ql_s = smem_u32(ql);
+    // ldmatrix row / chunk of this lane for an A (Q) fragment: matrices
+    // (rows 0-7, k 0-7), (rows 8-15, k 0-7), (rows 0-7, k 8-15), (rows 8-15, k 8-15)
+    const int a_row = (lane & 7) + ((lane >> 3) & 1) * 8, a_kc = (lane >> 4) & 1;
+    // B (K) fragments, non-transposed: (pos 0-7, k 0-7), (pos 0-7, k 8-15), (pos 8-15, k 0-7), (pos 8-15, k 8-15)
+    const int bk_row = (lane & 7) + ((lane >> 4) & 1) * 8, bk_kc = (lane >> 3) & 1;
+    // B (V) fragments, transposed: (pos 0-7, d 0-7), (pos 8-15, d 0-7), (pos 0-7, d 8-15), (pos 8-15, d 8-15)
+    const int bv_row = (lane & 7) + ((lane >> 3) & 1) * 8, bv_dc = (lane >> 4) & 1;
+
+#pragma unroll 1
+    for (int tile = 0; tile < ntile; tile++) {
+        issue(tile + kMmaStages - 1);
+        cp_async_wait_stages<kMmaStages - 1>();
+        __syncthreads();
+        const uint8_t* kt = ring + (size_t)(tile % kMmaStages) * 2 * SM::kTile;
+        const uint32_t kt_s = smem_u32(kt), vt_s = kt_s + SM::kTile;
+        const int p0 = warp * 16;  // this warp's 16 positions of the tile
+        const int tb = t0 + tile * kMmaTile + p0;
+        if (tb < t1) {
+            float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int kk = 0; kk < KS; kk++) {
+                uint32_t ah[4], al[4], bkr[4];
+                ldsm4(qh_s + sw_off<HD>(a_row, 2 * kk + a_kc), ah);
+                ldsm4(ql_s + sw_off<HD>(a_row, 2 * kk + a_kc), al);
+                ldsm4(kt_s + sw_off<HD>(p0 + bk_row, 2 * kk + bk_kc), bkr);
+                mma_f16_16816(s0, ah, bkr[0], bkr[1]);
+                mma_f16_16816(s0, al, bkr[0], bkr[1]);
+                mma_f16_16816(s1, ah, bkr[2], bkr[3]);
+                mma_f16_16816(s1, al, bkr[2], bkr[3]);
+            }
+            // positions past the slice: score -inf
+            const int c0 = tb + 2 * ti, c1 = tb + 8 + 2 * ti;
+            if (c0 >= t1) { s0[0] = -INFINITY; s0[2] = -INFINITY; }
+            if (c0 + 1 >= t1) { s0[1] = -INFINITY; s0[3] = -INFINITY; }
+            if (c1 >= t1) { s1[0] = -INFINITY; s1[2] = -INFINITY; }
+            if (c1 + 1 >= t1) { s1[1] = -INFINITY; s1[3] = -INFINITY; }
+            // online softmax per row (row gi: s*[0..1], row gi + 8: s*[2..3])
+            float r0 = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s1[0], s1[1]));
+            float r1 = fmaxf(fmaxf(s0[2], s0[3]), fmaxf(s1[2], s1[3]));
+            r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 1));
+            r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 1));
+            r0 = fmaxf(r0, __shfl_xor_sync(0xffffffffu, r0, 2));
+            r1 = fmaxf(r1, __shfl_xor_sync(0xffffffffu, r1, 2));
+            const float n0 = fmaxf(m0, r0), n1 = fmaxf(m1, r1);  // (finite: position tb is valid)
+            const float f0 = m0 == -INFINITY ? 0.0f : __expf(m0 - n0), f1 = m1 == -INFINITY ? 0.0f : __expf(m1 - n1);
+            m0 = n0;
+            m1 = n1;
+            float p[8] = {__expf(s0[0] - n0), __expf(s0[1] - n0), __expf(s0[2] - n1), __expf(s0[3] - n1),
+                          __expf(s1[0] - n0), __expf(s1[1] - n0), __expf(s1[2] - n1), __expf(s1[3] - n1)};
+            l0 = fmaf(l0, f0, p[0] + p[1] + p[4] + p[5]);
+            l1 = fmaf(l1, f1, p[2] + p[3] + p[6] + p[7]);
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                o[n][0] *= f0; o[n][1] *= f0; o[n][2] *= f1; o[n][3] *= f1;
+            }
+            // P as the A fragment of P V: (row gi, k 2ti..), (row gi + 8, ..), (row gi, k 8 + 2ti..), (row gi + 8, ..)
+            uint32_t ph[4], pl[4];
+            split2(p[0], p[1], ph[0], pl[0]);
+            split2(p[2], p[3], ph[1], pl[1]);
+            split2(p[4], p[5], ph[2], pl[2]);
+            split2(p[6], p[7], ph[3], pl[3]);
+#pragma unroll
+            for (int n2 = 0; n2 < NT / 2; n2++) {  // two n8 tiles (16 dims) per transposed load
+                uint32_t bvr[4];
+                ldsm4_t(vt_s + sw_off<HD>(p0 + bv_row, 2 * n2 + bv_dc), bvr);
+                mma_f16_16816(o[2 * n2], ph, bvr[0], bvr[1]);
+                mma_f16_16816(o[2 * n2], pl, bvr[0], bvr[1]);
+                mma_f16_16816(o[2 * n2 + 1], ph, bvr[2], bvr[3]);
+                mma_f16_16816(o[2 * n2 + 1], pl, bvr[2], bvr[3]);
+            }
+        }
+        __syncthreads();  // the slot is refilled by the next iteration's issue
+    }
+    cp_async_wait();
+    // row sums over the four lanes of a row
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    // merge the warps: [warp][16 rows][HD + 2] floats over the ring
+    __syncthreads();
+    float* mw = reinterpret_cast<float*>(ring);
+    float* wr = mw + (size_t)warp * 16 * (HD + 2);
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const int d = n * 8 + 2 * ti;
+        wr[gi * (HD + 2) + d] = o[n][0];
+        wr[gi * (HD + 2) + d + 1] = o[n][1];
+        wr[(gi + 8) * (HD + 2) + d] = o[n][2];
+        wr[(gi + 8) * (HD + 2) + d + 1] = o[n][3];
+    }
+    if (ti == 0) {
+        wr[gi * (HD + 2) + HD] = m0;
+        wr[gi * (HD + 2) + HD + 1] = l0;
+        wr[(gi + 8) * (HD + 2) + HD] = m1;
+        wr[(gi + 8) * (HD + 2) + HD + 1] = l1;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < grp * (HD + 2); i += kMmaThreads) {
+        const int h = i / (HD + 2), d = i - h * (HD + 2);
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) M = fmaxf(M, mw[((size_t)w * 16 + h) * (HD + 2) + HD]);
+        float val = M;
+        if (d != HD) {
+            val = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                const float* pw = mw + ((size_t)w * 16 + h) * (HD + 2);
+                const float f = pw[HD] == -INFINITY ? 0.0f : __expf(pw[HD] - M);
+                val = fmaf(pw[d], f, val);
+            }
+        }
+        part[(((size_t)b * nh + (size_t)g * grp + h) * S + s) * (HD + 2) + d] = val;
+    }
+}
+
+template <int HD, bool VAR>
+bool launch_mma_hd(int grp, int grid, cudaStream_t st, const float* q, const __half* k, const __half* v, float* part,
+                   int nh, int nkv, int ctx, int S, const AttnSeqs& seqs) {
+    static bool attr = false;
+    constexpr int smem = MmaSmem<HD>::kTotal;
+    static_assert(4 * 16 * (HD + 2) * 4 <= MmaSmem<HD>::kRing, "the warp merge fits over the ring");
+    if (!attr) {
+        if (cudaFuncSetAttribute(attn_mma_kernel<HD, VAR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return false;
+        attr = true;
+    }
+    attn_mma_kernel<HD, VAR><<<grid, kMmaThreads, smem, st>>>(q, k, v, part, nh, nkv, grp, ctx, S, seqs);
+    return true;
+}
+
 // Launches attn_split_kernel for head dimension hd (64, 128, 256) and group
 // size grp (1 .. 8); returns false for other geometries.
 template <int HD, bool VAR>
@@ -215,6 +488,13 @@ bool launch_split_hd(int grp, int grid, cudaStream_t st, const float* q, const _
 bool launch_split(int hd, int grp, int grid, cudaStream_t st, const float* q, const __half* k, const __half* v,
                   float* part, int nh, int nkv, int ctx, int S, const AttnSeqs* seqs = nullptr) {
     const AttnSeqs none{nullptr, 0, 0};
+    if (grp <= kMmaMaxGrp && (hd == 64 || hd == 128)) {  // the tensor-core form
+        if (hd == 64)
+            return seqs ? launch_mma_hd<64, true>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, *seqs)
+                        : launch_mma_hd<64, false>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, none);
+        return seqs ? launch_mma_hd<128, true>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, *seqs)
+                    : launch_mma_hd<128, false>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, none);
+    }
     switch (hd) {
         case 64:
             return seqs ? launch_split_hd<64, true>(grp, grid, st, q, k, v, part, nh, nkv, ctx, S, *seqs)

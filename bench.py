@@ -35,7 +35,12 @@ The other workloads (one GPU, one JSON line per case; not the driver's line):
              serve repeats;
   attention  b2_attention_decode, 32 query / 8 KV heads, head_dim 128, fp16 KV
              N(0,1), contexts 4096 / 16384 / 32768, batch 1 and 8, KV copies
-             rotated past L2 in the same way.
+             rotated past L2 in the same way;
+  gemm       the tcgen05 tensor-core GEMM (b2_model_gemm) on one Llama-3-8B
+             layer's Q4_0 matrices for --tokens tokens (512), TFLOP/s against
+             the measured dense bf16 peak.
+--case picks one case of a microbench (attention 32768x8, matvec
+q8_0:128256x4096:1, gemm blk.0.ffn_up.weight).
 With --batch B > 1 (qwen05b or llama3-8b, one GPU) the model workload runs as
 batched greedy decode (b2_batch_*): B sequences, each prefilled with a prompt
 of its own, then K steps of all of them; value = tokens of all sequences per
@@ -62,6 +67,12 @@ import numpy as np  # noqa: E402
 METRIC = "decode tok/s (B=1) and weight-stream HBM GB/s vs 8 TB/s peak"
 WORKLOAD = "qwen2.5-0.5b-shape q8_0 greedy decode, batch 1, prompt 128+BOS"
 FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks() -> dict:
+    """MEASURED_PEAKS.json as a dict ({} when absent)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
 
 
 def peaks():
@@ -197,15 +208,28 @@ def dist_env():
     return ws, rank, local
 
 
-def profile_traffic(kernel: str):
-    """DRAM bytes (read + write) per launch of the decode kernel, from the
-    committed ncu summary's `dram_bytes_per_launch:` line."""
+def profile_traffic(ms_per_step: float) -> tuple:
+    """DRAM bytes (read + write) per launch of the decode kernel from the
+    committed ncu summary (`dram_bytes_per_launch:`), used only when the
+    launch it profiled (`kernel_ms:`) took within 10 % of the timed step;
+    returns (bytes or None, a note naming the summary, its commit and time)."""
     p = os.path.join(ROOT, "profiles", "decode_kernel_qwen05b_q8_0.md")
-    if os.path.exists(p):
-        for line in open(p):
-            if line.startswith("dram_bytes_per_launch:"):
-                return int(line.split(":", 1)[1])
-    return None
+    if not os.path.exists(p):
+        return None, "no profile summary"
+    vals = {}
+    for line in open(p):
+        line = line.strip()
+        for key in ("dram_bytes_per_launch", "kernel_ms", "commit"):
+            if line.startswith(key + ":"):
+                vals[key] = line.split(":", 1)[1].strip()
+    if "dram_bytes_per_launch" not in vals or "kernel_ms" not in vals:
+        return None, "profile summary without traffic or kernel time"
+    kms = float(vals["kernel_ms"])
+    note = (f"profiles/decode_kernel_qwen05b_q8_0.md (commit {vals.get('commit', '?')}, "
+            f"profiled launch {kms:.3f} ms vs timed {ms_per_step:.3f} ms)")
+    if abs(kms - ms_per_step) > 0.1 * ms_per_step:
+        return None, note + ": more than 10 % apart, traffic not quoted"
+    return int(vals["dram_bytes_per_launch"]), note
 
 
 def cpu_model() -> str:
@@ -349,10 +373,12 @@ def run_b200(args) -> None:
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(dev_uuid) as clk:
+        torch.cuda.nvtx.range_push("timed")  # (lets a profiler keep to the timed steps)
         e0.record(stream)
         ids = m.decode_greedy(last, K)
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     barrier()
     ms = e0.elapsed_time(e1)
     ms_max = max_over_ranks(ms)
@@ -378,6 +404,7 @@ def run_b200(args) -> None:
     ctx_mid = len(prompt) + W + K // 2
     kv_bytes = 2 * cfg["num_layers"] * cfg["num_kv_heads"] * cfg["head_dim"] * 2 * ctx_mid
     achieved = bytes_tok / (ms_tok / 1000.0) / 1e9
+    traffic, traffic_note = profile_traffic(ms_max / K) if args.workload == "qwen05b" else (None, "not profiled")
     clocks = clk.summary()
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
@@ -391,19 +418,23 @@ def run_b200(args) -> None:
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong" if tpn > 1 else "weak",
             "vs_baseline": None,
-            "dtype": "fp32", "data": "synthetic",
+            "dtype": f"{shape.wtype.upper()} weights x int8 activation planes (3 per 32-block, |x - x'| <= "
+                     f"2^-22 of the block maximum), exact int32 products, fp32 accumulate; fp16 KV cache",
+            "data": "synthetic",
             "config": {"workload": workload, "weights": f"N(0,0.02) quantised {shape.wtype.upper()}, seed 0",
                        "prompt_tokens": int(len(prompt)), "decode_tokens_timed": K,
                        "ctx_range": [int(len(prompt) + W), int(len(prompt) + W + K)],
                        "l2": f"no flush needed: each token streams {bytes_tok / 1e6:.0f} MB of weights, > 126 MB L2",
                        "parallelism": (f"tp{tpn}" if tpn > 1 else (f"replicas x{ws}" if ws > 1 else "single gpu")),
                        "prefill_s": prefill_s,
-                       "prefill_path": "the decode kernel once per prompt token (b2_forward_argmax)",
+                       "prefill_path": ("b2_forward_argmax: the prompt in 128-token chunks on the tcgen05 GEMM path "
+                                        "into the model's KV cache" if tpn == 1 else
+                                        "b2_forward_argmax: the decode kernel once per prompt token (tensor parallel)"),
                        "load_s": load_s,
                        "kv_cache": "fp16"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": profile_traffic("decode_kernel") if args.workload == "qwen05b" else None,
+                         "traffic": traffic, "traffic_source": traffic_note,
                          "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
                          "algorithmic_bytes_per_token": bytes_tok, "kv_bytes_per_token": kv_bytes},
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
@@ -527,6 +558,8 @@ def run_matvec(args) -> None:
     for batch in (1, 8):
         for kind, qt in (("q8_0", 8), ("q4_0", 2)):
             for rows, cols in ((4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)):
+                if args.case and args.case != f"{kind}:{rows}x{cols}:{batch}":
+                    continue
                 rng = np.random.default_rng(rows * 7 + cols)
                 base = gw.quantize(rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02),
                                    gw.TYPE_NAMES[kind])
@@ -571,6 +604,8 @@ def run_attention(args) -> None:
     g = torch.Generator(device="cuda").manual_seed(0)
     for ctx in (4096, 16384, 32768):
         for B in (1, 8):
+            if args.case and args.case != f"{ctx}x{B}":
+                continue
             kvbytes = 2 * B * ctx * nkv * hd * 2
             ncp = _rotations(kvbytes)
             ks = [torch.randn(B * ctx * nkv * hd, generator=g, device="cuda").half() for _ in range(ncp)]
@@ -592,6 +627,61 @@ def run_attention(args) -> None:
             }), flush=True)
             del ks, vs
             torch.cuda.empty_cache()
+
+
+def run_gemm(args) -> None:
+    """The tcgen05 tensor-core GEMM (b2_model_gemm) on the matrices of one
+    Llama-3-8B layer (Q4_0: Wq, Wk, Wv, Wo, gate, up, down; the 4-layer file
+    of the real widths) for a prompt-sized token count (--tokens, 512 by
+    default): TFLOP/s = 2 x rows x cols x tokens / time, against the measured
+    dense bf16 peak (the fp16 kind runs at the same rate).  Gate and up are
+    each timed as b2_model_gemm runs them alone (the whole interleaved matrix,
+    then one half gathered); the batched forward runs them as one product."""
+    import torch
+
+    import b2decode
+    from b2decode import gguf_writer as gw
+    torch.cuda.set_device(0)
+    shape = gw.SHAPES["llama3-8b-4l"]
+    m = b2decode.Model(ensure_model("llama3-8b-4l"), num_ctx=64)
+    st = torch.cuda.ExternalStream(m.stream_handle())
+    H, FF, qd, kvd = shape.hidden, shape.ffn, shape.heads * shape.head_dim, shape.kv_dim
+    mats = {"blk.0.attn_q.weight": (qd, H), "blk.0.attn_k.weight": (kvd, H), "blk.0.attn_v.weight": (kvd, H),
+            "blk.0.attn_output.weight": (H, qd), "blk.0.ffn_gate.weight": (FF, H), "blk.0.ffn_up.weight": (FF, H),
+            "blk.0.ffn_down.weight": (H, FF)}
+    mp = measured_peaks()
+    peak = float(mp.get("bf16_tflops", 1590.0)) if mp else 1590.0
+    ntok = args.tokens
+    tot_flop, tot_ms = 0.0, 0.0
+    for name, (rows, cols) in mats.items():
+        if args.case and args.case != name:
+            continue
+        x = torch.randn(ntok, cols, device="cuda")
+        y = torch.empty(ntok, rows, device="cuda")
+        with torch.cuda.stream(st):
+            ms = _timed(torch, st, lambda i: m.gemm(name, x.data_ptr(), y.data_ptr(), ntok), 1, max(args.steps, 8))
+        flop = 2.0 * rows * cols * ntok
+        tf = flop / (ms / 1000.0) / 1e12
+        tot_flop += flop
+        tot_ms += ms
+        print(json.dumps({
+            "metric": "tensor-core GEMM TFLOP/s (prefill product)", "value": tf, "unit": "TFLOP/s", "n_gpus": 1,
+            "higher_is_better": True, "dtype": "Q4_0 weights -> fp16 (d*q rounded once) x fp16 activations "
+                                               "(power-of-two scale per token), fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": f"{name} {rows}x{cols} (Llama-3-8B widths, Q4_0) x {ntok} tokens",
+                       "us_per_call": ms * 1000.0, "path": "b2_model_gemm: tcgen05.mma kind::f16, TMA-staged tiles"},
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "peak_source": "MEASURED_PEAKS.json bf16_tflops" if mp else "fallback 1.59 PFLOP/s"},
+        }), flush=True)
+    if not args.case:
+        tf = tot_flop / (tot_ms / 1000.0) / 1e12
+        print(json.dumps({"metric": "tensor-core GEMM TFLOP/s, one Llama-3-8B layer's products", "value": tf,
+                          "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True,
+                          "config": {"workload": f"q, k, v, o, gate, up, down x {ntok} tokens", "ms": tot_ms},
+                          "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                       "frac": tf / peak}}), flush=True)
+    m.close()
 
 
 def run_batch(args) -> None:
@@ -629,6 +719,7 @@ def run_batch(args) -> None:
     except Exception:
         pass
     with Clocks(dev_uuid) as clk:
+        torch.cuda.nvtx.range_push("timed")  # (lets a profiler keep to the timed steps)
         e0.record(stream)
         t_host = time.perf_counter()
         for _ in range(K):
@@ -636,6 +727,7 @@ def run_batch(args) -> None:
         t_host = time.perf_counter() - t_host
         e1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     ms = e0.elapsed_time(e1)
     peak, peak_kind = peaks()
     bytes_step = int(m.cfg["stream_bytes_per_token"])
@@ -682,7 +774,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp72b", action="store_true",
                     help="qwen05b: skip the tensor-parallel 72B-shape measurement added to the line")
-    ap.add_argument("--workload", default="qwen05b", choices=["qwen05b", "llama3-8b", "qwen72b", "matvec", "attention"])
+    ap.add_argument("--workload", default="qwen05b",
+                    choices=["qwen05b", "llama3-8b", "qwen72b", "matvec", "attention", "gemm"])
+    ap.add_argument("--case", default="",
+                    help="one case of a microbench: attention CTXxB (32768x8), matvec KIND:ROWSxCOLS:B "
+                         "(q8_0:128256x4096:1), gemm tensor name (blk.0.ffn_up.weight)")
+    ap.add_argument("--tokens", type=int, default=512, help="--workload gemm: tokens per product")
     ap.add_argument("--batch", type=int, default=1,
                     help="> 1: batched greedy decode of that many sequences (qwen05b / llama3-8b workloads)")
     ap.add_argument("--graph", action="store_true", help="--batch: replay each step from a captured CUDA graph")
@@ -695,6 +792,8 @@ def main():
         run_matvec(args)
     elif args.workload == "attention":
         run_attention(args)
+    elif args.workload == "gemm":
+        run_gemm(args)
     elif args.batch > 1:
         run_batch(args)
     else:

@@ -201,7 +201,9 @@ int b2_model_matvec(const b2_model* m, const char* name, const float* x, float* 
  * Local-LLM/include/tensor.h:354-387 mat_mat_mul_tensor (Transformer::
  * forward_batch, Local-LLM/src/transformer.cpp:540-575).  Asynchronous on
  * `stream` (NULL = the model's stream), with a per-(device, stream) scratch
- * grown by cudaMalloc when a call needs more. */
+ * grown by cudaMalloc when a call needs more.  The gate and up matrices,
+ * stored interleaved, are computed whole and their half gathered (a buffer
+ * of ntok x 2 x rows floats allocated on the stream for the call). */
 int b2_model_gemm(const b2_model* m, const char* name, const float* x, float* y, int32_t ntok, void* stream);
 
 /* transformer.go:663-685 attention of one query token per sequence over an

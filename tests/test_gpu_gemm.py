@@ -66,6 +66,8 @@ def test_gemm_over_resident_tiled_weights(built_lib, torch_cuda, write_model, ke
             "blk.0.attn_output.weight": (H, qd), "blk.0.ffn_down.weight": (H, ff), "token_embd.weight": (V, H)}
     if not shape.tied:
         dims["output.weight"] = (V, H)
+    dims["blk.0.ffn_gate.weight"] = (ff, H)  # the two halves of the interleaved resident matrix
+    dims["blk.0.ffn_up.weight"] = (ff, H)
     rng = np.random.default_rng(11)
     for name, (rows, cols) in dims.items():
         w = m.dequant(name, rows * cols).reshape(rows, cols)
