@@ -45,6 +45,12 @@ class LoadOpts(C.Structure):
                 ("tp_rank", C.c_int32), ("reserved2", C.c_int32)]
 
 
+class LoadStats(C.Structure):
+    _fields_ = [("total_ns", C.c_int64), ("parse_ns", C.c_int64), ("upload_ns", C.c_int64),
+                ("host_copy_ns", C.c_int64), ("bytes_uploaded", C.c_int64), ("host_threads", C.c_int32),
+                ("mapped", C.c_int32)]
+
+
 class Config(C.Structure):
     _fields_ = [("arch", C.c_char * 32), ("vocab_size", C.c_int32), ("hidden_size", C.c_int32),
                 ("intermediate_size", C.c_int32), ("num_layers", C.c_int32), ("num_heads", C.c_int32),
@@ -88,6 +94,7 @@ SIGNATURES = {
     "b2_load": (C.c_int, [C.c_char_p, C.POINTER(LoadOpts), C.POINTER(_P)]),
     "b2_free": (None, [_P]),
     "b2_get_config": (C.c_int, [_P, C.POINTER(Config)]),
+    "b2_get_load_stats": (C.c_int, [_P, C.POINTER(LoadStats)]),
     "b2_last_error": (C.c_char_p, []),
     "b2_reset": (C.c_int, [_P]),
     "b2_cache_len": (C.c_int, [_P, _i32p]),
@@ -99,6 +106,8 @@ SIGNATURES = {
     "b2_stream_begin": (C.c_int, [_P, _i32p, _i32, C.POINTER(SampleOpts), _i32p, _i32]),
     "b2_stream_next": (C.c_int, [_P, _i32p, _i32p]),
     "b2_sample_logits": (C.c_int32, [_f32p, _i32, C.POINTER(SampleOpts), _i32p, _i32, C.c_float]),
+    "b2_sample_device": (C.c_int, [_P, _i32, _i32, _i64, C.POINTER(SampleOpts), _P, _i64, _i32p, _f32p, _P, _P, _P]),
+    "b2_sample_scratch_bytes": (_i64, [_i32, _i32]),
     "b2_embed": (C.c_int, [_P, _i32p, _i32, _f32p]),
     "b2_dequant_tensor": (C.c_int, [_P, C.c_char_p, _f32p, _i64, C.POINTER(_i64)]),
     "b2_matvec": (C.c_int, [_i32, _P, _P, _P, _i32, _i32, _P]),
@@ -176,6 +185,12 @@ class Model:
         self.cfg = {k: getattr(c, k) for k, _ in Config._fields_}
         self.cfg["arch"] = c.arch.decode()
         self.vocab = c.vocab_size
+
+    def load_stats(self) -> dict:
+        """b2_get_load_stats: where the load's time went."""
+        s = LoadStats()
+        _check(lib().b2_get_load_stats(self._h, C.byref(s)))
+        return {k: getattr(s, k) for k, _ in LoadStats._fields_}
 
     def tp_handle(self) -> bytes:
         """64-byte IPC handle of this rank's exchange buffer."""
@@ -323,6 +338,23 @@ def sample_logits(logits, opts: SampleOpts, generated=(), r: float = 0.5) -> int
     g, gp = _ids(list(generated) or [0])
     return int(lib().b2_sample_logits(lg.ctypes.data_as(_f32p), lg.size, C.byref(opts), gp, len(generated),
                                       float(r)))
+
+
+def sample_scratch_bytes(n: int, rows: int) -> int:
+    """Device scratch b2_sample_device needs for rows rows of n logits."""
+    return int(lib().b2_sample_scratch_bytes(n, rows))
+
+
+def sample_device(d_logits: int, n: int, rows: int, ld: int, opts: SampleOpts, d_generated: int = 0,
+                  gen_ld: int = 0, n_generated=None, r=(0.5,), d_scratch: int = 0, d_out: int = 0,
+                  stream: int = 0) -> None:
+    """b2_sample_device on device pointers (logits modified in place; d_scratch
+    of sample_scratch_bytes(n, rows) bytes); the ids land in d_out[rows] on
+    `stream`."""
+    ng = (C.c_int32 * rows)(*(list(n_generated) if n_generated is not None else [0] * rows))
+    rr = (C.c_float * rows)(*[float(x) for x in r])
+    _check(lib().b2_sample_device(d_logits, n, rows, ld, C.byref(opts), d_generated or None, gen_ld,
+                                  C.cast(ng, _i32p), C.cast(rr, _f32p), d_scratch or None, d_out, stream or None))
 
 
 class Batch:

@@ -9,7 +9,9 @@
 #include <string>
 #include <vector>
 
+#include "gemm.h"
 #include "model.h"
+#include "sample.h"
 
 int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std::string* err);
 void b2_free_impl(b2_model* m);
@@ -19,10 +21,6 @@ int b2_matvec_batch_impl(int qtype, const void* w, const float* x, float* y, int
                          cudaStream_t s, std::string* err);
 int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
-int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
-                       float* y, int ntok, cudaStream_t s, std::string* err);
-int b2_tiled_gemm_half_impl(int qtype, const void* base, int64_t rp, int half, int rows, int cols, const float* x,
-                            float* y, int ntok, cudaStream_t s, std::string* err);
 int b2_batch_create_impl(b2_model* m, int B, b2_batch** out, std::string* err);
 void b2_batch_free_impl(b2_batch* bt);
 int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, int32_t* next_out, std::string* err);
@@ -140,7 +138,19 @@ bool is_greedy(const b2_sample_opts& o) {
 
 float uniform01(std::mt19937_64& g) { return (float)((g() >> 40) * (1.0 / 16777216.0)); }
 
-// One engine step on host logits: copy logits back, sample.
+// The options as transformer.go:981-1004 decides them, for the device sampler.
+void sample_opts_to_args(const b2_sample_opts& o, b2::SampleArgs* a) {
+    const double temp = o.temperature <= 0 ? 1.0 : o.temperature;
+    a->greedy = temp < 0.01 ? 1 : 0;
+    a->temp = (float)temp;
+    a->pen = o.repeat_penalty > 1 ? (float)o.repeat_penalty : 0.0f;
+    a->top_k = o.top_k;
+    a->top_p = (o.top_p > 0 && o.top_p < 1) ? (float)o.top_p : 0.0f;
+}
+
+// One engine step's sample, on the device (sample.cu): the logits stay in
+// HBM, the ids generated so far are kept in d_gen (the kernel appends the
+// one it draws), and 4 bytes come back.
 int sample_from_device(b2_model* m, const b2_sample_opts& o, const std::vector<int32_t>& generated, int32_t* next,
                        std::string* err) {
     const int V = m->cfg.vocab_size;
@@ -148,11 +158,27 @@ int sample_from_device(b2_model* m, const b2_sample_opts& o, const std::vector<i
         *err = "sampling needs the whole vocabulary's logits: greedy only on a tensor-parallel model";
         return B2_ERR_BAD_ARG;
     }
-    if (!cuda_ok(cudaMemcpyAsync(m->h_logits, m->dev.logits, sizeof(float) * V, cudaMemcpyDeviceToHost, m->stream), err))
-        return B2_ERR_CUDA;
-    int rc = sync_and_check(m, err);
+    b2::SampleArgs a{};
+    sample_opts_to_args(o, &a);
+    a.logits = m->dev.logits;
+    a.ld = V;
+    a.n = V;
+    a.scratch = m->d_sample_ws;
+    a.err = m->dev.err;
+    a.gen = m->d_gen;
+    a.gen_ld = m->dev.max_seq;
+    a.gen_append = m->d_gen;
+    a.gen_cap = m->dev.max_seq;
+    a.out = m->d_sample_out;
+    a.ngen[0] = (int)std::min<size_t>(generated.size(), (size_t)m->dev.max_seq);
+    a.r[0] = uniform01(m->st.rng);
+    int rc = b2::launch_sample(a, 1, m->stream, err);
     if (rc) return rc;
-    *next = sample_impl(m->h_logits, V, o, generated.data(), (int32_t)generated.size(), uniform01(m->st.rng));
+    if (!cuda_ok(cudaMemcpyAsync(m->h_pinned, m->d_sample_out, sizeof(int32_t), cudaMemcpyDeviceToHost, m->stream), err))
+        return B2_ERR_CUDA;
+    rc = sync_and_check(m, err);
+    if (rc) return rc;
+    *next = m->h_pinned[0];
     return B2_OK;
 }
 
@@ -188,6 +214,13 @@ int b2_get_config(const b2_model* m, b2_config* out) {
     if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
     if (!out) return ret(B2_ERR_BAD_ARG, "null argument");
     *out = m->cfg;
+    return B2_OK;
+}
+
+int b2_get_load_stats(const b2_model* m, b2_load_stats* out) {
+    if (!m) return ret(B2_ERR_NOT_LOADED, "no model loaded");
+    if (!out) return ret(B2_ERR_BAD_ARG, "null argument");
+    *out = m->load;
     return B2_OK;
 }
 
@@ -246,6 +279,33 @@ int32_t b2_sample_logits(float* logits, int32_t n, const b2_sample_opts* opts, c
     if (!logits || n <= 0) return -1;
     b2_sample_opts o = opts ? *opts : default_opts();
     return sample_impl(logits, n, o, generated, generated ? n_generated : 0, r);
+}
+
+int64_t b2_sample_scratch_bytes(int32_t n, int32_t rows) {
+    if (n <= 0 || rows <= 0 || rows > b2::kSampleMaxRows) return -1;
+    return (int64_t)b2::sample_scratch_bytes(n, rows);
+}
+
+int b2_sample_device(float* d_logits, int32_t n, int32_t rows, int64_t ld, const b2_sample_opts* opts,
+                     const int32_t* d_generated, int64_t gen_ld, const int32_t* n_generated, const float* r,
+                     void* d_scratch, int32_t* d_out, void* stream) {
+    if (!d_logits || !d_out || !r || !d_scratch || n <= 0 || rows <= 0 || rows > b2::kSampleMaxRows || ld < n)
+        return ret(B2_ERR_BAD_ARG, "b2_sample_device: bad argument");
+    b2::SampleArgs a{};
+    sample_opts_to_args(opts ? *opts : default_opts(), &a);
+    a.logits = d_logits;
+    a.ld = ld;
+    a.n = n;
+    a.scratch = static_cast<unsigned char*>(d_scratch);
+    a.gen = d_generated;
+    a.gen_ld = gen_ld;
+    a.out = d_out;
+    for (int i = 0; i < rows; i++) {
+        a.ngen[i] = (d_generated && n_generated) ? std::max(0, n_generated[i]) : 0;
+        a.r[i] = r[i];
+    }
+    std::string err;
+    return ret(b2::launch_sample(a, rows, static_cast<cudaStream_t>(stream), &err), err);
 }
 
 int b2_predict(b2_model* m, const int32_t* prompt, int32_t n_prompt, const b2_sample_opts* opts,

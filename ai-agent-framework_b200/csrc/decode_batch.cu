@@ -25,14 +25,11 @@
 
 #include "../../include/b2decode.h"
 #include "dev.cuh"
+#include "gemm.h"
 #include "model.h"
 
 int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
                                const float* x, float* y, int nvec, cudaStream_t s, std::string* err);
-int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
-                       float* y, int ntok, cudaStream_t s, std::string* err);
-int b2_gemm_status(cudaStream_t s);
-unsigned long long b2_gemm_scratch_generation(cudaStream_t s);
 unsigned long long b2_mvb_scratch_generation(cudaStream_t s);
 int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, float* part, size_t part_floats,
                              float* out, int batch, int nh, int nkv, int hd, const int* lens, int add, int stride,
@@ -52,6 +49,9 @@ struct b2_batch {
     __half* vc = nullptr;
     float *x = nullptr, *xn = nullptr, *y = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr;
     float *gu = nullptr, *act = nullptr, *logits = nullptr, *part = nullptr;
+    __half* xh = nullptr;   // [kPrefillChunk + 16][max(H, FF)]: a product's input in the GEMM's fp16 form
+    float* tsc = nullptr;   // [kPrefillChunk + 16] its per-token scales
+    int xh_ld = 0;
     size_t part_floats = 0;
     int *d_pos = nullptr, *d_tok = nullptr, *d_next = nullptr;  // [kBatchMax]
     int* d_ppos = nullptr;                                      // [kBatchMax] prefill chunk positions
@@ -142,11 +142,147 @@ __global__ void __launch_bounds__(kNormThreads) bd_rmsnorm_kernel(const float* _
     }
 }
 
+// The GEMM's input form of one token's row (gemm.h): scaled by 2^e so the
+// largest magnitude lies in [2^14, 2^15), fp16, scale 2^-e.  mx is the
+// row's largest magnitude (the CTA's reduction).
+__device__ __forceinline__ float f16_row_up(float mx, float* scale_out) {
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+        int ex;
+        frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
+        e = 15 - ex;
+    }
+    if (threadIdx.x == 0) *scale_out = ldexpf(1.0f, -e);
+    return ldexpf(1.0f, e);
+}
+__device__ __forceinline__ void st_f16x4(__half* p, float4 v, float up) {
+    const __half2 a = __floats2half2_rn(v.x * up, v.y * up), b = __floats2half2_rn(v.z * up, v.w * up);
+    *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+}
+__device__ float block_max512(float v, float* red) {
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();  // (red may still be read by a previous reduction)
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = red[0];
+#pragma unroll
+    for (int i = 1; i < kNormThreads / 32; i++) v = fmaxf(v, red[i]);
+    return v;
+}
+
+// The residual update and the next RMSNorm in one pass per row: x += the
+// split-K partials of the product that ends the sub-block (k planes, summed
+// in plane order, then added: as a separate sum and add would), then
+// transformer.go:922-932 rmsNorm of the new x written in the GEMM's input
+// form (xh row, scale) for the next product, and as fp32 into xn when xn is
+// given.  One CTA of kNormThreads per row; H a multiple of 4, at most
+// 4 * kNormVec * kNormThreads.
+__global__ void __launch_bounds__(kNormThreads) bd_add_norm_f16_kernel(float* __restrict__ x, const float* __restrict__ part,
+                                                                        int k, size_t plane, const float* __restrict__ w,
+                                                                        int H, float eps, __half* __restrict__ xh,
+                                                                        int xh_ld, float* __restrict__ tsc,
+                                                                        float* __restrict__ xn) {
+    __shared__ float red[kNormThreads / 32];
+    __shared__ float rs;
+    const int b = blockIdx.x, n4 = H / 4;
+    float4* xb = reinterpret_cast<float4*>(x + (size_t)b * H);
+    const float4* wv = reinterpret_cast<const float4*>(w);
+    float4 v[kNormVec];
+    float ss = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < kNormVec; kk++) {
+        const int i = threadIdx.x + kk * kNormThreads;
+        v[kk] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < n4) {
+            float4 u = xb[i];
+            if (k > 0) {
+                const float4* pp = reinterpret_cast<const float4*>(part + (size_t)b * H) + i;
+                float4 sum = __ldcg(pp);
+                for (int s = 1; s < k; s++) {
+                    const float4 t = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pp) + s * plane));
+                    sum.x += t.x; sum.y += t.y; sum.z += t.z; sum.w += t.w;
+                }
+                u.x += sum.x; u.y += sum.y; u.z += sum.z; u.w += sum.w;
+                xb[i] = u;
+            }
+            v[kk] = u;
+        }
+        ss = fmaf(v[kk].x, v[kk].x, fmaf(v[kk].y, v[kk].y, fmaf(v[kk].z, v[kk].z, fmaf(v[kk].w, v[kk].w, ss))));
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int i = 0; i < kNormThreads / 32; i++) t += red[i];
+        rs = (float)(1.0 / sqrt((double)(t / (float)H) + (double)eps));
+    }
+    __syncthreads();
+    const float r = rs;
+    float mx = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < kNormVec; kk++) {
+        const int i = threadIdx.x + kk * kNormThreads;
+        if (i < n4) {
+            const float4 gg = __ldg(wv + i);
+            v[kk] = make_float4(v[kk].x * r * gg.x, v[kk].y * r * gg.y, v[kk].z * r * gg.z, v[kk].w * r * gg.w);
+            if (xn) reinterpret_cast<float4*>(xn + (size_t)b * H)[i] = v[kk];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[kk].x), fabsf(v[kk].y)), fmaxf(fabsf(v[kk].z), fabsf(v[kk].w))));
+        }
+    }
+    mx = block_max512(mx, red);
+    const float up = f16_row_up(mx, tsc + b);
+#pragma unroll
+    for (int kk = 0; kk < kNormVec; kk++) {
+        const int i = threadIdx.x + kk * kNormThreads;
+        if (i < n4) st_f16x4(xh + (size_t)b * xh_ld + 4 * i, v[kk], up);
+    }
+}
+
+// transformer.go:725-727, 954-956 SwiGLU over the split-K partials of the
+// interleaved gate/up product (output j of tile t: gate at row 16t + j % 8,
+// up 8 rows below), written in the GEMM's input form for the down product.
+// One CTA of kNormThreads per row, the row's activations kept in registers
+// (FF up to kSwigluVec * kNormThreads).
+constexpr int kSwigluVec = 32;
+__global__ void __launch_bounds__(kNormThreads) bd_swiglu_f16_kernel(const float* __restrict__ part, int k, size_t plane,
+                                                                      int FF, __half* __restrict__ xh, int xh_ld,
+                                                                      float* __restrict__ tsc) {
+    __shared__ float red[kNormThreads / 32];
+    const int b = blockIdx.x;
+    const float* row = part + (size_t)b * 2 * FF;
+    float act[kSwigluVec];
+    float mx = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < kSwigluVec; kk++) {
+        const int j = threadIdx.x + kk * kNormThreads;
+        act[kk] = 0.0f;
+        if (j < FF) {
+            const size_t o = (size_t)(j >> 3) * 16 + (j & 7);
+            float gv = __ldcg(row + o), uv = __ldcg(row + o + 8);
+            for (int s = 1; s < k; s++) {
+                gv += __ldcg(row + s * plane + o);
+                uv += __ldcg(row + s * plane + o + 8);
+            }
+            act[kk] = gv / (1.0f + expf(-gv)) * uv;
+            mx = fmaxf(mx, fabsf(act[kk]));
+        }
+    }
+    mx = block_max512(mx, red);
+    const float up = f16_row_up(mx, tsc + b);
+#pragma unroll
+    for (int kk = 0; kk < kSwigluVec; kk++) {
+        const int j = threadIdx.x + kk * kNormThreads;
+        if (j < FF) xh[(size_t)b * xh_ld + j] = __float2half_rn(act[kk] * up);
+    }
+}
+
 // transformer.go:632-656: bias, RoPE on interleaved pairs of every q and k
 // head at the row's position (936-951, the model's cos / sin table), then k
 // and v appended to the row's cache slot (rows slot_stride positions apart;
 // 0 when all rows are tokens of one sequence); q kept for attention.
-__global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, const float* __restrict__ bias,
+// The q / k / v rows are the sum of k split-K planes (plane floats apart).
+__global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, int k, size_t plane, const float* __restrict__ bias,
                                   const float* __restrict__ cosT, const float* __restrict__ sinT,
                                   const int* __restrict__ pos, float* __restrict__ q, __half* __restrict__ kc,
                                   __half* __restrict__ vc, int qd, int kvd, int hd, int slot_stride) {
@@ -154,7 +290,13 @@ __global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, const float* __
     const float* row = qkv + (size_t)b * n;
     for (int j = threadIdx.x; j < n / 2; j += blockDim.x) {
         const int r = 2 * j;
-        float a0 = row[r], a1 = row[r + 1];
+        float2 a = __ldcg(reinterpret_cast<const float2*>(row + r));
+        for (int s = 1; s < k; s++) {
+            const float2 t = __ldcg(reinterpret_cast<const float2*>(row + s * plane + r));
+            a.x += t.x;
+            a.y += t.y;
+        }
+        float a0 = a.x, a1 = a.y;
         if (bias) {
             a0 += bias[r];
             a1 += bias[r + 1];
@@ -335,6 +477,9 @@ int batch_create(b2_model* m, int B, bool model_cache, b2_batch** out, std::stri
     const size_t o_lg = take((size_t)kBatchMax * d.V * 4), o_part = take(bt->part_floats * 4);
     const size_t o_pos = take(R * 4), o_tok = take(R * 4), o_next = take(R * 4), o_ppos = take(R * 4);
     const size_t o_argv = take((size_t)kBatchMax * kArgParts * 4), o_argi = take((size_t)kBatchMax * kArgParts * 4);
+    // (rows past a pass's tokens are read by the GEMM's last N tile, never used)
+    const int xh_rows = kPrefillChunk + 16, xh_ld = std::max(d.H, d.FF);
+    const size_t o_xh = take((size_t)xh_rows * xh_ld * 2), o_tsc = take((size_t)xh_rows * 4);
     if (cudaMalloc(&bt->arena, off) != cudaSuccess) {
         delete bt;
         *err = "device allocation of the batch state failed";
@@ -365,6 +510,9 @@ int batch_create(b2_model* m, int B, bool model_cache, b2_batch** out, std::stri
     bt->d_ppos = reinterpret_cast<int*>(A + o_ppos);
     bt->arg_v = reinterpret_cast<float*>(A + o_argv);
     bt->arg_i = reinterpret_cast<int*>(A + o_argi);
+    bt->xh = reinterpret_cast<__half*>(A + o_xh);
+    bt->tsc = reinterpret_cast<float*>(A + o_tsc);
+    bt->xh_ld = xh_ld;
     if (!ok(cudaMemsetAsync(bt->arena, 0, off, m->stream), err, "clear") ||
         !ok(cudaStreamSynchronize(m->stream), err, "clear")) {
         cudaFreeHost(bt->h_io);
@@ -419,8 +567,75 @@ unsigned long long scratch_generation(cudaStream_t s) {
 // With all_logits the lm_head and argmax run for every row (d_next[r],
 // d_rpos[r] moved on by one); otherwise for the last row only, into logits
 // row 0 and d_next[0] (a prefill chunk needs the argmax after its last token).
+// The tensor-core form of forward_rows (every width a multiple of 64, at
+// least kGemmMinRows rows): each product takes its input in the GEMM's fp16
+// form from the kernel before it and leaves its split-K partials to the
+// kernel after it, which sums them: per layer the residual add, RMSNorm and
+// conversion are one launch (bd_add_norm_f16), the q/k/v sum rides in the
+// RoPE launch and the gate/up sum in the SwiGLU launch.
+bool tc_rows_ok(const ModelDev& d, int R) {
+    return R >= kGemmMinRows && R <= kPrefillChunk && d.H % 64 == 0 && d.qd % 64 == 0 && d.FF % 64 == 0 &&
+           d.H <= 4 * kNormVec * kNormThreads && d.FF <= kSwigluVec * kNormThreads;
+}
+
+int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err,
+                    bool all_logits) {
+    b2_model* m = bt->m;
+    const ModelDev& d = m->dev;
+    cudaStream_t s = m->stream;
+    const int H = d.H, qt = d.qtype, n_qkv = d.qd + 2 * d.kvd, ld = bt->xh_ld;
+    bd_embed_kernel<<<R, kBdThreads, 0, s>>>(d.tok_embd, d.Vemb, d.Vp_emb, H, qt, bt->d_tok, bt->x);
+    const size_t kv_layer = (size_t)bt->B * bt->max_seq * d.kvd;
+    GemmParts prev;  // the partials still to be added to x (none before layer 0)
+    int rc = B2_OK;
+    for (int l = 0; l < d.L && rc == B2_OK; l++) {
+        const LayerDev& lw = m->layers_host[l];
+        bd_add_norm_f16_kernel<<<R, kNormThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, lw.attn_norm, H, d.eps,
+                                                          bt->xh, ld, bt->tsc, nullptr);
+        GemmParts p;
+        rc = b2_tiled_gemm_f16_impl(qt, lw.wqkv, tiled_rows(n_qkv), 0, n_qkv, H, bt->xh, bt->tsc, R, bt->qkv, &p, s, err);
+        if (rc) break;
+        __half* kc = bt->kc + (size_t)l * kv_layer + kv_off;
+        __half* vc = bt->vc + (size_t)l * kv_layer + kv_off;
+        bd_rope_kv_kernel<<<R, kBdThreads, 0, s>>>(p.p, p.k, p.plane, lw.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc,
+                                                   vc, d.qd, d.kvd, d.hd, slot_stride);
+        rc = b2_attention_seqs_launch(bt->q, kc, vc, bt->part, bt->part_floats, bt->att, R, d.nh, d.nkv, d.hd, d_rpos,
+                                      1, slot_stride, max_len, m->grid, s);
+        if (rc) {
+            *err = "batched attention launch failed";
+            break;
+        }
+        rc = b2_tiled_gemm_impl(qt, lw.wo, tiled_rows(H), 0, H, d.qd, bt->att, bt->y, R, &p, s, err);
+        if (rc) break;
+        bd_add_norm_f16_kernel<<<R, kNormThreads, 0, s>>>(bt->x, p.p, p.k, p.plane, lw.ffn_norm, H, d.eps, bt->xh, ld,
+                                                          bt->tsc, nullptr);
+        rc = b2_tiled_gemm_f16_impl(qt, lw.wgu, tiled_rows(2 * d.FF), 0, 2 * d.FF, H, bt->xh, bt->tsc, R, bt->gu, &p, s,
+                                    err);
+        if (rc) break;
+        bd_swiglu_f16_kernel<<<R, kNormThreads, 0, s>>>(p.p, p.k, p.plane, d.FF, bt->xh, ld, bt->tsc);
+        rc = b2_tiled_gemm_f16_impl(qt, lw.wd, tiled_rows(H), 0, H, d.FF, bt->xh, bt->tsc, R, bt->y, &prev, s, err);
+    }
+    if (rc) return rc;
+    // the last down product's partials, the output norm: fp32 rows in xn (for
+    // a one-row lm_head on the batched matvec) and the GEMM's form in xh
+    bd_add_norm_f16_kernel<<<R, kNormThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, d.out_norm, H, d.eps, bt->xh,
+                                                      ld, bt->tsc, bt->xn);
+    const int r_lm = all_logits ? 0 : R - 1, n_lm = all_logits ? R : 1;
+    if (n_lm >= kGemmMinRows)
+        rc = b2_tiled_gemm_f16_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xh + (size_t)r_lm * ld, bt->tsc + r_lm, n_lm,
+                                    bt->logits, nullptr, s, err);
+    else
+        rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn + (size_t)r_lm * H, bt->logits, n_lm, s,
+                                        err);
+    if (rc) return rc;
+    bd_argmax_part_kernel<<<n_lm * kArgParts, kBdThreads, 0, s>>>(bt->logits, d.V, bt->arg_v, bt->arg_i);
+    bd_argmax_final_kernel<<<n_lm, 32, 0, s>>>(bt->arg_v, bt->arg_i, d.V, bt->d_next, d_rpos + r_lm);
+    return ok(cudaGetLastError(), err, "batched decode launch") ? B2_OK : B2_ERR_CUDA;
+}
+
 int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err,
                  bool all_logits = true) {
+    if (tc_rows_ok(bt->m->dev, R)) return forward_rows_tc(bt, R, d_rpos, kv_off, slot_stride, max_len, err, all_logits);
     b2_model* m = bt->m;
     const ModelDev& d = m->dev;
     cudaStream_t s = m->stream;
@@ -437,7 +652,7 @@ int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_strid
         if (rc) break;
         __half* kc = bt->kc + (size_t)l * kv_layer + kv_off;
         __half* vc = bt->vc + (size_t)l * kv_layer + kv_off;
-        bd_rope_kv_kernel<<<R, kBdThreads, 0, s>>>(bt->qkv, ld.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc, vc,
+        bd_rope_kv_kernel<<<R, kBdThreads, 0, s>>>(bt->qkv, 1, 0, ld.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc, vc,
                                                    d.qd, d.kvd, d.hd, slot_stride);
         rc = b2_attention_seqs_launch(bt->q, kc, vc, bt->part, bt->part_floats, bt->att, R, d.nh, d.nkv, d.hd, d_rpos,
                                       1, slot_stride, max_len, m->grid, s);

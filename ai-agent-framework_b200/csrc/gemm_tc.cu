@@ -45,11 +45,13 @@
 
 #include "../../include/b2decode.h"
 #include "dev.cuh"
+#include "gemm.h"
 
 namespace b2 {
 namespace {
 
-constexpr int kGemmThreads = 192;       // 6 warps: producer, MMA, 4 dequant / epilogue
+constexpr int kDqWarps = 8;             // dequantising / epilogue warps: two per TMEM lane quadrant
+constexpr int kGemmThreads = 64 + 32 * kDqWarps;  // + producer warp, MMA warp
 constexpr int kBM = 128;                // weight rows per CTA (MMA M)
 constexpr int kStageBlocks = 2;         // Q blocks (of 32) per K stage: 64 elements
 constexpr int kMaxKSplit = 8;
@@ -63,22 +65,39 @@ struct QShape {
     static constexpr int kRawS = kBM / kTileRows * kStageBlocks * kTileRows * 2;   // scales of a stage
 };
 
-// Shared-memory plan of one CTA (byte offsets from a 1024-aligned base).
+// Shared-memory plan of one CTA (byte offsets from a 1024-aligned base): a
+// deep ring of raw stages (the activation tile and the raw quant and scale
+// blocks of one K stage, filled by TMA) and a double-buffered dequantised A
+// tile.  The raw stages are what is in flight from HBM, so that ring is as
+// deep as shared memory allows.  The dequantised A tiles (16 KB of fp16 a
+// stage, four times the Q4_0 bytes they come from) never touch shared
+// memory: the dequantising warps store them into tensor memory, where the
+// MMA reads its A operand, in a ring four deep so they run ahead of the
+// MMA's round trip (issue, completion, commit).
 template <int QT, int BN>
 struct GemmSmem {
     static constexpr int kA = kBM * 128;  // fp16, 128 rows x 64 K, 128-byte swizzle
     static constexpr int kB = BN * 128;   // fp16, BN rows x 64 K
-    // (a multiple of 1024, so every stage's A and B tiles stay 1024-aligned)
-    static constexpr int kStage = (kA + kB + QShape<QT>::kRawQ + QShape<QT>::kRawS + 1023) & ~1023;
+    // raw slot [B | raw q | raw s], a multiple of 1024 so each B tile stays 1024-aligned
+    static constexpr int kSlot = (kB + QShape<QT>::kRawQ + QShape<QT>::kRawS + 1023) & ~1023;
+    static constexpr int kAStages = 4;
     static constexpr int kFixed = 2048;  // alignment slack, then barriers and the TMEM slot
-    // the decode-step forms (BN <= 32: the stage is mostly the dequantised A
-    // tile) run two CTAs per SM on a 4-stage ring, so twice the warps decode
-    // weights; the prefill forms one CTA with as many stages as fit (<= 8)
+    // the decode-step forms (BN <= 32) run two CTAs per SM, so twice the
+    // warps decode weights; the prefill forms one CTA
     static constexpr int kCtas = BN <= 32 ? 2 : 1;
-    static constexpr int kFit = (kGemmSmemMax / kCtas - kFixed) / kStage;
-    static constexpr int kStages = kCtas == 2 ? (kFit < 4 ? kFit : 4) : (kFit > 8 ? 8 : kFit);
-    static_assert(kStages >= 2, "a K stage must fit twice");
-    static constexpr int kTotal = kFixed + kStages * kStage;
+    // per CTA: the opt-in maximum, or an equal share of the SM's 228 KB less
+    // the 1 KB the hardware reserves per resident CTA
+    static constexpr int kBudget = kCtas == 1 ? kGemmSmemMax : 233472 / kCtas - 1024;
+    static constexpr int kFit = (kBudget - kFixed) / kSlot;
+    static constexpr int kStages = kFit > 24 ? 24 : kFit;  // raw stages
+    static_assert(kStages >= 2, "two raw stages must fit");
+    static constexpr int kTotal = kFixed + kStages * kSlot;
+    // tensor memory: the accumulator (BN columns, at least 32), then the A
+    // ring (32 columns a stage: 128 lanes x 64 fp16); 256 columns in all, so
+    // two CTAs of an SM fit its 512
+    static constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;
+    static constexpr uint32_t kTmemCols = 256;
+    static_assert(kAccCols + 32 * kAStages <= kTmemCols && kCtas * kTmemCols <= 512, "tensor memory plan");
 };
 
 struct GemmArgs {
@@ -142,6 +161,16 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_
         : "memory");
 }
 
+// A from tensor memory (M = 128 lanes, K = 16: 8 columns), B from shared memory.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -174,21 +203,34 @@ __device__ __forceinline__ void u4x4_to_h2(uint32_t w, __half2& lo, __half2& hi)
     hi = __hsub2(*reinterpret_cast<const __half2*>(&b), off);
 }
 
-// Row r (0..127) of a stage: its two Q blocks -> 64 fp16 (d * q) into the
-// swizzled A tile (16-byte chunk c of row r at chunk position c ^ (r & 7)).
-template <int QT>
-__device__ __forceinline__ void dequant_row(const uint8_t* rawq, const uint8_t* raws, uint8_t* a_tile, int r) {
+// 16 consecutive 32-bit tensor-memory columns of this thread's lane (one
+// lane per thread of the warp, the warp's 32-lane quadrant in taddr).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// Row r (0..127) of a stage: Q blocks kb0 .. kb0 + NKB - 1 of its two -> 32
+// fp16 (d * q) each, written to the row's tensor-memory lane as the A operand
+// of the MMA: element k of the stage in column k / 2 (low half for even k)
+// from the stage's first column a_col.
+template <int QT, int NKB>
+__device__ __forceinline__ void dequant_row(const uint8_t* rawq, const uint8_t* raws, uint32_t a_col, int r, int kb0) {
     constexpr int QB = QShape<QT>::QB;
     const int t = r >> 4, rr = r & 15;
-    uint8_t* arow = a_tile + r * 128;
 #pragma unroll
-    for (int kb = 0; kb < kStageBlocks; kb++) {
+    for (int kk = 0; kk < NKB; kk++) {
+        const int kb = kb0 + kk;
         // TMA box layout: [tile][block][16 rows][QB]; scales [tile][block][16] in (g, g + 8) order
         const uint8_t* q = rawq + ((t * kStageBlocks + kb) * kTileRows + rr) * QB;
         const uint16_t dbits =
             *reinterpret_cast<const uint16_t*>(raws + ((t * kStageBlocks + kb) * kTileRows + 2 * (rr & 7) + (rr >> 3)) * 2);
         const __half2 d2 = __halves2half2(__ushort_as_half(dbits), __ushort_as_half(dbits));
-        uint32_t w[8];
+        uint32_t w[8], out[16];
         if (QT == 8) {
             // rows with bit 2 set hold their two 16-byte halves swapped
             const uint4 h0 = *reinterpret_cast<const uint4*>(q + ((rr & 4) ? 16 : 0));
@@ -213,10 +255,12 @@ __device__ __forceinline__ void dequant_row(const uint8_t* rawq, const uint8_t* 
                 u4x4_to_h2(w[2 * c + 1], h[2], h[3]);
             }
 #pragma unroll
-            for (int i = 0; i < 4; i++) h[i] = __hmul2(h[i], d2);
-            const int chunk = kb * 4 + c;
-            *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = *reinterpret_cast<const uint4*>(h);
+            for (int i = 0; i < 4; i++) {
+                h[i] = __hmul2(h[i], d2);
+                out[4 * c + i] = *reinterpret_cast<const uint32_t*>(&h[i]);
+            }
         }
+        tmem_st16(a_col + (uint32_t)(16 * kb), out);  // block kb: columns 16 kb .. 16 kb + 15
     }
 }
 
@@ -228,11 +272,13 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
     constexpr int NS = SM::kStages;
     extern __shared__ __align__(1024) uint8_t gsm_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = base + 1024;  // [NS][A | B | raw q | raw s], A and B 1024-aligned
-    uint64_t* full = reinterpret_cast<uint64_t*>(base);
-    uint64_t* adone = full + NS;
-    uint64_t* empty = adone + NS;
-    uint64_t* accum = empty + NS;
+    constexpr int NA = SM::kAStages;
+    uint8_t* rawr = base + 1024;  // [NS][B | raw q | raw s]
+    uint64_t* full = reinterpret_cast<uint64_t*>(base);  // raw stage landed (TMA)
+    uint64_t* rempty = full + NS;                        // raw stage free (MMA done with its B)
+    uint64_t* afull = rempty + NS;                       // [NA] A tile decoded
+    uint64_t* aempty = afull + NA;                       // [NA] A tile free (MMA done)
+    uint64_t* accum = aempty + NA;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -240,13 +286,16 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
     const int mt = blockIdx.x, nt = blockIdx.y, ks = blockIdx.z;
     const int st0 = ks * a.kst_split;
     const int nst = max(0, min(a.kst_split, a.nst - st0));
-    constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+    constexpr uint32_t kTmemCols = SM::kTmemCols;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&adone[s], 4);
-            mbar_init(&empty[s], 1);
+            mbar_init(&rempty[s], 1);
+        }
+        for (int j = 0; j < NA; j++) {
+            mbar_init(&afull[j], kDqWarps);
+            mbar_init(&aempty[j], 1);
         }
         mbar_init(accum, 1);
         *abort_flag = 0;
@@ -270,15 +319,15 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
             int issued = 0;
             for (int it = 0; it < nst; it++) {
                 const int s = it % NS;
-                if (it >= NS && !gemm_wait(&empty[s], ((it / NS) - 1) & 1, a.err, abort_flag)) break;
-                uint8_t* st = stages + (size_t)s * SM::kStage;
+                if (it >= NS && !gemm_wait(&rempty[s], ((it / NS) - 1) & 1, a.err, abort_flag)) break;
+                uint8_t* st = rawr + (size_t)s * SM::kSlot;
                 const int kb = (st0 + it) * kStageBlocks;  // first Q block of the stage
                 mbar_arrive_expect_tx(&full[s], bytes);
-                tma_load_2d(st + SM::kA + SM::kB, &map_q, kb * (kTileRows * QShape<QT>::QB / 8),
+                tma_load_2d(st + SM::kB, &map_q, kb * (kTileRows * QShape<QT>::QB / 8),
                             a.tiles_q + mt * (kBM / kTileRows), &full[s]);
-                tma_load_2d(st + SM::kA + SM::kB + QShape<QT>::kRawQ, &map_s, kb * (kTileRows * 2 / 8),
+                tma_load_2d(st + SM::kB + QShape<QT>::kRawQ, &map_s, kb * (kTileRows * 2 / 8),
                             a.tiles_q + mt * (kBM / kTileRows), &full[s]);
-                tma_load_2d(st + SM::kA, &map_x, kb * 32, nt * BN, &full[s]);
+                tma_load_2d(st, &map_x, kb * 32, nt * BN, &full[s]);
                 issued = it + 1;
             }
             // every copy issued has landed before the CTA may exit
@@ -296,15 +345,15 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
             const uint32_t idesc = f16_idesc<BN>();
             int done = 0;
             for (int it = 0; it < nst; it++) {
-                const int s = it % NS;
-                if (!gemm_wait(&adone[s], (it / NS) & 1, a.err, abort_flag)) break;
+                const int s = it % NS, j = it % NA;
+                if (!gemm_wait(&afull[j], (it / NA) & 1, a.err, abort_flag)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                uint8_t* st = stages + (size_t)s * SM::kStage;
-                const uint32_t sa = smem_u32(st), sb = smem_u32(st + SM::kA);
+                const uint32_t ta = tmem + SM::kAccCols + 32u * (uint32_t)j, sb = smem_u32(rawr + (size_t)s * SM::kSlot);
 #pragma unroll
-                for (int k = 0; k < 4; k++)  // K = 16 per MMA: 32 bytes along the swizzled row
-                    mma_f16(tmem, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), idesc, (it | k) != 0);
-                mma_commit(&empty[s]);
+                for (int k = 0; k < 4; k++)  // K = 16 per MMA: 8 columns of A, 32 bytes along B's swizzled row
+                    mma_f16_ts(tmem, ta + 8u * (uint32_t)k, sw128_desc(sb + 32 * k), idesc, (it | k) != 0);
+                mma_commit(&aempty[j]);   // the A buffer, and
+                mma_commit(&rempty[s]);   // the raw stage (its B tile) are free once these products are done
                 done = it + 1;
             }
             mma_commit(accum);  // after every MMA issued above
@@ -312,29 +361,43 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
         }
     } else {
         // ---------------------------------------------- dequantisers, epilogue
-        const int r = threadIdx.x - 64;  // weight row of the tile, 0..127
+        // thread: weight row r of the tile; with eight warps the two halves of
+        // the row's stage (one Q block each) go to threads 128 apart
+        constexpr int kRowThreads = kDqWarps * 32 / kBM;  // 1 or 2
+        // (row = tensor-memory lane: a warp reaches lanes 32 (warp % 4) .. + 31)
+        const int dt = threadIdx.x - 64, r = 32 * (warp & 3) + lane, kb0 = (dt / kBM) * (kStageBlocks / kRowThreads);
         for (int it = 0; it < nst; it++) {
-            const int s = it % NS;
+            const int s = it % NS, j = it % NA;
             bool ok = gemm_wait(&full[s], (it / NS) & 1, a.err, abort_flag);
+            if (ok && it >= NA) ok = gemm_wait(&aempty[j], ((it / NA) - 1) & 1, a.err, abort_flag);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
-            uint8_t* st = stages + (size_t)s * SM::kStage;
-            dequant_row<QT>(st + SM::kA + SM::kB, st + SM::kA + SM::kB + QShape<QT>::kRawQ, st, r);
-            fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+            const uint8_t* st = rawr + (size_t)s * SM::kSlot;
+            // this warp's lane quadrant of A stage j
+            const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + SM::kAccCols + 32u * (uint32_t)j;
+            dequant_row<QT, kStageBlocks / kRowThreads>(st + SM::kB, st + SM::kB + QShape<QT>::kRawQ, ta, r, kb0);
+            // raw stage s is free once every dequantising warp has read it;
+            // its B tile still feeds the MMA, which releases the stage
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(&adone[s]);
+            if (lane == 0) mbar_arrive(&afull[j]);
         }
-        // epilogue: accumulator row r (TMEM lane r; warp w reads lanes 32 (w % 4) ..)
-        const int q = warp & 3;
+        // epilogue: accumulator row r (TMEM lane r; warp w reads lanes 32 (w % 4) ..);
+        // the warps of one lane quadrant split the columns
+        const int q = warp & 3, grp = (warp - 2) >> 2;
+        constexpr int kGroups = kDqWarps / 4;
+        constexpr int kColsPer = BN / kGroups < 16 ? 16 : BN / kGroups;
         const int row = 32 * q + lane;
         bool ok = gemm_wait(accum, 0, a.err, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         // one decision for all four epilogue warps (each arrives here whatever
         // its waits returned), so the barriers below are met by all or none
-        volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 4);  // [4]
+        volatile int* ep_ok = reinterpret_cast<volatile int*>(tmem_slot + 4);  // [kDqWarps]
         if (lane == 0) ep_ok[warp - 2] = ok ? 1 : 0;
-        named_bar_sync(1, 128);
-        ok = ep_ok[0] && ep_ok[1] && ep_ok[2] && ep_ok[3];
+        named_bar_sync(1, 32 * kDqWarps);
+#pragma unroll
+        for (int w = 0; w < kDqWarps; w++) ok = ok && ep_ok[w];
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok && nst > 0) {
             const int grow = mt * kBM + row;  // output row within the share
@@ -342,7 +405,7 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
             float* yb = a.ksplit > 1 ? a.part + (size_t)ks * plane : a.y;
             const int ld = a.ksplit > 1 ? a.rows : a.ldy;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
+            for (int c0 = grp * kColsPer; c0 < BN && c0 < (grp + 1) * kColsPer; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
 #pragma unroll
@@ -486,20 +549,29 @@ struct GemmScratch {
 };
 std::mutex g_gemm_mu;
 std::map<std::pair<int, cudaStream_t>, GemmScratch> g_gemm;
+constexpr int kMaxDevices = 64;
+// the whole gate/up product of b2_tiled_gemm_half_impl, per (device, stream)
+std::map<std::pair<int, cudaStream_t>, std::pair<float*, size_t>> g_gemm_fused;
 
 size_t al256(size_t n) { return (n + 255) & ~size_t(255); }
 
 template <int QT, int BN>
 int launch_qgemm(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap& mx, const GemmArgs& a, dim3 grid,
                  cudaStream_t s, std::string* err) {
-    static bool attr = false;
-    if (!attr) {
+    // the attribute belongs to a device: set once per device (under g_gemm_mu)
+    static bool attr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        *err = "no usable CUDA device";
+        return B2_ERR_CUDA;
+    }
+    if (!attr[dev]) {
         if (cudaFuncSetAttribute(qgemm_kernel<QT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  GemmSmem<QT, BN>::kTotal) != cudaSuccess) {
             *err = "cudaFuncSetAttribute (tensor-core GEMM) failed";
             return B2_ERR_CUDA;
         }
-        attr = true;
+        attr[dev] = true;
     }
     qgemm_kernel<QT, BN><<<grid, kGemmThreads, GemmSmem<QT, BN>::kTotal, s>>>(mq, ms, mx, a);
     return B2_OK;
@@ -524,8 +596,13 @@ using namespace b2;
 // Y = W X over rows [row0, row0 + rows) of a tiled Q8_0 / Q4_0 matrix
 // (base: the tiled matrix, rp its padded rows, cols = K) for ntok tokens:
 // x [ntok][cols] fp32, y [ntok][rows] fp32, device memory, stream s.
-int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
-                       float* y, int ntok, cudaStream_t s, std::string* err) {
+namespace {
+int bn_for(int ntok) { return ntok <= 16 ? 16 : ntok <= 32 ? 32 : ntok <= 64 ? 64 : 128; }
+
+// Both entry points: x (fp32, converted here) or xh / tsc (already fp16).
+int gemm_run(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
+             const __half* xh_in, const float* tsc_in, float* y, int ntok, GemmParts* parts, cudaStream_t s,
+             std::string* err) {
     if (qtype != 8 && qtype != 2) {
         *err = "tensor-core GEMM takes Q8_0 or Q4_0 weights";
         return B2_ERR_UNSUPPORTED_TYPE;
@@ -534,7 +611,8 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         *err = "tensor-core GEMM: cols must be a multiple of 64 and rows inside the matrix";
         return B2_ERR_BAD_ARG;
     }
-    if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 3)) {
+    if ((x ? (reinterpret_cast<uintptr_t>(x) & 15) : (!xh_in || !tsc_in || (reinterpret_cast<uintptr_t>(xh_in) & 15))) ||
+        (reinterpret_cast<uintptr_t>(y) & 3)) {
         *err = "x must be 16-byte aligned and y 4-byte aligned";
         return B2_ERR_BAD_ARG;
     }
@@ -549,7 +627,7 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         *err = "no CUDA device";
         return B2_ERR_CUDA;
     }
-    const int bn = ntok <= 16 ? 16 : ntok <= 32 ? 32 : ntok <= 64 ? 64 : 128;
+    const int bn = bn_for(ntok);
     const int n_tiles = (ntok + bn - 1) / bn;
     const int ntok_pad = n_tiles * bn;
     const int nb = cols / 32;
@@ -566,7 +644,7 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
     while (ksplit < kMaxKSplit && (long long)m_tiles * n_tiles * ksplit < sc->sms && nst / (2 * ksplit) >= 4) ksplit *= 2;
     const int kst = (nst + ksplit - 1) / ksplit;
     ksplit = (nst + kst - 1) / kst;
-    const size_t b_x = al256((size_t)ntok_pad * cols * 2), b_sc = al256((size_t)ntok_pad * 4);
+    const size_t b_x = x ? al256((size_t)ntok_pad * cols * 2) : 0, b_sc = x ? al256((size_t)ntok_pad * 4) : 0;
     const size_t b_part = ksplit > 1 ? al256((size_t)ksplit * ntok * rows * 4) : 0;
     const size_t need = 256 + b_x + b_sc + b_part;
     if (sc->bytes < need) {
@@ -582,8 +660,8 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         sc->err = reinterpret_cast<int*>(sc->buf);
         sc->gen++;
     }
-    __half* xh = reinterpret_cast<__half*>(sc->buf + 256);
-    float* tsc = reinterpret_cast<float*>(sc->buf + 256 + b_x);
+    __half* xh = x ? reinterpret_cast<__half*>(sc->buf + 256) : const_cast<__half*>(xh_in);
+    const float* tsc = x ? reinterpret_cast<float*>(sc->buf + 256 + b_x) : tsc_in;
     float* part = ksplit > 1 ? reinterpret_cast<float*>(sc->buf + 256 + b_x + b_sc) : nullptr;
 
     const bool q8 = qtype == 8;
@@ -603,7 +681,7 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         *err = "tensor map encoding failed (alignment)";
         return B2_ERR_BAD_ARG;
     }
-    to_f16_scaled_kernel<<<ntok_pad, kCvtThreads, 0, s>>>(x, ntok, cols, xh, tsc);
+    if (x) to_f16_scaled_kernel<<<ntok_pad, kCvtThreads, 0, s>>>(x, ntok, cols, xh, const_cast<float*>(tsc));
     GemmArgs a{};
     a.nst = nst;
     a.kst_split = kst;
@@ -619,7 +697,11 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
     const dim3 grid(m_tiles, n_tiles, ksplit);
     int rc = q8 ? launch_bn<8>(bn, mq, ms, mx, a, grid, s, err) : launch_bn<2>(bn, mq, ms, mx, a, grid, s, err);
     if (rc) return rc;
-    if (ksplit > 1) {
+    if (parts) {
+        parts->p = ksplit > 1 ? part : y;
+        parts->k = ksplit;
+        parts->plane = (size_t)ntok * rows;
+    } else if (ksplit > 1) {
         const size_t n = (size_t)ntok * rows;
         const bool vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;  // (part is 256-aligned)
         const size_t units = vec ? n / 4 : n;
@@ -633,6 +715,37 @@ int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, in
         return B2_ERR_CUDA;
     }
     return B2_OK;
+}
+}  // namespace
+
+int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
+                       float* y, int ntok, cudaStream_t s, std::string* err) {
+    if (!x) {
+        *err = "null argument";
+        return B2_ERR_BAD_ARG;
+    }
+    return gemm_run(qtype, base, rp, row0, rows, cols, x, nullptr, nullptr, y, ntok, nullptr, s, err);
+}
+
+int b2_tiled_gemm_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,
+                       float* y, int ntok, GemmParts* parts, cudaStream_t s, std::string* err) {
+    if (!x) {
+        *err = "null argument";
+        return B2_ERR_BAD_ARG;
+    }
+    return gemm_run(qtype, base, rp, row0, rows, cols, x, nullptr, nullptr, y, ntok, parts, s, err);
+}
+
+int b2_tiled_gemm_f16_impl(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols,
+                           const void* xh, const float* tok_scale, int ntok, float* y, GemmParts* parts,
+                           cudaStream_t s, std::string* err) {
+    return gemm_run(qtype, base, rp, row0, rows, cols, nullptr, static_cast<const __half*>(xh), tok_scale, y, ntok,
+                    parts, s, err);
+}
+
+int b2_gemm_pad_tokens(int ntok) {
+    const int bn = bn_for(ntok);
+    return (ntok + bn - 1) / bn * bn;
 }
 
 namespace b2 {
@@ -652,14 +765,33 @@ __global__ void gather_half_kernel(const float* __restrict__ fused, int ntok, in
 }  // namespace b2
 
 // The gate or up half (half 1 or 2) of the interleaved gate/up matrix (2 *
-// rows resident rows): the product over the whole matrix into a buffer the
-// call allocates on the stream, then that half's rows.
+// rows resident rows): the product over the whole matrix into a buffer kept
+// per (device, stream) and grown as needed, then that half's rows.
 int b2_tiled_gemm_half_impl(int qtype, const void* base, int64_t rp, int half, int rows, int cols, const float* x,
                             float* y, int ntok, cudaStream_t s, std::string* err) {
     float* fused = nullptr;
-    if (cudaMallocAsync(reinterpret_cast<void**>(&fused), sizeof(float) * (size_t)ntok * 2 * rows, s) != cudaSuccess) {
-        *err = "allocation of the gate/up product failed";
-        return B2_ERR_OOM;
+    {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) {
+            *err = "no CUDA device";
+            return B2_ERR_CUDA;
+        }
+        const size_t need = sizeof(float) * (size_t)ntok * 2 * rows;
+        std::lock_guard<std::mutex> lk(g_gemm_mu);
+        auto& f = g_gemm_fused[{dev, s}];
+        if (f.second < need) {
+            if (f.first) {
+                cudaStreamSynchronize(s);  // earlier calls on s may still read it
+                cudaFree(f.first);
+            }
+            f = {nullptr, 0};
+            if (cudaMalloc(reinterpret_cast<void**>(&f.first), need) != cudaSuccess) {
+                *err = "allocation of the gate/up product failed";
+                return B2_ERR_OOM;
+            }
+            f.second = need;
+        }
+        fused = f.first;
     }
     int rc = b2_tiled_gemm_impl(qtype, base, rp, 0, 2 * rows, cols, x, fused, ntok, s, err);
     if (!rc) {
@@ -670,7 +802,6 @@ int b2_tiled_gemm_half_impl(int qtype, const void* base, int64_t rp, int half, i
             rc = B2_ERR_CUDA;
         }
     }
-    cudaFreeAsync(fused, s);
     return rc;
 }
 

@@ -12,12 +12,15 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <vector>
 
 #include "model.h"
+#include "sample.h"
+#include "upload.h"
 
 namespace b2 {
 
@@ -370,8 +373,10 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         b2_free_impl(m);
         return code;
     };
+    const auto t_load0 = std::chrono::steady_clock::now();
     int rc = gguf_parse(path, &m->gguf, err);
     if (rc) { std::string e = *err; return bail(rc, e); }
+    m->load.parse_ns = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t_load0).count();
     const GgufFile& g = m->gguf;
     b2_config& c = m->cfg;
 
@@ -545,6 +550,11 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     const size_t off_toks = take((size_t)S * 4);
     const size_t off_ids = take((size_t)S * 4);
     const size_t off_done = take(4);
+    // device sampling: the ids generated so far (repetition penalty), the
+    // sampler's scratch, the sampled id
+    const size_t off_gen = take((size_t)S * 4);
+    const size_t off_sexp = take(sample_scratch_bytes(Vl, 1));
+    const size_t off_sout = take(4);
     const size_t off_layers = take(sizeof(LayerDev) * L);
     m->arena_bytes = off;
     // the tensor-parallel exchange buffer: its own allocation, so that its IPC
@@ -574,108 +584,99 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         return bail(B2_ERR_OOM, "pinned host allocation failed");
 
     // ---------------------------------------------------------- upload
-    FILE* f = fopen(path, "rb");
-    if (!f) return bail(B2_ERR_IO, std::string("open model file: ") + path);
-    const size_t stage_bytes = 64u << 20;
-    uint8_t* stage[2] = {nullptr, nullptr};
-    if (cudaMallocHost(&stage[0], stage_bytes) != cudaSuccess || cudaMallocHost(&stage[1], stage_bytes) != cudaSuccess) {
-        fclose(f);
-        if (stage[0]) cudaFreeHost(stage[0]);
-        return bail(B2_ERR_OOM, "pinned staging allocation failed");
-    }
-    cudaEvent_t sev[2];
-    cudaEventCreate(&sev[0]);
-    cudaEventCreate(&sev[1]);
-    bool sev_used[2] = {false, false};
-    int which = 0;
+    const auto t_up0 = std::chrono::steady_clock::now();
     bool io_ok = true;
-    // Weight matrices: file -> pinned stage -> raw device buffer (double-
-    // buffered), then one repack launch per matrix into the arena.
-    size_t raw_max = 0;
-    for (const MatGroup& gr : groups) {
-        int64_t r = 0;
-        for (const MatPart& pt : gr.parts) r += pt.rows;
-        raw_max = std::max(raw_max, (size_t)r * (size_t)gr.nb_src * bpb);
-    }
-    void* raw = nullptr;
-    if (dev_malloc(&raw, raw_max) != 0) {
-        fclose(f);
-        cudaFreeHost(stage[0]);
-        cudaFreeHost(stage[1]);
-        return bail(B2_ERR_OOM, "device allocation of the " + std::to_string(raw_max) + "-byte upload buffer failed");
-    }
-    for (const MatGroup& gr : groups) {
-        size_t dst = 0;
-        int64_t row0 = 0;
-        for (const MatPart& pt : gr.parts) {
-            const std::string& name = pt.name;
-            const GgufTensor* t = g.find(name);
-            const uint64_t rb_src = (uint64_t)gr.nb_src * bpb;  // source row bytes
-            uint64_t left = (uint64_t)pt.rows * rb_src, src = g.data_offset + t->offset + (uint64_t)pt.row0 * rb_src;
-            if (fseeko(f, (off_t)src, SEEK_SET) != 0) { io_ok = false; break; }
-            while (left > 0 && io_ok) {
-                const size_t nb = (size_t)std::min<uint64_t>(left, stage_bytes);
-                if (sev_used[which]) cudaEventSynchronize(sev[which]);
-                if (fread(stage[which], 1, nb, f) != nb) { io_ok = false; break; }
-                cudaMemcpyAsync(static_cast<uint8_t*>(raw) + dst, stage[which], nb, cudaMemcpyHostToDevice, m->stream);
-                cudaEventRecord(sev[which], m->stream);
-                sev_used[which] = true;
-                which ^= 1;
-                left -= nb;
-                dst += nb;
+    std::string io_err;
+    int64_t up_host_ns = 0;
+    uint64_t up_bytes = 0;
+    int up_threads = 0;
+    bool up_mapped = false;
+    {
+        Uploader up(path, m->stream);
+        if (!up.ok()) {
+            const bool oom = up.error().find("allocation") != std::string::npos;
+            return bail(oom ? B2_ERR_OOM : B2_ERR_IO, up.error());
+        }
+        // Weight matrices: file -> pinned stages -> raw device buffer, then
+        // one repack launch per matrix into the arena (the raw buffer is
+        // reused by the next matrix only after its repack, stream order).
+        size_t raw_max = 0;
+        for (const MatGroup& gr : groups) {
+            int64_t r = 0;
+            for (const MatPart& pt : gr.parts) r += pt.rows;
+            raw_max = std::max(raw_max, (size_t)r * (size_t)gr.nb_src * bpb);
+        }
+        void* raw = nullptr;
+        if (dev_malloc(&raw, raw_max) != 0)
+            return bail(B2_ERR_OOM, "device allocation of the " + std::to_string(raw_max) + "-byte upload buffer failed");
+        for (const MatGroup& gr : groups) {
+            size_t dst = 0;
+            int64_t row0 = 0;
+            for (const MatPart& pt : gr.parts) {
+                const std::string& name = pt.name;
+                const GgufTensor* t = g.find(name);
+                const uint64_t rb_src = (uint64_t)gr.nb_src * bpb;  // source row bytes
+                const uint64_t n = (uint64_t)pt.rows * rb_src, src = g.data_offset + t->offset + (uint64_t)pt.row0 * rb_src;
+                if (!up.to_device(src, n, static_cast<uint8_t*>(raw) + dst)) { io_ok = false; break; }
+                dst += n;
+                // this rank's share of the tensor (b2_dequant_tensor decodes it)
+                TensorLoc tl{A + gr.off, t->type, (uint64_t)pt.rows * (uint64_t)gr.cols};
+                tl.row0 = row0;
+                tl.cols = gr.cols;
+                tl.rp = tiled_rows(gr.rows);
+                tl.half = gr.half_rows ? (row0 == 0 ? 1 : 2) : 0;
+                if (!m->tensors.count(name)) m->tensors[name] = tl;
+                row0 += pt.rows;
             }
             if (!io_ok) break;
-            // this rank's share of the tensor (b2_dequant_tensor decodes it)
-            TensorLoc tl{A + gr.off, t->type, (uint64_t)pt.rows * (uint64_t)gr.cols};
-            tl.row0 = row0;
-            tl.cols = gr.cols;
-            tl.rp = tiled_rows(gr.rows);
-            tl.half = gr.half_rows ? (row0 == 0 ? 1 : 2) : 0;
-            if (!m->tensors.count(name)) m->tensors[name] = tl;
-            row0 += pt.rows;
+            const int64_t rp = tiled_rows(gr.rows), nbk = gr.cols / 32;
+            const int blocks = (int)std::min<int64_t>((rp * nbk + 255) / 256, 148 * 32);
+            repack_kernel<<<blocks, 256, 0, m->stream>>>(static_cast<const uint8_t*>(raw), A + gr.off, gr.rows, rp, nbk,
+                                                         qti, gr.half_rows, gr.nb_src, gr.cb0);
         }
-        if (!io_ok) break;
-        const int64_t rp = tiled_rows(gr.rows), nbk = gr.cols / 32;
-        const int blocks = (int)std::min<int64_t>((rp * nbk + 255) / 256, 148 * 32);
-        repack_kernel<<<blocks, 256, 0, m->stream>>>(static_cast<const uint8_t*>(raw), A + gr.off, gr.rows, rp, nbk, qti,
-                                                     gr.half_rows, gr.nb_src, gr.cb0);
-    }
-    cudaStreamSynchronize(m->stream);
-    cudaFree(raw);
-    // Small vectors (norm gains, biases) as fp32; F16/BF16 widened on the host
-    // exactly as gguf.go:510-536 does.
-    std::vector<float> buf;
-    for (const SmallVec& sv : small) {
-        if (!io_ok) break;
-        const GgufTensor* t = g.find(sv.name);
-        const size_t n = t ? (size_t)t->elements() : 0;
-        buf.assign(sv.n, 0.0f);  // an absent optional bias stays zero (transformer.go:632-646)
-        if (t) {
-            if ((int64_t)n != sv.total) { fclose(f); return bail(B2_ERR_FORMAT, sv.name + ": unexpected length"); }
-            std::vector<uint8_t> raw(t->bytes());
-            if (fseeko(f, (off_t)(g.data_offset + t->offset), SEEK_SET) != 0 || fread(raw.data(), 1, raw.size(), f) != raw.size()) {
-                io_ok = false;
-                break;
-            }
-            for (int64_t k = 0; k < sv.n; k++) {
-                const size_t i = (size_t)(sv.e0 + k);
-                if (t->type == GGML_F32) memcpy(&buf[k], &raw[i * 4], 4);
-                else if (t->type == GGML_F16) buf[k] = f16_to_f32((uint16_t)(raw[2 * i] | (raw[2 * i + 1] << 8)));
-                else if (t->type == GGML_BF16) { uint32_t bits = (uint32_t)(raw[2 * i] | (raw[2 * i + 1] << 8)) << 16; memcpy(&buf[k], &bits, 4); }
-                else { fclose(f); return bail(B2_ERR_UNSUPPORTED_TYPE, sv.name + ": vectors must be F32, F16 or BF16"); }
-            }
-            m->tensors[sv.name] = TensorLoc{A + sv.off, GGML_F32, (uint64_t)sv.n};
-        }
-        cudaMemcpyAsync(A + sv.off, buf.data(), buf.size() * 4, cudaMemcpyHostToDevice, m->stream);
+        if (!up.finish()) io_ok = false;
         cudaStreamSynchronize(m->stream);
+        cudaFree(raw);
+        // Small vectors (norm gains, biases) as fp32; F16/BF16 widened on the
+        // host exactly as gguf.go:510-536 does.
+        std::vector<float> buf;
+        for (const SmallVec& sv : small) {
+            if (!io_ok) break;
+            const GgufTensor* t = g.find(sv.name);
+            const size_t n = t ? (size_t)t->elements() : 0;
+            buf.assign(sv.n, 0.0f);  // an absent optional bias stays zero (transformer.go:632-646)
+            if (t) {
+                if ((int64_t)n != sv.total) return bail(B2_ERR_FORMAT, sv.name + ": unexpected length");
+                std::vector<uint8_t> rawv(t->bytes());
+                if (!up.to_host(g.data_offset + t->offset, rawv.size(), rawv.data())) {
+                    io_ok = false;
+                    break;
+                }
+                for (int64_t k = 0; k < sv.n; k++) {
+                    const size_t i = (size_t)(sv.e0 + k);
+                    if (t->type == GGML_F32) memcpy(&buf[k], &rawv[i * 4], 4);
+                    else if (t->type == GGML_F16) buf[k] = f16_to_f32((uint16_t)(rawv[2 * i] | (rawv[2 * i + 1] << 8)));
+                    else if (t->type == GGML_BF16) { uint32_t bits = (uint32_t)(rawv[2 * i] | (rawv[2 * i + 1] << 8)) << 16; memcpy(&buf[k], &bits, 4); }
+                    else return bail(B2_ERR_UNSUPPORTED_TYPE, sv.name + ": vectors must be F32, F16 or BF16");
+                }
+                m->tensors[sv.name] = TensorLoc{A + sv.off, GGML_F32, (uint64_t)sv.n};
+            }
+            cudaMemcpyAsync(A + sv.off, buf.data(), buf.size() * 4, cudaMemcpyHostToDevice, m->stream);
+            cudaStreamSynchronize(m->stream);
+        }
+        cudaStreamSynchronize(m->stream);
+        if (!io_ok) io_err = up.error().empty() ? "short read while uploading tensors" : up.error();
+        up_host_ns = up.host_ns();
+        up_bytes = up.bytes();
+        up_threads = up.threads();
+        up_mapped = up.mapped();
     }
-    fclose(f);
-    cudaStreamSynchronize(m->stream);
-    cudaEventDestroy(sev[0]);
-    cudaEventDestroy(sev[1]);
-    cudaFreeHost(stage[0]);
-    cudaFreeHost(stage[1]);
-    if (!io_ok) return bail(B2_ERR_IO, "short read while uploading tensors");
+    if (!io_ok) return bail(B2_ERR_IO, io_err);
+    m->load.upload_ns = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t_up0).count();
+    m->load.host_copy_ns = up_host_ns;
+    m->load.bytes_uploaded = (int64_t)up_bytes;
+    m->load.host_threads = up_threads;
+    m->load.mapped = up_mapped ? 1 : 0;
 
     // RoPE table with the Go formula (transformer.go:939-942): freq in float64
     // pow rounded to float32, angle in float32, cos/sin in float64 rounded.
@@ -729,6 +730,9 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     m->d_tokens = reinterpret_cast<int*>(A + off_toks);
     m->d_out_ids = reinterpret_cast<int*>(A + off_ids);
     m->d_done = reinterpret_cast<int*>(A + off_done);
+    m->d_gen = reinterpret_cast<int*>(A + off_gen);
+    m->d_sample_ws = A + off_sexp;
+    m->d_sample_out = reinterpret_cast<int*>(A + off_sout);
     m->layers_host.resize(L);
     for (int l = 0; l < L; l++) {
         LayerDev& ld = m->layers_host[l];
@@ -899,6 +903,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return bail(B2_ERR_CUDA, std::string("CUDA: ") + cudaGetErrorString(e));
+    m->load.total_ns = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t_load0).count();
     *out = m;
     return B2_OK;
 }

@@ -65,12 +65,16 @@ struct b2_model {
     int* d_tokens = nullptr;   // [max_seq] step inputs
     int* d_out_ids = nullptr;  // [max_seq] greedy outputs
     int* d_done = nullptr;     // [1] EOS seen by the device-resident loop
+    int* d_gen = nullptr;      // [max_seq] ids sampled so far (device sampling's penalty list)
+    unsigned char* d_sample_ws = nullptr;  // device sampler scratch (sample_scratch_bytes(vocab, 1))
+    int* d_sample_out = nullptr;  // [1] the sampled id
     int* h_pinned = nullptr;   // pinned staging for token ids (max_seq ints)
     float* h_logits = nullptr; // pinned staging for logits (vocab floats)
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     cudaEvent_t ev_pin = nullptr;  // last H2D copy out of h_pinned
     bool pin_pending = false;
     b2::StreamState st;
+    b2_load_stats load{};  // b2_get_load_stats
     // tensor parallelism: this rank's exchange buffer and the peers' (mapped
     // through CUDA IPC by b2_tp_connect; launches need the connection first)
     void* xch = nullptr;

@@ -353,6 +353,7 @@ def run_b200(args) -> None:
     t_load = time.perf_counter()
     m = b2decode.Model(path, num_ctx=num_ctx, device=local, tp_size=tpn, tp_rank=rank if tpn > 1 else 0)
     load_s = time.perf_counter() - t_load
+    load = _load_summary(m, load_s)
     if tpn > 1:
         from b2decode import tp as tpmod
         tpmod.connect(m)
@@ -430,7 +431,7 @@ def run_b200(args) -> None:
                        "prefill_path": ("b2_forward_argmax: the prompt in 128-token chunks on the tcgen05 GEMM path "
                                         "into the model's KV cache" if tpn == 1 else
                                         "b2_forward_argmax: the decode kernel once per prompt token (tensor parallel)"),
-                       "load_s": load_s,
+                       "load_s": load_s, "load": load,
                        "kv_cache": "fp16"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
@@ -480,6 +481,7 @@ def run_tp72b(args, ws, rank, local, barrier, max_over_ranks, peak, peak_kind) -
     m = b2decode.Model(path, num_ctx=len(prompt) + W + K + 8, device=local, tp_size=ws if ws > 1 else 0,
                        tp_rank=rank if ws > 1 else 0)
     load_s = time.perf_counter() - t0
+    load = _load_summary(m, load_s)
     if ws > 1:
         from b2decode import tp as tpmod
         tpmod.connect(m)
@@ -521,8 +523,19 @@ def run_tp72b(args, ws, rank, local, barrier, max_over_ranks, peak, peak_kind) -
                     "by peer stores over NVLink inside the decode kernel (no collective library); argmax over "
                     "the vocab shares the same way" if ws > 1 else "none (one GPU)",
         "ids_first": [int(i) for i in ids[:8]], "ids_agree_across_ranks": bool(same),
-        "load_s": load_s, "prefill_s": prefill_s,
+        "load_s": load_s, "load": load, "prefill_s": prefill_s,
     }
+
+
+def _load_summary(m, load_s: float) -> dict:
+    """b2_get_load_stats of a loaded model: the load's phases and the upload
+    rate (weight bytes / upload time)."""
+    s = m.load_stats()
+    up = s["upload_ns"] / 1e9
+    return {"wall_s": load_s, "b2_load_s": s["total_ns"] / 1e9, "parse_s": s["parse_ns"] / 1e9, "upload_s": up,
+            "host_copy_s": s["host_copy_ns"] / 1e9, "weight_bytes": s["bytes_uploaded"],
+            "upload_gbs": s["bytes_uploaded"] / up / 1e9 if up > 0 else None, "host_threads": s["host_threads"],
+            "file": "memory-mapped" if s["mapped"] else "pread"}
 
 
 def _rotations(nbytes: int) -> int:
@@ -635,8 +648,9 @@ def run_gemm(args) -> None:
     of the real widths) for a prompt-sized token count (--tokens, 512 by
     default): TFLOP/s = 2 x rows x cols x tokens / time, against the measured
     dense bf16 peak (the fp16 kind runs at the same rate).  Gate and up are
-    each timed as b2_model_gemm runs them alone (the whole interleaved matrix,
-    then one half gathered); the batched forward runs them as one product."""
+    resident as one interleaved matrix: b2_model_gemm on ffn_gate computes
+    the product of both halves (as the batched forward does) and gathers the
+    gate half, so that line counts the flops of both."""
     import torch
 
     import b2decode
@@ -647,8 +661,7 @@ def run_gemm(args) -> None:
     st = torch.cuda.ExternalStream(m.stream_handle())
     H, FF, qd, kvd = shape.hidden, shape.ffn, shape.heads * shape.head_dim, shape.kv_dim
     mats = {"blk.0.attn_q.weight": (qd, H), "blk.0.attn_k.weight": (kvd, H), "blk.0.attn_v.weight": (kvd, H),
-            "blk.0.attn_output.weight": (H, qd), "blk.0.ffn_gate.weight": (FF, H), "blk.0.ffn_up.weight": (FF, H),
-            "blk.0.ffn_down.weight": (H, FF)}
+            "blk.0.attn_output.weight": (H, qd), "blk.0.ffn_gate.weight": (FF, H), "blk.0.ffn_down.weight": (H, FF)}
     mp = measured_peaks()
     peak = float(mp.get("bf16_tflops", 1590.0)) if mp else 1590.0
     ntok = args.tokens
@@ -660,7 +673,10 @@ def run_gemm(args) -> None:
         y = torch.empty(ntok, rows, device="cuda")
         with torch.cuda.stream(st):
             ms = _timed(torch, st, lambda i: m.gemm(name, x.data_ptr(), y.data_ptr(), ntok), 1, max(args.steps, 8))
-        flop = 2.0 * rows * cols * ntok
+        both = name.endswith("ffn_gate.weight")  # the interleaved gate/up product
+        flop = 2.0 * rows * cols * ntok * (2 if both else 1)
+        label = f"{name} {rows}x{cols}" if not both else \
+            f"{name[:-len('gate.weight')]}gate+up interleaved {2 * rows}x{cols} (gate half gathered)"
         tf = flop / (ms / 1000.0) / 1e12
         tot_flop += flop
         tot_ms += ms
@@ -669,7 +685,7 @@ def run_gemm(args) -> None:
             "higher_is_better": True, "dtype": "Q4_0 weights -> fp16 (d*q rounded once) x fp16 activations "
                                                "(power-of-two scale per token), fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": f"{name} {rows}x{cols} (Llama-3-8B widths, Q4_0) x {ntok} tokens",
+            "config": {"workload": f"{label} (Llama-3-8B widths, Q4_0) x {ntok} tokens",
                        "us_per_call": ms * 1000.0, "path": "b2_model_gemm: tcgen05.mma kind::f16, TMA-staged tiles"},
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
                          "peak_source": "MEASURED_PEAKS.json bf16_tflops" if mp else "fallback 1.59 PFLOP/s"},
@@ -678,10 +694,63 @@ def run_gemm(args) -> None:
         tf = tot_flop / (tot_ms / 1000.0) / 1e12
         print(json.dumps({"metric": "tensor-core GEMM TFLOP/s, one Llama-3-8B layer's products", "value": tf,
                           "unit": "TFLOP/s", "n_gpus": 1, "higher_is_better": True,
-                          "config": {"workload": f"q, k, v, o, gate, up, down x {ntok} tokens", "ms": tot_ms},
+                          "config": {"workload": f"q, k, v, o, gate+up, down x {ntok} tokens", "ms": tot_ms},
                           "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
                                        "frac": tf / peak}}), flush=True)
     m.close()
+
+
+def run_sample(args) -> None:
+    """Device-side sampling (b2_sample_device, one launch per token) on a
+    Qwen2.5-vocabulary logits row (151936, N(0, 3)), per option set, against
+    the host path it replaces: the 608 KB logits copy to the host plus
+    sample() on the host (b2_sample_logits).  Each device call first restores
+    the row (the sampler modifies it in place); that copy is timed alone and
+    subtracted."""
+    import time
+
+    import numpy as np
+    import torch
+
+    import b2decode
+    torch.cuda.set_device(0)
+    V = 151936
+    rng = np.random.default_rng(0)
+    lg = (rng.standard_normal(V) * 3).astype(np.float32)
+    gen = rng.integers(0, V, 64).astype(np.int32)
+    src = torch.tensor(lg, device="cuda")
+    work = torch.empty_like(src)
+    scratch = torch.empty(b2decode.sample_scratch_bytes(V, 1), dtype=torch.uint8, device="cuda")
+    dgen = torch.tensor(gen, device="cuda")
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    host = torch.empty(V, dtype=torch.float32, pin_memory=True)
+    st = torch.cuda.current_stream()
+    sh = st.cuda_stream
+    iters = max(args.steps, 50)
+    copy_ms = _timed(torch, st, lambda i: work.copy_(src), 1, iters)
+    d2h_ms = _timed(torch, st, lambda i: host.copy_(src, non_blocking=True), 1, iters)
+    for temp, k, p, rp in ((0.8, 40, 0.9, 1.1), (1.0, 0, 0.9, 1.0), (0.7, 0, 0.0, 1.0), (0.001, 0, 0.0, 1.3)):
+        opts = b2decode.sample_opts(temp, k, p, rp)
+
+        def call(i):
+            work.copy_(src)
+            b2decode.sample_device(work.data_ptr(), V, 1, V, opts, dgen.data_ptr(), V, [len(gen)], [0.37],
+                                   scratch.data_ptr(), out.data_ptr(), sh)
+
+        dev_us = (_timed(torch, st, call, 1, iters) - copy_ms) * 1000.0
+        t0 = time.perf_counter()
+        n_host = 5
+        for _ in range(n_host):
+            b2decode.sample_logits(lg, opts, gen.tolist(), 0.37)
+        host_us = (time.perf_counter() - t0) / n_host * 1e6 + d2h_ms * 1000.0
+        print(json.dumps({
+            "metric": "sampling latency per token (device sampler)", "value": dev_us, "unit": "us",
+            "n_gpus": 1, "higher_is_better": False, "data": "synthetic",
+            "config": {"workload": f"vocab {V}, temperature {temp}, top_k {k}, top_p {p}, repeat_penalty {rp} "
+                                   f"over 64 ids",
+                       "host_path_us": host_us, "host_path": "608 KB logits to the host + sample() there",
+                       "d2h_us": d2h_ms * 1000.0, "speedup_vs_host_path": host_us / max(dev_us, 1e-9)},
+        }), flush=True)
 
 
 def run_batch(args) -> None:
@@ -775,7 +844,7 @@ def main():
     ap.add_argument("--no-tp72b", action="store_true",
                     help="qwen05b: skip the tensor-parallel 72B-shape measurement added to the line")
     ap.add_argument("--workload", default="qwen05b",
-                    choices=["qwen05b", "llama3-8b", "qwen72b", "matvec", "attention", "gemm"])
+                    choices=["qwen05b", "llama3-8b", "qwen72b", "matvec", "attention", "gemm", "sample"])
     ap.add_argument("--case", default="",
                     help="one case of a microbench: attention CTXxB (32768x8), matvec KIND:ROWSxCOLS:B "
                          "(q8_0:128256x4096:1), gemm tensor name (blk.0.ffn_up.weight)")
@@ -794,6 +863,8 @@ def main():
         run_attention(args)
     elif args.workload == "gemm":
         run_gemm(args)
+    elif args.workload == "sample":
+        run_sample(args)
     elif args.batch > 1:
         run_batch(args)
     else:

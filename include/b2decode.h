@@ -105,6 +105,22 @@ int b2_load(const char* gguf_path, const b2_load_opts* opts, b2_model** out);
 /* transformer.go:312-322 Unload. NULL is ignored. */
 void b2_free(b2_model* m);
 int b2_get_config(const b2_model* m, b2_config* out);
+
+/* Where b2_load's time went (transformer.go:1122-1335 loadWeights reads and
+ * dequantises on the host; here the blocks go to HBM as they are): the file
+ * is memory-mapped, a pool of host threads copies each 32 MB range into one
+ * of four pinned stages while the previous stages' cudaMemcpyAsync run, and
+ * the device retiles each matrix. */
+typedef struct {
+    int64_t total_ns;        /* the whole b2_load */
+    int64_t parse_ns;        /* GGUF header, metadata and tensor infos */
+    int64_t upload_ns;       /* weight and vector bytes to HBM, retiling included */
+    int64_t host_copy_ns;    /* of upload_ns: host threads filling the pinned stages */
+    int64_t bytes_uploaded;  /* weight bytes sent through the stages */
+    int32_t host_threads;
+    int32_t mapped;          /* 1: memory-mapped file; 0: pread */
+} b2_load_stats;
+int b2_get_load_stats(const b2_model* m, b2_load_stats* out);
 /* Message of the last failure on this thread ("" if none). */
 const char* b2_last_error(void);
 
@@ -134,8 +150,9 @@ int b2_decode_greedy(b2_model* m, int32_t first, int32_t n_steps, int32_t eos, i
 /* transformer.go:325-382 Predict: reset, prepend BOS, prefill, then up to
  * num_predict steps of forward + sample, stopping at EOS or at any id in
  * stop_ids (the token-id form of isStopToken, transformer.go:1430-1437).
- * Greedy runs device-resident; otherwise logits are sampled on the host
- * exactly as sample() does (transformer.go:981-1036). */
+ * Greedy runs device-resident; otherwise each step's logits are sampled on
+ * the device by the b2_sample_device sampler (transformer.go:981-1114), with
+ * the engine's seeded uniforms, and only the id comes back. */
 int b2_predict(b2_model* m, const int32_t* prompt, int32_t n_prompt, const b2_sample_opts* opts,
                const int32_t* stop_ids, int32_t n_stop, int32_t* out_ids, int32_t max_out, int32_t* n_out,
                b2_timings* timings);
@@ -150,6 +167,23 @@ int b2_stream_next(b2_model* m, int32_t* token_out, int32_t* done_out);
  * the caller's uniform r in [0,1) for the multinomial draw. */
 int32_t b2_sample_logits(float* logits, int32_t n, const b2_sample_opts* opts, const int32_t* generated,
                          int32_t n_generated, float r);
+/* transformer.go:981-1114 sample() on the DEVICE, the sampler b2_predict and
+ * b2_stream_next use: rows (<= 64) sequences, row i's logits at
+ * d_logits[i * ld .. + n) in device memory (modified in place: penalty,
+ * temperature, filtered entries), its generated ids at d_generated[i * gen_ld
+ * .. + n_generated[i]) (device; may be NULL without a penalty), its uniform
+ * r[i] in [0,1) (host array).  Top-K and top-P are radix selections (no
+ * sort) by a group of CTAs per row; the masses are summed exactly in fixed
+ * point, so the id equals the host sampler's except where r or top_p lies
+ * within the host's float rounding of a cumulative boundary.  d_scratch:
+ * b2_sample_scratch_bytes(n, rows) bytes of device memory.  The ids are
+ * written to d_out[rows] (device; -1 if a group barrier of the launch ran
+ * out); asynchronous on stream (a cudaStream_t; NULL = the legacy default
+ * stream). */
+int64_t b2_sample_scratch_bytes(int32_t n, int32_t rows);
+int b2_sample_device(float* d_logits, int32_t n, int32_t rows, int64_t ld, const b2_sample_opts* opts,
+                     const int32_t* d_generated, int64_t gen_ld, const int32_t* n_generated, const float* r,
+                     void* d_scratch, int32_t* d_out, void* stream);
 
 /* transformer.go:445-490 Embed: mean of the token_embd rows of the ids,
  * L2-normalised, written to out[hidden_size]. */

@@ -105,8 +105,9 @@ def test_stream_matches_predict(built_lib, tiny_gguf):
 
 
 def test_sampled_predict_with_fixed_uniforms(built_lib, oracle_lib, tiny_gguf):
-    # Non-greedy sampling runs on the host over the engine's logits; with the
-    # same logits and uniforms it picks what sample() picks.
+    # The host sampler (b2_sample_logits) over the engine's logits picks what
+    # sample() picks with the same uniforms (the device sampler has its own
+    # tests).
     m = b2decode.Model(tiny_gguf, kv_fp32=True)
     g = goref.GoRef(tiny_gguf, n_threads=4)
     toks = np.concatenate([[1], gw.make_prompt(512, 6, seed=7)])
@@ -152,6 +153,21 @@ def test_embed(built_lib, oracle_lib, tiny_gguf):
         e /= np.float32(np.sqrt(np.float64((e * e).sum(dtype=np.float32))))
         assert np.allclose(m.embed(toks), e, rtol=1e-5, atol=1e-6)
     assert not m.embed([]).any()
+
+
+def test_load_stats(built_lib, tiny_gguf):
+    # the weights travel through the mapped file and the pinned stages: every
+    # matrix byte of the file once, and the phases add up
+    import gguf
+    quant = sum(int(t.n_bytes) for t in gguf.GGUFReader(tiny_gguf).tensors
+                if t.tensor_type in (gguf.GGMLQuantizationType.Q8_0, gguf.GGMLQuantizationType.Q4_0))
+    m = b2decode.Model(tiny_gguf)
+    s = m.load_stats()
+    assert s["mapped"] == 1 and s["host_threads"] >= 1
+    assert s["bytes_uploaded"] == quant
+    assert 0 < s["parse_ns"] < s["total_ns"] and 0 < s["upload_ns"] < s["total_ns"]
+    assert 0 <= s["host_copy_ns"] <= s["upload_ns"]
+    m.close()
 
 
 def test_context_overflow_and_reset(built_lib, tiny_gguf):
