@@ -48,7 +48,7 @@ class LoadOpts(C.Structure):
 class LoadStats(C.Structure):
     _fields_ = [("total_ns", C.c_int64), ("parse_ns", C.c_int64), ("upload_ns", C.c_int64),
                 ("host_copy_ns", C.c_int64), ("bytes_uploaded", C.c_int64), ("host_threads", C.c_int32),
-                ("mapped", C.c_int32)]
+                ("mapped", C.c_int32), ("setup_ns", C.c_int64)]
 
 
 class Config(C.Structure):

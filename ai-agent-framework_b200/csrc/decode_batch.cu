@@ -16,6 +16,7 @@
 // The tile dots are the batched matvec over the resident tiled weights
 // (matvec_batch.cu).  A slot's prompt runs through the same launches in
 // chunks of up to 16 of its tokens.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -142,139 +143,209 @@ __global__ void __launch_bounds__(kNormThreads) bd_rmsnorm_kernel(const float* _
     }
 }
 
-// The GEMM's input form of one token's row (gemm.h): scaled by 2^e so the
-// largest magnitude lies in [2^14, 2^15), fp16, scale 2^-e.  mx is the
-// row's largest magnitude (the CTA's reduction).
-__device__ __forceinline__ float f16_row_up(float mx, float* scale_out) {
-    int e = 0;
-    if (mx > 0.0f && isfinite(mx)) {
-        int ex;
-        frexpf(mx, &ex);  // mx in [2^(ex-1), 2^ex)
-        e = 15 - ex;
-    }
-    if (threadIdx.x == 0) *scale_out = ldexpf(1.0f, -e);
-    return ldexpf(1.0f, e);
+// Split-K partial planes summed in plane order: the k (<= kMaxPlanes) loads
+// are issued together (predicated, unrolled) so they overlap in flight.
+constexpr int kMaxPlanes = 8;
+__device__ __forceinline__ float4 sum_planes4(const float* p, size_t plane, int k) {
+    float4 v[kMaxPlanes];
+#pragma unroll
+    for (int s = 0; s < kMaxPlanes; s++)
+        if (s < k) v[s] = __ldcg(reinterpret_cast<const float4*>(p + s * plane));
+    float4 r = v[0];
+#pragma unroll
+    for (int s = 1; s < kMaxPlanes; s++)
+        if (s < k) {
+            r.x += v[s].x; r.y += v[s].y; r.z += v[s].z; r.w += v[s].w;
+        }
+    return r;
 }
+__device__ __forceinline__ float2 sum_planes2(const float* p, size_t plane, int k) {
+    float2 v[kMaxPlanes];
+#pragma unroll
+    for (int s = 0; s < kMaxPlanes; s++)
+        if (s < k) v[s] = __ldcg(reinterpret_cast<const float2*>(p + s * plane));
+    float2 r = v[0];
+#pragma unroll
+    for (int s = 1; s < kMaxPlanes; s++)
+        if (s < k) {
+            r.x += v[s].x; r.y += v[s].y;
+        }
+    return r;
+}
+
+// The GEMM's input form of one token's row (gemm.h): scaled by 2^e so the
+// largest magnitude lies in [2^14, 2^15), fp16, scale 2^-e.
 __device__ __forceinline__ void st_f16x4(__half* p, float4 v, float up) {
     const __half2 a = __floats2half2_rn(v.x * up, v.y * up), b = __floats2half2_rn(v.z * up, v.w * up);
     *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
 }
-__device__ float block_max512(float v, float* red) {
+
+// The residual update and the next RMSNorm in one pass: x += the split-K
+// partials of the product that ends the sub-block (k planes, summed in
+// plane order, then added: as a separate sum and add would), then
+// transformer.go:922-932 rmsNorm of the new x written in the GEMM's input
+// form (xh row, scale) for the next product, and as fp32 into xn when xn is
+// given.  Each row is spread over a cluster of kRowCtas CTAs (one slice
+// each); the row's sum of squares and largest magnitude are combined over
+// the cluster through distributed shared memory (every CTA reads every
+// partial in rank order, so all agree).  Grid R * kRowCtas; H a multiple of
+// 4 kRowCtas, at most 4 kRowCtas kRowThreads kAddVec.
+namespace cg = cooperative_groups;
+constexpr int kRowCtas = 8;
+constexpr int kRowThreads = 128;
+constexpr int kAddVec = 4;  // float4 per thread
+
+__device__ float cluster_sum_ranked(cg::cluster_group& cl, float* mine, float v) {
+    // v: this CTA's partial (thread 0 writes it); the cluster's sum in rank order
+    if (threadIdx.x == 0) *mine = v;
+    cl.sync();
+    float t = 0.0f;
+    for (int r = 0; r < kRowCtas; r++) t += *cl.map_shared_rank(mine, r);
+    return t;
+}
+__device__ float cluster_max_ranked(cg::cluster_group& cl, float* mine, float v) {
+    if (threadIdx.x == 0) *mine = v;
+    cl.sync();
+    float t = 0.0f;
+    for (int r = 0; r < kRowCtas; r++) t = fmaxf(t, *cl.map_shared_rank(mine, r));
+    return t;
+}
+__device__ float block_sum128(float v, float* red) {
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    v = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRowThreads / 32; i++) v += red[i];
+    return v;
+}
+__device__ float block_max128(float v, float* red) {
     for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    __syncthreads();  // (red may still be read by a previous reduction)
+    __syncthreads();
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
     v = red[0];
 #pragma unroll
-    for (int i = 1; i < kNormThreads / 32; i++) v = fmaxf(v, red[i]);
+    for (int i = 1; i < kRowThreads / 32; i++) v = fmaxf(v, red[i]);
     return v;
 }
 
-// The residual update and the next RMSNorm in one pass per row: x += the
-// split-K partials of the product that ends the sub-block (k planes, summed
-// in plane order, then added: as a separate sum and add would), then
-// transformer.go:922-932 rmsNorm of the new x written in the GEMM's input
-// form (xh row, scale) for the next product, and as fp32 into xn when xn is
-// given.  One CTA of kNormThreads per row; H a multiple of 4, at most
-// 4 * kNormVec * kNormThreads.
-__global__ void __launch_bounds__(kNormThreads) bd_add_norm_f16_kernel(float* __restrict__ x, const float* __restrict__ part,
-                                                                        int k, size_t plane, const float* __restrict__ w,
-                                                                        int H, float eps, __half* __restrict__ xh,
-                                                                        int xh_ld, float* __restrict__ tsc,
-                                                                        float* __restrict__ xn) {
-    __shared__ float red[kNormThreads / 32];
-    __shared__ float rs;
-    const int b = blockIdx.x, n4 = H / 4;
+__global__ void __cluster_dims__(kRowCtas, 1, 1) __launch_bounds__(kRowThreads)
+    bd_add_norm_f16_kernel(float* __restrict__ x, const float* __restrict__ part, int k, size_t plane,
+                              const float* __restrict__ w, int H, float eps, __half* __restrict__ xh, int xh_ld,
+                              float* __restrict__ tsc, float* __restrict__ xn) {
+    __shared__ float red[kRowThreads / 32];
+    __shared__ float c_ss, c_mx;
+    cg::cluster_group cl = cg::this_cluster();
+    const int b = blockIdx.x / kRowCtas, c = (int)cl.block_rank();
+    const int n4 = H / 4 / kRowCtas;  // float4 of this CTA's slice
     float4* xb = reinterpret_cast<float4*>(x + (size_t)b * H);
-    const float4* wv = reinterpret_cast<const float4*>(w);
-    float4 v[kNormVec];
+    float4 u[kAddVec];
     float ss = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < kNormVec; kk++) {
-        const int i = threadIdx.x + kk * kNormThreads;
-        v[kk] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (i < n4) {
-            float4 u = xb[i];
+    for (int v = 0; v < kAddVec; v++) {
+        const int t = threadIdx.x + v * kRowThreads, i = c * n4 + t;
+        u[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (t < n4) {
+            u[v] = xb[i];
             if (k > 0) {
-                const float4* pp = reinterpret_cast<const float4*>(part + (size_t)b * H) + i;
-                float4 sum = __ldcg(pp);
-                for (int s = 1; s < k; s++) {
-                    const float4 t = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(pp) + s * plane));
-                    sum.x += t.x; sum.y += t.y; sum.z += t.z; sum.w += t.w;
-                }
-                u.x += sum.x; u.y += sum.y; u.z += sum.z; u.w += sum.w;
-                xb[i] = u;
+                const float4 s = sum_planes4(part + (size_t)b * H + 4 * i, plane, k);
+                u[v].x += s.x; u[v].y += s.y; u[v].z += s.z; u[v].w += s.w;
+                xb[i] = u[v];
             }
-            v[kk] = u;
         }
-        ss = fmaf(v[kk].x, v[kk].x, fmaf(v[kk].y, v[kk].y, fmaf(v[kk].z, v[kk].z, fmaf(v[kk].w, v[kk].w, ss))));
+        ss = fmaf(u[v].x, u[v].x, fmaf(u[v].y, u[v].y, fmaf(u[v].z, u[v].z, fmaf(u[v].w, u[v].w, ss))));
     }
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float t = 0.0f;
-        for (int i = 0; i < kNormThreads / 32; i++) t += red[i];
-        rs = (float)(1.0 / sqrt((double)(t / (float)H) + (double)eps));
-    }
-    __syncthreads();
-    const float r = rs;
+    ss = cluster_sum_ranked(cl, &c_ss, block_sum128(ss, red));
+    const float r = (float)(1.0 / sqrt((double)(ss / (float)H) + (double)eps));
     float mx = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < kNormVec; kk++) {
-        const int i = threadIdx.x + kk * kNormThreads;
-        if (i < n4) {
-            const float4 gg = __ldg(wv + i);
-            v[kk] = make_float4(v[kk].x * r * gg.x, v[kk].y * r * gg.y, v[kk].z * r * gg.z, v[kk].w * r * gg.w);
-            if (xn) reinterpret_cast<float4*>(xn + (size_t)b * H)[i] = v[kk];
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[kk].x), fabsf(v[kk].y)), fmaxf(fabsf(v[kk].z), fabsf(v[kk].w))));
+    for (int v = 0; v < kAddVec; v++) {
+        const int t = threadIdx.x + v * kRowThreads, i = c * n4 + t;
+        if (t < n4) {
+            const float4 gg = __ldg(reinterpret_cast<const float4*>(w) + i);
+            u[v] = make_float4(u[v].x * r * gg.x, u[v].y * r * gg.y, u[v].z * r * gg.z, u[v].w * r * gg.w);
+            if (xn) reinterpret_cast<float4*>(xn + (size_t)b * H)[i] = u[v];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(u[v].x), fabsf(u[v].y)), fmaxf(fabsf(u[v].z), fabsf(u[v].w))));
         }
     }
-    mx = block_max512(mx, red);
-    const float up = f16_row_up(mx, tsc + b);
-#pragma unroll
-    for (int kk = 0; kk < kNormVec; kk++) {
-        const int i = threadIdx.x + kk * kNormThreads;
-        if (i < n4) st_f16x4(xh + (size_t)b * xh_ld + 4 * i, v[kk], up);
+    mx = cluster_max_ranked(cl, &c_mx, block_max128(mx, red));
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+        int ex;
+        frexpf(mx, &ex);
+        e = 15 - ex;
     }
+    if (c == 0 && threadIdx.x == 0) tsc[b] = ldexpf(1.0f, -e);
+    const float up = ldexpf(1.0f, e);
+#pragma unroll
+    for (int v = 0; v < kAddVec; v++) {
+        const int t = threadIdx.x + v * kRowThreads, i = c * n4 + t;
+        if (t < n4) st_f16x4(xh + (size_t)b * xh_ld + 4 * i, u[v], up);
+    }
+    cl.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 // transformer.go:725-727, 954-956 SwiGLU over the split-K partials of the
 // interleaved gate/up product (output j of tile t: gate at row 16t + j % 8,
 // up 8 rows below), written in the GEMM's input form for the down product.
-// One CTA of kNormThreads per row, the row's activations kept in registers
-// (FF up to kSwigluVec * kNormThreads).
-constexpr int kSwigluVec = 32;
-__global__ void __launch_bounds__(kNormThreads) bd_swiglu_f16_kernel(const float* __restrict__ part, int k, size_t plane,
-                                                                      int FF, __half* __restrict__ xh, int xh_ld,
-                                                                      float* __restrict__ tsc) {
-    __shared__ float red[kNormThreads / 32];
-    const int b = blockIdx.x;
+// Each row is spread over a cluster of kRowCtas CTAs (CTA c: outputs
+// c FF / kRowCtas onwards, consecutive lanes on consecutive outputs; all of
+// a thread's loads issued before any is used); the row's largest magnitude
+// through distributed shared memory.  FF a multiple of 8 kRowCtas, at most
+// kRowCtas kRowThreads kSwClVec.
+constexpr int kSwClVec = 16;
+__global__ void __cluster_dims__(kRowCtas, 1, 1) __launch_bounds__(kRowThreads)
+    bd_swiglu_f16_kernel(const float* __restrict__ part, int k, size_t plane, int FF, __half* __restrict__ xh,
+                            int xh_ld, float* __restrict__ tsc) {
+    __shared__ float red[kRowThreads / 32];
+    __shared__ float c_mx;
+    cg::cluster_group cl = cg::this_cluster();
+    const int b = blockIdx.x / kRowCtas, c = (int)cl.block_rank();
     const float* row = part + (size_t)b * 2 * FF;
-    float act[kSwigluVec];
-    float mx = 0.0f;
+    const int per = FF / kRowCtas;  // this CTA's outputs: c per .. (c + 1) per - 1
+    float gv[kSwClVec], uv[kSwClVec];
 #pragma unroll
-    for (int kk = 0; kk < kSwigluVec; kk++) {
-        const int j = threadIdx.x + kk * kNormThreads;
-        act[kk] = 0.0f;
-        if (j < FF) {
-            const size_t o = (size_t)(j >> 3) * 16 + (j & 7);
-            float gv = __ldcg(row + o), uv = __ldcg(row + o + 8);
-            for (int s = 1; s < k; s++) {
-                gv += __ldcg(row + s * plane + o);
-                uv += __ldcg(row + s * plane + o + 8);
+    for (int kk = 0; kk < kSwClVec; kk++) {
+        const int jj = kk * kRowThreads + threadIdx.x, j = c * per + jj;
+        const size_t o = (size_t)(j >> 3) * 16 + (j & 7);
+        gv[kk] = jj < per ? __ldcg(row + o) : 0.0f;
+        uv[kk] = jj < per ? __ldcg(row + o + 8) : 0.0f;
+    }
+    for (int s = 1; s < k; s++) {
+#pragma unroll
+        for (int kk = 0; kk < kSwClVec; kk++) {
+            const int jj = kk * kRowThreads + threadIdx.x, j = c * per + jj;
+            const size_t o = s * plane + (size_t)(j >> 3) * 16 + (j & 7);
+            if (jj < per) {
+                gv[kk] += __ldcg(row + o);
+                uv[kk] += __ldcg(row + o + 8);
             }
-            act[kk] = gv / (1.0f + expf(-gv)) * uv;
-            mx = fmaxf(mx, fabsf(act[kk]));
         }
     }
-    mx = block_max512(mx, red);
-    const float up = f16_row_up(mx, tsc + b);
+    float mx = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < kSwigluVec; kk++) {
-        const int j = threadIdx.x + kk * kNormThreads;
-        if (j < FF) xh[(size_t)b * xh_ld + j] = __float2half_rn(act[kk] * up);
+    for (int kk = 0; kk < kSwClVec; kk++) {
+        const int jj = kk * kRowThreads + threadIdx.x, j = c * per + jj;
+        gv[kk] = jj < per ? gv[kk] / (1.0f + expf(-gv[kk])) * uv[kk] : 0.0f;
+        mx = fmaxf(mx, fabsf(gv[kk]));
     }
+    mx = cluster_max_ranked(cl, &c_mx, block_max128(mx, red));
+    int e = 0;
+    if (mx > 0.0f && isfinite(mx)) {
+        int ex;
+        frexpf(mx, &ex);
+        e = 15 - ex;
+    }
+    const float up = ldexpf(1.0f, e);
+    if (c == 0 && threadIdx.x == 0) tsc[b] = ldexpf(1.0f, -e);
+#pragma unroll
+    for (int kk = 0; kk < kSwClVec; kk++) {
+        const int jj = kk * kRowThreads + threadIdx.x, j = c * per + jj;
+        if (jj < per) xh[(size_t)b * xh_ld + j] = __float2half_rn(gv[kk] * up);
+    }
+    cl.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 // transformer.go:632-656: bias, RoPE on interleaved pairs of every q and k
@@ -288,14 +359,9 @@ __global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, int k, size_t p
                                   __half* __restrict__ vc, int qd, int kvd, int hd, int slot_stride) {
     const int b = blockIdx.x, p = pos[b], n = qd + 2 * kvd, hh = hd / 2;
     const float* row = qkv + (size_t)b * n;
-    for (int j = threadIdx.x; j < n / 2; j += blockDim.x) {
+    for (int j = blockIdx.y * blockDim.x + threadIdx.x; j < n / 2; j += gridDim.y * blockDim.x) {
         const int r = 2 * j;
-        float2 a = __ldcg(reinterpret_cast<const float2*>(row + r));
-        for (int s = 1; s < k; s++) {
-            const float2 t = __ldcg(reinterpret_cast<const float2*>(row + s * plane + r));
-            a.x += t.x;
-            a.y += t.y;
-        }
+        const float2 a = sum_planes2(row + r, plane, k);
         float a0 = a.x, a1 = a.y;
         if (bias) {
             a0 += bias[r];
@@ -575,7 +641,7 @@ unsigned long long scratch_generation(cudaStream_t s) {
 // RoPE launch and the gate/up sum in the SwiGLU launch.
 bool tc_rows_ok(const ModelDev& d, int R) {
     return R >= kGemmMinRows && R <= kPrefillChunk && d.H % 64 == 0 && d.qd % 64 == 0 && d.FF % 64 == 0 &&
-           d.H <= 4 * kNormVec * kNormThreads && d.FF <= kSwigluVec * kNormThreads;
+           d.H <= 4 * kRowCtas * kRowThreads * kAddVec && d.FF <= kRowCtas * kRowThreads * kSwClVec;
 }
 
 int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err,
@@ -583,21 +649,23 @@ int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_st
     b2_model* m = bt->m;
     const ModelDev& d = m->dev;
     cudaStream_t s = m->stream;
-    const int H = d.H, qt = d.qtype, n_qkv = d.qd + 2 * d.kvd, ld = bt->xh_ld;
+    // (xh rows are as long as the product that reads them: H, or FF for down)
+    const int H = d.H, qt = d.qtype, n_qkv = d.qd + 2 * d.kvd;
     bd_embed_kernel<<<R, kBdThreads, 0, s>>>(d.tok_embd, d.Vemb, d.Vp_emb, H, qt, bt->d_tok, bt->x);
     const size_t kv_layer = (size_t)bt->B * bt->max_seq * d.kvd;
     GemmParts prev;  // the partials still to be added to x (none before layer 0)
     int rc = B2_OK;
     for (int l = 0; l < d.L && rc == B2_OK; l++) {
         const LayerDev& lw = m->layers_host[l];
-        bd_add_norm_f16_kernel<<<R, kNormThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, lw.attn_norm, H, d.eps,
-                                                          bt->xh, ld, bt->tsc, nullptr);
+        bd_add_norm_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, lw.attn_norm, H, d.eps,
+                                                          bt->xh, H, bt->tsc, nullptr);
         GemmParts p;
         rc = b2_tiled_gemm_f16_impl(qt, lw.wqkv, tiled_rows(n_qkv), 0, n_qkv, H, bt->xh, bt->tsc, R, bt->qkv, &p, s, err);
         if (rc) break;
         __half* kc = bt->kc + (size_t)l * kv_layer + kv_off;
         __half* vc = bt->vc + (size_t)l * kv_layer + kv_off;
-        bd_rope_kv_kernel<<<R, kBdThreads, 0, s>>>(p.p, p.k, p.plane, lw.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc,
+        bd_rope_kv_kernel<<<dim3(R, (n_qkv / 2 + kBdThreads - 1) / kBdThreads), kBdThreads, 0, s>>>(
+            p.p, p.k, p.plane, lw.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc,
                                                    vc, d.qd, d.kvd, d.hd, slot_stride);
         rc = b2_attention_seqs_launch(bt->q, kc, vc, bt->part, bt->part_floats, bt->att, R, d.nh, d.nkv, d.hd, d_rpos,
                                       1, slot_stride, max_len, m->grid, s);
@@ -607,22 +675,22 @@ int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_st
         }
         rc = b2_tiled_gemm_impl(qt, lw.wo, tiled_rows(H), 0, H, d.qd, bt->att, bt->y, R, &p, s, err);
         if (rc) break;
-        bd_add_norm_f16_kernel<<<R, kNormThreads, 0, s>>>(bt->x, p.p, p.k, p.plane, lw.ffn_norm, H, d.eps, bt->xh, ld,
+        bd_add_norm_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(bt->x, p.p, p.k, p.plane, lw.ffn_norm, H, d.eps, bt->xh, H,
                                                           bt->tsc, nullptr);
         rc = b2_tiled_gemm_f16_impl(qt, lw.wgu, tiled_rows(2 * d.FF), 0, 2 * d.FF, H, bt->xh, bt->tsc, R, bt->gu, &p, s,
                                     err);
         if (rc) break;
-        bd_swiglu_f16_kernel<<<R, kNormThreads, 0, s>>>(p.p, p.k, p.plane, d.FF, bt->xh, ld, bt->tsc);
+        bd_swiglu_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(p.p, p.k, p.plane, d.FF, bt->xh, d.FF, bt->tsc);
         rc = b2_tiled_gemm_f16_impl(qt, lw.wd, tiled_rows(H), 0, H, d.FF, bt->xh, bt->tsc, R, bt->y, &prev, s, err);
     }
     if (rc) return rc;
     // the last down product's partials, the output norm: fp32 rows in xn (for
     // a one-row lm_head on the batched matvec) and the GEMM's form in xh
-    bd_add_norm_f16_kernel<<<R, kNormThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, d.out_norm, H, d.eps, bt->xh,
-                                                      ld, bt->tsc, bt->xn);
+    bd_add_norm_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, d.out_norm, H, d.eps, bt->xh,
+                                                      H, bt->tsc, bt->xn);
     const int r_lm = all_logits ? 0 : R - 1, n_lm = all_logits ? R : 1;
     if (n_lm >= kGemmMinRows)
-        rc = b2_tiled_gemm_f16_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xh + (size_t)r_lm * ld, bt->tsc + r_lm, n_lm,
+        rc = b2_tiled_gemm_f16_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xh + (size_t)r_lm * H, bt->tsc + r_lm, n_lm,
                                     bt->logits, nullptr, s, err);
     else
         rc = b2_tiled_matvec_batch_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xn + (size_t)r_lm * H, bt->logits, n_lm, s,

@@ -591,8 +591,10 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     uint64_t up_bytes = 0;
     int up_threads = 0;
     bool up_mapped = false;
+    int64_t up_setup_ns = 0;
     {
         Uploader up(path, m->stream);
+        up_setup_ns = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t_up0).count();
         if (!up.ok()) {
             const bool oom = up.error().find("allocation") != std::string::npos;
             return bail(oom ? B2_ERR_OOM : B2_ERR_IO, up.error());
@@ -677,6 +679,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     m->load.bytes_uploaded = (int64_t)up_bytes;
     m->load.host_threads = up_threads;
     m->load.mapped = up_mapped ? 1 : 0;
+    m->load.setup_ns = up_setup_ns;
 
     // RoPE table with the Go formula (transformer.go:939-942): freq in float64
     // pow rounded to float32, angle in float32, cos/sin in float64 rounded.

@@ -61,6 +61,9 @@ struct SampleSmem {
     int lidx[kSampleCap];         // compacted set: vocabulary index (ascending)
     float lval[kSampleCap];       //                logit
     float le[kSampleCap];         //                exp(logit - max)
+    unsigned long long gsum[160];  // a group's per-CTA values, staged from global memory
+    float gmax[160];
+    int gcnt[160];
     int sel, nlist, tie_last, out, ok;
     uint32_t thr_key;
     unsigned long long above;
@@ -254,7 +257,8 @@ __device__ int draw(const Set& S, const Cut& cut, float r, int n_vocab, SampleSm
 // global memory at group barriers (bounded waits: a barrier that is not met
 // within kSampleWaitNs sets the row's error and every CTA returns).
 
-constexpr int kMcMaxG = 160;
+constexpr int kMcMaxG = 160;  // (the group arrays of SampleSmem hold this many)
+constexpr int kSliceLogits = 4096;
 constexpr uint64_t kSampleWaitNs = 1000000000ull;
 
 struct McRow {
@@ -311,14 +315,29 @@ __device__ bool grp_sync(Grp& G, SampleSmem& s) {
     return s.ok != 0;
 }
 
+// Global tables and per-CTA values are read once, by many threads in
+// parallel, into shared memory before one thread walks them (a walk over
+// global memory would be a chain of L2 round trips).
+__device__ void stage_u32(const unsigned* src, int n, unsigned* dst) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kSampleThreads) dst[i] = __ldcg(src + i);
+    __syncthreads();
+}
+__device__ void stage_u64(const unsigned long long* src, int n, unsigned long long* dst) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += kSampleThreads) dst[i] = __ldcg(src + i);
+    __syncthreads();
+}
+
 // The digit selection every CTA of the group makes from the same table
 // (walking the digits from the largest key): the count form of top-K.
 __device__ void select_count(const unsigned* h, int krem, SampleSmem& s) {
+    stage_u32(h, 256, s.hc);
     if (threadIdx.x == 0) {
         int c = 0, sel = 0;
         for (int b = 255; b >= 0; b--) {
-            if (c + (int)h[b] >= krem) { sel = b; break; }
-            c += (int)h[b];
+            if (c + (int)s.hc[b] >= krem) { sel = b; break; }
+            c += s.hc[b];
         }
         s.sel = sel;
         s.above = (unsigned long long)c;
@@ -349,7 +368,7 @@ __device__ bool mc_kth_key(Grp& G, const float* L, int k, SampleSmem& s, uint32_
         greater += c;
         prefix |= (uint32_t)sel << shift;
         pmask |= 255u << shift;
-        if (rd == 3) *n_keep = greater + (int)G.sc->hk[3][sel];
+        if (rd == 3) *n_keep = greater + (int)s.hc[sel];
         __syncthreads();
     }
     *thr = prefix;
@@ -376,9 +395,10 @@ __device__ bool mc_compact_ge(Grp& G, const float* L, uint32_t thr, SampleSmem& 
         G.sc->pcnt[G.g] = t;
     }
     if (!grp_sync(G, s)) return false;
+    stage_u32(reinterpret_cast<const unsigned*>(G.sc->pcnt), G.G, reinterpret_cast<unsigned*>(s.gcnt));
     int base = 0, total = 0;
     for (int h = 0; h < G.G; h++) {
-        const int c = G.sc->pcnt[h];
+        const int c = s.gcnt[h];
         if (h < G.g) base += c;
         total += c;
     }
@@ -428,12 +448,14 @@ __device__ bool mc_top_p_cut(Grp& G, const float* L, const float* E, double P, S
             atomicAdd(&G.sc->hm[rd][threadIdx.x], s.hm[threadIdx.x]);
         }
         if (!grp_sync(G, s)) return false;
+        stage_u32(G.sc->hc[rd], 256, s.hc);
+        stage_u64(G.sc->hm[rd], 256, s.hm);
         if (threadIdx.x == 0) {
             unsigned long long acc = above;
             int sel = -1;
             for (int b = 255; b >= 0; b--) {
-                if ((double)(acc + G.sc->hm[rd][b]) >= P) { sel = b; break; }
-                acc += G.sc->hm[rd][b];
+                if ((double)(acc + s.hm[b]) >= P) { sel = b; break; }
+                acc += s.hm[b];
             }
             s.sel = sel;
             s.above = acc;
@@ -447,8 +469,8 @@ __device__ bool mc_top_p_cut(Grp& G, const float* L, const float* E, double P, S
         above = s.above;
         prefix |= (uint32_t)sel << shift;
         pmask |= 255u << shift;
-        ties = (int)G.sc->hc[rd][sel];
-        tie_mass = G.sc->hm[rd][sel];
+        ties = (int)s.hc[sel];
+        tie_mass = s.hm[sel];
         __syncthreads();
     }
     const double q = (double)(tie_mass / (unsigned long long)ties);
@@ -471,9 +493,10 @@ __device__ bool mc_top_p_cut(Grp& G, const float* L, const float* E, double P, S
         G.sc->ptie[G.g] = t;
     }
     if (!grp_sync(G, s)) return false;
+    stage_u32(reinterpret_cast<const unsigned*>(G.sc->ptie), G.G, reinterpret_cast<unsigned*>(s.gcnt));
     long long before = 0;
-    for (int h = 0; h < G.g; h++) before += G.sc->ptie[h];
-    const long long mine = G.sc->ptie[G.g];
+    for (int h = 0; h < G.g; h++) before += s.gcnt[h];
+    const long long mine = s.gcnt[G.g];
     if (before < m && m <= before + mine && threadIdx.x < 32) {
         const int l = threadIdx.x;
         long long seen = before;
@@ -492,7 +515,7 @@ __device__ bool mc_top_p_cut(Grp& G, const float* L, const float* E, double P, S
         }
     }
     if (!grp_sync(G, s)) return false;
-    *cut = Cut{prefix, G.sc->tie_last};
+    *cut = Cut{prefix, __ldcg(&G.sc->tie_last)};
     return true;
 }
 
@@ -525,14 +548,15 @@ __device__ int mc_draw(Grp& G, const float* L, const float* E, const Cut& cut, f
         *ok = false;
         return -2;
     }
+    stage_u64(G.sc->psum_d, G.G, s.gsum);
     if (threadIdx.x == 0) {
         unsigned long long tot = 0;
-        for (int h = 0; h < G.G; h++) tot += G.sc->psum_d[h];
+        for (int h = 0; h < G.G; h++) tot += s.gsum[h];
         const double R = (double)r * (double)tot;
         unsigned long long acc = 0;
         int hsel = -1;
         for (int h = 0; h < G.G; h++) {
-            const unsigned long long v = G.sc->psum_d[h];
+            const unsigned long long v = s.gsum[h];
             if (v > 0 && (double)(acc + v) >= R) { hsel = h; break; }
             acc += v;
         }
@@ -657,12 +681,16 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(const __grid_
             sc->pidx[g] = bi;
         }
         ok = grp_sync(grp, s);
-        if (ok && g == 0 && threadIdx.x == 0) {
-            int best = -1;
-            float v = -INFINITY;
-            for (int h = 0; h < G; h++)  // slices in vocabulary order: a later one wins only if larger
-                if (sc->pidx[h] >= 0 && (best < 0 || sc->pmax[h] > v)) { v = sc->pmax[h]; best = sc->pidx[h]; }
-            id = best < 0 ? 0 : best;
+        if (ok && g == 0) {
+            stage_u32(reinterpret_cast<const unsigned*>(sc->pmax), G, reinterpret_cast<unsigned*>(s.gmax));
+            stage_u32(reinterpret_cast<const unsigned*>(sc->pidx), G, reinterpret_cast<unsigned*>(s.gcnt));
+            if (threadIdx.x == 0) {
+                int best = -1;
+                float v = -INFINITY;
+                for (int h = 0; h < G; h++)  // slices in vocabulary order: a later one wins only if larger
+                    if (s.gcnt[h] >= 0 && (best < 0 || s.gmax[h] > v)) { v = s.gmax[h]; best = s.gcnt[h]; }
+                id = best < 0 ? 0 : best;
+            }
         }
     } else {
         float mx = -INFINITY;
@@ -675,8 +703,9 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(const __grid_
         if (threadIdx.x == 0) sc->pmax[g] = mx;
         ok = grp_sync(grp, s);
         if (ok) {
+            stage_u32(reinterpret_cast<const unsigned*>(sc->pmax), G, reinterpret_cast<unsigned*>(s.gmax));
             mx = -INFINITY;
-            for (int h = 0; h < G; h++) mx = fmaxf(mx, sc->pmax[h]);
+            for (int h = 0; h < G; h++) mx = fmaxf(mx, s.gmax[h]);
         }
         bool full = true;
         if (ok && a.top_k > 0 && a.top_k < n) {
@@ -689,8 +718,8 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(const __grid_
                 full = false;
                 if (ok && g == 0) {
                     for (int j = threadIdx.x; j < nl; j += kSampleThreads) {
-                        s.lidx[j] = sc->lidx[j];
-                        s.lval[j] = sc->lval[j];
+                        s.lidx[j] = __ldcg(&sc->lidx[j]);
+                        s.lval[j] = __ldcg(&sc->lval[j]);
                     }
                     __syncthreads();
                     id = list_filter_and_draw(nl, mx, a, a.r[row], s);
@@ -713,8 +742,9 @@ __global__ void __launch_bounds__(kSampleThreads, 1) sample_kernel(const __grid_
                 if (threadIdx.x == 0) sc->psum_s[g] = tot;
                 ok = grp_sync(grp, s);
                 if (ok) {
+                    stage_u64(sc->psum_s, G, s.gsum);
                     tot = 0;
-                    for (int h = 0; h < G; h++) tot += sc->psum_s[h];
+                    for (int h = 0; h < G; h++) tot += s.gsum[h];
                     ok = mc_top_p_cut(grp, L, E, (double)a.top_p * (double)tot, s, &cut);
                 }
             }
@@ -756,7 +786,9 @@ int launch_sample(const SampleArgs& a0, int rows, cudaStream_t s, std::string* e
     }
     SampleArgs a = a0;
     a.rows = rows;
-    a.group = std::max(1, std::min(kMcMaxG, sms * per_sm / rows));
+    // about 4096 logits a CTA: a group barrier costs more with every CTA it
+    // waits for, and a slice that small is a few loads per thread
+    a.group = std::max(1, std::min({kMcMaxG, sms * per_sm / rows, (a.n + kSliceLogits - 1) / kSliceLogits}));
     a.e_ld = (long long)((((size_t)a.n * 4 + 255) & ~size_t(255)) / 4);
     // the rows' barrier counters and digit tables start from zero
     for (int r = 0; r < rows; r++)

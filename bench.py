@@ -533,7 +533,7 @@ def _load_summary(m, load_s: float) -> dict:
     s = m.load_stats()
     up = s["upload_ns"] / 1e9
     return {"wall_s": load_s, "b2_load_s": s["total_ns"] / 1e9, "parse_s": s["parse_ns"] / 1e9, "upload_s": up,
-            "host_copy_s": s["host_copy_ns"] / 1e9, "weight_bytes": s["bytes_uploaded"],
+            "host_copy_s": s["host_copy_ns"] / 1e9, "setup_s": s["setup_ns"] / 1e9, "weight_bytes": s["bytes_uploaded"],
             "upload_gbs": s["bytes_uploaded"] / up / 1e9 if up > 0 else None, "host_threads": s["host_threads"],
             "file": "memory-mapped" if s["mapped"] else "pread"}
 
@@ -632,7 +632,10 @@ def run_attention(args) -> None:
             gbs = kvbytes / (ms / 1000.0) / 1e9
             print(json.dumps({
                 "metric": "GQA decode attention GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
-                "higher_is_better": True, "dtype": "fp16 KV, fp32 math", "data": "synthetic",
+                "higher_is_better": True,
+                "dtype": "fp16 KV; q and the probabilities split into two fp16 terms each on mma.m16n8k16, fp32 "
+                         "accumulate and softmax",
+                "data": "synthetic",
                 "config": {"workload": f"attention nh {nh} nkv {nkv} hd {hd} ctx {ctx} batch {B}",
                            "us_per_call": ms * 1000.0, "kv_bytes": kvbytes, "l2": f"{ncp} KV copies rotated"},
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
@@ -812,16 +815,20 @@ def run_batch(args) -> None:
     print(json.dumps({
         "metric": f"batched decode tok/s (B={B})", "value": B * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": 1,
         "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32 (int8 planes x Q weights)", "data": "synthetic",
+        "vs_baseline": None,
+        "dtype": (f"{shape.wtype.upper()} weights -> fp16 (d*q rounded once) x fp16 activations (power-of-two "
+                  f"scale per token), fp32 accumulate (tcgen05 kind::f16)"),
+        "data": "synthetic",
         "config": {"workload": f"{shape_name}-shape {shape.wtype} batched greedy decode, batch {B}, "
                                f"prompt {n_prompt} ids per sequence",
-                   "launches": "one CUDA graph per step" if args.graph else "eager (about 15 per layer)",
+                   "launches": "one CUDA graph per step" if args.graph else "eager (11 per layer)",
                    "prompt_tokens": n_prompt + 1, "prefill_s": prefill_s,
                    "prefill_tok_s": B * (n_prompt + 1) / prefill_s,
                    # 2 flops per weight per token; weights = streamed bytes x 32 / (bytes per 32-block)
                    "prefill_tflops": 2.0 * bytes_step * 32 / (34 if shape.wtype == "q8_0" else 18)
                                      * B * (n_prompt + 1) / prefill_s / 1e12,
-                   "prefill_path": "b2_batch_prefill: chunks of 16 prompt tokens, one weight pass each",
+                   "prefill_path": "b2_batch_prefill: chunks of up to 128 prompt tokens, one weight pass each on "
+                                   "the tcgen05 GEMM, the chunk's attention over the slot's cache",
                    "l2": f"no flush needed: each step streams {bytes_step / 1e6:.0f} MB of weights"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "algorithmic_bytes_per_step": bytes_step},

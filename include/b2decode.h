@@ -119,6 +119,7 @@ typedef struct {
     int64_t bytes_uploaded;  /* weight bytes sent through the stages */
     int32_t host_threads;
     int32_t mapped;          /* 1: memory-mapped file; 0: pread */
+    int64_t setup_ns;        /* of upload_ns: mapping the file, pinned stages, thread pool */
 } b2_load_stats;
 int b2_get_load_stats(const b2_model* m, b2_load_stats* out);
 /* Message of the last failure on this thread ("" if none). */
