@@ -528,10 +528,12 @@ __global__ void attn_merge_kernel(const float* __restrict__ part, float* __restr
 
 }  // namespace
 
-// Context splits per (sequence, KV head): at least two CTAs per SM, at
-// least 64 positions a split, and among up to four times that many the
-// count whose CTAs fill their last wave best (one CTA per SM: the
-// tensor-core form's shared memory), so no wave runs a few CTAs alone.
+// Context splits per (sequence, KV head): at least two CTAs per SM and at
+// least 64 positions a split; then, while every split keeps at least 256
+// positions (four K / V tiles: the per-CTA setup stays small against them),
+// among up to four times as many the count whose CTAs fill their last wave
+// best (one CTA per SM: the tensor-core form's shared memory), so no wave
+// runs a few CTAs alone.
 int attention_splits(int batch, int nkv, int ctx, int sms) {
     const int units = std::max(1, batch * nkv);
     const int want = (2 * sms + units - 1) / units;
@@ -541,7 +543,7 @@ int attention_splits(int batch, int nkv, int ctx, int sms) {
         const long long ctas = (long long)units * s, waves = (ctas + sms - 1) / sms;
         return (double)ctas / (double)(waves * sms);
     };
-    for (int s = best + 1; s <= std::min(4 * want, by_len); s++)
+    for (int s = best + 1; s <= std::min(4 * want, ctx / 256); s++)
         if (fill(s) > fill(best) + 1e-9) best = s;
     return best;
 }
