@@ -41,5 +41,8 @@ int b2_tiled_gemm_half_impl(int qtype, const void* base, int64_t rp, int half, i
                             float* y, int ntok, cudaStream_t s, std::string* err);
 // Device error flag of stream s's GEMM scratch (0 if none); clears it.
 int b2_gemm_status(cudaStream_t s);
+// Frees the GEMM scratch of stream s on device dev (a stream about to be
+// destroyed; nothing of it may still run).
+void b2_gemm_release(int dev, cudaStream_t s);
 // Changes whenever stream s's GEMM scratch is reallocated.
 unsigned long long b2_gemm_scratch_generation(cudaStream_t s);

@@ -821,6 +821,20 @@ int b2_gemm_status(cudaStream_t s) {
 
 // Generation of the GEMM scratch of stream s (a CUDA graph that captured a
 // GEMM on s stays valid while it is unchanged).
+void b2_gemm_release(int dev, cudaStream_t s) {
+    std::lock_guard<std::mutex> lk(g_gemm_mu);
+    const auto it = g_gemm.find({dev, s});
+    if (it != g_gemm.end()) {
+        if (it->second.buf) cudaFree(it->second.buf);
+        g_gemm.erase(it);
+    }
+    const auto f = g_gemm_fused.find({dev, s});
+    if (f != g_gemm_fused.end()) {
+        if (f->second.first) cudaFree(f->second.first);
+        g_gemm_fused.erase(f);
+    }
+}
+
 unsigned long long b2_gemm_scratch_generation(cudaStream_t s) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;

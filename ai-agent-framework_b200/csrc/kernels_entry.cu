@@ -548,6 +548,9 @@ int attention_splits(int batch, int nkv, int ctx, int sms) {
     return best;
 }
 
+int matvec_lean(int qtype, const void* w, const float* x, float* y, int rows, int cols, int sms, cudaStream_t s,
+                std::string* err);
+
 }  // namespace b2
 
 using namespace b2;
@@ -556,6 +559,12 @@ int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows,
                    std::string* err) {
     DeviceScratch* sc = scratch_for_current(err);
     if (!sc) return B2_ERR_CUDA;
+    // Q8_0 rows of a multiple of 256 columns: the matvec kernel of its own;
+    // the rest: the decode kernel's single-phase mode
+    if (qtype == 8) {  // (Q4_0 rows stay on the path below: faster for them)
+        const int lean = matvec_lean(qtype, w, x, y, rows, cols, sc->sms, s, err);
+        if (lean <= 0) return lean;
+    }
     if (reinterpret_cast<uintptr_t>(w) & 15) {
         *err = "weight pointer must be 16-byte aligned";
         return B2_ERR_BAD_ARG;

@@ -640,6 +640,17 @@ int b2_tiled_matvec_batch_impl(int qtype, const void* base, int64_t rp, int64_t 
 
 // Generation of the scratch buffer of stream s on the current device: a CUDA
 // graph that captured batched matvecs on s is valid while this is unchanged.
+// Frees the batched matvec's scratch of stream s on device dev (a stream
+// about to be destroyed; nothing of it may still run).
+void b2_mvb_release(int dev, cudaStream_t s) {
+    std::lock_guard<std::mutex> lk(g_mvb_mu);
+    const auto it = g_mvb.find({dev, s});
+    if (it != g_mvb.end()) {
+        if (it->second.buf) cudaFree(it->second.buf);
+        g_mvb.erase(it);
+    }
+}
+
 unsigned long long b2_mvb_scratch_generation(cudaStream_t s) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;

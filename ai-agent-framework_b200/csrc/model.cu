@@ -18,9 +18,12 @@
 #include <cstring>
 #include <vector>
 
+#include "gemm.h"
 #include "model.h"
 #include "sample.h"
 #include "upload.h"
+
+void b2_mvb_release(int dev, cudaStream_t s);
 
 namespace b2 {
 
@@ -42,6 +45,8 @@ int dev_malloc(void** p, size_t bytes) {
 }
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+constexpr int kWarmTokens = 128;  // the prompt path's warm-up at load: one full chunk
 
 // gguf.go:616-643 float16ToFloat32 (host side, for small F16 vectors).
 float f16_to_f32(uint16_t h) {
@@ -906,6 +911,18 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
     }
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return bail(B2_ERR_CUDA, std::string("CUDA: ") + cudaGetErrorString(e));
+    // The prompt path's one-time costs (its workspace, the GEMM scratch, the
+    // first launch of each of its kernels) are paid here, by a warm-up pass of
+    // up to kWarmTokens BOS tokens at position 0; the cache stays empty (the
+    // next prompt overwrites those positions before anything reads them).  On
+    // failure the prompt path makes its workspace again when first used.
+    const int n_warm = std::min(kWarmTokens, S);
+    if (prefill_gemm_ok(m, n_warm)) {
+        const std::vector<int32_t> warm(n_warm, c.bos_id >= 0 && c.bos_id < c.vocab_size ? c.bos_id : 0);
+        std::string e2;
+        if (prefill_gemm(m, warm.data(), n_warm, 0, &e2) != B2_OK) free_prefill_ws(m);
+        m->cache_len = 0;
+    }
     m->load.total_ns = std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - t_load0).count();
     *out = m;
     return B2_OK;
@@ -924,7 +941,12 @@ void b2_free_impl(b2_model* m) {
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
     if (m->ev_pin) cudaEventDestroy(m->ev_pin);
-    if (m->stream) cudaStreamDestroy(m->stream);
+    if (m->stream) {
+        // the per-stream scratch of the products that ran on this stream
+        b2_gemm_release(m->device, m->stream);
+        b2_mvb_release(m->device, m->stream);
+        cudaStreamDestroy(m->stream);
+    }
     delete m;
 }
 
