@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(kAttThreads, (GRP <= 4 ? 2 : 1))
 // ---------------------------------------------------------------------------
 constexpr int kMmaThreads = 128;
 constexpr int kMmaTile = 64;   // positions per ring tile (16 per warp)
-constexpr int kMmaStages = 4;
+constexpr int kMmaStages = 3;
 constexpr int kMmaMaxGrp = 16;
 
 template <int HD>
@@ -528,22 +528,24 @@ __global__ void attn_merge_kernel(const float* __restrict__ part, float* __restr
 
 }  // namespace
 
-// Context splits per (sequence, KV head): at least two CTAs per SM and at
-// least 64 positions a split; then, while every split keeps at least 256
-// positions (four K / V tiles: the per-CTA setup stays small against them),
-// among up to four times as many the count whose CTAs fill their last wave
-// best (one CTA per SM: the tensor-core form's shared memory), so no wave
-// runs a few CTAs alone.
+// Context splits per (sequence, KV head): up to two CTAs per SM worth, or
+// more while every split keeps at least 256 positions (four K / V tiles:
+// the per-CTA setup stays small against them) up to four times that, never
+// under 64 positions a split; among those the count whose CTAs fill their
+// last wave best (two CTAs per SM: the tensor-core form's shared memory and
+// registers), the smallest on a tie, so no wave runs a few CTAs alone.
 int attention_splits(int batch, int nkv, int ctx, int sms) {
     const int units = std::max(1, batch * nkv);
-    const int want = (2 * sms + units - 1) / units;
+    const int slots = 2 * sms;
+    const int want = (slots + units - 1) / units;
     const int by_len = std::max(1, (ctx + 63) / 64);
-    int best = std::max(1, std::min(want, by_len));
+    const int cap = std::max(1, std::min(by_len, std::max(want, std::min(4 * want, ctx / 256))));
     auto fill = [&](int s) {
-        const long long ctas = (long long)units * s, waves = (ctas + sms - 1) / sms;
-        return (double)ctas / (double)(waves * sms);
+        const long long ctas = (long long)units * s, waves = (ctas + slots - 1) / slots;
+        return (double)ctas / (double)(waves * slots);
     };
-    for (int s = best + 1; s <= std::min(4 * want, ctx / 256); s++)
+    int best = 1;
+    for (int s = 2; s <= cap; s++)
         if (fill(s) > fill(best) + 1e-9) best = s;
     return best;
 }
