@@ -237,6 +237,7 @@ __global__ void __cluster_dims__(kRowCtas, 1, 1) __launch_bounds__(kRowThreads)
                               float* __restrict__ tsc, float* __restrict__ xn) {
     __shared__ float red[kRowThreads / 32];
     __shared__ float c_ss, c_mx;
+    pdl_trigger();
     cg::cluster_group cl = cg::this_cluster();
     const int b = blockIdx.x / kRowCtas, c = (int)cl.block_rank();
     const int n4 = H / 4 / kRowCtas;  // float4 of this CTA's slice
@@ -301,6 +302,7 @@ __global__ void __cluster_dims__(kRowCtas, 1, 1) __launch_bounds__(kRowThreads)
                             int xh_ld, float* __restrict__ tsc) {
     __shared__ float red[kRowThreads / 32];
     __shared__ float c_mx;
+    pdl_trigger();
     cg::cluster_group cl = cg::this_cluster();
     const int b = blockIdx.x / kRowCtas, c = (int)cl.block_rank();
     const float* row = part + (size_t)b * 2 * FF;
@@ -776,7 +778,8 @@ int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, 
     }
     if (!device_current(m, err)) return B2_ERR_BAD_ARG;
     cudaStream_t s = m->stream;
-    const int chunk = prefill_chunk(d);
+    // chunks of equal size (no one-token tail off the tensor-core path)
+    const int cmax = prefill_chunk(d), nchunks = (n + cmax - 1) / cmax, chunk = (n + nchunks - 1) / nchunks;
     for (int p0 = 0; p0 < n; p0 += chunk) {
         const int c = std::min(chunk, n - p0);
         if (!ok(cudaMemcpyAsync(bt->d_tok, prompt + p0, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens"))
@@ -830,8 +833,11 @@ int prefill_gemm(b2_model* m, const int32_t* tokens, int n, int pos0, std::strin
     }
     b2_batch* bt = m->prefill_ws;
     cudaStream_t s = m->stream;
-    for (int p0 = 0; p0 < n; p0 += kPrefillChunk) {
-        const int c = std::min(kPrefillChunk, n - p0);
+    // chunks of equal size (129 tokens: 65 + 64, not 128 + 1): every chunk
+    // stays on the tensor-core path
+    const int nchunks = (n + kPrefillChunk - 1) / kPrefillChunk, csize = (n + nchunks - 1) / nchunks;
+    for (int p0 = 0; p0 < n; p0 += csize) {
+        const int c = std::min(csize, n - p0);
         if (!ok(cudaMemcpyAsync(bt->d_tok, tokens + p0, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens"))
             return B2_ERR_CUDA;
         bd_iota_kernel<<<(c + 255) / 256, 256, 0, s>>>(bt->d_ppos, c, pos0 + p0);

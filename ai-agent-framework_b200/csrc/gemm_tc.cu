@@ -316,18 +316,32 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
         // ---------------------------------------------------------- producer
         if (lane == 0) {
             const uint32_t bytes = QShape<QT>::kRawQ + QShape<QT>::kRawS + SM::kB;
-            int issued = 0;
-            for (int it = 0; it < nst; it++) {
-                const int s = it % NS;
-                if (it >= NS && !gemm_wait(&rempty[s], ((it / NS) - 1) & 1, a.err, abort_flag)) break;
+            auto load_w = [&](int it) {  // the stage's weight blocks and scales
+                const int s = it % NS, kb = (st0 + it) * kStageBlocks;  // first Q block of the stage
                 uint8_t* st = rawr + (size_t)s * SM::kSlot;
-                const int kb = (st0 + it) * kStageBlocks;  // first Q block of the stage
                 mbar_arrive_expect_tx(&full[s], bytes);
                 tma_load_2d(st + SM::kB, &map_q, kb * (kTileRows * QShape<QT>::QB / 8),
                             a.tiles_q + mt * (kBM / kTileRows), &full[s]);
                 tma_load_2d(st + SM::kB + QShape<QT>::kRawQ, &map_s, kb * (kTileRows * 2 / 8),
                             a.tiles_q + mt * (kBM / kTileRows), &full[s]);
-                tma_load_2d(st, &map_x, kb * 32, nt * BN, &full[s]);
+            };
+            auto load_x = [&](int it) {  // the stage's activation tile
+                const int s = it % NS, kb = (st0 + it) * kStageBlocks;
+                tma_load_2d(rawr + (size_t)s * SM::kSlot, &map_x, kb * 32, nt * BN, &full[s]);
+            };
+            // The weights depend on nothing a previous kernel writes: the first
+            // ring's worth streams before the wait on the kernel this launch
+            // follows (a programmatic dependent launch overlaps its tail);
+            // the activations, and everything after them, come after it.
+            const int pre = min(nst, NS);
+            for (int it = 0; it < pre; it++) load_w(it);
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            for (int it = 0; it < pre; it++) load_x(it);
+            int issued = pre;
+            for (int it = pre; it < nst; it++) {
+                if (!gemm_wait(&rempty[it % NS], ((it / NS) - 1) & 1, a.err, abort_flag)) break;
+                load_w(it);
+                load_x(it);
                 issued = it + 1;
             }
             // every copy issued has landed before the CTA may exit
@@ -442,6 +456,7 @@ constexpr int kCvtVec = 8;  // float4 per thread: cols up to 16384 in one pass
 __global__ void __launch_bounds__(kCvtThreads) to_f16_scaled_kernel(const float* __restrict__ x, int ntok, int cols,
                                                                       __half* __restrict__ xh, float* __restrict__ scale) {
     __shared__ float red[kCvtThreads / 32];
+    pdl_trigger();
     const int t = blockIdx.x, n4 = cols / 4;
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * cols);
     float4 v[kCvtVec];
@@ -573,7 +588,23 @@ int launch_qgemm(const CUtensorMap& mq, const CUtensorMap& ms, const CUtensorMap
         }
         attr[dev] = true;
     }
-    qgemm_kernel<QT, BN><<<grid, kGemmThreads, GemmSmem<QT, BN>::kTotal, s>>>(mq, ms, mx, a);
+    // programmatic dependent launch: the CTAs may start (and stream their
+    // first weights) while the previous kernel on the stream finishes; the
+    // kernel waits for it (griddepcontrol.wait) before it reads activations
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = GemmSmem<QT, BN>::kTotal;
+    cfg.stream = s;
+    cudaLaunchAttribute attr_pdl[1];
+    attr_pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr_pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr_pdl;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, qgemm_kernel<QT, BN>, mq, ms, mx, a) != cudaSuccess) {
+        *err = "tensor-core GEMM launch failed";
+        return B2_ERR_CUDA;
+    }
     return B2_OK;
 }
 
