@@ -561,9 +561,9 @@ int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows,
                    std::string* err) {
     DeviceScratch* sc = scratch_for_current(err);
     if (!sc) return B2_ERR_CUDA;
-    // Q8_0 rows of a multiple of 256 columns: the matvec kernel of its own;
-    // the rest: the decode kernel's single-phase mode
-    if (qtype == 8) {  // (Q4_0 rows stay on the path below: faster for them)
+    // rows of a multiple of 256 columns: the matvec kernel of its own; other
+    // widths: the decode kernel's single-phase mode
+    {
         const int lean = matvec_lean(qtype, w, x, y, rows, cols, sc->sms, s, err);
         if (lean <= 0) return lean;
     }
