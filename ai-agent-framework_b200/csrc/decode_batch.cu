@@ -37,7 +37,7 @@ int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, f
                              int max_len, int sms, cudaStream_t s);
 
 constexpr int kBatchMax = 16;
-constexpr int kPrefillChunk = 128;  // prompt tokens per weight pass of a prefill (tensor-core GEMM)
+constexpr int kPrefillChunk = 256;  // prompt tokens per weight pass of a prefill (tensor-core GEMM)
 constexpr int kBatchSplits = 32;    // attention splits the partial buffer holds (for kBatchMax rows)
 
 struct b2_batch {
@@ -634,7 +634,8 @@ unsigned long long scratch_generation(cudaStream_t s) {
 // (per layer, plus kv_off); its attention covers positions 0 .. d_rpos[r].
 // With all_logits the lm_head and argmax run for every row (d_next[r],
 // d_rpos[r] moved on by one); otherwise for the last row only, into logits
-// row 0 and d_next[0] (a prefill chunk needs the argmax after its last token).
+// row 0 and d_next[0] (a prefill chunk needs the argmax after its last token),
+// or not at all without any_logits (a prompt's chunks before its last).
 // The tensor-core form of forward_rows (every width a multiple of 64, at
 // least kGemmMinRows rows): each product takes its input in the GEMM's fp16
 // form from the kernel before it and leaves its split-K partials to the
@@ -647,7 +648,7 @@ bool tc_rows_ok(const ModelDev& d, int R) {
 }
 
 int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err,
-                    bool all_logits) {
+                    bool all_logits, bool any_logits) {
     b2_model* m = bt->m;
     const ModelDev& d = m->dev;
     cudaStream_t s = m->stream;
@@ -686,6 +687,7 @@ int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_st
         rc = b2_tiled_gemm_f16_impl(qt, lw.wd, tiled_rows(H), 0, H, d.FF, bt->xh, bt->tsc, R, bt->y, &prev, s, err);
     }
     if (rc) return rc;
+    if (!any_logits) return ok(cudaGetLastError(), err, "batched decode launch") ? B2_OK : B2_ERR_CUDA;
     // the last down product's partials, the output norm: fp32 rows in xn (for
     // a one-row lm_head on the batched matvec) and the GEMM's form in xh
     bd_add_norm_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, d.out_norm, H, d.eps, bt->xh,
@@ -704,8 +706,9 @@ int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_st
 }
 
 int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_stride, int max_len, std::string* err,
-                 bool all_logits = true) {
-    if (tc_rows_ok(bt->m->dev, R)) return forward_rows_tc(bt, R, d_rpos, kv_off, slot_stride, max_len, err, all_logits);
+                 bool all_logits = true, bool any_logits = true) {
+    if (tc_rows_ok(bt->m->dev, R))
+        return forward_rows_tc(bt, R, d_rpos, kv_off, slot_stride, max_len, err, all_logits, any_logits);
     b2_model* m = bt->m;
     const ModelDev& d = m->dev;
     cudaStream_t s = m->stream;
@@ -742,6 +745,7 @@ int forward_rows(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_strid
         bd_add_kernel<<<add_blocks, kBdThreads, 0, s>>>(bt->x, bt->y, R * H);
     }
     if (rc) return rc;
+    if (!any_logits) return ok(cudaGetLastError(), err, "batched decode launch") ? B2_OK : B2_ERR_CUDA;
     const int r_lm = all_logits ? 0 : R - 1, n_lm = all_logits ? R : 1;
     bd_rmsnorm_kernel<<<n_lm, kNormThreads, 0, s>>>(bt->x + (size_t)r_lm * H, d.out_norm, bt->xn, H, d.eps);
     rc = matmul_rows(qt, d.lm_head, d.Vp, d.V, H, bt->xn, bt->logits, n_lm, s, err);
@@ -785,7 +789,8 @@ int b2_batch_prefill_impl(b2_batch* bt, int slot, const int32_t* prompt, int n, 
         if (!ok(cudaMemcpyAsync(bt->d_tok, prompt + p0, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens"))
             return B2_ERR_CUDA;
         bd_iota_kernel<<<(c + 255) / 256, 256, 0, s>>>(bt->d_ppos, c, p0);
-        const int rc = forward_rows(bt, c, bt->d_ppos, (size_t)slot * bt->max_seq * d.kvd, 0, p0 + c, err, false);
+        const int rc = forward_rows(bt, c, bt->d_ppos, (size_t)slot * bt->max_seq * d.kvd, 0, p0 + c, err, false,
+                                    p0 + c == n);
         if (rc) return rc;
         // (prompt is pageable host memory: the copy above is complete when the call returns)
     }
@@ -841,7 +846,7 @@ int prefill_gemm(b2_model* m, const int32_t* tokens, int n, int pos0, std::strin
         if (!ok(cudaMemcpyAsync(bt->d_tok, tokens + p0, sizeof(int) * c, cudaMemcpyHostToDevice, s), err, "tokens"))
             return B2_ERR_CUDA;
         bd_iota_kernel<<<(c + 255) / 256, 256, 0, s>>>(bt->d_ppos, c, pos0 + p0);
-        const int rc = forward_rows(bt, c, bt->d_ppos, 0, 0, pos0 + p0 + c, err, false);
+        const int rc = forward_rows(bt, c, bt->d_ppos, 0, 0, pos0 + p0 + c, err, false, p0 + c == n);
         if (rc) return rc;
     }
     if (!ok(cudaMemcpyAsync(d.logits, bt->logits, sizeof(float) * d.V, cudaMemcpyDeviceToDevice, s), err, "logits") ||

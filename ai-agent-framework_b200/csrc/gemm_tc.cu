@@ -8,23 +8,32 @@
 // batched decode steps.  W stays in the decode kernel's tiled Q8_0 / Q4_0
 // layout (dev.cuh); nothing is dequantised in HBM.
 //
-// One CTA computes a 128-row x BN-token tile of Y over its K range:
+// One CTA computes a 128-row x BN-token tile of Y over its K range (BN 16,
+// 32, 64, 128 or 256: the token count rounded up):
 //   warp 0      producer: TMA tensor loads (cp.async.bulk.tensor.2d, this
 //               GPU's own memory, no multicast) of each K stage's raw quant
 //               and scale blocks of the 128 weight rows and of the BN x 64
-//               fp16 activation tile (128-byte swizzle) into a ring of stages;
+//               fp16 activation tile (128-byte swizzle) into a ring of raw
+//               stages as deep as shared memory allows; the first ring's
+//               weights before the wait on the previous kernel (the launch
+//               is a programmatic dependent launch), the activations after;
 //   warp 1      MMA issuer: one thread issues tcgen05.mma kind::f16 (M 128,
-//               N BN, K 16) four times per stage, A and B from shared memory
-//               by descriptor, the fp32 accumulator in tensor memory (BN
-//               columns); tcgen05.commit frees each stage;
-//   warps 2..5  dequantisers: thread r decodes weight row r of the stage
-//               (f16 scale x int8 or nibble - 8, rounded once to fp16) into
-//               the 128-byte-swizzled K-major A tile the MMA reads; then
-//               the epilogue: tcgen05.ld of its accumulator row, times the
-//               token's activation scale, to Y (coalesced over rows).
-// Activations are converted once per call to fp16 with a power-of-two scale
-// per token (its largest magnitude maps into [2^14, 2^15)), so they keep 11
-// significant bits without overflow; products accumulate in fp32.  The
+//               N BN, K 16) four times per stage, A from tensor memory, B
+//               (the activation tile) from shared memory by descriptor, the
+//               fp32 accumulator in tensor memory (BN columns);
+//               tcgen05.commit frees the A stage and the raw stage;
+//   warps 2..9  dequantisers, two per tensor-memory lane quadrant (one Q
+//               block of the stage each): thread (lane) r decodes its weight
+//               row (f16 scale x int8 or nibble - 8, rounded once to fp16)
+//               and stores it with tcgen05.st into its lane of a 4-deep ring
+//               of A stages in tensor memory (the dequantised tile never
+//               touches shared memory); then the epilogue: tcgen05.ld of its
+//               accumulator row, times the token's activation scale, to Y
+//               (coalesced over rows).
+// Activations arrive in fp16 with a power-of-two scale per token (its
+// largest magnitude maps into [2^14, 2^15); converted by the call, or by the
+// kernel before it), so they keep 11 significant bits without overflow;
+// products accumulate in fp32.  The
 // weight d * q is rounded to fp16 once (at most 2^-12 relative error per
 // weight).  Every wait is bounded (globaltimer) and reports B2_ERR_TIMEOUT
 // through the device error flag; a CTA that gave up stops issuing work,
@@ -96,7 +105,7 @@ struct GemmSmem {
     // ring (32 columns a stage: 128 lanes x 64 fp16); 256 columns in all, so
     // two CTAs of an SM fit its 512
     static constexpr uint32_t kAccCols = BN < 32 ? 32 : BN;
-    static constexpr uint32_t kTmemCols = 256;
+    static constexpr uint32_t kTmemCols = BN <= 128 ? 256 : 512;
     static_assert(kAccCols + 32 * kAStages <= kTmemCols && kCtas * kTmemCols <= 512, "tensor memory plan");
 };
 
@@ -615,7 +624,8 @@ int launch_bn(int bn, const CUtensorMap& mq, const CUtensorMap& ms, const CUtens
         case 16: return launch_qgemm<QT, 16>(mq, ms, mx, a, grid, s, err);
         case 32: return launch_qgemm<QT, 32>(mq, ms, mx, a, grid, s, err);
         case 64: return launch_qgemm<QT, 64>(mq, ms, mx, a, grid, s, err);
-        default: return launch_qgemm<QT, 128>(mq, ms, mx, a, grid, s, err);
+        case 128: return launch_qgemm<QT, 128>(mq, ms, mx, a, grid, s, err);
+        default: return launch_qgemm<QT, 256>(mq, ms, mx, a, grid, s, err);
     }
 }
 
@@ -628,7 +638,9 @@ using namespace b2;
 // (base: the tiled matrix, rp its padded rows, cols = K) for ntok tokens:
 // x [ntok][cols] fp32, y [ntok][rows] fp32, device memory, stream s.
 namespace {
-int bn_for(int ntok) { return ntok <= 16 ? 16 : ntok <= 32 ? 32 : ntok <= 64 ? 64 : 128; }
+// N tile: the token count rounded up, 256 at most (the widest MMA: each
+// dequantised A tile then feeds twice the products of a 128-token tile)
+int bn_for(int ntok) { return ntok <= 16 ? 16 : ntok <= 32 ? 32 : ntok <= 64 ? 64 : ntok <= 128 ? 128 : 256; }
 
 // Both entry points: x (fp32, converted here) or xh / tsc (already fp16).
 int gemm_run(int qtype, const void* base, int64_t rp, int64_t row0, int rows, int cols, const float* x,

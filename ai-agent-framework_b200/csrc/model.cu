@@ -46,7 +46,7 @@ int dev_malloc(void** p, size_t bytes) {
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
-constexpr int kWarmTokens = 128;  // the prompt path's warm-up at load: one full chunk
+constexpr int kWarmTokens = 256;  // the prompt path's warm-up at load: one full chunk
 
 // gguf.go:616-643 float16ToFloat32 (host side, for small F16 vectors).
 float f16_to_f32(uint16_t h) {

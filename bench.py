@@ -363,7 +363,9 @@ def run_b200(args) -> None:
     # prefill (timed for information)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
+    torch.cuda.nvtx.range_push("prefill")  # (lets a profiler keep to the prompt)
     first = m.forward_argmax(prompt)
+    torch.cuda.nvtx.range_pop()
     prefill_s = time.perf_counter() - t0
     # warm-up decode steps
     warm = m.decode_greedy(first, W) if W > 0 else np.array([first])
@@ -428,7 +430,7 @@ def run_b200(args) -> None:
                        "l2": f"no flush needed: each token streams {bytes_tok / 1e6:.0f} MB of weights, > 126 MB L2",
                        "parallelism": (f"tp{tpn}" if tpn > 1 else (f"replicas x{ws}" if ws > 1 else "single gpu")),
                        "prefill_s": prefill_s,
-                       "prefill_path": ("b2_forward_argmax: the prompt in 128-token chunks on the tcgen05 GEMM path "
+                       "prefill_path": ("b2_forward_argmax: the prompt in chunks of up to 256 tokens on the tcgen05 GEMM path "
                                         "into the model's KV cache" if tpn == 1 else
                                         "b2_forward_argmax: the decode kernel once per prompt token (tensor parallel)"),
                        "load_s": load_s, "load": load,
@@ -827,7 +829,7 @@ def run_batch(args) -> None:
                    # 2 flops per weight per token; weights = streamed bytes x 32 / (bytes per 32-block)
                    "prefill_tflops": 2.0 * bytes_step * 32 / (34 if shape.wtype == "q8_0" else 18)
                                      * B * (n_prompt + 1) / prefill_s / 1e12,
-                   "prefill_path": "b2_batch_prefill: chunks of up to 128 prompt tokens, one weight pass each on "
+                   "prefill_path": "b2_batch_prefill: chunks of up to 256 prompt tokens, one weight pass each on "
                                    "the tcgen05 GEMM, the chunk's attention over the slot's cache",
                    "l2": f"no flush needed: each step streams {bytes_step / 1e6:.0f} MB of weights"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

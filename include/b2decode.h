@@ -277,7 +277,7 @@ int b2_attention_decode_noalloc(const float* q, const uint16_t* k, const uint16_
  * b2_batch_logits copies the logits of the last forward of the batch,
  * [B][vocab_size]: the B rows of the last b2_batch_step, or, after a
  * b2_batch_prefill, the prompt's last token in row 0.  A prompt runs in
- * chunks of up to 128 of its tokens, each one pass over the weights on the
+ * chunks of up to 256 of its tokens, each one pass over the weights on the
  * tensor cores (b2_model_gemm's product) with the chunk's attention over the
  * slot's cache.  Needs a
  * single-GPU model with the fp16 cache; the model's device must be current.

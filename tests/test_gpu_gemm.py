@@ -73,7 +73,7 @@ def test_gemm_over_resident_tiled_weights(built_lib, torch_cuda, write_model, ke
         w = m.dequant(name, rows * cols).reshape(rows, cols)
         w64 = w.astype(np.float64)
         w16 = w.astype(np.float16).astype(np.float64)
-        for ntok in (1, 7, 16, 40, 100, 130):
+        for ntok in (1, 7, 16, 40, 100, 130, 300):
             x = rng.standard_normal((ntok, cols), dtype=np.float32)
             x[0, :32] *= 1e-3
             dx = torch.from_numpy(x).cuda()
