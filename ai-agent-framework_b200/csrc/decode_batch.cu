@@ -238,6 +238,7 @@ __global__ void __cluster_dims__(kRowCtas, 1, 1) __launch_bounds__(kRowThreads)
     __shared__ float red[kRowThreads / 32];
     __shared__ float c_ss, c_mx;
     pdl_trigger();
+    pdl_wait();
     cg::cluster_group cl = cg::this_cluster();
     const int b = blockIdx.x / kRowCtas, c = (int)cl.block_rank();
     const int n4 = H / 4 / kRowCtas;  // float4 of this CTA's slice
@@ -303,6 +304,7 @@ __global__ void __cluster_dims__(kRowCtas, 1, 1) __launch_bounds__(kRowThreads)
     __shared__ float red[kRowThreads / 32];
     __shared__ float c_mx;
     pdl_trigger();
+    pdl_wait();
     cg::cluster_group cl = cg::this_cluster();
     const int b = blockIdx.x / kRowCtas, c = (int)cl.block_rank();
     const float* row = part + (size_t)b * 2 * FF;
@@ -359,6 +361,8 @@ __global__ void bd_rope_kv_kernel(const float* __restrict__ qkv, int k, size_t p
                                   const float* __restrict__ cosT, const float* __restrict__ sinT,
                                   const int* __restrict__ pos, float* __restrict__ q, __half* __restrict__ kc,
                                   __half* __restrict__ vc, int qd, int kvd, int hd, int slot_stride) {
+    pdl_trigger();
+    pdl_wait();
     const int b = blockIdx.x, p = pos[b], n = qd + 2 * kvd, hh = hd / 2;
     const float* row = qkv + (size_t)b * n;
     for (int j = blockIdx.y * blockDim.x + threadIdx.x; j < n / 2; j += gridDim.y * blockDim.x) {
@@ -641,7 +645,10 @@ unsigned long long scratch_generation(cudaStream_t s) {
 // form from the kernel before it and leaves its split-K partials to the
 // kernel after it, which sums them: per layer the residual add, RMSNorm and
 // conversion are one launch (bd_add_norm_f16), the q/k/v sum rides in the
-// RoPE launch and the gate/up sum in the SwiGLU launch.
+// RoPE launch and the gate/up sum in the SwiGLU launch.  Every launch of a
+// layer is a programmatic dependent launch (launch_pdl): its CTAs are placed
+// while the kernel before it drains and wait for it in pdl_wait, so the
+// 11 launches of a layer do not each pay a launch and a ramp-up.
 bool tc_rows_ok(const ModelDev& d, int R) {
     return R >= kGemmMinRows && R <= kPrefillChunk && d.H % 64 == 0 && d.qd % 64 == 0 && d.FF % 64 == 0 &&
            d.H <= 4 * kRowCtas * kRowThreads * kAddVec && d.FF <= kRowCtas * kRowThreads * kSwClVec;
@@ -660,16 +667,16 @@ int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_st
     int rc = B2_OK;
     for (int l = 0; l < d.L && rc == B2_OK; l++) {
         const LayerDev& lw = m->layers_host[l];
-        bd_add_norm_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, lw.attn_norm, H, d.eps,
-                                                          bt->xh, H, bt->tsc, nullptr);
+        launch_pdl(bd_add_norm_f16_kernel, dim3(R * kRowCtas), dim3(kRowThreads), 0, s, bt->x, prev.p, prev.k,
+                   prev.plane, lw.attn_norm, H, d.eps, bt->xh, H, bt->tsc, nullptr);
         GemmParts p;
         rc = b2_tiled_gemm_f16_impl(qt, lw.wqkv, tiled_rows(n_qkv), 0, n_qkv, H, bt->xh, bt->tsc, R, bt->qkv, &p, s, err);
         if (rc) break;
         __half* kc = bt->kc + (size_t)l * kv_layer + kv_off;
         __half* vc = bt->vc + (size_t)l * kv_layer + kv_off;
-        bd_rope_kv_kernel<<<dim3(R, (n_qkv / 2 + kBdThreads - 1) / kBdThreads), kBdThreads, 0, s>>>(
-            p.p, p.k, p.plane, lw.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc,
-                                                   vc, d.qd, d.kvd, d.hd, slot_stride);
+        launch_pdl(bd_rope_kv_kernel, dim3(R, (n_qkv / 2 + kBdThreads - 1) / kBdThreads), dim3(kBdThreads), 0, s,
+                   p.p, p.k, p.plane, lw.bqkv, d.rope_cos, d.rope_sin, d_rpos, bt->q, kc, vc, d.qd, d.kvd, d.hd,
+                   slot_stride);
         rc = b2_attention_seqs_launch(bt->q, kc, vc, bt->part, bt->part_floats, bt->att, R, d.nh, d.nkv, d.hd, d_rpos,
                                       1, slot_stride, max_len, m->grid, s);
         if (rc) {
@@ -678,20 +685,21 @@ int forward_rows_tc(b2_batch* bt, int R, int* d_rpos, size_t kv_off, int slot_st
         }
         rc = b2_tiled_gemm_impl(qt, lw.wo, tiled_rows(H), 0, H, d.qd, bt->att, bt->y, R, &p, s, err);
         if (rc) break;
-        bd_add_norm_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(bt->x, p.p, p.k, p.plane, lw.ffn_norm, H, d.eps, bt->xh, H,
-                                                          bt->tsc, nullptr);
+        launch_pdl(bd_add_norm_f16_kernel, dim3(R * kRowCtas), dim3(kRowThreads), 0, s, bt->x, p.p, p.k, p.plane,
+                   lw.ffn_norm, H, d.eps, bt->xh, H, bt->tsc, nullptr);
         rc = b2_tiled_gemm_f16_impl(qt, lw.wgu, tiled_rows(2 * d.FF), 0, 2 * d.FF, H, bt->xh, bt->tsc, R, bt->gu, &p, s,
                                     err);
         if (rc) break;
-        bd_swiglu_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(p.p, p.k, p.plane, d.FF, bt->xh, d.FF, bt->tsc);
+        launch_pdl(bd_swiglu_f16_kernel, dim3(R * kRowCtas), dim3(kRowThreads), 0, s, p.p, p.k, p.plane, d.FF,
+                   bt->xh, d.FF, bt->tsc);
         rc = b2_tiled_gemm_f16_impl(qt, lw.wd, tiled_rows(H), 0, H, d.FF, bt->xh, bt->tsc, R, bt->y, &prev, s, err);
     }
     if (rc) return rc;
     if (!any_logits) return ok(cudaGetLastError(), err, "batched decode launch") ? B2_OK : B2_ERR_CUDA;
     // the last down product's partials, the output norm: fp32 rows in xn (for
     // a one-row lm_head on the batched matvec) and the GEMM's form in xh
-    bd_add_norm_f16_kernel<<<R * kRowCtas, kRowThreads, 0, s>>>(bt->x, prev.p, prev.k, prev.plane, d.out_norm, H, d.eps, bt->xh,
-                                                      H, bt->tsc, bt->xn);
+    launch_pdl(bd_add_norm_f16_kernel, dim3(R * kRowCtas), dim3(kRowThreads), 0, s, bt->x, prev.p, prev.k, prev.plane,
+               d.out_norm, H, d.eps, bt->xh, H, bt->tsc, bt->xn);
     const int r_lm = all_logits ? 0 : R - 1, n_lm = all_logits ? R : 1;
     if (n_lm >= kGemmMinRows)
         rc = b2_tiled_gemm_f16_impl(qt, d.lm_head, d.Vp, 0, d.V, H, bt->xh + (size_t)r_lm * H, bt->tsc + r_lm, n_lm,

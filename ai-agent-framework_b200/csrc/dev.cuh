@@ -3,6 +3,7 @@
 #include <stdint.h>
 #ifdef __CUDACC__
 #include <cuda_fp16.h>
+#include <utility>
 #endif
 
 namespace b2 {
@@ -492,6 +493,35 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 // dependent launch start now (it waits for this grid's completion, with
 // griddepcontrol.wait, before it reads anything this grid writes).
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Waits until the grid this one was launched after (programmatic dependent
+// launch) has completed and its writes are visible; returns at once for a
+// grid launched without the attribute.  A kernel launched by launch_pdl
+// calls it before its first global read or write, in every thread, so its
+// own completion still implies its predecessor's (the chain of launches
+// stays ordered for the kernels after it).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Launches kern<<<grid, block, smem, s>>>(args...) as a programmatic
+// dependent launch: its CTAs may be scheduled while the kernel before it on
+// the stream finishes (once that one has called pdl_trigger in every CTA, or
+// exited), and wait in pdl_wait for its completion.  Hides the launch and
+// the prologue of a short kernel behind its predecessor's tail; inside a
+// captured graph the dependency becomes a programmatic edge.
+template <typename... P, typename... A>
+cudaError_t launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...);
+}
 
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;

@@ -320,6 +320,10 @@ __global__ void __launch_bounds__(kGemmThreads, GemmSmem<QT, BN>::kCtas)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // The kernel after this one may launch now.  Only after the tensor
+    // memory is held: a dependent GEMM's CTA placed on this SM early must
+    // not take the columns a CTA of this grid still waits to allocate.
+    pdl_trigger();
 
     if (warp == 0) {
         // ---------------------------------------------------------- producer
@@ -466,6 +470,7 @@ __global__ void __launch_bounds__(kCvtThreads) to_f16_scaled_kernel(const float*
                                                                       __half* __restrict__ xh, float* __restrict__ scale) {
     __shared__ float red[kCvtThreads / 32];
     pdl_trigger();
+    pdl_wait();
     const int t = blockIdx.x, n4 = cols / 4;
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * cols);
     float4 v[kCvtVec];
@@ -515,6 +520,8 @@ __global__ void __launch_bounds__(kCvtThreads) to_f16_scaled_kernel(const float*
 // (the same sums whatever order the CTAs finished in): float4 elements when
 // y is 16-byte aligned and the count divides by 4, single floats otherwise.
 __global__ void splitk_sum4_kernel(const float* __restrict__ part, int ks, size_t n4, float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     const float4* p = reinterpret_cast<const float4*>(part);
     float4* o = reinterpret_cast<float4*>(y);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
@@ -527,6 +534,8 @@ __global__ void splitk_sum4_kernel(const float* __restrict__ part, int ks, size_
     }
 }
 __global__ void splitk_sum1_kernel(const float* __restrict__ part, int ks, size_t n, float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         float v = __ldcg(part + i);
         for (int s = 1; s < ks; s++) v += __ldcg(part + (size_t)s * n + i);
@@ -724,7 +733,9 @@ int gemm_run(int qtype, const void* base, int64_t rp, int64_t row0, int rows, in
         *err = "tensor map encoding failed (alignment)";
         return B2_ERR_BAD_ARG;
     }
-    if (x) to_f16_scaled_kernel<<<ntok_pad, kCvtThreads, 0, s>>>(x, ntok, cols, xh, const_cast<float*>(tsc));
+    if (x)
+        launch_pdl(to_f16_scaled_kernel, dim3(ntok_pad), dim3(kCvtThreads), 0, s, x, ntok, cols, xh,
+                   const_cast<float*>(tsc));
     GemmArgs a{};
     a.nst = nst;
     a.kst_split = kst;
@@ -749,8 +760,8 @@ int gemm_run(int qtype, const void* base, int64_t rp, int64_t row0, int rows, in
         const bool vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;  // (part is 256-aligned)
         const size_t units = vec ? n / 4 : n;
         const int blocks = (int)std::min<size_t>((size_t)sc->sms * 8, (units + 255) / 256);
-        if (vec) splitk_sum4_kernel<<<std::max(blocks, 1), 256, 0, s>>>(part, ksplit, units, y);
-        else splitk_sum1_kernel<<<std::max(blocks, 1), 256, 0, s>>>(part, ksplit, units, y);
+        if (vec) launch_pdl(splitk_sum4_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, s, part, ksplit, units, y);
+        else launch_pdl(splitk_sum1_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, s, part, ksplit, units, y);
     }
     cudaError_t ce = cudaGetLastError();
     if (ce != cudaSuccess) {
@@ -797,6 +808,8 @@ namespace {
 // up 2) of a gate/up product computed over the interleaved resident matrix.
 __global__ void gather_half_kernel(const float* __restrict__ fused, int ntok, int rows, int half,
                                    float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     const size_t n = (size_t)ntok * rows;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const size_t t = i / rows;
@@ -839,7 +852,7 @@ int b2_tiled_gemm_half_impl(int qtype, const void* base, int64_t rp, int half, i
     int rc = b2_tiled_gemm_impl(qtype, base, rp, 0, 2 * rows, cols, x, fused, ntok, s, err);
     if (!rc) {
         const int blocks = (int)std::min<size_t>(4096, ((size_t)ntok * rows + 255) / 256);
-        gather_half_kernel<<<std::max(blocks, 1), 256, 0, s>>>(fused, ntok, rows, half, y);
+        launch_pdl(gather_half_kernel, dim3(std::max(blocks, 1)), dim3(256), 0, s, fused, ntok, rows, half, y);
         if (cudaGetLastError() != cudaSuccess) {
             *err = "gate/up gather launch failed";
             rc = B2_ERR_CUDA;

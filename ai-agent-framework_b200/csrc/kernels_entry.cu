@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(kAttThreads, (GRP <= 4 ? 2 : 1))
                       float* __restrict__ part, int nh, int nkv, int ctx, int S, const AttnSeqs seqs) {
     constexpr int DL = 8, LP = HD / DL, G = 32 / LP, U = GRP <= 3 ? 4 : (GRP == 4 ? 3 : 2);
     extern __shared__ float sm[];
+    pdl_trigger();
+    pdl_wait();
     const int cta = blockIdx.x;
     const int s = cta % S, g = (cta / S) % nkv, b = cta / (S * nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -276,6 +278,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     uint8_t* ring = asm_raw;                         // [stage][K tile | V tile]
     uint8_t* qh = ring + SM::kRing;                  // [16][HD] fp16, swizzled
     uint8_t* ql = qh + SM::kQ;
+    pdl_trigger();
+    pdl_wait();
     const int cta = blockIdx.x;
     const int s = cta % S, g = (cta / S) % nkv, b = cta / (S * nkv);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gi = lane >> 2, ti = lane & 3;
@@ -456,7 +460,8 @@ bool launch_mma_hd(int grp, int grid, cudaStream_t st, const float* q, const __h
             return false;
         attr = true;
     }
-    attn_mma_kernel<HD, VAR><<<grid, kMmaThreads, smem, st>>>(q, k, v, part, nh, nkv, grp, ctx, S, seqs);
+    launch_pdl(attn_mma_kernel<HD, VAR>, dim3(grid), dim3(kMmaThreads), smem, st, q, k, v, part, nh, nkv, grp, ctx, S,
+               seqs);
     return true;
 }
 
@@ -468,7 +473,7 @@ bool launch_split_hd(int grp, int grid, cudaStream_t st, const float* q, const _
     auto go = [&](auto kern, int g) {
         const size_t smem = sizeof(float) * (size_t)kAttWarps * g * (HD + 2);
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        kern<<<grid, kAttThreads, smem, st>>>(q, k, v, part, nh, nkv, ctx, S, seqs);
+        launch_pdl(kern, dim3(grid), dim3(kAttThreads), smem, st, q, k, v, part, nh, nkv, ctx, S, seqs);
         return true;
     };
     switch (grp) {
@@ -510,6 +515,8 @@ bool launch_split(int hd, int grp, int grid, cudaStream_t st, const float* q, co
 }
 
 __global__ void attn_merge_kernel(const float* __restrict__ part, float* __restrict__ out, int nh, int hd, int S) {
+    pdl_trigger();
+    pdl_wait();
     const int bh = blockIdx.x;  // sequence * nh + head
     const float* ph = part + (size_t)bh * S * (hd + 2);
     float M = -INFINITY;
@@ -638,7 +645,7 @@ int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, floa
         *err = "head_dim must be 64, 128 or 256";
         return B2_ERR_BAD_ARG;
     }
-    attn_merge_kernel<<<batch * nh, std::min(hd, 256), 0, s>>>(sc->part, out, nh, hd, S);
+    launch_pdl(attn_merge_kernel, dim3(batch * nh), dim3(std::min(hd, 256)), 0, s, sc->part, out, nh, hd, S);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = std::string("attention launch: ") + cudaGetErrorString(e);
@@ -661,7 +668,7 @@ int b2_attention_seqs_launch(const float* q, const __half* k, const __half* v, f
     S = (int)std::max<size_t>(1, std::min<size_t>((size_t)S, part_floats / per_split));
     const AttnSeqs seqs{lens, add, stride};
     if (!launch_split(hd, grp, batch * nkv * S, s, q, k, v, part, nh, nkv, 0, S, &seqs)) return B2_ERR_UNSUPPORTED_TYPE;
-    attn_merge_kernel<<<batch * nh, std::min(hd, 256), 0, s>>>(part, out, nh, hd, S);
+    launch_pdl(attn_merge_kernel, dim3(batch * nh), dim3(std::min(hd, 256)), 0, s, part, out, nh, hd, S);
     return cudaGetLastError() == cudaSuccess ? B2_OK : B2_ERR_CUDA;
 }
 
