@@ -94,10 +94,10 @@ __host__ __device__ inline int64_t src_row(int64_t r, int64_t half_rows) {
 }
 
 // One thread per (row, block) of the padded matrix: ggml block -> tiled
-// quants + scale (padding rows become zero).  Source rows have nb_src blocks,
-// of which blocks cb0 .. cb0 + nb go in (a tensor-parallel column share).
+// quants + scale (padding rows become zero).  Source rows have nb blocks (a
+// tensor-parallel column share arrives already cut to its window).
 __global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, int64_t rp, int64_t nb, int qtype,
-                              int64_t half_rows, int64_t nb_src, int64_t cb0) {
+                              int64_t half_rows) {
     const int bpb = qtype == 8 ? 34 : 18, qb = tile_qb(qtype);
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rp * nb; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / nb, b = i - r * nb;
@@ -107,7 +107,7 @@ __global__ void repack_kernel(const uint8_t* raw, uint8_t* dst, int64_t rows, in
             for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = 0;
             continue;
         }
-        const uint8_t* src = raw + (src_row(r, half_rows) * nb_src + cb0 + b) * bpb;
+        const uint8_t* src = raw + (src_row(r, half_rows) * nb + b) * bpb;
         sd[0] = src[0];
         sd[1] = src[1];
         for (int e = 0; e < qb; e++) dst[tiled_qoff(r, b, e, nb, qtype)] = src[2 + e];
@@ -607,11 +607,12 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
         // Weight matrices: file -> pinned stages -> raw device buffer, then
         // one repack launch per matrix into the arena (the raw buffer is
         // reused by the next matrix only after its repack, stream order).
+        // A column share reads only its window of each row from the file.
         size_t raw_max = 0;
         for (const MatGroup& gr : groups) {
             int64_t r = 0;
             for (const MatPart& pt : gr.parts) r += pt.rows;
-            raw_max = std::max(raw_max, (size_t)r * (size_t)gr.nb_src * bpb);
+            raw_max = std::max(raw_max, (size_t)r * (size_t)(gr.cols / 32) * bpb);
         }
         void* raw = nullptr;
         if (dev_malloc(&raw, raw_max) != 0)
@@ -622,10 +623,14 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             for (const MatPart& pt : gr.parts) {
                 const std::string& name = pt.name;
                 const GgufTensor* t = g.find(name);
-                const uint64_t rb_src = (uint64_t)gr.nb_src * bpb;  // source row bytes
-                const uint64_t n = (uint64_t)pt.rows * rb_src, src = g.data_offset + t->offset + (uint64_t)pt.row0 * rb_src;
-                if (!up.to_device(src, n, static_cast<uint8_t*>(raw) + dst)) { io_ok = false; break; }
-                dst += n;
+                const uint64_t rb_src = (uint64_t)gr.nb_src * bpb;      // source row bytes
+                const uint64_t rb = (uint64_t)(gr.cols / 32) * bpb;     // the share's window of a row
+                const uint64_t src = g.data_offset + t->offset + (uint64_t)pt.row0 * rb_src + (uint64_t)gr.cb0 * bpb;
+                if (!up.to_device_window(src, rb_src, rb, (uint64_t)pt.rows, static_cast<uint8_t*>(raw) + dst)) {
+                    io_ok = false;
+                    break;
+                }
+                dst += (uint64_t)pt.rows * rb;
                 // this rank's share of the tensor (b2_dequant_tensor decodes it)
                 TensorLoc tl{A + gr.off, t->type, (uint64_t)pt.rows * (uint64_t)gr.cols};
                 tl.row0 = row0;
@@ -639,7 +644,7 @@ int b2_load_impl(const char* path, const b2_load_opts* opts, b2_model** out, std
             const int64_t rp = tiled_rows(gr.rows), nbk = gr.cols / 32;
             const int blocks = (int)std::min<int64_t>((rp * nbk + 255) / 256, 148 * 32);
             repack_kernel<<<blocks, 256, 0, m->stream>>>(static_cast<const uint8_t*>(raw), A + gr.off, gr.rows, rp, nbk,
-                                                         qti, gr.half_rows, gr.nb_src, gr.cb0);
+                                                         qti, gr.half_rows);
         }
         if (!up.finish()) io_ok = false;
         cudaStreamSynchronize(m->stream);

@@ -95,11 +95,21 @@ bool Uploader::read_range(uint8_t* dst, uint64_t off, size_t n) {
     return true;
 }
 
+bool Uploader::read_packed(uint8_t* dst, uint64_t p, size_t b, size_t e) {
+    while (b < e) {
+        const uint64_t q = p + b, r = q / win_width_, c = q - r * win_width_;
+        const size_t n = (size_t)std::min<uint64_t>(win_width_ - c, e - b);
+        if (!read_range(dst + b, win_off_ + r * win_pitch_ + c, n)) return false;
+        b += n;
+    }
+    return true;
+}
+
 void Uploader::worker(int id) {
     uint64_t seen = 0;
     for (;;) {
         uint8_t* dst;
-        uint64_t off;
+        uint64_t p;
         size_t n;
         {
             std::unique_lock<std::mutex> lk(mu_);
@@ -107,12 +117,12 @@ void Uploader::worker(int id) {
             if (stop_) return;
             seen = job_gen_;
             dst = job_dst_;
-            off = job_off_;
+            p = job_p_;
             n = job_n_;
         }
         const size_t slice = ((n + parts_ - 1) / parts_ + kSliceAlign - 1) / kSliceAlign * kSliceAlign;
         const size_t b = std::min(n, (size_t)id * slice), e = std::min(n, b + slice);
-        const bool ok = e <= b || read_range(dst + b, off + b, e - b);
+        const bool ok = read_packed(dst, p, b, e);
         {
             std::lock_guard<std::mutex> lk(mu_);
             if (!ok) job_fail_ = true;
@@ -121,22 +131,22 @@ void Uploader::worker(int id) {
     }
 }
 
-void Uploader::fill(uint8_t* dst, uint64_t off, size_t n) {
+void Uploader::fill(uint8_t* dst, uint64_t p, size_t n) {
     const int64_t t0 = now_ns();
     if (pool_.empty() || n < kInlineBytes) {
-        if (!read_range(dst, off, n)) job_fail_ = true;
+        if (!read_packed(dst, p, 0, n)) job_fail_ = true;
     } else {
         {
             std::lock_guard<std::mutex> lk(mu_);
             job_dst_ = dst;
-            job_off_ = off;
+            job_p_ = p;
             job_n_ = n;
             job_pending_ = (int)pool_.size();
             job_gen_++;
         }
         cv_job_.notify_all();
         const size_t slice = ((n + parts_ - 1) / parts_ + kSliceAlign - 1) / kSliceAlign * kSliceAlign;
-        if (!read_range(dst, off, std::min(n, slice))) {
+        if (!read_packed(dst, p, 0, std::min(n, slice))) {
             std::lock_guard<std::mutex> lk(mu_);
             job_fail_ = true;
         }
@@ -146,12 +156,27 @@ void Uploader::fill(uint8_t* dst, uint64_t off, size_t n) {
     host_ns_ += now_ns() - t0;
 }
 
-bool Uploader::to_device(uint64_t off, size_t n, void* dst) {
+bool Uploader::to_device_window(uint64_t off, uint64_t pitch, uint64_t width, uint64_t rows, void* dst) {
     if (!ok()) return false;
-    if (off > file_bytes_ || n > file_bytes_ - off) {
+    if (rows == 0 || width == 0) return true;
+    if (width > pitch) {
+        err_ = "upload window wider than its row pitch";
+        return false;
+    }
+    const uint64_t span = (rows - 1) * pitch + width;  // (rows - 1) * pitch < file size checked below
+    if (off > file_bytes_ || rows - 1 > (file_bytes_ - off) / pitch || span > file_bytes_ - off) {
         err_ = "tensor data beyond the end of the file";
         return false;
     }
+    if (width == pitch) {  // whole rows: one contiguous range
+        width = pitch = span;
+        rows = 1;
+    }
+    win_off_ = off;
+    win_pitch_ = pitch;
+    win_width_ = width;
+    uint64_t p = 0;
+    size_t n = (size_t)(rows * width);
     uint8_t* d = static_cast<uint8_t*>(dst);
     while (n > 0) {
         const size_t nb = std::min(n, kStageBytes);
@@ -160,7 +185,7 @@ bool Uploader::to_device(uint64_t off, size_t n, void* dst) {
             err_ = "upload copy failed";
             return false;
         }
-        fill(stage_[s], off, nb);
+        fill(stage_[s], p, nb);
         if (job_fail_) {
             err_ = "short read while uploading tensors";
             return false;
@@ -172,7 +197,7 @@ bool Uploader::to_device(uint64_t off, size_t n, void* dst) {
         }
         used_[s] = true;
         next_ = (next_ + 1) % kStages;
-        off += nb;
+        p += nb;
         d += nb;
         n -= nb;
         bytes_ += nb;

@@ -36,7 +36,11 @@ public:
     // Queue the copy of file bytes [off, off + n) to device memory dst on the
     // stream (returns once the bytes are in pinned stages; the device copies
     // may still run).  False (and error()) on a short file or a CUDA error.
-    bool to_device(uint64_t off, size_t n, void* dst);
+    bool to_device(uint64_t off, size_t n, void* dst) { return to_device_window(off, n, n, 1, dst); }
+    // The same for a window of `width` bytes of each of `rows` rows that
+    // start `pitch` bytes apart from off (a column share of a matrix): the
+    // windows land back to back at dst, only their bytes are read and sent.
+    bool to_device_window(uint64_t off, uint64_t pitch, uint64_t width, uint64_t rows, void* dst);
     // Synchronous read of a small range into host memory.
     bool to_host(uint64_t off, size_t n, void* dst);
     // Wait for every queued device copy.
@@ -48,9 +52,14 @@ public:
     int threads() const { return (int)parts_; }
 
 private:
-    void fill(uint8_t* dst, uint64_t off, size_t n);  // parallel over the pool
+    // packed bytes [p, p + n) of the current window into dst, in parallel
+    // over the pool
+    void fill(uint8_t* dst, uint64_t p, size_t n);
     void worker(int id);
-    bool read_range(uint8_t* dst, uint64_t off, size_t n);  // one thread's slice
+    bool read_range(uint8_t* dst, uint64_t off, size_t n);
+    // packed bytes [p + b, p + e) of the current window into dst + b (one
+    // thread's slice)
+    bool read_packed(uint8_t* dst, uint64_t p, size_t b, size_t e);
 
     int fd_ = -1;
     const uint8_t* map_ = nullptr;
@@ -64,7 +73,10 @@ private:
     int64_t host_ns_ = 0;
     uint64_t bytes_ = 0;
 
-    // pool: job = (dst, off, n) split into equal slices, slice i to thread i
+    // the window being copied: packed byte q is file byte
+    // win_off_ + (q / win_width_) * win_pitch_ + q % win_width_
+    uint64_t win_off_ = 0, win_pitch_ = 1, win_width_ = 1;
+    // pool: job = (dst, p, n) split into equal slices, slice i to thread i
     std::vector<std::thread> pool_;
     size_t parts_ = 1;  // threads sharing a stage: the pool plus the caller
     std::mutex mu_;
@@ -74,7 +86,7 @@ private:
     bool stop_ = false;
     bool job_fail_ = false;
     uint8_t* job_dst_ = nullptr;
-    uint64_t job_off_ = 0;
+    uint64_t job_p_ = 0;
     size_t job_n_ = 0;
 };
 
