@@ -13,9 +13,12 @@
 //   gate/up tile dot (interleaved 8 rows at a time) -> SwiGLU -> down tile dot
 //   -> residual add
 //   final RMSNorm -> lm_head tile dot -> argmax per sequence (first maximum).
-// The tile dots are the batched matvec over the resident tiled weights
-// (matvec_batch.cu).  A slot's prompt runs through the same launches in
-// chunks of up to 16 of its tokens.
+// When every width is a multiple of 64 the products run on the tcgen05
+// tensor-core GEMM (gemm_tc.cu) and the norms, RoPE and SwiGLU are fused
+// into the kernels between them (forward_rows_tc); otherwise the tile dots
+// are the batched matvec over the resident tiled weights (matvec_batch.cu).
+// A slot's prompt runs through the same launches in chunks of up to
+// kPrefillChunk of its tokens.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>

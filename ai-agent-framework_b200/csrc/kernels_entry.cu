@@ -2,8 +2,11 @@
 // long-context GQA decode attention.
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/b2decode.h"
@@ -15,8 +18,6 @@ namespace {
 
 struct DeviceScratch {
     int* err = nullptr;
-    float* part = nullptr;
-    size_t part_floats = 0;
     int sms = 0;
 };
 
@@ -448,17 +449,22 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     }
 }
 
+constexpr int kMaxAttnDevices = 64;
+
 template <int HD, bool VAR>
 bool launch_mma_hd(int grp, int grid, cudaStream_t st, const float* q, const __half* k, const __half* v, float* part,
                    int nh, int nkv, int ctx, int S, const AttnSeqs& seqs) {
-    static bool attr = false;
+    // the attribute belongs to a device: set on each device's first launch
+    static std::atomic<bool> attr[kMaxAttnDevices] = {};
     constexpr int smem = MmaSmem<HD>::kTotal;
     static_assert(4 * 16 * (HD + 2) * 4 <= MmaSmem<HD>::kRing, "the warp merge fits over the ring");
-    if (!attr) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxAttnDevices) return false;
+    if (!attr[dev]) {
         if (cudaFuncSetAttribute(attn_mma_kernel<HD, VAR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)
             return false;
-        attr = true;
+        attr[dev] = true;
     }
     launch_pdl(attn_mma_kernel<HD, VAR>, dim3(grid), dim3(kMmaThreads), smem, st, q, k, v, part, nh, nkv, grp, ctx, S,
                seqs);
@@ -610,6 +616,15 @@ int b2_matvec_impl(int qtype, const void* w, const float* x, float* y, int rows,
     return launch_decode(m, a, sc->sms, s, err);
 }
 
+// The allocating entry point's split partials, one buffer per (device,
+// stream): calls on one stream are ordered and share it; calls on different
+// streams never race on each other's.
+struct AttnScratch {
+    float* part = nullptr;
+    size_t part_floats = 0;
+};
+std::map<std::pair<int, cudaStream_t>, AttnScratch> g_attn_scratch;  // under g_mu
+
 int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, float* out, int batch, int nh, int nkv,
                       int hd, int ctx, cudaStream_t s, std::string* err) {
     const int grp = nh / nkv;
@@ -623,29 +638,34 @@ int b2_attention_impl(const float* q, const uint16_t* k, const uint16_t* v, floa
     }
     DeviceScratch* sc = scratch_for_current(err);
     if (!sc) return B2_ERR_CUDA;
+    int dev = 0;
+    cudaGetDevice(&dev);
     const int S = attention_splits(batch, nkv, ctx, sc->sms);
     const size_t need = (size_t)batch * nh * S * (hd + 2);
+    float* part;
     {
         std::lock_guard<std::mutex> g(g_mu);
-        if (sc->part_floats < need) {
-            if (sc->part) cudaFree(sc->part);
-            sc->part = nullptr;
-            sc->part_floats = 0;
-            if (cudaMalloc(&sc->part, need * sizeof(float)) != cudaSuccess) {
+        AttnScratch& a = g_attn_scratch[{dev, s}];
+        if (a.part_floats < need) {
+            if (a.part) cudaFree(a.part);
+            a.part = nullptr;
+            a.part_floats = 0;
+            if (cudaMalloc(&a.part, need * sizeof(float)) != cudaSuccess) {
                 *err = "scratch allocation failed";
                 return B2_ERR_OOM;
             }
-            sc->part_floats = need;
+            a.part_floats = need;
         }
+        part = a.part;
     }
     const int grid = batch * nkv * S;
     const __half* kh = reinterpret_cast<const __half*>(k);
     const __half* vh = reinterpret_cast<const __half*>(v);
-    if (!launch_split(hd, grp, grid, s, q, kh, vh, sc->part, nh, nkv, ctx, S)) {
+    if (!launch_split(hd, grp, grid, s, q, kh, vh, part, nh, nkv, ctx, S)) {
         *err = "head_dim must be 64, 128 or 256";
         return B2_ERR_BAD_ARG;
     }
-    launch_pdl(attn_merge_kernel, dim3(batch * nh), dim3(std::min(hd, 256)), 0, s, sc->part, out, nh, hd, S);
+    launch_pdl(attn_merge_kernel, dim3(batch * nh), dim3(std::min(hd, 256)), 0, s, part, out, nh, hd, S);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = std::string("attention launch: ") + cudaGetErrorString(e);
