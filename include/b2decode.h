@@ -245,9 +245,10 @@ int b2_model_gemm(const b2_model* m, const char* name, const float* x, float* y,
  * fp16 KV cache, split over the context with a log-sum-exp merge.
  * q [batch][nh*hd] fp32; k, v [batch][ctx][nkv*hd] fp16 (binary16 bits);
  * out [batch][nh*hd] fp32.  DEVICE pointers.  Asynchronous on `stream`; the
- * split partials live in a scratch kept per (device, stream) and grown by
- * cudaMalloc when a call needs more, so calls on different streams may
- * overlap. */
+ * split partials live in a scratch kept per (device, stream), grown by
+ * cudaMalloc when a call needs more and held until the process exits, so
+ * calls on different streams may overlap (a caller that cycles through many
+ * short-lived streams holds one buffer per stream it used). */
 int b2_attention_decode(const float* q, const uint16_t* k, const uint16_t* v, float* out, int32_t batch,
                         int32_t nh, int32_t nkv, int32_t hd, int32_t ctx, void* stream);
 
