@@ -849,7 +849,7 @@ int prefill_gemm(b2_model* m, const int32_t* tokens, int n, int pos0, std::strin
     }
     b2_batch* bt = m->prefill_ws;
     cudaStream_t s = m->stream;
-    // chunks of equal size (129 tokens: 65 + 64, not 128 + 1): every chunk
+    // chunks of equal size (300 tokens: 150 + 150, not 256 + 44): every chunk
     // stays on the tensor-core path
     const int nchunks = (n + kPrefillChunk - 1) / kPrefillChunk, csize = (n + nchunks - 1) / nchunks;
     for (int p0 = 0; p0 < n; p0 += csize) {

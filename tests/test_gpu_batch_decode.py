@@ -93,8 +93,8 @@ def test_batch_rejects_what_it_cannot_run(built_lib, write_model):
 
 
 def test_batch_prefill_long_prompt_chunks(built_lib, oracle_lib, write_model):
-    """A 300-token prompt runs in three chunks (128, 128, 44 tokens) on the
-    tensor-core GEMM, each attending over the cache the earlier chunks
+    """A 300-token prompt runs in two chunks of 150 tokens on the
+    tensor-core GEMM, the second attending over the cache the first
     wrote: the argmax after the prompt, its logits (row 0) and four steps
     after it against the oracle."""
     shape = SHAPES["llama-hd128-q4"].with_(context=512)

@@ -120,8 +120,7 @@ def test_gemm_large_k_split_and_deterministic(built_lib, torch_cuda, write_model
 @pytest.mark.parametrize("key", ["qwen2-hd64-q8", "llama-hd128-q4"])
 def test_model_prefill_on_tensor_cores(built_lib, oracle_lib, write_model, key):
     """b2_forward with a prompt of 16+ tokens runs the prefill on the GEMM
-    path into the model's own cache (chunks of 128: 200 tokens are two
-    chunks); the same prompt fed one token per decode-kernel launch, and the
+    path into the model's own cache (one chunk of 200 tokens); the same prompt fed one token per decode-kernel launch, and the
     oracle, give the same logits to 1e-2 relative L2 and the same argmax;
     decode steps after either prefill agree too."""
     import goref
