@@ -150,3 +150,28 @@ def test_model_prefill_on_tensor_cores(built_lib, oracle_lib, write_model, key):
         t = int(np.argmax(z))
     gemm.close()
     step.close()
+
+
+def test_model_prefill_in_chunks_continues_the_cache(built_lib, oracle_lib, write_model):
+    """b2_forward with a 300-token prompt: two chunks of 150 tokens on the
+    GEMM path, the second attending over the cache the first wrote; then a
+    second call of 40 tokens continues the same cache from position 300 (one
+    more chunk), and a decode step follows.  Logits and argmax against the
+    oracle after each call."""
+    import goref
+    shape = gw.ModelShape("llama", 512, 2, 4, 1, 1024, 384, 512, 1e-5, 5e5, False, False, "q4_0", 1, 2)
+    path = write_model("llama-hd128-q4-chunks", shape)
+    m = b2decode.Model(path, num_ctx=400)
+    g = goref.GoRef(path, num_ctx=400, n_threads=0, mode=goref.MODE_GGML_Q4)
+    # (seeds whose top-1 logit leads the next by over 0.15 rms at every check)
+    prompt = np.concatenate([[shape.bos_id], gw.make_prompt(shape.vocab, 299, seed=33)]).astype(np.int32)
+    more = gw.make_prompt(shape.vocab, 40, seed=133).astype(np.int32)
+    for toks, pos in ((prompt, 300), (more, 340)):
+        a, c = m.forward(toks), g.forward(toks)
+        assert m.cache_len == pos
+        assert rel_l2(a, c) < 1e-2, (pos, rel_l2(a, c))
+        assert int(np.argmax(a)) == int(np.argmax(c)), pos
+    t = int(np.argmax(c))
+    a, c = m.forward([t]), g.forward([t])
+    assert rel_l2(a, c) < 1e-2 and int(np.argmax(a)) == int(np.argmax(c))
+    m.close()
